@@ -1,0 +1,278 @@
+/*
+ * wzyb200.h -- C ABI of the B200 (sm_100a) per-layer fused elementwise kernels.
+ *
+ * Drop-in replacements for the elementwise kernels that the layer executors of wzy-flash-serve
+ * launch directly with <<<grid, block, 0, stream>>>:
+ *   StageGpu::record_forward            (src/wzy_stage_v2.cuh:476-857, decode / verify, T <= 8)
+ *   PrefillStageCtx::run_stage_prefill  (src/wzy_prefill_tc.cuh:546-1058, chunked prefill)
+ * plus the token-embedding and 3-gram PLE gathers that the engine driver does on the host
+ * (src/wzy_engine_v2.cu:862-875, :943-978, :1210-1265).
+ *
+ * Conventions (shared by every entry point):
+ *  - All tensors are caller-owned DEVICE buffers; nothing here allocates, synchronises or reads
+ *    device memory from the host, so every launcher may be recorded into a CUDA graph by stream
+ *    capture (call wzyb_prepare_device() once per device before the first capture).
+ *  - fp16 tensors are passed as uint16_t* (IEEE binary16 bit patterns, i.e. __half storage);
+ *    fp32 tensors as float*. Arithmetic is fp32; fp16 outputs are rounded to nearest-even once.
+ *  - Row-major layouts; every row / head start must be 16-byte aligned (checked).
+ *  - The kernel is enqueued on `stream` (a cudaStream_t) of the CURRENT device; the caller sets the
+ *    device, as StageGpu does with cudaSetDevice(dev).
+ *  - Return value: 0 = enqueued; > 0 = the cudaError_t of the launch; < 0 = WZYB_ERR_* argument
+ *    error detected on the host before anything was enqueued. Launchers never exit the process.
+ *  - Kernels never trap. If a device-side check fails (a position outside the RoPE table, a
+ *    bounded wait that gave up) they record a WZYB_FAULT_* bit, skip the affected work and return;
+ *    wzyb_read_faults() reports and clears those bits.
+ */
+#ifndef WZYB200_H
+#define WZYB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* wzyb_stream_t; /* identical to cudaStream_t */
+
+/* ---- status codes ------------------------------------------------------------------------ */
+#define WZYB_OK 0
+#define WZYB_ERR_NULL (-1)   /* a required pointer is NULL                                     */
+#define WZYB_ERR_ALIGN (-2)  /* a pointer / row / head start is not 16-byte aligned            */
+#define WZYB_ERR_SHAPE (-3)  /* a size is out of the supported range or inconsistent           */
+#define WZYB_ERR_DEVICE (-4) /* the current device is not an sm_100 (B200) GPU, or no device   */
+#define WZYB_ERR_VALUE (-5)  /* an enum / mode argument has an unknown value                   */
+
+/* ---- device fault bits (wzyb_read_faults) ------------------------------------------------ */
+#define WZYB_FAULT_WAIT_TIMEOUT 0x1u /* a TMA / mbarrier wait gave up after its time limit      */
+#define WZYB_FAULT_POS_RANGE 0x2u    /* a RoPE position fell outside [0, table_rows)           */
+
+/* ---- modes --------------------------------------------------------------------------------- */
+#define WZYB_GATE_SIGMOID 0 /* y = norm(o)*gamma*sigmoid(z): what the reference computes        */
+#define WZYB_GATE_SILU 1    /* y = norm(o)*gamma*z*sigmoid(z): the literal "silu(z)" reading    */
+
+#define WZYB_OOB_CLAMP 0    /* out-of-range id -> clamp to [0, vocab-1] (device gather)          */
+#define WZYB_OOB_ZERO_ID 1  /* out-of-range id -> row 0 (host gather)                            */
+
+#define WZYB_PLE_HASH_C_PRECEDENCE 0 /* row = (a ^ b ^ (c + head)) mod rows  (formula as C parses it) */
+#define WZYB_PLE_HASH_XOR_THEN_ADD 1 /* row = ((a ^ b ^ c) + head) mod rows                           */
+#define WZYB_PLE_EOS_DEFAULT 248044  /* PLE_EOS, src/wzy_kernels_v2.cuh:19                            */
+
+/* ============================================================================================
+ * Residual add + RMSNorm.
+ *   v = residual + x;  residual <- v (only when x != NULL);
+ *   y = (v * rsqrt(mean(v^2) + eps)) * (w_offset + weight)
+ * x == NULL: plain row RMSNorm of `residual` (residual is not written).
+ * w_offset = 1.0f gives the zero-centred "(1+w)" weight, 0.0f the raw weight.
+ * Shapes: x, residual, y [T, hidden]; weight [hidden]. hidden % 8 == 0, 8 <= hidden <= 16384.
+ * Replaces fused_gr_norm_multi (src/wzy_kernels_v2.cuh:409-456, launched from gr_read_fused at
+ * src/wzy_stage_v2.cuh:466) and pf_gr_norm_fp16 (src/wzy_qsa_wmma.cuh:197-232, launched at
+ * src/wzy_prefill_tc.cuh:697) in their single-stream (hc = 1, inject gate 1.0) form.
+ * ========================================================================================== */
+int wzyb_add_rmsnorm_f16(const uint16_t* x, uint16_t* residual, const uint16_t* weight, uint16_t* y,
+                         int64_t T, int hidden, float eps, float w_offset, wzyb_stream_t stream);
+
+/* Hyper-connection form with the reference's own fp32 types, argument for argument:
+ *   R [T, hc, n_embd] fp32 (in/out), w_norm [hc, n_embd], bo_prev [T, n_embd] or NULL,
+ *   inj_prev [T, hc] or NULL, xn [T, hc, n_embd].
+ *   v = R + bo_prev[t] * 2*sigmoid(inj_prev[t,c]/hc)   (gate 1.0 when inj_prev == NULL)
+ *   R <- v (when bo_prev != NULL); xn = (v * rsqrt(mean(v^2) + eps)) * w_norm[c]
+ * _f32 writes xn as fp32 (fused_gr_norm_multi, src/wzy_kernels_v2.cuh:409-456, without the
+ * optional Q8 side output); _f32_f16 writes xn as fp16 (pf_gr_norm_fp16, src/wzy_qsa_wmma.cuh:197-232). */
+int wzyb_gr_norm_f32(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, float* xn,
+                     int64_t T, int n_embd, int hc, float eps, wzyb_stream_t stream);
+int wzyb_gr_norm_f32_f16(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev,
+                         uint16_t* xn, int64_t T, int n_embd, int hc, float eps, wzyb_stream_t stream);
+
+/* ============================================================================================
+ * Per-head RMSNorm + partial NeoX RoPE, in place.
+ *   p = data + t*row_stride + h*head_stride  (h < heads, head_dim elements)
+ *   p *= rsqrt(mean(p^2) + eps) * (w_offset + gamma)           gamma [head_dim], shared by heads
+ *   for i < rot_dims/2:  (a, d) = (p[i], p[i + rot_dims/2]);
+ *       p[i] = a*cos - d*sin;  p[i + rot_dims/2] = a*sin + d*cos
+ *   cos/sin = cos_tab/sin_tab[pos * (rot_dims/2) + i], pos = (d_base_pos ? *d_base_pos : 0)
+ *             + pos_offset + t, and must lie in [0, table_rows) (else WZYB_FAULT_POS_RANGE and the
+ *             token is left un-rotated).
+ * head_dim in {64, 128, 256}; rot_dims % 16 == 0, 0 <= rot_dims <= head_dim; strides in elements.
+ * Replaces fused_head_norm_rope_multi (src/wzy_qsa_256k.cuh:50-84; launched at
+ * src/wzy_stage_v2.cuh:638-643 and src/wzy_prefill_tc.cuh:862-867), whose rot_dims is fixed at 64.
+ * ========================================================================================== */
+int wzyb_head_norm_rope_f16(uint16_t* data, const uint16_t* gamma, const float* cos_tab, const float* sin_tab,
+                            int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset, int64_t T,
+                            int heads, int head_dim, int64_t head_stride, int64_t row_stride, int rot_dims,
+                            float eps, float w_offset, wzyb_stream_t stream);
+int wzyb_head_norm_rope_f32(float* data, const float* gamma, const float* cos_tab, const float* sin_tab,
+                            int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset, int64_t T,
+                            int heads, int head_dim, int64_t head_stride, int64_t row_stride, int rot_dims,
+                            float eps, float w_offset, wzyb_stream_t stream);
+
+/* q and k of one token in ONE launch (what the reference does with two launches,
+ * src/wzy_prefill_tc.cuh:862-865). Each tensor has its own gamma, head count and strides. */
+typedef struct {
+    void* data;          /* [T, ...] fp16 (the _f16 entry point)                                 */
+    const void* gamma;   /* [head_dim]                                                            */
+    int heads;
+    int64_t head_stride; /* elements between heads of one token                                  */
+    int64_t row_stride;  /* elements between tokens                                              */
+} wzyb_head_tensor;
+
+int wzyb_qk_norm_rope_f16(const wzyb_head_tensor* q, const wzyb_head_tensor* k, const float* cos_tab,
+                          const float* sin_tab, int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset,
+                          int64_t T, int head_dim, int rot_dims, float eps, float w_offset, wzyb_stream_t stream);
+
+/* RoPE cos/sin tables [rows, rot_dims/2] fp32: angle = pos * theta^(-2i/rot_dims) in fp64, then
+ * cos/sin in fp64 rounded to fp32 -- build_rope_cos_sin_host (src/wzy_qsa_256k.cuh:33-46).
+ * _host fills host arrays (the reference's own procedure, libm); the device version fills device
+ * arrays on `stream` with CUDA's fp64 cos/sin. */
+int wzyb_rope_table_host_f32(float* h_cos, float* h_sin, int64_t rows, int rot_dims, double theta);
+int wzyb_rope_table_f32(float* d_cos, float* d_sin, int64_t rows, int rot_dims, double theta,
+                        wzyb_stream_t stream);
+
+/* ============================================================================================
+ * GDN output gated RMSNorm, per head of head_dim:
+ *   y = ((o * rsqrt(mean(o^2) + eps)) * (w_offset + gamma[col])) / (1 + exp(-z))    (SIGMOID)
+ *   y = ((o * rsqrt(mean(o^2) + eps)) * (w_offset + gamma[col])) * (z / (1 + exp(-z))) (SILU)
+ * o, z, y [T, heads, head_dim]; gamma [head_dim] shared by heads; head_dim in {64, 128, 256}.
+ * Replaces pf_gdn_rmsnorm_gate_parallel (src/wzy_qsa_wmma.cuh:178-195, launched at
+ * src/wzy_prefill_tc.cuh:845) and the gated-norm tail of fused_gdn_step_norm_multi
+ * (src/wzy_kernels_v2.cuh:966-976). The reference multiplies by sigmoid(z) at every site.
+ * ========================================================================================== */
+int wzyb_gdn_gated_norm_f16(const uint16_t* o, const uint16_t* z, const uint16_t* gamma, uint16_t* y,
+                            int64_t T, int heads, int head_dim, float eps, float w_offset, int gate_mode,
+                            wzyb_stream_t stream);
+/* fp32 o/z/gamma in, fp16 y out: pf_gdn_rmsnorm_gate_parallel's own types. */
+int wzyb_gdn_gated_norm_f32_f16(const float* o, const float* z, const float* gamma, uint16_t* y, int64_t T,
+                                int heads, int head_dim, float eps, float w_offset, int gate_mode,
+                                wzyb_stream_t stream);
+
+/* ============================================================================================
+ * SwiGLU activation  out = (g / (1 + exp(-g))) * u.
+ * Separate layout: gate, up, out [n], n % 8 == 0 -- silu_mul_multi (src/wzy_kernels_v2.cuh:1240-1244,
+ * launched at src/wzy_stage_v2.cuh:733).
+ * Interleaved layout: gu [T, 2*nff] = [gate | up] per row -> out [T, nff], nff % 8 == 0 --
+ * pf_silu_mul_interleaved_to_fp16 (src/wzy_prefill_tc.cuh:69-80, launched at :942).
+ * ========================================================================================== */
+int wzyb_swiglu_f16(const uint16_t* gate, const uint16_t* up, uint16_t* out, int64_t n, wzyb_stream_t stream);
+int wzyb_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, wzyb_stream_t stream);
+int wzyb_swiglu_interleaved_f16(const uint16_t* gu, uint16_t* out, int64_t T, int nff, wzyb_stream_t stream);
+int wzyb_swiglu_interleaved_f32_f16(const float* gu, uint16_t* out, int64_t T, int nff, wzyb_stream_t stream);
+
+/* ============================================================================================
+ * Token-embedding gather: out[t, :] = table[id(t), :], bit-exact row copy.
+ * id(t) = ids[t] when 0 <= ids[t] < vocab; otherwise clamp to [0, vocab-1] (WZYB_OOB_CLAMP, as the
+ * device gather mtp_gather_bf16_emb, src/wzy_kernels_v2.cuh:27-36) or 0 (WZYB_OOB_ZERO_ID, as the
+ * host gather stage_one_emb, src/wzy_engine_v2.cu:862-875). If d_oob_count != NULL the number of
+ * out-of-range ids is ADDED to *d_oob_count (a device uint32).
+ * _rows: any element type, row_bytes % 16 == 0.  _f16: row_bytes = 2*hidden.
+ * _bf16_f32: bf16 table -> fp32 rows, exactly mtp_gather_bf16_emb's conversion.
+ * ========================================================================================== */
+int wzyb_embed_gather_rows(const void* table, int64_t vocab, int64_t row_bytes, const int32_t* ids, int64_t T,
+                           void* out, int oob_policy, uint32_t* d_oob_count, wzyb_stream_t stream);
+int wzyb_embed_gather_f16(const uint16_t* table, int64_t vocab, int hidden, const int32_t* ids, int64_t T,
+                          uint16_t* out, int oob_policy, uint32_t* d_oob_count, wzyb_stream_t stream);
+int wzyb_embed_gather_bf16_f32(const uint16_t* table, int64_t vocab, int hidden, const int32_t* ids, int64_t T,
+                               float* out, int oob_policy, uint32_t* d_oob_count, wzyb_stream_t stream);
+
+/* ============================================================================================
+ * 16-head 3-gram PLE gather (fp16 tables).
+ *   For token i with history (t0, t1, t2) = (ids[i], ids[i-1], ids[i-2]):
+ *     history ids before the first token come from prev_ids = {id[-2], id[-1]} (host array, copied
+ *     into the launch; NULL = no history). A history id that is negative or == eos_id cuts the
+ *     context: it and every older id become eos_id (the reference's rule, src/wzy_engine_v2.cu:946-953).
+ *     a = t0*0x9E3779B1, b = t1*0x85EBCA77, c = t2*0xC2B2AE3D  (uint32 wrap-around)
+ *     row_h = (a ^ b ^ (c + h)) mod rows_per_table   (WZYB_PLE_HASH_C_PRECEDENCE)
+ *           = ((a ^ b ^ c) + h) mod rows_per_table   (WZYB_PLE_HASH_XOR_THEN_ADD)
+ *     out[i, h*head_dim : (h+1)*head_dim] = tables[h][row_h, :]
+ * tables: HOST array of `heads` device pointers (heads <= 32), each [rows_per_table, head_dim];
+ * out [T, heads*head_dim]; head_dim % 8 == 0. Bit-exact copy.
+ * Replaces the host staging loops stage_ple_window / stage_emb_ple_pf (src/wzy_engine_v2.cu:943-978,
+ * :1210-1265) with the table format and hash of the fp16 synthetic configuration.
+ * ========================================================================================== */
+int wzyb_ple_gather_f16(const uint16_t* const* tables, int heads, int64_t rows_per_table, int head_dim,
+                        const int32_t* ids, int64_t T, const int32_t* prev_ids, int32_t eos_id, int hash_variant,
+                        uint16_t* out, wzyb_stream_t stream);
+
+/* Host restatement of the row index (for halos, tests and callers that stage on the host). */
+uint32_t wzyb_ple_row_index(int32_t t0, int32_t t1, int32_t t2, int head, int64_t rows_per_table,
+                            int32_t eos_id, int hash_variant);
+
+/* ============================================================================================
+ * Layer bundles: the host-side executor issues the path's kernels in the order the reference's
+ * prefill executor does (src/wzy_prefill_tc.cuh:697 norm, :862-867 q/k norm+RoPE, :942 SwiGLU,
+ * :845 GDN gated norm), with the q and k tensors fused into one launch.
+ * ========================================================================================== */
+typedef struct {
+    /* residual add + RMSNorm, [T, hidden] */
+    const uint16_t* x;
+    uint16_t* residual;
+    const uint16_t* norm_weight;
+    uint16_t* normed;
+    int hidden;
+    /* q/k norm + RoPE, in place */
+    wzyb_head_tensor q;
+    wzyb_head_tensor k;
+    int head_dim;
+    int rot_dims;
+    const float* cos_tab;
+    const float* sin_tab;
+    int64_t table_rows;
+    const int32_t* d_base_pos;
+    int64_t pos_offset;
+    float eps;
+    float w_offset; /* applied to norm_weight and the q/k gammas */
+} wzyb_attn_prep_args;
+
+typedef struct {
+    /* SwiGLU over act_rows rows of ffn elements (routed + shared expert rows) */
+    const uint16_t* gate;
+    const uint16_t* up;
+    uint16_t* act;
+    int64_t act_rows;
+    int ffn;
+    /* GDN gated norm over T tokens of gdn_heads x gdn_head_dim */
+    const uint16_t* o;
+    const uint16_t* z;
+    const uint16_t* gdn_gamma;
+    uint16_t* gdn_out;
+    int gdn_heads;
+    int gdn_head_dim;
+    float eps;
+    float gdn_w_offset;
+    int gate_mode;
+} wzyb_act_args;
+
+int wzyb_attn_prep_f16(const wzyb_attn_prep_args* a, int64_t T, wzyb_stream_t stream);
+int wzyb_act_f16(const wzyb_act_args* a, int64_t T, wzyb_stream_t stream);
+
+/* Token-row sharding for G independent GPUs (no collective): rank r gets rows
+ * [row0, row0 + rows) of a contiguous ceil(total/G) split. */
+int wzyb_shard_rows(int64_t total, int world, int rank, int64_t* row0, int64_t* rows);
+/* PLE history halo for a shard starting at row0 of host ids[]: out_prev = {id[row0-2], id[row0-1]},
+ * taking ids before the sequence from seq_prev (2 ids, or NULL = none = -1). */
+int wzyb_ple_halo(const int32_t* ids, int64_t row0, const int32_t* seq_prev, int32_t out_prev[2]);
+
+/* ============================================================================================
+ * Runtime helpers.
+ * ========================================================================================== */
+/* One-time per-device set-up (device check, SM count, shared-memory opt-in). Launchers call it
+ * lazily; call it explicitly before capturing a stream into a CUDA graph. */
+int wzyb_prepare_device(void);
+/* Read the current device's fault bits (synchronous); clears them when clear != 0. */
+int wzyb_read_faults(uint32_t* faults, int clear);
+/* Launch-shape tuning per kernel family (process-wide): CTAs per SM (1..16) and TMA ring depth
+ * (0 = as deep as the shared-memory budget allows, else 1..64 stages).
+ * Families: 0 add+RMSNorm, 1 head norm+RoPE, 2 GDN gated norm, 3 SwiGLU, 4 gathers. */
+#define WZYB_FAM_NORM 0
+#define WZYB_FAM_HEAD_ROPE 1
+#define WZYB_FAM_GDN 2
+#define WZYB_FAM_SWIGLU 3
+#define WZYB_FAM_GATHER 4
+int wzyb_set_launch_tuning(int family, int ctas_per_sm, int stages);
+const char* wzyb_status_string(int status);
+int wzyb_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WZYB200_H */

@@ -1,0 +1,219 @@
+"""TEST INFRASTRUCTURE ONLY: numpy/ctypes binding of the CPU oracle (liboracle.so) and of the
+reference's own kernels built from its sources (_ref/libwzyref.so).
+
+Imported by tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg only -- as the checker,
+never as the measured or shipped path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_double, c_float, c_int, c_int32, c_int64, c_uint16, c_uint32, c_void_p
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_PATH = os.path.join(HERE, "liboracle.so")
+REF_PATH = os.path.join(HERE, "_ref", "libwzyref.so")
+
+P = c_void_p
+_SIGS = {
+    "or_h2f": (c_float, [c_uint16]),
+    "or_f2h": (c_uint16, [c_float]),
+    "or_h2f_array": (None, [P, P, c_int64]),
+    "or_f2h_array": (None, [P, P, c_int64]),
+    "or_set_threads": (None, [c_int]),
+    "or_get_threads": (c_int, []),
+    "or_add_rmsnorm_f16": (None, [P, P, P, P, c_int64, c_int, c_float, c_float]),
+    "or_gr_norm_f32": (None, [P, P, P, P, P, P, c_int64, c_int, c_int, c_float]),
+    "or_head_norm_rope_f16": (
+        None, [P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, c_int64, c_int64, c_int, c_float, c_float]),
+    "or_head_norm_rope_f32": (
+        None, [P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, c_int64, c_int64, c_int, c_float, c_float]),
+    "or_rope_table": (None, [P, P, c_int64, c_int, c_double]),
+    "or_gdn_gated_norm_f16": (None, [P, P, P, P, c_int64, c_int, c_int, c_float, c_float, c_int]),
+    "or_gdn_gated_norm_f32": (None, [P, P, P, P, c_int64, c_int, c_int, c_float, c_float, c_int]),
+    "or_swiglu_f16": (None, [P, P, P, c_int64]),
+    "or_swiglu_f32": (None, [P, P, P, c_int64]),
+    "or_swiglu_interleaved_f16": (None, [P, P, c_int64, c_int]),
+    "or_swiglu_interleaved_f32": (None, [P, P, c_int64, c_int]),
+    "or_embed_gather_rows": (c_uint32, [P, c_int64, c_int64, P, c_int64, P, c_int]),
+    "or_embed_gather_bf16_f32": (c_uint32, [P, c_int64, c_int, P, c_int64, P, c_int]),
+    "or_ple_row": (c_uint32, [c_int32, c_int32, c_int32, c_int, c_int64, c_int32, c_int]),
+    "or_ple_gather_f16": (None, [POINTER(c_void_p), c_int, c_int64, c_int, P, c_int64, POINTER(c_int32), c_int32,
+                                 c_int, P]),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(ORACLE_PATH):
+            raise OSError(f"{ORACLE_PATH} is missing: build it with `make -C oracle`")
+        L = ctypes.CDLL(ORACLE_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return a.ctypes.data_as(c_void_p) if a is not None else None
+
+
+def set_threads(n: int) -> None:
+    lib().or_set_threads(n)
+
+
+def get_threads() -> int:
+    return lib().or_get_threads()
+
+
+# ---- numpy wrappers; fp16 tensors are np.float16 arrays (bit patterns passed as uint16) --------
+def add_rmsnorm_f16(x, res, w, eps=1e-6, w_offset=1.0):
+    """Returns (y, res_out); inputs are not modified."""
+    res_out = np.array(res, dtype=np.float16, copy=True)
+    y = np.empty_like(res_out)
+    T, n = res_out.shape
+    xx = np.ascontiguousarray(x, dtype=np.float16) if x is not None else None
+    lib().or_add_rmsnorm_f16(_p(xx), _p(res_out), _p(np.ascontiguousarray(w, dtype=np.float16)), _p(y), T, n, eps,
+                             w_offset)
+    return y, res_out
+
+
+def gr_norm_f32(R, w, bo, inj, T, n, hc, eps=1e-6):
+    """fp32 hyper-connection norm; returns (xn_f32, xn_f16, R_out)."""
+    R_out = np.array(R, dtype=np.float32, copy=True)
+    xn = np.empty((T * hc, n), dtype=np.float32)
+    xh = np.empty((T * hc, n), dtype=np.float16)
+    lib().or_gr_norm_f32(_p(R_out), _p(np.ascontiguousarray(w, np.float32)),
+                         _p(np.ascontiguousarray(bo, np.float32)) if bo is not None else None,
+                         _p(np.ascontiguousarray(inj, np.float32)) if inj is not None else None,
+                         _p(xn), _p(xh), T, n, hc, eps)
+    return xn, xh, R_out
+
+
+def rope_table(rows, rot=64, theta=1e7):
+    half = rot // 2
+    c = np.empty((rows, half), dtype=np.float32)
+    s = np.empty((rows, half), dtype=np.float32)
+    lib().or_rope_table(_p(c), _p(s), rows, rot, theta)
+    return c, s
+
+
+def head_norm_rope(data, gamma, cos_tab, sin_tab, T, heads, hd, head_stride, row_stride, rot=64, eps=1e-6,
+                   w_offset=0.0, base_pos=0):
+    """In-place op on a copy of `data` (fp16 or fp32 flat array); returns the copy."""
+    out = np.array(data, copy=True)
+    rows = cos_tab.shape[0] if cos_tab is not None else 0
+    fn = lib().or_head_norm_rope_f16 if out.dtype == np.float16 else lib().or_head_norm_rope_f32
+    fn(_p(out), _p(np.ascontiguousarray(gamma, out.dtype)), _p(cos_tab), _p(sin_tab), rows, base_pos, T, heads, hd,
+       head_stride, row_stride, rot, eps, w_offset)
+    return out
+
+
+def gdn_gated_norm(o, z, gamma, T, heads, hd=128, eps=1e-6, w_offset=0.0, gate_mode=0):
+    if o.dtype == np.float16:
+        y = np.empty(o.shape, dtype=np.float16)
+        lib().or_gdn_gated_norm_f16(_p(o), _p(z), _p(np.ascontiguousarray(gamma, np.float16)), _p(y), T, heads, hd,
+                                    eps, w_offset, gate_mode)
+    else:
+        y = np.empty(o.shape, dtype=np.float32)
+        lib().or_gdn_gated_norm_f32(_p(o), _p(z), _p(np.ascontiguousarray(gamma, np.float32)), _p(y), T, heads, hd,
+                                    eps, w_offset, gate_mode)
+    return y
+
+
+def swiglu(g, u):
+    out = np.empty(g.shape, dtype=g.dtype)
+    fn = lib().or_swiglu_f16 if g.dtype == np.float16 else lib().or_swiglu_f32
+    fn(_p(np.ascontiguousarray(g)), _p(np.ascontiguousarray(u)), _p(out), g.size)
+    return out
+
+
+def swiglu_interleaved(gu, T, nff):
+    out = np.empty((T, nff), dtype=gu.dtype)
+    fn = lib().or_swiglu_interleaved_f16 if gu.dtype == np.float16 else lib().or_swiglu_interleaved_f32
+    fn(_p(np.ascontiguousarray(gu)), _p(out), T, nff)
+    return out
+
+
+def embed_gather_rows(table, ids, oob_policy=0):
+    vocab = table.shape[0]
+    row_bytes = table[0].nbytes
+    out = np.empty((ids.size,) + table.shape[1:], dtype=table.dtype)
+    bad = lib().or_embed_gather_rows(_p(np.ascontiguousarray(table)), vocab, row_bytes,
+                                     _p(np.ascontiguousarray(ids, np.int32)), ids.size, _p(out), oob_policy)
+    return out, int(bad)
+
+
+def embed_gather_bf16_f32(table_bits, ids, oob_policy=0):
+    vocab, hidden = table_bits.shape
+    out = np.empty((ids.size, hidden), dtype=np.float32)
+    bad = lib().or_embed_gather_bf16_f32(_p(np.ascontiguousarray(table_bits, np.uint16)), vocab, hidden,
+                                         _p(np.ascontiguousarray(ids, np.int32)), ids.size, _p(out), oob_policy)
+    return out, int(bad)
+
+
+def ple_row(t0, t1, t2, head, rows, eos=248044, variant=0) -> int:
+    return int(lib().or_ple_row(t0, t1, t2, head, rows, eos, variant))
+
+
+def ple_gather_f16(tables, ids, prev_ids=None, eos=248044, variant=0):
+    heads = len(tables)
+    rows, hd = tables[0].shape
+    arr = (c_void_p * heads)(*[t.ctypes.data for t in tables])
+    prev = (c_int32 * 2)(*prev_ids) if prev_ids is not None else None
+    ids = np.ascontiguousarray(ids, np.int32)
+    out = np.empty((ids.size, heads * hd), dtype=np.float16)
+    lib().or_ple_gather_f16(arr, heads, rows, hd, _p(ids), ids.size, prev, eos, variant, _p(out))
+    return out
+
+
+# ---- the reference's own kernels (GPU) and host table builder --------------------------------
+_ref = None
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_PATH)
+
+
+def ref_lib() -> ctypes.CDLL:
+    global _ref
+    if _ref is None:
+        L = ctypes.CDLL(REF_PATH)
+        I = c_int
+        F = c_float
+        sigs = {
+            "ref_fused_gr_norm_multi": [P, P, P, P, P, I, I, I, F, P],
+            "ref_pf_gr_norm_fp16": [P, P, P, P, P, I, I, I, F, P],
+            "ref_gr_write_multi": [P, P, P, I, I, I, P],
+            "ref_fused_head_norm_rope_multi": [P, P, P, P, P, I, I, I, I, I, F, P],
+            "ref_pf_gdn_rmsnorm_gate_parallel": [P, P, P, P, I, I, F, P],
+            "ref_silu_mul_multi": [P, P, P, I, P],
+            "ref_pf_silu_mul_interleaved_to_fp16": [P, P, I, I, P],
+            "ref_mtp_gather_bf16_emb": [P, P, P, I, P],
+            "ref_ple_group_multi": [P, P, P, I, I, I, F, P],
+        }
+        for name, args in sigs.items():
+            fn = getattr(L, name)
+            fn.restype = c_int
+            fn.argtypes = args
+        L.ref_build_rope_cos_sin_host.restype = None
+        L.ref_build_rope_cos_sin_host.argtypes = [I, F, P, P]
+        L.ref_dims.restype = c_int
+        L.ref_dims.argtypes = [POINTER(c_int), POINTER(c_int)]
+        _ref = L
+    return _ref
+
+
+def ref_rope_table(rows, theta=1e7):
+    """The reference's own host builder (32 pairs = rot 64)."""
+    c = np.empty((rows, 32), dtype=np.float32)
+    s = np.empty((rows, 32), dtype=np.float32)
+    ref_lib().ref_build_rope_cos_sin_host(rows, theta, _p(c), _p(s))
+    return c, s

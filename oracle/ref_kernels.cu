@@ -1,0 +1,88 @@
+// ref_kernels.cu -- TEST INFRASTRUCTURE ONLY: extern "C" launchers for the reference's OWN
+// elementwise kernels, compiled from its unmodified headers (include path = the reference's src/).
+// Used by the GPU parity tests to pin the CPU oracle against the reference itself, and never by the
+// product library. Launch shapes are the reference's own (grid/block as at its call sites).
+// Same include order as the reference engine (src/wzy_engine_v2.cu), since wzy_prefill_tc.cuh
+// uses helpers from wzy_mtp.cuh.
+#include "wzy_stage_v2.cuh"
+#include "wzy_mtp.cuh"
+#include "wzy_prefill_tc.cuh"
+
+extern "C" {
+
+// fused_gr_norm_multi (src/wzy_kernels_v2.cuh:409-456), launched as in gr_read_fused
+// (src/wzy_stage_v2.cuh:466): grid (hc, T) x 256.
+int ref_fused_gr_norm_multi(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, float* xn,
+                            int T, int n_embd, int hc, float eps, cudaStream_t s) {
+    fused_gr_norm_multi<<<dim3(hc, T), 256, 0, s>>>(R, w_norm, bo_prev, inj_prev, xn, n_embd, hc, eps, nullptr,
+                                                     nullptr);
+    return (int)cudaGetLastError();
+}
+
+// pf_gr_norm_fp16 (src/wzy_qsa_wmma.cuh:197-232), launched as at src/wzy_prefill_tc.cuh:697.
+int ref_pf_gr_norm_fp16(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, __half* xn, int T,
+                        int n_embd, int hc, float eps, cudaStream_t s) {
+    pf_gr_norm_fp16<<<dim3(hc, T), 256, 0, s>>>(R, w_norm, bo_prev, inj_prev, xn, n_embd, hc, eps);
+    return (int)cudaGetLastError();
+}
+
+// gr_write_multi (src/wzy_kernels_v2.cuh:813-828), launched as at src/wzy_stage_v2.cuh:692: grid (80, T) x 256.
+int ref_gr_write_multi(float* R, const float* blk, const float* inj, int T, int n_embd, int hc, cudaStream_t s) {
+    gr_write_multi<<<dim3(80, T), 256, 0, s>>>(R, blk, inj, n_embd, hc);
+    return (int)cudaGetLastError();
+}
+
+// fused_head_norm_rope_multi (src/wzy_qsa_256k.cuh:50-84), grid (heads, T) x 128 (T <= 65535).
+int ref_fused_head_norm_rope_multi(float* data, const float* gamma, const float* cos_tab, const float* sin_tab,
+                                   const int* base_pos_dev, int T, int heads, int hd, int head_stride, int row_stride,
+                                   float eps, cudaStream_t s) {
+    fused_head_norm_rope_multi<<<dim3(heads, T), 128, 0, s>>>(data, gamma, cos_tab, sin_tab, base_pos_dev, heads, hd,
+                                                              head_stride, row_stride, eps);
+    return (int)cudaGetLastError();
+}
+
+// build_rope_cos_sin_host (src/wzy_qsa_256k.cuh:33-46): the reference's host table (32 pairs).
+void ref_build_rope_cos_sin_host(int max_ctx, float theta, float* h_cos, float* h_sin) {
+    build_rope_cos_sin_host(max_ctx, theta, h_cos, h_sin);
+}
+
+// pf_gdn_rmsnorm_gate_parallel (src/wzy_qsa_wmma.cuh:178-195), grid (hv, T) x 128.
+int ref_pf_gdn_rmsnorm_gate_parallel(const float* o, const float* z, const float* gamma, __half* y, int T, int hv,
+                                     float eps, cudaStream_t s) {
+    pf_gdn_rmsnorm_gate_parallel<<<dim3(hv, T), 128, 0, s>>>(o, z, gamma, y, hv, eps);
+    return (int)cudaGetLastError();
+}
+
+// silu_mul_multi (src/wzy_kernels_v2.cuh:1240-1244), launched as at src/wzy_stage_v2.cuh:733.
+int ref_silu_mul_multi(const float* gate, const float* up, float* out, int total, cudaStream_t s) {
+    silu_mul_multi<<<(total + 255) / 256, 256, 0, s>>>(gate, up, out, total);
+    return (int)cudaGetLastError();
+}
+
+// pf_silu_mul_interleaved_to_fp16 (src/wzy_prefill_tc.cuh:69-80), launched as at :942.
+int ref_pf_silu_mul_interleaved_to_fp16(const float* gu, __half* out, int T, int nff, cudaStream_t s) {
+    pf_silu_mul_interleaved_to_fp16<<<(int)((((size_t)T * nff + 1) / 2 + 255) / 256), 256, 0, s>>>(gu, out, T, nff);
+    return (int)cudaGetLastError();
+}
+
+// mtp_gather_bf16_emb (src/wzy_kernels_v2.cuh:27-36): table [NVOCAB=248320, NE=2560] bf16, launched as at
+// src/wzy_stage_v2.cuh:567-568.
+int ref_mtp_gather_bf16_emb(const uint16_t* table, const int* toks, float* out, int T, cudaStream_t s) {
+    mtp_gather_bf16_emb<<<dim3((NE + 255) / 256, T), 256, 0, s>>>(table, toks, out, T);
+    return (int)cudaGetLastError();
+}
+
+// ple_group_multi (src/wzy_kernels_v2.cuh:1299-1319): row RMSNorm twin, grid (hc, T) x 256.
+int ref_ple_group_multi(const float* x, const float* gamma, float* y, int T, int n_embd, int hc, float eps,
+                        cudaStream_t s) {
+    ple_group_multi<<<dim3(hc, T), 256, 0, s>>>(x, gamma, y, n_embd, hc, eps);
+    return (int)cudaGetLastError();
+}
+
+int ref_dims(int* ne, int* nvocab) {
+    *ne = NE;
+    *nvocab = NVOCAB;
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,344 @@
+/*
+ * wzyb_oracle.c -- CPU restatement of wzy-flash-serve's per-layer elementwise math.
+ *
+ * TEST INFRASTRUCTURE ONLY: the parity checker and the timed CPU baseline. Nothing in the product
+ * library links or loads it. Each function names the reference lines it restates.
+ *
+ * Build: gcc -O3 -march=x86-64-v2 -ffp-contract=off -fopenmp -shared -fPIC (oracle/Makefile).
+ */
+#include "wzyb_oracle.h"
+
+#include <math.h>
+#include <omp.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------------------------------- */
+/* IEEE binary16 <-> binary32                                                                  */
+/* ------------------------------------------------------------------------------------------- */
+float or_h2f(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    const uint32_t e = (h >> 10) & 0x1Fu;
+    const uint32_t m = h & 0x3FFu;
+    uint32_t bits;
+    if (e == 0x1F) {
+        bits = sign | 0x7F800000u | (m << 13);
+    } else if (e != 0) {
+        bits = sign | ((e + 112u) << 23) | (m << 13);
+    } else if (m == 0) {
+        bits = sign;
+    } else { /* subnormal: m * 2^-24, exact in float */
+        const float v = (float)m * 5.9604644775390625e-08f;
+        float out = (sign ? -v : v);
+        return out;
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+/* round-to-nearest-even, overflow to inf, NaN kept quiet */
+uint16_t or_f2h(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    const uint16_t sign = (uint16_t)((x >> 16) & 0x8000u);
+    const uint32_t ax = x & 0x7FFFFFFFu;
+    if (ax >= 0x7F800000u) return (uint16_t)(sign | 0x7C00u | (ax > 0x7F800000u ? 0x200u : 0u));
+    if (ax >= 0x477FF000u) return (uint16_t)(sign | 0x7C00u); /* >= 65520 rounds to inf */
+    if (ax < 0x38800000u) {                                  /* below 2^-14: subnormal or zero */
+        float a;
+        memcpy(&a, &ax, 4);
+        const float s = a * 16777216.0f; /* exact: scaling by 2^24 */
+        return (uint16_t)(sign | (uint16_t)rintf(s));
+    }
+    const uint32_t e = (ax >> 23) - 112u;
+    const uint32_t mant = ax & 0x7FFFFFu;
+    uint32_t h = (e << 10) | (mant >> 13);
+    const uint32_t rem = mant & 0x1FFFu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h += 1u;
+    return (uint16_t)(sign | h);
+}
+
+void or_h2f_array(const uint16_t* in, float* out, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) out[i] = or_h2f(in[i]);
+}
+
+void or_f2h_array(const float* in, uint16_t* out, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) out[i] = or_f2h(in[i]);
+}
+
+void or_set_threads(int n) { omp_set_num_threads(n > 0 ? n : 1); }
+int or_get_threads(void) { return omp_get_max_threads(); }
+
+static inline float sigmoid_den(float z) { return 1.0f + expf(-z); }
+
+/* ------------------------------------------------------------------------------------------- */
+/* residual add + RMSNorm                                                                      */
+/* fused_gr_norm_multi (src/wzy_kernels_v2.cuh:409-456) / pf_gr_norm_fp16                      */
+/* (src/wzy_qsa_wmma.cuh:197-232): v = R + bo*gw; R <- v; xn = (v * rsqrt(sum(v^2)/n + eps)) * g */
+/* with gw = 2*sigmoid(inj/hc) (:419), == 1.0 for the single-stream add.                        */
+/* ------------------------------------------------------------------------------------------- */
+void or_add_rmsnorm_f16(const uint16_t* x, uint16_t* res, const uint16_t* w, uint16_t* y, int64_t T, int n,
+                        float eps, float w_offset) {
+#pragma omp parallel
+    {
+        float* v = (float*)malloc(sizeof(float) * (size_t)n);
+#pragma omp for schedule(static)
+        for (int64_t t = 0; t < T; ++t) {
+            uint16_t* r = res + t * n;
+            double ss = 0.0;
+            for (int d = 0; d < n; ++d) {
+                float val = or_h2f(r[d]);
+                if (x) val = val + or_h2f(x[t * n + d]);
+                v[d] = val;
+                ss += (double)val * (double)val;
+            }
+            const float sc = 1.0f / sqrtf((float)ss / (float)n + eps);
+            for (int d = 0; d < n; ++d) {
+                const float g = w_offset + or_h2f(w[d]);
+                y[t * n + d] = or_f2h((v[d] * sc) * g);
+                if (x) r[d] = or_f2h(v[d]);
+            }
+        }
+        free(v);
+    }
+}
+
+void or_gr_norm_f32(float* R, const float* w, const float* bo, const float* inj, float* xn, uint16_t* xn_h16,
+                    int64_t T, int n, int hc, float eps) {
+#pragma omp parallel for schedule(static)
+    for (int64_t u = 0; u < T * hc; ++u) {
+        const int64_t t = u / hc;
+        const int c = (int)(u % hc);
+        float* rc = R + u * n;
+        const float* gc = w + (int64_t)c * n;
+        const float gw = bo ? (inj ? 2.0f / (1.0f + expf(-inj[u] / (float)hc)) : 1.0f) : 0.0f;
+        double ss = 0.0;
+        for (int d = 0; d < n; ++d) {
+            float val = rc[d];
+            if (bo) {
+                val = val + bo[t * n + d] * gw;
+                rc[d] = val;
+            }
+            ss += (double)val * (double)val;
+        }
+        const float sc = 1.0f / sqrtf((float)ss / (float)n + eps);
+        for (int d = 0; d < n; ++d) {
+            const float yn = (rc[d] * sc) * gc[d];
+            if (xn) xn[u * n + d] = yn;
+            if (xn_h16) xn_h16[u * n + d] = or_f2h(yn);
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------------------------- */
+/* per-head RMSNorm + partial NeoX RoPE: fused_head_norm_rope_multi (src/wzy_qsa_256k.cuh:50-84) */
+/*   p *= rsqrt(sum(p^2)/hd + eps) * gamma;  (a, d) = (p[i], p[i+R/2])                          */
+/*   p[i] = a*cos - d*sin;  p[i+R/2] = a*sin + d*cos, cos/sin = tab[pos*(R/2) + i]              */
+/* A position outside the table leaves the head un-rotated (the CUDA path flags it).            */
+/* ------------------------------------------------------------------------------------------- */
+static void head_norm_rope_row(float* p, const float* g, const float* cos_tab, const float* sin_tab,
+                               int64_t table_rows, int64_t pos, int hd, int rot, float eps) {
+    double ss = 0.0;
+    for (int i = 0; i < hd; ++i) ss += (double)p[i] * (double)p[i];
+    const float sc = 1.0f / sqrtf((float)ss / (float)hd + eps);
+    for (int i = 0; i < hd; ++i) p[i] *= sc * g[i];
+    const int half = rot / 2;
+    if (half == 0 || pos < 0 || pos >= table_rows) return;
+    for (int i = 0; i < half; ++i) {
+        const float cs = cos_tab[pos * half + i], sn = sin_tab[pos * half + i];
+        const float a = p[i], d = p[i + half];
+        p[i] = a * cs - d * sn;
+        p[i + half] = a * sn + d * cs;
+    }
+}
+
+void or_head_norm_rope_f16(uint16_t* data, const uint16_t* gamma, const float* cos_tab, const float* sin_tab,
+                           int64_t table_rows, int64_t base_pos, int64_t T, int heads, int hd, int64_t head_stride,
+                           int64_t row_stride, int rot, float eps, float w_offset) {
+    float g[1024];
+    for (int i = 0; i < hd; ++i) g[i] = w_offset + or_h2f(gamma[i]);
+#pragma omp parallel for schedule(static)
+    for (int64_t th = 0; th < T * heads; ++th) {
+        const int64_t t = th / heads;
+        const int h = (int)(th % heads);
+        uint16_t* p = data + t * row_stride + (int64_t)h * head_stride;
+        float buf[1024];
+        for (int i = 0; i < hd; ++i) buf[i] = or_h2f(p[i]);
+        head_norm_rope_row(buf, g, cos_tab, sin_tab, table_rows, base_pos + t, hd, rot, eps);
+        for (int i = 0; i < hd; ++i) p[i] = or_f2h(buf[i]);
+    }
+}
+
+void or_head_norm_rope_f32(float* data, const float* gamma, const float* cos_tab, const float* sin_tab,
+                           int64_t table_rows, int64_t base_pos, int64_t T, int heads, int hd, int64_t head_stride,
+                           int64_t row_stride, int rot, float eps, float w_offset) {
+    float g[1024];
+    for (int i = 0; i < hd; ++i) g[i] = w_offset + gamma[i];
+#pragma omp parallel for schedule(static)
+    for (int64_t th = 0; th < T * heads; ++th) {
+        const int64_t t = th / heads;
+        const int h = (int)(th % heads);
+        head_norm_rope_row(data + t * row_stride + (int64_t)h * head_stride, g, cos_tab, sin_tab, table_rows,
+                           base_pos + t, hd, rot, eps);
+    }
+}
+
+/* build_rope_cos_sin_host (src/wzy_qsa_256k.cuh:33-46): inv_i = theta^(-2i/R) in fp64,        */
+/* angle = p * inv_i in fp64, cos/sin in fp64 rounded to fp32; layout [p][R/2].                 */
+void or_rope_table(float* cos_tab, float* sin_tab, int64_t rows, int rot, double theta) {
+    const int half = rot / 2;
+    double inv[512];
+    for (int i = 0; i < half; ++i) inv[i] = pow(theta, -2.0 * (double)i / (double)rot);
+#pragma omp parallel for schedule(static)
+    for (int64_t p = 0; p < rows; ++p) {
+        for (int i = 0; i < half; ++i) {
+            const double ang = (double)p * inv[i];
+            cos_tab[p * half + i] = (float)cos(ang);
+            sin_tab[p * half + i] = (float)sin(ang);
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------------------------- */
+/* GDN gated RMSNorm: pf_gdn_rmsnorm_gate_parallel (src/wzy_qsa_wmma.cuh:178-195)               */
+/*   y = o * rsqrt(sum(o^2) * (1/hd) + eps) * gamma[col] / (1 + exp(-z))                        */
+/* ------------------------------------------------------------------------------------------- */
+static inline float gdn_out(float o, float sc, float g, float z, int gate_mode) {
+    const float den = sigmoid_den(z);
+    return gate_mode == 1 ? (o * sc * g) * (z / den) : o * sc * g / den;
+}
+
+void or_gdn_gated_norm_f16(const uint16_t* o, const uint16_t* z, const uint16_t* gamma, uint16_t* y, int64_t T,
+                           int heads, int hd, float eps, float w_offset, int gate_mode) {
+    float g[1024];
+    for (int i = 0; i < hd; ++i) g[i] = w_offset + or_h2f(gamma[i]);
+#pragma omp parallel for schedule(static)
+    for (int64_t th = 0; th < T * heads; ++th) {
+        const int64_t base = th * hd;
+        double ss = 0.0;
+        for (int i = 0; i < hd; ++i) {
+            const double v = (double)or_h2f(o[base + i]);
+            ss += v * v;
+        }
+        const float sc = 1.0f / sqrtf((float)ss * (1.0f / (float)hd) + eps);
+        for (int i = 0; i < hd; ++i)
+            y[base + i] = or_f2h(gdn_out(or_h2f(o[base + i]), sc, g[i], or_h2f(z[base + i]), gate_mode));
+    }
+}
+
+void or_gdn_gated_norm_f32(const float* o, const float* z, const float* gamma, float* y, int64_t T, int heads, int hd,
+                           float eps, float w_offset, int gate_mode) {
+#pragma omp parallel for schedule(static)
+    for (int64_t th = 0; th < T * heads; ++th) {
+        const int64_t base = th * hd;
+        double ss = 0.0;
+        for (int i = 0; i < hd; ++i) ss += (double)o[base + i] * (double)o[base + i];
+        const float sc = 1.0f / sqrtf((float)ss * (1.0f / (float)hd) + eps);
+        for (int i = 0; i < hd; ++i)
+            y[base + i] = gdn_out(o[base + i], sc, w_offset + gamma[i], z[base + i], gate_mode);
+    }
+}
+
+/* ------------------------------------------------------------------------------------------- */
+/* SwiGLU: silu_mul_multi (src/wzy_kernels_v2.cuh:1240-1244) (g / (1 + exp(-g))) * u;           */
+/* interleaved rows [gate | up]: pf_silu_mul_interleaved_to_fp16 (src/wzy_prefill_tc.cuh:69-80)  */
+/* ------------------------------------------------------------------------------------------- */
+static inline float swiglu1(float g, float u) { return (g / sigmoid_den(g)) * u; }
+
+void or_swiglu_f16(const uint16_t* g, const uint16_t* u, uint16_t* out, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) out[i] = or_f2h(swiglu1(or_h2f(g[i]), or_h2f(u[i])));
+}
+
+void or_swiglu_f32(const float* g, const float* u, float* out, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) out[i] = swiglu1(g[i], u[i]);
+}
+
+void or_swiglu_interleaved_f16(const uint16_t* gu, uint16_t* out, int64_t T, int nff) {
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < T; ++t)
+        for (int c = 0; c < nff; ++c)
+            out[t * nff + c] = or_f2h(swiglu1(or_h2f(gu[t * 2 * nff + c]), or_h2f(gu[t * 2 * nff + nff + c])));
+}
+
+void or_swiglu_interleaved_f32(const float* gu, float* out, int64_t T, int nff) {
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < T; ++t)
+        for (int c = 0; c < nff; ++c) out[t * nff + c] = swiglu1(gu[t * 2 * nff + c], gu[t * 2 * nff + nff + c]);
+}
+
+/* ------------------------------------------------------------------------------------------- */
+/* token-embedding gather: out-of-range id -> 0 as stage_one_emb (src/wzy_engine_v2.cu:863) or  */
+/* clamped as mtp_gather_bf16_emb (src/wzy_kernels_v2.cuh:30)                                   */
+/* ------------------------------------------------------------------------------------------- */
+static inline int64_t resolve_id(int32_t id, int64_t vocab, int policy) {
+    if (id >= 0 && id < vocab) return id;
+    if (policy == 1) return 0;
+    return id < 0 ? 0 : vocab - 1;
+}
+
+uint32_t or_embed_gather_rows(const void* table, int64_t vocab, int64_t row_bytes, const int32_t* ids, int64_t T,
+                              void* out, int oob_policy) {
+    uint32_t bad = 0;
+#pragma omp parallel for schedule(static) reduction(+ : bad)
+    for (int64_t t = 0; t < T; ++t) {
+        if (!(ids[t] >= 0 && ids[t] < vocab)) ++bad;
+        const int64_t id = resolve_id(ids[t], vocab, oob_policy);
+        memcpy((char*)out + t * row_bytes, (const char*)table + id * row_bytes, (size_t)row_bytes);
+    }
+    return bad;
+}
+
+/* bf16 -> fp32 by placing the 16 bits in the high half: db2f (src/wzy_kernels_v2.cuh:23) */
+uint32_t or_embed_gather_bf16_f32(const uint16_t* table, int64_t vocab, int hidden, const int32_t* ids, int64_t T,
+                                  float* out, int oob_policy) {
+    uint32_t bad = 0;
+#pragma omp parallel for schedule(static) reduction(+ : bad)
+    for (int64_t t = 0; t < T; ++t) {
+        if (!(ids[t] >= 0 && ids[t] < vocab)) ++bad;
+        const int64_t id = resolve_id(ids[t], vocab, oob_policy);
+        for (int d = 0; d < hidden; ++d) {
+            const uint32_t bits = (uint32_t)table[id * hidden + d] << 16;
+            memcpy(&out[t * hidden + d], &bits, 4);
+        }
+    }
+    return bad;
+}
+
+/* ------------------------------------------------------------------------------------------- */
+/* 3-gram PLE row index. History cut as stage_ple_window builds ctx[1..2]                        */
+/* (src/wzy_engine_v2.cu:946-953): an id < 0 or == EOS cuts, and it and all older ids become EOS. */
+/* Mix: a = t0*0x9E3779B1, b = t1*0x85EBCA77, c = t2*0xC2B2AE3D (uint32),                         */
+/* row = (a ^ b ^ (c + head)) mod rows [variant 0] or ((a ^ b ^ c) + head) mod rows [variant 1]. */
+/* ------------------------------------------------------------------------------------------- */
+uint32_t or_ple_row(int32_t t0, int32_t t1, int32_t t2, int head, int64_t rows, int32_t eos, int variant) {
+    int32_t ctx1, ctx2;
+    int cut = (t1 < 0 || t1 == eos);
+    ctx1 = cut ? eos : t1;
+    cut = cut || (t2 < 0 || t2 == eos);
+    ctx2 = cut ? eos : t2;
+    const uint32_t a = (uint32_t)t0 * 0x9E3779B1u;
+    const uint32_t b = (uint32_t)ctx1 * 0x85EBCA77u;
+    const uint32_t c = (uint32_t)ctx2 * 0xC2B2AE3Du;
+    const uint32_t h = variant == 1 ? ((a ^ b ^ c) + (uint32_t)head) : (a ^ b ^ (c + (uint32_t)head));
+    return (uint32_t)((uint64_t)h % (uint64_t)rows);
+}
+
+void or_ple_gather_f16(const uint16_t* const* tables, int heads, int64_t rows, int hd, const int32_t* ids, int64_t T,
+                       const int32_t* prev_ids, int32_t eos, int variant, uint16_t* out) {
+    const int32_t prev2 = prev_ids ? prev_ids[0] : -1;
+    const int32_t prev1 = prev_ids ? prev_ids[1] : -1;
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < T; ++t) {
+        const int32_t t1 = t >= 1 ? ids[t - 1] : prev1;
+        const int32_t t2 = t >= 2 ? ids[t - 2] : (t == 1 ? prev1 : prev2);
+        for (int h = 0; h < heads; ++h) {
+            const uint32_t r = or_ple_row(ids[t], t1, t2, h, rows, eos, variant);
+            memcpy(out + (t * heads + h) * (int64_t)hd, tables[h] + (int64_t)r * hd, sizeof(uint16_t) * (size_t)hd);
+        }
+    }
+}

@@ -1,0 +1,65 @@
+/*
+ * wzyb_oracle.h -- CPU restatement of wzy-flash-serve's per-layer elementwise math.
+ *
+ * TEST INFRASTRUCTURE ONLY. This library is the parity checker for the CUDA path and the timed CPU
+ * baseline; it is never linked into, loaded by, or called from the product library
+ * (wzy-flash-serve_b200/). Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use it.
+ *
+ * Arithmetic: fp32 as written (built with -ffp-contract=off), libm expf / sqrtf, fp16 inputs
+ * widened exactly, fp16 outputs rounded to nearest-even once. Sums of squares are accumulated in
+ * double (the reference accumulates in fp32 in a thread/shuffle order that no CPU loop reproduces;
+ * the double sum is the value both approximate). Rows run in parallel with OpenMP.
+ */
+#ifndef WZYB_ORACLE_H
+#define WZYB_ORACLE_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+float or_h2f(uint16_t h);
+uint16_t or_f2h(float f);
+void or_h2f_array(const uint16_t* in, float* out, int64_t n);
+void or_f2h_array(const float* in, uint16_t* out, int64_t n);
+
+void or_set_threads(int n);
+int or_get_threads(void);
+
+/* residual add + RMSNorm (fp16 I/O); x may be NULL (plain RMSNorm, residual untouched) */
+void or_add_rmsnorm_f16(const uint16_t* x, uint16_t* res, const uint16_t* w, uint16_t* y, int64_t T, int n,
+                        float eps, float w_offset);
+/* hyper-connection form, fp32 I/O (xn_h16 != NULL additionally writes an fp16 copy of xn) */
+void or_gr_norm_f32(float* R, const float* w, const float* bo, const float* inj, float* xn, uint16_t* xn_h16,
+                    int64_t T, int n, int hc, float eps);
+/* per-head RMSNorm + partial NeoX RoPE, in place */
+void or_head_norm_rope_f16(uint16_t* data, const uint16_t* gamma, const float* cos_tab, const float* sin_tab,
+                           int64_t table_rows, int64_t base_pos, int64_t T, int heads, int hd, int64_t head_stride,
+                           int64_t row_stride, int rot, float eps, float w_offset);
+void or_head_norm_rope_f32(float* data, const float* gamma, const float* cos_tab, const float* sin_tab,
+                           int64_t table_rows, int64_t base_pos, int64_t T, int heads, int hd, int64_t head_stride,
+                           int64_t row_stride, int rot, float eps, float w_offset);
+void or_rope_table(float* cos_tab, float* sin_tab, int64_t rows, int rot, double theta);
+/* GDN gated RMSNorm; gate_mode 0 = sigmoid(z) (reference), 1 = z*sigmoid(z) */
+void or_gdn_gated_norm_f16(const uint16_t* o, const uint16_t* z, const uint16_t* gamma, uint16_t* y, int64_t T,
+                           int heads, int hd, float eps, float w_offset, int gate_mode);
+void or_gdn_gated_norm_f32(const float* o, const float* z, const float* gamma, float* y, int64_t T, int heads, int hd,
+                           float eps, float w_offset, int gate_mode);
+/* SwiGLU */
+void or_swiglu_f16(const uint16_t* g, const uint16_t* u, uint16_t* out, int64_t n);
+void or_swiglu_f32(const float* g, const float* u, float* out, int64_t n);
+void or_swiglu_interleaved_f16(const uint16_t* gu, uint16_t* out, int64_t T, int nff);
+void or_swiglu_interleaved_f32(const float* gu, float* out, int64_t T, int nff);
+/* gathers; return the number of out-of-range ids */
+uint32_t or_embed_gather_rows(const void* table, int64_t vocab, int64_t row_bytes, const int32_t* ids, int64_t T,
+                              void* out, int oob_policy);
+uint32_t or_embed_gather_bf16_f32(const uint16_t* table, int64_t vocab, int hidden, const int32_t* ids, int64_t T,
+                                  float* out, int oob_policy);
+uint32_t or_ple_row(int32_t t0, int32_t t1, int32_t t2, int head, int64_t rows, int32_t eos, int variant);
+void or_ple_gather_f16(const uint16_t* const* tables, int heads, int64_t rows, int hd, const int32_t* ids, int64_t T,
+                       const int32_t* prev_ids, int32_t eos, int variant, uint16_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

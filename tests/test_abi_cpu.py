@@ -1,0 +1,117 @@
+"""CPU checks of the C ABI: the library loads, exports every declared entry point, validates
+arguments on the host before touching the GPU, and its host-side helpers agree with the oracle.
+No kernel is launched here."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+
+def test_exports_every_declared_symbol(wz):
+    names = wz.declared_functions()
+    assert len(names) >= 25
+    missing = [n for n in names if not hasattr(wz.lib(), n)]
+    assert not missing, missing
+    # and the binding declares a signature for each of them
+    assert set(names) <= set(wz._SIGS), set(names) - set(wz._SIGS)
+
+
+def test_status_strings(wz):
+    assert wz.status_string(0) == "ok"
+    for code in (wz.ERR_NULL, wz.ERR_ALIGN, wz.ERR_SHAPE, wz.ERR_DEVICE, wz.ERR_VALUE):
+        assert "unknown" not in wz.status_string(code) or code == wz.ERR_VALUE
+    assert wz.lib().wzyb_version() >= 100
+
+
+NULL = ctypes.c_void_p(0)
+A16 = ctypes.c_void_p(0x10000)      # aligned, never dereferenced: validation fails first
+A8 = ctypes.c_void_p(0x10008)       # 8-byte aligned only
+
+
+def test_argument_validation_before_any_cuda_call(wz):
+    L = wz.lib()
+    # NULL operands
+    assert L.wzyb_add_rmsnorm_f16(NULL, NULL, A16, A16, 4, 2048, 1e-6, 1.0, NULL) == wz.ERR_NULL
+    # unsupported hidden (not a multiple of 8)
+    assert L.wzyb_add_rmsnorm_f16(A16, A16, A16, A16, 4, 2044, 1e-6, 1.0, NULL) == wz.ERR_SHAPE
+    # misaligned pointer
+    assert L.wzyb_add_rmsnorm_f16(A8, A16, A16, A16, 4, 2048, 1e-6, 1.0, NULL) == wz.ERR_ALIGN
+    # head_dim / rot_dims outside the supported set
+    args = [A16, A16, A16, A16, 4096, NULL, 0, 8, 16, 96, 96, 16 * 96, 64, 1e-6, 1.0, NULL]
+    assert L.wzyb_head_norm_rope_f16(*args) == wz.ERR_SHAPE
+    args = [A16, A16, A16, A16, 4096, NULL, 0, 8, 16, 256, 256, 16 * 256, 72, 1e-6, 1.0, NULL]
+    assert L.wzyb_head_norm_rope_f16(*args) == wz.ERR_SHAPE
+    # rotary requested without a table
+    args = [A16, A16, NULL, NULL, 4096, NULL, 0, 8, 16, 256, 256, 16 * 256, 64, 1e-6, 1.0, NULL]
+    assert L.wzyb_head_norm_rope_f16(*args) == wz.ERR_NULL
+    # misaligned head stride (fp16: stride*2 must be a multiple of 16)
+    args = [A16, A16, A16, A16, 4096, NULL, 0, 8, 2, 256, 260, 1024, 64, 1e-6, 1.0, NULL]
+    assert L.wzyb_head_norm_rope_f16(*args) == wz.ERR_ALIGN
+    # gate mode
+    assert L.wzyb_gdn_gated_norm_f16(A16, A16, A16, A16, 4, 32, 128, 1e-6, 0.0, 7, NULL) == wz.ERR_VALUE
+    assert L.wzyb_gdn_gated_norm_f16(A16, A16, A16, A16, 4, 32, 96, 1e-6, 0.0, 0, NULL) == wz.ERR_SHAPE
+    # SwiGLU sizes
+    assert L.wzyb_swiglu_f16(A16, A16, A16, 12, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_swiglu_interleaved_f16(A16, A16, 4, 12, NULL) == wz.ERR_SHAPE
+    # gathers
+    assert L.wzyb_embed_gather_rows(A16, 100, 24, A16, 4, A16, 0, NULL, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_embed_gather_rows(A16, 100, 32, A16, 4, A16, 9, NULL, NULL) == wz.ERR_VALUE
+    assert L.wzyb_embed_gather_f16(A16, 0, 2048, A16, 4, A16, 0, NULL, NULL) == wz.ERR_SHAPE
+    tables = (ctypes.c_void_p * 2)(0x10000, 0)
+    assert L.wzyb_ple_gather_f16(tables, 2, 1 << 20, 128, A16, 4, None, 248044, 0, A16, NULL) == wz.ERR_NULL
+    assert L.wzyb_ple_gather_f16(tables, 33, 1 << 20, 128, A16, 4, None, 248044, 0, A16, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_ple_gather_f16(tables, 1, 1 << 20, 128, A16, 4, None, 248044, 5, A16, NULL) == wz.ERR_VALUE
+    # empty work is a no-op that succeeds without a device
+    assert L.wzyb_swiglu_f16(A16, A16, A16, 0, NULL) == wz.OK
+    assert L.wzyb_add_rmsnorm_f16(A16, A16, A16, A16, 0, 2048, 1e-6, 1.0, NULL) == wz.OK
+    # tuning knobs
+    assert L.wzyb_set_launch_tuning(9, 1, 0) == wz.ERR_VALUE
+    assert L.wzyb_set_launch_tuning(0, 0, 0) == wz.ERR_VALUE
+
+
+def test_no_device_is_reported_not_crashed(wz):
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    assert wz.lib().wzyb_prepare_device() == wz.ERR_DEVICE
+
+
+@pytest.mark.parametrize("total,world", [(4096, 1), (4096, 2), (4096, 8), (262144, 8), (17, 4), (3, 8), (0, 2)])
+def test_shard_rows_partition(wz, total, world):
+    seen = []
+    for r in range(world):
+        r0, n = wz.shard_rows(total, world, r)
+        assert n >= 0
+        seen.extend(range(r0, r0 + n))
+    assert seen == list(range(total))
+
+
+def test_ple_halo(wz):
+    ids = np.arange(100, 120, dtype=np.int32)
+    assert wz.ple_halo(ids, 0) == (-1, -1)
+    assert wz.ple_halo(ids, 0, (7, 8)) == (7, 8)
+    assert wz.ple_halo(ids, 1, (7, 8)) == (8, 100)
+    assert wz.ple_halo(ids, 5) == (103, 104)
+
+
+def test_ple_row_index_matches_oracle(wz, orc):
+    rng = np.random.default_rng(5)
+    for _ in range(500):
+        t0, t1, t2 = (int(v) for v in rng.integers(-3, 300000, 3))
+        h = int(rng.integers(0, 16))
+        for rows in (1 << 20, 20000003):
+            for var in (0, 1):
+                assert wz.ple_row_index(t0, t1, t2, h, rows, 248044, var) == orc.ple_row(t0, t1, t2, h, rows,
+                                                                                         248044, var)
+
+
+def test_host_rope_table_matches_oracle(wz, orc):
+    rows, rot = 3000, 64
+    c = np.empty((rows, rot // 2), np.float32)
+    s = np.empty((rows, rot // 2), np.float32)
+    wz.call("wzyb_rope_table_host_f32", c.ctypes.data, s.ctypes.data, rows, rot, 1e7)
+    oc, os_ = orc.rope_table(rows, rot, 1e7)
+    assert np.array_equal(c, oc) and np.array_equal(s, os_)

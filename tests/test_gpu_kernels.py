@@ -1,0 +1,342 @@
+"""GPU parity: every CUDA entry point against the CPU oracle on the same seeded inputs.
+
+Tolerances (north star): gathers bit-exact; norms / activation / RoPE within 2 fp16 ulp of the
+oracle (max-abs and max-rel reported in the assertion message). fp32-output variants: within
+2e-6 relative + 2e-6 absolute of the oracle (fp32 reduction order, rsqrtf and __expf differ from
+libm by a few fp32 ulp).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ULP_TOL, assert_f16_close
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def rng(seed):
+    return np.random.default_rng(seed)
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def f16n(r, shape, std=1.0, mean=0.0):
+    return (r.standard_normal(shape) * std + mean).astype(np.float16)
+
+
+@pytest.fixture(autouse=True)
+def _faults_clear(wz):
+    torch.cuda.set_device(0)
+    wz.read_faults(clear=True)
+    yield
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------------------------
+# residual add + RMSNorm
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("T,n", [(1, 2048), (3, 2048), (17, 2048), (4096, 2048), (5, 2560), (9, 24),
+                                 (7, 5120), (3, 16384), (300, 1000)])
+def test_add_rmsnorm_f16(wz, orc, T, n):
+    r = rng(T * 7 + n)
+    x, res = f16n(r, (T, n)), f16n(r, (T, n))
+    w = f16n(r, (n,), 0.02)
+    y_ref, res_ref = orc.add_rmsnorm_f16(x, res, w, 1e-6, 1.0)
+    dx, dres, dw = dev(x), dev(res), dev(w)
+    dy = torch.empty_like(dres)
+    wz.add_rmsnorm_f16(dx, dres, dw, dy, 1e-6, 1.0)
+    assert np.array_equal(host(dres), res_ref), "residual must be fp16(x + residual) exactly"
+    assert_f16_close(host(dy), y_ref, ULP_TOL, f"add_rmsnorm T={T} n={n}")
+    assert wz.read_faults() == 0
+
+
+def test_rmsnorm_without_add(wz, orc):
+    r = rng(3)
+    T, n = 33, 2048
+    res, w = f16n(r, (T, n)), f16n(r, (n,), 0.02, 1.0)
+    y_ref, _ = orc.add_rmsnorm_f16(None, res, w, 1e-6, 0.0)
+    dres = dev(res)
+    dy = torch.empty_like(dres)
+    wz.add_rmsnorm_f16(None, dres, dev(w), dy, 1e-6, 0.0)
+    assert np.array_equal(host(dres), res)
+    assert_f16_close(host(dy), y_ref, ULP_TOL, "rmsnorm only")
+
+
+@pytest.mark.parametrize("hc,with_inj,out16", [(1, False, False), (4, True, False), (4, True, True), (4, False, True)])
+def test_gr_norm_f32_hyper_connection(wz, orc, hc, with_inj, out16):
+    r = rng(11 + hc)
+    T, n = 19, 2560
+    R = r.standard_normal((T * hc, n)).astype(np.float32)
+    bo = r.standard_normal((T, n)).astype(np.float32)
+    inj = r.standard_normal((T * hc,)).astype(np.float32) if with_inj else None
+    w = (1 + 0.02 * r.standard_normal((hc, n))).astype(np.float32)
+    xn_ref, xh_ref, R_ref = orc.gr_norm_f32(R, w, bo, inj, T, n, hc)
+    dR = dev(R)
+    dxn = torch.empty((T * hc, n), dtype=torch.float16 if out16 else torch.float32, device=DEV)
+    wz.gr_norm_f32(dR, dev(w), dev(bo), dev(inj) if inj is not None else None, dxn, T, n, hc)
+    np.testing.assert_allclose(host(dR), R_ref, rtol=1e-6, atol=1e-6)
+    if out16:
+        assert_f16_close(host(dxn), xh_ref, ULP_TOL, "gr_norm f16 out")
+    else:
+        np.testing.assert_allclose(host(dxn), xn_ref, rtol=2e-6, atol=2e-6)
+
+
+# ---------------------------------------------------------------------------------------------
+# per-head norm + RoPE
+# ---------------------------------------------------------------------------------------------
+def _rope_tab(orc, rows, rot, theta=1e7):
+    c, s = orc.rope_table(rows, rot, theta)
+    return c, s, dev(c), dev(s)
+
+
+@pytest.mark.parametrize("T", [1, 5, 4096])
+def test_qk_norm_rope_fused_baseline_shape(wz, orc, T):
+    """q [T,16,256], k [T,2,256], (1+w) gammas, rot 64, theta 1e7, positions 0..T-1."""
+    r = rng(100 + T)
+    hd, rot = 256, 64
+    q, k = f16n(r, (T, 16, hd)), f16n(r, (T, 2, hd))
+    gq, gk = f16n(r, (hd,), 0.02), f16n(r, (hd,), 0.02)
+    c, s, dc, ds = _rope_tab(orc, T, rot)
+    q_ref = orc.head_norm_rope(q.reshape(-1), gq, c, s, T, 16, hd, hd, 16 * hd, rot, 1e-6, 1.0, 0)
+    k_ref = orc.head_norm_rope(k.reshape(-1), gk, c, s, T, 2, hd, hd, 2 * hd, rot, 1e-6, 1.0, 0)
+    dq, dk = dev(q), dev(k)
+    dgq, dgk = dev(gq), dev(gk)
+    wz.qk_norm_rope_f16(wz.head_tensor(dq, dgq, 16, hd, 16 * hd), wz.head_tensor(dk, dgk, 2, hd, 2 * hd), dc, ds, T,
+                        hd, rot, 1e-6, 1.0)
+    assert_f16_close(host(dq).reshape(-1), q_ref, ULP_TOL, "q")
+    assert_f16_close(host(dk).reshape(-1), k_ref, ULP_TOL, "k")
+    assert wz.read_faults() == 0
+
+
+@pytest.mark.parametrize("hd,rot", [(256, 0), (256, 16), (256, 128), (256, 256), (128, 64), (64, 32), (128, 48)])
+def test_head_norm_rope_dims(wz, orc, hd, rot):
+    r = rng(hd * 1000 + rot)
+    T, H = 13, 3
+    x = f16n(r, (T, H, hd))
+    g = f16n(r, (hd,), 0.02)
+    rows = 64
+    c, s, dc, ds = _rope_tab(orc, rows, max(rot, 2))
+    want = orc.head_norm_rope(x.reshape(-1), g, c, s, T, H, hd, hd, H * hd, rot, 1e-6, 1.0, 40)
+    d = dev(x)
+    base = torch.tensor([30], dtype=torch.int32, device=DEV)
+    wz.head_norm_rope(d, dev(g), dc, ds, T, H, hd, hd, H * hd, rot, 1e-6, 1.0, d_base_pos=base, pos_offset=10)
+    assert_f16_close(host(d).reshape(-1), want, ULP_TOL, f"hd={hd} rot={rot}")
+
+
+def test_head_norm_rope_strided_heads_f32(wz, orc):
+    """The reference's own q layout: heads interleaved with the gate (head_stride = 2*HD), fp32."""
+    r = rng(77)
+    T, H, hd, rot = 6, 24, 256, 64
+    buf = r.standard_normal((T, H, 2 * hd)).astype(np.float32)
+    g = (1 + 0.02 * r.standard_normal(hd)).astype(np.float32)
+    c, s, dc, ds = _rope_tab(orc, 16, rot)
+    want = orc.head_norm_rope(buf.reshape(-1), g, c, s, T, H, hd, 2 * hd, 2 * H * hd, rot, 1e-6, 0.0, 3)
+    d = dev(buf)
+    wz.head_norm_rope(d, dev(g), dc, ds, T, H, hd, 2 * hd, 2 * H * hd, rot, 1e-6, 0.0, pos_offset=3)
+    got = host(d).reshape(-1)
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5)
+    # the gate halves are untouched
+    assert np.array_equal(got.reshape(T, H, 2 * hd)[..., hd:], buf[..., hd:])
+
+
+def test_head_norm_rope_position_out_of_table(wz, orc):
+    """Positions past the table are flagged (fault bit), not read; those heads stay un-rotated."""
+    r = rng(5)
+    T, H, hd, rot = 8, 2, 128, 64
+    x = f16n(r, (T, H, hd))
+    g = f16n(r, (hd,), 0.02)
+    c, s, dc, ds = _rope_tab(orc, 4, rot)
+    want = orc.head_norm_rope(x.reshape(-1), g, c, s, T, H, hd, hd, H * hd, rot, 1e-6, 1.0, 0)
+    d = dev(x)
+    wz.head_norm_rope(d, dev(g), dc, ds, T, H, hd, hd, H * hd, rot, 1e-6, 1.0)
+    assert_f16_close(host(d).reshape(-1), want, ULP_TOL, "pos range")
+    assert wz.read_faults() & wz.FAULT_POS_RANGE
+
+
+# ---------------------------------------------------------------------------------------------
+# GDN gated norm
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("T,H,hd,mode", [(4096, 32, 128, 0), (7, 32, 128, 1), (3, 48, 128, 0), (5, 8, 64, 0),
+                                         (5, 4, 256, 1), (2, 160, 128, 0)])
+def test_gdn_gated_norm_f16(wz, orc, T, H, hd, mode):
+    r = rng(T + H + hd + mode)
+    o, z = f16n(r, (T, H, hd)), f16n(r, (T, H, hd))
+    gm = f16n(r, (hd,), 0.02, 1.0)
+    want = orc.gdn_gated_norm(o, z, gm, T, H, hd, 1e-6, 0.0, mode)
+    dy = torch.empty((T, H, hd), dtype=torch.float16, device=DEV)
+    wz.gdn_gated_norm(dev(o), dev(z), dev(gm), dy, T, H, hd, 1e-6, 0.0, mode)
+    assert_f16_close(host(dy), want, ULP_TOL, f"gdn T={T} H={H} hd={hd} mode={mode}")
+
+
+def test_gdn_gated_norm_f32_in(wz, orc):
+    r = rng(9)
+    T, H, hd = 21, 48, 128
+    o = r.standard_normal((T, H, hd)).astype(np.float32)
+    z = r.standard_normal((T, H, hd)).astype(np.float32)
+    gm = (1 + 0.02 * r.standard_normal(hd)).astype(np.float32)
+    want = orc.gdn_gated_norm(o, z, gm, T, H, hd, 1e-6, 0.0, 0).astype(np.float16)
+    dy = torch.empty((T, H, hd), dtype=torch.float16, device=DEV)
+    wz.gdn_gated_norm(dev(o), dev(z), dev(gm), dy, T, H, hd, 1e-6, 0.0, 0)
+    assert_f16_close(host(dy), want, ULP_TOL, "gdn f32 in")
+
+
+# ---------------------------------------------------------------------------------------------
+# SwiGLU
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("rows,cols", [(4096 * 11, 512), (1, 8), (3, 640), (1001, 512)])
+def test_swiglu_f16(wz, orc, rows, cols):
+    r = rng(rows + cols)
+    g, u = f16n(r, (rows, cols)), f16n(r, (rows, cols))
+    want = orc.swiglu(g, u)
+    dout = torch.empty((rows, cols), dtype=torch.float16, device=DEV)
+    wz.swiglu(dev(g), dev(u), dout)
+    assert_f16_close(host(dout), want, ULP_TOL, f"swiglu {rows}x{cols}")
+
+
+def test_swiglu_f32_and_interleaved(wz, orc):
+    r = rng(4)
+    g = r.standard_normal(8 * 1234).astype(np.float32) * 4
+    u = r.standard_normal(8 * 1234).astype(np.float32)
+    out = torch.empty(g.size, dtype=torch.float32, device=DEV)
+    wz.swiglu(dev(g), dev(u), out)
+    np.testing.assert_allclose(host(out), orc.swiglu(g, u), rtol=2e-6, atol=2e-6)
+    T, nff = 77, 640
+    gu16 = f16n(r, (T, 2 * nff))
+    o16 = torch.empty((T, nff), dtype=torch.float16, device=DEV)
+    wz.swiglu_interleaved(dev(gu16), o16, T, nff)
+    assert_f16_close(host(o16), orc.swiglu_interleaved(gu16, T, nff), ULP_TOL, "interleaved f16")
+    gu32 = r.standard_normal((T, 2 * nff)).astype(np.float32)
+    o16b = torch.empty((T, nff), dtype=torch.float16, device=DEV)
+    wz.swiglu_interleaved(dev(gu32), o16b, T, nff)
+    want = orc.swiglu_interleaved(gu32, T, nff).astype(np.float16)
+    assert_f16_close(host(o16b), want, ULP_TOL, "interleaved f32->f16")
+
+
+# ---------------------------------------------------------------------------------------------
+# gathers (bit-exact)
+# ---------------------------------------------------------------------------------------------
+def test_embed_gather_baseline_shape(wz, orc):
+    """fp16 table [151936, 2048] ~N(0,0.02), 4096 uniform ids."""
+    gen = torch.Generator(device=DEV).manual_seed(31)
+    table = (torch.randn((151936, 2048), generator=gen, device=DEV) * 0.02).half()
+    ids = rng(32).integers(0, 151936, 4096).astype(np.int32)
+    out = torch.empty((4096, 2048), dtype=torch.float16, device=DEV)
+    cnt = torch.zeros(1, dtype=torch.int32, device=DEV)
+    wz.embed_gather_f16(table, dev(ids), out, wz.OOB_CLAMP, cnt)
+    want, bad = orc.embed_gather_rows(host(table), ids, 0)
+    assert np.array_equal(host(out).view(np.uint16), want.view(np.uint16))
+    assert int(host(cnt)[0]) == bad == 0
+
+
+@pytest.mark.parametrize("policy", [0, 1])
+def test_embed_gather_out_of_range(wz, orc, policy):
+    r = rng(8)
+    table = f16n(r, (1000, 72))
+    ids = np.array([0, 999, -5, 1000, 123456, 17, -1], dtype=np.int32)
+    out = torch.empty((ids.size, 72), dtype=torch.float16, device=DEV)
+    cnt = torch.zeros(1, dtype=torch.int32, device=DEV)
+    wz.embed_gather_f16(dev(table), dev(ids), out, policy, cnt)
+    want, bad = orc.embed_gather_rows(table, ids, policy)
+    assert np.array_equal(host(out).view(np.uint16), want.view(np.uint16))
+    assert int(host(cnt)[0]) == bad == 4
+
+
+def test_embed_gather_bf16_f32(wz, orc):
+    r = rng(10)
+    bits = r.integers(0, 65536, (5000, 2560), dtype=np.uint16)
+    ids = r.integers(-10, 5010, 97).astype(np.int32)
+    out = torch.empty((97, 2560), dtype=torch.float32, device=DEV)
+    wz.embed_gather_bf16_f32(dev(bits.view(np.int16)), dev(ids), out, wz.OOB_CLAMP)
+    want, _ = orc.embed_gather_bf16_f32(bits, ids, 0)
+    assert np.array_equal(host(out).view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("variant", [0, 1])
+def test_ple_gather_baseline_shape(wz, orc, variant):
+    """configs[3] PLE: 16 fp16 tables [2^20, 128] ~N(0,0.02), 4096 uniform ids -> [4096, 2048]."""
+    gen = torch.Generator(device=DEV).manual_seed(41)
+    tables = [(torch.randn((1 << 20, 128), generator=gen, device=DEV) * 0.02).half() for _ in range(16)]
+    ids = rng(42).integers(0, 151936, 4096).astype(np.int32)
+    out = torch.empty((4096, 2048), dtype=torch.float16, device=DEV)
+    wz.ple_gather_f16(tables, dev(ids), out, prev_ids=None, hash_variant=variant)
+    want = orc.ple_gather_f16([host(t) for t in tables], ids, None, 248044, variant)
+    assert np.array_equal(host(out).view(np.uint16), want.view(np.uint16))
+
+
+def test_ple_gather_history_and_eos(wz, orc):
+    r = rng(12)
+    tables = [f16n(r, (4099, 64)) for _ in range(5)]  # rows not a power of two
+    ids = np.array([5, 248044, 7, 8, -1, 9, 10, 11], dtype=np.int32)
+    for prev in [None, (1, 2), (248044, 3), (4, -1)]:
+        out = torch.empty((ids.size, 5 * 64), dtype=torch.float16, device=DEV)
+        wz.ple_gather_f16([dev(t) for t in tables], dev(ids), out, prev_ids=prev)
+        want = orc.ple_gather_f16(tables, ids, prev, 248044, 0)
+        assert np.array_equal(host(out).view(np.uint16), want.view(np.uint16)), prev
+
+
+# ---------------------------------------------------------------------------------------------
+# run-to-run determinism and shard equivalence (no collective: shards are independent)
+# ---------------------------------------------------------------------------------------------
+def test_bitwise_deterministic(wz):
+    r = rng(13)
+    T, n = 1024, 2048
+    x, res, w = f16n(r, (T, n)), f16n(r, (T, n)), f16n(r, (n,), 0.02)
+    outs = []
+    for _ in range(2):
+        dres, dy = dev(res), torch.empty((T, n), dtype=torch.float16, device=DEV)
+        wz.add_rmsnorm_f16(dev(x), dres, dev(w), dy)
+        outs.append(host(dy).view(np.uint16).copy())
+    assert np.array_equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("shards", [2, 8])
+def test_sharded_equals_unsharded(wz, orc, shards):
+    """Each shard gets its row slice, a RoPE pos_offset = its first row, and a 2-id PLE halo."""
+    r = rng(14)
+    T, hd = 600, 256
+    q = f16n(r, (T, 4, hd))
+    gq = f16n(r, (hd,), 0.02)
+    c, s, dc, ds = _rope_tab(orc, T, 64)
+    full = dev(q)
+    wz.head_norm_rope(full, dev(gq), dc, ds, T, 4, hd, hd, 4 * hd, 64, 1e-6, 1.0)
+    tables = [dev(f16n(r, (1 << 12, 128))) for _ in range(16)]
+    ids = r.integers(0, 151936, T).astype(np.int32)
+    ple_full = torch.empty((T, 2048), dtype=torch.float16, device=DEV)
+    wz.ple_gather_f16(tables, dev(ids), ple_full, prev_ids=(11, 12))
+    parts, ple_parts = [], []
+    for k in range(shards):
+        r0, n = wz.shard_rows(T, shards, k)
+        part = dev(q[r0:r0 + n])
+        wz.head_norm_rope(part, dev(gq), dc, ds, n, 4, hd, hd, 4 * hd, 64, 1e-6, 1.0, pos_offset=r0)
+        parts.append(host(part))
+        halo = wz.ple_halo(ids, r0, (11, 12))
+        po = torch.empty((n, 2048), dtype=torch.float16, device=DEV)
+        wz.ple_gather_f16(tables, dev(ids[r0:r0 + n]), po, prev_ids=halo)
+        ple_parts.append(host(po))
+    assert np.array_equal(np.concatenate(parts).view(np.uint16), host(full).view(np.uint16))
+    assert np.array_equal(np.concatenate(ple_parts).view(np.uint16), host(ple_full).view(np.uint16))
+
+
+def test_device_rope_table_close_to_host(wz, orc):
+    rows = 262144
+    c, s = orc.rope_table(rows, 64, 1e7)
+    dc = torch.empty((rows, 32), dtype=torch.float32, device=DEV)
+    ds = torch.empty_like(dc)
+    wz.rope_table(dc, ds, rows, 64, 1e7)
+    gc, gs = host(dc), host(ds)
+    # CUDA's fp64 cos/sin vs libm, both rounded to fp32: equal or 1 fp32 ulp apart
+    dcos = np.abs(gc.view(np.int32).astype(np.int64) - c.view(np.int32).astype(np.int64))
+    dsin = np.abs(gs.view(np.int32).astype(np.int64) - s.view(np.int32).astype(np.int64))
+    assert dcos.max() <= 1 and dsin.max() <= 1
+    assert (dcos == 0).mean() > 0.999 and (dsin == 0).mean() > 0.999

@@ -1,0 +1,189 @@
+"""GPU: pin the oracle (and the CUDA path) against the reference's OWN kernels, compiled from its
+unmodified headers into oracle/_ref/libwzyref.so and launched with the reference's launch shapes.
+
+Inputs are fp16-exact values fed to the reference's fp32 kernels; the zero-centred weight (1+w) is
+handed to the reference as g = 1.0f + w computed in fp32, since the reference applies raw weights.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ULP_TOL, assert_f16_close
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+@pytest.fixture(scope="module")
+def ref(orc):
+    if not orc.ref_available():
+        pytest.skip("oracle/_ref/libwzyref.so not built (needs the reference sources at build time)")
+    return orc.ref_lib()
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def sp():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def test_pin_add_rmsnorm_baseline(ref, orc, wz):
+    """configs[1] add+RMSNorm [4096, 2048] vs pf_gr_norm_fp16 (hc=1, gate 1.0)."""
+    r = np.random.default_rng(201)
+    T, n = 4096, 2048
+    x = r.standard_normal((T, n)).astype(np.float16)
+    res = r.standard_normal((T, n)).astype(np.float16)
+    w = (0.02 * r.standard_normal(n)).astype(np.float16)
+    g32 = (np.float32(1.0) + w.astype(np.float32)).astype(np.float32)
+    dR = dev(res.astype(np.float32))
+    dxn = torch.empty((T, n), dtype=torch.float16, device=DEV)
+    inj0 = torch.zeros(T, dtype=torch.float32, device=DEV)
+    assert ref.ref_pf_gr_norm_fp16(dR.data_ptr(), dev(g32).data_ptr(), dev(x.astype(np.float32)).data_ptr(),
+                                   inj0.data_ptr(), dxn.data_ptr(), T, n, 1, 1e-6, sp()) == 0
+    ref_y, ref_R = host(dxn), host(dR)
+    y_or, res_or = orc.add_rmsnorm_f16(x, res, w, 1e-6, 1.0)
+    assert np.array_equal(res_or, ref_R.astype(np.float16))
+    assert_f16_close(y_or, ref_y, 1, "oracle vs reference pf_gr_norm_fp16")
+    dres, dy = dev(res), torch.empty((T, n), dtype=torch.float16, device=DEV)
+    wz.add_rmsnorm_f16(dev(x), dres, dev(w), dy, 1e-6, 1.0)
+    assert np.array_equal(host(dres), res_or)
+    assert_f16_close(host(dy), ref_y, ULP_TOL, "CUDA vs reference pf_gr_norm_fp16")
+
+
+def test_pin_gr_norm_hyper_connection(ref, orc, wz):
+    """fused_gr_norm_multi with 4 streams and learned inject gates (fp32)."""
+    r = np.random.default_rng(202)
+    T, n, hc = 8, 2560, 4
+    R = r.standard_normal((T * hc, n)).astype(np.float32)
+    bo = r.standard_normal((T, n)).astype(np.float32)
+    inj = r.standard_normal((T * hc,)).astype(np.float32)
+    w = (1 + 0.02 * r.standard_normal((hc, n))).astype(np.float32)
+    dR, dxn = dev(R), torch.empty((T * hc, n), dtype=torch.float32, device=DEV)
+    assert ref.ref_fused_gr_norm_multi(dR.data_ptr(), dev(w).data_ptr(), dev(bo).data_ptr(), dev(inj).data_ptr(),
+                                       dxn.data_ptr(), T, n, hc, 1e-6, sp()) == 0
+    ref_xn, ref_R = host(dxn), host(dR)
+    xn_or, _, R_or = orc.gr_norm_f32(R, w, bo, inj, T, n, hc)
+    np.testing.assert_allclose(R_or, ref_R, rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(xn_or, ref_xn, rtol=2e-6, atol=2e-6)
+    dR2, dxn2 = dev(R), torch.empty((T * hc, n), dtype=torch.float32, device=DEV)
+    wz.gr_norm_f32(dR2, dev(w), dev(bo), dev(inj), dxn2, T, n, hc)
+    np.testing.assert_allclose(host(dR2), ref_R, rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(host(dxn2), ref_xn, rtol=2e-6, atol=2e-6)
+
+
+@pytest.mark.parametrize("heads,hd", [(16, 256), (2, 256), (4, 128)])
+def test_pin_head_norm_rope(ref, orc, wz, heads, hd):
+    """fused_head_norm_rope_multi (rot 64, theta 1e7) at the configs[1] token count."""
+    r = np.random.default_rng(203 + heads)
+    T = 4096
+    x = r.standard_normal((T, heads, hd)).astype(np.float16)
+    gam = (0.02 * r.standard_normal(hd)).astype(np.float16)
+    g32 = (np.float32(1.0) + gam.astype(np.float32)).astype(np.float32)
+    c, s = orc.ref_rope_table(T + 100, 1e7)
+    dc, ds = dev(c), dev(s)
+    base = torch.tensor([100], dtype=torch.int32, device=DEV)
+    d32 = dev(x.astype(np.float32))
+    assert ref.ref_fused_head_norm_rope_multi(d32.data_ptr(), dev(g32).data_ptr(), dc.data_ptr(), ds.data_ptr(),
+                                              base.data_ptr(), T, heads, hd, hd, heads * hd, 1e-6, sp()) == 0
+    ref_out = host(d32).reshape(-1)
+    # oracle fp32 path vs the reference, then the fp16 outputs
+    or32 = orc.head_norm_rope(x.astype(np.float32).reshape(-1), g32, c, s, T, heads, hd, hd, heads * hd, 64, 1e-6,
+                              0.0, 100)
+    np.testing.assert_allclose(or32, ref_out, rtol=1e-5, atol=2e-6)
+    or16 = orc.head_norm_rope(x.reshape(-1), gam, c, s, T, heads, hd, hd, heads * hd, 64, 1e-6, 1.0, 100)
+    assert_f16_close(or16, ref_out.astype(np.float16), 1, "oracle vs reference head norm rope")
+    d16 = dev(x)
+    wz.head_norm_rope(d16, dev(gam), dc, ds, T, heads, hd, hd, heads * hd, 64, 1e-6, 1.0, d_base_pos=base)
+    assert_f16_close(host(d16).reshape(-1), ref_out.astype(np.float16), ULP_TOL, "CUDA vs reference")
+
+
+def test_pin_gdn_gated_norm(ref, orc, wz):
+    """configs[2] GDN gated norm [4096, 32, 128] vs pf_gdn_rmsnorm_gate_parallel (sigmoid gate)."""
+    r = np.random.default_rng(204)
+    T, H, hd = 4096, 32, 128
+    o = r.standard_normal((T, H, hd)).astype(np.float16)
+    z = r.standard_normal((T, H, hd)).astype(np.float16)
+    gm = (1 + 0.02 * r.standard_normal(hd)).astype(np.float16)
+    dy = torch.empty((T, H, hd), dtype=torch.float16, device=DEV)
+    assert ref.ref_pf_gdn_rmsnorm_gate_parallel(dev(o.astype(np.float32)).data_ptr(),
+                                                dev(z.astype(np.float32)).data_ptr(),
+                                                dev(gm.astype(np.float32)).data_ptr(), dy.data_ptr(), T, H, 1e-6,
+                                                sp()) == 0
+    ref_y = host(dy)
+    assert_f16_close(orc.gdn_gated_norm(o, z, gm, T, H, hd, 1e-6, 0.0, 0), ref_y, 1, "oracle vs reference gdn")
+    dy2 = torch.empty_like(dy)
+    wz.gdn_gated_norm(dev(o), dev(z), dev(gm), dy2, T, H, hd, 1e-6, 0.0, 0)
+    assert_f16_close(host(dy2), ref_y, ULP_TOL, "CUDA vs reference gdn")
+
+
+def test_pin_swiglu(ref, orc, wz):
+    """configs[2] SwiGLU [45056, 512] vs silu_mul_multi; interleaved vs pf_silu_mul_interleaved_to_fp16."""
+    r = np.random.default_rng(205)
+    rows, cols = 4096 * 11, 512
+    g = r.standard_normal((rows, cols)).astype(np.float16)
+    u = r.standard_normal((rows, cols)).astype(np.float16)
+    out = torch.empty((rows, cols), dtype=torch.float32, device=DEV)
+    assert ref.ref_silu_mul_multi(dev(g.astype(np.float32)).data_ptr(), dev(u.astype(np.float32)).data_ptr(),
+                                  out.data_ptr(), rows * cols, sp()) == 0
+    ref_o = host(out)
+    np.testing.assert_allclose(orc.swiglu(g.astype(np.float32), u.astype(np.float32)), ref_o, rtol=2e-6, atol=2e-6)
+    assert_f16_close(orc.swiglu(g, u), ref_o.astype(np.float16), 1, "oracle vs reference silu_mul")
+    o16 = torch.empty((rows, cols), dtype=torch.float16, device=DEV)
+    wz.swiglu(dev(g), dev(u), o16)
+    assert_f16_close(host(o16), ref_o.astype(np.float16), ULP_TOL, "CUDA vs reference silu_mul")
+    T, nff = 4096, 640
+    gu = r.standard_normal((T, 2 * nff)).astype(np.float32)
+    ro = torch.empty((T, nff), dtype=torch.float16, device=DEV)
+    assert ref.ref_pf_silu_mul_interleaved_to_fp16(dev(gu).data_ptr(), ro.data_ptr(), T, nff, sp()) == 0
+    mine = torch.empty_like(ro)
+    wz.swiglu_interleaved(dev(gu), mine, T, nff)
+    assert_f16_close(host(mine), host(ro), ULP_TOL, "CUDA vs reference interleaved")
+    assert_f16_close(orc.swiglu_interleaved(gu, T, nff).astype(np.float16), host(ro), 1, "oracle vs reference il")
+
+
+def test_pin_bf16_embedding_gather(ref, orc, wz):
+    """mtp_gather_bf16_emb at its own hard-wired shape [248320, 2560], incl. out-of-range ids."""
+    ne, nv = ctypes_dims(ref)
+    gen = torch.Generator(device=DEV).manual_seed(206)
+    table = torch.randint(-32768, 32767, (nv, ne), generator=gen, device=DEV, dtype=torch.int32).to(torch.int16)
+    ids = np.concatenate([np.random.default_rng(206).integers(0, nv, 60), [-7, nv, nv + 100, 0]]).astype(np.int32)
+    dids = dev(ids)
+    ro = torch.empty((ids.size, ne), dtype=torch.float32, device=DEV)
+    assert ref.ref_mtp_gather_bf16_emb(table.data_ptr(), dids.data_ptr(), ro.data_ptr(), ids.size, sp()) == 0
+    mine = torch.empty_like(ro)
+    wz.embed_gather_bf16_f32(table, dids, mine, wz.OOB_CLAMP)
+    assert np.array_equal(host(mine).view(np.uint32), host(ro).view(np.uint32))
+    want, _ = orc.embed_gather_bf16_f32(host(table).view(np.uint16), ids, 0)
+    assert np.array_equal(want.view(np.uint32), host(ro).view(np.uint32))
+
+
+def test_pin_plain_row_norm(ref, orc, wz):
+    """ple_group_multi (the reference's generic per-stream row RMSNorm) vs the no-add norm path."""
+    r = np.random.default_rng(207)
+    T, n, hc = 6, 2560, 4
+    x = r.standard_normal((T * hc, n)).astype(np.float32)
+    g = (1 + 0.02 * r.standard_normal((hc, n))).astype(np.float32)
+    ry = torch.empty((T * hc, n), dtype=torch.float32, device=DEV)
+    assert ref.ref_ple_group_multi(dev(x).data_ptr(), dev(g).data_ptr(), ry.data_ptr(), T, n, hc, 1e-6, sp()) == 0
+    mine = torch.empty_like(ry)
+    dx = dev(x)
+    wz.gr_norm_f32(dx, dev(g), None, None, mine, T, n, hc)
+    np.testing.assert_allclose(host(mine), host(ry), rtol=2e-6, atol=2e-6)
+    assert np.array_equal(host(dx), x)
+
+
+def ctypes_dims(ref):
+    import ctypes
+
+    a, b = ctypes.c_int(), ctypes.c_int()
+    ref.ref_dims(ctypes.byref(a), ctypes.byref(b))
+    return a.value, b.value

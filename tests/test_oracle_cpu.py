@@ -1,0 +1,180 @@
+"""CPU checks of the oracle itself: fp16 conversion, an independent numpy restatement of each op,
+the reference's own host RoPE table, and the PLE hash against a pure-Python restatement."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import assert_f16_close, f16_ulp_distance
+
+RNG = np.random.default_rng(1234)
+
+
+def test_f16_roundtrip_matches_numpy(orc):
+    # every fp16 bit pattern widens exactly
+    bits = np.arange(65536, dtype=np.uint16)
+    want = bits.view(np.float16).astype(np.float32)
+    got = np.empty(65536, dtype=np.float32)
+    orc.lib().or_h2f_array(bits.ctypes.data, got.ctypes.data, 65536)
+    finite = np.isfinite(want)
+    assert np.array_equal(got[finite].view(np.uint32), want[finite].view(np.uint32))
+    assert np.all(np.isnan(got[~finite & np.isnan(want)]))
+    # float -> fp16 rounding (RN-even) matches numpy on a wide sample incl. subnormals, ties, overflow
+    x = np.concatenate([
+        RNG.standard_normal(200000).astype(np.float32) * np.float32(10.0) ** RNG.integers(-9, 6, 200000),
+        (np.arange(-4096, 4096, dtype=np.float32) + 0.5) * np.float32(2.0 ** -24),  # ties in the subnormal range
+        np.array([65504, 65519.99, 65520, 70000, -65520, 6.1035156e-05, 5.96e-08, 2.98e-08, 0.0, -0.0],
+                 dtype=np.float32),
+    ]).astype(np.float32)
+    got = np.empty(x.size, dtype=np.uint16)
+    orc.lib().or_f2h_array(x.ctypes.data, got.ctypes.data, x.size)
+    with np.errstate(over="ignore"):
+        want16 = x.astype(np.float16).view(np.uint16)
+    assert np.array_equal(got, want16)
+
+
+def _ref64_rmsnorm(v, g, eps):
+    v = v.astype(np.float64)
+    return v / np.sqrt((v * v).mean(axis=-1, keepdims=True) + eps) * g
+
+
+def test_add_rmsnorm_against_float64(orc):
+    T, n = 37, 2048
+    x = RNG.standard_normal((T, n)).astype(np.float16)
+    r = RNG.standard_normal((T, n)).astype(np.float16)
+    w = (RNG.standard_normal(n) * 0.02).astype(np.float16)
+    y, r2 = orc.add_rmsnorm_f16(x, r, w, 1e-6, 1.0)
+    v = x.astype(np.float32) + r.astype(np.float32)
+    assert np.array_equal(r2, v.astype(np.float16))
+    want = _ref64_rmsnorm(v, 1.0 + w.astype(np.float64), 1e-6).astype(np.float16)
+    assert_f16_close(y, want, 1, "add_rmsnorm vs f64")
+    # x = None: plain norm, residual untouched
+    y2, r3 = orc.add_rmsnorm_f16(None, r, w, 1e-6, 0.0)
+    assert np.array_equal(r3, r)
+    assert_f16_close(y2, _ref64_rmsnorm(r.astype(np.float32), w.astype(np.float64), 1e-6).astype(np.float16), 1)
+
+
+def test_gr_norm_hyper_connection_against_float64(orc):
+    T, n, hc = 5, 256, 4
+    R = RNG.standard_normal((T * hc, n)).astype(np.float32)
+    bo = RNG.standard_normal((T, n)).astype(np.float32)
+    inj = RNG.standard_normal((T * hc,)).astype(np.float32)
+    w = (1 + 0.02 * RNG.standard_normal((hc, n))).astype(np.float32)
+    xn, xh, R2 = orc.gr_norm_f32(R, w, bo, inj, T, n, hc)
+    gw = 2.0 / (1.0 + np.exp(-inj.astype(np.float64) / hc))
+    v = R.astype(np.float64) + np.repeat(bo, hc, axis=0) * gw[:, None]
+    np.testing.assert_allclose(R2, v, rtol=1e-6, atol=1e-6)
+    want = _ref64_rmsnorm(v, np.tile(w, (T, 1)), 1e-6)
+    np.testing.assert_allclose(xn, want, rtol=2e-6, atol=2e-6)
+
+
+def test_rope_table_matches_reference_host_builder(orc):
+    """The oracle's table equals the reference's own build_rope_cos_sin_host bit for bit."""
+    if not orc.ref_available():
+        pytest.skip("reference kernels library not built (needs the reference sources)")
+    rows = 5000
+    c, s = orc.rope_table(rows, 64, 1e7)
+    rc, rs = orc.ref_rope_table(rows, 1e7)
+    assert np.array_equal(c.view(np.uint32), rc.view(np.uint32))
+    assert np.array_equal(s.view(np.uint32), rs.view(np.uint32))
+
+
+def test_head_norm_rope_against_float64(orc):
+    T, H, hd, rot = 9, 3, 256, 64
+    data = RNG.standard_normal((T, H, hd)).astype(np.float16)
+    gam = (0.02 * RNG.standard_normal(hd)).astype(np.float16)
+    c, s = orc.rope_table(64, rot, 1e7)
+    got = orc.head_norm_rope(data.reshape(-1), gam, c, s, T, H, hd, hd, H * hd, rot, 1e-6, 1.0, base_pos=7)
+    p = _ref64_rmsnorm(data.astype(np.float32), 1.0 + gam.astype(np.float64), 1e-6)
+    half = rot // 2
+    pos = 7 + np.arange(T)
+    cs = c[pos][:, None, :].astype(np.float64)
+    sn = s[pos][:, None, :].astype(np.float64)
+    a, d = p[..., :half].copy(), p[..., half:rot].copy()
+    p[..., :half] = a * cs - d * sn
+    p[..., half:rot] = a * sn + d * cs
+    assert_f16_close(got.reshape(T, H, hd), p.astype(np.float16), 1, "head_norm_rope vs f64")
+
+
+def test_gdn_and_swiglu_against_float64(orc):
+    T, H, hd = 11, 4, 128
+    o = RNG.standard_normal((T, H, hd)).astype(np.float16)
+    z = RNG.standard_normal((T, H, hd)).astype(np.float16)
+    gm = (1 + 0.02 * RNG.standard_normal(hd)).astype(np.float16)
+    y = orc.gdn_gated_norm(o, z, gm, T, H, hd, 1e-6, 0.0, 0)
+    want = _ref64_rmsnorm(o.astype(np.float32), gm.astype(np.float64), 1e-6) / (1 + np.exp(-z.astype(np.float64)))
+    assert_f16_close(y, want.astype(np.float16), 1, "gdn sigmoid")
+    y2 = orc.gdn_gated_norm(o, z, gm, T, H, hd, 1e-6, 0.0, 1)
+    want2 = want * z.astype(np.float64)
+    assert_f16_close(y2, want2.astype(np.float16), 1, "gdn silu")
+    g = RNG.standard_normal(4096).astype(np.float16)
+    u = RNG.standard_normal(4096).astype(np.float16)
+    out = orc.swiglu(g, u)
+    g64 = g.astype(np.float64)
+    assert_f16_close(out, (g64 / (1 + np.exp(-g64)) * u).astype(np.float16), 1, "swiglu")
+    gu = np.concatenate([g.reshape(8, 512), u.reshape(8, 512)], axis=1)
+    out2 = orc.swiglu_interleaved(gu, 8, 512)
+    assert np.array_equal(out2.reshape(-1), out)
+
+
+def _py_ple_row(t0, t1, t2, head, rows, eos, variant):
+    cut = t1 < 0 or t1 == eos
+    c1 = eos if cut else t1
+    cut = cut or t2 < 0 or t2 == eos
+    c2 = eos if cut else t2
+    m = 0xFFFFFFFF
+    a = (t0 * 0x9E3779B1) & m
+    b = (c1 * 0x85EBCA77) & m
+    c = (c2 * 0xC2B2AE3D) & m
+    h = ((a ^ b ^ c) + head) & m if variant == 1 else (a ^ b ^ ((c + head) & m))
+    return h % rows
+
+
+@pytest.mark.parametrize("variant", [0, 1])
+def test_ple_row_matches_python(orc, variant):
+    rows = 1 << 20
+    cases = [(5, 7, 9), (0, -1, -1), (123, 248044, 55), (123, 55, 248044), (-3, 4, 5), (151935, 151934, 151933)]
+    cases += [tuple(int(v) for v in RNG.integers(-2, 151936, 3)) for _ in range(200)]
+    for t0, t1, t2 in cases:
+        for h in (0, 1, 15):
+            assert orc.ple_row(t0, t1, t2, h, rows, 248044, variant) == _py_ple_row(t0, t1, t2, h, rows, 248044,
+                                                                                     variant)
+    # the two readings of the formula differ (so the choice is observable)
+    assert any(orc.ple_row(t0, t1, t2, 3, rows, 248044, 0) != orc.ple_row(t0, t1, t2, 3, rows, 248044, 1)
+               for t0, t1, t2 in cases)
+
+
+def test_ple_gather_boundary_and_cut(orc):
+    heads, rows, hd = 4, 64, 16
+    tables = [RNG.standard_normal((rows, hd)).astype(np.float16) for _ in range(heads)]
+    ids = np.array([3, 248044, 9, 10, 11], dtype=np.int32)
+    out = orc.ple_gather_f16(tables, ids, prev_ids=(1, 2), eos=248044, variant=0)
+    seq = [1, 2] + [int(v) for v in ids]  # prev_ids = (id[-2], id[-1])
+    for t in range(ids.size):
+        t0, t1, t2 = seq[t + 2], seq[t + 1], seq[t]
+        for h in range(heads):
+            r = _py_ple_row(t0, t1, t2, h, rows, 248044, 0)
+            assert np.array_equal(out[t, h * hd:(h + 1) * hd], tables[h][r])
+    # no history = (-1, -1): both history slots become EOS
+    out2 = orc.ple_gather_f16(tables, ids[:1], prev_ids=None)
+    r = _py_ple_row(3, 248044, 248044, 0, rows, 248044, 0)
+    assert np.array_equal(out2[0, :hd], tables[0][r])
+
+
+def test_embed_gather_policies(orc):
+    table = RNG.standard_normal((100, 64)).astype(np.float16)
+    ids = np.array([0, 5, 99, -1, 100, 7], dtype=np.int32)
+    out, bad = orc.embed_gather_rows(table, ids, 0)
+    assert bad == 2
+    assert np.array_equal(out, table[[0, 5, 99, 0, 99, 7]])
+    out, bad = orc.embed_gather_rows(table, ids, 1)
+    assert np.array_equal(out, table[[0, 5, 99, 0, 0, 7]])
+    bits = RNG.integers(0, 65536, (10, 16), dtype=np.uint16)
+    f, _ = orc.embed_gather_bf16_f32(bits, np.array([1, 3], dtype=np.int32))
+    assert np.array_equal(f.view(np.uint32), bits[[1, 3]].astype(np.uint32) << 16)
+
+
+def test_ulp_helper():
+    a = np.array([1.0, -0.0, 0.0, 65504], dtype=np.float16)
+    b = np.array([1.0009765625, 0.0, 5.96e-08, 65504], dtype=np.float16)
+    assert list(f16_ulp_distance(a, b)) == [1, 0, 1, 0]

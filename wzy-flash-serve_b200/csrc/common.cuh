@@ -1,0 +1,225 @@
+// common.cuh -- device helpers shared by the wzyb200 layer kernels (sm_100a only).
+//
+// Everything on this path is HBM-bound streaming work (no dense contraction), so the helpers here are
+// about moving bytes: 16-byte vector loads/stores of 8 elements, 1-D TMA bulk copies
+// (cp.async.bulk) into shared memory completed on an mbarrier, and bounded mbarrier waits that give
+// up after a time limit instead of spinning forever.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "../../include/wzyb200.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "wzyb200 kernels are written for sm_100a (Blackwell) only"
+#endif
+
+namespace wzyb {
+
+// ----------------------------------------------------------------------------------------------
+// Fault word. Kernels never trap: when a bounded wait gives up or a device-side range check fails,
+// they OR a WZYB_FAULT_* bit into this word and return. The host reads it with wzyb_read_faults().
+// Defined here: the library is a single CUDA translation unit (wzyb200_all.cu).
+// ----------------------------------------------------------------------------------------------
+__device__ unsigned int g_fault_word = 0;
+
+__device__ __forceinline__ void raise_fault(unsigned int bit) { atomicOr(&g_fault_word, bit); }
+
+// A wait that has not completed after this many nanoseconds is treated as lost (1 s; a healthy
+// wait here lasts a few microseconds at most).
+constexpr unsigned long long kWaitLimitNs = 1000000000ull;
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ----------------------------------------------------------------------------------------------
+// mbarrier + 1-D bulk copy (TMA without a tensor map) primitives.
+// ----------------------------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Make mbarrier initialisation visible to the async (TMA) proxy before any bulk copy uses it.
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` to complete. Returns false (and raises WZYB_FAULT_WAIT_TIMEOUT)
+// if it has not completed within kWaitLimitNs; the caller must then stop using the pipeline.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 0u && globaltimer_ns() - t0 > kWaitLimitNs) {
+            raise_fault(WZYB_FAULT_WAIT_TIMEOUT);
+            return false;
+        }
+    }
+}
+
+// Like mbar_wait, but against an absolute %globaltimer deadline and without raising a fault:
+// used to drain copies that are still in flight after a pipeline has been abandoned.
+__device__ __forceinline__ bool mbar_wait_until(uint64_t* bar, uint32_t parity, unsigned long long deadline) {
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 255u && globaltimer_ns() > deadline) return false;
+    }
+}
+
+// L2 eviction policy for bytes that are read exactly once.
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` (bytes must be a multiple of 16 and
+// both addresses 16-byte aligned; the launchers check this on the host).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar,
+                                          uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+            "r"(smem_u32(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// ----------------------------------------------------------------------------------------------
+// 8-element vectors. fp16: one 16-byte access; fp32: two 16-byte accesses.
+// ----------------------------------------------------------------------------------------------
+template <typename T>
+struct Vec8;
+
+template <>
+struct Vec8<__half> {
+    static constexpr int kBytes = 16;
+    // raw (unconverted) form, so several vectors can be in flight at 4 registers each
+    struct Raw {
+        uint4 u;
+    };
+    __device__ __forceinline__ static Raw ldcs_raw(const __half* p) {
+        return Raw{__ldcs(reinterpret_cast<const uint4*>(p))};
+    }
+    __device__ __forceinline__ static void cvt(const Raw& r, float (&f)[8]) { to_f32(r.u, f); }
+    __device__ __forceinline__ static void to_f32(const uint4& u, float (&f)[8]) {
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 p = __half22float2(h[i]);
+            f[2 * i] = p.x;
+            f[2 * i + 1] = p.y;
+        }
+    }
+    __device__ __forceinline__ static uint4 from_f32(const float (&f)[8]) {
+        uint4 u;
+        __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+        return u;
+    }
+    // generic (smem or global) load
+    __device__ __forceinline__ static void load(const __half* p, float (&f)[8]) {
+        to_f32(*reinterpret_cast<const uint4*>(p), f);
+    }
+    // read-only global load through the non-coherent path
+    __device__ __forceinline__ static void load_ro(const __half* p, float (&f)[8]) {
+        to_f32(__ldg(reinterpret_cast<const uint4*>(p)), f);
+    }
+    // streaming global load (read once)
+    __device__ __forceinline__ static void load_stream(const __half* p, float (&f)[8]) {
+        to_f32(__ldcs(reinterpret_cast<const uint4*>(p)), f);
+    }
+    __device__ __forceinline__ static void store(__half* p, const float (&f)[8]) {
+        *reinterpret_cast<uint4*>(p) = from_f32(f);
+    }
+    __device__ __forceinline__ static void store_stream(__half* p, const float (&f)[8]) {
+        __stcs(reinterpret_cast<uint4*>(p), from_f32(f));
+    }
+};
+
+template <>
+struct Vec8<float> {
+    static constexpr int kBytes = 32;
+    struct Raw {
+        float4 a, b;
+    };
+    __device__ __forceinline__ static Raw ldcs_raw(const float* p) {
+        return Raw{__ldcs(reinterpret_cast<const float4*>(p)), __ldcs(reinterpret_cast<const float4*>(p) + 1)};
+    }
+    __device__ __forceinline__ static void cvt(const Raw& r, float (&f)[8]) {
+        f[0] = r.a.x; f[1] = r.a.y; f[2] = r.a.z; f[3] = r.a.w;
+        f[4] = r.b.x; f[5] = r.b.y; f[6] = r.b.z; f[7] = r.b.w;
+    }
+    __device__ __forceinline__ static void load(const float* p, float (&f)[8]) {
+        const float4 a = reinterpret_cast<const float4*>(p)[0];
+        const float4 b = reinterpret_cast<const float4*>(p)[1];
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    }
+    __device__ __forceinline__ static void load_ro(const float* p, float (&f)[8]) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    }
+    __device__ __forceinline__ static void load_stream(const float* p, float (&f)[8]) {
+        const float4 a = __ldcs(reinterpret_cast<const float4*>(p));
+        const float4 b = __ldcs(reinterpret_cast<const float4*>(p) + 1);
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    }
+    __device__ __forceinline__ static void store(float* p, const float (&f)[8]) {
+        reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+        reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+    }
+    __device__ __forceinline__ static void store_stream(float* p, const float (&f)[8]) {
+        __stcs(reinterpret_cast<float4*>(p), make_float4(f[0], f[1], f[2], f[3]));
+        __stcs(reinterpret_cast<float4*>(p) + 1, make_float4(f[4], f[5], f[6], f[7]));
+    }
+};
+
+// Sum over aligned groups of `kLanes` lanes (kLanes a power of two <= 32) with xor shuffles.
+template <int kLanes>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+    for (int o = kLanes / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Named barrier among `nthreads` threads (a multiple of 32), id 1..15 (0 is __syncthreads).
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+}  // namespace wzyb

@@ -1,0 +1,235 @@
+// gather.cu -- token-embedding gather and 16-head 3-gram PLE gather (bit-exact row copies).
+//
+// The reference stages both on the host: stage_one_emb (src/wzy_engine_v2.cu:862-875) copies one
+// bf16 row per token and converts it to fp32, and stage_ple_window / stage_emb_ple_pf
+// (src/wzy_engine_v2.cu:943-978, :1210-1265) hash each token's 3-gram context into 16 rows and copy
+// them, then H2D the result. Its only device gather, mtp_gather_bf16_emb (src/wzy_kernels_v2.cuh:27-36),
+// reads 2-byte elements with a 256-thread block per token. Here both gathers run on the device:
+// a warp (embedding) or a lane group (PLE) per row, 16-byte accesses, several row chunks in flight
+// per lane before any store.
+#include "launch.hpp"
+#include "common.cuh"
+
+namespace wzyb {
+
+constexpr int kGatherThreads = 256;
+constexpr int kRowUnroll = 8;  // 16-byte chunks in flight per lane
+
+__device__ __forceinline__ int64_t resolve_id(int32_t id, int64_t vocab, int policy, uint32_t* oob, int lane) {
+    if (id >= 0 && id < vocab) return id;
+    if (oob != nullptr && lane == 0) atomicAdd(oob, 1u);
+    if (policy == WZYB_OOB_ZERO_ID) return 0;
+    return id < 0 ? 0 : vocab - 1;
+}
+
+// One warp per output row: out[t] = table[id(t)], row_chunks 16-byte chunks per row.
+__global__ void __launch_bounds__(kGatherThreads) gather_rows_kernel(const uint4* __restrict__ table, int64_t vocab,
+                                                                      int64_t row_chunks, const int32_t* __restrict__ ids,
+                                                                      int64_t T, uint4* __restrict__ out, int policy,
+                                                                      uint32_t* oob) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
+        const int64_t id = resolve_id(__ldg(ids + t), vocab, policy, oob, lane);
+        const uint4* src = table + id * row_chunks;
+        uint4* dst = out + t * row_chunks;
+        for (int64_t c0 = lane; c0 < row_chunks; c0 += 32 * kRowUnroll) {
+            uint4 buf[kRowUnroll];
+#pragma unroll
+            for (int k = 0; k < kRowUnroll; ++k)
+                if (c0 + 32 * k < row_chunks) buf[k] = __ldg(src + c0 + 32 * k);
+#pragma unroll
+            for (int k = 0; k < kRowUnroll; ++k)
+                if (c0 + 32 * k < row_chunks) __stcs(dst + c0 + 32 * k, buf[k]);
+        }
+    }
+}
+
+// bf16 table -> fp32 rows: each lane converts 8 bf16 (16 B in) to 8 fp32 (32 B out) by shifting the
+// bit pattern into the high half, which is exactly the reference's db2f (src/wzy_kernels_v2.cuh:23).
+__global__ void __launch_bounds__(kGatherThreads) gather_bf16_f32_kernel(const uint4* __restrict__ table,
+                                                                          int64_t vocab, int64_t row_chunks,
+                                                                          const int32_t* __restrict__ ids, int64_t T,
+                                                                          uint4* __restrict__ out, int policy,
+                                                                          uint32_t* oob) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
+        const int64_t id = resolve_id(__ldg(ids + t), vocab, policy, oob, lane);
+        const uint4* src = table + id * row_chunks;
+        uint4* dst = out + t * row_chunks * 2;
+        for (int64_t c0 = lane; c0 < row_chunks; c0 += 32 * kRowUnroll) {
+            uint4 buf[kRowUnroll];
+#pragma unroll
+            for (int k = 0; k < kRowUnroll; ++k)
+                if (c0 + 32 * k < row_chunks) buf[k] = __ldg(src + c0 + 32 * k);
+#pragma unroll
+            for (int k = 0; k < kRowUnroll; ++k) {
+                const int64_t c = c0 + 32 * k;
+                if (c < row_chunks) {
+                    const uint4 b = buf[k];
+                    const uint4 lo = make_uint4(b.x << 16, b.x & 0xFFFF0000u, b.y << 16, b.y & 0xFFFF0000u);
+                    const uint4 hi = make_uint4(b.z << 16, b.z & 0xFFFF0000u, b.w << 16, b.w & 0xFFFF0000u);
+                    __stcs(dst + 2 * c, lo);
+                    __stcs(dst + 2 * c + 1, hi);
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// PLE
+// ---------------------------------------------------------------------------------------------
+__host__ __device__ __forceinline__ uint32_t ple_row(int32_t t0, int32_t h1, int32_t h2, int head, uint64_t rows,
+                                                     int32_t eos, int variant) {
+    // EOS cut over the history, as the reference builds ctx[1..2] (src/wzy_engine_v2.cu:946-953):
+    // once an id is negative or EOS, it and every older id become EOS.
+    bool cut = h1 < 0 || h1 == eos;
+    const int32_t c1 = cut ? eos : h1;
+    cut = cut || h2 < 0 || h2 == eos;
+    const int32_t c2 = cut ? eos : h2;
+    const uint32_t a = (uint32_t)t0 * 0x9E3779B1u;
+    const uint32_t b = (uint32_t)c1 * 0x85EBCA77u;
+    const uint32_t c = (uint32_t)c2 * 0xC2B2AE3Du;
+    const uint32_t h = variant == WZYB_PLE_HASH_XOR_THEN_ADD ? ((a ^ b ^ c) + (uint32_t)head)
+                                                             : (a ^ b ^ (c + (uint32_t)head));
+    return (uint32_t)((uint64_t)h % rows);
+}
+
+struct PleArgs {
+    const uint4* tables[32];
+    int heads;
+    uint64_t rows;
+    int chunks;  // 16-byte chunks per head row
+    const int32_t* ids;
+    int64_t T;
+    int32_t prev2;  // id[-2]
+    int32_t prev1;  // id[-1]
+    int32_t eos;
+    int variant;
+    uint4* out;  // [T, heads * chunks]
+};
+
+// Flattened over (token, head, chunk); each thread keeps kRowUnroll chunks in flight.
+__global__ void __launch_bounds__(kGatherThreads) ple_gather_kernel(const PleArgs a) {
+    const int64_t per_tok = (int64_t)a.heads * a.chunks;
+    const int64_t total = a.T * per_tok;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < total; base += stride * kRowUnroll) {
+        uint4 buf[kRowUnroll];
+        int64_t dsti[kRowUnroll];
+#pragma unroll
+        for (int k = 0; k < kRowUnroll; ++k) {
+            const int64_t idx = base + k * stride;
+            dsti[k] = idx;
+            if (idx < total) {
+                const int64_t t = idx / per_tok;
+                const int rem = (int)(idx - t * per_tok);
+                const int h = rem / a.chunks;
+                const int c = rem - h * a.chunks;
+                const int32_t t0 = __ldg(a.ids + t);
+                const int32_t h1 = t >= 1 ? __ldg(a.ids + t - 1) : a.prev1;
+                const int32_t h2 = t >= 2 ? __ldg(a.ids + t - 2) : (t == 1 ? a.prev1 : a.prev2);
+                const uint32_t row = ple_row(t0, h1, h2, h, a.rows, a.eos, a.variant);
+                buf[k] = __ldg(a.tables[h] + (int64_t)row * a.chunks + c);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kRowUnroll; ++k)
+            if (dsti[k] < total) __stcs(a.out + dsti[k], buf[k]);
+    }
+}
+
+static int grid_for(int64_t work_threads, int ctas_per_sm, const DeviceInfo& di) {
+    const int64_t per_wave = (int64_t)di.sms * ctas_per_sm;
+    const int64_t need = (work_threads + kGatherThreads - 1) / kGatherThreads;
+    return (int)(need < per_wave ? need : per_wave) > 0 ? (int)(need < per_wave ? need : per_wave) : 1;
+}
+
+}  // namespace wzyb
+
+extern "C" {
+
+int wzyb_embed_gather_rows(const void* table, int64_t vocab, int64_t row_bytes, const int32_t* ids, int64_t T,
+                           void* out, int oob_policy, uint32_t* d_oob_count, wzyb_stream_t stream) {
+    if (!table || !ids || !out) return WZYB_ERR_NULL;
+    if (oob_policy != WZYB_OOB_CLAMP && oob_policy != WZYB_OOB_ZERO_ID) return WZYB_ERR_VALUE;
+    if (vocab < 1 || T < 0 || row_bytes < 16 || (row_bytes % 16) != 0) return WZYB_ERR_SHAPE;
+    if (!wzyb::aligned16(table) || !wzyb::aligned16(out)) return WZYB_ERR_ALIGN;
+    if (T == 0) return WZYB_OK;
+    wzyb::DeviceInfo di;
+    const int rc = wzyb::device_info(&di);
+    if (rc != WZYB_OK) return rc;
+    const int grid = wzyb::grid_for(T * 32, 8, di);
+    wzyb::gather_rows_kernel<<<grid, wzyb::kGatherThreads, 0, (cudaStream_t)stream>>>(
+        (const uint4*)table, vocab, row_bytes / 16, ids, T, (uint4*)out, oob_policy, d_oob_count);
+    return wzyb::launch_status();
+}
+
+int wzyb_embed_gather_f16(const uint16_t* table, int64_t vocab, int hidden, const int32_t* ids, int64_t T,
+                          uint16_t* out, int oob_policy, uint32_t* d_oob_count, wzyb_stream_t stream) {
+    if (hidden < 8 || (hidden % 8) != 0) return WZYB_ERR_SHAPE;
+    return wzyb_embed_gather_rows(table, vocab, (int64_t)hidden * 2, ids, T, out, oob_policy, d_oob_count, stream);
+}
+
+int wzyb_embed_gather_bf16_f32(const uint16_t* table, int64_t vocab, int hidden, const int32_t* ids, int64_t T,
+                               float* out, int oob_policy, uint32_t* d_oob_count, wzyb_stream_t stream) {
+    if (!table || !ids || !out) return WZYB_ERR_NULL;
+    if (oob_policy != WZYB_OOB_CLAMP && oob_policy != WZYB_OOB_ZERO_ID) return WZYB_ERR_VALUE;
+    if (vocab < 1 || T < 0 || hidden < 8 || (hidden % 8) != 0) return WZYB_ERR_SHAPE;
+    if (!wzyb::aligned16(table) || !wzyb::aligned16(out)) return WZYB_ERR_ALIGN;
+    if (T == 0) return WZYB_OK;
+    wzyb::DeviceInfo di;
+    const int rc = wzyb::device_info(&di);
+    if (rc != WZYB_OK) return rc;
+    const int grid = wzyb::grid_for(T * 32, 8, di);
+    wzyb::gather_bf16_f32_kernel<<<grid, wzyb::kGatherThreads, 0, (cudaStream_t)stream>>>(
+        (const uint4*)table, vocab, hidden / 8, ids, T, (uint4*)out, oob_policy, d_oob_count);
+    return wzyb::launch_status();
+}
+
+uint32_t wzyb_ple_row_index(int32_t t0, int32_t t1, int32_t t2, int head, int64_t rows_per_table, int32_t eos_id,
+                            int hash_variant) {
+    if (rows_per_table < 1) return 0;
+    return wzyb::ple_row(t0, t1, t2, head, (uint64_t)rows_per_table, eos_id, hash_variant);
+}
+
+int wzyb_ple_gather_f16(const uint16_t* const* tables, int heads, int64_t rows_per_table, int head_dim,
+                        const int32_t* ids, int64_t T, const int32_t* prev_ids, int32_t eos_id, int hash_variant,
+                        uint16_t* out, wzyb_stream_t stream) {
+    if (!tables || !ids || !out) return WZYB_ERR_NULL;
+    if (hash_variant != WZYB_PLE_HASH_C_PRECEDENCE && hash_variant != WZYB_PLE_HASH_XOR_THEN_ADD)
+        return WZYB_ERR_VALUE;
+    if (heads < 1 || heads > 32 || rows_per_table < 1 || rows_per_table > (int64_t(1) << 32) || head_dim < 8 ||
+        (head_dim % 8) != 0 || T < 0)
+        return WZYB_ERR_SHAPE;
+    wzyb::PleArgs a;
+    for (int h = 0; h < 32; ++h) a.tables[h] = nullptr;
+    for (int h = 0; h < heads; ++h) {
+        if (!tables[h]) return WZYB_ERR_NULL;
+        if (!wzyb::aligned16(tables[h])) return WZYB_ERR_ALIGN;
+        a.tables[h] = (const uint4*)tables[h];
+    }
+    if (!wzyb::aligned16(out)) return WZYB_ERR_ALIGN;
+    if (T == 0) return WZYB_OK;
+    wzyb::DeviceInfo di;
+    const int rc = wzyb::device_info(&di);
+    if (rc != WZYB_OK) return rc;
+    a.heads = heads;
+    a.rows = (uint64_t)rows_per_table;
+    a.chunks = head_dim / 8;
+    a.ids = ids;
+    a.T = T;
+    a.prev2 = prev_ids ? prev_ids[0] : -1;
+    a.prev1 = prev_ids ? prev_ids[1] : -1;
+    a.eos = eos_id;
+    a.variant = hash_variant;
+    a.out = (uint4*)out;
+    const int64_t total = T * heads * (int64_t)a.chunks;
+    const int grid = wzyb::grid_for((total + wzyb::kRowUnroll - 1) / wzyb::kRowUnroll, 8, di);
+    wzyb::ple_gather_kernel<<<grid, wzyb::kGatherThreads, 0, (cudaStream_t)stream>>>(a);
+    return wzyb::launch_status();
+}
+
+}  // extern "C"

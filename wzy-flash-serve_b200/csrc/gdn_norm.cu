@@ -1,0 +1,200 @@
+// gdn_norm.cu -- GDN output gated RMSNorm, one HBM pass.
+//
+// Math follows pf_gdn_rmsnorm_gate_parallel (src/wzy_qsa_wmma.cuh:178-195) and the tail of
+// fused_gdn_step_norm_multi (src/wzy_kernels_v2.cuh:966-976):
+//   y = o * rsqrt(sum(o^2)/hd + eps) * gamma[col] / (1 + exp(-z))
+// i.e. the gate is sigmoid(z) at every reference site; WZYB_GATE_SILU selects z*sigmoid(z).
+// The reference runs one 128-thread block per (head, token) with a shared-memory reduction. Here a
+// unit is one token (o row + z row, all heads) staged by TMA bulk copies (ring.cuh); each head is
+// owned by hd/8 lanes that reduce with xor shuffles, and y leaves with one 16-byte store per lane.
+#include "launch.hpp"
+#include "ring.cuh"
+
+namespace wzyb {
+
+struct GdnArgs {
+    const void* o;
+    const void* z;
+    const void* gamma;
+    void* y;
+    int64_t T;
+    int heads;
+    float eps;
+    float w_offset;
+    int gate_mode;
+    int stages;
+    uint32_t row_bytes;  // heads * hd * sizeof(TI)
+    uint32_t stage_bytes;
+};
+
+template <typename TI, typename TO, int HD, int VPT>
+__global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) gdn_norm_kernel(const GdnArgs a) {
+    constexpr int L = HD / 8;
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int S = a.stages;
+    const int64_t G = gridDim.x;
+    const int64_t first = blockIdx.x;
+    if (first >= a.T) return;
+    const int64_t my_units = (a.T - 1 - first) / G + 1;
+    const RingSmem ring = ring_carve(smem, S);
+    ring_init(ring, S);
+
+    const int tid = threadIdx.x;
+    const int row_elems = a.heads * HD;
+    const TI* __restrict__ o = static_cast<const TI*>(a.o);
+    const TI* __restrict__ z = static_cast<const TI*>(a.z);
+    TO* __restrict__ y = static_cast<TO*>(a.y);
+
+    uint64_t pol = 0;
+    int64_t issued = 0;
+    auto issue = [&](int64_t i) {
+        const int s = (int)(i % S);
+        const int64_t t = first + i * G;
+        unsigned char* st = ring.data + (size_t)s * a.stage_bytes;
+        mbar_arrive_expect_tx(&ring.full[s], a.stage_bytes);
+        bulk_load(st, o + t * row_elems, a.row_bytes, &ring.full[s], pol);
+        bulk_load(st + a.row_bytes, z + t * row_elems, a.row_bytes, &ring.full[s], pol);
+    };
+    if (tid == 0) {
+        pol = policy_evict_first();
+        issued = my_units < S ? my_units : (int64_t)S;
+        for (int64_t i = 0; i < issued; ++i) issue(i);
+    }
+
+    int col[VPT];  // element offset inside the row
+    bool act[VPT];
+    float g[VPT][8];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+        const int j = k * (int)blockDim.x + tid;
+        col[k] = j * 8;
+        act[k] = col[k] < row_elems;
+        if (act[k]) {
+            Vec8<TI>::load_ro(static_cast<const TI*>(a.gamma) + (j % L) * 8, g[k]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) g[k][e] = a.w_offset + g[k][e];
+        }
+    }
+    const bool silu = a.gate_mode == WZYB_GATE_SILU;
+
+    for (int64_t i = 0; i < my_units; ++i) {
+        const int s = (int)(i % S);
+        const int64_t t = first + i * G;
+        const bool ok = mbar_wait(&ring.full[s], (uint32_t)((i / S) & 1));
+        if (!ok) *ring.abort_flag = 1;
+        float ov[VPT][8], zv[VPT][8];
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            if (act[k] && ok) {
+                const TI* so = reinterpret_cast<const TI*>(ring.data + (size_t)s * a.stage_bytes);
+                const TI* sz = reinterpret_cast<const TI*>(ring.data + (size_t)s * a.stage_bytes + a.row_bytes);
+                Vec8<TI>::load(so + col[k], ov[k]);
+                Vec8<TI>::load(sz + col[k], zv[k]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ov[k][e] = zv[k][e] = 0.f;
+            }
+        }
+        __syncthreads();  // the unit is in registers: the stage may be refilled
+        if (*ring.abort_flag) {
+            ring_drain(ring, S, i, issued);
+            return;
+        }
+        if (tid == 0 && issued < my_units) {
+            issue(issued);
+            ++issued;
+        }
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            float ss = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ss += ov[k][e] * ov[k][e];
+            ss = group_sum<L>(ss);
+            const float sc = rsqrtf(ss * (1.0f / (float)HD) + a.eps);
+            float out[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float den = 1.0f + __expf(-zv[k][e]);
+                out[e] = silu ? (ov[k][e] * sc * g[k][e]) * (zv[k][e] / den) : ov[k][e] * sc * g[k][e] / den;
+            }
+            if (act[k]) Vec8<TO>::store(y + t * row_elems + col[k], out);
+        }
+    }
+}
+
+template <typename TI, typename TO>
+static int launch_gdn(const void* o, const void* z, const void* gamma, void* y, int64_t T, int heads, int hd, float eps,
+                      float w_offset, int gate_mode, cudaStream_t stream) {
+    if (o == nullptr || z == nullptr || gamma == nullptr || y == nullptr) return WZYB_ERR_NULL;
+    if (gate_mode != WZYB_GATE_SIGMOID && gate_mode != WZYB_GATE_SILU) return WZYB_ERR_VALUE;
+    if (hd != 64 && hd != 128 && hd != 256) return WZYB_ERR_SHAPE;
+    if (T < 0 || T > (int64_t(1) << 40) || heads < 1 || heads > 512) return WZYB_ERR_SHAPE;
+    if (!aligned16(o) || !aligned16(z) || !aligned16(gamma) || !aligned16(y)) return WZYB_ERR_ALIGN;
+    if (T == 0) return WZYB_OK;
+    DeviceInfo di;
+    int rc = device_info(&di);
+    if (rc != WZYB_OK) return rc;
+
+    GdnArgs a;
+    a.o = o;
+    a.z = z;
+    a.gamma = gamma;
+    a.y = y;
+    a.T = T;
+    a.heads = heads;
+    a.eps = eps;
+    a.w_offset = w_offset;
+    a.gate_mode = gate_mode;
+    a.row_bytes = (uint32_t)((int64_t)heads * hd * sizeof(TI));
+    a.stage_bytes = 2u * a.row_bytes;
+    const int slots = heads * hd / 8;
+    const int vpt = slots <= 1024 ? 1 : 4;  // VPT 4 keeps the CTA at <= 512 threads (128 registers)
+    if (slots > 2048) return WZYB_ERR_SHAPE;
+    const int threads = ((slots + vpt - 1) / vpt + 31) / 32 * 32;
+
+    const Tuning tu = tuning(kFamGdn);
+    const int budget =
+        kSmemPerSm / tu.ctas_per_sm < di.max_smem_optin ? kSmemPerSm / tu.ctas_per_sm : di.max_smem_optin;
+    int S = tu.stages > 0 ? tu.stages : (int)((budget - (int)ring_header_bytes(32)) / (int)a.stage_bytes);
+    if (S > 32) S = 32;
+    while (S > 1 && (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes) > di.max_smem_optin) --S;
+    if (S < 1 || (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes) > di.max_smem_optin) return WZYB_ERR_SHAPE;
+    a.stages = S;
+    const int smem = (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes);
+    const int64_t want = (int64_t)di.sms * tu.ctas_per_sm;
+    const int grid = (int)(T < want ? T : want);
+
+#define WZYB_GDN_CASE(HDV, V)                                                      \
+    if (hd == HDV && vpt == V) {                                                   \
+        rc = ensure_smem((const void*)gdn_norm_kernel<TI, TO, HDV, V>, smem);      \
+        if (rc != WZYB_OK) return rc;                                              \
+        gdn_norm_kernel<TI, TO, HDV, V><<<grid, threads, smem, stream>>>(a);       \
+        return launch_status();                                                    \
+    }
+    WZYB_GDN_CASE(64, 1)
+    WZYB_GDN_CASE(64, 4)
+    WZYB_GDN_CASE(128, 1)
+    WZYB_GDN_CASE(128, 4)
+    WZYB_GDN_CASE(256, 1)
+    WZYB_GDN_CASE(256, 4)
+#undef WZYB_GDN_CASE
+    return WZYB_ERR_SHAPE;
+}
+
+}  // namespace wzyb
+
+extern "C" {
+
+int wzyb_gdn_gated_norm_f16(const uint16_t* o, const uint16_t* z, const uint16_t* gamma, uint16_t* y, int64_t T,
+                            int heads, int head_dim, float eps, float w_offset, int gate_mode, wzyb_stream_t stream) {
+    return wzyb::launch_gdn<__half, __half>(o, z, gamma, y, T, heads, head_dim, eps, w_offset, gate_mode,
+                                            (cudaStream_t)stream);
+}
+
+int wzyb_gdn_gated_norm_f32_f16(const float* o, const float* z, const float* gamma, uint16_t* y, int64_t T, int heads,
+                                int head_dim, float eps, float w_offset, int gate_mode, wzyb_stream_t stream) {
+    return wzyb::launch_gdn<float, __half>(o, z, gamma, y, T, heads, head_dim, eps, w_offset, gate_mode,
+                                           (cudaStream_t)stream);
+}
+
+}  // extern "C"

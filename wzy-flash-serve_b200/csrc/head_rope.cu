@@ -1,0 +1,346 @@
+// head_rope.cu -- per-head RMSNorm + partial NeoX RoPE, in place; q and k of a token in one unit.
+//
+// Math follows fused_head_norm_rope_multi (src/wzy_qsa_256k.cuh:50-84):
+//   p *= rsqrt(sum(p^2)/hd + eps) * gamma
+//   (a, d) = (p[i], p[i+R/2]), i < R/2:  p[i] = a*cos - d*sin;  p[i+R/2] = a*sin + d*cos
+// with cos/sin from a [pos][R/2] fp32 table built in fp64 (build_rope_cos_sin_host,
+// src/wzy_qsa_256k.cuh:33-46). The reference runs one 128-thread block per (head, token) with three
+// __syncthreads and rotates on 32 of the 128 threads. Here a unit is one token (all q heads + all k
+// heads), staged by TMA bulk copies (ring.cuh); each head is owned by hd/8 lanes holding 8 elements
+// each, reduced with xor shuffles inside the lane group, and the rotation partner (i +- R/2) is the
+// lane R/16 positions away, fetched with one shuffle per element. No shared-memory reduction.
+#include <cmath>
+
+#include "launch.hpp"
+#include "ring.cuh"
+
+namespace wzyb {
+
+struct HeadSection {
+    void* data;
+    const void* gamma;
+    int heads;
+    int64_t head_stride;
+    int64_t row_stride;
+};
+
+struct HeadRopeArgs {
+    HeadSection sec[2];  // q, k (k.heads may be 0)
+    const float* cos_tab;
+    const float* sin_tab;
+    int64_t table_rows;
+    const int32_t* d_base_pos;
+    int64_t pos_offset;
+    int64_t T;
+    int rot;  // rot_dims
+    float eps;
+    float w_offset;
+    int stages;
+    uint32_t head_bytes;   // hd * sizeof(T)
+    uint32_t stage_bytes;  // (heads_q + heads_k) * head_bytes
+    int contig[2];         // head_stride == hd: one bulk copy per section
+};
+
+template <typename T, int HD, int VPT>
+__global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) head_rope_kernel(const HeadRopeArgs a) {
+    constexpr int L = HD / 8;  // lanes per head (8, 16 or 32)
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int S = a.stages;
+    const int64_t G = gridDim.x;
+    const int64_t first = blockIdx.x;
+    if (first >= a.T) return;
+    const int64_t my_units = (a.T - 1 - first) / G + 1;
+    const RingSmem ring = ring_carve(smem, S);
+    ring_init(ring, S);
+
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int hq = a.sec[0].heads, hk = a.sec[1].heads, htot = hq + hk;
+
+    uint64_t pol = 0;
+    int64_t issued = 0;
+    auto issue = [&](int64_t i) {
+        const int s = (int)(i % S);
+        const int64_t t = first + i * G;
+        unsigned char* st = ring.data + (size_t)s * a.stage_bytes;
+        mbar_arrive_expect_tx(&ring.full[s], a.stage_bytes);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const HeadSection& sc = a.sec[q];
+            if (sc.heads == 0) continue;
+            const T* base = static_cast<const T*>(sc.data) + t * sc.row_stride;
+            if (a.contig[q]) {
+                bulk_load(st, base, a.head_bytes * sc.heads, &ring.full[s], pol);
+            } else {
+                for (int h = 0; h < sc.heads; ++h)
+                    bulk_load(st + (size_t)h * a.head_bytes, base + h * sc.head_stride, a.head_bytes, &ring.full[s],
+                              pol);
+            }
+            st += (size_t)sc.heads * a.head_bytes;
+        }
+    };
+    if (tid == 0) {
+        pol = policy_evict_first();
+        issued = my_units < S ? my_units : (int64_t)S;
+        for (int64_t i = 0; i < issued; ++i) issue(i);
+    }
+
+    // Fixed per-thread ownership: slot j = tid + k*blockDim -> head j / L, lane-in-head j % L.
+    const int half = a.rot / 2;  // rotated pairs per head
+    const int hl = half / 8;     // lanes per rotation half
+    int head[VPT], li[VPT], sec[VPT];
+    bool act[VPT];
+    float g[VPT][8];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+        const int j = k * (int)blockDim.x + tid;
+        head[k] = j / L;
+        li[k] = j % L;
+        act[k] = head[k] < htot;
+        sec[k] = head[k] < hq ? 0 : 1;
+        if (act[k]) {
+            const T* gm = static_cast<const T*>(a.sec[sec[k]].gamma);
+            Vec8<T>::load_ro(gm + li[k] * 8, g[k]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) g[k][e] = a.w_offset + g[k][e];
+        }
+    }
+    const int64_t base_pos = (a.d_base_pos ? (int64_t)__ldg(a.d_base_pos) : 0) + a.pos_offset;
+
+    for (int64_t i = 0; i < my_units; ++i) {
+        const int s = (int)(i % S);
+        const int64_t t = first + i * G;
+        const bool ok = mbar_wait(&ring.full[s], (uint32_t)((i / S) & 1));
+        if (!ok) *ring.abort_flag = 1;
+        float p[VPT][8];
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            if (act[k] && ok) {
+                const T* sp =
+                    reinterpret_cast<const T*>(ring.data + (size_t)s * a.stage_bytes + (size_t)head[k] * a.head_bytes);
+                Vec8<T>::load(sp + li[k] * 8, p[k]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) p[k][e] = 0.f;
+            }
+        }
+        __syncthreads();  // every thread has its unit in registers: the stage may be refilled
+        if (*ring.abort_flag) {
+            ring_drain(ring, S, i, issued);
+            return;
+        }
+        if (tid == 0 && issued < my_units) {
+            issue(issued);
+            ++issued;
+        }
+        const int64_t pos = base_pos + t;
+        const bool pos_ok = pos >= 0 && pos < a.table_rows;
+        if (!pos_ok && tid == 0 && a.rot > 0) raise_fault(WZYB_FAULT_POS_RANGE);
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            // sum of squares over the head's L lanes (lanes of one head are an aligned group)
+            float ss = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ss += p[k][e] * p[k][e];
+            ss = group_sum<L>(ss);
+            const float sc = rsqrtf(ss / (float)HD + a.eps);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) p[k][e] *= sc * g[k][e];
+
+            // partial rotary on dims [0, rot): lane-in-head li < hl holds the first halves,
+            // hl <= li < 2*hl the second halves; the partner is hl lanes away.
+            const bool rot_lane = li[k] < 2 * hl;
+            const bool first_half = li[k] < hl;
+            const int src = rot_lane ? (first_half ? lane + hl : lane - hl) : lane;
+            float q2[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) q2[e] = __shfl_sync(0xffffffffu, p[k][e], src);
+            if (rot_lane && act[k] && pos_ok) {
+                const int ci = (first_half ? li[k] : li[k] - hl) * 8;
+                const float4* cp = reinterpret_cast<const float4*>(a.cos_tab + pos * half + ci);
+                const float4* sp = reinterpret_cast<const float4*>(a.sin_tab + pos * half + ci);
+                const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
+                const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+                if (first_half) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) p[k][e] = p[k][e] * cs[e] - q2[e] * sn[e];  // a*cos - d*sin
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) p[k][e] = q2[e] * sn[e] + p[k][e] * cs[e];  // a*sin + d*cos
+                }
+            }
+            if (act[k]) {
+                const HeadSection& scn = a.sec[sec[k]];
+                const int hh = sec[k] == 0 ? head[k] : head[k] - hq;
+                T* dst = static_cast<T*>(scn.data) + t * scn.row_stride + hh * scn.head_stride + li[k] * 8;
+                Vec8<T>::store(dst, p[k]);
+            }
+        }
+    }
+}
+
+template <typename T>
+static int launch_head_rope(const HeadSection& q, const HeadSection& k, const float* cos_tab, const float* sin_tab,
+                            int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset, int64_t T_, int hd,
+                            int rot, float eps, float w_offset, cudaStream_t stream) {
+    if (q.data == nullptr || q.gamma == nullptr) return WZYB_ERR_NULL;
+    if (k.heads > 0 && (k.data == nullptr || k.gamma == nullptr)) return WZYB_ERR_NULL;
+    if (rot > 0 && (cos_tab == nullptr || sin_tab == nullptr)) return WZYB_ERR_NULL;
+    if (hd != 64 && hd != 128 && hd != 256) return WZYB_ERR_SHAPE;
+    if (rot < 0 || rot > hd || (rot % 16) != 0) return WZYB_ERR_SHAPE;
+    if (T_ < 0 || T_ > (int64_t(1) << 40) || q.heads < 1 || k.heads < 0 || q.heads + k.heads > 256)
+        return WZYB_ERR_SHAPE;
+    if (rot > 0 && table_rows < 1) return WZYB_ERR_SHAPE;
+    const HeadSection* secs[2] = {&q, &k};
+    for (int s = 0; s < 2; ++s) {
+        const HeadSection& c = *secs[s];
+        if (c.heads == 0) continue;
+        if (c.head_stride < hd && c.heads > 1) return WZYB_ERR_SHAPE;
+        if (c.row_stride < 0 || c.head_stride < 0) return WZYB_ERR_SHAPE;
+        if (!aligned16(c.data) || !aligned16(c.gamma) || ((c.head_stride * (int64_t)sizeof(T)) % 16) != 0 ||
+            ((c.row_stride * (int64_t)sizeof(T)) % 16) != 0)
+            return WZYB_ERR_ALIGN;
+    }
+    if (rot > 0 && (!aligned16(cos_tab) || !aligned16(sin_tab))) return WZYB_ERR_ALIGN;
+    if (T_ == 0) return WZYB_OK;
+    DeviceInfo di;
+    int rc = device_info(&di);
+    if (rc != WZYB_OK) return rc;
+
+    HeadRopeArgs a;
+    a.sec[0] = q;
+    a.sec[1] = k;
+    if (k.heads == 0) a.sec[1] = HeadSection{nullptr, nullptr, 0, 0, 0};
+    a.cos_tab = cos_tab;
+    a.sin_tab = sin_tab;
+    a.table_rows = rot > 0 ? table_rows : 0;
+    a.d_base_pos = d_base_pos;
+    a.pos_offset = pos_offset;
+    a.T = T_;
+    a.rot = rot;
+    a.eps = eps;
+    a.w_offset = w_offset;
+    a.head_bytes = (uint32_t)(hd * sizeof(T));
+    const int htot = q.heads + k.heads;
+    a.stage_bytes = a.head_bytes * (uint32_t)htot;
+    a.contig[0] = (q.head_stride == hd || q.heads == 1) ? 1 : 0;
+    a.contig[1] = (k.head_stride == hd || k.heads <= 1) ? 1 : 0;
+
+    const int slots = htot * (hd / 8);
+    const int vpt = slots <= 1024 ? 1 : 4;  // VPT 4 keeps the CTA at <= 512 threads (128 registers)
+    if (slots > 2048) return WZYB_ERR_SHAPE;
+    const int threads = ((slots + vpt - 1) / vpt + 31) / 32 * 32;
+
+    const Tuning tu = tuning(kFamHeadRope);
+    const int budget =
+        kSmemPerSm / tu.ctas_per_sm < di.max_smem_optin ? kSmemPerSm / tu.ctas_per_sm : di.max_smem_optin;
+    int S = tu.stages > 0 ? tu.stages : (int)((budget - (int)ring_header_bytes(32)) / (int)a.stage_bytes);
+    if (S > 32) S = 32;
+    while (S > 1 && (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes) > di.max_smem_optin) --S;
+    if (S < 1 || (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes) > di.max_smem_optin) return WZYB_ERR_SHAPE;
+    a.stages = S;
+    const int smem = (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes);
+    const int64_t want = (int64_t)di.sms * tu.ctas_per_sm;
+    const int grid = (int)(T_ < want ? T_ : want);
+
+#define WZYB_HR_CASE(HDV, V)                                                       \
+    if (hd == HDV && vpt == V) {                                                   \
+        rc = ensure_smem((const void*)head_rope_kernel<T, HDV, V>, smem);          \
+        if (rc != WZYB_OK) return rc;                                              \
+        head_rope_kernel<T, HDV, V><<<grid, threads, smem, stream>>>(a);           \
+        return launch_status();                                                    \
+    }
+    WZYB_HR_CASE(64, 1)
+    WZYB_HR_CASE(64, 4)
+    WZYB_HR_CASE(128, 1)
+    WZYB_HR_CASE(128, 4)
+    WZYB_HR_CASE(256, 1)
+    WZYB_HR_CASE(256, 4)
+#undef WZYB_HR_CASE
+    return WZYB_ERR_SHAPE;
+}
+
+// ---------------------------------------------------------------------------------------------
+// RoPE cos/sin table on the device: one thread per (pos, i), fp64 pow and sincos, rounded to fp32.
+// ---------------------------------------------------------------------------------------------
+__global__ void rope_table_kernel(float* cos_tab, float* sin_tab, int64_t rows, int half, double theta, int rot) {
+    const int64_t n = rows * half;
+    for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < n;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t p = idx / half;
+        const int i = (int)(idx - p * half);
+        const double inv = pow(theta, -2.0 * (double)i / (double)rot);
+        const double ang = (double)p * inv;
+        double sv, cv;
+        sincos(ang, &sv, &cv);
+        cos_tab[idx] = (float)cv;
+        sin_tab[idx] = (float)sv;
+    }
+}
+
+}  // namespace wzyb
+
+extern "C" {
+
+int wzyb_head_norm_rope_f16(uint16_t* data, const uint16_t* gamma, const float* cos_tab, const float* sin_tab,
+                            int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset, int64_t T, int heads,
+                            int head_dim, int64_t head_stride, int64_t row_stride, int rot_dims, float eps,
+                            float w_offset, wzyb_stream_t stream) {
+    const wzyb::HeadSection q{data, gamma, heads, head_stride, row_stride};
+    const wzyb::HeadSection k{nullptr, nullptr, 0, 0, 0};
+    return wzyb::launch_head_rope<__half>(q, k, cos_tab, sin_tab, table_rows, d_base_pos, pos_offset, T, head_dim,
+                                          rot_dims, eps, w_offset, (cudaStream_t)stream);
+}
+
+int wzyb_head_norm_rope_f32(float* data, const float* gamma, const float* cos_tab, const float* sin_tab,
+                            int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset, int64_t T, int heads,
+                            int head_dim, int64_t head_stride, int64_t row_stride, int rot_dims, float eps,
+                            float w_offset, wzyb_stream_t stream) {
+    const wzyb::HeadSection q{data, gamma, heads, head_stride, row_stride};
+    const wzyb::HeadSection k{nullptr, nullptr, 0, 0, 0};
+    return wzyb::launch_head_rope<float>(q, k, cos_tab, sin_tab, table_rows, d_base_pos, pos_offset, T, head_dim,
+                                         rot_dims, eps, w_offset, (cudaStream_t)stream);
+}
+
+int wzyb_qk_norm_rope_f16(const wzyb_head_tensor* q, const wzyb_head_tensor* k, const float* cos_tab,
+                          const float* sin_tab, int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset,
+                          int64_t T, int head_dim, int rot_dims, float eps, float w_offset, wzyb_stream_t stream) {
+    if (q == nullptr) return WZYB_ERR_NULL;
+    const wzyb::HeadSection qs{q->data, q->gamma, q->heads, q->head_stride, q->row_stride};
+    wzyb::HeadSection ks{nullptr, nullptr, 0, 0, 0};
+    if (k != nullptr && k->heads > 0) ks = wzyb::HeadSection{k->data, k->gamma, k->heads, k->head_stride, k->row_stride};
+    return wzyb::launch_head_rope<__half>(qs, ks, cos_tab, sin_tab, table_rows, d_base_pos, pos_offset, T, head_dim,
+                                          rot_dims, eps, w_offset, (cudaStream_t)stream);
+}
+
+int wzyb_rope_table_host_f32(float* h_cos, float* h_sin, int64_t rows, int rot_dims, double theta) {
+    if (h_cos == nullptr || h_sin == nullptr) return WZYB_ERR_NULL;
+    if (rows < 0 || rot_dims < 2 || (rot_dims % 2) != 0) return WZYB_ERR_SHAPE;
+    const int half = rot_dims / 2;
+    for (int i = 0; i < half; ++i) {
+        const double inv = std::pow(theta, -2.0 * (double)i / (double)rot_dims);
+        for (int64_t p = 0; p < rows; ++p) {
+            const double ang = (double)p * inv;
+            h_cos[p * half + i] = (float)std::cos(ang);
+            h_sin[p * half + i] = (float)std::sin(ang);
+        }
+    }
+    return WZYB_OK;
+}
+
+int wzyb_rope_table_f32(float* d_cos, float* d_sin, int64_t rows, int rot_dims, double theta, wzyb_stream_t stream) {
+    if (d_cos == nullptr || d_sin == nullptr) return WZYB_ERR_NULL;
+    if (rows < 0 || rot_dims < 2 || (rot_dims % 2) != 0) return WZYB_ERR_SHAPE;
+    if (rows == 0) return WZYB_OK;
+    wzyb::DeviceInfo di;
+    const int rc = wzyb::device_info(&di);
+    if (rc != WZYB_OK) return rc;
+    const int half = rot_dims / 2;
+    const int64_t n = rows * half;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > (int64_t)di.sms * 16) blocks = (int64_t)di.sms * 16;
+    wzyb::rope_table_kernel<<<(int)blocks, 256, 0, (cudaStream_t)stream>>>(d_cos, d_sin, rows, half, theta, rot_dims);
+    return wzyb::launch_status();
+}
+
+}  // extern "C"

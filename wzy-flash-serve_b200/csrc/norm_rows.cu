@@ -1,0 +1,226 @@
+// norm_rows.cu -- residual add + RMSNorm over rows, one HBM pass.
+//
+// Math follows fused_gr_norm_multi (src/wzy_kernels_v2.cuh:409-456) and its prefill twin
+// pf_gr_norm_fp16 (src/wzy_qsa_wmma.cuh:197-232):
+//   v = R + bo * gw          gw = 2*sigmoid(inj/hc) (exactly 1.0 for the single-stream add)
+//   R <- v;  xn = (v * rsqrt(sum(v^2)/n + eps)) * g
+// The reference runs one 256-thread block per (stream, token) row, reads R twice (the second pass
+// re-reads it from cache) with scalar 4-byte accesses. Here each unit (= one row of R) is staged
+// into shared memory by a TMA bulk copy S units ahead (ring.cuh), read once into registers, reduced
+// with one warp-shuffle + one CTA barrier, and both outputs are written with 16-byte stores.
+#include "launch.hpp"
+#include "ring.cuh"
+
+namespace wzyb {
+
+struct NormRowsArgs {
+    const void* x;     // bo_prev [T, n] (NULL: plain RMSNorm of res, res not written)
+    void* res;         // R [T*hc, n]
+    const void* w;     // gamma [hc, n]
+    const float* inj;  // [T*hc] inject logits (NULL: gate 1.0)
+    void* y;           // xn [T*hc, n]
+    int64_t units;     // T * hc
+    int n;
+    int hc;
+    float eps;
+    float w_offset;
+    int stages;
+    uint32_t row_bytes;
+    uint32_t stage_bytes;
+};
+
+template <typename TI, typename TO, int VPT>
+__global__ void __launch_bounds__(512) norm_rows_kernel(const NormRowsArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int S = a.stages;
+    const int64_t G = gridDim.x;
+    const int64_t first = blockIdx.x;
+    if (first >= a.units) return;  // uniform across the CTA
+    const int64_t my_units = (a.units - 1 - first) / G + 1;
+    const RingSmem ring = ring_carve(smem, S);
+    ring_init(ring, S);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    const TI* __restrict__ x = static_cast<const TI*>(a.x);
+    TI* __restrict__ res = static_cast<TI*>(a.res);
+    const TI* __restrict__ w = static_cast<const TI*>(a.w);
+    TO* __restrict__ y = static_cast<TO*>(a.y);
+    const bool has_x = x != nullptr;
+    const int n = a.n;
+
+    uint64_t pol = 0;
+    int64_t issued = 0;
+    auto issue = [&](int64_t i) {
+        const int s = (int)(i % S);
+        const int64_t u = first + i * G;
+        unsigned char* st = ring.data + (size_t)s * a.stage_bytes;
+        mbar_arrive_expect_tx(&ring.full[s], a.stage_bytes);
+        bulk_load(st, res + u * n, a.row_bytes, &ring.full[s], pol);
+        if (has_x) bulk_load(st + a.row_bytes, x + (u / a.hc) * n, a.row_bytes, &ring.full[s], pol);
+    };
+    if (tid == 0) {
+        pol = policy_evict_first();
+        issued = my_units < S ? my_units : (int64_t)S;
+        for (int64_t i = 0; i < issued; ++i) issue(i);
+    }
+
+    int col[VPT];
+    bool act[VPT];
+    float g[VPT][8];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+        col[k] = (k * (int)blockDim.x + tid) * 8;
+        act[k] = col[k] < n;
+        if (act[k] && a.hc == 1) {
+            Vec8<TI>::load_ro(w + col[k], g[k]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) g[k][j] = a.w_offset + g[k][j];
+        }
+    }
+
+    for (int64_t i = 0; i < my_units; ++i) {
+        const int s = (int)(i % S);
+        const int64_t u = first + i * G;
+        const bool ok = mbar_wait(&ring.full[s], (uint32_t)((i / S) & 1));
+        if (!ok) *ring.abort_flag = 1;
+        float v[VPT][8];
+        float ss = 0.f;
+        {
+            const TI* sr = reinterpret_cast<const TI*>(ring.data + (size_t)s * a.stage_bytes);
+            const TI* sx = reinterpret_cast<const TI*>(ring.data + (size_t)s * a.stage_bytes + a.row_bytes);
+            float gate = 1.0f;
+            if (has_x && a.inj != nullptr) gate = 2.0f / (1.0f + __expf(-a.inj[u] / (float)a.hc));
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+                if (act[k] && ok) {
+                    Vec8<TI>::load(sr + col[k], v[k]);
+                    if (has_x) {
+                        float xv[8];
+                        Vec8<TI>::load(sx + col[k], xv);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) v[k][j] += xv[j] * gate;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) ss += v[k][j] * v[k][j];
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v[k][j] = 0.f;
+                }
+            }
+        }
+        ss = group_sum<32>(ss);
+        if (lane == 0) ring.red[(i & 1) * 32 + warp] = ss;
+        __syncthreads();
+        if (*ring.abort_flag) {
+            ring_drain(ring, S, i, issued);
+            return;
+        }
+        if (tid == 0 && issued < my_units) {
+            issue(issued);
+            ++issued;
+        }
+        float tot = 0.f;
+        for (int q = 0; q < nwarps; ++q) tot += ring.red[(i & 1) * 32 + q];
+        const float sc = rsqrtf(tot / (float)n + a.eps);
+        const int c = (int)(u % a.hc);
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            if (!act[k]) continue;
+            float gk[8];
+            if (a.hc == 1) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) gk[j] = g[k][j];
+            } else {
+                Vec8<TI>::load_ro(w + (size_t)c * n + col[k], gk);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) gk[j] = a.w_offset + gk[j];
+            }
+            float o[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = (v[k][j] * sc) * gk[j];
+            Vec8<TO>::store(y + u * n + col[k], o);
+            if (has_x) Vec8<TI>::store(res + u * n + col[k], v[k]);
+        }
+    }
+}
+
+template <typename TI, typename TO>
+static int launch_norm_rows(const void* x, void* res, const void* w, const float* inj, void* y, int64_t T, int n,
+                            int hc, float eps, float w_offset, cudaStream_t stream) {
+    if (res == nullptr || w == nullptr || y == nullptr) return WZYB_ERR_NULL;
+    if (T < 0 || T > (int64_t(1) << 40) || n < 8 || n > 16384 || (n % 8) != 0 || hc < 1 || hc > 64)
+        return WZYB_ERR_SHAPE;
+    if (!aligned16(res) || !aligned16(w) || !aligned16(y) || (x && !aligned16(x))) return WZYB_ERR_ALIGN;
+    if (T == 0) return WZYB_OK;
+    DeviceInfo di;
+    int rc = device_info(&di);
+    if (rc != WZYB_OK) return rc;
+
+    const int vpt = n <= 4096 ? 1 : (n <= 8192 ? 2 : 4);
+    const int vecs = n / 8;
+    const int threads = ((vecs + vpt - 1) / vpt + 31) / 32 * 32;
+    NormRowsArgs a;
+    a.x = x;
+    a.res = res;
+    a.w = w;
+    a.inj = x ? inj : nullptr;
+    a.y = y;
+    a.units = T * hc;
+    a.n = n;
+    a.hc = hc;
+    a.eps = eps;
+    a.w_offset = w_offset;
+    a.row_bytes = (uint32_t)(n * sizeof(TI));
+    a.stage_bytes = a.row_bytes * (x ? 2u : 1u);
+
+    const Tuning tu = tuning(kFamNorm);
+    const int budget = (kSmemPerSm / tu.ctas_per_sm < di.max_smem_optin ? kSmemPerSm / tu.ctas_per_sm
+                                                                          : di.max_smem_optin);
+    int S = tu.stages > 0 ? tu.stages : (int)((budget - (int)ring_header_bytes(32)) / (int)a.stage_bytes);
+    if (S > 32) S = 32;
+    while (S > 1 && (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes) > di.max_smem_optin) --S;
+    if (S < 1 || (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes) > di.max_smem_optin) return WZYB_ERR_SHAPE;
+    a.stages = S;
+    const int smem = (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes);
+    const int64_t want = (int64_t)di.sms * tu.ctas_per_sm;
+    const int grid = (int)(a.units < want ? a.units : want);
+
+    const void* kern = nullptr;
+    switch (vpt) {
+        case 1: kern = (const void*)norm_rows_kernel<TI, TO, 1>; break;
+        case 2: kern = (const void*)norm_rows_kernel<TI, TO, 2>; break;
+        default: kern = (const void*)norm_rows_kernel<TI, TO, 4>; break;
+    }
+    rc = ensure_smem(kern, smem);
+    if (rc != WZYB_OK) return rc;
+    switch (vpt) {
+        case 1: norm_rows_kernel<TI, TO, 1><<<grid, threads, smem, stream>>>(a); break;
+        case 2: norm_rows_kernel<TI, TO, 2><<<grid, threads, smem, stream>>>(a); break;
+        default: norm_rows_kernel<TI, TO, 4><<<grid, threads, smem, stream>>>(a); break;
+    }
+    return launch_status();
+}
+
+}  // namespace wzyb
+
+extern "C" {
+
+int wzyb_add_rmsnorm_f16(const uint16_t* x, uint16_t* residual, const uint16_t* weight, uint16_t* y, int64_t T,
+                         int hidden, float eps, float w_offset, wzyb_stream_t stream) {
+    return wzyb::launch_norm_rows<__half, __half>(x, residual, weight, nullptr, y, T, hidden, 1, eps, w_offset,
+                                                  (cudaStream_t)stream);
+}
+
+int wzyb_gr_norm_f32(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, float* xn,
+                     int64_t T, int n_embd, int hc, float eps, wzyb_stream_t stream) {
+    return wzyb::launch_norm_rows<float, float>(bo_prev, R, w_norm, inj_prev, xn, T, n_embd, hc, eps, 0.0f,
+                                                (cudaStream_t)stream);
+}
+
+int wzyb_gr_norm_f32_f16(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, uint16_t* xn,
+                         int64_t T, int n_embd, int hc, float eps, wzyb_stream_t stream) {
+    return wzyb::launch_norm_rows<float, __half>(bo_prev, R, w_norm, inj_prev, xn, T, n_embd, hc, eps, 0.0f,
+                                                 (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,286 @@
+"""ctypes binding of libwzyb200.so, the C ABI declared in include/wzyb200.h.
+
+The kernels, their launchers and the host-side executor are native (CUDA/C++ in csrc/). This module
+only loads the shared library, declares the entry points, and offers thin wrappers that take torch
+tensors (torch is used for device memory and streams) and raise on a non-zero status.
+
+There is no fallback: if the library is missing or the device is not an sm_100 GPU the calls raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_double, c_float, c_int, c_int32, c_int64, c_uint32, c_void_p
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libwzyb200.so")
+HEADER_PATH = os.path.join(os.path.dirname(HERE), "include", "wzyb200.h")
+
+OK = 0
+ERR_NULL, ERR_ALIGN, ERR_SHAPE, ERR_DEVICE, ERR_VALUE = -1, -2, -3, -4, -5
+FAULT_WAIT_TIMEOUT, FAULT_POS_RANGE = 0x1, 0x2
+GATE_SIGMOID, GATE_SILU = 0, 1
+OOB_CLAMP, OOB_ZERO_ID = 0, 1
+PLE_HASH_C_PRECEDENCE, PLE_HASH_XOR_THEN_ADD = 0, 1
+PLE_EOS_DEFAULT = 248044
+FAM_NORM, FAM_HEAD_ROPE, FAM_GDN, FAM_SWIGLU, FAM_GATHER = 0, 1, 2, 3, 4
+
+
+class WzybError(RuntimeError):
+    def __init__(self, fn: str, code: int, msg: str):
+        super().__init__(f"{fn} returned {code}: {msg}")
+        self.code = code
+
+
+class HeadTensor(ctypes.Structure):
+    _fields_ = [
+        ("data", c_void_p),
+        ("gamma", c_void_p),
+        ("heads", c_int),
+        ("head_stride", c_int64),
+        ("row_stride", c_int64),
+    ]
+
+
+class AttnPrepArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", c_void_p),
+        ("residual", c_void_p),
+        ("norm_weight", c_void_p),
+        ("normed", c_void_p),
+        ("hidden", c_int),
+        ("q", HeadTensor),
+        ("k", HeadTensor),
+        ("head_dim", c_int),
+        ("rot_dims", c_int),
+        ("cos_tab", c_void_p),
+        ("sin_tab", c_void_p),
+        ("table_rows", c_int64),
+        ("d_base_pos", c_void_p),
+        ("pos_offset", c_int64),
+        ("eps", c_float),
+        ("w_offset", c_float),
+    ]
+
+
+class ActArgs(ctypes.Structure):
+    _fields_ = [
+        ("gate", c_void_p),
+        ("up", c_void_p),
+        ("act", c_void_p),
+        ("act_rows", c_int64),
+        ("ffn", c_int),
+        ("o", c_void_p),
+        ("z", c_void_p),
+        ("gdn_gamma", c_void_p),
+        ("gdn_out", c_void_p),
+        ("gdn_heads", c_int),
+        ("gdn_head_dim", c_int),
+        ("eps", c_float),
+        ("gdn_w_offset", c_float),
+        ("gate_mode", c_int),
+    ]
+
+
+P = c_void_p
+S = c_void_p  # cudaStream_t
+_SIGS = {
+    "wzyb_add_rmsnorm_f16": (c_int, [P, P, P, P, c_int64, c_int, c_float, c_float, S]),
+    "wzyb_gr_norm_f32": (c_int, [P, P, P, P, P, c_int64, c_int, c_int, c_float, S]),
+    "wzyb_gr_norm_f32_f16": (c_int, [P, P, P, P, P, c_int64, c_int, c_int, c_float, S]),
+    "wzyb_head_norm_rope_f16": (
+        c_int,
+        [P, P, P, P, c_int64, P, c_int64, c_int64, c_int, c_int, c_int64, c_int64, c_int, c_float, c_float, S],
+    ),
+    "wzyb_head_norm_rope_f32": (
+        c_int,
+        [P, P, P, P, c_int64, P, c_int64, c_int64, c_int, c_int, c_int64, c_int64, c_int, c_float, c_float, S],
+    ),
+    "wzyb_qk_norm_rope_f16": (
+        c_int,
+        [POINTER(HeadTensor), POINTER(HeadTensor), P, P, c_int64, P, c_int64, c_int64, c_int, c_int, c_float,
+         c_float, S],
+    ),
+    "wzyb_rope_table_host_f32": (c_int, [P, P, c_int64, c_int, c_double]),
+    "wzyb_rope_table_f32": (c_int, [P, P, c_int64, c_int, c_double, S]),
+    "wzyb_gdn_gated_norm_f16": (c_int, [P, P, P, P, c_int64, c_int, c_int, c_float, c_float, c_int, S]),
+    "wzyb_gdn_gated_norm_f32_f16": (c_int, [P, P, P, P, c_int64, c_int, c_int, c_float, c_float, c_int, S]),
+    "wzyb_swiglu_f16": (c_int, [P, P, P, c_int64, S]),
+    "wzyb_swiglu_f32": (c_int, [P, P, P, c_int64, S]),
+    "wzyb_swiglu_interleaved_f16": (c_int, [P, P, c_int64, c_int, S]),
+    "wzyb_swiglu_interleaved_f32_f16": (c_int, [P, P, c_int64, c_int, S]),
+    "wzyb_embed_gather_rows": (c_int, [P, c_int64, c_int64, P, c_int64, P, c_int, P, S]),
+    "wzyb_embed_gather_f16": (c_int, [P, c_int64, c_int, P, c_int64, P, c_int, P, S]),
+    "wzyb_embed_gather_bf16_f32": (c_int, [P, c_int64, c_int, P, c_int64, P, c_int, P, S]),
+    "wzyb_ple_gather_f16": (
+        c_int,
+        [POINTER(c_void_p), c_int, c_int64, c_int, P, c_int64, POINTER(c_int32), c_int32, c_int, P, S],
+    ),
+    "wzyb_ple_row_index": (c_uint32, [c_int32, c_int32, c_int32, c_int, c_int64, c_int32, c_int]),
+    "wzyb_attn_prep_f16": (c_int, [POINTER(AttnPrepArgs), c_int64, S]),
+    "wzyb_act_f16": (c_int, [POINTER(ActArgs), c_int64, S]),
+    "wzyb_shard_rows": (c_int, [c_int64, c_int, c_int, POINTER(c_int64), POINTER(c_int64)]),
+    "wzyb_ple_halo": (c_int, [POINTER(c_int32), c_int64, POINTER(c_int32), POINTER(c_int32)]),
+    "wzyb_prepare_device": (c_int, []),
+    "wzyb_read_faults": (c_int, [POINTER(c_uint32), c_int]),
+    "wzyb_set_launch_tuning": (c_int, [c_int, c_int, c_int]),
+    "wzyb_status_string": (ctypes.c_char_p, [c_int]),
+    "wzyb_version": (c_int, []),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load libwzyb200.so once (raises OSError when it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise OSError(f"{LIB_PATH} is missing: build it with `make -C wzy-flash-serve_b200`")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def status_string(code: int) -> str:
+    return lib().wzyb_status_string(code).decode()
+
+
+def check(fn: str, code: int) -> None:
+    if code != OK:
+        raise WzybError(fn, code, status_string(code))
+
+
+def call(fn: str, *args) -> None:
+    """Call an int-returning entry point and raise WzybError on a non-zero status."""
+    check(fn, getattr(lib(), fn)(*args))
+
+
+# ------------------------------------------------------------------------------------------------
+# torch-tensor wrappers (device pointers + the current stream)
+# ------------------------------------------------------------------------------------------------
+def _stream(stream=None):
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return c_void_p(s.cuda_stream)
+
+
+def _ptr(t):
+    return c_void_p(t.data_ptr()) if t is not None else c_void_p(0)
+
+
+def add_rmsnorm_f16(x, residual, weight, y, eps=1e-6, w_offset=1.0, stream=None):
+    T, hidden = residual.shape
+    call("wzyb_add_rmsnorm_f16", _ptr(x), _ptr(residual), _ptr(weight), _ptr(y), T, hidden, eps, w_offset,
+         _stream(stream))
+
+
+def gr_norm_f32(R, w_norm, bo_prev, inj_prev, xn, T, n_embd, hc, eps=1e-6, stream=None):
+    fn = "wzyb_gr_norm_f32" if xn.element_size() == 4 else "wzyb_gr_norm_f32_f16"
+    call(fn, _ptr(R), _ptr(w_norm), _ptr(bo_prev), _ptr(inj_prev), _ptr(xn), T, n_embd, hc, eps, _stream(stream))
+
+
+def head_norm_rope(data, gamma, cos_tab, sin_tab, T, heads, head_dim, head_stride, row_stride, rot_dims=64,
+                   eps=1e-6, w_offset=0.0, d_base_pos=None, pos_offset=0, stream=None):
+    fn = "wzyb_head_norm_rope_f16" if data.element_size() == 2 else "wzyb_head_norm_rope_f32"
+    rows = cos_tab.numel() // max(1, rot_dims // 2) if cos_tab is not None else 0
+    call(fn, _ptr(data), _ptr(gamma), _ptr(cos_tab), _ptr(sin_tab), rows, _ptr(d_base_pos), pos_offset, T, heads,
+         head_dim, head_stride, row_stride, rot_dims, eps, w_offset, _stream(stream))
+
+
+def head_tensor(data, gamma, heads, head_stride, row_stride) -> HeadTensor:
+    return HeadTensor(data.data_ptr(), gamma.data_ptr(), heads, head_stride, row_stride)
+
+
+def qk_norm_rope_f16(q: HeadTensor, k: HeadTensor | None, cos_tab, sin_tab, T, head_dim, rot_dims=64, eps=1e-6,
+                     w_offset=1.0, d_base_pos=None, pos_offset=0, stream=None):
+    rows = cos_tab.numel() // max(1, rot_dims // 2)
+    call("wzyb_qk_norm_rope_f16", ctypes.byref(q), ctypes.byref(k) if k is not None else None, _ptr(cos_tab),
+         _ptr(sin_tab), rows, _ptr(d_base_pos), pos_offset, T, head_dim, rot_dims, eps, w_offset, _stream(stream))
+
+
+def rope_table(cos_tab, sin_tab, rows, rot_dims=64, theta=1e7, stream=None):
+    call("wzyb_rope_table_f32", _ptr(cos_tab), _ptr(sin_tab), rows, rot_dims, theta, _stream(stream))
+
+
+def gdn_gated_norm(o, z, gamma, y, T, heads, head_dim=128, eps=1e-6, w_offset=0.0, gate_mode=GATE_SIGMOID,
+                   stream=None):
+    fn = "wzyb_gdn_gated_norm_f16" if o.element_size() == 2 else "wzyb_gdn_gated_norm_f32_f16"
+    call(fn, _ptr(o), _ptr(z), _ptr(gamma), _ptr(y), T, heads, head_dim, eps, w_offset, gate_mode, _stream(stream))
+
+
+def swiglu(gate, up, out, stream=None):
+    fn = "wzyb_swiglu_f16" if gate.element_size() == 2 else "wzyb_swiglu_f32"
+    call(fn, _ptr(gate), _ptr(up), _ptr(out), gate.numel(), _stream(stream))
+
+
+def swiglu_interleaved(gu, out, T, nff, stream=None):
+    fn = "wzyb_swiglu_interleaved_f16" if gu.element_size() == 2 else "wzyb_swiglu_interleaved_f32_f16"
+    call(fn, _ptr(gu), _ptr(out), T, nff, _stream(stream))
+
+
+def embed_gather_f16(table, ids, out, oob_policy=OOB_CLAMP, oob_count=None, stream=None):
+    vocab, hidden = table.shape
+    call("wzyb_embed_gather_f16", _ptr(table), vocab, hidden, _ptr(ids), ids.numel(), _ptr(out), oob_policy,
+         _ptr(oob_count), _stream(stream))
+
+
+def embed_gather_bf16_f32(table, ids, out, oob_policy=OOB_CLAMP, oob_count=None, stream=None):
+    vocab, hidden = table.shape
+    call("wzyb_embed_gather_bf16_f32", _ptr(table), vocab, hidden, _ptr(ids), ids.numel(), _ptr(out), oob_policy,
+         _ptr(oob_count), _stream(stream))
+
+
+def ple_gather_f16(tables, ids, out, prev_ids=None, eos_id=PLE_EOS_DEFAULT, hash_variant=PLE_HASH_C_PRECEDENCE,
+                   stream=None):
+    heads = len(tables)
+    rows, hd = tables[0].shape
+    arr = (c_void_p * heads)(*[t.data_ptr() for t in tables])
+    prev = (c_int32 * 2)(*prev_ids) if prev_ids is not None else None
+    call("wzyb_ple_gather_f16", arr, heads, rows, hd, _ptr(ids), ids.numel(), prev, eos_id, hash_variant, _ptr(out),
+         _stream(stream))
+
+
+def ple_row_index(t0, t1, t2, head, rows, eos_id=PLE_EOS_DEFAULT, hash_variant=PLE_HASH_C_PRECEDENCE) -> int:
+    return int(lib().wzyb_ple_row_index(t0, t1, t2, head, rows, eos_id, hash_variant))
+
+
+def shard_rows(total: int, world: int, rank: int) -> tuple[int, int]:
+    r0, n = c_int64(), c_int64()
+    call("wzyb_shard_rows", total, world, rank, ctypes.byref(r0), ctypes.byref(n))
+    return r0.value, n.value
+
+
+def ple_halo(ids_host, row0: int, seq_prev=None) -> tuple[int, int]:
+    """ids_host: a contiguous int32 numpy array (the whole sequence on the host)."""
+    import numpy as np
+
+    arr = np.ascontiguousarray(ids_host, dtype=np.int32)
+    out = (c_int32 * 2)()
+    sp = (c_int32 * 2)(*seq_prev) if seq_prev is not None else None
+    call("wzyb_ple_halo", arr.ctypes.data_as(POINTER(c_int32)) if arr.size else None, row0, sp, out)
+    return int(out[0]), int(out[1])
+
+
+def read_faults(clear=True) -> int:
+    v = c_uint32()
+    call("wzyb_read_faults", ctypes.byref(v), 1 if clear else 0)
+    return int(v.value)
+
+
+def set_launch_tuning(family: int, ctas_per_sm: int, stages: int = 0) -> None:
+    call("wzyb_set_launch_tuning", family, ctas_per_sm, stages)
+
+
+def declared_functions(header_path: str = HEADER_PATH) -> list[str]:
+    """Names of every function the C header declares."""
+    import re
+
+    text = open(header_path).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(wzyb_[a-z0-9_]+)\s*\(", text)))

@@ -174,9 +174,11 @@ def run_e2e(wz, torch, n, row0, dev, steps, chunk=16384):
                 ("z", (GDN_H, GDN_HD))]
     specs_out = [("res", (HIDDEN,)), ("y", (HIDDEN,)), ("q", (QH, HD)), ("k", (KH, HD)),
                  ("act", (EXPERT_ROWS, FFN)), ("gy", (GDN_H, GDN_HD))]
-    g = torch.Generator().manual_seed(7 + row0)
-    hin = {k: (torch.randn((pool_chunks * chunk,) + s, generator=g) * 1.0).to(f16).pin_memory()
-           for k, s in specs_in}
+    g = torch.Generator(device=dev).manual_seed(7 + row0)
+    hin = {}
+    for k, s in specs_in:
+        hin[k] = torch.empty((pool_chunks * chunk,) + s, dtype=f16).pin_memory()
+        hin[k].copy_(torch.randn((pool_chunks * chunk,) + s, generator=g, device=dev).to(f16))
     hout = {k: torch.empty((pool_chunks * chunk,) + s, dtype=f16).pin_memory() for k, s in specs_out}
     streams = [torch.cuda.Stream(device=dev) for _ in range(2)]
     dbuf = []
@@ -248,6 +250,7 @@ def measure_kernels_4096(wz, torch, dev, peak, reps=20):
     T = 4096
     sh = Shard(wz, torch, T, 0, 99, dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush_r = torch.ones(256 << 20, dtype=torch.uint8, device=dev)
     gen = torch.Generator(device=dev).manual_seed(5)
     table = (torch.randn((151936, HIDDEN), generator=gen, device=dev) * 0.02).half()
     ids = torch.randint(0, 151936, (T,), generator=gen, device=dev, dtype=torch.int32)
@@ -266,7 +269,12 @@ def measure_kernels_4096(wz, torch, dev, peak, reps=20):
     for name, fn, nbytes in jobs:
         ts = []
         for r in range(reps + 3):
+            # flush L2: write a buffer larger than L2, then read another one so that the dirty lines
+            # of the write are written back here and not inside the timed kernel
             flush.fill_(r & 0xFF)
+            flush_r.sum(dtype=torch.int32)
+            # keep the stream busy while the host enqueues e0 + the launch, so no host gap is timed
+            torch.cuda._sleep(200000)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(s)
             fn(s)
@@ -278,7 +286,7 @@ def measure_kernels_4096(wz, torch, dev, peak, reps=20):
         gbs = nbytes / (us * 1e-6) / 1e9
         res[name] = {"us": round(us, 2), "bytes": int(nbytes), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
                      "frac_of_8tbs": round(gbs / NOMINAL_HBM_GBS, 4)}
-    del table, ple_tabs, flush
+    del table, ple_tabs, flush, flush_r
     return res
 
 
@@ -343,6 +351,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-kernels", action="store_true")
+    ap.add_argument("--variant", default="auto", choices=["auto", "ring", "direct", "async"],
+                    help="kernel design of the norm families (A/B measurement)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -391,6 +401,10 @@ def main():
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
     wz.check("wzyb_prepare_device", wz.lib().wzyb_prepare_device())
+    var = {"auto": wz.VARIANT_AUTO, "ring": wz.VARIANT_RING, "direct": wz.VARIANT_DIRECT,
+           "async": wz.VARIANT_ASYNC}[args.variant]
+    for fam in (wz.FAM_NORM, wz.FAM_HEAD_ROPE, wz.FAM_GDN):
+        wz.set_kernel_variant(fam, var)
 
     row0, n = wz.shard_rows(args.tokens, world, rank)
     sh = Shard(wz, torch, n, row0, 1000 + rank, dev)
@@ -495,6 +509,7 @@ def main():
                        "tokens": args.tokens, "tokens_per_gpu": n, "hidden": HIDDEN, "q_heads": QH, "kv_heads": KH,
                        "head_dim": HD, "rot_dims": ROT, "expert_rows_per_token": EXPERT_ROWS, "ffn": FFN,
                        "gdn_heads": GDN_H, "gdn_head_dim": GDN_HD, "parallelism": f"token-shard x{world}",
+                       "norm_kernel_design": args.variant,
                        "l2": "inputs larger than L2 (no flush)"},
             "hbm": {"bundle_gbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9, 1),
                     "bundle_frac_of_8tbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9 / NOMINAL_HBM_GBS / world, 4),

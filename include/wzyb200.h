@@ -268,6 +268,18 @@ int wzyb_read_faults(uint32_t* faults, int clear);
 #define WZYB_FAM_SWIGLU 3
 #define WZYB_FAM_GATHER 4
 int wzyb_set_launch_tuning(int family, int ctas_per_sm, int stages);
+/* Kernel design per family (process-wide), for A/B measurement:
+ *   WZYB_VARIANT_AUTO   the library's choice for the shape (default)
+ *   WZYB_VARIANT_RING   TMA bulk-copy ring staged through shared memory, one CTA barrier per unit
+ *   WZYB_VARIANT_DIRECT warp-owned units, 16-byte loads prefetched into registers, no CTA barrier
+ *   WZYB_VARIANT_ASYNC  warp-owned units staged in a lane-private shared-memory ring by cp.async
+ * Families 0 (add+RMSNorm), 1 (head norm+RoPE) and 2 (GDN gated norm) have the RING and DIRECT
+ * designs; families 1 and 2 also ASYNC (a family without a design falls back to AUTO). */
+#define WZYB_VARIANT_AUTO 0
+#define WZYB_VARIANT_RING 1
+#define WZYB_VARIANT_DIRECT 2
+#define WZYB_VARIANT_ASYNC 3
+int wzyb_set_kernel_variant(int family, int variant);
 const char* wzyb_status_string(int status);
 int wzyb_version(void);
 

@@ -41,6 +41,17 @@ def _faults_clear(wz):
     wz.read_faults(clear=True)
     yield
     torch.cuda.synchronize()
+    for fam in (wz.FAM_NORM, wz.FAM_HEAD_ROPE, wz.FAM_GDN):
+        wz.set_kernel_variant(fam, wz.VARIANT_AUTO)
+
+
+# The norm families have two kernel designs (TMA ring, direct); parity must hold for both.
+@pytest.fixture(params=["ring", "direct", "async"])
+def variant(request, wz):
+    v = {"ring": wz.VARIANT_RING, "direct": wz.VARIANT_DIRECT, "async": wz.VARIANT_ASYNC}[request.param]
+    for fam in (wz.FAM_NORM, wz.FAM_HEAD_ROPE, wz.FAM_GDN):
+        wz.set_kernel_variant(fam, v)
+    return request.param
 
 
 # ---------------------------------------------------------------------------------------------
@@ -48,7 +59,7 @@ def _faults_clear(wz):
 # ---------------------------------------------------------------------------------------------
 @pytest.mark.parametrize("T,n", [(1, 2048), (3, 2048), (17, 2048), (4096, 2048), (5, 2560), (9, 24),
                                  (7, 5120), (3, 16384), (300, 1000)])
-def test_add_rmsnorm_f16(wz, orc, T, n):
+def test_add_rmsnorm_f16(wz, orc, T, n, variant):
     r = rng(T * 7 + n)
     x, res = f16n(r, (T, n)), f16n(r, (T, n))
     w = f16n(r, (n,), 0.02)
@@ -61,7 +72,7 @@ def test_add_rmsnorm_f16(wz, orc, T, n):
     assert wz.read_faults() == 0
 
 
-def test_rmsnorm_without_add(wz, orc):
+def test_rmsnorm_without_add(wz, orc, variant):
     r = rng(3)
     T, n = 33, 2048
     res, w = f16n(r, (T, n)), f16n(r, (n,), 0.02, 1.0)
@@ -74,7 +85,7 @@ def test_rmsnorm_without_add(wz, orc):
 
 
 @pytest.mark.parametrize("hc,with_inj,out16", [(1, False, False), (4, True, False), (4, True, True), (4, False, True)])
-def test_gr_norm_f32_hyper_connection(wz, orc, hc, with_inj, out16):
+def test_gr_norm_f32_hyper_connection(wz, orc, hc, with_inj, out16, variant):
     r = rng(11 + hc)
     T, n = 19, 2560
     R = r.standard_normal((T * hc, n)).astype(np.float32)
@@ -101,7 +112,7 @@ def _rope_tab(orc, rows, rot, theta=1e7):
 
 
 @pytest.mark.parametrize("T", [1, 5, 4096])
-def test_qk_norm_rope_fused_baseline_shape(wz, orc, T):
+def test_qk_norm_rope_fused_baseline_shape(wz, orc, T, variant):
     """q [T,16,256], k [T,2,256], (1+w) gammas, rot 64, theta 1e7, positions 0..T-1."""
     r = rng(100 + T)
     hd, rot = 256, 64
@@ -120,7 +131,7 @@ def test_qk_norm_rope_fused_baseline_shape(wz, orc, T):
 
 
 @pytest.mark.parametrize("hd,rot", [(256, 0), (256, 16), (256, 128), (256, 256), (128, 64), (64, 32), (128, 48)])
-def test_head_norm_rope_dims(wz, orc, hd, rot):
+def test_head_norm_rope_dims(wz, orc, hd, rot, variant):
     r = rng(hd * 1000 + rot)
     T, H = 13, 3
     x = f16n(r, (T, H, hd))
@@ -134,7 +145,7 @@ def test_head_norm_rope_dims(wz, orc, hd, rot):
     assert_f16_close(host(d).reshape(-1), want, ULP_TOL, f"hd={hd} rot={rot}")
 
 
-def test_head_norm_rope_strided_heads_f32(wz, orc):
+def test_head_norm_rope_strided_heads_f32(wz, orc, variant):
     """The reference's own q layout: heads interleaved with the gate (head_stride = 2*HD), fp32."""
     r = rng(77)
     T, H, hd, rot = 6, 24, 256, 64
@@ -150,7 +161,7 @@ def test_head_norm_rope_strided_heads_f32(wz, orc):
     assert np.array_equal(got.reshape(T, H, 2 * hd)[..., hd:], buf[..., hd:])
 
 
-def test_head_norm_rope_position_out_of_table(wz, orc):
+def test_head_norm_rope_position_out_of_table(wz, orc, variant):
     """Positions past the table are flagged (fault bit), not read; those heads stay un-rotated."""
     r = rng(5)
     T, H, hd, rot = 8, 2, 128, 64
@@ -168,8 +179,8 @@ def test_head_norm_rope_position_out_of_table(wz, orc):
 # GDN gated norm
 # ---------------------------------------------------------------------------------------------
 @pytest.mark.parametrize("T,H,hd,mode", [(4096, 32, 128, 0), (7, 32, 128, 1), (3, 48, 128, 0), (5, 8, 64, 0),
-                                         (5, 4, 256, 1), (2, 160, 128, 0)])
-def test_gdn_gated_norm_f16(wz, orc, T, H, hd, mode):
+                                         (5, 4, 256, 1), (2, 96, 128, 0), (3, 5, 128, 0)])
+def test_gdn_gated_norm_f16(wz, orc, T, H, hd, mode, variant):
     r = rng(T + H + hd + mode)
     o, z = f16n(r, (T, H, hd)), f16n(r, (T, H, hd))
     gm = f16n(r, (hd,), 0.02, 1.0)
@@ -179,7 +190,7 @@ def test_gdn_gated_norm_f16(wz, orc, T, H, hd, mode):
     assert_f16_close(host(dy), want, ULP_TOL, f"gdn T={T} H={H} hd={hd} mode={mode}")
 
 
-def test_gdn_gated_norm_f32_in(wz, orc):
+def test_gdn_gated_norm_f32_in(wz, orc, variant):
     r = rng(9)
     T, H, hd = 21, 48, 128
     o = r.standard_normal((T, H, hd)).astype(np.float32)
@@ -335,8 +346,7 @@ def test_device_rope_table_close_to_host(wz, orc):
     ds = torch.empty_like(dc)
     wz.rope_table(dc, ds, rows, 64, 1e7)
     gc, gs = host(dc), host(ds)
-    # CUDA's fp64 cos/sin vs libm, both rounded to fp32: equal or 1 fp32 ulp apart
-    dcos = np.abs(gc.view(np.int32).astype(np.int64) - c.view(np.int32).astype(np.int64))
-    dsin = np.abs(gs.view(np.int32).astype(np.int64) - s.view(np.int32).astype(np.int64))
-    assert dcos.max() <= 1 and dsin.max() <= 1
-    assert (dcos == 0).mean() > 0.999 and (dsin == 0).mean() > 0.999
+    # CUDA's fp64 pow/cos/sin vs libm, both rounded to fp32: the angles agree to ~1e-16 relative, so
+    # the values agree to ~1e-10 absolute (near a zero crossing that is many fp32 ulp of a tiny value)
+    assert np.abs(gc - c).max() <= 1.2e-7 and np.abs(gs - s).max() <= 1.2e-7  # <= 2 fp32 ulp at 1.0
+    assert (gc == c).mean() > 0.999 and (gs == s).mean() > 0.999

@@ -116,6 +116,18 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, 
 }
 
 // ----------------------------------------------------------------------------------------------
+// Per-thread asynchronous 16-byte copies global -> shared (cp.async.cg: L2 only). Each thread waits
+// only for its own groups, so a lane that copies and later reads the same bytes needs no barrier.
+// ----------------------------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// ----------------------------------------------------------------------------------------------
 // 8-element vectors. fp16: one 16-byte access; fp32: two 16-byte accesses.
 // ----------------------------------------------------------------------------------------------
 template <typename T>
@@ -132,6 +144,14 @@ struct Vec8<__half> {
         return Raw{__ldcs(reinterpret_cast<const uint4*>(p))};
     }
     __device__ __forceinline__ static void cvt(const Raw& r, float (&f)[8]) { to_f32(r.u, f); }
+    // lane-private staging: a vector occupies kChunks 16-byte chunks, chunk c of lane l at slot[c*32 + l]
+    static constexpr int kChunks = 1;
+    __device__ __forceinline__ static void stage_async(uint4* slot, int lane, const __half* g) {
+        cp_async16(slot + lane, g);
+    }
+    __device__ __forceinline__ static void unstage(const uint4* slot, int lane, float (&f)[8]) {
+        to_f32(slot[lane], f);
+    }
     __device__ __forceinline__ static void to_f32(const uint4& u, float (&f)[8]) {
         const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
@@ -181,6 +201,17 @@ struct Vec8<float> {
         f[0] = r.a.x; f[1] = r.a.y; f[2] = r.a.z; f[3] = r.a.w;
         f[4] = r.b.x; f[5] = r.b.y; f[6] = r.b.z; f[7] = r.b.w;
     }
+    static constexpr int kChunks = 2;
+    __device__ __forceinline__ static void stage_async(uint4* slot, int lane, const float* g) {
+        cp_async16(slot + lane, g);
+        cp_async16(slot + 32 + lane, g + 4);
+    }
+    __device__ __forceinline__ static void unstage(const uint4* slot, int lane, float (&f)[8]) {
+        const float4 a = reinterpret_cast<const float4*>(slot)[lane];
+        const float4 b = reinterpret_cast<const float4*>(slot)[32 + lane];
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    }
     __device__ __forceinline__ static void load(const float* p, float (&f)[8]) {
         const float4 a = reinterpret_cast<const float4*>(p)[0];
         const float4 b = reinterpret_cast<const float4*>(p)[1];
@@ -206,6 +237,31 @@ struct Vec8<float> {
     __device__ __forceinline__ static void store_stream(float* p, const float (&f)[8]) {
         __stcs(reinterpret_cast<float4*>(p), make_float4(f[0], f[1], f[2], f[3]));
         __stcs(reinterpret_cast<float4*>(p) + 1, make_float4(f[4], f[5], f[6], f[7]));
+    }
+};
+
+// Position q*d + r of a grid-stride walk, advanced by a fixed step without dividing: the quotient and
+// remainder of the step are computed once, each advance is two adds and a carry. (A 64-bit division
+// per work item costs dozens of instructions, which the byte-light kernels here cannot afford.)
+struct StridePos {
+    int64_t q;
+    int r;
+    int64_t dq;
+    int dr;
+    int d;
+    __device__ __forceinline__ StridePos(int64_t start, int64_t step, int divisor) : d(divisor) {
+        q = start / divisor;
+        r = (int)(start - q * divisor);
+        dq = step / divisor;
+        dr = (int)(step - dq * divisor);
+    }
+    __device__ __forceinline__ void advance() {
+        q += dq;
+        r += dr;
+        if (r >= d) {
+            r -= d;
+            ++q;
+        }
     }
 };
 

@@ -97,10 +97,28 @@ __host__ __device__ __forceinline__ uint32_t ple_row(int32_t t0, int32_t h1, int
     return (uint32_t)((uint64_t)h % rows);
 }
 
+// Same index with the modulo specialised: rows_mask = rows - 1 when rows is a power of two.
+__device__ __forceinline__ uint32_t ple_row_fast(int32_t t0, int32_t h1, int32_t h2, int head, uint64_t rows,
+                                                 uint32_t rows_mask, int32_t eos, int variant) {
+    bool cut = h1 < 0 || h1 == eos;
+    const int32_t c1 = cut ? eos : h1;
+    cut = cut || h2 < 0 || h2 == eos;
+    const int32_t c2 = cut ? eos : h2;
+    const uint32_t a = (uint32_t)t0 * 0x9E3779B1u;
+    const uint32_t b = (uint32_t)c1 * 0x85EBCA77u;
+    const uint32_t c = (uint32_t)c2 * 0xC2B2AE3Du;
+    const uint32_t h = variant == WZYB_PLE_HASH_XOR_THEN_ADD ? ((a ^ b ^ c) + (uint32_t)head)
+                                                             : (a ^ b ^ (c + (uint32_t)head));
+    if (rows_mask != 0u || rows == 1) return h & rows_mask;
+    if (rows > 0xFFFFFFFFull) return h;  // every 32-bit hash value is a valid row
+    return h % (uint32_t)rows;
+}
+
 struct PleArgs {
     const uint4* tables[32];
     int heads;
     uint64_t rows;
+    uint32_t rows_mask;  // rows - 1 when rows is a power of two, else 0
     int chunks;  // 16-byte chunks per head row
     const int32_t* ids;
     int64_t T;
@@ -141,10 +159,45 @@ __global__ void __launch_bounds__(kGatherThreads) ple_gather_kernel(const PleArg
     }
 }
 
+// Fast path when a head row is CH = 8, 16 or 32 chunks of 16 bytes: a group of CH lanes copies one
+// (token, head) row, 32/CH groups per warp, kRowUnroll rows in flight per group. The (token, head)
+// position is stepped without division and the row index uses a mask for power-of-two tables.
+template <int CH>
+__global__ void __launch_bounds__(kGatherThreads) ple_gather_groups_kernel(const PleArgs a) {
+    constexpr int GPW = 32 / CH;
+    const int lane = threadIdx.x & 31;
+    const int c = lane % CH;
+    const int64_t ngroups = (int64_t)gridDim.x * (blockDim.x >> 5) * GPW;
+    const int64_t ggrp = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * GPW + lane / CH;
+    const int64_t items = a.T * a.heads;
+    StridePos pos(ggrp, ngroups, a.heads);  // item it = (token q, head r)
+    for (int64_t base = ggrp; base < items; base += ngroups * kRowUnroll) {
+        uint4 buf[kRowUnroll];
+        int64_t dst[kRowUnroll];
+#pragma unroll
+        for (int k = 0; k < kRowUnroll; ++k) {
+            const int64_t it = base + k * ngroups;
+            dst[k] = -1;
+            if (it < items) {
+                const int64_t t = pos.q;
+                const int h = pos.r;
+                const int32_t t0 = __ldg(a.ids + t);
+                const int32_t h1 = t >= 1 ? __ldg(a.ids + t - 1) : a.prev1;
+                const int32_t h2 = t >= 2 ? __ldg(a.ids + t - 2) : (t == 1 ? a.prev1 : a.prev2);
+                const uint32_t row = ple_row_fast(t0, h1, h2, h, a.rows, a.rows_mask, a.eos, a.variant);
+                buf[k] = __ldg(a.tables[h] + (int64_t)row * CH + c);
+                dst[k] = it * CH + c;
+            }
+            pos.advance();
+        }
+#pragma unroll
+        for (int k = 0; k < kRowUnroll; ++k)
+            if (dst[k] >= 0) __stcs(a.out + dst[k], buf[k]);
+    }
+}
+
 static int grid_for(int64_t work_threads, int ctas_per_sm, const DeviceInfo& di) {
-    const int64_t per_wave = (int64_t)di.sms * ctas_per_sm;
-    const int64_t need = (work_threads + kGatherThreads - 1) / kGatherThreads;
-    return (int)(need < per_wave ? need : per_wave) > 0 ? (int)(need < per_wave ? need : per_wave) : 1;
+    return persistent_grid(di, ctas_per_sm, (work_threads + kGatherThreads - 1) / kGatherThreads);
 }
 
 }  // namespace wzyb
@@ -226,6 +279,16 @@ int wzyb_ple_gather_f16(const uint16_t* const* tables, int heads, int64_t rows_p
     a.eos = eos_id;
     a.variant = hash_variant;
     a.out = (uint4*)out;
+    a.rows_mask = (rows_per_table & (rows_per_table - 1)) == 0 ? (uint32_t)(rows_per_table - 1) : 0u;
+    if (a.chunks == 8 || a.chunks == 16 || a.chunks == 32) {
+        const int64_t threads = T * heads * (int64_t)a.chunks / wzyb::kRowUnroll;
+        const int grid = wzyb::grid_for(threads, 8, di);
+        cudaStream_t s = (cudaStream_t)stream;
+        if (a.chunks == 8) wzyb::ple_gather_groups_kernel<8><<<grid, wzyb::kGatherThreads, 0, s>>>(a);
+        else if (a.chunks == 16) wzyb::ple_gather_groups_kernel<16><<<grid, wzyb::kGatherThreads, 0, s>>>(a);
+        else wzyb::ple_gather_groups_kernel<32><<<grid, wzyb::kGatherThreads, 0, s>>>(a);
+        return wzyb::launch_status();
+    }
     const int64_t total = T * heads * (int64_t)a.chunks;
     const int grid = wzyb::grid_for((total + wzyb::kRowUnroll - 1) / wzyb::kRowUnroll, 8, di);
     wzyb::ple_gather_kernel<<<grid, wzyb::kGatherThreads, 0, (cudaStream_t)stream>>>(a);

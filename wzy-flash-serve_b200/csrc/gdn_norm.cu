@@ -12,6 +12,15 @@
 
 namespace wzyb {
 
+// x gated by sigmoid(z) (or z*sigmoid(z)), with x = o * rsqrt(...) * gamma already formed in the
+// reference's order. The reference divides x by (1 + exp(-z)); __fdividef is the fast divide
+// (<= 2 fp32 ulp apart, far inside an fp16 ulp). When 1 + exp(-z) exceeds 2^126 (z < -87) it
+// returns 0, where the exact quotient is below 1e-37.
+__device__ __forceinline__ float gdn_gate(float x, float z, bool silu) {
+    const float den = 1.0f + __expf(-z);
+    return silu ? x * __fdividef(z, den) : __fdividef(x, den);
+}
+
 struct GdnArgs {
     const void* o;
     const void* z;
@@ -114,12 +123,155 @@ __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) gdn_norm_kernel(const G
             float out[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-                const float den = 1.0f + __expf(-zv[k][e]);
-                out[e] = silu ? (ov[k][e] * sc * g[k][e]) * (zv[k][e] / den) : ov[k][e] * sc * g[k][e] / den;
+                out[e] = gdn_gate(ov[k][e] * sc * g[k][e], zv[k][e], silu);
             }
             if (act[k]) Vec8<TO>::store(y + t * row_elems + col[k], out);
         }
     }
+}
+
+// Direct design: a warp owns one 256-element slab of a token row (32/L whole heads), keeps kU slabs of
+// o and z in flight as raw 16-byte registers, then normalises each head inside its lane group. No
+// shared memory, no CTA barrier: warps stream independently like a copy kernel.
+template <typename TI, typename TO, int HD, int kU>
+__global__ void __launch_bounds__(256) gdn_direct_kernel(const GdnArgs a) {
+    constexpr int L = HD / 8;
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int row_elems = a.heads * HD;
+    const int slabs = (row_elems + 255) / 256;
+    const int64_t items = a.T * slabs;
+    const TI* __restrict__ o = static_cast<const TI*>(a.o);
+    const TI* __restrict__ z = static_cast<const TI*>(a.z);
+    TO* __restrict__ y = static_cast<TO*>(a.y);
+    float g[8];
+    Vec8<TI>::load_ro(static_cast<const TI*>(a.gamma) + (lane % L) * 8, g);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) g[e] = a.w_offset + g[e];
+    const bool silu = a.gate_mode == WZYB_GATE_SILU;
+
+    StridePos pos(gwarp, nwarps, slabs);  // item it = (token q, slab r)
+    for (int64_t base = gwarp; base < items; base += nwarps * kU) {
+        typename Vec8<TI>::Raw ro[kU], rz[kU];
+        int64_t off[kU];
+#pragma unroll
+        for (int k = 0; k < kU; ++k) {
+            const int64_t it = base + k * nwarps;
+            off[k] = -1;
+            if (it < items) {
+                const int e = pos.r * 256 + lane * 8;
+                if (e < row_elems) {
+                    off[k] = pos.q * row_elems + e;
+                    ro[k] = Vec8<TI>::ldcs_raw(o + off[k]);
+                    rz[k] = Vec8<TI>::ldcs_raw(z + off[k]);
+                }
+            }
+            pos.advance();
+        }
+#pragma unroll
+        for (int k = 0; k < kU; ++k) {
+            if (base + k * nwarps >= items) break;  // warp-uniform
+            float ov[8], zv[8];
+            if (off[k] >= 0) {
+                Vec8<TI>::cvt(ro[k], ov);
+                Vec8<TI>::cvt(rz[k], zv);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ov[e] = zv[e] = 0.f;
+            }
+            float ss = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ss += ov[e] * ov[e];
+            ss = group_sum<L>(ss);
+            const float sc = rsqrtf(ss * (1.0f / (float)HD) + a.eps);
+            float out[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                out[e] = gdn_gate(ov[e] * sc * g[e], zv[e], silu);
+            }
+            if (off[k] >= 0) Vec8<TO>::store(y + off[k], out);
+        }
+    }
+}
+
+// Async design: the direct design's warp-owned slabs, but the kP slabs in flight per warp sit in a
+// lane-private shared-memory ring filled by cp.async instead of in registers. Each lane copies and
+// later reads only its own 16-byte chunks, so the ring needs no barrier at all; the register file is
+// no longer what bounds the bytes in flight.
+template <typename TI, typename TO, int HD, int kP>
+__global__ void __launch_bounds__(256) gdn_async_kernel(const GdnArgs a) {
+    constexpr int L = HD / 8;
+    constexpr int C = Vec8<TI>::kChunks;   // 16-byte chunks per 8-element vector
+    constexpr int SLOT = 2 * C * 32;       // uint4 per ring slot: o and z vectors of 32 lanes
+    extern __shared__ __align__(16) uint4 sm_gdn[];
+    const int lane = threadIdx.x & 31;
+    uint4* ring = sm_gdn + (size_t)(threadIdx.x >> 5) * kP * SLOT;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int row_elems = a.heads * HD;
+    const int slabs = (row_elems + 255) / 256;
+    const int64_t items = a.T * slabs;
+    const TI* __restrict__ o = static_cast<const TI*>(a.o);
+    const TI* __restrict__ z = static_cast<const TI*>(a.z);
+    TO* __restrict__ y = static_cast<TO*>(a.y);
+    float g[8];
+    Vec8<TI>::load_ro(static_cast<const TI*>(a.gamma) + (lane % L) * 8, g);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) g[e] = a.w_offset + g[e];
+    const bool silu = a.gate_mode == WZYB_GATE_SILU;
+
+    // element offset of this lane's vector for the item at `p`, or -1
+    auto offset = [&](int64_t it, const StridePos& p) -> int64_t {
+        if (it >= items) return -1;
+        const int e = p.r * 256 + lane * 8;
+        return e < row_elems ? p.q * row_elems + e : -1;
+    };
+    StridePos ipos(gwarp, nwarps, slabs);  // next item to issue
+    StridePos cpos(gwarp, nwarps, slabs);  // next item to consume
+    auto issue = [&](int64_t it, int slot) {
+        const int64_t off = offset(it, ipos);
+        ipos.advance();
+        if (off >= 0) {
+            Vec8<TI>::stage_async(ring + slot * SLOT, lane, o + off);
+            Vec8<TI>::stage_async(ring + slot * SLOT + C * 32, lane, z + off);
+        }
+        cp_async_commit();  // one group per item, empty or not, so wait_group counts items
+    };
+#pragma unroll
+    for (int j = 0; j < kP; ++j) issue(gwarp + j * nwarps, j);
+
+    for (int64_t j = 0;; ++j) {
+        const int64_t it = gwarp + j * nwarps;
+        if (it >= items) break;  // warp-uniform
+        const int slot = (int)(j % kP);
+        cp_async_wait<kP - 1>();
+        const int64_t off = offset(it, cpos);
+        cpos.advance();
+        float ov[8], zv[8];
+        if (off >= 0) {
+            Vec8<TI>::unstage(ring + slot * SLOT, lane, ov);
+            Vec8<TI>::unstage(ring + slot * SLOT + C * 32, lane, zv);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ov[e] = zv[e] = 0.f;
+        }
+        // Refill the slot. Only this lane reads or writes its chunks of the slot, and its unstaging
+        // loads precede the new copy in program order, which orders them before the copy's write.
+        issue(it + kP * nwarps, slot);
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += ov[e] * ov[e];
+        ss = group_sum<L>(ss);
+        const float sc = rsqrtf(ss * (1.0f / (float)HD) + a.eps);
+        float out[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            out[e] = gdn_gate(ov[e] * sc * g[e], zv[e], silu);
+        }
+        if (off >= 0) Vec8<TO>::store(y + off, out);
+    }
+    cp_async_wait<0>();
 }
 
 template <typename TI, typename TO>
@@ -147,6 +299,34 @@ static int launch_gdn(const void* o, const void* z, const void* gamma, void* y, 
     a.gate_mode = gate_mode;
     a.row_bytes = (uint32_t)((int64_t)heads * hd * sizeof(TI));
     a.stage_bytes = 2u * a.row_bytes;
+
+    if (variant(kFamGdn) == WZYB_VARIANT_ASYNC) {
+        constexpr int kP = sizeof(TI) == 2 ? 8 : 4;
+        const void* kern = hd == 64    ? (const void*)gdn_async_kernel<TI, TO, 64, kP>
+                           : hd == 128 ? (const void*)gdn_async_kernel<TI, TO, 128, kP>
+                                       : (const void*)gdn_async_kernel<TI, TO, 256, kP>;
+        const int smem = 8 * kP * 2 * Vec8<TI>::kChunks * 32 * 16;
+        rc = ensure_smem(kern, smem);
+        if (rc != WZYB_OK) return rc;
+        const int64_t warp_items = T * (((int64_t)heads * hd + 255) / 256);
+        const int grid = persistent_grid(di, resident_ctas(kern, 256, smem), (warp_items + 7) / 8);
+        if (hd == 64) gdn_async_kernel<TI, TO, 64, kP><<<grid, 256, smem, stream>>>(a);
+        else if (hd == 128) gdn_async_kernel<TI, TO, 128, kP><<<grid, 256, smem, stream>>>(a);
+        else gdn_async_kernel<TI, TO, 256, kP><<<grid, 256, smem, stream>>>(a);
+        return launch_status();
+    }
+    if (variant(kFamGdn) != WZYB_VARIANT_RING) {
+        const void* kern = hd == 64    ? (const void*)gdn_direct_kernel<TI, TO, 64, 4>
+                           : hd == 128 ? (const void*)gdn_direct_kernel<TI, TO, 128, 4>
+                                       : (const void*)gdn_direct_kernel<TI, TO, 256, 4>;
+        const int64_t warp_items = T * (((int64_t)heads * hd + 255) / 256);
+        const int grid = persistent_grid(di, resident_ctas(kern, 256, 0), (warp_items + 7) / 8);
+        if (hd == 64) gdn_direct_kernel<TI, TO, 64, 4><<<grid, 256, 0, stream>>>(a);
+        else if (hd == 128) gdn_direct_kernel<TI, TO, 128, 4><<<grid, 256, 0, stream>>>(a);
+        else gdn_direct_kernel<TI, TO, 256, 4><<<grid, 256, 0, stream>>>(a);
+        return launch_status();
+    }
+
     const int slots = heads * hd / 8;
     const int vpt = slots <= 1024 ? 1 : 4;  // VPT 4 keeps the CTA at <= 512 threads (128 registers)
     if (slots > 2048) return WZYB_ERR_SHAPE;

@@ -55,6 +55,12 @@ __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) head_rope_kernel(const 
 
     const int tid = threadIdx.x, lane = tid & 31;
     const int hq = a.sec[0].heads, hk = a.sec[1].heads, htot = hq + hk;
+    const int half = a.rot / 2;  // rotated pairs per head
+    const int hl = half / 8;     // lanes per rotation half
+    const int64_t base_pos = (a.d_base_pos ? (int64_t)__ldg(a.d_base_pos) : 0) + a.pos_offset;
+    // stage = [all heads][cos row (half floats)][sin row (half floats)]
+    const uint32_t heads_bytes = a.head_bytes * (uint32_t)htot;
+    const uint32_t tab_bytes = (uint32_t)half * 4u;
 
     uint64_t pol = 0;
     int64_t issued = 0;
@@ -62,7 +68,13 @@ __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) head_rope_kernel(const 
         const int s = (int)(i % S);
         const int64_t t = first + i * G;
         unsigned char* st = ring.data + (size_t)s * a.stage_bytes;
-        mbar_arrive_expect_tx(&ring.full[s], a.stage_bytes);
+        const int64_t pos = base_pos + t;
+        const bool tab = half > 0 && pos >= 0 && pos < a.table_rows;
+        mbar_arrive_expect_tx(&ring.full[s], heads_bytes + (tab ? 2u * tab_bytes : 0u));
+        if (tab) {
+            bulk_load(st + heads_bytes, a.cos_tab + pos * half, tab_bytes, &ring.full[s], pol);
+            bulk_load(st + heads_bytes + tab_bytes, a.sin_tab + pos * half, tab_bytes, &ring.full[s], pol);
+        }
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
             const HeadSection& sc = a.sec[q];
@@ -85,8 +97,6 @@ __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) head_rope_kernel(const 
     }
 
     // Fixed per-thread ownership: slot j = tid + k*blockDim -> head j / L, lane-in-head j % L.
-    const int half = a.rot / 2;  // rotated pairs per head
-    const int hl = half / 8;     // lanes per rotation half
     int head[VPT], li[VPT], sec[VPT];
     bool act[VPT];
     float g[VPT][8];
@@ -104,23 +114,29 @@ __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) head_rope_kernel(const 
             for (int e = 0; e < 8; ++e) g[k][e] = a.w_offset + g[k][e];
         }
     }
-    const int64_t base_pos = (a.d_base_pos ? (int64_t)__ldg(a.d_base_pos) : 0) + a.pos_offset;
 
     for (int64_t i = 0; i < my_units; ++i) {
         const int s = (int)(i % S);
         const int64_t t = first + i * G;
+        const int64_t pos = base_pos + t;
+        const bool pos_ok = pos >= 0 && pos < a.table_rows;
         const bool ok = mbar_wait(&ring.full[s], (uint32_t)((i / S) & 1));
         if (!ok) *ring.abort_flag = 1;
         float p[VPT][8];
+        float cs[VPT][8], sn[VPT][8];
+        const unsigned char* st = ring.data + (size_t)s * a.stage_bytes;
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
             if (act[k] && ok) {
-                const T* sp =
-                    reinterpret_cast<const T*>(ring.data + (size_t)s * a.stage_bytes + (size_t)head[k] * a.head_bytes);
-                Vec8<T>::load(sp + li[k] * 8, p[k]);
+                Vec8<T>::load(reinterpret_cast<const T*>(st + (size_t)head[k] * a.head_bytes) + li[k] * 8, p[k]);
             } else {
 #pragma unroll
                 for (int e = 0; e < 8; ++e) p[k][e] = 0.f;
+            }
+            if (act[k] && ok && pos_ok && li[k] < 2 * hl) {
+                const int ci = (li[k] < hl ? li[k] : li[k] - hl) * 8;
+                Vec8<float>::load(reinterpret_cast<const float*>(st + heads_bytes) + ci, cs[k]);
+                Vec8<float>::load(reinterpret_cast<const float*>(st + heads_bytes + tab_bytes) + ci, sn[k]);
             }
         }
         __syncthreads();  // every thread has its unit in registers: the stage may be refilled
@@ -132,8 +148,6 @@ __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) head_rope_kernel(const 
             issue(issued);
             ++issued;
         }
-        const int64_t pos = base_pos + t;
-        const bool pos_ok = pos >= 0 && pos < a.table_rows;
         if (!pos_ok && tid == 0 && a.rot > 0) raise_fault(WZYB_FAULT_POS_RANGE);
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
@@ -155,18 +169,12 @@ __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) head_rope_kernel(const 
 #pragma unroll
             for (int e = 0; e < 8; ++e) q2[e] = __shfl_sync(0xffffffffu, p[k][e], src);
             if (rot_lane && act[k] && pos_ok) {
-                const int ci = (first_half ? li[k] : li[k] - hl) * 8;
-                const float4* cp = reinterpret_cast<const float4*>(a.cos_tab + pos * half + ci);
-                const float4* sp = reinterpret_cast<const float4*>(a.sin_tab + pos * half + ci);
-                const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
-                const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
                 if (first_half) {
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) p[k][e] = p[k][e] * cs[e] - q2[e] * sn[e];  // a*cos - d*sin
+                    for (int e = 0; e < 8; ++e) p[k][e] = p[k][e] * cs[k][e] - q2[e] * sn[k][e];  // a*cos - d*sin
                 } else {
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) p[k][e] = q2[e] * sn[e] + p[k][e] * cs[e];  // a*sin + d*cos
+                    for (int e = 0; e < 8; ++e) p[k][e] = q2[e] * sn[k][e] + p[k][e] * cs[k][e];  // a*sin + d*cos
                 }
             }
             if (act[k]) {
@@ -177,6 +185,239 @@ __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) head_rope_kernel(const 
             }
         }
     }
+}
+
+// Direct design: a warp owns a chunk of kNH*(32/L) consecutive heads of ONE token (q heads first,
+// then k heads), so the token's cos/sin row is fetched once per chunk. All heads of the chunk are
+// loaded as raw 16-byte registers before any arithmetic; each head is then normalised inside its
+// lane group and rotated with one shuffle per element, and written back in place. No shared memory,
+// no CTA barrier.
+template <typename T, int HD, int kNH>
+__global__ void __launch_bounds__(256) head_rope_direct_kernel(const HeadRopeArgs a) {
+    constexpr int L = HD / 8;
+    constexpr int HPW = 32 / L;         // heads side by side in one warp
+    constexpr int CH = kNH * HPW;       // heads per chunk
+    const int lane = threadIdx.x & 31;
+    const int li = lane % L;            // lane inside its head
+    const int hw = lane / L;            // head slot inside the warp
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int hq = a.sec[0].heads, htot = hq + a.sec[1].heads;
+    const int chunks = (htot + CH - 1) / CH;
+    const int64_t items = a.T * chunks;
+    const int half = a.rot / 2, hl = half / 8;
+    const bool rot_lane = li < 2 * hl, first_half = li < hl;
+    const int src = rot_lane ? (first_half ? lane + hl : lane - hl) : lane;
+    const int ci = (first_half ? li : li - hl) * 8;
+    const int64_t base_pos = (a.d_base_pos ? (int64_t)__ldg(a.d_base_pos) : 0) + a.pos_offset;
+
+    float g[2][8];
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) g[s][e] = 0.f;
+        if (a.sec[s].heads > 0) {
+            Vec8<T>::load_ro(static_cast<const T*>(a.sec[s].gamma) + li * 8, g[s]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) g[s][e] = a.w_offset + g[s][e];
+        }
+    }
+
+    StridePos ps(gwarp, nwarps, chunks);  // item it = (token q, chunk r)
+    for (int64_t it = gwarp; it < items; it += nwarps, ps.advance()) {
+        const int64_t t = ps.q;
+        const int h0 = ps.r * CH;
+        typename Vec8<T>::Raw rp[kNH];
+        T* dst[kNH];
+#pragma unroll
+        for (int j = 0; j < kNH; ++j) {
+            const int h = h0 + j * HPW + hw;
+            dst[j] = nullptr;
+            if (h < htot) {
+                const int s = h < hq ? 0 : 1;
+                const HeadSection& sc = a.sec[s];
+                dst[j] = static_cast<T*>(sc.data) + t * sc.row_stride + (int64_t)(s == 0 ? h : h - hq) * sc.head_stride +
+                         li * 8;
+                rp[j] = Vec8<T>::ldcs_raw(dst[j]);
+            }
+        }
+        const int64_t pos = base_pos + t;
+        const bool pos_ok = half > 0 && pos >= 0 && pos < a.table_rows;
+        float c8[8], s8[8];
+        if (pos_ok && rot_lane) {
+            Vec8<float>::load_ro(a.cos_tab + pos * half + ci, c8);
+            Vec8<float>::load_ro(a.sin_tab + pos * half + ci, s8);
+        }
+        if (half > 0 && !pos_ok && lane == 0 && h0 == 0) raise_fault(WZYB_FAULT_POS_RANGE);
+#pragma unroll
+        for (int j = 0; j < kNH; ++j) {
+            if (h0 + j * HPW >= htot) break;  // warp-uniform: no head of this round exists
+            const int h = h0 + j * HPW + hw;
+            float p[8];
+            if (dst[j] != nullptr) {
+                Vec8<T>::cvt(rp[j], p);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) p[e] = 0.f;
+            }
+            float ss = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ss += p[e] * p[e];
+            ss = group_sum<L>(ss);
+            const float sc = rsqrtf(ss / (float)HD + a.eps);
+            const float* gs = g[h < hq ? 0 : 1];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) p[e] *= sc * gs[e];
+            float q2[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) q2[e] = __shfl_sync(0xffffffffu, p[e], src);
+            if (pos_ok && rot_lane) {
+                if (first_half) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) p[e] = p[e] * c8[e] - q2[e] * s8[e];  // a*cos - d*sin
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) p[e] = q2[e] * s8[e] + p[e] * c8[e];  // a*sin + d*cos
+                }
+            }
+            if (dst[j] != nullptr) Vec8<T>::store(dst[j], p);
+        }
+    }
+}
+
+// Async design: the direct design's per-token head chunks, but the kP chunks in flight per warp sit
+// in a shared-memory ring filled by cp.async (16 bytes per lane per head) together with the token's
+// cos/sin row, instead of in registers. Head vectors are lane-private; the cos/sin row is copied by
+// the first-half rotary lanes and read by both halves, so each slot is bracketed by __syncwarp.
+template <typename T, int HD, int kNH, int kP>
+__global__ void __launch_bounds__(128) head_rope_async_kernel(const HeadRopeArgs a) {
+    constexpr int L = HD / 8;
+    constexpr int HPW = 32 / L;
+    constexpr int CH = kNH * HPW;
+    constexpr int C = Vec8<T>::kChunks;
+    extern __shared__ __align__(16) uint4 sm_hr[];
+    const int lane = threadIdx.x & 31;
+    const int li = lane % L, hw = lane / L;
+    const int half = a.rot / 2, hl = half / 8;
+    const int slot_u4 = kNH * C * 32 + 4 * hl;  // head vectors + cos/sin row (hl x 32 B each)
+    uint4* ring = sm_hr + (size_t)(threadIdx.x >> 5) * kP * slot_u4;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int hq = a.sec[0].heads, htot = hq + a.sec[1].heads;
+    const int chunks = (htot + CH - 1) / CH;
+    const int64_t items = a.T * chunks;
+    const bool rot_lane = li < 2 * hl, first_half = li < hl;
+    const int src = rot_lane ? (first_half ? lane + hl : lane - hl) : lane;
+    const int c8i = first_half ? li : li - hl;  // which 8 cos/sin values this lane uses
+    const int64_t base_pos = (a.d_base_pos ? (int64_t)__ldg(a.d_base_pos) : 0) + a.pos_offset;
+
+    float g[2][8];
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) g[s][e] = 0.f;
+        if (a.sec[s].heads > 0) {
+            Vec8<T>::load_ro(static_cast<const T*>(a.sec[s].gamma) + li * 8, g[s]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) g[s][e] = a.w_offset + g[s][e];
+        }
+    }
+    auto head_ptr = [&](int64_t t, int h) -> T* {
+        const int s = h < hq ? 0 : 1;
+        const HeadSection& sc = a.sec[s];
+        return static_cast<T*>(sc.data) + t * sc.row_stride + (int64_t)(s == 0 ? h : h - hq) * sc.head_stride + li * 8;
+    };
+    auto pos_in_table = [&](int64_t pos) { return half > 0 && pos >= 0 && pos < a.table_rows; };
+    StridePos ipos(gwarp, nwarps, chunks);  // next item to issue
+    StridePos cpos(gwarp, nwarps, chunks);  // next item to consume
+    auto issue = [&](int64_t it, int slot) {
+        const int64_t t = ipos.q;
+        const int h0 = ipos.r * CH;
+        ipos.advance();
+        if (it < items) {
+            uint4* sl = ring + slot * slot_u4;
+#pragma unroll
+            for (int j = 0; j < kNH; ++j) {
+                const int h = h0 + j * HPW + hw;
+                if (h < htot) Vec8<T>::stage_async(sl + j * C * 32, lane, head_ptr(t, h));
+            }
+            const int64_t pos = base_pos + t;
+            if (pos_in_table(pos) && hw == 0 && li < hl) {
+                uint4* tab = sl + kNH * C * 32;
+                cp_async16(tab + li * 2, a.cos_tab + pos * half + li * 8);
+                cp_async16(tab + li * 2 + 1, a.cos_tab + pos * half + li * 8 + 4);
+                cp_async16(tab + (hl + li) * 2, a.sin_tab + pos * half + li * 8);
+                cp_async16(tab + (hl + li) * 2 + 1, a.sin_tab + pos * half + li * 8 + 4);
+            }
+        }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int j = 0; j < kP; ++j) issue(gwarp + j * nwarps, j);
+
+    for (int64_t jj = 0;; ++jj) {
+        const int64_t it = gwarp + jj * nwarps;
+        if (it >= items) break;  // warp-uniform
+        const int slot = (int)(jj % kP);
+        const int64_t t = cpos.q;
+        const int h0 = cpos.r * CH;
+        cpos.advance();
+        const int64_t pos = base_pos + t;
+        const bool pos_ok = pos_in_table(pos);
+        if (half > 0 && !pos_ok && lane == 0 && h0 == 0) raise_fault(WZYB_FAULT_POS_RANGE);
+        cp_async_wait<kP - 1>();
+        __syncwarp();  // the cos/sin row copied by other lanes is visible
+        const uint4* sl = ring + slot * slot_u4;
+        float p[kNH][8];
+#pragma unroll
+        for (int j = 0; j < kNH; ++j) {
+            if (h0 + j * HPW + hw < htot) {
+                Vec8<T>::unstage(sl + j * C * 32, lane, p[j]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) p[j][e] = 0.f;
+            }
+        }
+        float c8[8], s8[8];
+        if (pos_ok && rot_lane) {
+            const float4* tab = reinterpret_cast<const float4*>(sl + kNH * C * 32);
+            const float4 c0 = tab[c8i * 2], c1 = tab[c8i * 2 + 1];
+            const float4 s0 = tab[(hl + c8i) * 2], s1 = tab[(hl + c8i) * 2 + 1];
+            c8[0] = c0.x; c8[1] = c0.y; c8[2] = c0.z; c8[3] = c0.w;
+            c8[4] = c1.x; c8[5] = c1.y; c8[6] = c1.z; c8[7] = c1.w;
+            s8[0] = s0.x; s8[1] = s0.y; s8[2] = s0.z; s8[3] = s0.w;
+            s8[4] = s1.x; s8[5] = s1.y; s8[6] = s1.z; s8[7] = s1.w;
+        }
+        __syncwarp();  // every lane has read the slot: it may be refilled
+        issue(it + kP * nwarps, slot);
+#pragma unroll
+        for (int j = 0; j < kNH; ++j) {
+            if (h0 + j * HPW >= htot) break;  // warp-uniform
+            const int h = h0 + j * HPW + hw;
+            float ss = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ss += p[j][e] * p[j][e];
+            ss = group_sum<L>(ss);
+            const float sc = rsqrtf(ss / (float)HD + a.eps);
+            const float* gs = g[h < hq ? 0 : 1];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) p[j][e] *= sc * gs[e];
+            float q2[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) q2[e] = __shfl_sync(0xffffffffu, p[j][e], src);
+            if (pos_ok && rot_lane) {
+                if (first_half) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) p[j][e] = p[j][e] * c8[e] - q2[e] * s8[e];  // a*cos - d*sin
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) p[j][e] = q2[e] * s8[e] + p[j][e] * c8[e];  // a*sin + d*cos
+                }
+            }
+            if (h < htot) Vec8<T>::store(head_ptr(t, h), p[j]);
+        }
+    }
+    cp_async_wait<0>();
 }
 
 template <typename T>
@@ -222,9 +463,40 @@ static int launch_head_rope(const HeadSection& q, const HeadSection& k, const fl
     a.w_offset = w_offset;
     a.head_bytes = (uint32_t)(hd * sizeof(T));
     const int htot = q.heads + k.heads;
-    a.stage_bytes = a.head_bytes * (uint32_t)htot;
+    a.stage_bytes = a.head_bytes * (uint32_t)htot + (rot > 0 ? 2u * (uint32_t)(rot / 2) * 4u : 0u);
     a.contig[0] = (q.head_stride == hd || q.heads == 1) ? 1 : 0;
     a.contig[1] = (k.head_stride == hd || k.heads <= 1) ? 1 : 0;
+
+    if (variant(kFamHeadRope) == WZYB_VARIANT_ASYNC) {
+        constexpr int kNH = 6, kP = 4;
+        const void* kern = hd == 64    ? (const void*)head_rope_async_kernel<T, 64, kNH, kP>
+                           : hd == 128 ? (const void*)head_rope_async_kernel<T, 128, kNH, kP>
+                                       : (const void*)head_rope_async_kernel<T, 256, kNH, kP>;
+        const int slot_u4 = kNH * Vec8<T>::kChunks * 32 + 4 * (rot / 16);
+        const int smem = 4 * kP * slot_u4 * 16;
+        rc = ensure_smem(kern, smem);
+        if (rc != WZYB_OK) return rc;
+        const int ch = kNH * (256 / hd);
+        const int64_t warp_items = T_ * ((htot + ch - 1) / ch);
+        const int grid = persistent_grid(di, resident_ctas(kern, 128, smem), (warp_items + 3) / 4);
+        if (hd == 64) head_rope_async_kernel<T, 64, kNH, kP><<<grid, 128, smem, stream>>>(a);
+        else if (hd == 128) head_rope_async_kernel<T, 128, kNH, kP><<<grid, 128, smem, stream>>>(a);
+        else head_rope_async_kernel<T, 256, kNH, kP><<<grid, 128, smem, stream>>>(a);
+        return launch_status();
+    }
+    if (variant(kFamHeadRope) != WZYB_VARIANT_RING) {
+        constexpr int kNH = 6;
+        const void* kern = hd == 64    ? (const void*)head_rope_direct_kernel<T, 64, kNH>
+                           : hd == 128 ? (const void*)head_rope_direct_kernel<T, 128, kNH>
+                                       : (const void*)head_rope_direct_kernel<T, 256, kNH>;
+        const int ch = kNH * (256 / hd);
+        const int64_t warp_items = T_ * ((htot + ch - 1) / ch);
+        const int grid = persistent_grid(di, resident_ctas(kern, 256, 0), (warp_items + 7) / 8);
+        if (hd == 64) head_rope_direct_kernel<T, 64, kNH><<<grid, 256, 0, stream>>>(a);
+        else if (hd == 128) head_rope_direct_kernel<T, 128, kNH><<<grid, 256, 0, stream>>>(a);
+        else head_rope_direct_kernel<T, 256, kNH><<<grid, 256, 0, stream>>>(a);
+        return launch_status();
+    }
 
     const int slots = htot * (hd / 8);
     const int vpt = slots <= 1024 ? 1 : 4;  // VPT 4 keeps the CTA at <= 512 threads (128 registers)

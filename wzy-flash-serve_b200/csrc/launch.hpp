@@ -33,6 +33,20 @@ struct Tuning {
     int stages;  // 0 = as many as the shared-memory budget allows
 };
 Tuning tuning(int family);
+// WZYB_VARIANT_* chosen for a family (AUTO unless set by wzyb_set_kernel_variant).
+int variant(int family);
+
+// Resident CTAs per SM of `kernel` at `threads` threads and `smem` dynamic bytes on the current
+// device (cached per kernel and device; at least 1).
+int resident_ctas(const void* kernel, int threads, int smem);
+
+// Persistent grid for a kernel whose CTAs loop over work: every SM filled once, never more CTAs
+// than there is work for.
+inline int persistent_grid(const DeviceInfo& di, int ctas_per_sm, int64_t ctas_of_work) {
+    const int64_t want = (int64_t)di.sms * ctas_per_sm;
+    const int64_t g = ctas_of_work < want ? ctas_of_work : want;
+    return g < 1 ? 1 : (int)g;
+}
 
 // Shared-memory budget for one SM's worth of ring stages (bytes), leaving headroom for the L1.
 constexpr int kSmemPerSm = 200 * 1024;

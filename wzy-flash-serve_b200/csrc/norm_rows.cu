@@ -144,6 +144,79 @@ __global__ void __launch_bounds__(512) norm_rows_kernel(const NormRowsArgs a) {
     }
 }
 
+// Direct design: one warp per row. Lane l owns the 8-element vectors l, l+32, ... of the row, so each
+// warp-wide 16-byte load covers 512 contiguous bytes. All VPL vectors of residual and x are loaded
+// before any arithmetic (VPL*2 loads in flight per lane); the sum of squares is reduced with five
+// xor shuffles; v is recomputed from the raw registers in the second pass instead of being kept in
+// fp32, which keeps a row of 2048 at ~100 registers. No shared memory, no CTA barrier.
+template <typename TI, typename TO, int VPL>
+__global__ void __launch_bounds__(256, 2) norm_rows_direct_kernel(const NormRowsArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const TI* __restrict__ x = static_cast<const TI*>(a.x);
+    TI* __restrict__ res = static_cast<TI*>(a.res);
+    const TI* __restrict__ w = static_cast<const TI*>(a.w);
+    TO* __restrict__ y = static_cast<TO*>(a.y);
+    const bool has_x = x != nullptr;
+    const int n = a.n;
+
+    for (int64_t u = gwarp; u < a.units; u += nwarps) {
+        typename Vec8<TI>::Raw rr[VPL], rx[VPL];
+        const TI* rrow = res + u * n;
+        const int64_t t = a.hc == 1 ? u : u / a.hc;  // token of this (token, stream) row
+        const TI* xrow = has_x ? x + t * n : nullptr;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int e = (k * 32 + lane) * 8;
+            if (e < n) {
+                rr[k] = Vec8<TI>::ldcs_raw(rrow + e);
+                if (has_x) rx[k] = Vec8<TI>::ldcs_raw(xrow + e);
+            }
+        }
+        const float gate = (has_x && a.inj != nullptr) ? 2.0f / (1.0f + __expf(-a.inj[u] / (float)a.hc)) : 1.0f;
+        float ss = 0.f;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int e = (k * 32 + lane) * 8;
+            if (e < n) {
+                float v[8];
+                Vec8<TI>::cvt(rr[k], v);
+                if (has_x) {
+                    float xv[8];
+                    Vec8<TI>::cvt(rx[k], xv);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v[j] += xv[j] * gate;
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+            }
+        }
+        ss = group_sum<32>(ss);
+        const float sc = rsqrtf(ss / (float)n + a.eps);
+        const TI* wrow = w + (u - t * a.hc) * n;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int e = (k * 32 + lane) * 8;
+            if (e < n) {
+                float v[8], g[8], o[8];
+                Vec8<TI>::cvt(rr[k], v);
+                if (has_x) {
+                    float xv[8];
+                    Vec8<TI>::cvt(rx[k], xv);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v[j] += xv[j] * gate;
+                }
+                Vec8<TI>::load_ro(wrow + e, g);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) o[j] = (v[j] * sc) * (a.w_offset + g[j]);
+                Vec8<TO>::store(y + u * n + e, o);
+                if (has_x) Vec8<TI>::store(res + u * n + e, v);
+            }
+        }
+    }
+}
+
 template <typename TI, typename TO>
 static int launch_norm_rows(const void* x, void* res, const void* w, const float* inj, void* y, int64_t T, int n,
                             int hc, float eps, float w_offset, cudaStream_t stream) {
@@ -172,6 +245,40 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
     a.w_offset = w_offset;
     a.row_bytes = (uint32_t)(n * sizeof(TI));
     a.stage_bytes = a.row_bytes * (x ? 2u : 1u);
+
+    // Direct design while a row fits the register budget (<= 12 fp16 or 6 fp32 vectors per lane).
+    const int vpl_need = (n + 255) / 256;
+    const int vpl_max = sizeof(TI) == 2 ? 12 : 6;
+    if (variant(kFamNorm) != WZYB_VARIANT_RING && vpl_need <= vpl_max) {
+        const void* kern = nullptr;
+        int vpl = 0;
+#define WZYB_NR_PICK(V)                                                  \
+    if (!kern && vpl_need <= V) {                                        \
+        kern = (const void*)norm_rows_direct_kernel<TI, TO, V>;          \
+        vpl = V;                                                         \
+    }
+        WZYB_NR_PICK(1)
+        WZYB_NR_PICK(2)
+        WZYB_NR_PICK(4)
+        WZYB_NR_PICK(6)
+        if (sizeof(TI) == 2) {
+            WZYB_NR_PICK(8)
+            WZYB_NR_PICK(10)
+            WZYB_NR_PICK(12)
+        }
+#undef WZYB_NR_PICK
+        const int grid = persistent_grid(di, resident_ctas(kern, 256, 0), (a.units + 7) / 8);
+        switch (vpl) {
+            case 1: norm_rows_direct_kernel<TI, TO, 1><<<grid, 256, 0, stream>>>(a); break;
+            case 2: norm_rows_direct_kernel<TI, TO, 2><<<grid, 256, 0, stream>>>(a); break;
+            case 4: norm_rows_direct_kernel<TI, TO, 4><<<grid, 256, 0, stream>>>(a); break;
+            case 6: norm_rows_direct_kernel<TI, TO, 6><<<grid, 256, 0, stream>>>(a); break;
+            case 8: norm_rows_direct_kernel<TI, TO, 8><<<grid, 256, 0, stream>>>(a); break;
+            case 10: norm_rows_direct_kernel<TI, TO, 10><<<grid, 256, 0, stream>>>(a); break;
+            default: norm_rows_direct_kernel<TI, TO, 12><<<grid, 256, 0, stream>>>(a); break;
+        }
+        return launch_status();
+    }
 
     const Tuning tu = tuning(kFamNorm);
     const int budget = (kSmemPerSm / tu.ctas_per_sm < di.max_smem_optin ? kSmemPerSm / tu.ctas_per_sm

@@ -1,7 +1,9 @@
 // runtime.cu -- per-device set-up, the device fault word, tuning knobs and status strings.
 #include <atomic>
 #include <mutex>
+#include <map>
 #include <set>
+#include <tuple>
 #include <utility>
 
 #include "common.cuh"
@@ -26,6 +28,7 @@ std::set<std::pair<const void*, int>> g_smem_done;  // (kernel, device)
 
 std::atomic<int> g_tune_ctas[kFamCount] = {{2}, {1}, {1}, {4}, {4}};
 std::atomic<int> g_tune_stages[kFamCount] = {{0}, {0}, {0}, {0}, {0}};
+std::atomic<int> g_variant[kFamCount] = {{0}, {0}, {0}, {0}, {0}};
 
 }  // namespace
 
@@ -87,6 +90,32 @@ Tuning tuning(int family) {
     return t;
 }
 
+int variant(int family) { return g_variant[family].load(std::memory_order_relaxed); }
+
+namespace {
+std::mutex g_occ_mu;
+std::map<std::tuple<const void*, int, int, int>, int> g_occ;  // (kernel, device, threads, smem)
+}  // namespace
+
+int resident_ctas(const void* kernel, int threads, int smem) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 1;
+    }
+    std::lock_guard<std::mutex> lk(g_occ_mu);
+    const auto key = std::make_tuple(kernel, dev, threads, smem);
+    auto it = g_occ.find(key);
+    if (it != g_occ.end()) return it->second;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, (size_t)smem) != cudaSuccess || n < 1) {
+        cudaGetLastError();
+        n = 1;
+    }
+    g_occ[key] = n;
+    return n;
+}
+
 }  // namespace wzyb
 
 extern "C" {
@@ -117,6 +146,13 @@ int wzyb_set_launch_tuning(int family, int ctas_per_sm, int stages) {
     if (ctas_per_sm < 1 || ctas_per_sm > 16 || stages < 0 || stages > 64) return WZYB_ERR_VALUE;
     wzyb::g_tune_ctas[family].store(ctas_per_sm);
     wzyb::g_tune_stages[family].store(stages);
+    return WZYB_OK;
+}
+
+int wzyb_set_kernel_variant(int family, int variant) {
+    if (family < 0 || family >= wzyb::kFamCount) return WZYB_ERR_VALUE;
+    if (variant < WZYB_VARIANT_AUTO || variant > WZYB_VARIANT_ASYNC) return WZYB_ERR_VALUE;
+    wzyb::g_variant[family].store(variant);
     return WZYB_OK;
 }
 

@@ -24,6 +24,7 @@ OOB_CLAMP, OOB_ZERO_ID = 0, 1
 PLE_HASH_C_PRECEDENCE, PLE_HASH_XOR_THEN_ADD = 0, 1
 PLE_EOS_DEFAULT = 248044
 FAM_NORM, FAM_HEAD_ROPE, FAM_GDN, FAM_SWIGLU, FAM_GATHER = 0, 1, 2, 3, 4
+VARIANT_AUTO, VARIANT_RING, VARIANT_DIRECT, VARIANT_ASYNC = 0, 1, 2, 3
 
 
 class WzybError(RuntimeError):
@@ -124,6 +125,7 @@ _SIGS = {
     "wzyb_prepare_device": (c_int, []),
     "wzyb_read_faults": (c_int, [POINTER(c_uint32), c_int]),
     "wzyb_set_launch_tuning": (c_int, [c_int, c_int, c_int]),
+    "wzyb_set_kernel_variant": (c_int, [c_int, c_int]),
     "wzyb_status_string": (ctypes.c_char_p, [c_int]),
     "wzyb_version": (c_int, []),
 }
@@ -275,6 +277,10 @@ def read_faults(clear=True) -> int:
 
 def set_launch_tuning(family: int, ctas_per_sm: int, stages: int = 0) -> None:
     call("wzyb_set_launch_tuning", family, ctas_per_sm, stages)
+
+
+def set_kernel_variant(family: int, variant: int) -> None:
+    call("wzyb_set_kernel_variant", family, variant)
 
 
 def declared_functions(header_path: str = HEADER_PATH) -> list[str]:

@@ -353,6 +353,8 @@ def main():
     ap.add_argument("--no-kernels", action="store_true")
     ap.add_argument("--variant", default="auto", choices=["auto", "ring", "direct", "async"],
                     help="kernel design of the norm families (A/B measurement)")
+    ap.add_argument("--tune", action="append", default=[],
+                    help="FAMILY:CTAS_PER_SM:STAGES launch tuning (wzyb_set_launch_tuning), repeatable")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -405,6 +407,9 @@ def main():
            "async": wz.VARIANT_ASYNC}[args.variant]
     for fam in (wz.FAM_NORM, wz.FAM_HEAD_ROPE, wz.FAM_GDN):
         wz.set_kernel_variant(fam, var)
+    for spec in args.tune:
+        fam, ctas, stages = (int(v) for v in spec.split(":"))
+        wz.set_launch_tuning(fam, ctas, stages)
 
     row0, n = wz.shard_rows(args.tokens, world, rank)
     sh = Shard(wz, torch, n, row0, 1000 + rank, dev)

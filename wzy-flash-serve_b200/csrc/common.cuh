@@ -144,8 +144,28 @@ struct Vec8<__half> {
         return Raw{__ldcs(reinterpret_cast<const uint4*>(p))};
     }
     __device__ __forceinline__ static void cvt(const Raw& r, float (&f)[8]) { to_f32(r.u, f); }
+    // packed forms: 8 elements as float2[4]
+    __device__ __forceinline__ static void cvt2(const uint4& u, float2 (&f)[4]) {
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) f[i] = __half22float2(h[i]);
+    }
+    __device__ __forceinline__ static void cvt2(const Raw& r, float2 (&f)[4]) { cvt2(r.u, f); }
+    __device__ __forceinline__ static void load_ro2(const __half* p, float2 (&f)[4]) {
+        cvt2(__ldg(reinterpret_cast<const uint4*>(p)), f);
+    }
+    __device__ __forceinline__ static void store2(__half* p, const float2 (&f)[4]) {
+        uint4 u;
+        __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __float22half2_rn(f[i]);
+        *reinterpret_cast<uint4*>(p) = u;
+    }
     // lane-private staging: a vector occupies kChunks 16-byte chunks, chunk c of lane l at slot[c*32 + l]
     static constexpr int kChunks = 1;
+    __device__ __forceinline__ static void unstage2(const uint4* slot, int lane, float2 (&f)[4]) {
+        cvt2(slot[lane], f);
+    }
     __device__ __forceinline__ static void stage_async(uint4* slot, int lane, const __half* g) {
         cp_async16(slot + lane, g);
     }
@@ -200,6 +220,32 @@ struct Vec8<float> {
     __device__ __forceinline__ static void cvt(const Raw& r, float (&f)[8]) {
         f[0] = r.a.x; f[1] = r.a.y; f[2] = r.a.z; f[3] = r.a.w;
         f[4] = r.b.x; f[5] = r.b.y; f[6] = r.b.z; f[7] = r.b.w;
+    }
+    __device__ __forceinline__ static void cvt2(const Raw& r, float2 (&f)[4]) {
+        f[0] = make_float2(r.a.x, r.a.y);
+        f[1] = make_float2(r.a.z, r.a.w);
+        f[2] = make_float2(r.b.x, r.b.y);
+        f[3] = make_float2(r.b.z, r.b.w);
+    }
+    __device__ __forceinline__ static void load_ro2(const float* p, float2 (&f)[4]) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+        f[0] = make_float2(a.x, a.y);
+        f[1] = make_float2(a.z, a.w);
+        f[2] = make_float2(b.x, b.y);
+        f[3] = make_float2(b.z, b.w);
+    }
+    __device__ __forceinline__ static void store2(float* p, const float2 (&f)[4]) {
+        reinterpret_cast<float4*>(p)[0] = make_float4(f[0].x, f[0].y, f[1].x, f[1].y);
+        reinterpret_cast<float4*>(p)[1] = make_float4(f[2].x, f[2].y, f[3].x, f[3].y);
+    }
+    __device__ __forceinline__ static void unstage2(const uint4* slot, int lane, float2 (&f)[4]) {
+        const float4 a = reinterpret_cast<const float4*>(slot)[lane];
+        const float4 b = reinterpret_cast<const float4*>(slot)[32 + lane];
+        f[0] = make_float2(a.x, a.y);
+        f[1] = make_float2(a.z, a.w);
+        f[2] = make_float2(b.x, b.y);
+        f[3] = make_float2(b.z, b.w);
     }
     static constexpr int kChunks = 2;
     __device__ __forceinline__ static void stage_async(uint4* slot, int lane, const float* g) {
@@ -264,6 +310,32 @@ struct StridePos {
         }
     }
 };
+
+// ----------------------------------------------------------------------------------------------
+// Packed fp32 (sm_100 FFMA2 / FMUL2 / FADD2): two independent fp32 operations per instruction, each
+// rounded exactly like its scalar counterpart. An 8-element vector is held as float2[4].
+// ----------------------------------------------------------------------------------------------
+__device__ __forceinline__ float2 splat2(float s) { return make_float2(s, s); }
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+
+// sum of squares of an 8-vector: two interleaved partial sums, then one add
+__device__ __forceinline__ float sumsq8(const float2 (&v)[4]) {
+    float2 acc = fmul2(v[0], v[0]);
+#pragma unroll
+    for (int i = 1; i < 4; ++i) acc = ffma2(v[i], v[i], acc);
+    return acc.x + acc.y;
+}
+
+// 1/sqrt(x) with the hardware approximation (PTX rsqrt.approx, one instruction). The reference calls
+// rsqrtf, also an approximate reciprocal square root; the .ftz form only differs for subnormal x,
+// and here x = mean(v^2) + eps >= eps > 0 is never subnormal.
+__device__ __forceinline__ float rsqrt_approx(float x) {
+    float y;
+    asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 // Sum over aligned groups of `kLanes` lanes (kLanes a power of two <= 32) with xor shuffles.
 template <int kLanes>

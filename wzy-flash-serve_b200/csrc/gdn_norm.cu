@@ -18,7 +18,22 @@ namespace wzyb {
 // returns 0, where the exact quotient is below 1e-37.
 __device__ __forceinline__ float gdn_gate(float x, float z, bool silu) {
     const float den = 1.0f + __expf(-z);
-    return silu ? x * __fdividef(z, den) : __fdividef(x, den);
+    const float q = __fdividef(silu ? z : x, den);  // one divide for either gate
+    return silu ? x * q : q;
+}
+
+// One head's 8-element slice in this lane (packed fp32): out = gdn_gate((o * rsqrt(...)) * gamma, z)
+// with the sum of squares reduced over the head's L lanes.
+template <int L, int HD>
+__device__ __forceinline__ void gdn_vec(const float2 (&o)[4], const float2 (&z)[4], const float2 (&g)[4], float eps,
+                                        bool silu, float2 (&out)[4]) {
+    const float ss = group_sum<L>(sumsq8(o));
+    const float2 sc = splat2(rsqrt_approx(ss * (1.0f / (float)HD) + eps));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 x = fmul2(fmul2(o[i], sc), g[i]);
+        out[i] = make_float2(gdn_gate(x.x, z[i].x, silu), gdn_gate(x.y, z[i].y, silu));
+    }
 }
 
 struct GdnArgs {
@@ -119,7 +134,7 @@ __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) gdn_norm_kernel(const G
 #pragma unroll
             for (int e = 0; e < 8; ++e) ss += ov[k][e] * ov[k][e];
             ss = group_sum<L>(ss);
-            const float sc = rsqrtf(ss * (1.0f / (float)HD) + a.eps);
+            const float sc = rsqrt_approx(ss * (1.0f / (float)HD) + a.eps);
             float out[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
@@ -145,10 +160,10 @@ __global__ void __launch_bounds__(256) gdn_direct_kernel(const GdnArgs a) {
     const TI* __restrict__ o = static_cast<const TI*>(a.o);
     const TI* __restrict__ z = static_cast<const TI*>(a.z);
     TO* __restrict__ y = static_cast<TO*>(a.y);
-    float g[8];
-    Vec8<TI>::load_ro(static_cast<const TI*>(a.gamma) + (lane % L) * 8, g);
+    float2 g[4];
+    Vec8<TI>::load_ro2(static_cast<const TI*>(a.gamma) + (lane % L) * 8, g);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) g[e] = a.w_offset + g[e];
+    for (int i = 0; i < 4; ++i) g[i] = fadd2(splat2(a.w_offset), g[i]);
     const bool silu = a.gate_mode == WZYB_GATE_SILU;
 
     StridePos pos(gwarp, nwarps, slabs);  // item it = (token q, slab r)
@@ -172,25 +187,16 @@ __global__ void __launch_bounds__(256) gdn_direct_kernel(const GdnArgs a) {
 #pragma unroll
         for (int k = 0; k < kU; ++k) {
             if (base + k * nwarps >= items) break;  // warp-uniform
-            float ov[8], zv[8];
+            float2 ov[4], zv[4], out[4];
             if (off[k] >= 0) {
-                Vec8<TI>::cvt(ro[k], ov);
-                Vec8<TI>::cvt(rz[k], zv);
+                Vec8<TI>::cvt2(ro[k], ov);
+                Vec8<TI>::cvt2(rz[k], zv);
             } else {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) ov[e] = zv[e] = 0.f;
+                for (int i = 0; i < 4; ++i) ov[i] = zv[i] = splat2(0.f);
             }
-            float ss = 0.f;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) ss += ov[e] * ov[e];
-            ss = group_sum<L>(ss);
-            const float sc = rsqrtf(ss * (1.0f / (float)HD) + a.eps);
-            float out[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                out[e] = gdn_gate(ov[e] * sc * g[e], zv[e], silu);
-            }
-            if (off[k] >= 0) Vec8<TO>::store(y + off[k], out);
+            gdn_vec<L, HD>(ov, zv, g, a.eps, silu, out);
+            if (off[k] >= 0) Vec8<TO>::store2(y + off[k], out);
         }
     }
 }
@@ -215,10 +221,10 @@ __global__ void __launch_bounds__(256) gdn_async_kernel(const GdnArgs a) {
     const TI* __restrict__ o = static_cast<const TI*>(a.o);
     const TI* __restrict__ z = static_cast<const TI*>(a.z);
     TO* __restrict__ y = static_cast<TO*>(a.y);
-    float g[8];
-    Vec8<TI>::load_ro(static_cast<const TI*>(a.gamma) + (lane % L) * 8, g);
+    float2 g[4];
+    Vec8<TI>::load_ro2(static_cast<const TI*>(a.gamma) + (lane % L) * 8, g);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) g[e] = a.w_offset + g[e];
+    for (int i = 0; i < 4; ++i) g[i] = fadd2(splat2(a.w_offset), g[i]);
     const bool silu = a.gate_mode == WZYB_GATE_SILU;
 
     // element offset of this lane's vector for the item at `p`, or -1
@@ -248,28 +254,19 @@ __global__ void __launch_bounds__(256) gdn_async_kernel(const GdnArgs a) {
         cp_async_wait<kP - 1>();
         const int64_t off = offset(it, cpos);
         cpos.advance();
-        float ov[8], zv[8];
+        float2 ov[4], zv[4], out[4];
         if (off >= 0) {
-            Vec8<TI>::unstage(ring + slot * SLOT, lane, ov);
-            Vec8<TI>::unstage(ring + slot * SLOT + C * 32, lane, zv);
+            Vec8<TI>::unstage2(ring + slot * SLOT, lane, ov);
+            Vec8<TI>::unstage2(ring + slot * SLOT + C * 32, lane, zv);
         } else {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) ov[e] = zv[e] = 0.f;
+            for (int i = 0; i < 4; ++i) ov[i] = zv[i] = splat2(0.f);
         }
         // Refill the slot. Only this lane reads or writes its chunks of the slot, and its unstaging
         // loads precede the new copy in program order, which orders them before the copy's write.
         issue(it + kP * nwarps, slot);
-        float ss = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) ss += ov[e] * ov[e];
-        ss = group_sum<L>(ss);
-        const float sc = rsqrtf(ss * (1.0f / (float)HD) + a.eps);
-        float out[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            out[e] = gdn_gate(ov[e] * sc * g[e], zv[e], silu);
-        }
-        if (off >= 0) Vec8<TO>::store(y + off, out);
+        gdn_vec<L, HD>(ov, zv, g, a.eps, silu, out);
+        if (off >= 0) Vec8<TO>::store2(y + off, out);
     }
     cp_async_wait<0>();
 }

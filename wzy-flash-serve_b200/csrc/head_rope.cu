@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) head_rope_kernel(const 
 #pragma unroll
             for (int e = 0; e < 8; ++e) ss += p[k][e] * p[k][e];
             ss = group_sum<L>(ss);
-            const float sc = rsqrtf(ss / (float)HD + a.eps);
+            const float sc = rsqrt_approx(ss / (float)HD + a.eps);
 #pragma unroll
             for (int e = 0; e < 8; ++e) p[k][e] *= sc * g[k][e];
 
@@ -187,13 +187,64 @@ __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) head_rope_kernel(const 
     }
 }
 
+// ---- per-head math shared by the direct and async designs (packed fp32) ------------------------
+// gamma of this lane's 8 dims for the q (g[0]) and k (g[1]) sections, with the weight offset added
+template <typename T>
+__device__ __forceinline__ void load_head_gammas(const HeadRopeArgs& a, int li, float2 (&g)[2][4]) {
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) g[s][i] = splat2(0.f);
+        if (a.sec[s].heads > 0) {
+            Vec8<T>::load_ro2(static_cast<const T*>(a.sec[s].gamma) + li * 8, g[s]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) g[s][i] = fadd2(splat2(a.w_offset), g[s][i]);
+        }
+    }
+}
+
+// cos and a signed sin, so that both halves rotate with out = own*cos + partner*ssin:
+// first half a*cos - d*sin (ssin = -sin), second half d*cos + a*sin (ssin = +sin).
+__device__ __forceinline__ void sign_sin(bool first_half, float2 (&s2)[4]) {
+    if (first_half) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s2[i] = make_float2(-s2[i].x, -s2[i].y);
+    }
+}
+
+// One head's 8-element slice in this lane: p *= rsqrt(mean(p^2) + eps) * gamma over the head's L
+// lanes, then (rotate) the NeoX pair rotation with the partner slice fetched from lane `src`.
+template <int L, int HD>
+__device__ __forceinline__ void norm_rope_head(float2 (&p)[4], bool q_gamma, const float2 (&g)[2][4], float eps,
+                                               int src, bool rotate, const float2 (&c2)[4], const float2 (&s2)[4]) {
+    const float ss = group_sum<L>(sumsq8(p));
+    const float2 sc = splat2(rsqrt_approx(ss / (float)HD + eps));
+    if (q_gamma) {  // warp-uniform when a warp holds one head
+#pragma unroll
+        for (int i = 0; i < 4; ++i) p[i] = fmul2(p[i], fmul2(sc, g[0][i]));
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) p[i] = fmul2(p[i], fmul2(sc, g[1][i]));
+    }
+    float2 q[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        q[i].x = __shfl_sync(0xffffffffu, p[i].x, src);
+        q[i].y = __shfl_sync(0xffffffffu, p[i].y, src);
+    }
+    if (rotate) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) p[i] = ffma2(q[i], s2[i], fmul2(p[i], c2[i]));
+    }
+}
+
 // Direct design: a warp owns a chunk of kNH*(32/L) consecutive heads of ONE token (q heads first,
 // then k heads), so the token's cos/sin row is fetched once per chunk. All heads of the chunk are
 // loaded as raw 16-byte registers before any arithmetic; each head is then normalised inside its
 // lane group and rotated with one shuffle per element, and written back in place. No shared memory,
 // no CTA barrier.
 template <typename T, int HD, int kNH>
-__global__ void __launch_bounds__(256) head_rope_direct_kernel(const HeadRopeArgs a) {
+__global__ void __launch_bounds__(256, kNH <= 4 ? 3 : 2) head_rope_direct_kernel(const HeadRopeArgs a) {
     constexpr int L = HD / 8;
     constexpr int HPW = 32 / L;         // heads side by side in one warp
     constexpr int CH = kNH * HPW;       // heads per chunk
@@ -211,76 +262,51 @@ __global__ void __launch_bounds__(256) head_rope_direct_kernel(const HeadRopeArg
     const int ci = (first_half ? li : li - hl) * 8;
     const int64_t base_pos = (a.d_base_pos ? (int64_t)__ldg(a.d_base_pos) : 0) + a.pos_offset;
 
-    float g[2][8];
-#pragma unroll
-    for (int s = 0; s < 2; ++s) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) g[s][e] = 0.f;
-        if (a.sec[s].heads > 0) {
-            Vec8<T>::load_ro(static_cast<const T*>(a.sec[s].gamma) + li * 8, g[s]);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) g[s][e] = a.w_offset + g[s][e];
-        }
-    }
+    float2 g[2][4];
+    load_head_gammas<T>(a, li, g);
+
+    // Section row bases are formed once per token; a head is then one 64-bit multiply-add away.
+    T* const qdata = static_cast<T*>(a.sec[0].data);
+    T* const kdata = static_cast<T*>(a.sec[1].heads > 0 ? a.sec[1].data : a.sec[0].data);
+    const int64_t qrs = a.sec[0].row_stride, qhs = a.sec[0].head_stride;
+    const int64_t krs = a.sec[1].row_stride, khs = a.sec[1].head_stride;
 
     StridePos ps(gwarp, nwarps, chunks);  // item it = (token q, chunk r)
     for (int64_t it = gwarp; it < items; it += nwarps, ps.advance()) {
         const int64_t t = ps.q;
         const int h0 = ps.r * CH;
+        T* const qrow = qdata + t * qrs + li * 8;
+        T* const krow = kdata + t * krs + li * 8;
         typename Vec8<T>::Raw rp[kNH];
         T* dst[kNH];
 #pragma unroll
         for (int j = 0; j < kNH; ++j) {
             const int h = h0 + j * HPW + hw;
-            dst[j] = nullptr;
-            if (h < htot) {
-                const int s = h < hq ? 0 : 1;
-                const HeadSection& sc = a.sec[s];
-                dst[j] = static_cast<T*>(sc.data) + t * sc.row_stride + (int64_t)(s == 0 ? h : h - hq) * sc.head_stride +
-                         li * 8;
-                rp[j] = Vec8<T>::ldcs_raw(dst[j]);
-            }
+            dst[j] = h < hq ? qrow + h * qhs : krow + (h - hq) * khs;
+            if (h < htot) rp[j] = Vec8<T>::ldcs_raw(dst[j]);
         }
         const int64_t pos = base_pos + t;
         const bool pos_ok = half > 0 && pos >= 0 && pos < a.table_rows;
-        float c8[8], s8[8];
+        float2 c2[4], s2[4];
         if (pos_ok && rot_lane) {
-            Vec8<float>::load_ro(a.cos_tab + pos * half + ci, c8);
-            Vec8<float>::load_ro(a.sin_tab + pos * half + ci, s8);
+            Vec8<float>::load_ro2(a.cos_tab + pos * half + ci, c2);
+            Vec8<float>::load_ro2(a.sin_tab + pos * half + ci, s2);
+            sign_sin(first_half, s2);
         }
         if (half > 0 && !pos_ok && lane == 0 && h0 == 0) raise_fault(WZYB_FAULT_POS_RANGE);
 #pragma unroll
         for (int j = 0; j < kNH; ++j) {
             if (h0 + j * HPW >= htot) break;  // warp-uniform: no head of this round exists
             const int h = h0 + j * HPW + hw;
-            float p[8];
-            if (dst[j] != nullptr) {
-                Vec8<T>::cvt(rp[j], p);
+            float2 p[4];
+            if (h < htot) {
+                Vec8<T>::cvt2(rp[j], p);
             } else {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) p[e] = 0.f;
+                for (int i = 0; i < 4; ++i) p[i] = splat2(0.f);
             }
-            float ss = 0.f;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) ss += p[e] * p[e];
-            ss = group_sum<L>(ss);
-            const float sc = rsqrtf(ss / (float)HD + a.eps);
-            const float* gs = g[h < hq ? 0 : 1];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) p[e] *= sc * gs[e];
-            float q2[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) q2[e] = __shfl_sync(0xffffffffu, p[e], src);
-            if (pos_ok && rot_lane) {
-                if (first_half) {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) p[e] = p[e] * c8[e] - q2[e] * s8[e];  // a*cos - d*sin
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) p[e] = q2[e] * s8[e] + p[e] * c8[e];  // a*sin + d*cos
-                }
-            }
-            if (dst[j] != nullptr) Vec8<T>::store(dst[j], p);
+            norm_rope_head<L, HD>(p, h < hq, g, a.eps, src, pos_ok && rot_lane, c2, s2);
+            if (h < htot) Vec8<T>::store2(dst[j], p);
         }
     }
 }
@@ -311,17 +337,8 @@ __global__ void __launch_bounds__(128) head_rope_async_kernel(const HeadRopeArgs
     const int c8i = first_half ? li : li - hl;  // which 8 cos/sin values this lane uses
     const int64_t base_pos = (a.d_base_pos ? (int64_t)__ldg(a.d_base_pos) : 0) + a.pos_offset;
 
-    float g[2][8];
-#pragma unroll
-    for (int s = 0; s < 2; ++s) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) g[s][e] = 0.f;
-        if (a.sec[s].heads > 0) {
-            Vec8<T>::load_ro(static_cast<const T*>(a.sec[s].gamma) + li * 8, g[s]);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) g[s][e] = a.w_offset + g[s][e];
-        }
-    }
+    float2 g[2][4];
+    load_head_gammas<T>(a, li, g);
     auto head_ptr = [&](int64_t t, int h) -> T* {
         const int s = h < hq ? 0 : 1;
         const HeadSection& sc = a.sec[s];
@@ -368,25 +385,31 @@ __global__ void __launch_bounds__(128) head_rope_async_kernel(const HeadRopeArgs
         cp_async_wait<kP - 1>();
         __syncwarp();  // the cos/sin row copied by other lanes is visible
         const uint4* sl = ring + slot * slot_u4;
-        float p[kNH][8];
+        float2 p[kNH][4];
 #pragma unroll
         for (int j = 0; j < kNH; ++j) {
             if (h0 + j * HPW + hw < htot) {
-                Vec8<T>::unstage(sl + j * C * 32, lane, p[j]);
+                Vec8<T>::unstage2(sl + j * C * 32, lane, p[j]);
             } else {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) p[j][e] = 0.f;
+                for (int i = 0; i < 4; ++i) p[j][i] = splat2(0.f);
             }
         }
-        float c8[8], s8[8];
+        float2 c2[4], s2[4];
         if (pos_ok && rot_lane) {
+            // cos chunk k at tab[2k], tab[2k+1]; sin chunk k at tab[2(hl+k)], tab[2(hl+k)+1]
             const float4* tab = reinterpret_cast<const float4*>(sl + kNH * C * 32);
-            const float4 c0 = tab[c8i * 2], c1 = tab[c8i * 2 + 1];
-            const float4 s0 = tab[(hl + c8i) * 2], s1 = tab[(hl + c8i) * 2 + 1];
-            c8[0] = c0.x; c8[1] = c0.y; c8[2] = c0.z; c8[3] = c0.w;
-            c8[4] = c1.x; c8[5] = c1.y; c8[6] = c1.z; c8[7] = c1.w;
-            s8[0] = s0.x; s8[1] = s0.y; s8[2] = s0.z; s8[3] = s0.w;
-            s8[4] = s1.x; s8[5] = s1.y; s8[6] = s1.z; s8[7] = s1.w;
+            const float4 ca = tab[c8i * 2], cb = tab[c8i * 2 + 1];
+            const float4 sa = tab[(hl + c8i) * 2], sb = tab[(hl + c8i) * 2 + 1];
+            c2[0] = make_float2(ca.x, ca.y);
+            c2[1] = make_float2(ca.z, ca.w);
+            c2[2] = make_float2(cb.x, cb.y);
+            c2[3] = make_float2(cb.z, cb.w);
+            s2[0] = make_float2(sa.x, sa.y);
+            s2[1] = make_float2(sa.z, sa.w);
+            s2[2] = make_float2(sb.x, sb.y);
+            s2[3] = make_float2(sb.z, sb.w);
+            sign_sin(first_half, s2);
         }
         __syncwarp();  // every lane has read the slot: it may be refilled
         issue(it + kP * nwarps, slot);
@@ -394,30 +417,26 @@ __global__ void __launch_bounds__(128) head_rope_async_kernel(const HeadRopeArgs
         for (int j = 0; j < kNH; ++j) {
             if (h0 + j * HPW >= htot) break;  // warp-uniform
             const int h = h0 + j * HPW + hw;
-            float ss = 0.f;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) ss += p[j][e] * p[j][e];
-            ss = group_sum<L>(ss);
-            const float sc = rsqrtf(ss / (float)HD + a.eps);
-            const float* gs = g[h < hq ? 0 : 1];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) p[j][e] *= sc * gs[e];
-            float q2[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) q2[e] = __shfl_sync(0xffffffffu, p[j][e], src);
-            if (pos_ok && rot_lane) {
-                if (first_half) {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) p[j][e] = p[j][e] * c8[e] - q2[e] * s8[e];  // a*cos - d*sin
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) p[j][e] = q2[e] * s8[e] + p[j][e] * c8[e];  // a*sin + d*cos
-                }
-            }
-            if (h < htot) Vec8<T>::store(head_ptr(t, h), p[j]);
+            norm_rope_head<L, HD>(p[j], h < hq, g, a.eps, src, pos_ok && rot_lane, c2, s2);
+            if (h < htot) Vec8<T>::store2(head_ptr(t, h), p[j]);
         }
     }
     cp_async_wait<0>();
+}
+
+template <typename T, int kNH>
+static int launch_head_rope_direct(const HeadRopeArgs& a, int hd, int htot, const DeviceInfo& di,
+                                   cudaStream_t stream) {
+    const void* kern = hd == 64    ? (const void*)head_rope_direct_kernel<T, 64, kNH>
+                       : hd == 128 ? (const void*)head_rope_direct_kernel<T, 128, kNH>
+                                   : (const void*)head_rope_direct_kernel<T, 256, kNH>;
+    const int ch = kNH * (256 / hd);
+    const int64_t warp_items = a.T * ((htot + ch - 1) / ch);
+    const int grid = persistent_grid(di, resident_ctas(kern, 256, 0), (warp_items + 7) / 8);
+    if (hd == 64) head_rope_direct_kernel<T, 64, kNH><<<grid, 256, 0, stream>>>(a);
+    else if (hd == 128) head_rope_direct_kernel<T, 128, kNH><<<grid, 256, 0, stream>>>(a);
+    else head_rope_direct_kernel<T, 256, kNH><<<grid, 256, 0, stream>>>(a);
+    return launch_status();
 }
 
 template <typename T>
@@ -485,17 +504,10 @@ static int launch_head_rope(const HeadSection& q, const HeadSection& k, const fl
         return launch_status();
     }
     if (variant(kFamHeadRope) != WZYB_VARIANT_RING) {
-        constexpr int kNH = 6;
-        const void* kern = hd == 64    ? (const void*)head_rope_direct_kernel<T, 64, kNH>
-                           : hd == 128 ? (const void*)head_rope_direct_kernel<T, 128, kNH>
-                                       : (const void*)head_rope_direct_kernel<T, 256, kNH>;
-        const int ch = kNH * (256 / hd);
-        const int64_t warp_items = T_ * ((htot + ch - 1) / ch);
-        const int grid = persistent_grid(di, resident_ctas(kern, 256, 0), (warp_items + 7) / 8);
-        if (hd == 64) head_rope_direct_kernel<T, 64, kNH><<<grid, 256, 0, stream>>>(a);
-        else if (hd == 128) head_rope_direct_kernel<T, 128, kNH><<<grid, 256, 0, stream>>>(a);
-        else head_rope_direct_kernel<T, 256, kNH><<<grid, 256, 0, stream>>>(a);
-        return launch_status();
+        // Two instantiations: 6 heads per chunk at 2 CTAs/SM (no spill), or 4 heads per chunk capped
+        // at 3 CTAs/SM (more warps); a ctas_per_sm tuning of 3 or more selects the second.
+        if (tuning(kFamHeadRope).ctas_per_sm >= 3) return launch_head_rope_direct<T, 4>(a, hd, htot, di, stream);
+        return launch_head_rope_direct<T, 6>(a, hd, htot, di, stream);
     }
 
     const int slots = htot * (hd / 8);

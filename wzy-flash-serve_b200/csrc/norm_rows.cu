@@ -121,7 +121,7 @@ __global__ void __launch_bounds__(512) norm_rows_kernel(const NormRowsArgs a) {
         }
         float tot = 0.f;
         for (int q = 0; q < nwarps; ++q) tot += ring.red[(i & 1) * 32 + q];
-        const float sc = rsqrtf(tot / (float)n + a.eps);
+        const float sc = rsqrt_approx(tot / (float)n + a.eps);
         const int c = (int)(u % a.hc);
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
@@ -174,44 +174,42 @@ __global__ void __launch_bounds__(256, 2) norm_rows_direct_kernel(const NormRows
                 if (has_x) rx[k] = Vec8<TI>::ldcs_raw(xrow + e);
             }
         }
-        const float gate = (has_x && a.inj != nullptr) ? 2.0f / (1.0f + __expf(-a.inj[u] / (float)a.hc)) : 1.0f;
+        const float2 gate = splat2((has_x && a.inj != nullptr) ? 2.0f / (1.0f + __expf(-a.inj[u] / (float)a.hc))
+                                                                : 1.0f);
+        // v = residual + x * gate (packed FFMA2, the same rounding as the reference's scalar fma)
+        auto residual_sum = [&](int k, float2 (&v)[4]) {
+            Vec8<TI>::cvt2(rr[k], v);
+            if (has_x) {
+                float2 xv[4];
+                Vec8<TI>::cvt2(rx[k], xv);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) v[i] = ffma2(xv[i], gate, v[i]);
+            }
+        };
         float ss = 0.f;
 #pragma unroll
         for (int k = 0; k < VPL; ++k) {
-            const int e = (k * 32 + lane) * 8;
-            if (e < n) {
-                float v[8];
-                Vec8<TI>::cvt(rr[k], v);
-                if (has_x) {
-                    float xv[8];
-                    Vec8<TI>::cvt(rx[k], xv);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) v[j] += xv[j] * gate;
-                }
-#pragma unroll
-                for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+            if ((k * 32 + lane) * 8 < n) {
+                float2 v[4];
+                residual_sum(k, v);
+                ss += sumsq8(v);
             }
         }
         ss = group_sum<32>(ss);
-        const float sc = rsqrtf(ss / (float)n + a.eps);
+        const float2 sc = splat2(rsqrt_approx(ss / (float)n + a.eps));
+        const float2 woff = splat2(a.w_offset);
         const TI* wrow = w + (u - t * a.hc) * n;
 #pragma unroll
         for (int k = 0; k < VPL; ++k) {
             const int e = (k * 32 + lane) * 8;
             if (e < n) {
-                float v[8], g[8], o[8];
-                Vec8<TI>::cvt(rr[k], v);
-                if (has_x) {
-                    float xv[8];
-                    Vec8<TI>::cvt(rx[k], xv);
+                float2 v[4], g[4], o[4];
+                residual_sum(k, v);
+                Vec8<TI>::load_ro2(wrow + e, g);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) v[j] += xv[j] * gate;
-                }
-                Vec8<TI>::load_ro(wrow + e, g);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) o[j] = (v[j] * sc) * (a.w_offset + g[j]);
-                Vec8<TO>::store(y + u * n + e, o);
-                if (has_x) Vec8<TI>::store(res + u * n + e, v);
+                for (int i = 0; i < 4; ++i) o[i] = fmul2(fmul2(v[i], sc), fadd2(woff, g[i]));  // (v*sc)*g
+                Vec8<TO>::store2(y + u * n + e, o);
+                if (has_x) Vec8<TI>::store2(res + u * n + e, v);
             }
         }
     }

@@ -337,6 +337,29 @@ __device__ __forceinline__ float rsqrt_approx(float x) {
     return y;
 }
 
+// Logistic-function building blocks written from the identities e^x = 2^(x * log2 e) and
+// a / b = a * (1 / b), on the PTX approximate base-2 exponential and reciprocal instructions
+// (ex2.approx.ftz, rcp.approx.ftz; relative errors around 2^-22). For the gates here:
+//   sigmoid(z) = 1 / (1 + 2^(-z * log2 e))
+// which saturates correctly: z > 88 gives 2^(..) -> 0 (sigmoid 1), z < -88 gives inf (sigmoid 0).
+constexpr float kLog2e = 1.4426950408889634f;
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+// sigmoid of a pair
+__device__ __forceinline__ float2 sigmoid2(float2 z) {
+    const float2 t = fmul2(z, splat2(-kLog2e));
+    const float2 den = fadd2(splat2(1.0f), make_float2(ex2_approx(t.x), ex2_approx(t.y)));
+    return make_float2(rcp_approx(den.x), rcp_approx(den.y));
+}
+
 // Sum over aligned groups of `kLanes` lanes (kLanes a power of two <= 32) with xor shuffles.
 template <int kLanes>
 __device__ __forceinline__ float group_sum(float v) {

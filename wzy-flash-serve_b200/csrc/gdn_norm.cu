@@ -22,17 +22,20 @@ __device__ __forceinline__ float gdn_gate(float x, float z, bool silu) {
     return silu ? x * q : q;
 }
 
-// One head's 8-element slice in this lane (packed fp32): out = gdn_gate((o * rsqrt(...)) * gamma, z)
-// with the sum of squares reduced over the head's L lanes.
-template <int L, int HD>
+// One head's 8-element slice in this lane (packed fp32), the sum of squares reduced over the head's
+// L lanes:  x = (o * rsqrt(sum/hd + eps)) * gamma;  out = x * sigmoid(z)  or  x * (z * sigmoid(z)).
+// The reference divides x by (1 + exp(-z)); here x is multiplied by the approximate reciprocal of
+// 1 + 2^(-z log2 e) (sigmoid2), a few fp32 ulp from the IEEE quotient.
+template <int L, int HD, bool SILU>
 __device__ __forceinline__ void gdn_vec(const float2 (&o)[4], const float2 (&z)[4], const float2 (&g)[4], float eps,
-                                        bool silu, float2 (&out)[4]) {
+                                        float2 (&out)[4]) {
     const float ss = group_sum<L>(sumsq8(o));
     const float2 sc = splat2(rsqrt_approx(ss * (1.0f / (float)HD) + eps));
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const float2 x = fmul2(fmul2(o[i], sc), g[i]);
-        out[i] = make_float2(gdn_gate(x.x, z[i].x, silu), gdn_gate(x.y, z[i].y, silu));
+        const float2 s = sigmoid2(z[i]);
+        out[i] = SILU ? fmul2(x, fmul2(z[i], s)) : fmul2(x, s);
     }
 }
 
@@ -148,7 +151,7 @@ __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) gdn_norm_kernel(const G
 // Direct design: a warp owns one 256-element slab of a token row (32/L whole heads), keeps kU slabs of
 // o and z in flight as raw 16-byte registers, then normalises each head inside its lane group. No
 // shared memory, no CTA barrier: warps stream independently like a copy kernel.
-template <typename TI, typename TO, int HD, int kU>
+template <typename TI, typename TO, int HD, int kU, bool SILU>
 __global__ void __launch_bounds__(256) gdn_direct_kernel(const GdnArgs a) {
     constexpr int L = HD / 8;
     const int lane = threadIdx.x & 31;
@@ -164,7 +167,6 @@ __global__ void __launch_bounds__(256) gdn_direct_kernel(const GdnArgs a) {
     Vec8<TI>::load_ro2(static_cast<const TI*>(a.gamma) + (lane % L) * 8, g);
 #pragma unroll
     for (int i = 0; i < 4; ++i) g[i] = fadd2(splat2(a.w_offset), g[i]);
-    const bool silu = a.gate_mode == WZYB_GATE_SILU;
 
     StridePos pos(gwarp, nwarps, slabs);  // item it = (token q, slab r)
     for (int64_t base = gwarp; base < items; base += nwarps * kU) {
@@ -195,7 +197,7 @@ __global__ void __launch_bounds__(256) gdn_direct_kernel(const GdnArgs a) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) ov[i] = zv[i] = splat2(0.f);
             }
-            gdn_vec<L, HD>(ov, zv, g, a.eps, silu, out);
+            gdn_vec<L, HD, SILU>(ov, zv, g, a.eps, out);
             if (off[k] >= 0) Vec8<TO>::store2(y + off[k], out);
         }
     }
@@ -205,7 +207,7 @@ __global__ void __launch_bounds__(256) gdn_direct_kernel(const GdnArgs a) {
 // lane-private shared-memory ring filled by cp.async instead of in registers. Each lane copies and
 // later reads only its own 16-byte chunks, so the ring needs no barrier at all; the register file is
 // no longer what bounds the bytes in flight.
-template <typename TI, typename TO, int HD, int kP>
+template <typename TI, typename TO, int HD, int kP, bool SILU>
 __global__ void __launch_bounds__(256) gdn_async_kernel(const GdnArgs a) {
     constexpr int L = HD / 8;
     constexpr int C = Vec8<TI>::kChunks;   // 16-byte chunks per 8-element vector
@@ -225,7 +227,6 @@ __global__ void __launch_bounds__(256) gdn_async_kernel(const GdnArgs a) {
     Vec8<TI>::load_ro2(static_cast<const TI*>(a.gamma) + (lane % L) * 8, g);
 #pragma unroll
     for (int i = 0; i < 4; ++i) g[i] = fadd2(splat2(a.w_offset), g[i]);
-    const bool silu = a.gate_mode == WZYB_GATE_SILU;
 
     // element offset of this lane's vector for the item at `p`, or -1
     auto offset = [&](int64_t it, const StridePos& p) -> int64_t {
@@ -265,10 +266,38 @@ __global__ void __launch_bounds__(256) gdn_async_kernel(const GdnArgs a) {
         // Refill the slot. Only this lane reads or writes its chunks of the slot, and its unstaging
         // loads precede the new copy in program order, which orders them before the copy's write.
         issue(it + kP * nwarps, slot);
-        gdn_vec<L, HD>(ov, zv, g, a.eps, silu, out);
+        gdn_vec<L, HD, SILU>(ov, zv, g, a.eps, out);
         if (off >= 0) Vec8<TO>::store2(y + off, out);
     }
     cp_async_wait<0>();
+}
+
+// Launch one of the warp-owned designs (direct or cp.async) for head size hd.
+template <typename TI, typename TO, bool SILU>
+static int launch_gdn_warp(const GdnArgs& a, int hd, bool async_design, const DeviceInfo& di, cudaStream_t stream) {
+    constexpr int kP = sizeof(TI) == 2 ? 8 : 4;
+    const int64_t warp_items = a.T * (((int64_t)a.heads * hd + 255) / 256);
+    if (async_design) {
+        const void* kern = hd == 64    ? (const void*)gdn_async_kernel<TI, TO, 64, kP, SILU>
+                           : hd == 128 ? (const void*)gdn_async_kernel<TI, TO, 128, kP, SILU>
+                                       : (const void*)gdn_async_kernel<TI, TO, 256, kP, SILU>;
+        const int smem = 8 * kP * 2 * Vec8<TI>::kChunks * 32 * 16;
+        const int rc = ensure_smem(kern, smem);
+        if (rc != WZYB_OK) return rc;
+        const int grid = persistent_grid(di, resident_ctas(kern, 256, smem), (warp_items + 7) / 8);
+        if (hd == 64) gdn_async_kernel<TI, TO, 64, kP, SILU><<<grid, 256, smem, stream>>>(a);
+        else if (hd == 128) gdn_async_kernel<TI, TO, 128, kP, SILU><<<grid, 256, smem, stream>>>(a);
+        else gdn_async_kernel<TI, TO, 256, kP, SILU><<<grid, 256, smem, stream>>>(a);
+        return launch_status();
+    }
+    const void* kern = hd == 64    ? (const void*)gdn_direct_kernel<TI, TO, 64, 4, SILU>
+                       : hd == 128 ? (const void*)gdn_direct_kernel<TI, TO, 128, 4, SILU>
+                                   : (const void*)gdn_direct_kernel<TI, TO, 256, 4, SILU>;
+    const int grid = persistent_grid(di, resident_ctas(kern, 256, 0), (warp_items + 7) / 8);
+    if (hd == 64) gdn_direct_kernel<TI, TO, 64, 4, SILU><<<grid, 256, 0, stream>>>(a);
+    else if (hd == 128) gdn_direct_kernel<TI, TO, 128, 4, SILU><<<grid, 256, 0, stream>>>(a);
+    else gdn_direct_kernel<TI, TO, 256, 4, SILU><<<grid, 256, 0, stream>>>(a);
+    return launch_status();
 }
 
 template <typename TI, typename TO>
@@ -297,31 +326,13 @@ static int launch_gdn(const void* o, const void* z, const void* gamma, void* y, 
     a.row_bytes = (uint32_t)((int64_t)heads * hd * sizeof(TI));
     a.stage_bytes = 2u * a.row_bytes;
 
-    if (variant(kFamGdn) == WZYB_VARIANT_ASYNC) {
-        constexpr int kP = sizeof(TI) == 2 ? 8 : 4;
-        const void* kern = hd == 64    ? (const void*)gdn_async_kernel<TI, TO, 64, kP>
-                           : hd == 128 ? (const void*)gdn_async_kernel<TI, TO, 128, kP>
-                                       : (const void*)gdn_async_kernel<TI, TO, 256, kP>;
-        const int smem = 8 * kP * 2 * Vec8<TI>::kChunks * 32 * 16;
-        rc = ensure_smem(kern, smem);
-        if (rc != WZYB_OK) return rc;
-        const int64_t warp_items = T * (((int64_t)heads * hd + 255) / 256);
-        const int grid = persistent_grid(di, resident_ctas(kern, 256, smem), (warp_items + 7) / 8);
-        if (hd == 64) gdn_async_kernel<TI, TO, 64, kP><<<grid, 256, smem, stream>>>(a);
-        else if (hd == 128) gdn_async_kernel<TI, TO, 128, kP><<<grid, 256, smem, stream>>>(a);
-        else gdn_async_kernel<TI, TO, 256, kP><<<grid, 256, smem, stream>>>(a);
-        return launch_status();
-    }
-    if (variant(kFamGdn) != WZYB_VARIANT_RING) {
-        const void* kern = hd == 64    ? (const void*)gdn_direct_kernel<TI, TO, 64, 4>
-                           : hd == 128 ? (const void*)gdn_direct_kernel<TI, TO, 128, 4>
-                                       : (const void*)gdn_direct_kernel<TI, TO, 256, 4>;
-        const int64_t warp_items = T * (((int64_t)heads * hd + 255) / 256);
-        const int grid = persistent_grid(di, resident_ctas(kern, 256, 0), (warp_items + 7) / 8);
-        if (hd == 64) gdn_direct_kernel<TI, TO, 64, 4><<<grid, 256, 0, stream>>>(a);
-        else if (hd == 128) gdn_direct_kernel<TI, TO, 128, 4><<<grid, 256, 0, stream>>>(a);
-        else gdn_direct_kernel<TI, TO, 256, 4><<<grid, 256, 0, stream>>>(a);
-        return launch_status();
+    // The direct design is the default (measured on B200 at 262,144 tokens: direct 84%, cp.async 83%,
+    // TMA ring 43% of HBM peak).
+    const int v = variant(kFamGdn);
+    if (v == WZYB_VARIANT_AUTO || v == WZYB_VARIANT_ASYNC || v == WZYB_VARIANT_DIRECT) {
+        const bool async_design = v == WZYB_VARIANT_ASYNC;
+        return gate_mode == WZYB_GATE_SILU ? launch_gdn_warp<TI, TO, true>(a, hd, async_design, di, stream)
+                                           : launch_gdn_warp<TI, TO, false>(a, hd, async_design, di, stream);
     }
 
     const int slots = heads * hd / 8;

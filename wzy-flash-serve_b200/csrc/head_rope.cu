@@ -316,7 +316,7 @@ __global__ void __launch_bounds__(256, kNH <= 4 ? 3 : 2) head_rope_direct_kernel
 // cos/sin row, instead of in registers. Head vectors are lane-private; the cos/sin row is copied by
 // the first-half rotary lanes and read by both halves, so each slot is bracketed by __syncwarp.
 template <typename T, int HD, int kNH, int kP>
-__global__ void __launch_bounds__(128) head_rope_async_kernel(const HeadRopeArgs a) {
+__global__ void __launch_bounds__(128, 6) head_rope_async_kernel(const HeadRopeArgs a) {
     constexpr int L = HD / 8;
     constexpr int HPW = 32 / L;
     constexpr int CH = kNH * HPW;
@@ -385,16 +385,6 @@ __global__ void __launch_bounds__(128) head_rope_async_kernel(const HeadRopeArgs
         cp_async_wait<kP - 1>();
         __syncwarp();  // the cos/sin row copied by other lanes is visible
         const uint4* sl = ring + slot * slot_u4;
-        float2 p[kNH][4];
-#pragma unroll
-        for (int j = 0; j < kNH; ++j) {
-            if (h0 + j * HPW + hw < htot) {
-                Vec8<T>::unstage2(sl + j * C * 32, lane, p[j]);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 4; ++i) p[j][i] = splat2(0.f);
-            }
-        }
         float2 c2[4], s2[4];
         if (pos_ok && rot_lane) {
             // cos chunk k at tab[2k], tab[2k+1]; sin chunk k at tab[2(hl+k)], tab[2(hl+k)+1]
@@ -411,15 +401,24 @@ __global__ void __launch_bounds__(128) head_rope_async_kernel(const HeadRopeArgs
             s2[3] = make_float2(sb.z, sb.w);
             sign_sin(first_half, s2);
         }
-        __syncwarp();  // every lane has read the slot: it may be refilled
-        issue(it + kP * nwarps, slot);
+        // Heads are unstaged one at a time (8 live registers per head, not kNH*8); the other kP-1
+        // slots stay in flight meanwhile, and this slot is refilled once all its heads are done.
 #pragma unroll
         for (int j = 0; j < kNH; ++j) {
             if (h0 + j * HPW >= htot) break;  // warp-uniform
             const int h = h0 + j * HPW + hw;
-            norm_rope_head<L, HD>(p[j], h < hq, g, a.eps, src, pos_ok && rot_lane, c2, s2);
-            if (h < htot) Vec8<T>::store2(head_ptr(t, h), p[j]);
+            float2 p[4];
+            if (h < htot) {
+                Vec8<T>::unstage2(sl + j * C * 32, lane, p);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) p[i] = splat2(0.f);
+            }
+            norm_rope_head<L, HD>(p, h < hq, g, a.eps, src, pos_ok && rot_lane, c2, s2);
+            if (h < htot) Vec8<T>::store2(head_ptr(t, h), p);
         }
+        __syncwarp();  // every lane has read the slot: it may be refilled
+        issue(it + kP * nwarps, slot);
     }
     cp_async_wait<0>();
 }
@@ -487,7 +486,7 @@ static int launch_head_rope(const HeadSection& q, const HeadSection& k, const fl
     a.contig[1] = (k.head_stride == hd || k.heads <= 1) ? 1 : 0;
 
     if (variant(kFamHeadRope) == WZYB_VARIANT_ASYNC) {
-        constexpr int kNH = 6, kP = 4;
+        constexpr int kNH = 4, kP = 4;
         const void* kern = hd == 64    ? (const void*)head_rope_async_kernel<T, 64, kNH, kP>
                            : hd == 128 ? (const void*)head_rope_async_kernel<T, 128, kNH, kP>
                                        : (const void*)head_rope_async_kernel<T, 256, kNH, kP>;

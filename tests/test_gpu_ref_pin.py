@@ -23,8 +23,22 @@ def ref(orc):
     return orc.ref_lib()
 
 
+_KEEP = []
+
+
+@pytest.fixture(autouse=True)
+def _keep_alive():
+    yield
+    torch.cuda.synchronize()
+    _KEEP.clear()
+
+
 def dev(a):
-    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+    # Kept alive until the test ends: a raw pointer taken from a temporary tensor would otherwise let
+    # the caching allocator hand the same block to the next tensor before the kernel has run.
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+    _KEEP.append(t)
+    return t
 
 
 def host(t):

@@ -55,9 +55,11 @@ WEIGHT_BYTES = {"add_rmsnorm": HIDDEN * 2, "qk_norm_rope": 2 * HD * 2, "swiglu":
 ROPE_TABLE_BYTES_PER_TOKEN = ROT // 2 * 4 * 2  # cos + sin row per position (reported separately)
 KERNELS = ["add_rmsnorm", "qk_norm_rope", "swiglu", "gdn_gated_norm"]
 
-# DRAM traffic per launch from ncu (dram__bytes_read.sum + dram__bytes_write.sum), per token, for the
-# dominant kernel; filled from the profiles/ capture of the same kernel (None until captured).
-NCU_TRAFFIC_PER_TOKEN = {"swiglu": None}
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per token of the dominant kernel, from
+# one ncu capture of a 32,768-token launch (profiles/layer_kernels_32768_ncu_full.md), scaled by the
+# tokens of a launch: reads scale exactly; writes are slightly under-counted at that size because the
+# tail of the output is still in L2 when the kernel ends.
+NCU_TRAFFIC_PER_TOKEN = {"swiglu": 32101}
 
 
 def peaks():

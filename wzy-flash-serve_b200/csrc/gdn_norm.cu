@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) gdn_norm_kernel(const G
 // o and z in flight as raw 16-byte registers, then normalises each head inside its lane group. No
 // shared memory, no CTA barrier: warps stream independently like a copy kernel.
 template <typename TI, typename TO, int HD, int kU, bool SILU>
-__global__ void __launch_bounds__(256) gdn_direct_kernel(const GdnArgs a) {
+__global__ void __launch_bounds__(256, sizeof(TI) == 2 ? 3 : 2) gdn_direct_kernel(const GdnArgs a) {
     constexpr int L = HD / 8;
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);

@@ -238,13 +238,39 @@ __device__ __forceinline__ void norm_rope_head(float2 (&p)[4], bool q_gamma, con
     }
 }
 
+// The same per-head math with the gamma slice read from shared memory (sg = this lane's 4 float2 of
+// the head's section), which keeps 16 registers per thread free for more resident warps.
+template <int L, int HD>
+__device__ __forceinline__ void norm_rope_head_sg(float2 (&p)[4], const float2* sg, float eps, int src, bool rotate,
+                                                  const float2 (&c2)[4], const float2 (&s2)[4]) {
+    const float ss = group_sum<L>(sumsq8(p));
+    const float2 sc = splat2(rsqrt_approx(ss / (float)HD + eps));
+    const float4 ga = reinterpret_cast<const float4*>(sg)[0];
+    const float4 gb = reinterpret_cast<const float4*>(sg)[1];
+    p[0] = fmul2(p[0], fmul2(sc, make_float2(ga.x, ga.y)));
+    p[1] = fmul2(p[1], fmul2(sc, make_float2(ga.z, ga.w)));
+    p[2] = fmul2(p[2], fmul2(sc, make_float2(gb.x, gb.y)));
+    p[3] = fmul2(p[3], fmul2(sc, make_float2(gb.z, gb.w)));
+    float2 q[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        q[i].x = __shfl_sync(0xffffffffu, p[i].x, src);
+        q[i].y = __shfl_sync(0xffffffffu, p[i].y, src);
+    }
+    if (rotate) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) p[i] = ffma2(q[i], s2[i], fmul2(p[i], c2[i]));
+    }
+}
+
 // Direct design: a warp owns a chunk of kNH*(32/L) consecutive heads of ONE token (q heads first,
 // then k heads), so the token's cos/sin row is fetched once per chunk. All heads of the chunk are
 // loaded as raw 16-byte registers before any arithmetic; each head is then normalised inside its
-// lane group and rotated with one shuffle per element, and written back in place. No shared memory,
-// no CTA barrier.
+// lane group and rotated with one shuffle per element, and written back in place. The only shared
+// memory holds the two gammas (2 KB, written once before the single CTA barrier at kernel start);
+// 128-thread CTAs and ~90 registers give ~20 resident warps per SM.
 template <typename T, int HD, int kNH>
-__global__ void __launch_bounds__(256, kNH <= 4 ? 3 : 2) head_rope_direct_kernel(const HeadRopeArgs a) {
+__global__ void __launch_bounds__(128) head_rope_direct_kernel(const HeadRopeArgs a) {
     constexpr int L = HD / 8;
     constexpr int HPW = 32 / L;         // heads side by side in one warp
     constexpr int CH = kNH * HPW;       // heads per chunk
@@ -262,8 +288,18 @@ __global__ void __launch_bounds__(256, kNH <= 4 ? 3 : 2) head_rope_direct_kernel
     const int ci = (first_half ? li : li - hl) * 8;
     const int64_t base_pos = (a.d_base_pos ? (int64_t)__ldg(a.d_base_pos) : 0) + a.pos_offset;
 
-    float2 g[2][4];
-    load_head_gammas<T>(a, li, g);
+    // gammas (+ weight offset) of both sections as fp32 in shared memory
+    __shared__ __align__(16) float2 sg[2][HD / 2];
+    for (int i = threadIdx.x; i < HD; i += blockDim.x) {
+        const int s = i / (HD / 2), c = (i % (HD / 2)) * 2;
+        float2 v = splat2(0.f);
+        if (a.sec[s].heads > 0) {
+            const T* gm = static_cast<const T*>(a.sec[s].gamma);
+            v = make_float2(a.w_offset + (float)gm[c], a.w_offset + (float)gm[c + 1]);
+        }
+        sg[s][c / 2] = v;
+    }
+    __syncthreads();
 
     // Section row bases are formed once per token; a head is then one 64-bit multiply-add away.
     T* const qdata = static_cast<T*>(a.sec[0].data);
@@ -277,13 +313,12 @@ __global__ void __launch_bounds__(256, kNH <= 4 ? 3 : 2) head_rope_direct_kernel
         const int h0 = ps.r * CH;
         T* const qrow = qdata + t * qrs + li * 8;
         T* const krow = kdata + t * krs + li * 8;
+        auto head_ptr = [&](int h) -> T* { return h < hq ? qrow + h * qhs : krow + (h - hq) * khs; };
         typename Vec8<T>::Raw rp[kNH];
-        T* dst[kNH];
 #pragma unroll
         for (int j = 0; j < kNH; ++j) {
             const int h = h0 + j * HPW + hw;
-            dst[j] = h < hq ? qrow + h * qhs : krow + (h - hq) * khs;
-            if (h < htot) rp[j] = Vec8<T>::ldcs_raw(dst[j]);
+            if (h < htot) rp[j] = Vec8<T>::ldcs_raw(head_ptr(h));
         }
         const int64_t pos = base_pos + t;
         const bool pos_ok = half > 0 && pos >= 0 && pos < a.table_rows;
@@ -305,8 +340,8 @@ __global__ void __launch_bounds__(256, kNH <= 4 ? 3 : 2) head_rope_direct_kernel
 #pragma unroll
                 for (int i = 0; i < 4; ++i) p[i] = splat2(0.f);
             }
-            norm_rope_head<L, HD>(p, h < hq, g, a.eps, src, pos_ok && rot_lane, c2, s2);
-            if (h < htot) Vec8<T>::store2(dst[j], p);
+            norm_rope_head_sg<L, HD>(p, &sg[h < hq ? 0 : 1][li * 4], a.eps, src, pos_ok && rot_lane, c2, s2);
+            if (h < htot) Vec8<T>::store2(head_ptr(h), p);
         }
     }
 }
@@ -431,10 +466,10 @@ static int launch_head_rope_direct(const HeadRopeArgs& a, int hd, int htot, cons
                                    : (const void*)head_rope_direct_kernel<T, 256, kNH>;
     const int ch = kNH * (256 / hd);
     const int64_t warp_items = a.T * ((htot + ch - 1) / ch);
-    const int grid = persistent_grid(di, resident_ctas(kern, 256, 0), (warp_items + 7) / 8);
-    if (hd == 64) head_rope_direct_kernel<T, 64, kNH><<<grid, 256, 0, stream>>>(a);
-    else if (hd == 128) head_rope_direct_kernel<T, 128, kNH><<<grid, 256, 0, stream>>>(a);
-    else head_rope_direct_kernel<T, 256, kNH><<<grid, 256, 0, stream>>>(a);
+    const int grid = persistent_grid(di, resident_ctas(kern, 128, 0), (warp_items + 3) / 4);
+    if (hd == 64) head_rope_direct_kernel<T, 64, kNH><<<grid, 128, 0, stream>>>(a);
+    else if (hd == 128) head_rope_direct_kernel<T, 128, kNH><<<grid, 128, 0, stream>>>(a);
+    else head_rope_direct_kernel<T, 256, kNH><<<grid, 128, 0, stream>>>(a);
     return launch_status();
 }
 
@@ -503,10 +538,11 @@ static int launch_head_rope(const HeadSection& q, const HeadSection& k, const fl
         return launch_status();
     }
     if (variant(kFamHeadRope) != WZYB_VARIANT_RING) {
-        // Two instantiations: 6 heads per chunk at 2 CTAs/SM (no spill), or 4 heads per chunk capped
-        // at 3 CTAs/SM (more warps); a ctas_per_sm tuning of 3 or more selects the second.
-        if (tuning(kFamHeadRope).ctas_per_sm >= 3) return launch_head_rope_direct<T, 4>(a, hd, htot, di, stream);
-        return launch_head_rope_direct<T, 6>(a, hd, htot, di, stream);
+        // Two instantiations: 4 heads per chunk (80 registers, 24 warps/SM; default: equal at 262K
+        // tokens, 51% vs 47% of peak at 4096) or 6 heads per chunk (96 registers, 20 warps/SM), which
+        // a ctas_per_sm tuning of 2 selects.
+        if (tuning(kFamHeadRope).ctas_per_sm == 2) return launch_head_rope_direct<T, 6>(a, hd, htot, di, stream);
+        return launch_head_rope_direct<T, 4>(a, hd, htot, di, stream);
     }
 
     const int slots = htot * (hd / 8);

@@ -215,6 +215,95 @@ __global__ void __launch_bounds__(256, 2) norm_rows_direct_kernel(const NormRows
     }
 }
 
+// Async design: one warp per row as in the direct design, but the row's residual and x vectors are
+// staged in a lane-private shared-memory slot by cp.async (each lane copies and later reads back only
+// its own 16-byte chunks, so no barrier is needed) and read from there twice -- once for the sum of
+// squares, once for the outputs. Registers stay low, so at layer-sized T every row of the call is in
+// flight at once (kP = 1); kP = 2 double-buffers rows for long streams.
+template <typename TI, typename TO, int VPL, int kP>
+__global__ void __launch_bounds__(128) norm_rows_async_kernel(const NormRowsArgs a) {
+    constexpr int C = Vec8<TI>::kChunks;
+    constexpr int SLOT = 2 * VPL * C * 32;  // uint4: residual vectors, then x vectors
+    extern __shared__ __align__(16) uint4 sm_nr[];
+    const int lane = threadIdx.x & 31;
+    uint4* ring = sm_nr + (size_t)(threadIdx.x >> 5) * kP * SLOT;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const TI* __restrict__ x = static_cast<const TI*>(a.x);
+    TI* __restrict__ res = static_cast<TI*>(a.res);
+    const TI* __restrict__ w = static_cast<const TI*>(a.w);
+    TO* __restrict__ y = static_cast<TO*>(a.y);
+    const bool has_x = x != nullptr;
+    const int n = a.n;
+
+    auto issue = [&](int64_t u, int slot) {
+        if (u < a.units) {
+            const int64_t t = a.hc == 1 ? u : u / a.hc;
+            uint4* sl = ring + slot * SLOT;
+#pragma unroll
+            for (int k = 0; k < VPL; ++k) {
+                const int e = (k * 32 + lane) * 8;
+                if (e < n) {
+                    Vec8<TI>::stage_async(sl + k * C * 32, lane, res + u * n + e);
+                    if (has_x) Vec8<TI>::stage_async(sl + (VPL + k) * C * 32, lane, x + t * n + e);
+                }
+            }
+        }
+        cp_async_commit();  // one group per row, empty or not
+    };
+#pragma unroll
+    for (int j = 0; j < kP; ++j) issue(gwarp + j * nwarps, j);
+
+    for (int64_t j = 0;; ++j) {
+        const int64_t u = gwarp + j * nwarps;
+        if (u >= a.units) break;  // warp-uniform
+        const int slot = (int)(j % kP);
+        const uint4* sl = ring + slot * SLOT;
+        cp_async_wait<kP - 1>();
+        const int64_t t = a.hc == 1 ? u : u / a.hc;
+        const float2 gate = splat2((has_x && a.inj != nullptr) ? 2.0f / (1.0f + __expf(-a.inj[u] / (float)a.hc))
+                                                                : 1.0f);
+        auto residual_sum = [&](int k, float2 (&v)[4]) {  // v = residual + x * gate, from the slot
+            Vec8<TI>::unstage2(sl + k * C * 32, lane, v);
+            if (has_x) {
+                float2 xv[4];
+                Vec8<TI>::unstage2(sl + (VPL + k) * C * 32, lane, xv);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) v[i] = ffma2(xv[i], gate, v[i]);
+            }
+        };
+        float ss = 0.f;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            if ((k * 32 + lane) * 8 < n) {
+                float2 v[4];
+                residual_sum(k, v);
+                ss += sumsq8(v);
+            }
+        }
+        ss = group_sum<32>(ss);
+        const float2 sc = splat2(rsqrt_approx(ss / (float)n + a.eps));
+        const float2 woff = splat2(a.w_offset);
+        const TI* wrow = w + (u - t * a.hc) * n;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int e = (k * 32 + lane) * 8;
+            if (e < n) {
+                float2 v[4], g[4], o[4];
+                residual_sum(k, v);
+                Vec8<TI>::load_ro2(wrow + e, g);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[i] = fmul2(fmul2(v[i], sc), fadd2(woff, g[i]));  // (v*sc)*g
+                Vec8<TO>::store2(y + u * n + e, o);
+                if (has_x) Vec8<TI>::store2(res + u * n + e, v);
+            }
+        }
+        // Refill the slot: only this lane touches its chunks, and its reads precede the new copy.
+        issue(u + kP * nwarps, slot);
+    }
+    cp_async_wait<0>();
+}
+
 template <typename TI, typename TO>
 static int launch_norm_rows(const void* x, void* res, const void* w, const float* inj, void* y, int64_t T, int n,
                             int hc, float eps, float w_offset, cudaStream_t stream) {
@@ -247,6 +336,28 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
     // Direct design while a row fits the register budget (<= 12 fp16 or 6 fp32 vectors per lane).
     const int vpl_need = (n + 255) / 256;
     const int vpl_max = sizeof(TI) == 2 ? 12 : 6;
+    if (variant(kFamNorm) == WZYB_VARIANT_ASYNC && vpl_need <= (sizeof(TI) == 2 ? 8 : 4)) {
+        const int vpl = vpl_need <= 1 ? 1 : vpl_need <= 2 ? 2 : vpl_need <= 4 ? 4 : 8;
+        // one row in flight per warp when every row of the call fits in one round, else two
+        const int64_t one_round = (int64_t)di.sms * 28;
+        const int kp = a.units <= one_round ? 1 : 2;
+        const int smem = 4 * kp * 2 * vpl * Vec8<TI>::kChunks * 32 * 16;
+        const void* kern = nullptr;
+#define WZYB_NRA(V, P) \
+    if (vpl == V && kp == P) kern = (const void*)norm_rows_async_kernel<TI, TO, V, P>;
+        WZYB_NRA(1, 1) WZYB_NRA(1, 2) WZYB_NRA(2, 1) WZYB_NRA(2, 2)
+        WZYB_NRA(4, 1) WZYB_NRA(4, 2) WZYB_NRA(8, 1) WZYB_NRA(8, 2)
+#undef WZYB_NRA
+        rc = ensure_smem(kern, smem);
+        if (rc != WZYB_OK) return rc;
+        const int grid = persistent_grid(di, resident_ctas(kern, 128, smem), (a.units + 3) / 4);
+#define WZYB_NRA(V, P) \
+    if (vpl == V && kp == P) norm_rows_async_kernel<TI, TO, V, P><<<grid, 128, smem, stream>>>(a);
+        WZYB_NRA(1, 1) WZYB_NRA(1, 2) WZYB_NRA(2, 1) WZYB_NRA(2, 2)
+        WZYB_NRA(4, 1) WZYB_NRA(4, 2) WZYB_NRA(8, 1) WZYB_NRA(8, 2)
+#undef WZYB_NRA
+        return launch_status();
+    }
     if (variant(kFamNorm) != WZYB_VARIANT_RING && vpl_need <= vpl_max) {
         const void* kern = nullptr;
         int vpl = 0;

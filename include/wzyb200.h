@@ -83,6 +83,11 @@ int wzyb_gr_norm_f32(float* R, const float* w_norm, const float* bo_prev, const 
                      int64_t T, int n_embd, int hc, float eps, wzyb_stream_t stream);
 int wzyb_gr_norm_f32_f16(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev,
                          uint16_t* xn, int64_t T, int n_embd, int hc, float eps, wzyb_stream_t stream);
+/* ... with fused_gr_norm_multi's optional Q8_0 side output as well (src/wzy_kernels_v2.cuh:440-454):
+ * xq8 [T, hc, n_embd] int8 and xs8 [T, hc, n_embd/32] fp32; per 32-element group d = amax/127,
+ * q = rint(xn * 127/amax) clamped to [-127, 127]. n_embd % 32 == 0, n_embd <= 4096. */
+int wzyb_gr_norm_q8_f32(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, float* xn,
+                        int8_t* xq8, float* xs8, int64_t T, int n_embd, int hc, float eps, wzyb_stream_t stream);
 
 /* ============================================================================================
  * Per-head RMSNorm + partial NeoX RoPE, in place.
@@ -154,6 +159,10 @@ int wzyb_gdn_gated_norm_f32_f16(const float* o, const float* z, const float* gam
  * ========================================================================================== */
 int wzyb_swiglu_f16(const uint16_t* gate, const uint16_t* up, uint16_t* out, int64_t n, wzyb_stream_t stream);
 int wzyb_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, wzyb_stream_t stream);
+/* SwiGLU fused with Q8_0 quantisation and no activation output: silu_mul_quant32_multi
+ * (src/wzy_kernels_v2.cuh:1247-1279, launched at src/wzy_stage_v2.cuh:713). q32 [n] int8, s32 [n/32]
+ * fp32, n % 32 == 0; the activation uses the reference's expression (IEEE divide). */
+int wzyb_swiglu_q8_f32(const float* gate, const float* up, int8_t* q32, float* s32, int64_t n, wzyb_stream_t stream);
 int wzyb_swiglu_interleaved_f16(const uint16_t* gu, uint16_t* out, int64_t T, int nff, wzyb_stream_t stream);
 int wzyb_swiglu_interleaved_f32_f16(const float* gu, uint16_t* out, int64_t T, int nff, wzyb_stream_t stream);
 

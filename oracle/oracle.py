@@ -26,6 +26,8 @@ _SIGS = {
     "or_get_threads": (c_int, []),
     "or_add_rmsnorm_f16": (None, [P, P, P, P, c_int64, c_int, c_float, c_float]),
     "or_gr_norm_f32": (None, [P, P, P, P, P, P, c_int64, c_int, c_int, c_float]),
+    "or_gr_norm_q8_f32": (None, [P, P, P, P, P, P, P, c_int64, c_int, c_int, c_float]),
+    "or_swiglu_q8_f32": (None, [P, P, P, P, c_int64]),
     "or_head_norm_rope_f16": (
         None, [P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, c_int64, c_int64, c_int, c_float, c_float]),
     "or_head_norm_rope_f32": (
@@ -95,6 +97,28 @@ def gr_norm_f32(R, w, bo, inj, T, n, hc, eps=1e-6):
                          _p(np.ascontiguousarray(inj, np.float32)) if inj is not None else None,
                          _p(xn), _p(xh), T, n, hc, eps)
     return xn, xh, R_out
+
+
+def gr_norm_q8_f32(R, w, bo, inj, T, n, hc, eps=1e-6):
+    """fp32 hyper-connection norm with the Q8_0 side output; returns (xn, q8, s8, R_out)."""
+    R_out = np.array(R, dtype=np.float32, copy=True)
+    xn = np.empty((T * hc, n), dtype=np.float32)
+    q8 = np.empty((T * hc, n), dtype=np.int8)
+    s8 = np.empty((T * hc, n // 32), dtype=np.float32)
+    lib().or_gr_norm_q8_f32(_p(R_out), _p(np.ascontiguousarray(w, np.float32)),
+                            _p(np.ascontiguousarray(bo, np.float32)) if bo is not None else None,
+                            _p(np.ascontiguousarray(inj, np.float32)) if inj is not None else None,
+                            _p(xn), _p(q8), _p(s8), T, n, hc, eps)
+    return xn, q8, s8, R_out
+
+
+def swiglu_q8_f32(g, u):
+    g = np.ascontiguousarray(g, np.float32)
+    u = np.ascontiguousarray(u, np.float32)
+    q = np.empty(g.size, dtype=np.int8)
+    s = np.empty(g.size // 32, dtype=np.float32)
+    lib().or_swiglu_q8_f32(_p(g), _p(u), _p(q), _p(s), g.size)
+    return q, s
 
 
 def rope_table(rows, rot=64, theta=1e7):
@@ -190,6 +214,8 @@ def ref_lib() -> ctypes.CDLL:
         F = c_float
         sigs = {
             "ref_fused_gr_norm_multi": [P, P, P, P, P, I, I, I, F, P],
+            "ref_fused_gr_norm_multi_q8": [P, P, P, P, P, P, P, I, I, I, F, P],
+            "ref_silu_mul_quant32_multi": [P, P, P, P, I, P],
             "ref_pf_gr_norm_fp16": [P, P, P, P, P, I, I, I, F, P],
             "ref_gr_write_multi": [P, P, P, I, I, I, P],
             "ref_fused_head_norm_rope_multi": [P, P, P, P, P, I, I, I, I, I, F, P],

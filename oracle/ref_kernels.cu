@@ -19,6 +19,21 @@ int ref_fused_gr_norm_multi(float* R, const float* w_norm, const float* bo_prev,
     return (int)cudaGetLastError();
 }
 
+// fused_gr_norm_multi with its Q8_0 side output (xq8 / xs8), as gr_read_fused passes them.
+int ref_fused_gr_norm_multi_q8(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, float* xn,
+                               signed char* xq8, float* xs8, int T, int n_embd, int hc, float eps, cudaStream_t s) {
+    fused_gr_norm_multi<<<dim3(hc, T), 256, 0, s>>>(R, w_norm, bo_prev, inj_prev, xn, n_embd, hc, eps, xq8, xs8);
+    return (int)cudaGetLastError();
+}
+
+// silu_mul_quant32_multi (src/wzy_kernels_v2.cuh:1247-1279), launched as at src/wzy_stage_v2.cuh:713:
+// one thread per 32-element group.
+int ref_silu_mul_quant32_multi(const float* gate, const float* up, signed char* q32, float* s32, int total_g32,
+                               cudaStream_t s) {
+    silu_mul_quant32_multi<<<(total_g32 + 127) / 128, 128, 0, s>>>(gate, up, q32, s32, total_g32);
+    return (int)cudaGetLastError();
+}
+
 // pf_gr_norm_fp16 (src/wzy_qsa_wmma.cuh:197-232), launched as at src/wzy_prefill_tc.cuh:697.
 int ref_pf_gr_norm_fp16(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, __half* xn, int T,
                         int n_embd, int hc, float eps, cudaStream_t s) {

@@ -133,6 +133,36 @@ void or_gr_norm_f32(float* R, const float* w, const float* bo, const float* inj,
     }
 }
 
+/* Q8_0 of one 32-element group: the xq8 path of fused_gr_norm_multi (src/wzy_kernels_v2.cuh:440-454)  */
+/* and silu_mul_quant32_multi (:1247-1279): d = amax/127; q = rint(v * 127/amax) in [-127, 127].     */
+static void q8_group(const float* v, int8_t* q, float* s) {
+    float am = 0.f;
+    for (int i = 0; i < 32; ++i) am = fmaxf(am, fabsf(v[i]));
+    const float d = am / 127.0f;
+    const float inv = d > 0.f ? 127.0f / am : 0.f;
+    for (int i = 0; i < 32; ++i) {
+        int qi = (int)rintf(v[i] * inv);
+        q[i] = (int8_t)(qi < -127 ? -127 : (qi > 127 ? 127 : qi));
+    }
+    *s = d;
+}
+
+void or_gr_norm_q8_f32(float* R, const float* w, const float* bo, const float* inj, float* xn, int8_t* q8,
+                       float* s8, int64_t T, int n, int hc, float eps) {
+    or_gr_norm_f32(R, w, bo, inj, xn, NULL, T, n, hc, eps);
+#pragma omp parallel for schedule(static)
+    for (int64_t g = 0; g < T * hc * (int64_t)n / 32; ++g) q8_group(xn + g * 32, q8 + g * 32, s8 + g);
+}
+
+void or_swiglu_q8_f32(const float* g, const float* u, int8_t* q, float* s, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t grp = 0; grp < n / 32; ++grp) {
+        float v[32];
+        for (int i = 0; i < 32; ++i) v[i] = (g[grp * 32 + i] / sigmoid_den(g[grp * 32 + i])) * u[grp * 32 + i];
+        q8_group(v, q + grp * 32, s + grp);
+    }
+}
+
 /* ------------------------------------------------------------------------------------------- */
 /* per-head RMSNorm + partial NeoX RoPE: fused_head_norm_rope_multi (src/wzy_qsa_256k.cuh:50-84) */
 /*   p *= rsqrt(sum(p^2)/hd + eps) * gamma;  (a, d) = (p[i], p[i+R/2])                          */

@@ -32,6 +32,11 @@ void or_add_rmsnorm_f16(const uint16_t* x, uint16_t* res, const uint16_t* w, uin
 /* hyper-connection form, fp32 I/O (xn_h16 != NULL additionally writes an fp16 copy of xn) */
 void or_gr_norm_f32(float* R, const float* w, const float* bo, const float* inj, float* xn, uint16_t* xn_h16,
                     int64_t T, int n, int hc, float eps);
+/* ... plus the Q8_0 side output of xn (per 32 elements: int8 codes, fp32 scale) */
+void or_gr_norm_q8_f32(float* R, const float* w, const float* bo, const float* inj, float* xn, int8_t* q8,
+                       float* s8, int64_t T, int n, int hc, float eps);
+/* SwiGLU fused with Q8_0 quantisation (no activation output) */
+void or_swiglu_q8_f32(const float* g, const float* u, int8_t* q, float* s, int64_t n);
 /* per-head RMSNorm + partial NeoX RoPE, in place */
 void or_head_norm_rope_f16(uint16_t* data, const uint16_t* gamma, const float* cos_tab, const float* sin_tab,
                            int64_t table_rows, int64_t base_pos, int64_t T, int heads, int hd, int64_t head_stride,

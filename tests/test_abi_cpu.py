@@ -63,6 +63,16 @@ def test_argument_validation_before_any_cuda_call(wz):
     assert L.wzyb_ple_gather_f16(tables, 2, 1 << 20, 128, A16, 4, None, 248044, 0, A16, NULL) == wz.ERR_NULL
     assert L.wzyb_ple_gather_f16(tables, 33, 1 << 20, 128, A16, 4, None, 248044, 0, A16, NULL) == wz.ERR_SHAPE
     assert L.wzyb_ple_gather_f16(tables, 1, 1 << 20, 128, A16, 4, None, 248044, 5, A16, NULL) == wz.ERR_VALUE
+    # Q8_0 side outputs: whole 32-wide groups, n_embd <= 4096, every buffer 16-byte aligned
+    assert L.wzyb_gr_norm_q8_f32(A16, A16, A16, A16, A16, NULL, A16, 4, 2560, 4, 1e-6, NULL) == wz.ERR_NULL
+    assert L.wzyb_gr_norm_q8_f32(A16, A16, A16, A16, A16, A16, A16, 4, 2568, 4, 1e-6, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_gr_norm_q8_f32(A16, A16, A16, A16, A16, A16, A16, 4, 8192, 4, 1e-6, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_gr_norm_q8_f32(A16, A16, A16, A16, A16, A8, A16, 4, 2560, 4, 1e-6, NULL) == wz.ERR_ALIGN
+    assert L.wzyb_gr_norm_q8_f32(A16, A16, A16, A16, A16, A16, A16, 0, 2560, 4, 1e-6, NULL) == wz.OK
+    assert L.wzyb_swiglu_q8_f32(A16, A16, NULL, A16, 64, NULL) == wz.ERR_NULL
+    assert L.wzyb_swiglu_q8_f32(A16, A16, A16, A16, 48, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_swiglu_q8_f32(A16, A16, A16, A8, 64, NULL) == wz.ERR_ALIGN
+    assert L.wzyb_swiglu_q8_f32(A16, A16, A16, A16, 0, NULL) == wz.OK
     # empty work is a no-op that succeeds without a device
     assert L.wzyb_swiglu_f16(A16, A16, A16, 0, NULL) == wz.OK
     assert L.wzyb_add_rmsnorm_f16(A16, A16, A16, A16, 0, 2048, 1e-6, 1.0, NULL) == wz.OK

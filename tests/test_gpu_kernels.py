@@ -350,3 +350,43 @@ def test_device_rope_table_close_to_host(wz, orc):
     # the values agree to ~1e-10 absolute (near a zero crossing that is many fp32 ulp of a tiny value)
     assert np.abs(gc - c).max() <= 1.2e-7 and np.abs(gs - s).max() <= 1.2e-7  # <= 2 fp32 ulp at 1.0
     assert (gc == c).mean() > 0.999 and (gs == s).mean() > 0.999
+
+
+# ---------------------------------------------------------------------------------------------
+# Q8_0 side outputs (decode path)
+# ---------------------------------------------------------------------------------------------
+def _q8_close(q_got, s_got, q_want, s_want, what):
+    dq = np.abs(q_got.astype(np.int32) - q_want.astype(np.int32))
+    # fp32 inputs to the rounding differ by a few ulp (reduction order, exp): a code may sit on the
+    # other side of a .5 boundary, never further
+    assert dq.max() <= 1 and (dq > 0).mean() < 1e-3, f"{what}: max {dq.max()} frac {(dq > 0).mean()}"
+    np.testing.assert_allclose(s_got, s_want, rtol=4e-6, atol=0)
+
+
+@pytest.mark.parametrize("T,n,hc", [(1, 2560, 4), (8, 2560, 4), (5, 2048, 1), (3, 96, 2)])
+def test_gr_norm_q8_f32(wz, orc, T, n, hc):
+    r = rng(T * n + hc)
+    R = r.standard_normal((T * hc, n)).astype(np.float32)
+    bo = r.standard_normal((T, n)).astype(np.float32)
+    inj = r.standard_normal(T * hc).astype(np.float32)
+    w = (1 + 0.02 * r.standard_normal((hc, n))).astype(np.float32)
+    xn_ref, q_ref, s_ref, R_ref = orc.gr_norm_q8_f32(R, w, bo, inj, T, n, hc)
+    dR, dxn = dev(R), torch.empty((T * hc, n), dtype=torch.float32, device=DEV)
+    dq = torch.empty((T * hc, n), dtype=torch.int8, device=DEV)
+    ds = torch.empty((T * hc, n // 32), dtype=torch.float32, device=DEV)
+    wz.gr_norm_q8_f32(dR, dev(w), dev(bo), dev(inj), dxn, dq, ds, T, n, hc)
+    np.testing.assert_allclose(host(dR), R_ref, rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(host(dxn), xn_ref, rtol=2e-6, atol=2e-6)
+    _q8_close(host(dq), host(ds), q_ref, s_ref, "gr_norm q8")
+
+
+@pytest.mark.parametrize("n", [32, 640 * 8, 45056 * 512])
+def test_swiglu_q8_f32(wz, orc, n):
+    r = rng(n % 1000)
+    g = (2 * r.standard_normal(n)).astype(np.float32)
+    u = r.standard_normal(n).astype(np.float32)
+    q_ref, s_ref = orc.swiglu_q8_f32(g, u)
+    dq = torch.empty(n, dtype=torch.int8, device=DEV)
+    ds = torch.empty(n // 32, dtype=torch.float32, device=DEV)
+    wz.swiglu_q8_f32(dev(g), dev(u), dq, ds)
+    _q8_close(host(dq), host(ds), q_ref, s_ref, "swiglu q8")

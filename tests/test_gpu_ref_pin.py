@@ -203,3 +203,38 @@ def ctypes_dims(ref):
     a, b = ctypes.c_int(), ctypes.c_int()
     ref.ref_dims(ctypes.byref(a), ctypes.byref(b))
     return a.value, b.value
+
+
+def test_pin_q8_side_outputs(ref, orc, wz):
+    """fused_gr_norm_multi's xq8/xs8 and silu_mul_quant32_multi at the reference's decode shapes."""
+    r = np.random.default_rng(208)
+    T, n, hc = 8, 2560, 4
+    R = r.standard_normal((T * hc, n)).astype(np.float32)
+    bo = r.standard_normal((T, n)).astype(np.float32)
+    inj = r.standard_normal(T * hc).astype(np.float32)
+    w = (1 + 0.02 * r.standard_normal((hc, n))).astype(np.float32)
+    dR, dxn = dev(R), torch.empty((T * hc, n), dtype=torch.float32, device=DEV)
+    dq = torch.empty((T * hc, n), dtype=torch.int8, device=DEV)
+    ds = torch.empty((T * hc, n // 32), dtype=torch.float32, device=DEV)
+    assert ref.ref_fused_gr_norm_multi_q8(dR.data_ptr(), dev(w).data_ptr(), dev(bo).data_ptr(), dev(inj).data_ptr(),
+                                          dxn.data_ptr(), dq.data_ptr(), ds.data_ptr(), T, n, hc, 1e-6, sp()) == 0
+    rq, rs = host(dq), host(ds)
+    mq = torch.empty_like(dq)
+    ms = torch.empty_like(ds)
+    wz.gr_norm_q8_f32(dev(R), dev(w), dev(bo), dev(inj), torch.empty_like(dxn), mq, ms, T, n, hc)
+    d = np.abs(host(mq).astype(np.int32) - rq.astype(np.int32))
+    assert d.max() <= 1 and (d > 0).mean() < 1e-3
+    np.testing.assert_allclose(host(ms), rs, rtol=4e-6)
+    # SwiGLU + Q8: the same expression on the same inputs -> identical codes and scales
+    nff = 640
+    g = (2 * r.standard_normal(nff * T)).astype(np.float32)
+    u = r.standard_normal(nff * T).astype(np.float32)
+    q32 = torch.empty(nff * T, dtype=torch.int8, device=DEV)
+    s32 = torch.empty(nff * T // 32, dtype=torch.float32, device=DEV)
+    dg, du = dev(g), dev(u)
+    assert ref.ref_silu_mul_quant32_multi(dg.data_ptr(), du.data_ptr(), q32.data_ptr(), s32.data_ptr(),
+                                          nff * T // 32, sp()) == 0
+    mq2, ms2 = torch.empty_like(q32), torch.empty_like(s32)
+    wz.swiglu_q8_f32(dg, du, mq2, ms2)
+    assert np.array_equal(host(mq2), host(q32))
+    assert np.array_equal(host(ms2).view(np.uint32), host(s32).view(np.uint32))

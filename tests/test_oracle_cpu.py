@@ -178,3 +178,32 @@ def test_ulp_helper():
     a = np.array([1.0, -0.0, 0.0, 65504], dtype=np.float16)
     b = np.array([1.0009765625, 0.0, 5.96e-08, 65504], dtype=np.float16)
     assert list(f16_ulp_distance(a, b)) == [1, 0, 1, 0]
+
+
+def _np_q8(v):
+    """Q8_0 per 32-element group restated in numpy (round half to even, clamp to +-127)."""
+    g = v.reshape(-1, 32).astype(np.float32)
+    am = np.abs(g).max(axis=1)
+    d = (am / np.float32(127.0)).astype(np.float32)
+    inv = np.where(d > 0, np.float32(127.0) / np.where(am > 0, am, 1), 0).astype(np.float32)
+    q = np.clip(np.rint(g * inv[:, None]), -127, 127).astype(np.int8)
+    return q.reshape(v.shape), d
+
+
+def test_q8_paths_against_numpy(orc):
+    r = np.random.default_rng(31)
+    T, n, hc = 3, 256, 4
+    R = r.standard_normal((T * hc, n)).astype(np.float32)
+    bo = r.standard_normal((T, n)).astype(np.float32)
+    inj = r.standard_normal(T * hc).astype(np.float32)
+    w = (1 + 0.02 * r.standard_normal((hc, n))).astype(np.float32)
+    xn, q8, s8, _ = orc.gr_norm_q8_f32(R, w, bo, inj, T, n, hc)
+    q_np, d_np = _np_q8(xn)
+    assert np.array_equal(q8, q_np) and np.array_equal(s8.reshape(-1), d_np)
+    g = (3 * r.standard_normal(32 * 50)).astype(np.float32)
+    u = r.standard_normal(32 * 50).astype(np.float32)
+    g[:32] = 0.0  # an all-zero group: scale 0, codes 0
+    q, s = orc.swiglu_q8_f32(g, u)
+    q_np, d_np = _np_q8(orc.swiglu(g, u))
+    assert np.array_equal(q, q_np) and np.array_equal(s, d_np)
+    assert s[0] == 0 and not q[:32].any()

@@ -27,6 +27,8 @@ struct NormRowsArgs {
     int stages;
     uint32_t row_bytes;
     uint32_t stage_bytes;
+    signed char* q8;  // optional Q8_0 codes of xn [T*hc, n] (async design only)
+    float* s8;        // its per-32-element scales [T*hc, n/32]
 };
 
 template <typename TI, typename TO, int VPT>
@@ -220,7 +222,7 @@ __global__ void __launch_bounds__(256, 2) norm_rows_direct_kernel(const NormRows
 // its own 16-byte chunks, so no barrier is needed) and read from there twice -- once for the sum of
 // squares, once for the outputs. Registers stay low, so at layer-sized T every row of the call is in
 // flight at once (kP = 1); kP = 2 double-buffers rows for long streams.
-template <typename TI, typename TO, int VPL, int kP>
+template <typename TI, typename TO, int VPL, int kP, bool Q8 = false>
 __global__ void __launch_bounds__(128) norm_rows_async_kernel(const NormRowsArgs a) {
     constexpr int C = Vec8<TI>::kChunks;
     constexpr int SLOT = 2 * VPL * C * 32;  // uint4: residual vectors, then x vectors
@@ -288,14 +290,19 @@ __global__ void __launch_bounds__(128) norm_rows_async_kernel(const NormRowsArgs
 #pragma unroll
         for (int k = 0; k < VPL; ++k) {
             const int e = (k * 32 + lane) * 8;
+            float2 o[4] = {};
             if (e < n) {
-                float2 v[4], g[4], o[4];
+                float2 v[4], g[4];
                 residual_sum(k, v);
                 Vec8<TI>::load_ro2(wrow + e, g);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) o[i] = fmul2(fmul2(v[i], sc), fadd2(woff, g[i]));  // (v*sc)*g
                 Vec8<TO>::store2(y + u * n + e, o);
                 if (has_x) Vec8<TI>::store2(res + u * n + e, v);
+            }
+            if (Q8) {  // all lanes: the group max is a shuffle
+                const float yo[8] = {o[0].x, o[0].y, o[1].x, o[1].y, o[2].x, o[2].y, o[3].x, o[3].y};
+                q8_group_store(yo, e < n, a.q8 + u * n + e, a.s8 + ((u * n + e) >> 5), lane);
             }
         }
         // Refill the slot: only this lane touches its chunks, and its reads precede the new copy.
@@ -332,6 +339,8 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
     a.w_offset = w_offset;
     a.row_bytes = (uint32_t)(n * sizeof(TI));
     a.stage_bytes = a.row_bytes * (x ? 2u : 1u);
+    a.q8 = nullptr;
+    a.s8 = nullptr;
 
     // Direct design while a row fits the register budget (<= 12 fp16 or 6 fp32 vectors per lane).
     const int vpl_need = (n + 255) / 256;
@@ -417,9 +426,63 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
     return launch_status();
 }
 
+// Residual fold + norm with the Q8_0 side output: the async design (rows staged in shared memory),
+// one row in flight per warp, any n up to 16 fp32 vectors per lane (n <= 4096).
+template <typename TI, typename TO>
+static int launch_norm_rows_q8(const void* x, void* res, const void* w, const float* inj, void* y, signed char* q8,
+                               float* s8, int64_t T, int n, int hc, float eps, cudaStream_t stream) {
+    if (res == nullptr || w == nullptr || y == nullptr || q8 == nullptr || s8 == nullptr) return WZYB_ERR_NULL;
+    if (T < 0 || T > (int64_t(1) << 40) || n < 32 || n > 4096 || (n % 32) != 0 || hc < 1 || hc > 64)
+        return WZYB_ERR_SHAPE;
+    if (!aligned16(res) || !aligned16(w) || !aligned16(y) || (x && !aligned16(x)) || !aligned16(q8) ||
+        !aligned16(s8))
+        return WZYB_ERR_ALIGN;
+    if (T == 0) return WZYB_OK;
+    DeviceInfo di;
+    int rc = device_info(&di);
+    if (rc != WZYB_OK) return rc;
+    NormRowsArgs a;
+    a.x = x;
+    a.res = res;
+    a.w = w;
+    a.inj = x ? inj : nullptr;
+    a.y = y;
+    a.units = T * hc;
+    a.n = n;
+    a.hc = hc;
+    a.eps = eps;
+    a.w_offset = 0.0f;
+    a.stages = 0;
+    a.row_bytes = a.stage_bytes = 0;
+    a.q8 = q8;
+    a.s8 = s8;
+    const int vpl_need = (n + 255) / 256;
+    const int vpl = vpl_need <= 1 ? 1 : vpl_need <= 2 ? 2 : vpl_need <= 4 ? 4 : vpl_need <= 8 ? 8 : vpl_need <= 12 ? 12 : 16;
+    const int smem = 4 * 2 * vpl * Vec8<TI>::kChunks * 32 * 16;
+    const void* kern = nullptr;
+#define WZYB_NRQ(V) \
+    if (vpl == V) kern = (const void*)norm_rows_async_kernel<TI, TO, V, 1, true>;
+    WZYB_NRQ(1) WZYB_NRQ(2) WZYB_NRQ(4) WZYB_NRQ(8) WZYB_NRQ(12) WZYB_NRQ(16)
+#undef WZYB_NRQ
+    rc = ensure_smem(kern, smem);
+    if (rc != WZYB_OK) return rc;
+    const int grid = persistent_grid(di, resident_ctas(kern, 128, smem), (a.units + 3) / 4);
+#define WZYB_NRQ(V) \
+    if (vpl == V) norm_rows_async_kernel<TI, TO, V, 1, true><<<grid, 128, smem, stream>>>(a);
+    WZYB_NRQ(1) WZYB_NRQ(2) WZYB_NRQ(4) WZYB_NRQ(8) WZYB_NRQ(12) WZYB_NRQ(16)
+#undef WZYB_NRQ
+    return launch_status();
+}
+
 }  // namespace wzyb
 
 extern "C" {
+
+int wzyb_gr_norm_q8_f32(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, float* xn,
+                        int8_t* xq8, float* xs8, int64_t T, int n_embd, int hc, float eps, wzyb_stream_t stream) {
+    return wzyb::launch_norm_rows_q8<float, float>(bo_prev, R, w_norm, inj_prev, xn, (signed char*)xq8, xs8, T,
+                                                   n_embd, hc, eps, (cudaStream_t)stream);
+}
 
 int wzyb_add_rmsnorm_f16(const uint16_t* x, uint16_t* residual, const uint16_t* weight, uint16_t* y, int64_t T,
                          int hidden, float eps, float w_offset, wzyb_stream_t stream) {

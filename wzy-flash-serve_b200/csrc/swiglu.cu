@@ -85,6 +85,33 @@ __global__ void __launch_bounds__(kSwigluThreads) swiglu_kernel(const TI* __rest
     }
 }
 
+// SwiGLU fused with Q8_0 quantisation, no activation output: silu_mul_quant32_multi
+// (src/wzy_kernels_v2.cuh:1247-1279). A warp covers 32 consecutive 8-element vectors (8 groups of
+// 32); each group's max is two shuffles over its 4 lanes. The activation uses the reference's own
+// expression, (g / (1 + __expf(-g))) * u with the IEEE divide, so on the same inputs the codes and
+// scales come out as the reference kernel's.
+template <typename TI>
+__global__ void __launch_bounds__(256) swiglu_q8_kernel(const TI* __restrict__ gate, const TI* __restrict__ up,
+                                                        signed char* __restrict__ q, float* __restrict__ s,
+                                                        int64_t nvec) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; base < nvec;
+         base += nwarps * 32) {
+        const int64_t v = base + lane;
+        const bool act = v < nvec;
+        float o[8] = {};
+        if (act) {
+            float g[8], u[8];
+            Vec8<TI>::load_stream(gate + v * 8, g);
+            Vec8<TI>::load_stream(up + v * 8, u);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = (g[e] / (1.0f + __expf(-g[e]))) * u[e];
+        }
+        q8_group_store(o, act, q + v * 8, s + (v >> 2), lane);
+    }
+}
+
 template <typename TI, typename TO, bool INTERLEAVED>
 static int launch_swiglu(const TI* gate, const TI* up, TO* out, int64_t nvec, int64_t vpr, int64_t nff,
                          cudaStream_t stream) {
@@ -123,6 +150,21 @@ int wzyb_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, w
     if (n < 0 || (n % 8) != 0) return WZYB_ERR_SHAPE;
     if (!wzyb::aligned16(gate) || !wzyb::aligned16(up) || !wzyb::aligned16(out)) return WZYB_ERR_ALIGN;
     return wzyb::launch_swiglu<float, float, false>(gate, up, out, n / 8, 0, 0, (cudaStream_t)stream);
+}
+
+int wzyb_swiglu_q8_f32(const float* gate, const float* up, int8_t* q32, float* s32, int64_t n, wzyb_stream_t stream) {
+    if (!gate || !up || !q32 || !s32) return WZYB_ERR_NULL;
+    if (n < 0 || (n % 32) != 0) return WZYB_ERR_SHAPE;
+    if (!wzyb::aligned16(gate) || !wzyb::aligned16(up) || !wzyb::aligned16(q32) || !wzyb::aligned16(s32))
+        return WZYB_ERR_ALIGN;
+    if (n == 0) return WZYB_OK;
+    wzyb::DeviceInfo di;
+    const int rc = wzyb::device_info(&di);
+    if (rc != WZYB_OK) return rc;
+    const int64_t nvec = n / 8;
+    const int grid = wzyb::persistent_grid(di, 8, (nvec + 255) / 256);
+    wzyb::swiglu_q8_kernel<float><<<grid, 256, 0, (cudaStream_t)stream>>>(gate, up, (signed char*)q32, s32, nvec);
+    return wzyb::launch_status();
 }
 
 int wzyb_swiglu_interleaved_f16(const uint16_t* gu, uint16_t* out, int64_t T, int nff, wzyb_stream_t stream) {

@@ -89,6 +89,8 @@ _SIGS = {
     "wzyb_add_rmsnorm_f16": (c_int, [P, P, P, P, c_int64, c_int, c_float, c_float, S]),
     "wzyb_gr_norm_f32": (c_int, [P, P, P, P, P, c_int64, c_int, c_int, c_float, S]),
     "wzyb_gr_norm_f32_f16": (c_int, [P, P, P, P, P, c_int64, c_int, c_int, c_float, S]),
+    "wzyb_gr_norm_q8_f32": (c_int, [P, P, P, P, P, P, P, c_int64, c_int, c_int, c_float, S]),
+    "wzyb_swiglu_q8_f32": (c_int, [P, P, P, P, c_int64, S]),
     "wzyb_head_norm_rope_f16": (
         c_int,
         [P, P, P, P, c_int64, P, c_int64, c_int64, c_int, c_int, c_int64, c_int64, c_int, c_float, c_float, S],
@@ -185,6 +187,15 @@ def add_rmsnorm_f16(x, residual, weight, y, eps=1e-6, w_offset=1.0, stream=None)
 def gr_norm_f32(R, w_norm, bo_prev, inj_prev, xn, T, n_embd, hc, eps=1e-6, stream=None):
     fn = "wzyb_gr_norm_f32" if xn.element_size() == 4 else "wzyb_gr_norm_f32_f16"
     call(fn, _ptr(R), _ptr(w_norm), _ptr(bo_prev), _ptr(inj_prev), _ptr(xn), T, n_embd, hc, eps, _stream(stream))
+
+
+def gr_norm_q8_f32(R, w_norm, bo_prev, inj_prev, xn, xq8, xs8, T, n_embd, hc, eps=1e-6, stream=None):
+    call("wzyb_gr_norm_q8_f32", _ptr(R), _ptr(w_norm), _ptr(bo_prev), _ptr(inj_prev), _ptr(xn), _ptr(xq8), _ptr(xs8),
+         T, n_embd, hc, eps, _stream(stream))
+
+
+def swiglu_q8_f32(gate, up, q32, s32, stream=None):
+    call("wzyb_swiglu_q8_f32", _ptr(gate), _ptr(up), _ptr(q32), _ptr(s32), gate.numel(), _stream(stream))
 
 
 def head_norm_rope(data, gamma, cos_tab, sin_tab, T, heads, head_dim, head_stride, row_stride, rot_dims=64,

@@ -263,6 +263,32 @@ def measure_kernels_4096(wz, torch, dev, peak, reps=60):
         "embed_gather": (lambda s: wz.embed_gather_f16(table, ids, emb, stream=s), T * HIDDEN * 2 * 2 + T * 4),
         "ple_gather": (lambda s: wz.ple_gather_f16(ple_tabs, ids, ple, stream=s), T * 16 * 256 + T * 2048 * 2 + T * 4),
     }
+    # the reference model's 4-stream residual (n_embd 2560): gated write, stream mixing, and the
+    # Q8_0-quantising norm and SwiGLU, at the same 4096 tokens
+    NE, HC = 2560, 4
+    R = torch.randn((T * HC, NE), generator=gen, device=dev)
+    blk = torch.randn((T, NE), generator=gen, device=dev)
+    inj = torch.randn((T * HC,), generator=gen, device=dev)
+    wn = 1 + 0.02 * torch.randn((HC, NE), generator=gen, device=dev)
+    xn16 = torch.randn((T, HC, NE), generator=gen, device=dev).half()
+    gg16 = torch.randn((T, HC, NE), generator=gen, device=dev).half()
+    mx, mx16 = torch.empty((T, NE), device=dev), torch.empty((T, NE), dtype=torch.float16, device=dev)
+    xn32 = torch.empty((T * HC, NE), device=dev)
+    xq8 = torch.empty((T * HC, NE), dtype=torch.int8, device=dev)
+    xs8 = torch.empty((T * HC, NE // 32), device=dev)
+    nq = T * EXPERT_ROWS * FFN
+    g32, u32 = torch.randn(nq, generator=gen, device=dev), torch.randn(nq, generator=gen, device=dev)
+    q32, s32 = torch.empty(nq, dtype=torch.int8, device=dev), torch.empty(nq // 32, device=dev)
+    rows = T * HC * NE
+    extra.update({
+        "gr_write_hc4": (lambda s: wz.gr_write_f32(R, blk, inj, T, NE, HC, stream=s), rows * 8 + T * NE * 4 + T * HC * 4),
+        "hc_mix_hc4": (lambda s: wz.hc_mix(xn16, gg16, mx, mx16, T, NE, HC, stream=s), rows * 4 + T * NE * 6),
+        "gr_norm_hc4": (lambda s: wz.gr_norm_f32(R, wn, blk, inj, xn32, T, NE, HC, stream=s),
+                        rows * (8 + 4) + T * NE * 4 + T * HC * 4 + HC * NE * 4),
+        "gr_norm_q8_hc4": (lambda s: wz.gr_norm_q8_f32(R, wn, blk, inj, xn32, xq8, xs8, T, NE, HC, stream=s),
+                           rows * (8 + 4 + 1) + rows // 8 + T * NE * 4 + T * HC * 4 + HC * NE * 4),
+        "swiglu_q8": (lambda s: wz.swiglu_q8_f32(g32, u32, q32, s32, stream=s), nq * (8 + 1) + nq // 8),
+    })
     s = torch.cuda.current_stream()
 
     def timed(fn):
@@ -303,7 +329,7 @@ def measure_kernels_4096(wz, torch, dev, peak, reps=60):
         res[name] = {"us": round(us, 2), "bytes": int(nbytes), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
                      "frac_of_8tbs": round(gbs / NOMINAL_HBM_GBS, 4), "copy_us": round(copy_us, 2),
                      "frac_of_copy": round(copy_us / us, 4)}
-    del table, ple_tabs, flush, flush_r
+    del table, ple_tabs, flush, flush_r, R, blk, xn16, gg16, xn32, g32, u32
     return res
 
 
@@ -368,7 +394,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-kernels", action="store_true")
-    ap.add_argument("--variant", default="auto", choices=["auto", "ring", "direct", "async"],
+    ap.add_argument("--variant", default="auto", choices=["auto", "ring", "direct", "async", "wide"],
                     help="kernel design of the norm families (A/B measurement)")
     ap.add_argument("--tune", action="append", default=[],
                     help="FAMILY:CTAS_PER_SM:STAGES launch tuning (wzyb_set_launch_tuning), repeatable")
@@ -421,7 +447,7 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
     wz.check("wzyb_prepare_device", wz.lib().wzyb_prepare_device())
     var = {"auto": wz.VARIANT_AUTO, "ring": wz.VARIANT_RING, "direct": wz.VARIANT_DIRECT,
-           "async": wz.VARIANT_ASYNC}[args.variant]
+           "async": wz.VARIANT_ASYNC, "wide": wz.VARIANT_WIDE}[args.variant]
     for fam in (wz.FAM_NORM, wz.FAM_HEAD_ROPE, wz.FAM_GDN):
         wz.set_kernel_variant(fam, var)
     for spec in args.tune:

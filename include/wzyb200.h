@@ -85,9 +85,31 @@ int wzyb_gr_norm_f32_f16(float* R, const float* w_norm, const float* bo_prev, co
                          uint16_t* xn, int64_t T, int n_embd, int hc, float eps, wzyb_stream_t stream);
 /* ... with fused_gr_norm_multi's optional Q8_0 side output as well (src/wzy_kernels_v2.cuh:440-454):
  * xq8 [T, hc, n_embd] int8 and xs8 [T, hc, n_embd/32] fp32; per 32-element group d = amax/127,
- * q = rint(xn * 127/amax) clamped to [-127, 127]. n_embd % 32 == 0, n_embd <= 4096. */
+ * q = rint(xn * 127/amax) clamped to [-127, 127]. n_embd % 32 == 0, n_embd <= 16384. */
 int wzyb_gr_norm_q8_f32(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, float* xn,
                         int8_t* xq8, float* xs8, int64_t T, int n_embd, int hc, float eps, wzyb_stream_t stream);
+
+/* ============================================================================================
+ * Multi-stream (hyper-connection) residual outside the norm. n_embd % 8 == 0, 1 <= hc <= 64.
+ * ========================================================================================== */
+/* R[t,c,:] += blk[t,:] * 2*sigmoid(inj[t,c]/hc)  (gate 1.0 when inj == NULL), fp32, in place.
+ * R [T, hc, n_embd], blk [T, n_embd], inj [T, hc]. Replaces gr_write_multi
+ * (src/wzy_kernels_v2.cuh:813-828; launched at src/wzy_stage_v2.cuh:585/693/800 and
+ * src/wzy_prefill_tc.cuh:810/926/1054). */
+int wzyb_gr_write_f32(float* R, const float* blk, const float* inj, int64_t T, int n_embd, int hc,
+                      wzyb_stream_t stream);
+/* Stream mixing  mixed[t,:] = (1/hc) * sum_c xn[t,c,:] / (1 + exp(-gg[t,c,:])).
+ * xn, gg [T, hc, n_embd]; mixed [T, n_embd] fp32 and/or mixed_f16 [T, n_embd] fp16 (either may be
+ * NULL, not both). _f16: pf_gr_up_mean_fp16 (src/wzy_qsa_wmma.cuh:234-253, launched at
+ * src/wzy_prefill_tc.cuh:712), whose 4 streams give the scale 0.25. _f32: gr_up_gate_mean_pf_kernel
+ * (src/wzy_prefill_tc.cuh:37-51). */
+int wzyb_hc_mix_f16(const uint16_t* xn, const uint16_t* gg, float* mixed, uint16_t* mixed_f16, int64_t T,
+                    int n_embd, int hc, wzyb_stream_t stream);
+int wzyb_hc_mix_f32(const float* xn, const float* gg, float* mixed, int64_t T, int n_embd, int hc,
+                    wzyb_stream_t stream);
+/* out = fp16(silu(lo * scale)), n % 8 == 0: silu_div_hc_to_fp16_kernel (src/wzy_prefill_tc.cuh:24-35,
+ * launched at :706 with scale 1/hc on the low-rank mixing activations). */
+int wzyb_silu_scale_f16(const float* lo, uint16_t* out, int64_t n, float scale, wzyb_stream_t stream);
 
 /* ============================================================================================
  * Per-head RMSNorm + partial NeoX RoPE, in place.
@@ -282,12 +304,15 @@ int wzyb_set_launch_tuning(int family, int ctas_per_sm, int stages);
  *   WZYB_VARIANT_RING   TMA bulk-copy ring staged through shared memory, one CTA barrier per unit
  *   WZYB_VARIANT_DIRECT warp-owned units, 16-byte loads prefetched into registers, no CTA barrier
  *   WZYB_VARIANT_ASYNC  warp-owned units staged in a lane-private shared-memory ring by cp.async
- * Families 0 (add+RMSNorm), 1 (head norm+RoPE) and 2 (GDN gated norm) have the RING and DIRECT
- * designs; families 1 and 2 also ASYNC (a family without a design falls back to AUTO). */
+ *   WZYB_VARIANT_WIDE   CTA-owned rows (4-16 warps), registers, one CTA barrier per row
+ * Families 0 (add+RMSNorm), 1 (head norm+RoPE) and 2 (GDN gated norm) have the RING, DIRECT and
+ * ASYNC designs; family 0 also WIDE, which AUTO picks for rows past one warp's register budget
+ * (a family without a design falls back to AUTO; DIRECT and ASYNC do so for rows too wide). */
 #define WZYB_VARIANT_AUTO 0
 #define WZYB_VARIANT_RING 1
 #define WZYB_VARIANT_DIRECT 2
 #define WZYB_VARIANT_ASYNC 3
+#define WZYB_VARIANT_WIDE 4
 int wzyb_set_kernel_variant(int family, int variant);
 const char* wzyb_status_string(int status);
 int wzyb_version(void);

@@ -28,6 +28,10 @@ _SIGS = {
     "or_gr_norm_f32": (None, [P, P, P, P, P, P, c_int64, c_int, c_int, c_float]),
     "or_gr_norm_q8_f32": (None, [P, P, P, P, P, P, P, c_int64, c_int, c_int, c_float]),
     "or_swiglu_q8_f32": (None, [P, P, P, P, c_int64]),
+    "or_gr_write_f32": (None, [P, P, P, c_int64, c_int, c_int]),
+    "or_hc_mix_f16": (None, [P, P, P, P, c_int64, c_int, c_int]),
+    "or_hc_mix_f32": (None, [P, P, P, c_int64, c_int, c_int]),
+    "or_silu_scale_f16": (None, [P, P, c_int64, c_float]),
     "or_head_norm_rope_f16": (
         None, [P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, c_int64, c_int64, c_int, c_float, c_float]),
     "or_head_norm_rope_f32": (
@@ -119,6 +123,33 @@ def swiglu_q8_f32(g, u):
     s = np.empty(g.size // 32, dtype=np.float32)
     lib().or_swiglu_q8_f32(_p(g), _p(u), _p(q), _p(s), g.size)
     return q, s
+
+
+def gr_write_f32(R, blk, inj, T, n, hc):
+    """R [T*hc, n] + blk[t] * 2*sigmoid(inj/hc) (gate 1.0 with inj None); returns the new R."""
+    out = np.array(R, dtype=np.float32, copy=True)
+    lib().or_gr_write_f32(_p(out), _p(np.ascontiguousarray(blk, np.float32)),
+                          _p(np.ascontiguousarray(inj, np.float32)) if inj is not None else None, T, n, hc)
+    return out
+
+
+def hc_mix(xn, gg, T, n, hc):
+    """Stream mixing; fp16 inputs give (mixed fp32, mixed fp16), fp32 inputs give mixed fp32."""
+    mixed = np.empty((T, n), dtype=np.float32)
+    if xn.dtype == np.float16:
+        m16 = np.empty((T, n), dtype=np.float16)
+        lib().or_hc_mix_f16(_p(np.ascontiguousarray(xn)), _p(np.ascontiguousarray(gg)), _p(mixed), _p(m16), T, n, hc)
+        return mixed, m16
+    lib().or_hc_mix_f32(_p(np.ascontiguousarray(xn, np.float32)), _p(np.ascontiguousarray(gg, np.float32)),
+                        _p(mixed), T, n, hc)
+    return mixed
+
+
+def silu_scale_f16(lo, scale):
+    lo = np.ascontiguousarray(lo, np.float32)
+    out = np.empty(lo.shape, dtype=np.float16)
+    lib().or_silu_scale_f16(_p(lo), _p(out), lo.size, scale)
+    return out
 
 
 def rope_table(rows, rot=64, theta=1e7):
@@ -218,6 +249,9 @@ def ref_lib() -> ctypes.CDLL:
             "ref_silu_mul_quant32_multi": [P, P, P, P, I, P],
             "ref_pf_gr_norm_fp16": [P, P, P, P, P, I, I, I, F, P],
             "ref_gr_write_multi": [P, P, P, I, I, I, P],
+            "ref_pf_gr_up_mean_fp16": [P, P, P, P, I, I, P],
+            "ref_gr_up_gate_mean_pf": [P, P, P, I, I, P],
+            "ref_silu_div_hc_to_fp16": [P, P, I, F, P],
             "ref_fused_head_norm_rope_multi": [P, P, P, P, P, I, I, I, I, I, F, P],
             "ref_pf_gdn_rmsnorm_gate_parallel": [P, P, P, P, I, I, F, P],
             "ref_silu_mul_multi": [P, P, P, I, P],

@@ -47,6 +47,25 @@ int ref_gr_write_multi(float* R, const float* blk, const float* inj, int T, int 
     return (int)cudaGetLastError();
 }
 
+// pf_gr_up_mean_fp16 (src/wzy_qsa_wmma.cuh:234-253), launched as at src/wzy_prefill_tc.cuh:712.
+int ref_pf_gr_up_mean_fp16(const __half* xn, const __half* gg, float* mixed, __half* mixed16, int T, int n_embd,
+                           cudaStream_t s) {
+    pf_gr_up_mean_fp16<<<(int)(((size_t)T * n_embd + 255) / 256), 256, 0, s>>>(xn, gg, mixed, mixed16, T, n_embd);
+    return (int)cudaGetLastError();
+}
+
+// gr_up_gate_mean_pf_kernel (src/wzy_prefill_tc.cuh:37-51), one element per thread.
+int ref_gr_up_gate_mean_pf(const float* xn, const float* gg, float* mixed, int T, int n_embd, cudaStream_t s) {
+    gr_up_gate_mean_pf_kernel<<<(int)(((size_t)T * n_embd + 255) / 256), 256, 0, s>>>(xn, gg, mixed, T, n_embd);
+    return (int)cudaGetLastError();
+}
+
+// silu_div_hc_to_fp16_kernel (src/wzy_prefill_tc.cuh:24-35), launched as at src/wzy_prefill_tc.cuh:706.
+int ref_silu_div_hc_to_fp16(const float* lo, __half* out, int n, float inv_hc, cudaStream_t s) {
+    silu_div_hc_to_fp16_kernel<<<(int)((((size_t)n + 1) / 2 + 255) / 256), 256, 0, s>>>(lo, out, n, inv_hc);
+    return (int)cudaGetLastError();
+}
+
 // fused_head_norm_rope_multi (src/wzy_qsa_256k.cuh:50-84), grid (heads, T) x 128 (T <= 65535).
 int ref_fused_head_norm_rope_multi(float* data, const float* gamma, const float* cos_tab, const float* sin_tab,
                                    const int* base_pos_dev, int T, int heads, int hd, int head_stride, int row_stride,

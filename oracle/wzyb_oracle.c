@@ -164,6 +164,62 @@ void or_swiglu_q8_f32(const float* g, const float* u, int8_t* q, float* s, int64
 }
 
 /* ------------------------------------------------------------------------------------------- */
+/* multi-stream residual outside the norm                                                      */
+/* gr_write_multi (src/wzy_kernels_v2.cuh:813-828): R[t,c,:] += blk[t,:] * 2/(1+exp(-inj/hc))  */
+/* ------------------------------------------------------------------------------------------- */
+void or_gr_write_f32(float* R, const float* blk, const float* inj, int64_t T, int n, int hc) {
+#pragma omp parallel for schedule(static)
+    for (int64_t u = 0; u < T * hc; ++u) {
+        const float gw = inj ? 2.0f / sigmoid_den(inj[u] / (float)hc) : 1.0f;
+        const float* b = blk + (u / hc) * n;
+        float* r = R + u * n;
+        for (int d = 0; d < n; ++d) r[d] = r[d] + b[d] * gw;
+    }
+}
+
+/* pf_gr_up_mean_fp16 (src/wzy_qsa_wmma.cuh:234-253) / gr_up_gate_mean_pf_kernel                */
+/* (src/wzy_prefill_tc.cuh:37-51): mixed[t,d] = (sum_c xn[t,c,d] / (1 + exp(-gg[t,c,d]))) / hc,  */
+/* streams summed in order c = 0..hc-1; the reference's 4 streams scale by 0.25.                 */
+static void hc_mix_row(const float* x, const float* g, int64_t n, int hc, int64_t d, float* out) {
+    float acc = 0.f;
+    for (int c = 0; c < hc; ++c) acc += x[c * n + d] / sigmoid_den(g[c * n + d]);
+    *out = acc * (1.0f / (float)hc);
+}
+
+void or_hc_mix_f16(const uint16_t* xn, const uint16_t* gg, float* mixed, uint16_t* mixed_h16, int64_t T, int n,
+                   int hc) {
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < T; ++t) {
+        float* x = (float*)malloc(sizeof(float) * 2 * (size_t)hc * n);
+        float* g = x + (size_t)hc * n;
+        or_h2f_array(xn + t * hc * n, x, (int64_t)hc * n);
+        or_h2f_array(gg + t * hc * n, g, (int64_t)hc * n);
+        for (int64_t d = 0; d < n; ++d) {
+            float m;
+            hc_mix_row(x, g, n, hc, d, &m);
+            if (mixed) mixed[t * n + d] = m;
+            if (mixed_h16) mixed_h16[t * n + d] = or_f2h(m);
+        }
+        free(x);
+    }
+}
+
+void or_hc_mix_f32(const float* xn, const float* gg, float* mixed, int64_t T, int n, int hc) {
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < T; ++t)
+        for (int64_t d = 0; d < n; ++d) hc_mix_row(xn + t * hc * n, gg + t * hc * n, n, hc, d, mixed + t * n + d);
+}
+
+/* silu_div_hc_to_fp16_kernel (src/wzy_prefill_tc.cuh:24-35): v = lo * scale; out = fp16(v / (1 + exp(-v))) */
+void or_silu_scale_f16(const float* lo, uint16_t* out, int64_t n, float scale) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        const float v = lo[i] * scale;
+        out[i] = or_f2h(v / sigmoid_den(v));
+    }
+}
+
+/* ------------------------------------------------------------------------------------------- */
 /* per-head RMSNorm + partial NeoX RoPE: fused_head_norm_rope_multi (src/wzy_qsa_256k.cuh:50-84) */
 /*   p *= rsqrt(sum(p^2)/hd + eps) * gamma;  (a, d) = (p[i], p[i+R/2])                          */
 /*   p[i] = a*cos - d*sin;  p[i+R/2] = a*sin + d*cos, cos/sin = tab[pos*(R/2) + i]              */

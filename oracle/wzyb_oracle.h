@@ -37,6 +37,12 @@ void or_gr_norm_q8_f32(float* R, const float* w, const float* bo, const float* i
                        float* s8, int64_t T, int n, int hc, float eps);
 /* SwiGLU fused with Q8_0 quantisation (no activation output) */
 void or_swiglu_q8_f32(const float* g, const float* u, int8_t* q, float* s, int64_t n);
+/* multi-stream residual: gated write, stream mixing, scaled SiLU to fp16 */
+void or_gr_write_f32(float* R, const float* blk, const float* inj, int64_t T, int n, int hc);
+void or_hc_mix_f16(const uint16_t* xn, const uint16_t* gg, float* mixed, uint16_t* mixed_h16, int64_t T, int n,
+                   int hc);
+void or_hc_mix_f32(const float* xn, const float* gg, float* mixed, int64_t T, int n, int hc);
+void or_silu_scale_f16(const float* lo, uint16_t* out, int64_t n, float scale);
 /* per-head RMSNorm + partial NeoX RoPE, in place */
 void or_head_norm_rope_f16(uint16_t* data, const uint16_t* gamma, const float* cos_tab, const float* sin_tab,
                            int64_t table_rows, int64_t base_pos, int64_t T, int heads, int hd, int64_t head_stride,

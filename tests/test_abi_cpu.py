@@ -66,13 +66,25 @@ def test_argument_validation_before_any_cuda_call(wz):
     # Q8_0 side outputs: whole 32-wide groups, n_embd <= 4096, every buffer 16-byte aligned
     assert L.wzyb_gr_norm_q8_f32(A16, A16, A16, A16, A16, NULL, A16, 4, 2560, 4, 1e-6, NULL) == wz.ERR_NULL
     assert L.wzyb_gr_norm_q8_f32(A16, A16, A16, A16, A16, A16, A16, 4, 2568, 4, 1e-6, NULL) == wz.ERR_SHAPE
-    assert L.wzyb_gr_norm_q8_f32(A16, A16, A16, A16, A16, A16, A16, 4, 8192, 4, 1e-6, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_gr_norm_q8_f32(A16, A16, A16, A16, A16, A16, A16, 4, 16416, 4, 1e-6, NULL) == wz.ERR_SHAPE
     assert L.wzyb_gr_norm_q8_f32(A16, A16, A16, A16, A16, A8, A16, 4, 2560, 4, 1e-6, NULL) == wz.ERR_ALIGN
     assert L.wzyb_gr_norm_q8_f32(A16, A16, A16, A16, A16, A16, A16, 0, 2560, 4, 1e-6, NULL) == wz.OK
     assert L.wzyb_swiglu_q8_f32(A16, A16, NULL, A16, 64, NULL) == wz.ERR_NULL
     assert L.wzyb_swiglu_q8_f32(A16, A16, A16, A16, 48, NULL) == wz.ERR_SHAPE
     assert L.wzyb_swiglu_q8_f32(A16, A16, A16, A8, 64, NULL) == wz.ERR_ALIGN
     assert L.wzyb_swiglu_q8_f32(A16, A16, A16, A16, 0, NULL) == wz.OK
+    # multi-stream residual
+    assert L.wzyb_gr_write_f32(NULL, A16, NULL, 4, 2560, 4, NULL) == wz.ERR_NULL
+    assert L.wzyb_gr_write_f32(A16, A16, NULL, 4, 2564, 4, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_gr_write_f32(A16, A16, NULL, 4, 2560, 0, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_gr_write_f32(A8, A16, NULL, 4, 2560, 4, NULL) == wz.ERR_ALIGN
+    assert L.wzyb_hc_mix_f16(A16, A16, NULL, NULL, 4, 2560, 4, NULL) == wz.ERR_NULL
+    assert L.wzyb_hc_mix_f16(A16, A16, A16, NULL, 4, 2562, 4, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_hc_mix_f16(A16, A16, NULL, A8, 4, 2560, 4, NULL) == wz.ERR_ALIGN
+    assert L.wzyb_hc_mix_f32(A16, A16, NULL, 4, 2560, 4, NULL) == wz.ERR_NULL
+    assert L.wzyb_hc_mix_f32(A16, A16, A16, 0, 2560, 4, NULL) == wz.OK
+    assert L.wzyb_silu_scale_f16(A16, A16, 12, 0.25, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_silu_scale_f16(A16, A8, 16, 0.25, NULL) == wz.ERR_ALIGN
     # empty work is a no-op that succeeds without a device
     assert L.wzyb_swiglu_f16(A16, A16, A16, 0, NULL) == wz.OK
     assert L.wzyb_add_rmsnorm_f16(A16, A16, A16, A16, 0, 2048, 1e-6, 1.0, NULL) == wz.OK

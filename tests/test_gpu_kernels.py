@@ -45,10 +45,12 @@ def _faults_clear(wz):
         wz.set_kernel_variant(fam, wz.VARIANT_AUTO)
 
 
-# The norm families have two kernel designs (TMA ring, direct); parity must hold for both.
-@pytest.fixture(params=["ring", "direct", "async"])
+# The norm families have several kernel designs (TMA ring, direct, cp.async, CTA-wide rows; a family
+# without one falls back to its default); parity must hold for each.
+@pytest.fixture(params=["ring", "direct", "async", "wide"])
 def variant(request, wz):
-    v = {"ring": wz.VARIANT_RING, "direct": wz.VARIANT_DIRECT, "async": wz.VARIANT_ASYNC}[request.param]
+    v = {"ring": wz.VARIANT_RING, "direct": wz.VARIANT_DIRECT, "async": wz.VARIANT_ASYNC,
+         "wide": wz.VARIANT_WIDE}[request.param]
     for fam in (wz.FAM_NORM, wz.FAM_HEAD_ROPE, wz.FAM_GDN):
         wz.set_kernel_variant(fam, v)
     return request.param
@@ -390,3 +392,56 @@ def test_swiglu_q8_f32(wz, orc, n):
     ds = torch.empty(n // 32, dtype=torch.float32, device=DEV)
     wz.swiglu_q8_f32(dev(g), dev(u), dq, ds)
     _q8_close(host(dq), host(ds), q_ref, s_ref, "swiglu q8")
+
+
+# ---------------------------------------------------------------------------------------------
+# multi-stream residual: gated write, stream mixing, scaled SiLU
+# ---------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("T,n,hc,with_inj", [(1, 2560, 4, True), (37, 2560, 4, True), (5, 2048, 1, False),
+                                             (3, 24, 3, True), (4096, 2048, 1, False)])
+def test_gr_write_f32(wz, orc, T, n, hc, with_inj):
+    r = rng(T + n + hc)
+    R = r.standard_normal((T * hc, n)).astype(np.float32)
+    blk = r.standard_normal((T, n)).astype(np.float32)
+    inj = r.standard_normal(T * hc).astype(np.float32) if with_inj else None
+    want = orc.gr_write_f32(R, blk, inj, T, n, hc)
+    dR = dev(R)
+    wz.gr_write_f32(dR, dev(blk), dev(inj) if inj is not None else None, T, n, hc)
+    got = host(dR)
+    if with_inj:  # __expf in the gate: a few fp32 ulp
+        np.testing.assert_allclose(got, want, rtol=1e-6, atol=1e-6)
+    else:  # gate 1.0: fma(b, 1, R) is the exact sum
+        assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("T,n,hc", [(1, 2560, 4), (19, 2560, 4), (4096, 2048, 4), (7, 64, 3), (5, 128, 1)])
+def test_hc_mix(wz, orc, T, n, hc):
+    r = rng(T * 3 + n + hc)
+    xn = f16n(r, (T, hc, n))
+    gg = f16n(r, (T, hc, n), 2.0)
+    m32_ref, m16_ref = orc.hc_mix(xn, gg, T, n, hc)
+    d32 = torch.empty((T, n), dtype=torch.float32, device=DEV)
+    d16 = torch.empty((T, n), dtype=torch.float16, device=DEV)
+    dx, dg = dev(xn), dev(gg)
+    wz.hc_mix(dx, dg, d32, d16, T, n, hc)
+    np.testing.assert_allclose(host(d32), m32_ref, rtol=2e-6, atol=2e-6)
+    assert_f16_close(host(d16), m16_ref, ULP_TOL, "hc_mix fp16 out")
+    # either output alone
+    e16 = torch.empty_like(d16)
+    wz.hc_mix(dx, dg, None, e16, T, n, hc)
+    assert np.array_equal(host(e16), host(d16))
+    # fp32 inputs (the fp32 twin)
+    x32, g32 = xn.astype(np.float32), gg.astype(np.float32)
+    f32 = torch.empty((T, n), dtype=torch.float32, device=DEV)
+    wz.hc_mix(dev(x32), dev(g32), f32, None, T, n, hc)
+    np.testing.assert_allclose(host(f32), orc.hc_mix(x32, g32, T, n, hc), rtol=2e-6, atol=2e-6)
+
+
+@pytest.mark.parametrize("n", [8, 4096 * 320, 262144 * 320])
+def test_silu_scale_f16(wz, orc, n):
+    r = rng(n % 977)
+    lo = (4 * r.standard_normal(n)).astype(np.float32)
+    want = orc.silu_scale_f16(lo, 0.25)
+    out = torch.empty(n, dtype=torch.float16, device=DEV)
+    wz.silu_scale_f16(dev(lo), out, 0.25)
+    assert_f16_close(host(out), want, ULP_TOL, "silu_scale")

@@ -238,3 +238,52 @@ def test_pin_q8_side_outputs(ref, orc, wz):
     wz.swiglu_q8_f32(dg, du, mq2, ms2)
     assert np.array_equal(host(mq2), host(q32))
     assert np.array_equal(host(ms2).view(np.uint32), host(s32).view(np.uint32))
+
+
+def test_pin_hyper_connection_residual(ref, orc, wz):
+    """gr_write_multi, pf_gr_up_mean_fp16, gr_up_gate_mean_pf_kernel and silu_div_hc_to_fp16_kernel at the
+    reference's stream count (4) and width (2560)."""
+    r = np.random.default_rng(209)
+    T, n, hc = 64, 2560, 4
+    # gated write: same gate expression, same fused multiply-add -> identical R
+    R = r.standard_normal((T * hc, n)).astype(np.float32)
+    blk = r.standard_normal((T, n)).astype(np.float32)
+    inj = r.standard_normal(T * hc).astype(np.float32)
+    dR, dblk, dinj = dev(R), dev(blk), dev(inj)
+    assert ref.ref_gr_write_multi(dR.data_ptr(), dblk.data_ptr(), dinj.data_ptr(), T, n, hc, sp()) == 0
+    ref_R = host(dR)
+    np.testing.assert_allclose(orc.gr_write_f32(R, blk, inj, T, n, hc), ref_R, rtol=1e-6, atol=1e-6)
+    mR = dev(R)
+    wz.gr_write_f32(mR, dblk, dinj, T, n, hc)
+    assert np.array_equal(host(mR), ref_R)
+    # stream mixing, fp16 in
+    xn = r.standard_normal((T, hc, n)).astype(np.float16)
+    gg = (2 * r.standard_normal((T, hc, n))).astype(np.float16)
+    dx, dg = dev(xn), dev(gg)
+    m32 = torch.empty((T, n), dtype=torch.float32, device=DEV)
+    m16 = torch.empty((T, n), dtype=torch.float16, device=DEV)
+    assert ref.ref_pf_gr_up_mean_fp16(dx.data_ptr(), dg.data_ptr(), m32.data_ptr(), m16.data_ptr(), T, n, sp()) == 0
+    r32, r16 = host(m32), host(m16)
+    o32, o16 = orc.hc_mix(xn, gg, T, n, hc)
+    np.testing.assert_allclose(o32, r32, rtol=2e-6, atol=2e-6)
+    assert_f16_close(o16, r16, 1, "oracle vs reference pf_gr_up_mean_fp16")
+    w32, w16 = torch.empty_like(m32), torch.empty_like(m16)
+    wz.hc_mix(dx, dg, w32, w16, T, n, hc)
+    np.testing.assert_allclose(host(w32), r32, rtol=2e-6, atol=2e-6)
+    assert_f16_close(host(w16), r16, ULP_TOL, "CUDA vs reference pf_gr_up_mean_fp16")
+    # stream mixing, fp32 in
+    dx32, dg32 = dev(xn.astype(np.float32)), dev(gg.astype(np.float32))
+    assert ref.ref_gr_up_gate_mean_pf(dx32.data_ptr(), dg32.data_ptr(), m32.data_ptr(), T, n, sp()) == 0
+    f32 = torch.empty_like(m32)
+    wz.hc_mix(dx32, dg32, f32, None, T, n, hc)
+    np.testing.assert_allclose(host(f32), host(m32), rtol=2e-6, atol=2e-6)
+    # scaled SiLU of the low-rank activations [T, 320] -> fp16
+    lo = (4 * r.standard_normal(T * 320)).astype(np.float32)
+    dlo = dev(lo)
+    lo16 = torch.empty(T * 320, dtype=torch.float16, device=DEV)
+    assert ref.ref_silu_div_hc_to_fp16(dlo.data_ptr(), lo16.data_ptr(), T * 320, 0.25, sp()) == 0
+    r_lo = host(lo16)
+    assert_f16_close(orc.silu_scale_f16(lo, 0.25), r_lo, 1, "oracle vs reference silu_div_hc")
+    w_lo = torch.empty_like(lo16)
+    wz.silu_scale_f16(dlo, w_lo, 0.25)
+    assert_f16_close(host(w_lo), r_lo, ULP_TOL, "CUDA vs reference silu_div_hc")

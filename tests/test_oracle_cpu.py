@@ -207,3 +207,25 @@ def test_q8_paths_against_numpy(orc):
     q_np, d_np = _np_q8(orc.swiglu(g, u))
     assert np.array_equal(q, q_np) and np.array_equal(s, d_np)
     assert s[0] == 0 and not q[:32].any()
+
+
+def test_hyper_connection_residual_against_float64(orc):
+    r = np.random.default_rng(41)
+    T, n, hc = 6, 80, 4
+    R = r.standard_normal((T * hc, n)).astype(np.float32)
+    blk = r.standard_normal((T, n)).astype(np.float32)
+    inj = r.standard_normal(T * hc).astype(np.float32)
+    gw = 2.0 / (1.0 + np.exp(-inj.astype(np.float64) / hc))
+    want = R.astype(np.float64) + np.repeat(blk, hc, axis=0) * gw[:, None]
+    np.testing.assert_allclose(orc.gr_write_f32(R, blk, inj, T, n, hc), want, rtol=1e-6, atol=1e-6)
+    assert np.array_equal(orc.gr_write_f32(R, blk, None, T, n, hc), R + np.repeat(blk, hc, axis=0))
+    xn = r.standard_normal((T, hc, n)).astype(np.float16)
+    gg = (2 * r.standard_normal((T, hc, n))).astype(np.float16)
+    m32, m16 = orc.hc_mix(xn, gg, T, n, hc)
+    w = (xn.astype(np.float64) / (1 + np.exp(-gg.astype(np.float64)))).mean(axis=1)
+    np.testing.assert_allclose(m32, w, rtol=1e-5, atol=1e-6)
+    assert np.array_equal(m16, m32.astype(np.float16))
+    np.testing.assert_array_equal(orc.hc_mix(xn.astype(np.float32), gg.astype(np.float32), T, n, hc), m32)
+    lo = (4 * r.standard_normal(1000)).astype(np.float32)
+    v = lo.astype(np.float64) * 0.25
+    assert_f16_close(orc.silu_scale_f16(lo, 0.25), (v / (1 + np.exp(-v))).astype(np.float16), 1, "silu_scale")

@@ -235,6 +235,15 @@ struct Vec8<float> {
         f[2] = make_float2(b.x, b.y);
         f[3] = make_float2(b.z, b.w);
     }
+    // coherent load, for rows this kernel also writes
+    __device__ __forceinline__ static void load2(const float* p, float2 (&f)[4]) {
+        const float4 a = reinterpret_cast<const float4*>(p)[0];
+        const float4 b = reinterpret_cast<const float4*>(p)[1];
+        f[0] = make_float2(a.x, a.y);
+        f[1] = make_float2(a.z, a.w);
+        f[2] = make_float2(b.x, b.y);
+        f[3] = make_float2(b.z, b.w);
+    }
     __device__ __forceinline__ static void store2(float* p, const float2 (&f)[4]) {
         reinterpret_cast<float4*>(p)[0] = make_float4(f[0].x, f[0].y, f[1].x, f[1].y);
         reinterpret_cast<float4*>(p)[1] = make_float4(f[2].x, f[2].y, f[3].x, f[3].y);

@@ -329,7 +329,7 @@ static int launch_gdn(const void* o, const void* z, const void* gamma, void* y, 
     // The direct design is the default (measured on B200 at 262,144 tokens: direct 84%, cp.async 83%,
     // TMA ring 43% of HBM peak).
     const int v = variant(kFamGdn);
-    if (v == WZYB_VARIANT_AUTO || v == WZYB_VARIANT_ASYNC || v == WZYB_VARIANT_DIRECT) {
+    if (v != WZYB_VARIANT_RING) {
         const bool async_design = v == WZYB_VARIANT_ASYNC;
         return gate_mode == WZYB_GATE_SILU ? launch_gdn_warp<TI, TO, true>(a, hd, async_design, di, stream)
                                            : launch_gdn_warp<TI, TO, false>(a, hd, async_design, di, stream);

@@ -27,7 +27,7 @@ struct NormRowsArgs {
     int stages;
     uint32_t row_bytes;
     uint32_t stage_bytes;
-    signed char* q8;  // optional Q8_0 codes of xn [T*hc, n] (async design only)
+    signed char* q8;  // optional Q8_0 codes of xn [T*hc, n] (wide design only)
     float* s8;        // its per-32-element scales [T*hc, n/32]
 };
 
@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(256, 2) norm_rows_direct_kernel(const NormRows
 // its own 16-byte chunks, so no barrier is needed) and read from there twice -- once for the sum of
 // squares, once for the outputs. Registers stay low, so at layer-sized T every row of the call is in
 // flight at once (kP = 1); kP = 2 double-buffers rows for long streams.
-template <typename TI, typename TO, int VPL, int kP, bool Q8 = false>
+template <typename TI, typename TO, int VPL, int kP>
 __global__ void __launch_bounds__(128) norm_rows_async_kernel(const NormRowsArgs a) {
     constexpr int C = Vec8<TI>::kChunks;
     constexpr int SLOT = 2 * VPL * C * 32;  // uint4: residual vectors, then x vectors
@@ -300,15 +300,130 @@ __global__ void __launch_bounds__(128) norm_rows_async_kernel(const NormRowsArgs
                 Vec8<TO>::store2(y + u * n + e, o);
                 if (has_x) Vec8<TI>::store2(res + u * n + e, v);
             }
-            if (Q8) {  // all lanes: the group max is a shuffle
-                const float yo[8] = {o[0].x, o[0].y, o[1].x, o[1].y, o[2].x, o[2].y, o[3].x, o[3].y};
-                q8_group_store(yo, e < n, a.q8 + u * n + e, a.s8 + ((u * n + e) >> 5), lane);
-            }
         }
         // Refill the slot: only this lane touches its chunks, and its reads precede the new copy.
         issue(u + kP * nwarps, slot);
     }
     cp_async_wait<0>();
+}
+
+// Wide design, for rows past one warp's register budget (fp32 rows past 1536, fp16 past 3072 -- the
+// reference model's 2560-wide fp32 streams among them): a CTA of NW = blockDim/32 warps (4, 8 or 16)
+// owns one row at a time. Thread i of the CTA holds the 8-element vectors k*blockDim + i (k < VPL),
+// so each warp-wide load still covers 512 contiguous bytes and every 32-element group sits in 4
+// consecutive lanes of one warp (the Q8_0 side output quantises it with two shuffles). The warps'
+// partial sums of squares meet in shared memory behind ONE barrier per row: the partials are
+// double-buffered by row parity, and a warp can only come back to a slot after passing the next
+// row's barrier, which the slowest warp reaches only once it has read the slot. Rows are spread
+// over a persistent grid; several CTAs per SM keep rows in flight across the barriers.
+template <typename TI, typename TO, int VPL, bool Q8>
+__global__ void __launch_bounds__(512) norm_rows_wide_kernel(const NormRowsArgs a) {
+    __shared__ float part[2][16];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int nw = blockDim.x >> 5;
+    const int span = blockDim.x * 8;
+    const TI* __restrict__ x = static_cast<const TI*>(a.x);
+    TI* __restrict__ res = static_cast<TI*>(a.res);
+    const TI* __restrict__ w = static_cast<const TI*>(a.w);
+    TO* __restrict__ y = static_cast<TO*>(a.y);
+    const bool has_x = x != nullptr;
+    const int n = a.n;
+    int par = 0;
+
+    for (int64_t u = blockIdx.x; u < a.units; u += gridDim.x, par ^= 1) {
+        typename Vec8<TI>::Raw rr[VPL], rx[VPL];
+        const int64_t t = a.hc == 1 ? u : u / a.hc;
+        const TI* rrow = res + u * n;
+        const TI* xrow = has_x ? x + t * n : nullptr;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int e = k * span + threadIdx.x * 8;
+            if (e < n) {
+                rr[k] = Vec8<TI>::ldcs_raw(rrow + e);
+                if (has_x) rx[k] = Vec8<TI>::ldcs_raw(xrow + e);
+            }
+        }
+        const float2 gate = splat2((has_x && a.inj != nullptr) ? 2.0f / (1.0f + __expf(-a.inj[u] / (float)a.hc))
+                                                                : 1.0f);
+        auto residual_sum = [&](int k, float2 (&v)[4]) {  // v = residual + x * gate
+            Vec8<TI>::cvt2(rr[k], v);
+            if (has_x) {
+                float2 xv[4];
+                Vec8<TI>::cvt2(rx[k], xv);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) v[i] = ffma2(xv[i], gate, v[i]);
+            }
+        };
+        float ss = 0.f;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            if (k * span + threadIdx.x * 8 < n) {
+                float2 v[4];
+                residual_sum(k, v);
+                ss += sumsq8(v);
+            }
+        }
+        ss = group_sum<32>(ss);
+        if (lane == 0) part[par][warp] = ss;
+        __syncthreads();
+        float tot = 0.f;
+        for (int i = 0; i < nw; ++i) tot += part[par][i];  // same order in every thread
+        const float2 sc = splat2(rsqrt_approx(tot / (float)n + a.eps));
+        const float2 woff = splat2(a.w_offset);
+        const TI* wrow = w + (u - t * a.hc) * n;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int e = k * span + threadIdx.x * 8;
+            float2 o[4] = {};
+            if (e < n) {
+                float2 v[4], g[4];
+                residual_sum(k, v);
+                Vec8<TI>::load_ro2(wrow + e, g);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[i] = fmul2(fmul2(v[i], sc), fadd2(woff, g[i]));  // (v*sc)*g
+                Vec8<TO>::store2(y + u * n + e, o);
+                if (has_x) Vec8<TI>::store2(res + u * n + e, v);
+            }
+            if (Q8) {  // every lane: the group max is a shuffle
+                const float yo[8] = {o[0].x, o[0].y, o[1].x, o[1].y, o[2].x, o[2].y, o[3].x, o[3].y};
+                q8_group_store(yo, e < n, a.q8 + u * n + e, a.s8 + ((u * n + e) >> 5), lane);
+            }
+        }
+    }
+}
+
+// Warps per CTA and vectors per thread of the wide design for a row of `vecs` 8-element vectors:
+// the fewest warps (4, 8, 16) that keep VPL within the register budget, VPL rounded up to an
+// instantiated count.
+template <typename TI>
+static void wide_shape(int vecs, int& nw, int& vpl) {
+    const int vmax = sizeof(TI) == 2 ? 8 : 4;
+    nw = 4;
+    while (nw < 16 && (vecs + nw * 32 - 1) / (nw * 32) > vmax) nw *= 2;
+    const int need = (vecs + nw * 32 - 1) / (nw * 32);
+    vpl = need <= 1 ? 1 : need <= 2 ? 2 : need <= 3 ? 3 : need <= 4 ? 4 : need <= 6 ? 6 : 8;
+}
+
+template <typename TI, typename TO, bool Q8>
+static int launch_norm_rows_wide(const NormRowsArgs& a, const DeviceInfo& di, cudaStream_t stream) {
+    int nw = 0, vpl = 0;
+    wide_shape<TI>(a.n / 8, nw, vpl);
+    const int threads = nw * 32;
+    const void* kern = nullptr;
+#define WZYB_NRW(V) \
+    if (vpl == V) kern = (const void*)norm_rows_wide_kernel<TI, TO, V, Q8>;
+    WZYB_NRW(1) WZYB_NRW(2) WZYB_NRW(3) WZYB_NRW(4)
+    if constexpr (sizeof(TI) == 2) { WZYB_NRW(6) WZYB_NRW(8) }
+#undef WZYB_NRW
+    if (kern == nullptr) return WZYB_ERR_SHAPE;
+    const int grid = persistent_grid(di, resident_ctas(kern, threads, 0), a.units);
+#define WZYB_NRW(V) \
+    if (vpl == V) norm_rows_wide_kernel<TI, TO, V, Q8><<<grid, threads, 0, stream>>>(a);
+    WZYB_NRW(1) WZYB_NRW(2) WZYB_NRW(3) WZYB_NRW(4)
+    if constexpr (sizeof(TI) == 2) { WZYB_NRW(6) WZYB_NRW(8) }
+#undef WZYB_NRW
+    return launch_status();
 }
 
 template <typename TI, typename TO>
@@ -342,10 +457,14 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
     a.q8 = nullptr;
     a.s8 = nullptr;
 
-    // Direct design while a row fits the register budget (<= 12 fp16 or 6 fp32 vectors per lane).
+    // Direct design while a row fits one warp's register budget (<= 12 fp16 or 6 fp32 vectors per
+    // lane), the wide design (CTA-owned rows) past it; the TMA ring only on request.
     const int vpl_need = (n + 255) / 256;
     const int vpl_max = sizeof(TI) == 2 ? 12 : 6;
-    if (variant(kFamNorm) == WZYB_VARIANT_ASYNC && vpl_need <= (sizeof(TI) == 2 ? 8 : 4)) {
+    const int var = variant(kFamNorm);
+    if (var == WZYB_VARIANT_WIDE || (var != WZYB_VARIANT_RING && vpl_need > vpl_max))
+        return launch_norm_rows_wide<TI, TO, false>(a, di, stream);
+    if (var == WZYB_VARIANT_ASYNC && vpl_need <= (sizeof(TI) == 2 ? 8 : 4)) {
         const int vpl = vpl_need <= 1 ? 1 : vpl_need <= 2 ? 2 : vpl_need <= 4 ? 4 : 8;
         // one row in flight per warp when every row of the call fits in one round, else two
         const int64_t one_round = (int64_t)di.sms * 28;
@@ -426,13 +545,12 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
     return launch_status();
 }
 
-// Residual fold + norm with the Q8_0 side output: the async design (rows staged in shared memory),
-// one row in flight per warp, any n up to 16 fp32 vectors per lane (n <= 4096).
+// Residual fold + norm with the Q8_0 side output: the wide design at every width (n <= 16384).
 template <typename TI, typename TO>
 static int launch_norm_rows_q8(const void* x, void* res, const void* w, const float* inj, void* y, signed char* q8,
                                float* s8, int64_t T, int n, int hc, float eps, cudaStream_t stream) {
     if (res == nullptr || w == nullptr || y == nullptr || q8 == nullptr || s8 == nullptr) return WZYB_ERR_NULL;
-    if (T < 0 || T > (int64_t(1) << 40) || n < 32 || n > 4096 || (n % 32) != 0 || hc < 1 || hc > 64)
+    if (T < 0 || T > (int64_t(1) << 40) || n < 32 || n > 16384 || (n % 32) != 0 || hc < 1 || hc > 64)
         return WZYB_ERR_SHAPE;
     if (!aligned16(res) || !aligned16(w) || !aligned16(y) || (x && !aligned16(x)) || !aligned16(q8) ||
         !aligned16(s8))
@@ -456,22 +574,7 @@ static int launch_norm_rows_q8(const void* x, void* res, const void* w, const fl
     a.row_bytes = a.stage_bytes = 0;
     a.q8 = q8;
     a.s8 = s8;
-    const int vpl_need = (n + 255) / 256;
-    const int vpl = vpl_need <= 1 ? 1 : vpl_need <= 2 ? 2 : vpl_need <= 4 ? 4 : vpl_need <= 8 ? 8 : vpl_need <= 12 ? 12 : 16;
-    const int smem = 4 * 2 * vpl * Vec8<TI>::kChunks * 32 * 16;
-    const void* kern = nullptr;
-#define WZYB_NRQ(V) \
-    if (vpl == V) kern = (const void*)norm_rows_async_kernel<TI, TO, V, 1, true>;
-    WZYB_NRQ(1) WZYB_NRQ(2) WZYB_NRQ(4) WZYB_NRQ(8) WZYB_NRQ(12) WZYB_NRQ(16)
-#undef WZYB_NRQ
-    rc = ensure_smem(kern, smem);
-    if (rc != WZYB_OK) return rc;
-    const int grid = persistent_grid(di, resident_ctas(kern, 128, smem), (a.units + 3) / 4);
-#define WZYB_NRQ(V) \
-    if (vpl == V) norm_rows_async_kernel<TI, TO, V, 1, true><<<grid, 128, smem, stream>>>(a);
-    WZYB_NRQ(1) WZYB_NRQ(2) WZYB_NRQ(4) WZYB_NRQ(8) WZYB_NRQ(12) WZYB_NRQ(16)
-#undef WZYB_NRQ
-    return launch_status();
+    return launch_norm_rows_wide<TI, TO, true>(a, di, stream);
 }
 
 }  // namespace wzyb

@@ -6,3 +6,4 @@
 #include "gdn_norm.cu"
 #include "swiglu.cu"
 #include "gather.cu"
+#include "hc_stream.cu"

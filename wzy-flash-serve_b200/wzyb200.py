@@ -24,7 +24,7 @@ OOB_CLAMP, OOB_ZERO_ID = 0, 1
 PLE_HASH_C_PRECEDENCE, PLE_HASH_XOR_THEN_ADD = 0, 1
 PLE_EOS_DEFAULT = 248044
 FAM_NORM, FAM_HEAD_ROPE, FAM_GDN, FAM_SWIGLU, FAM_GATHER = 0, 1, 2, 3, 4
-VARIANT_AUTO, VARIANT_RING, VARIANT_DIRECT, VARIANT_ASYNC = 0, 1, 2, 3
+VARIANT_AUTO, VARIANT_RING, VARIANT_DIRECT, VARIANT_ASYNC, VARIANT_WIDE = 0, 1, 2, 3, 4
 
 
 class WzybError(RuntimeError):
@@ -91,6 +91,10 @@ _SIGS = {
     "wzyb_gr_norm_f32_f16": (c_int, [P, P, P, P, P, c_int64, c_int, c_int, c_float, S]),
     "wzyb_gr_norm_q8_f32": (c_int, [P, P, P, P, P, P, P, c_int64, c_int, c_int, c_float, S]),
     "wzyb_swiglu_q8_f32": (c_int, [P, P, P, P, c_int64, S]),
+    "wzyb_gr_write_f32": (c_int, [P, P, P, c_int64, c_int, c_int, S]),
+    "wzyb_hc_mix_f16": (c_int, [P, P, P, P, c_int64, c_int, c_int, S]),
+    "wzyb_hc_mix_f32": (c_int, [P, P, P, c_int64, c_int, c_int, S]),
+    "wzyb_silu_scale_f16": (c_int, [P, P, c_int64, c_float, S]),
     "wzyb_head_norm_rope_f16": (
         c_int,
         [P, P, P, P, c_int64, P, c_int64, c_int64, c_int, c_int, c_int64, c_int64, c_int, c_float, c_float, S],
@@ -196,6 +200,23 @@ def gr_norm_q8_f32(R, w_norm, bo_prev, inj_prev, xn, xq8, xs8, T, n_embd, hc, ep
 
 def swiglu_q8_f32(gate, up, q32, s32, stream=None):
     call("wzyb_swiglu_q8_f32", _ptr(gate), _ptr(up), _ptr(q32), _ptr(s32), gate.numel(), _stream(stream))
+
+
+def gr_write_f32(R, blk, inj, T, n_embd, hc, stream=None):
+    """R[t,c,:] += blk[t,:] * 2*sigmoid(inj[t,c]/hc) in place (gate 1.0 with inj None)."""
+    call("wzyb_gr_write_f32", _ptr(R), _ptr(blk), _ptr(inj), T, n_embd, hc, _stream(stream))
+
+
+def hc_mix(xn, gg, mixed, mixed_f16, T, n_embd, hc, stream=None):
+    """mixed[t,:] = mean_c xn[t,c,:] * sigmoid(gg[t,c,:]); fp16 inputs may write either output."""
+    if xn.element_size() == 2:
+        call("wzyb_hc_mix_f16", _ptr(xn), _ptr(gg), _ptr(mixed), _ptr(mixed_f16), T, n_embd, hc, _stream(stream))
+    else:
+        call("wzyb_hc_mix_f32", _ptr(xn), _ptr(gg), _ptr(mixed), T, n_embd, hc, _stream(stream))
+
+
+def silu_scale_f16(lo, out, scale, stream=None):
+    call("wzyb_silu_scale_f16", _ptr(lo), _ptr(out), lo.numel(), scale, _stream(stream))
 
 
 def head_norm_rope(data, gamma, cos_tab, sin_tab, T, heads, head_dim, head_stride, row_stride, rot_dims=64,

@@ -280,6 +280,20 @@ def measure_kernels_4096(wz, torch, dev, peak, reps=60):
     g32, u32 = torch.randn(nq, generator=gen, device=dev), torch.randn(nq, generator=gen, device=dev)
     q32, s32 = torch.empty(nq, dtype=torch.int8, device=dev), torch.empty(nq // 32, device=dev)
     rows = T * HC * NE
+    # k norm + RoPE fused with the INT8 KV append (fp16 k, v [T, 2 x 256]; ring + full-context mirror)
+    KVD = KH * HD
+    kk16 = torch.randn((T, KVD), generator=gen, device=dev).half()
+    vv16 = torch.randn((T, KVD), generator=gen, device=dev).half()
+    kg16 = (0.02 * torch.randn(HD, generator=gen, device=dev)).half()
+    kv_planes = [torch.zeros((T, KVD), dtype=torch.int8, device=dev) if i % 2 == 0 else
+                 torch.zeros((T, KVD // 64), dtype=torch.int16, device=dev) for i in range(8)]
+    kvc = wz.kv_cache(*kv_planes[:4], T, T, *kv_planes[4:])  # ring of T cells: every token lands in it
+    kv_tab = (torch.empty((T, ROT // 2), device=dev), torch.empty((T, ROT // 2), device=dev))
+    wz.rope_table(kv_tab[0], kv_tab[1], T, ROT, THETA)
+    extra["k_rope_kv_append"] = (
+        lambda s: wz.k_rope_kv_append(kk16, kg16, vv16, kv_tab[0], kv_tab[1], T, KH, HD, kvc, rot_dims=ROT, eps=EPS,
+                                      w_offset=1.0, stream=s),
+        T * KVD * 2 * 3 + T * KVD * 4 + T * (KVD // 64) * 2 * 4 + HD * 2)
     extra.update({
         "gr_write_hc4": (lambda s: wz.gr_write_f32(R, blk, inj, T, NE, HC, stream=s), rows * 8 + T * NE * 4 + T * HC * 4),
         "hc_mix_hc4": (lambda s: wz.hc_mix(xn16, gg16, mx, mx16, T, NE, HC, stream=s), rows * 4 + T * NE * 6),

@@ -156,6 +156,51 @@ int wzyb_rope_table_f32(float* d_cos, float* d_sin, int64_t rows, int rot_dims, 
                         wzyb_stream_t stream);
 
 /* ============================================================================================
+ * INT8 KV-cache append, optionally fused with k's per-head RMSNorm + partial NeoX RoPE.
+ * k, v [T, kv_heads * head_dim] (kvd = kv_heads * head_dim, head_dim in {64, 128, 256}).
+ * Per 64-element group of k (after RoPE) and of v:  sh = fp16(max|x| / 127), d = float(sh),
+ *   q = d > 0 ? rint(x / d) : 0 clamped to [-127, 127]; codes [cell, kvd] int8, scales
+ *   [cell, kvd/64] fp16 (bits in uint16_t).
+ * Cells, for pos = (d_base_pos ? *d_base_pos : 0) + pos_offset + t and end = that base + T:
+ *   tokens with pos outside [0, max_ctx) are not appended;
+ *   ring: ring_cap <= 8192  -> cell pos % ring_cap, written when pos >= end - ring_cap;
+ *         ring_cap  > 8192  -> pos < 4096 (pinned sink): cell pos;
+ *                              else cell 4096 + (pos - 4096) % (ring_cap - 4096), written when
+ *                              pos >= max(4096, end - (ring_cap - 4096));
+ *   full-context mirror (all four full_* pointers, or none): cell pos.
+ * Replaces kv_append_int8_multi (src/wzy_qsa_256k.cuh:86-145 with kv_is_in_vram / kv_vram_slot at
+ * :17-29; launched at src/wzy_stage_v2.cuh:655, src/wzy_prefill_tc.cuh:878 and src/wzy_mtp.cuh:681).
+ * ========================================================================================== */
+typedef struct {
+    int8_t* ring_k_q;    /* [ring_cap, kvd]     */
+    uint16_t* ring_k_s;  /* [ring_cap, kvd/64]  */
+    int8_t* ring_v_q;
+    uint16_t* ring_v_s;
+    int8_t* full_k_q;    /* [max_ctx, kvd] or NULL */
+    uint16_t* full_k_s;
+    int8_t* full_v_q;
+    uint16_t* full_v_s;
+    int64_t ring_cap;
+    int64_t max_ctx;
+} wzyb_kv_cache;
+/* The append alone (k as given): kv_append_int8_multi. */
+int wzyb_kv_append_int8_f32(const float* k, const float* v, int64_t T, int kv_heads, int head_dim,
+                            const int32_t* d_base_pos, int64_t pos_offset, const wzyb_kv_cache* cache,
+                            wzyb_stream_t stream);
+/* k normalised and rotated in place exactly as wzyb_head_norm_rope_* (head_stride = head_dim,
+ * row_stride = kvd, gamma k_gamma), then k and v appended: the reference's k
+ * fused_head_norm_rope_multi (src/wzy_stage_v2.cuh:640-641, src/wzy_prefill_tc.cuh:864-865) and
+ * kv_append_int8_multi in one launch. */
+int wzyb_k_rope_kv_append_f32(float* k, const float* k_gamma, const float* v, const float* cos_tab,
+                              const float* sin_tab, int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset,
+                              int64_t T, int kv_heads, int head_dim, int rot_dims, float eps, float w_offset,
+                              const wzyb_kv_cache* cache, wzyb_stream_t stream);
+int wzyb_k_rope_kv_append_f16(uint16_t* k, const uint16_t* k_gamma, const uint16_t* v, const float* cos_tab,
+                              const float* sin_tab, int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset,
+                              int64_t T, int kv_heads, int head_dim, int rot_dims, float eps, float w_offset,
+                              const wzyb_kv_cache* cache, wzyb_stream_t stream);
+
+/* ============================================================================================
  * GDN output gated RMSNorm, per head of head_dim:
  *   y = ((o * rsqrt(mean(o^2) + eps)) * (w_offset + gamma[col])) / (1 + exp(-z))    (SIGMOID)
  *   y = ((o * rsqrt(mean(o^2) + eps)) * (w_offset + gamma[col])) * (z / (1 + exp(-z))) (SILU)

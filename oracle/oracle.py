@@ -32,6 +32,10 @@ _SIGS = {
     "or_hc_mix_f16": (None, [P, P, P, P, c_int64, c_int, c_int]),
     "or_hc_mix_f32": (None, [P, P, P, c_int64, c_int, c_int]),
     "or_silu_scale_f16": (None, [P, P, c_int64, c_float]),
+    "or_kv_append_int8_f32": (None, [P, P, c_int64, c_int, c_int64, P, P, P, P, P, P, P, P, c_int64, c_int64]),
+    "or_k_rope_kv_append_f16": (
+        None, [P, P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, c_int, c_float, c_float,
+               P, P, P, P, P, P, P, P, c_int64, c_int64]),
     "or_head_norm_rope_f16": (
         None, [P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, c_int64, c_int64, c_int, c_float, c_float]),
     "or_head_norm_rope_f32": (
@@ -171,6 +175,51 @@ def head_norm_rope(data, gamma, cos_tab, sin_tab, T, heads, hd, head_stride, row
     return out
 
 
+class KvCache:
+    """Host INT8 KV cache: ring [ring_cap, kvd] codes + [ring_cap, kvd/64] fp16 scale bits, and an
+    optional full-context mirror [max_ctx, ...]. Cells start zeroed."""
+
+    def __init__(self, ring_cap, max_ctx, kvd, full=True):
+        self.ring_cap, self.max_ctx, self.kvd = ring_cap, max_ctx, kvd
+        self.rkq = np.zeros((ring_cap, kvd), np.int8)
+        self.rvq = np.zeros((ring_cap, kvd), np.int8)
+        self.rks = np.zeros((ring_cap, kvd // 64), np.uint16)
+        self.rvs = np.zeros((ring_cap, kvd // 64), np.uint16)
+        self.full = full
+        if full:
+            self.fkq = np.zeros((max_ctx, kvd), np.int8)
+            self.fvq = np.zeros((max_ctx, kvd), np.int8)
+            self.fks = np.zeros((max_ctx, kvd // 64), np.uint16)
+            self.fvs = np.zeros((max_ctx, kvd // 64), np.uint16)
+
+    def args(self):
+        f = (lambda a: _p(a)) if self.full else (lambda a: None)
+        return [_p(self.rkq), _p(self.rks), _p(self.rvq), _p(self.rvs),
+                f(getattr(self, "fkq", None)), f(getattr(self, "fks", None)), f(getattr(self, "fvq", None)),
+                f(getattr(self, "fvs", None)), self.ring_cap, self.max_ctx]
+
+
+def kv_append_int8_f32(k, v, T, kvd, base_pos, cache: KvCache):
+    lib().or_kv_append_int8_f32(_p(np.ascontiguousarray(k, np.float32)), _p(np.ascontiguousarray(v, np.float32)), T,
+                                kvd, base_pos, *cache.args())
+
+
+def k_rope_kv_append(k, gamma, v, cos_tab, sin_tab, T, kv_heads, hd, rot, eps, w_offset, base_pos, cache: KvCache):
+    """k normalised + rotated (returned as a new array) and k, v appended to `cache`."""
+    kvd = kv_heads * hd
+    rows = cos_tab.shape[0] if cos_tab is not None else 0
+    if k.dtype == np.float16:
+        out = np.array(k, copy=True)
+        lib().or_k_rope_kv_append_f16(_p(out), _p(np.ascontiguousarray(gamma, np.float16)),
+                                      _p(np.ascontiguousarray(v, np.float16)), _p(cos_tab), _p(sin_tab), rows, base_pos,
+                                      T, kv_heads, hd, rot, eps, w_offset, *cache.args())
+        return out
+    out = head_norm_rope(np.ascontiguousarray(k, np.float32).reshape(-1), gamma, cos_tab, sin_tab, T, kv_heads, hd, hd,
+                         kvd, rot, eps, w_offset, base_pos)
+    kv_append_int8_f32(out, v, T, kvd, base_pos, cache)
+    return out.reshape(k.shape)
+
+
 def gdn_gated_norm(o, z, gamma, T, heads, hd=128, eps=1e-6, w_offset=0.0, gate_mode=0):
     if o.dtype == np.float16:
         y = np.empty(o.shape, dtype=np.float16)
@@ -250,6 +299,7 @@ def ref_lib() -> ctypes.CDLL:
             "ref_pf_gr_norm_fp16": [P, P, P, P, P, I, I, I, F, P],
             "ref_gr_write_multi": [P, P, P, I, I, I, P],
             "ref_pf_gr_up_mean_fp16": [P, P, P, P, I, I, P],
+            "ref_kv_append_int8_multi": [P, P, P, P, P, P, P, P, P, P, P, I, I, I, P],
             "ref_gr_up_gate_mean_pf": [P, P, P, I, I, P],
             "ref_silu_div_hc_to_fp16": [P, P, I, F, P],
             "ref_fused_head_norm_rope_multi": [P, P, P, P, P, I, I, I, I, I, F, P],

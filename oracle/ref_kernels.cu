@@ -47,6 +47,16 @@ int ref_gr_write_multi(float* R, const float* blk, const float* inj, int T, int 
     return (int)cudaGetLastError();
 }
 
+// kv_append_int8_multi (src/wzy_qsa_256k.cuh:86-145), launched as at src/wzy_stage_v2.cuh:655:
+// grid (8 groups, T) x 64 over the reference's KVD = 512.
+int ref_kv_append_int8_multi(const float* k, const float* v, signed char* vkq, unsigned short* vks, signed char* vvq,
+                             unsigned short* vvs, signed char* hkq, unsigned short* hks, signed char* hvq,
+                             unsigned short* hvs, const int* dpos, int T, int ring_cap, int max_ctx, cudaStream_t s) {
+    kv_append_int8_multi<<<dim3(8, T), 64, 0, s>>>(k, v, vkq, vks, vvq, vvs, hkq, hks, hvq, hvs, dpos, ring_cap,
+                                                   max_ctx);
+    return (int)cudaGetLastError();
+}
+
 // pf_gr_up_mean_fp16 (src/wzy_qsa_wmma.cuh:234-253), launched as at src/wzy_prefill_tc.cuh:712.
 int ref_pf_gr_up_mean_fp16(const __half* xn, const __half* gg, float* mixed, __half* mixed16, int T, int n_embd,
                            cudaStream_t s) {

@@ -272,6 +272,96 @@ void or_head_norm_rope_f32(float* data, const float* gamma, const float* cos_tab
     }
 }
 
+/* ------------------------------------------------------------------------------------------- */
+/* INT8 KV append: kv_append_int8_multi (src/wzy_qsa_256k.cuh:86-145), cells per kv_is_in_vram /  */
+/* kv_vram_slot (:17-29) with the mirror pointer the reference passes as non-NULL. Per 64 group:  */
+/* sh = fp16(max|x|/127), d = float(sh), q = d > 0 ? rint(x/d) : 0 clamped to [-127, 127].        */
+/* ------------------------------------------------------------------------------------------- */
+static int kv_in_ring(int64_t p, int64_t end, int64_t cap) {
+    if (cap <= 2 * 4096) return p >= (end - cap > 0 ? end - cap : 0);
+    if (p < 4096) return 1;
+    const int64_t lo = end - (cap - 4096);
+    return p >= (lo > 4096 ? lo : 4096);
+}
+
+static int64_t kv_ring_cell(int64_t p, int64_t cap) {
+    if (cap <= 2 * 4096) return p % cap;
+    if (p < 4096) return p;
+    return 4096 + (p - 4096) % (cap - 4096);
+}
+
+static void kv_q8_group(const float* x, int8_t* q, uint16_t* s) {
+    float am = 0.f;
+    for (int i = 0; i < 64; ++i) am = fmaxf(am, fabsf(x[i]));
+    const uint16_t sh = or_f2h(am / 127.0f);
+    const float d = or_h2f(sh);
+    for (int i = 0; i < 64; ++i) {
+        long qi = d > 0.f ? lrintf(x[i] / d) : 0;
+        q[i] = (int8_t)(qi < -127 ? -127 : qi > 127 ? 127 : qi);
+    }
+    *s = sh;
+}
+
+/* one token's fp32 k and v rows [kvd] into its cells */
+static void kv_append_token(const float* k, const float* v, int kvd, int64_t pos, int64_t end, int8_t* rkq,
+                            uint16_t* rks, int8_t* rvq, uint16_t* rvs, int8_t* fkq, uint16_t* fks, int8_t* fvq,
+                            uint16_t* fvs, int64_t ring_cap, int64_t max_ctx) {
+    if (pos < 0 || pos >= max_ctx) return;
+    const int spc = kvd / 64;
+    for (int g = 0; g < spc; ++g) {
+        int8_t qk[64], qv[64];
+        uint16_t sk, sv;
+        kv_q8_group(k + g * 64, qk, &sk);
+        kv_q8_group(v + g * 64, qv, &sv);
+        if (kv_in_ring(pos, end, ring_cap)) {
+            const int64_t c = kv_ring_cell(pos, ring_cap);
+            memcpy(rkq + c * kvd + g * 64, qk, 64);
+            memcpy(rvq + c * kvd + g * 64, qv, 64);
+            rks[c * spc + g] = sk;
+            rvs[c * spc + g] = sv;
+        }
+        if (fkq) {
+            memcpy(fkq + pos * kvd + g * 64, qk, 64);
+            memcpy(fvq + pos * kvd + g * 64, qv, 64);
+            fks[pos * spc + g] = sk;
+            fvs[pos * spc + g] = sv;
+        }
+    }
+}
+
+/* Tokens are visited in order, so a ring cell shared by two tokens keeps the later one (the      */
+/* in-window rule makes that impossible within one call).                                        */
+void or_kv_append_int8_f32(const float* k, const float* v, int64_t T, int kvd, int64_t base_pos, int8_t* rkq,
+                           uint16_t* rks, int8_t* rvq, uint16_t* rvs, int8_t* fkq, uint16_t* fks, int8_t* fvq,
+                           uint16_t* fvs, int64_t ring_cap, int64_t max_ctx) {
+    for (int64_t t = 0; t < T; ++t)
+        kv_append_token(k + t * kvd, v + t * kvd, kvd, base_pos + t, base_pos + T, rkq, rks, rvq, rvs, fkq, fks, fvq,
+                        fvs, ring_cap, max_ctx);
+}
+
+/* fp16 k and v: k normalised and rotated in fp32 (as or_head_norm_rope_f16), quantised from those  */
+/* fp32 values, and written back rounded to fp16; v widened exactly.                              */
+void or_k_rope_kv_append_f16(uint16_t* k, const uint16_t* gamma, const uint16_t* v, const float* cos_tab,
+                             const float* sin_tab, int64_t table_rows, int64_t base_pos, int64_t T, int kv_heads, int hd,
+                             int rot, float eps, float w_offset, int8_t* rkq, uint16_t* rks, int8_t* rvq, uint16_t* rvs,
+                             int8_t* fkq, uint16_t* fks, int8_t* fvq, uint16_t* fvs, int64_t ring_cap, int64_t max_ctx) {
+    const int kvd = kv_heads * hd;
+    float g[1024];
+    for (int i = 0; i < hd; ++i) g[i] = w_offset + or_h2f(gamma[i]);
+    float* kb = (float*)malloc(sizeof(float) * 2 * (size_t)kvd);
+    float* vb = kb + kvd;
+    for (int64_t t = 0; t < T; ++t) {
+        or_h2f_array(k + t * kvd, kb, kvd);
+        or_h2f_array(v + t * kvd, vb, kvd);
+        for (int h = 0; h < kv_heads; ++h)
+            head_norm_rope_row(kb + h * hd, g, cos_tab, sin_tab, table_rows, base_pos + t, hd, rot, eps);
+        for (int i = 0; i < kvd; ++i) k[t * kvd + i] = or_f2h(kb[i]);
+        kv_append_token(kb, vb, kvd, base_pos + t, base_pos + T, rkq, rks, rvq, rvs, fkq, fks, fvq, fvs, ring_cap,
+                        max_ctx);
+    }
+    free(kb);
+}
+
 /* build_rope_cos_sin_host (src/wzy_qsa_256k.cuh:33-46): inv_i = theta^(-2i/R) in fp64,        */
 /* angle = p * inv_i in fp64, cos/sin in fp64 rounded to fp32; layout [p][R/2].                 */
 void or_rope_table(float* cos_tab, float* sin_tab, int64_t rows, int rot, double theta) {

@@ -51,6 +51,14 @@ void or_head_norm_rope_f32(float* data, const float* gamma, const float* cos_tab
                            int64_t table_rows, int64_t base_pos, int64_t T, int heads, int hd, int64_t head_stride,
                            int64_t row_stride, int rot, float eps, float w_offset);
 void or_rope_table(float* cos_tab, float* sin_tab, int64_t rows, int rot, double theta);
+/* INT8 KV append (base_pos = device base + pos_offset); the full-mirror pointers may all be NULL */
+void or_kv_append_int8_f32(const float* k, const float* v, int64_t T, int kvd, int64_t base_pos, int8_t* rkq,
+                           uint16_t* rks, int8_t* rvq, uint16_t* rvs, int8_t* fkq, uint16_t* fks, int8_t* fvq,
+                           uint16_t* fvs, int64_t ring_cap, int64_t max_ctx);
+void or_k_rope_kv_append_f16(uint16_t* k, const uint16_t* gamma, const uint16_t* v, const float* cos_tab,
+                             const float* sin_tab, int64_t table_rows, int64_t base_pos, int64_t T, int kv_heads, int hd,
+                             int rot, float eps, float w_offset, int8_t* rkq, uint16_t* rks, int8_t* rvq, uint16_t* rvs,
+                             int8_t* fkq, uint16_t* fks, int8_t* fvq, uint16_t* fvs, int64_t ring_cap, int64_t max_ctx);
 /* GDN gated RMSNorm; gate_mode 0 = sigmoid(z) (reference), 1 = z*sigmoid(z) */
 void or_gdn_gated_norm_f16(const uint16_t* o, const uint16_t* z, const uint16_t* gamma, uint16_t* y, int64_t T,
                            int heads, int hd, float eps, float w_offset, int gate_mode);

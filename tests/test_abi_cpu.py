@@ -85,6 +85,21 @@ def test_argument_validation_before_any_cuda_call(wz):
     assert L.wzyb_hc_mix_f32(A16, A16, A16, 0, 2560, 4, NULL) == wz.OK
     assert L.wzyb_silu_scale_f16(A16, A16, 12, 0.25, NULL) == wz.ERR_SHAPE
     assert L.wzyb_silu_scale_f16(A16, A8, 16, 0.25, NULL) == wz.ERR_ALIGN
+    # INT8 KV append: ring planes required, the mirror all-or-none, scales 2-byte aligned
+    a = 0x10000
+    kc = ctypes.byref(wz.KvCache(a, a, a, a, None, None, None, None, 64, 128))
+    assert L.wzyb_kv_append_int8_f32(A16, A16, 4, 2, 256, None, 0, None, NULL) == wz.ERR_NULL
+    assert L.wzyb_kv_append_int8_f32(A16, A16, 4, 2, 96, None, 0, kc, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_kv_append_int8_f32(A8, A16, 4, 2, 256, None, 0, kc, NULL) == wz.ERR_ALIGN
+    assert L.wzyb_kv_append_int8_f32(A16, A16, 0, 2, 256, None, 0, kc, NULL) == wz.OK
+    part = ctypes.byref(wz.KvCache(a, a, a, a, a, None, None, None, 64, 128))
+    assert L.wzyb_kv_append_int8_f32(A16, A16, 4, 2, 256, None, 0, part, NULL) == wz.ERR_NULL
+    odd = ctypes.byref(wz.KvCache(a, a + 1, a, a, None, None, None, None, 64, 128))
+    assert L.wzyb_kv_append_int8_f32(A16, A16, 4, 2, 256, None, 0, odd, NULL) == wz.ERR_ALIGN
+    fused = L.wzyb_k_rope_kv_append_f16
+    assert fused(A16, NULL, A16, A16, A16, 64, None, 0, 4, 2, 256, 64, 1e-6, 1.0, kc, NULL) == wz.ERR_NULL
+    assert fused(A16, A16, A16, A16, A16, 64, None, 0, 4, 2, 256, 24, 1e-6, 1.0, kc, NULL) == wz.ERR_SHAPE
+    assert fused(A16, A16, A16, NULL, NULL, 64, None, 0, 4, 2, 256, 64, 1e-6, 1.0, kc, NULL) == wz.ERR_NULL
     # empty work is a no-op that succeeds without a device
     assert L.wzyb_swiglu_f16(A16, A16, A16, 0, NULL) == wz.OK
     assert L.wzyb_add_rmsnorm_f16(A16, A16, A16, A16, 0, 2048, 1e-6, 1.0, NULL) == wz.OK

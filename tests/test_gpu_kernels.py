@@ -445,3 +445,79 @@ def test_silu_scale_f16(wz, orc, n):
     out = torch.empty(n, dtype=torch.float16, device=DEV)
     wz.silu_scale_f16(dev(lo), out, 0.25)
     assert_f16_close(host(out), want, ULP_TOL, "silu_scale")
+
+
+# ---------------------------------------------------------------------------------------------
+# INT8 KV append (alone, and fused after k's norm + RoPE)
+# ---------------------------------------------------------------------------------------------
+_KV_PLANES = ["rkq", "rks", "rvq", "rvs", "fkq", "fks", "fvq", "fvs"]
+
+
+def _kv_seeded(orc, r, cap, max_ctx, kvd, full):
+    """Oracle cache pre-filled with random bytes (untouched cells must keep them) + its device copy."""
+    c = orc.KvCache(cap, max_ctx, kvd, full)
+    for nm in _KV_PLANES[: 8 if full else 4]:
+        a = getattr(c, nm)
+        a[...] = r.integers(0, 256 if a.dtype == np.int8 else 65536, a.shape).astype(a.dtype)
+    d = {nm: dev(getattr(c, nm).view(np.int16) if nm.endswith("s") else getattr(c, nm))
+         for nm in _KV_PLANES[: 8 if full else 4]}
+    return c, d
+
+
+def _kv_desc(wz, d, cap, max_ctx, full):
+    return wz.kv_cache(d["rkq"], d["rks"], d["rvq"], d["rvs"], cap, max_ctx, *(
+        (d["fkq"], d["fks"], d["fvq"], d["fvs"]) if full else ()))
+
+
+def _kv_host(d, nm):
+    a = host(d[nm])
+    return a.view(np.uint16) if nm.endswith("s") else a
+
+
+@pytest.mark.parametrize("T,heads,hd,base,cap,max_ctx,full", [
+    (7, 2, 256, 100, 64, 200, True), (300, 2, 256, 4000, 8200, 9000, True), (50, 4, 128, -5, 16, 40, False),
+    (4096, 2, 256, 0, 32768, 8192, True), (9, 3, 64, 1, 16, 64, True), (1, 2, 256, 8191, 32768, 8192, True)])
+def test_kv_append_int8_f32(wz, orc, T, heads, hd, base, cap, max_ctx, full):
+    r = rng(T + heads + cap)
+    kvd = heads * hd
+    k = r.standard_normal((T, kvd)).astype(np.float32)
+    v = (3 * r.standard_normal((T, kvd))).astype(np.float32)
+    v[0, :64] = 0.0
+    c, d = _kv_seeded(orc, r, cap, max_ctx, kvd, full)
+    orc.kv_append_int8_f32(k, v, T, kvd, base, c)
+    bp = torch.tensor([base - 3], dtype=torch.int32, device=DEV)  # device base + pos_offset 3
+    wz.kv_append_int8_f32(dev(k), dev(v), T, heads, hd, _kv_desc(wz, d, cap, max_ctx, full), d_base_pos=bp,
+                          pos_offset=3)
+    for nm in _KV_PLANES[: 8 if full else 4]:
+        assert np.array_equal(_kv_host(d, nm), getattr(c, nm)), nm
+
+
+@pytest.mark.parametrize("dtype", [np.float16, np.float32])
+@pytest.mark.parametrize("T,heads,hd,base", [(5, 2, 256, 17), (4096, 2, 256, 0), (33, 1, 128, 3)])
+def test_k_rope_kv_append_fused(wz, orc, dtype, T, heads, hd, base):
+    r = rng(T * 5 + heads + hd)
+    kvd, rot, cap, max_ctx = heads * hd, 64, 32768, 8192
+    k = r.standard_normal((T, kvd)).astype(dtype)
+    v = r.standard_normal((T, kvd)).astype(dtype)
+    gam = (0.02 * r.standard_normal(hd)).astype(dtype)
+    c_, s_, dc, ds = _rope_tab(orc, base + T + 8, rot)
+    cache, d = _kv_seeded(orc, r, cap, max_ctx, kvd, True)
+    k_ref = orc.k_rope_kv_append(k, gam, v, c_, s_, T, heads, hd, rot, 1e-6, 1.0, base, cache)
+    dk = dev(k)
+    wz.k_rope_kv_append(dk, dev(gam), dev(v), dc, ds, T, heads, hd, _kv_desc(wz, d, cap, max_ctx, True), rot_dims=rot,
+                        eps=1e-6, w_offset=1.0, pos_offset=base)
+    if dtype == np.float16:
+        assert_f16_close(host(dk).reshape(-1), k_ref.reshape(-1), ULP_TOL, "k")
+    else:
+        np.testing.assert_allclose(host(dk), k_ref.reshape(T, kvd), rtol=1e-5, atol=1e-5)
+    # v is quantised from the same values on both sides: identical
+    for nm in ["rvq", "rvs", "fvq", "fvs"]:
+        assert np.array_equal(_kv_host(d, nm), getattr(cache, nm)), nm
+    # k is quantised after the rotation, whose fp32 results differ by a few ulp: a code may sit on the
+    # other side of a rounding boundary, a scale one fp16 ulp away
+    for q, s in (("rkq", "rks"), ("fkq", "fks")):
+        dq = np.abs(_kv_host(d, q).astype(np.int32) - getattr(cache, q).astype(np.int32))
+        assert dq.max() <= 1 and (dq > 0).mean() < 2e-3, (q, dq.max(), (dq > 0).mean())
+        ds_ = np.abs(_kv_host(d, s).astype(np.int32) - getattr(cache, s).astype(np.int32))
+        assert ds_.max() <= 1, s
+    assert wz.read_faults() == 0

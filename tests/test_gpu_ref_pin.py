@@ -287,3 +287,71 @@ def test_pin_hyper_connection_residual(ref, orc, wz):
     w_lo = torch.empty_like(lo16)
     wz.silu_scale_f16(dlo, w_lo, 0.25)
     assert_f16_close(host(w_lo), r_lo, ULP_TOL, "CUDA vs reference silu_div_hc")
+
+
+def _kv_planes(ring_cap, max_ctx, kvd=512):
+    z = lambda rows, cols, dt: torch.zeros((rows, cols), dtype=dt, device=DEV)  # noqa: E731
+    return {"rkq": z(ring_cap, kvd, torch.int8), "rks": z(ring_cap, kvd // 64, torch.int16),
+            "rvq": z(ring_cap, kvd, torch.int8), "rvs": z(ring_cap, kvd // 64, torch.int16),
+            "fkq": z(max_ctx, kvd, torch.int8), "fks": z(max_ctx, kvd // 64, torch.int16),
+            "fvq": z(max_ctx, kvd, torch.int8), "fvs": z(max_ctx, kvd // 64, torch.int16)}
+
+
+def _ref_append(ref, k, v, p, dpos, T, cap, max_ctx):
+    assert ref.ref_kv_append_int8_multi(k.data_ptr(), v.data_ptr(), *(p[n].data_ptr() for n in (
+        "rkq", "rks", "rvq", "rvs", "fkq", "fks", "fvq", "fvs")), dpos.data_ptr(), T, cap, max_ctx, sp()) == 0
+
+
+@pytest.mark.parametrize("T,base,cap,max_ctx", [(300, 4000, 8200, 9000), (40, 5, 16, 40), (4096, 0, 32768, 4096)])
+def test_pin_kv_append_int8(ref, orc, wz, T, base, cap, max_ctx):
+    """kv_append_int8_multi (KVD 512 = 2 heads x 256) with the ring's sink, window and wrap, and the
+    full-context mirror: identical codes and fp16 scales."""
+    r = np.random.default_rng(210 + T)
+    k = r.standard_normal((T, 512)).astype(np.float32)
+    v = (3 * r.standard_normal((T, 512))).astype(np.float32)
+    dk, dv = dev(k), dev(v)
+    dpos = torch.tensor([base], dtype=torch.int32, device=DEV)
+    pr = _kv_planes(cap, max_ctx)
+    _ref_append(ref, dk, dv, pr, dpos, T, cap, max_ctx)
+    pm = _kv_planes(cap, max_ctx)
+    cache = wz.kv_cache(pm["rkq"], pm["rks"], pm["rvq"], pm["rvs"], cap, max_ctx, pm["fkq"], pm["fks"], pm["fvq"],
+                        pm["fvs"])
+    wz.kv_append_int8_f32(dk, dv, T, 2, 256, cache, d_base_pos=dpos)
+    oc = orc.KvCache(cap, max_ctx, 512, True)
+    orc.kv_append_int8_f32(k, v, T, 512, base, oc)
+    for nm in pr:
+        got_ref = host(pr[nm])
+        assert np.array_equal(host(pm[nm]), got_ref), f"CUDA vs reference {nm}"
+        want = getattr(oc, nm)
+        assert np.array_equal(got_ref.view(want.dtype), want), f"oracle vs reference {nm}"
+
+
+def test_pin_k_rope_kv_append(ref, orc, wz):
+    """The reference's k fused_head_norm_rope_multi + kv_append_int8_multi vs the one fused launch."""
+    r = np.random.default_rng(211)
+    T, base, cap, max_ctx = 64, 4090, 32768, 8192
+    k = r.standard_normal((T, 512)).astype(np.float32)
+    v = r.standard_normal((T, 512)).astype(np.float32)
+    gam = (0.02 * r.standard_normal(256)).astype(np.float32)
+    g32 = (np.float32(1.0) + gam).astype(np.float32)
+    c, s = orc.ref_rope_table(base + T + 8, 1e7)
+    dc, ds = dev(c), dev(s)
+    dpos = torch.tensor([base], dtype=torch.int32, device=DEV)
+    dk, dv = dev(k), dev(v)
+    assert ref.ref_fused_head_norm_rope_multi(dk.data_ptr(), dev(g32).data_ptr(), dc.data_ptr(), ds.data_ptr(),
+                                              dpos.data_ptr(), T, 2, 256, 256, 512, 1e-6, sp()) == 0
+    pr = _kv_planes(cap, max_ctx)
+    _ref_append(ref, dk, dv, pr, dpos, T, cap, max_ctx)
+    mk = dev(k)
+    pm = _kv_planes(cap, max_ctx)
+    cache = wz.kv_cache(pm["rkq"], pm["rks"], pm["rvq"], pm["rvs"], cap, max_ctx, pm["fkq"], pm["fks"], pm["fvq"],
+                        pm["fvs"])
+    wz.k_rope_kv_append(mk, dev(gam), dv, dc, ds, T, 2, 256, cache, rot_dims=64, eps=1e-6, w_offset=1.0,
+                        d_base_pos=dpos)
+    np.testing.assert_allclose(host(mk), host(dk), rtol=1e-5, atol=2e-6)
+    for nm in ("rvq", "rvs", "fvq", "fvs"):
+        assert np.array_equal(host(pm[nm]), host(pr[nm])), nm
+    for q, sc in (("rkq", "rks"), ("fkq", "fks")):
+        d = np.abs(host(pm[q]).astype(np.int32) - host(pr[q]).astype(np.int32))
+        assert d.max() <= 1 and (d > 0).mean() < 2e-3
+        assert np.abs(host(pm[sc]).astype(np.int32) - host(pr[sc]).astype(np.int32)).max() <= 1

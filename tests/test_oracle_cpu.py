@@ -209,6 +209,56 @@ def test_q8_paths_against_numpy(orc):
     assert s[0] == 0 and not q[:32].any()
 
 
+def _np_kv_q8(x):
+    """64-element groups: fp16 scale of max/127, codes rint(x / scale) clamped to +-127."""
+    g = x.reshape(-1, 64).astype(np.float32)
+    sh = (np.abs(g).max(axis=1) / np.float32(127.0)).astype(np.float32).astype(np.float16)
+    d = sh.astype(np.float32)
+    safe = np.where(d > 0, d, np.float32(1.0))
+    q = np.where(d[:, None] > 0, np.clip(np.rint(g / safe[:, None]), -127, 127), 0).astype(np.int8)
+    return q.reshape(x.shape), sh.view(np.uint16).reshape(x.shape[:-1] + (x.shape[-1] // 64,))
+
+
+def _np_ring_cell(p, end, cap):
+    if cap <= 8192:
+        return (p % cap) if p >= max(0, end - cap) else None
+    if p < 4096:
+        return p
+    return 4096 + (p - 4096) % (cap - 4096) if p >= max(4096, end - (cap - 4096)) else None
+
+
+@pytest.mark.parametrize("T,base,cap,max_ctx,full", [(40, 5, 16, 40, True), (10, 4090, 8200, 9000, True),
+                                                     (5000, 20000, 8200, 30000, False), (6, -3, 64, 100, True)])
+def test_kv_append_against_numpy(orc, T, base, cap, max_ctx, full):
+    r = np.random.default_rng(T + cap)
+    kvd = 128
+    k = r.standard_normal((T, kvd)).astype(np.float32)
+    v = (3 * r.standard_normal((T, kvd))).astype(np.float32)
+    v[0, :64] = 0.0  # an all-zero group: scale 0, codes 0
+    c = orc.KvCache(cap, max_ctx, kvd, full)
+    orc.kv_append_int8_f32(k, v, T, kvd, base, c)
+    w = orc.KvCache(cap, max_ctx, kvd, full)
+    kq, ks = _np_kv_q8(k)
+    vq, vs = _np_kv_q8(v)
+    for t in range(T):
+        p = base + t
+        if p < 0 or p >= max_ctx:
+            continue
+        cell = _np_ring_cell(p, base + T, cap)
+        if cell is not None:
+            w.rkq[cell], w.rks[cell], w.rvq[cell], w.rvs[cell] = kq[t], ks[t], vq[t], vs[t]
+        if full:
+            w.fkq[p], w.fks[p], w.fvq[p], w.fvs[p] = kq[t], ks[t], vq[t], vs[t]
+    names = ["rkq", "rks", "rvq", "rvs"] + (["fkq", "fks", "fvq", "fvs"] if full else [])
+    for nm in names:
+        assert np.array_equal(getattr(c, nm), getattr(w, nm)), nm
+    # past the sink, only the last (ring_cap - 4096) positions of the call land in the ring, and the
+    # pinned sink cells stay untouched
+    if cap > 8192 and base >= 4096:
+        assert not c.rks[:4096].any()
+        assert np.count_nonzero(c.rks[4096:, 0]) == min(T, cap - 4096)
+
+
 def test_hyper_connection_residual_against_float64(orc):
     r = np.random.default_rng(41)
     T, n, hc = 6, 80, 4

@@ -1,0 +1,274 @@
+// kv_append.cu -- k per-head RMSNorm + partial NeoX RoPE fused with the INT8 KV-cache append.
+//
+// The reference appends in three launches per layer: fused_head_norm_rope_multi on k
+// (src/wzy_stage_v2.cuh:640-641, src/wzy_prefill_tc.cuh:864-865), then kv_append_int8_multi
+// (src/wzy_qsa_256k.cuh:86-145, launched at src/wzy_stage_v2.cuh:655 and src/wzy_prefill_tc.cuh:878),
+// which re-reads k and v, one 64-thread block per (64-element group, token). Here one warp owns a
+// token: it loads the token's k and v heads once, normalises and rotates k (written back in place),
+// and quantises both into the cache:
+//   per 64-element group  sh = fp16(max|x| / 127),  d = float(sh),  q = d > 0 ? rint(x / d) : 0,
+//   q clamped to [-127, 127]; codes [cell, kvd] int8, scales [cell, kvd/64] fp16.
+// A 64-element group is 8 consecutive lanes (8 elements each); its max is three xor shuffles.
+// Cells (restating kv_is_in_vram / kv_vram_slot, src/wzy_qsa_256k.cuh:17-29, with the mirror pointer
+// the reference always passes as non-NULL):
+//   pos = base_pos + pos_offset + t; tokens with pos outside [0, max_ctx) are not appended;
+//   ring (device) cell: ring_cap <= 2*4096: pos % ring_cap, written when pos >= end - ring_cap;
+//                       else pos < 4096 (pinned sink): pos, always written;
+//                            else 4096 + (pos - 4096) % (ring_cap - 4096), written when
+//                            pos >= max(4096, end - (ring_cap - 4096));
+//   end = base_pos + pos_offset + T (one past this call's last position), so a call never writes two
+//   of its own tokens into one ring cell; full-context mirror cell: pos (when the mirror is given).
+#include "launch.hpp"
+#include "common.cuh"
+
+namespace wzyb {
+
+constexpr int kKvSinkPin = 4096;
+constexpr int kKvGroup = 64;
+
+struct KvAppendArgs {
+    void* k;              // [T, kv_heads * HD] (normed + rotated in place when norm_rope)
+    const void* k_gamma;  // [HD]
+    const void* v;        // [T, kv_heads * HD]
+    const float* cos_tab;
+    const float* sin_tab;
+    int64_t table_rows;
+    const int32_t* d_base_pos;
+    int64_t pos_offset;
+    int64_t T;
+    int kv_heads;
+    int rot;
+    float eps;
+    float w_offset;
+    int norm_rope;
+    wzyb_kv_cache c;
+};
+
+__device__ __forceinline__ bool kv_in_ring(int64_t p, int64_t end, int64_t cap) {
+    if (cap <= 2 * kKvSinkPin) return p >= (end - cap > 0 ? end - cap : 0);
+    if (p < kKvSinkPin) return true;
+    const int64_t lo = end - (cap - kKvSinkPin);
+    return p >= (lo > kKvSinkPin ? lo : kKvSinkPin);
+}
+
+__device__ __forceinline__ int64_t kv_ring_cell(int64_t p, int64_t cap) {
+    if (cap <= 2 * kKvSinkPin) return p % cap;
+    if (p < kKvSinkPin) return p;
+    return kKvSinkPin + (p - kKvSinkPin) % (cap - kKvSinkPin);
+}
+
+// Quantise this lane's 8 elements as part of its 64-element group (lanes 8m..8m+7) and store the codes
+// (and, from the group's first lane, the fp16 scale) to up to two cells. Every lane must call it.
+__device__ __forceinline__ void kv_q8_store(const float2 (&x)[4], bool act, int lane, int8_t* q0, uint16_t* s0,
+                                            int8_t* q1, uint16_t* s1) {
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) am = fmaxf(am, fmaxf(fabsf(x[i].x), fabsf(x[i].y)));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
+    if (!act) return;
+    const __half sh = __float2half_rn(am / 127.0f);
+    const float d = __half2float(sh);
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float v = (i & 1) ? x[i >> 1].y : x[i >> 1].x;
+        const int qi = d > 0.f ? max(-127, min(127, __float2int_rn(v / d))) : 0;
+        w[i >> 2] |= ((uint32_t)(qi & 0xFF)) << ((i & 3) * 8);
+    }
+    const uint2 packed = make_uint2(w[0], w[1]);
+    const uint16_t sbits = __half_as_ushort(sh);
+    const bool first = (lane & 7) == 0;
+    if (q0 != nullptr) {
+        *reinterpret_cast<uint2*>(q0) = packed;
+        if (first) *s0 = sbits;
+    }
+    if (q1 != nullptr) {
+        *reinterpret_cast<uint2*>(q1) = packed;
+        if (first) *s1 = sbits;
+    }
+}
+
+// One warp per token. HD/8 lanes per head, 32/(HD/8) heads side by side; the token's heads are
+// visited in rounds of that many. k and v of a round are loaded together (4 x 16 B per lane in
+// flight for fp32) before any arithmetic.
+template <typename T, int HD>
+__global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
+    constexpr int L = HD / 8;
+    constexpr int HPW = 32 / L;
+    const int lane = threadIdx.x & 31;
+    const int li = lane % L, hw = lane / L;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int kvd = a.kv_heads * HD;
+    const int spc = kvd / kKvGroup;  // scales per cell
+    const int half = a.rot / 2, hl = half / 8;
+    const bool rot_lane = li < 2 * hl, first_half = li < hl;
+    const int src = rot_lane ? (first_half ? lane + hl : lane - hl) : lane;
+    const int ci = (first_half ? li : li - hl) * 8;
+    const int64_t base = (a.d_base_pos ? (int64_t)__ldg(a.d_base_pos) : 0) + a.pos_offset;
+    const int64_t end = base + a.T;
+    const int rounds = (a.kv_heads + HPW - 1) / HPW;
+    T* const kd = static_cast<T*>(a.k);
+    const T* const vd = static_cast<const T*>(a.v);
+
+    float2 g[2][4];  // g[1]: k gamma (+ offset) of this lane's 8 dims; g[0] unused
+#pragma unroll
+    for (int i = 0; i < 4; ++i) g[0][i] = g[1][i] = splat2(0.f);
+    if (a.norm_rope) {
+        Vec8<T>::load_ro2(static_cast<const T*>(a.k_gamma) + li * 8, g[1]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) g[1][i] = fadd2(splat2(a.w_offset), g[1][i]);
+    }
+
+    for (int64_t t = gwarp; t < a.T; t += nwarps) {
+        const int64_t pos = base + t;
+        const bool keep = pos >= 0 && pos < a.c.max_ctx;
+        const bool ring = keep && kv_in_ring(pos, end, a.c.ring_cap);
+        const int64_t rcell = ring ? kv_ring_cell(pos, a.c.ring_cap) : 0;
+        const bool full = keep && a.c.full_k_q != nullptr;
+        const bool pos_ok = half > 0 && pos >= 0 && pos < a.table_rows;
+        float2 c2[4], s2[4];
+        if (a.norm_rope) {
+            if (pos_ok && rot_lane) {
+                Vec8<float>::load_ro2(a.cos_tab + pos * half + ci, c2);
+                Vec8<float>::load_ro2(a.sin_tab + pos * half + ci, s2);
+                if (first_half) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) s2[i] = make_float2(-s2[i].x, -s2[i].y);
+                }
+            }
+            if (half > 0 && !pos_ok && lane == 0) raise_fault(WZYB_FAULT_POS_RANGE);
+        }
+        for (int r = 0; r < rounds; ++r) {
+            const int h = r * HPW + hw;
+            const bool act = h < a.kv_heads;
+            const int64_t off = t * kvd + h * HD + li * 8;
+            float2 p[4], v[4];
+            if (act) {
+                const typename Vec8<T>::Raw kr = Vec8<T>::ldcs_raw(kd + off);
+                const typename Vec8<T>::Raw vr = Vec8<T>::ldcs_raw(vd + off);
+                Vec8<T>::cvt2(kr, p);
+                Vec8<T>::cvt2(vr, v);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) p[i] = v[i] = splat2(0.f);
+            }
+            if (a.norm_rope) {
+                // p *= rsqrt(mean(p^2) + eps) * gamma, then the pair rotation (one shuffle per element)
+                const float ss = group_sum<L>(sumsq8(p));
+                const float2 sc = splat2(rsqrt_approx(ss / (float)HD + a.eps));
+#pragma unroll
+                for (int i = 0; i < 4; ++i) p[i] = fmul2(p[i], fmul2(sc, g[1][i]));
+                float2 q[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    q[i].x = __shfl_sync(0xffffffffu, p[i].x, src);
+                    q[i].y = __shfl_sync(0xffffffffu, p[i].y, src);
+                }
+                if (pos_ok && rot_lane) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) p[i] = ffma2(q[i], s2[i], fmul2(p[i], c2[i]));
+                }
+                if (act) Vec8<T>::store2(kd + off, p);
+            }
+            if (keep) {  // warp-uniform
+                const int col = h * HD + li * 8;
+                const int sc_i = col / kKvGroup;
+                kv_q8_store(p, act, lane, ring ? a.c.ring_k_q + rcell * kvd + col : nullptr,
+                            a.c.ring_k_s + rcell * spc + sc_i, full ? a.c.full_k_q + pos * kvd + col : nullptr,
+                            full ? a.c.full_k_s + pos * spc + sc_i : nullptr);
+                kv_q8_store(v, act, lane, ring ? a.c.ring_v_q + rcell * kvd + col : nullptr,
+                            a.c.ring_v_s + rcell * spc + sc_i, full ? a.c.full_v_q + pos * kvd + col : nullptr,
+                            full ? a.c.full_v_s + pos * spc + sc_i : nullptr);
+            }
+        }
+    }
+}
+
+template <typename T>
+static int launch_kv_append(const KvAppendArgs& a0, int head_dim, cudaStream_t stream) {
+    const KvAppendArgs& a = a0;
+    const wzyb_kv_cache& c = a.c;
+    if (!a.k || !a.v || !c.ring_k_q || !c.ring_k_s || !c.ring_v_q || !c.ring_v_s) return WZYB_ERR_NULL;
+    const bool has_full = c.full_k_q || c.full_k_s || c.full_v_q || c.full_v_s;
+    if (has_full && !(c.full_k_q && c.full_k_s && c.full_v_q && c.full_v_s)) return WZYB_ERR_NULL;
+    if (a.norm_rope && (!a.k_gamma || (a.rot > 0 && (!a.cos_tab || !a.sin_tab)))) return WZYB_ERR_NULL;
+    if (a.T < 0 || a.T > (int64_t(1) << 40) || a.kv_heads < 1 || a.kv_heads > 64 ||
+        (head_dim != 64 && head_dim != 128 && head_dim != 256) || c.ring_cap < 1 || c.max_ctx < 0)
+        return WZYB_ERR_SHAPE;
+    if (a.norm_rope && (a.rot < 0 || a.rot > head_dim || (a.rot % 16) != 0 || a.table_rows < 0)) return WZYB_ERR_SHAPE;
+    if (!aligned16(a.k) || !aligned16(a.v) || (a.norm_rope && !aligned16(a.k_gamma)) || !aligned16(c.ring_k_q) ||
+        !aligned16(c.ring_v_q) || (has_full && (!aligned16(c.full_k_q) || !aligned16(c.full_v_q))) ||
+        (a.norm_rope && a.rot > 0 && (!aligned16(a.cos_tab) || !aligned16(a.sin_tab))))
+        return WZYB_ERR_ALIGN;
+    if (((uintptr_t)c.ring_k_s | (uintptr_t)c.ring_v_s | (uintptr_t)c.full_k_s | (uintptr_t)c.full_v_s) & 1)
+        return WZYB_ERR_ALIGN;
+    if (a.T == 0) return WZYB_OK;
+    DeviceInfo di;
+    const int rc = device_info(&di);
+    if (rc != WZYB_OK) return rc;
+    const int grid = persistent_grid(di, 8, (a.T + 7) / 8);
+    switch (head_dim) {
+        case 64: kv_append_kernel<T, 64><<<grid, 256, 0, stream>>>(a); break;
+        case 128: kv_append_kernel<T, 128><<<grid, 256, 0, stream>>>(a); break;
+        default: kv_append_kernel<T, 256><<<grid, 256, 0, stream>>>(a); break;
+    }
+    return launch_status();
+}
+
+template <typename T>
+static int kv_append_entry(T* k, const T* k_gamma, const T* v, const float* cos_tab, const float* sin_tab,
+                           int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset, int64_t T_, int kv_heads,
+                           int head_dim, int rot_dims, float eps, float w_offset, int norm_rope,
+                           const wzyb_kv_cache* cache, cudaStream_t stream) {
+    if (cache == nullptr) return WZYB_ERR_NULL;
+    KvAppendArgs a;
+    a.k = k;
+    a.k_gamma = k_gamma;
+    a.v = v;
+    a.cos_tab = cos_tab;
+    a.sin_tab = sin_tab;
+    a.table_rows = table_rows;
+    a.d_base_pos = d_base_pos;
+    a.pos_offset = pos_offset;
+    a.T = T_;
+    a.kv_heads = kv_heads;
+    a.rot = norm_rope ? rot_dims : 0;
+    a.eps = eps;
+    a.w_offset = w_offset;
+    a.norm_rope = norm_rope;
+    a.c = *cache;
+    return launch_kv_append<T>(a, head_dim, stream);
+}
+
+}  // namespace wzyb
+
+extern "C" {
+
+int wzyb_kv_append_int8_f32(const float* k, const float* v, int64_t T, int kv_heads, int head_dim,
+                            const int32_t* d_base_pos, int64_t pos_offset, const wzyb_kv_cache* cache,
+                            wzyb_stream_t stream) {
+    return wzyb::kv_append_entry<float>(const_cast<float*>(k), nullptr, v, nullptr, nullptr, 0, d_base_pos, pos_offset,
+                                        T, kv_heads, head_dim, 0, 0.f, 0.f, 0, cache, (cudaStream_t)stream);
+}
+
+int wzyb_k_rope_kv_append_f32(float* k, const float* k_gamma, const float* v, const float* cos_tab,
+                              const float* sin_tab, int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset,
+                              int64_t T, int kv_heads, int head_dim, int rot_dims, float eps, float w_offset,
+                              const wzyb_kv_cache* cache, wzyb_stream_t stream) {
+    return wzyb::kv_append_entry<float>(k, k_gamma, v, cos_tab, sin_tab, table_rows, d_base_pos, pos_offset, T,
+                                        kv_heads, head_dim, rot_dims, eps, w_offset, 1, cache, (cudaStream_t)stream);
+}
+
+int wzyb_k_rope_kv_append_f16(uint16_t* k, const uint16_t* k_gamma, const uint16_t* v, const float* cos_tab,
+                              const float* sin_tab, int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset,
+                              int64_t T, int kv_heads, int head_dim, int rot_dims, float eps, float w_offset,
+                              const wzyb_kv_cache* cache, wzyb_stream_t stream) {
+    return wzyb::kv_append_entry<__half>((__half*)k, (const __half*)k_gamma, (const __half*)v, cos_tab, sin_tab,
+                                         table_rows, d_base_pos, pos_offset, T, kv_heads, head_dim, rot_dims, eps,
+                                         w_offset, 1, cache, (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -7,3 +7,4 @@
 #include "swiglu.cu"
 #include "gather.cu"
 #include "hc_stream.cu"
+#include "kv_append.cu"

@@ -33,6 +33,22 @@ class WzybError(RuntimeError):
         self.code = code
 
 
+class KvCache(ctypes.Structure):
+    """wzyb_kv_cache: INT8 ring (and optional full-context mirror) codes and fp16 scale bits."""
+    _fields_ = [
+        ("ring_k_q", c_void_p),
+        ("ring_k_s", c_void_p),
+        ("ring_v_q", c_void_p),
+        ("ring_v_s", c_void_p),
+        ("full_k_q", c_void_p),
+        ("full_k_s", c_void_p),
+        ("full_v_q", c_void_p),
+        ("full_v_s", c_void_p),
+        ("ring_cap", c_int64),
+        ("max_ctx", c_int64),
+    ]
+
+
 class HeadTensor(ctypes.Structure):
     _fields_ = [
         ("data", c_void_p),
@@ -95,6 +111,15 @@ _SIGS = {
     "wzyb_hc_mix_f16": (c_int, [P, P, P, P, c_int64, c_int, c_int, S]),
     "wzyb_hc_mix_f32": (c_int, [P, P, P, c_int64, c_int, c_int, S]),
     "wzyb_silu_scale_f16": (c_int, [P, P, c_int64, c_float, S]),
+    "wzyb_kv_append_int8_f32": (c_int, [P, P, c_int64, c_int, c_int, P, c_int64, POINTER(KvCache), S]),
+    "wzyb_k_rope_kv_append_f32": (
+        c_int,
+        [P, P, P, P, P, c_int64, P, c_int64, c_int64, c_int, c_int, c_int, c_float, c_float, POINTER(KvCache), S],
+    ),
+    "wzyb_k_rope_kv_append_f16": (
+        c_int,
+        [P, P, P, P, P, c_int64, P, c_int64, c_int64, c_int, c_int, c_int, c_float, c_float, POINTER(KvCache), S],
+    ),
     "wzyb_head_norm_rope_f16": (
         c_int,
         [P, P, P, P, c_int64, P, c_int64, c_int64, c_int, c_int, c_int64, c_int64, c_int, c_float, c_float, S],
@@ -236,6 +261,27 @@ def qk_norm_rope_f16(q: HeadTensor, k: HeadTensor | None, cos_tab, sin_tab, T, h
     rows = cos_tab.numel() // max(1, rot_dims // 2)
     call("wzyb_qk_norm_rope_f16", ctypes.byref(q), ctypes.byref(k) if k is not None else None, _ptr(cos_tab),
          _ptr(sin_tab), rows, _ptr(d_base_pos), pos_offset, T, head_dim, rot_dims, eps, w_offset, _stream(stream))
+
+
+def kv_cache(ring_k_q, ring_k_s, ring_v_q, ring_v_s, ring_cap, max_ctx, full_k_q=None, full_k_s=None, full_v_q=None,
+             full_v_s=None) -> KvCache:
+    """Cache descriptor from device tensors (scales: int16/uint16 tensors holding fp16 bits)."""
+    return KvCache(ring_k_q.data_ptr(), ring_k_s.data_ptr(), ring_v_q.data_ptr(), ring_v_s.data_ptr(),
+                   _ptr(full_k_q).value, _ptr(full_k_s).value, _ptr(full_v_q).value, _ptr(full_v_s).value, ring_cap,
+                   max_ctx)
+
+
+def kv_append_int8_f32(k, v, T, kv_heads, head_dim, cache: KvCache, d_base_pos=None, pos_offset=0, stream=None):
+    call("wzyb_kv_append_int8_f32", _ptr(k), _ptr(v), T, kv_heads, head_dim, _ptr(d_base_pos), pos_offset,
+         ctypes.byref(cache), _stream(stream))
+
+
+def k_rope_kv_append(k, k_gamma, v, cos_tab, sin_tab, T, kv_heads, head_dim, cache: KvCache, rot_dims=64, eps=1e-6,
+                     w_offset=0.0, d_base_pos=None, pos_offset=0, stream=None):
+    fn = "wzyb_k_rope_kv_append_f16" if k.element_size() == 2 else "wzyb_k_rope_kv_append_f32"
+    rows = cos_tab.numel() // max(1, rot_dims // 2) if cos_tab is not None else 0
+    call(fn, _ptr(k), _ptr(k_gamma), _ptr(v), _ptr(cos_tab), _ptr(sin_tab), rows, _ptr(d_base_pos), pos_offset, T,
+         kv_heads, head_dim, rot_dims, eps, w_offset, ctypes.byref(cache), _stream(stream))
 
 
 def rope_table(cos_tab, sin_tab, rows, rot_dims=64, theta=1e7, stream=None):

@@ -294,6 +294,23 @@ def measure_kernels_4096(wz, torch, dev, peak, reps=60):
         lambda s: wz.k_rope_kv_append(kk16, kg16, vv16, kv_tab[0], kv_tab[1], T, KH, HD, kvc, rot_dims=ROT, eps=EPS,
                                       w_offset=1.0, stream=s),
         T * KVD * 2 * 3 + T * KVD * 4 + T * (KVD // 64) * 2 * 4 + HD * 2)
+    # the reference model's PLE: full fp8 table (320,001,446 rows x 160 B = 51.2 GB) by its n-gram hash,
+    # then the gate and the causal conv at the block's widths (n_embd 2560 x 4 streams, HCD 10240)
+    ple8_hash = wz.ple_fp8_hash()
+    ple8 = torch.randint(0, 256, (320001446, 160), generator=gen, device=dev, dtype=torch.uint8)
+    ple8_out = torch.empty((T, 2560), device=dev)
+    pk = torch.randn((T * HC, NE), generator=gen, device=dev)
+    pq = torch.randn((T * HC, NE), generator=gen, device=dev)
+    pgv = torch.empty((T * HC, NE), device=dev)
+    pcw = 0.5 * torch.randn((HC * NE, 4), generator=gen, device=dev)
+    phist = torch.randn((HC * NE, 9), generator=gen, device=dev)
+    extra["ple_gather_fp8"] = (
+        lambda s: wz.ple_gather_fp8_f32(ple8, 160, 0.5, ple8_hash, ids, ple8_out, stream=s),
+        T * 16 * 160 + T * 2560 * 4 + T * 4)
+    extra["ple_gate_hc4"] = (lambda s: wz.ple_gate_f32(pk, pq, blk, pgv, T, NE, HC, stream=s),
+                             rows * 12 + T * NE * 4)
+    extra["ple_conv"] = (lambda s: wz.ple_conv_f32(xn32, pcw, phist, pgv, R, T, HC * NE, stream=s),
+                         rows * 16 + HC * NE * (4 + 9 + 9) * 4)
     extra.update({
         "gr_write_hc4": (lambda s: wz.gr_write_f32(R, blk, inj, T, NE, HC, stream=s), rows * 8 + T * NE * 4 + T * HC * 4),
         "hc_mix_hc4": (lambda s: wz.hc_mix(xn16, gg16, mx, mx16, T, NE, HC, stream=s), rows * 4 + T * NE * 6),
@@ -343,7 +360,7 @@ def measure_kernels_4096(wz, torch, dev, peak, reps=60):
         res[name] = {"us": round(us, 2), "bytes": int(nbytes), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
                      "frac_of_8tbs": round(gbs / NOMINAL_HBM_GBS, 4), "copy_us": round(copy_us, 2),
                      "frac_of_copy": round(copy_us / us, 4)}
-    del table, ple_tabs, flush, flush_r, R, blk, xn16, gg16, xn32, g32, u32
+    del table, ple_tabs, flush, flush_r, R, blk, xn16, gg16, xn32, g32, u32, ple8, pk, pq, pgv
     return res
 
 

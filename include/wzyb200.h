@@ -268,6 +268,40 @@ int wzyb_ple_gather_f16(const uint16_t* const* tables, int heads, int64_t rows_p
                         const int32_t* ids, int64_t T, const int32_t* prev_ids, int32_t eos_id, int hash_variant,
                         uint16_t* out, wzyb_stream_t stream);
 
+/* ============================================================================================
+ * PLE in the reference model's own format and its downstream block.
+ * ========================================================================================== */
+/* 2-gram / 3-gram u64 hash: for token t with history cut as above (c0 = id[t], c1, c2):
+ *   m2 = c0*mult[0] ^ c1*mult[1];  m3 = m2 ^ c2*mult[2]       (u64 wrap; c0 sign-extended)
+ *   head h < 8: row = (uint32)(m2 % vocab[h] + off[h]);  h >= 8: (uint32)(m3 % vocab[h] + off[h]) */
+typedef struct {
+    uint64_t mult[3];
+    uint64_t vocab[16];
+    uint64_t off[16];
+} wzyb_ple_fp8_hash;
+/* The reference's constants (stage_ple_window, src/wzy_engine_v2.cu:909-916): 320,001,446 rows. */
+int wzyb_ple_fp8_reference_hash(wzyb_ple_fp8_hash* out);
+/* out[t, h*row_bytes + i] = e4m3(table[row_h, i]) * scale, fp32 [T, 16*row_bytes]; the e4m3 NaN codes
+ * (0x7F, 0xFF) read as signed zero. table [table_rows, row_bytes] fp8 e4m3 bytes, row_bytes % 16 == 0
+ * (the reference's 160); every off[h] + vocab[h] <= table_rows; prev_ids as wzyb_ple_gather_f16.
+ * Replaces stage_ple_window / stage_emb_ple_pf (src/wzy_engine_v2.cu:943-978, :1210-1265) with
+ * PleSrc's row decode (src/wzy_stage_v2.cuh:215-324) and the H2D copy of the staged rows. */
+int wzyb_ple_gather_fp8_f32(const uint8_t* table, int64_t table_rows, int row_bytes, float scale,
+                            const wzyb_ple_fp8_hash* hash, const int32_t* ids, int64_t T, const int32_t* prev_ids,
+                            int32_t eos_id, float* out, wzyb_stream_t stream);
+/* gv[t,c,:] = value[t,:] * 1/(1 + exp(-s * sqrt(max(|d|, 1e-6)))), d = dot(key[t,c,:], query[t,c,:]) /
+ * sqrt(n_embd), s = sign(d) (+1 at 0). key, query, gv [T, hc, n_embd]; value [T, n_embd]; fp32.
+ * ple_gate_gv_multi (src/wzy_kernels_v2.cuh:1321-1346, launched at src/wzy_stage_v2.cuh:592). */
+int wzyb_ple_gate_f32(const float* key, const float* query, const float* value, float* gv, int64_t T, int n_embd,
+                      int hc, wzyb_stream_t stream);
+/* Causal 4-tap conv of dilation 3 per channel c < hcd over x(s) = norm[s, c] (s >= 0) or
+ * hist[c, 9 + s] (-9 <= s < 0):  acc = cw[c,0]*x(t-9) + cw[c,1]*x(t-6) + cw[c,2]*x(t-3) + cw[c,3]*x(t);
+ * R[t,c] += gv[t,c] + acc / (1 + exp(-acc)); afterwards hist[c, i] = x(T - 9 + i). With hist_snaps
+ * (or NULL), hist_snaps[t, c, 0..8] = x(t-8..t). norm, gv, R [T, hcd]; cw [hcd, 4]; hist [hcd, 9].
+ * ple_conv_multi (src/wzy_kernels_v2.cuh:1348-1373, launched at src/wzy_stage_v2.cuh:594). */
+int wzyb_ple_conv_f32(const float* norm, const float* cw, float* hist, const float* gv, float* R, int64_t T, int hcd,
+                      float* hist_snaps, wzyb_stream_t stream);
+
 /* Host restatement of the row index (for halos, tests and callers that stage on the host). */
 uint32_t wzyb_ple_row_index(int32_t t0, int32_t t1, int32_t t2, int head, int64_t rows_per_table,
                             int32_t eos_id, int hash_variant);

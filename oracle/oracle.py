@@ -33,6 +33,10 @@ _SIGS = {
     "or_hc_mix_f32": (None, [P, P, P, c_int64, c_int, c_int]),
     "or_silu_scale_f16": (None, [P, P, c_int64, c_float]),
     "or_kv_append_int8_f32": (None, [P, P, c_int64, c_int, c_int64, P, P, P, P, P, P, P, P, c_int64, c_int64]),
+    "or_ple_fp8_row": (c_uint32, [c_int32, c_int32, c_int32, c_int, P, P, P, c_int32]),
+    "or_ple_gather_fp8_f32": (None, [P, c_int, c_float, P, P, P, P, c_int64, POINTER(c_int32), c_int32, P]),
+    "or_ple_gate_f32": (None, [P, P, P, P, c_int64, c_int, c_int]),
+    "or_ple_conv_f32": (None, [P, P, P, P, P, c_int64, c_int, P]),
     "or_k_rope_kv_append_f16": (
         None, [P, P, P, P, P, c_int64, c_int64, c_int64, c_int, c_int, c_int, c_float, c_float,
                P, P, P, P, P, P, P, P, c_int64, c_int64]),
@@ -278,6 +282,54 @@ def ple_gather_f16(tables, ids, prev_ids=None, eos=248044, variant=0):
     return out
 
 
+class PleFp8Hash:
+    """mult[3], vocab[16], off[16] as uint64 arrays (the reference's by default)."""
+
+    REF_VOCAB = [20000003, 20000023, 20000033, 20000047, 20000059, 20000063, 20000069, 20000077,
+                 20000081, 20000093, 20000107, 20000147, 20000153, 20000159, 20000161, 20000171]
+    REF_MULT = [23703573157769, 20109073645365, 8052911324071]
+
+    def __init__(self, vocab=None, mult=None):
+        self.vocab = np.array(vocab if vocab is not None else self.REF_VOCAB, dtype=np.uint64)
+        self.mult = np.array(mult if mult is not None else self.REF_MULT, dtype=np.uint64)
+        self.off = np.concatenate([[0], np.cumsum(self.vocab)[:-1]]).astype(np.uint64)
+
+    @property
+    def rows(self):
+        return int(self.off[-1] + self.vocab[-1])
+
+
+def ple_fp8_row(cur, p1, p0, h, hsh: PleFp8Hash, eos=248044):
+    return lib().or_ple_fp8_row(cur, p1, p0, h, _p(hsh.mult), _p(hsh.vocab), _p(hsh.off), eos)
+
+
+def ple_gather_fp8_f32(table, row_bytes, scale, hsh: PleFp8Hash, ids, prev_ids=None, eos=248044):
+    ids = np.ascontiguousarray(ids, np.int32)
+    prev = (c_int32 * 2)(*prev_ids) if prev_ids is not None else None
+    out = np.empty((ids.size, 16 * row_bytes), dtype=np.float32)
+    lib().or_ple_gather_fp8_f32(_p(np.ascontiguousarray(table, np.uint8)), row_bytes, scale, _p(hsh.mult),
+                                _p(hsh.vocab), _p(hsh.off), _p(ids), ids.size, prev, eos, _p(out))
+    return out
+
+
+def ple_gate_f32(key, query, value, T, n, hc):
+    gv = np.empty((T * hc, n), dtype=np.float32)
+    lib().or_ple_gate_f32(_p(np.ascontiguousarray(key, np.float32)), _p(np.ascontiguousarray(query, np.float32)),
+                          _p(np.ascontiguousarray(value, np.float32)), _p(gv), T, n, hc)
+    return gv
+
+
+def ple_conv_f32(norm, cw, hist, gv, R, T, hcd, snaps=False):
+    """Returns (R', hist', snaps or None); inputs are not modified."""
+    R2 = np.array(R, dtype=np.float32, copy=True)
+    h2 = np.array(hist, dtype=np.float32, copy=True)
+    sn = np.zeros((T, hcd, 9), dtype=np.float32) if snaps else None
+    lib().or_ple_conv_f32(_p(np.ascontiguousarray(norm, np.float32)), _p(np.ascontiguousarray(cw, np.float32)),
+                          _p(h2), _p(np.ascontiguousarray(gv, np.float32)), _p(R2), T, hcd,
+                          _p(sn) if snaps else None)
+    return R2, h2, sn
+
+
 # ---- the reference's own kernels (GPU) and host table builder --------------------------------
 _ref = None
 
@@ -300,6 +352,8 @@ def ref_lib() -> ctypes.CDLL:
             "ref_gr_write_multi": [P, P, P, I, I, I, P],
             "ref_pf_gr_up_mean_fp16": [P, P, P, P, I, I, P],
             "ref_kv_append_int8_multi": [P, P, P, P, P, P, P, P, P, P, P, I, I, I, P],
+            "ref_ple_gate_gv_multi": [P, P, P, P, I, I, I, P],
+            "ref_ple_conv_multi": [P, P, P, P, P, I, I, P, P],
             "ref_gr_up_gate_mean_pf": [P, P, P, I, I, P],
             "ref_silu_div_hc_to_fp16": [P, P, I, F, P],
             "ref_fused_head_norm_rope_multi": [P, P, P, P, P, I, I, I, I, I, F, P],

@@ -123,6 +123,20 @@ int ref_ple_group_multi(const float* x, const float* gamma, float* y, int T, int
     return (int)cudaGetLastError();
 }
 
+// ple_gate_gv_multi (src/wzy_kernels_v2.cuh:1321-1346), launched as at src/wzy_stage_v2.cuh:592.
+int ref_ple_gate_gv_multi(const float* key, const float* query, const float* value, float* gv, int T, int hc,
+                          int n_embd, cudaStream_t s) {
+    ple_gate_gv_multi<<<dim3(hc, T), 256, 0, s>>>(key, query, value, gv, hc, n_embd);
+    return (int)cudaGetLastError();
+}
+
+// ple_conv_multi (src/wzy_kernels_v2.cuh:1348-1373), launched as at src/wzy_stage_v2.cuh:594.
+int ref_ple_conv_multi(const float* norm, const float* cw, float* hist, const float* gv, float* R, int hcd, int T,
+                       float* snaps, cudaStream_t s) {
+    ple_conv_multi<<<(hcd + 255) / 256, 256, 0, s>>>(norm, cw, hist, gv, R, hcd, PLE_NG, PLE_KERN, T, snaps);
+    return (int)cudaGetLastError();
+}
+
 int ref_dims(int* ne, int* nvocab) {
     *ne = NE;
     *nvocab = NVOCAB;

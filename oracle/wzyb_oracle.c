@@ -518,3 +518,93 @@ void or_ple_gather_f16(const uint16_t* const* tables, int heads, int64_t rows, i
         }
     }
 }
+
+/* ------------------------------------------------------------------------------------------- */
+/* PLE in the reference model's own format                                                     */
+/* stage_ple_window (src/wzy_engine_v2.cu:943-978): context [cur, prev1, prev2] with the EOS cut; */
+/* for n in {2, 3}: mixed = xor_j ctx[j] * mult[j] (u64); 8 heads per n:                        */
+/* row = (uint32)(mixed % vocab[h] + off[h]). PleSrc (src/wzy_stage_v2.cuh:278-285): e4m3 byte   */
+/* decoded by a 256-entry table (subnormal mm*2^-9, NaN codes -> 0) times the global scale.      */
+/* ------------------------------------------------------------------------------------------- */
+uint32_t or_ple_fp8_row(int32_t cur, int32_t p1, int32_t p0, int h, const uint64_t* mult, const uint64_t* vocab,
+                        const uint64_t* off, int32_t eos) {
+    const int32_t t3[3] = {p0, p1, cur};
+    int64_t ctx[3];
+    ctx[0] = cur;
+    int cut = 0;
+    for (int s = 1; s < 3; ++s) {
+        const int32_t v = cut ? -1 : t3[2 - s];
+        cut = cut || v < 0 || v == eos;
+        ctx[s] = cut ? eos : v;
+    }
+    const int n = h < 8 ? 2 : 3;
+    uint64_t mixed = (uint64_t)ctx[0] * mult[0];
+    for (int j = 1; j < n; ++j) mixed ^= (uint64_t)ctx[j] * mult[j];
+    return (uint32_t)(mixed % vocab[h] + off[h]);
+}
+
+void or_ple_gather_fp8_f32(const uint8_t* table, int row_bytes, float scale, const uint64_t* mult,
+                           const uint64_t* vocab, const uint64_t* off, const int32_t* ids, int64_t T,
+                           const int32_t* prev_ids, int32_t eos, float* out) {
+    float lut[256];
+    for (int v = 0; v < 256; ++v) {
+        const int sg = (v >> 7) & 1, e = (v >> 3) & 0xF, mm = v & 7;
+        float f;
+        if (e == 0) f = ldexpf((float)mm, -9);
+        else if (e == 15 && mm == 7) f = 0.f;
+        else f = ldexpf(1.f + (float)mm / 8.f, e - 7);
+        lut[v] = (sg ? -f : f) * scale;
+    }
+    const int32_t prev2 = prev_ids ? prev_ids[0] : -1;
+    const int32_t prev1 = prev_ids ? prev_ids[1] : -1;
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < T; ++t) {
+        const int32_t p1 = t >= 1 ? ids[t - 1] : prev1;
+        const int32_t p0 = t >= 2 ? ids[t - 2] : (t == 1 ? prev1 : prev2);
+        for (int h = 0; h < 16; ++h) {
+            const uint32_t r = or_ple_fp8_row(ids[t], p1, p0, h, mult, vocab, off, eos);
+            const uint8_t* src = table + (uint64_t)r * (uint64_t)row_bytes;
+            float* dst = out + (t * 16 + h) * (int64_t)row_bytes;
+            for (int i = 0; i < row_bytes; ++i) dst[i] = lut[src[i]];
+        }
+    }
+}
+
+/* ple_gate_gv_multi (src/wzy_kernels_v2.cuh:1321-1346): d = dot(key, query) / sqrt(n) (double sum); */
+/* g = 1/(1 + exp(-sign(d) * sqrt(max(|d|, 1e-6)))); gv = value[t] * g.                           */
+void or_ple_gate_f32(const float* key, const float* query, const float* value, float* gv, int64_t T, int n, int hc) {
+#pragma omp parallel for schedule(static)
+    for (int64_t u = 0; u < T * hc; ++u) {
+        const float* k = key + u * n;
+        const float* q = query + u * n;
+        const float* v = value + (u / hc) * n;
+        double acc = 0.0;
+        for (int d = 0; d < n; ++d) acc += (double)k[d] * (double)q[d];
+        float tot = (float)acc / sqrtf((float)n);
+        const float sg = tot < 0.f ? -1.f : 1.f;
+        const float g = 1.f / (1.f + expf(-sg * sqrtf(fmaxf(fabsf(tot), 1e-6f))));
+        for (int d = 0; d < n; ++d) gv[u * n + d] = v[d] * g;
+    }
+}
+
+/* ple_conv_multi (src/wzy_kernels_v2.cuh:1348-1373), sequential over T per channel as there:      */
+/* h = hist[c, 0..8]; acc = w0*h0 + w1*h3 + w2*h6 + w3*cur; shift in cur; R += gv + silu(acc).      */
+void or_ple_conv_f32(const float* norm, const float* cw, float* hist, const float* gv, float* R, int64_t T, int hcd,
+                     float* snaps) {
+#pragma omp parallel for schedule(static)
+    for (int c = 0; c < hcd; ++c) {
+        float h[9];
+        for (int i = 0; i < 9; ++i) h[i] = hist[(int64_t)9 * c + i];
+        const float w0 = cw[4 * c], w1 = cw[4 * c + 1], w2 = cw[4 * c + 2], w3 = cw[4 * c + 3];
+        for (int64_t t = 0; t < T; ++t) {
+            const float cur = norm[t * hcd + c];
+            const float acc = w0 * h[0] + w1 * h[3] + w2 * h[6] + w3 * cur;
+            for (int i = 0; i < 8; ++i) h[i] = h[i + 1];
+            h[8] = cur;
+            R[t * hcd + c] += gv[t * hcd + c] + acc / (1.0f + expf(-acc));
+            if (snaps)
+                for (int i = 0; i < 9; ++i) snaps[(t * hcd + c) * 9 + i] = h[i];
+        }
+        for (int i = 0; i < 9; ++i) hist[(int64_t)9 * c + i] = h[i];
+    }
+}

@@ -77,6 +77,15 @@ uint32_t or_embed_gather_bf16_f32(const uint16_t* table, int64_t vocab, int hidd
 uint32_t or_ple_row(int32_t t0, int32_t t1, int32_t t2, int head, int64_t rows, int32_t eos, int variant);
 void or_ple_gather_f16(const uint16_t* const* tables, int heads, int64_t rows, int hd, const int32_t* ids, int64_t T,
                        const int32_t* prev_ids, int32_t eos, int variant, uint16_t* out);
+/* the reference model's PLE: fp8 rows by the u64 n-gram hash, then the gate and the causal conv */
+uint32_t or_ple_fp8_row(int32_t cur, int32_t p1, int32_t p0, int h, const uint64_t* mult, const uint64_t* vocab,
+                        const uint64_t* off, int32_t eos);
+void or_ple_gather_fp8_f32(const uint8_t* table, int row_bytes, float scale, const uint64_t* mult,
+                           const uint64_t* vocab, const uint64_t* off, const int32_t* ids, int64_t T,
+                           const int32_t* prev_ids, int32_t eos, float* out);
+void or_ple_gate_f32(const float* key, const float* query, const float* value, float* gv, int64_t T, int n, int hc);
+void or_ple_conv_f32(const float* norm, const float* cw, float* hist, const float* gv, float* R, int64_t T, int hcd,
+                     float* snaps);
 
 #ifdef __cplusplus
 }

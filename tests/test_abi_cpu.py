@@ -96,6 +96,21 @@ def test_argument_validation_before_any_cuda_call(wz):
     assert L.wzyb_kv_append_int8_f32(A16, A16, 4, 2, 256, None, 0, part, NULL) == wz.ERR_NULL
     odd = ctypes.byref(wz.KvCache(a, a + 1, a, a, None, None, None, None, 64, 128))
     assert L.wzyb_kv_append_int8_f32(A16, A16, 4, 2, 256, None, 0, odd, NULL) == wz.ERR_ALIGN
+    # PLE in the reference format: every hashed row inside the table, whole 16-byte chunks
+    h = wz.ple_fp8_hash()
+    assert [h.off[i] for i in range(3)] == [0, 20000003, 40000026] and h.off[15] + h.vocab[15] == 320001446
+    hb = ctypes.byref(h)
+    g8 = L.wzyb_ple_gather_fp8_f32
+    assert g8(A16, 320001446, 160, 1.0, None, A16, 4, None, 248044, A16, NULL) == wz.ERR_NULL
+    assert g8(A16, 320001445, 160, 1.0, hb, A16, 4, None, 248044, A16, NULL) == wz.ERR_SHAPE
+    assert g8(A16, 320001446, 150, 1.0, hb, A16, 4, None, 248044, A16, NULL) == wz.ERR_SHAPE
+    assert g8(A8, 320001446, 160, 1.0, hb, A16, 4, None, 248044, A16, NULL) == wz.ERR_ALIGN
+    assert g8(A16, 320001446, 160, 1.0, hb, A16, 0, None, 248044, A16, NULL) == wz.OK
+    assert L.wzyb_ple_gate_f32(A16, A16, NULL, A16, 4, 2560, 4, NULL) == wz.ERR_NULL
+    assert L.wzyb_ple_gate_f32(A16, A16, A16, A16, 4, 2564, 4, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_ple_conv_f32(A16, A16, A16, A16, NULL, 4, 10240, NULL, NULL) == wz.ERR_NULL
+    assert L.wzyb_ple_conv_f32(A16, A16, A16, A16, A16, 4, 10242, NULL, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_ple_conv_f32(A16, A8, A16, A16, A16, 4, 10240, NULL, NULL) == wz.ERR_ALIGN
     fused = L.wzyb_k_rope_kv_append_f16
     assert fused(A16, NULL, A16, A16, A16, 64, None, 0, 4, 2, 256, 64, 1e-6, 1.0, kc, NULL) == wz.ERR_NULL
     assert fused(A16, A16, A16, A16, A16, 64, None, 0, 4, 2, 256, 24, 1e-6, 1.0, kc, NULL) == wz.ERR_SHAPE

@@ -521,3 +521,87 @@ def test_k_rope_kv_append_fused(wz, orc, dtype, T, heads, hd, base):
         ds_ = np.abs(_kv_host(d, s).astype(np.int32) - getattr(cache, s).astype(np.int32))
         assert ds_.max() <= 1, s
     assert wz.read_faults() == 0
+
+
+# ---------------------------------------------------------------------------------------------
+# the reference model's PLE: fp8 rows by the n-gram hash, gate, causal conv
+# ---------------------------------------------------------------------------------------------
+_SMALL_PLE_VOCAB = [1009, 1013, 1019, 1021, 1031, 1033, 1039, 1049, 1051, 1061, 1063, 1069, 1087, 1091, 1093, 1097]
+
+
+@pytest.mark.parametrize("rb,prev", [(160, (1, 2)), (160, None), (32, (248044, 7)), (48, (-1, 5))])
+def test_ple_gather_fp8(wz, orc, rb, prev):
+    r = rng(rb)
+    hsh_o = orc.PleFp8Hash(vocab=_SMALL_PLE_VOCAB)
+    table = r.integers(0, 256, (hsh_o.rows, rb)).astype(np.uint8)
+    table[:, 0] = 0x7F  # NaN codes in every row
+    table[:, 1] = 0xFF
+    T = 300
+    ids = r.integers(-2, 248320, T).astype(np.int32)
+    ids[5], ids[9] = 248044, -1
+    want = orc.ple_gather_fp8_f32(table, rb, 0.61, hsh_o, ids, prev_ids=prev)
+    out = torch.empty((T, 16 * rb), dtype=torch.float32, device=DEV)
+    wz.ple_gather_fp8_f32(dev(table), rb, 0.61, wz.ple_fp8_hash(vocab=_SMALL_PLE_VOCAB), dev(ids), out,
+                          prev_ids=prev)
+    assert np.array_equal(host(out).view(np.uint32), want.view(np.uint32))
+
+
+def test_ple_gather_fp8_full_reference_table(wz, orc):
+    """The reference's hash over its full 320,001,446-row x 160-byte table (51.2 GB in HBM)."""
+    hsh_o = orc.PleFp8Hash()
+    rb, T = 160, 64
+    gen = torch.Generator(device=DEV).manual_seed(9)
+    table = torch.randint(0, 256, (hsh_o.rows, rb), generator=gen, device=DEV, dtype=torch.uint8)
+    ids_np = rng(77).integers(0, 248320, T).astype(np.int32)
+    out = torch.empty((T, 16 * rb), dtype=torch.float32, device=DEV)
+    wz.ple_gather_fp8_f32(table, rb, 0.5, wz.ple_fp8_hash(), dev(ids_np), out, prev_ids=(100, 200))
+    seq = [100, 200] + [int(v) for v in ids_np]
+    rows = [orc.ple_fp8_row(seq[t + 2], seq[t + 1], seq[t], h, hsh_o) for t in range(T) for h in range(16)]
+    assert max(rows) < hsh_o.rows and min(rows) >= 0
+    sub = table[torch.tensor(rows, device=DEV, dtype=torch.int64)].cpu()  # [T*16, rb]
+    # the rows the oracle's hash names, decoded on the host (e4m3 as torch reads it, NaN codes -> 0)
+    dec = sub.view(torch.float8_e4m3fn).float().numpy()
+    raw = sub.numpy()
+    dec = np.where((raw & 0x7F) == 0x7F, np.where(raw & 0x80, -0.0, 0.0), dec).astype(np.float32) * np.float32(0.5)
+    got = host(out).reshape(T * 16, rb)
+    del table
+    torch.cuda.empty_cache()
+    assert np.array_equal(got.view(np.uint32), dec.view(np.uint32))
+
+
+@pytest.mark.parametrize("T,n,hc", [(1, 2560, 4), (8, 2560, 4), (4096, 2560, 4), (3, 96, 2), (5, 16384, 1)])
+def test_ple_gate_f32(wz, orc, T, n, hc):
+    r = rng(T + n + hc)
+    k = r.standard_normal((T * hc, n)).astype(np.float32)
+    q = r.standard_normal((T * hc, n)).astype(np.float32)
+    q[0] = -k[0]
+    v = r.standard_normal((T, n)).astype(np.float32)
+    want = orc.ple_gate_f32(k, q, v, T, n, hc)
+    gv = torch.empty((T * hc, n), dtype=torch.float32, device=DEV)
+    wz.ple_gate_f32(dev(k), dev(q), dev(v), gv, T, n, hc)
+    got = host(gv)
+    # The gate is sigmoid(sqrt|d|) of an n-term fp32 dot product d: where d cancels towards 0 the
+    # rounding of the sum (reduction order differs) is amplified by 1/sqrt|d|, so a few rows may sit
+    # several fp32 ulp away; nearly every element is within 2e-6.
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-7)
+    close = np.isclose(got, want, rtol=2e-6, atol=1e-7)
+    assert close.mean() > 0.999
+
+
+@pytest.mark.parametrize("T,hcd,snaps", [(1, 10240, False), (5, 12, True), (9, 40, True), (40, 12, True),
+                                         (4096, 10240, False), (77, 10240, True)])
+def test_ple_conv_f32(wz, orc, T, hcd, snaps):
+    r = rng(T * 3 + hcd)
+    norm = r.standard_normal((T, hcd)).astype(np.float32)
+    cw = (0.5 * r.standard_normal((hcd, 4))).astype(np.float32)
+    hist = r.standard_normal((hcd, 9)).astype(np.float32)
+    gv = r.standard_normal((T, hcd)).astype(np.float32)
+    R = r.standard_normal((T, hcd)).astype(np.float32)
+    R_ref, h_ref, s_ref = orc.ple_conv_f32(norm, cw, hist, gv, R, T, hcd, snaps=snaps)
+    dR, dh = dev(R), dev(hist)
+    ds = torch.empty((T, hcd, 9), dtype=torch.float32, device=DEV) if snaps else None
+    wz.ple_conv_f32(dev(norm), dev(cw), dh, dev(gv), dR, T, hcd, hist_snaps=ds)
+    np.testing.assert_allclose(host(dR), R_ref, rtol=2e-6, atol=2e-6)
+    assert np.array_equal(host(dh), h_ref)
+    if snaps:
+        assert np.array_equal(host(ds), s_ref)

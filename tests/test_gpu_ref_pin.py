@@ -355,3 +355,42 @@ def test_pin_k_rope_kv_append(ref, orc, wz):
         d = np.abs(host(pm[q]).astype(np.int32) - host(pr[q]).astype(np.int32))
         assert d.max() <= 1 and (d > 0).mean() < 2e-3
         assert np.abs(host(pm[sc]).astype(np.int32) - host(pr[sc]).astype(np.int32)).max() <= 1
+
+
+def test_pin_ple_gate_and_conv(ref, orc, wz):
+    """ple_gate_gv_multi and ple_conv_multi at the reference's widths (n_embd 2560, 4 streams,
+    HCD 10240), with a carried history and per-token snapshots."""
+    r = np.random.default_rng(212)
+    T, n, hc = 12, 2560, 4
+    k = r.standard_normal((T * hc, n)).astype(np.float32)
+    q = r.standard_normal((T * hc, n)).astype(np.float32)
+    q[3] = -k[3]
+    v = r.standard_normal((T, n)).astype(np.float32)
+    dk, dq, dv = dev(k), dev(q), dev(v)
+    rg = torch.empty((T * hc, n), dtype=torch.float32, device=DEV)
+    assert ref.ref_ple_gate_gv_multi(dk.data_ptr(), dq.data_ptr(), dv.data_ptr(), rg.data_ptr(), T, hc, n, sp()) == 0
+    ref_gv = host(rg)
+    np.testing.assert_allclose(orc.ple_gate_f32(k, q, v, T, n, hc), ref_gv, rtol=2e-6, atol=1e-7)
+    mg = torch.empty_like(rg)
+    wz.ple_gate_f32(dk, dq, dv, mg, T, n, hc)
+    np.testing.assert_allclose(host(mg), ref_gv, rtol=2e-6, atol=1e-7)
+    hcd = hc * n
+    norm = r.standard_normal((T, hcd)).astype(np.float32)
+    cw = (0.5 * r.standard_normal((hcd, 4))).astype(np.float32)
+    hist = r.standard_normal((hcd, 9)).astype(np.float32)
+    gv = r.standard_normal((T, hcd)).astype(np.float32)
+    R = r.standard_normal((T, hcd)).astype(np.float32)
+    dn, dcw, dgv = dev(norm), dev(cw), dev(gv)
+    rR, rh = dev(R), dev(hist)
+    rs = torch.zeros((T, hcd, 9), dtype=torch.float32, device=DEV)
+    assert ref.ref_ple_conv_multi(dn.data_ptr(), dcw.data_ptr(), rh.data_ptr(), dgv.data_ptr(), rR.data_ptr(), hcd, T,
+                                  rs.data_ptr(), sp()) == 0
+    mR, mh = dev(R), dev(hist)
+    ms = torch.zeros_like(rs)
+    wz.ple_conv_f32(dn, dcw, mh, dgv, mR, T, hcd, hist_snaps=ms)
+    np.testing.assert_allclose(host(mR), host(rR), rtol=1e-6, atol=1e-6)
+    assert np.array_equal(host(mh), host(rh))
+    assert np.array_equal(host(ms), host(rs))
+    oR, oh, osn = orc.ple_conv_f32(norm, cw, hist, gv, R, T, hcd, snaps=True)
+    np.testing.assert_allclose(oR, host(rR), rtol=2e-6, atol=2e-6)
+    assert np.array_equal(oh, host(rh)) and np.array_equal(osn, host(rs))

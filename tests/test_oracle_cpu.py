@@ -279,3 +279,78 @@ def test_hyper_connection_residual_against_float64(orc):
     lo = (4 * r.standard_normal(1000)).astype(np.float32)
     v = lo.astype(np.float64) * 0.25
     assert_f16_close(orc.silu_scale_f16(lo, 0.25), (v / (1 + np.exp(-v))).astype(np.float16), 1, "silu_scale")
+
+
+def _py_ple_fp8_row(cur, p1, p0, h, mult, vocab, off, eos=248044):
+    m64 = (1 << 64) - 1
+    c1 = eos if (p1 < 0 or p1 == eos) else p1
+    cut = p1 < 0 or p1 == eos or p0 < 0 or p0 == eos
+    c2 = eos if cut else p0
+    mixed = ((cur & m64) * mult[0] & m64) ^ (c1 * mult[1] & m64)
+    if h >= 8:
+        mixed ^= c2 * mult[2] & m64
+    return (mixed % vocab[h] + off[h]) & 0xFFFFFFFF
+
+
+def test_ple_fp8_hash_matches_python(orc):
+    hsh = orc.PleFp8Hash()
+    assert hsh.rows == 320001446
+    mult, vocab, off = ([int(x) for x in a] for a in (hsh.mult, hsh.vocab, hsh.off))
+    r = np.random.default_rng(51)
+    cases = [(5, 7, 9), (0, -1, -1), (123, 248044, 55), (123, 55, 248044), (-3, 4, 5), (248044, 1, 2),
+             (151935, 151934, 151933), (2 ** 31 - 1, 2 ** 31 - 1, 2 ** 31 - 1)]
+    cases += [tuple(int(v) for v in r.integers(-2, 248320, 3)) for _ in range(300)]
+    for cur, p1, p0 in cases:
+        for h in range(16):
+            assert orc.ple_fp8_row(cur, p1, p0, h, hsh) == _py_ple_fp8_row(cur, p1, p0, h, mult, vocab, off)
+
+
+def test_ple_fp8_gather_decode_and_context(orc):
+    """Every e4m3 code decodes as torch's float8_e4m3fn times the scale (the NaN codes as signed zero),
+    and each token reads the rows its (id, id[-1], id[-2]) context hashes to."""
+    import torch
+
+    hsh = orc.PleFp8Hash(vocab=[13, 17, 19, 23, 29, 31, 37, 41, 43, 47, 53, 59, 61, 67, 71, 73])
+    rb, scale = 32, 0.37
+    table = np.arange(hsh.rows * rb, dtype=np.int64).astype(np.uint8).reshape(hsh.rows, rb)  # every code
+    ids = np.array([3, 248044, 9, -1, 11, 12], dtype=np.int32)
+    out = orc.ple_gather_fp8_f32(table, rb, scale, hsh, ids, prev_ids=(1, 2))
+    dec = torch.from_numpy(table.reshape(-1).copy()).view(torch.float8_e4m3fn).float().numpy()
+    dec = np.where((table.reshape(-1) & 0x7F) == 0x7F, np.where(table.reshape(-1) & 0x80, -0.0, 0.0), dec)
+    dec = (dec.astype(np.float32) * np.float32(scale)).reshape(hsh.rows, rb)
+    seq = [1, 2] + [int(v) for v in ids]
+    for t in range(ids.size):
+        for h in range(16):
+            row = orc.ple_fp8_row(seq[t + 2], seq[t + 1], seq[t], h, hsh)
+            got = out[t, h * rb:(h + 1) * rb]
+            assert np.array_equal(got.view(np.uint32), dec[row].view(np.uint32)), (t, h)
+
+
+def test_ple_gate_and_conv_against_numpy(orc):
+    r = np.random.default_rng(52)
+    T, n, hc = 5, 96, 4
+    k = r.standard_normal((T * hc, n)).astype(np.float32)
+    q = r.standard_normal((T * hc, n)).astype(np.float32)
+    q[1] = -k[1]  # a negative dot product
+    v = r.standard_normal((T, n)).astype(np.float32)
+    gv = orc.ple_gate_f32(k, q, v, T, n, hc)
+    d = (k.astype(np.float64) * q).sum(axis=1) / np.sqrt(n)
+    g = 1 / (1 + np.exp(-np.sign(np.where(d == 0, 1, d)) * np.sqrt(np.maximum(np.abs(d), 1e-6))))
+    np.testing.assert_allclose(gv, np.repeat(v, hc, axis=0) * g[:, None], rtol=2e-6, atol=1e-7)
+    # conv: the sequential restatement equals the time-parallel form, history carried across calls
+    hcd = 12
+    cw = r.standard_normal((hcd, 4)).astype(np.float32)
+    hist = r.standard_normal((hcd, 9)).astype(np.float32)
+    for T in (3, 20):
+        norm = r.standard_normal((T, hcd)).astype(np.float32)
+        gvc = r.standard_normal((T, hcd)).astype(np.float32)
+        R = r.standard_normal((T, hcd)).astype(np.float32)
+        R2, h2, sn = orc.ple_conv_f32(norm, cw, hist, gvc, R, T, hcd, snaps=True)
+        x = np.concatenate([hist.T, norm], axis=0).astype(np.float64)  # x[s + 9]
+        acc = sum(cw[:, j] * x[3 * j:3 * j + T] for j in range(4))
+        want = R + gvc + acc / (1 + np.exp(-acc))
+        np.testing.assert_allclose(R2, want, rtol=1e-5, atol=1e-6)
+        assert np.array_equal(h2, x[T:T + 9].T.astype(np.float32))
+        for t in range(T):
+            assert np.array_equal(sn[t], x[t + 1:t + 10].T.astype(np.float32))
+        hist = h2

@@ -91,12 +91,13 @@ __device__ __forceinline__ void kv_q8_store(const float2 (&x)[4], bool act, int 
 }
 
 // One warp per token. HD/8 lanes per head, 32/(HD/8) heads side by side; the token's heads are
-// visited in rounds of that many. k and v of a round are loaded together (4 x 16 B per lane in
-// flight for fp32) before any arithmetic.
+// visited in rounds of that many. The k and v vectors of kR = 2 rounds (the reference's 2 heads of
+// 256) are loaded before any arithmetic, with the cos/sin slice behind them.
 template <typename T, int HD>
 __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
     constexpr int L = HD / 8;
     constexpr int HPW = 32 / L;
+    constexpr int kR = 2;
     const int lane = threadIdx.x & 31;
     const int li = lane % L, hw = lane / L;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -129,6 +130,19 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
         const int64_t rcell = ring ? kv_ring_cell(pos, a.c.ring_cap) : 0;
         const bool full = keep && a.c.full_k_q != nullptr;
         const bool pos_ok = half > 0 && pos >= 0 && pos < a.table_rows;
+        // Loads first: the k and v vectors of kR rounds of heads, then the token's cos/sin slice.
+        typename Vec8<T>::Raw kr[kR], vr[kR];
+        auto load_rounds = [&](int r0) {
+#pragma unroll
+            for (int j = 0; j < kR; ++j) {
+                const int h = (r0 + j) * HPW + hw;
+                if (r0 + j < rounds && h < a.kv_heads) {
+                    kr[j] = Vec8<T>::ldcs_raw(kd + t * kvd + h * HD + li * 8);
+                    vr[j] = Vec8<T>::ldcs_raw(vd + t * kvd + h * HD + li * 8);
+                }
+            }
+        };
+        load_rounds(0);
         float2 c2[4], s2[4];
         if (a.norm_rope) {
             if (pos_ok && rot_lane) {
@@ -141,16 +155,19 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
             }
             if (half > 0 && !pos_ok && lane == 0) raise_fault(WZYB_FAULT_POS_RANGE);
         }
-        for (int r = 0; r < rounds; ++r) {
+        for (int r0 = 0; r0 < rounds; r0 += kR) {
+          if (r0 > 0) load_rounds(r0);  // more heads than kR rounds hold
+#pragma unroll
+          for (int j = 0; j < kR; ++j) {
+            const int r = r0 + j;
+            if (r >= rounds) break;  // warp-uniform
             const int h = r * HPW + hw;
             const bool act = h < a.kv_heads;
             const int64_t off = t * kvd + h * HD + li * 8;
             float2 p[4], v[4];
             if (act) {
-                const typename Vec8<T>::Raw kr = Vec8<T>::ldcs_raw(kd + off);
-                const typename Vec8<T>::Raw vr = Vec8<T>::ldcs_raw(vd + off);
-                Vec8<T>::cvt2(kr, p);
-                Vec8<T>::cvt2(vr, v);
+                Vec8<T>::cvt2(kr[j], p);
+                Vec8<T>::cvt2(vr[j], v);
             } else {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) p[i] = v[i] = splat2(0.f);
@@ -183,6 +200,7 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
                             a.c.ring_v_s + rcell * spc + sc_i, full ? a.c.full_v_q + pos * kvd + col : nullptr,
                             full ? a.c.full_v_s + pos * spc + sc_i : nullptr);
             }
+          }
         }
     }
 }

@@ -8,3 +8,4 @@
 #include "gather.cu"
 #include "hc_stream.cu"
 #include "kv_append.cu"
+#include "ple_block.cu"

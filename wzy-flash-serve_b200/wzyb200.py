@@ -49,6 +49,11 @@ class KvCache(ctypes.Structure):
     ]
 
 
+class PleFp8Hash(ctypes.Structure):
+    """wzyb_ple_fp8_hash: n-gram multipliers and the 16 heads' sub-table sizes and offsets."""
+    _fields_ = [("mult", ctypes.c_uint64 * 3), ("vocab", ctypes.c_uint64 * 16), ("off", ctypes.c_uint64 * 16)]
+
+
 class HeadTensor(ctypes.Structure):
     _fields_ = [
         ("data", c_void_p),
@@ -112,6 +117,11 @@ _SIGS = {
     "wzyb_hc_mix_f32": (c_int, [P, P, P, c_int64, c_int, c_int, S]),
     "wzyb_silu_scale_f16": (c_int, [P, P, c_int64, c_float, S]),
     "wzyb_kv_append_int8_f32": (c_int, [P, P, c_int64, c_int, c_int, P, c_int64, POINTER(KvCache), S]),
+    "wzyb_ple_fp8_reference_hash": (c_int, [POINTER(PleFp8Hash)]),
+    "wzyb_ple_gather_fp8_f32": (
+        c_int, [P, c_int64, c_int, c_float, POINTER(PleFp8Hash), P, c_int64, POINTER(c_int32), c_int32, P, S]),
+    "wzyb_ple_gate_f32": (c_int, [P, P, P, P, c_int64, c_int, c_int, S]),
+    "wzyb_ple_conv_f32": (c_int, [P, P, P, P, P, c_int64, c_int, P, S]),
     "wzyb_k_rope_kv_append_f32": (
         c_int,
         [P, P, P, P, P, c_int64, P, c_int64, c_int64, c_int, c_int, c_int, c_float, c_float, POINTER(KvCache), S],
@@ -328,6 +338,38 @@ def ple_gather_f16(tables, ids, out, prev_ids=None, eos_id=PLE_EOS_DEFAULT, hash
 
 def ple_row_index(t0, t1, t2, head, rows, eos_id=PLE_EOS_DEFAULT, hash_variant=PLE_HASH_C_PRECEDENCE) -> int:
     return int(lib().wzyb_ple_row_index(t0, t1, t2, head, rows, eos_id, hash_variant))
+
+
+def ple_fp8_hash(vocab=None, mult=None) -> PleFp8Hash:
+    """The reference's hash constants, or sub-tables of the given sizes packed end to end."""
+    h = PleFp8Hash()
+    check("wzyb_ple_fp8_reference_hash", lib().wzyb_ple_fp8_reference_hash(ctypes.byref(h)))
+    if mult is not None:
+        for i in range(3):
+            h.mult[i] = int(mult[i])
+    if vocab is not None:
+        off = 0
+        for i in range(16):
+            h.vocab[i] = int(vocab[i])
+            h.off[i] = off
+            off += int(vocab[i])
+    return h
+
+
+def ple_gather_fp8_f32(table, row_bytes, scale, hsh: PleFp8Hash, ids, out, prev_ids=None, eos_id=PLE_EOS_DEFAULT,
+                       stream=None):
+    prev = (c_int32 * 2)(*prev_ids) if prev_ids is not None else None
+    call("wzyb_ple_gather_fp8_f32", _ptr(table), table.numel() // row_bytes, row_bytes, scale, ctypes.byref(hsh),
+         _ptr(ids), ids.numel(), prev, eos_id, _ptr(out), _stream(stream))
+
+
+def ple_gate_f32(key, query, value, gv, T, n_embd, hc, stream=None):
+    call("wzyb_ple_gate_f32", _ptr(key), _ptr(query), _ptr(value), _ptr(gv), T, n_embd, hc, _stream(stream))
+
+
+def ple_conv_f32(norm, cw, hist, gv, R, T, hcd, hist_snaps=None, stream=None):
+    call("wzyb_ple_conv_f32", _ptr(norm), _ptr(cw), _ptr(hist), _ptr(gv), _ptr(R), T, hcd, _ptr(hist_snaps),
+         _stream(stream))
 
 
 def shard_rows(total: int, world: int, rank: int) -> tuple[int, int]:

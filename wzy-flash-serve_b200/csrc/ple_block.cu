@@ -13,8 +13,7 @@
 // The reference stages the PLE rows on the host (a hash + an 84 MB direct-mapped row cache + an
 // H2D copy per window). Here the 51 GB fp8 table sits in HBM and one warp per token hashes (16
 // lanes, one head each) and streams its 16 rows. ple_conv_multi walks T sequentially per channel
-// (10,240 threads); its output does not feed back, so here it runs parallel over (token chunk,
-// 4 channels) with the 9-input window in registers.
+// (10,240 threads); its output does not feed back, so here every (token, 4 channels) is a thread.
 #include <cuda_fp8.h>
 
 #include "launch.hpp"
@@ -25,6 +24,7 @@ namespace wzyb {
 // ---- fp8 PLE gather -----------------------------------------------------------------------------
 constexpr int kPleHeads = 16;  // 8 heads per n-gram order, orders 2 and 3
 constexpr int kPleHpn = 8;
+constexpr int kPleQuads = 20;  // 4-byte loads per lane in flight
 
 struct PleFp8Args {
     const uint8_t* table;
@@ -55,51 +55,53 @@ __device__ __forceinline__ uint32_t ple_fp8_row(const PleFp8Args& a, int64_t t, 
     return (uint32_t)(mixed % a.vocab[h] + a.off[h]);
 }
 
-// 16 fp8 e4m3 bytes -> 16 fp32 values times the scale. e4m3 -> fp16 is exact (hardware convert);
-// the NaN codes (0x7F, 0xFF) read as signed zero, as in the reference's decode table.
-__device__ __forceinline__ void fp8x16_decode(const uint4& raw, float scale, float4 (&o)[4]) {
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+// 4 fp8 e4m3 bytes (little-endian in a u32) -> 4 fp32 values times the scale. e4m3 -> fp16 is exact
+// (hardware convert); the NaN codes (0x7F, 0xFF) read as signed zero, as in the reference's table.
+__device__ __forceinline__ float4 fp8x4_decode(uint32_t w, float scale) {
+    float f[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        float f[4];
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const __nv_fp8x2_storage_t pair = (__nv_fp8x2_storage_t)((w[i] >> (16 * j)) & 0xFFFFu);
-            const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
-            __half2 h2;
-            *reinterpret_cast<__half2_raw*>(&h2) = hr;
-            const float2 v = __half22float2(h2);
-            const uint32_t b0 = (w[i] >> (16 * j)) & 0xFFu, b1 = (w[i] >> (16 * j + 8)) & 0xFFu;
-            f[2 * j] = ((b0 & 0x7Fu) == 0x7Fu ? ((b0 & 0x80u) ? -0.f : 0.f) : v.x) * scale;
-            f[2 * j + 1] = ((b1 & 0x7Fu) == 0x7Fu ? ((b1 & 0x80u) ? -0.f : 0.f) : v.y) * scale;
-        }
-        o[i] = make_float4(f[0], f[1], f[2], f[3]);
+    for (int j = 0; j < 2; ++j) {
+        const __nv_fp8x2_storage_t pair = (__nv_fp8x2_storage_t)((w >> (16 * j)) & 0xFFFFu);
+        const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
+        __half2 h2;
+        *reinterpret_cast<__half2_raw*>(&h2) = hr;
+        const float2 v = __half22float2(h2);
+        const uint32_t b0 = (w >> (16 * j)) & 0xFFu, b1 = (w >> (16 * j + 8)) & 0xFFu;
+        f[2 * j] = ((b0 & 0x7Fu) == 0x7Fu ? ((b0 & 0x80u) ? -0.f : 0.f) : v.x) * scale;
+        f[2 * j + 1] = ((b1 & 0x7Fu) == 0x7Fu ? ((b1 & 0x80u) ? -0.f : 0.f) : v.y) * scale;
     }
+    return make_float4(f[0], f[1], f[2], f[3]);
 }
 
-// One warp per token: lanes 0..15 hash one head each; the token's 16 * row_bytes/16 chunks of 16 B
-// are then spread over the lanes (each chunk fetches its row index from the hashing lane).
+// One warp per token: lanes 0..15 hash one head each; the token's rows are then read in 4-byte
+// quads spread over the lanes (each quad fetches its row index from the hashing lane).
 __global__ void __launch_bounds__(256) ple_fp8_gather_kernel(const PleFp8Args a) {
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-    const int cpr = a.row_bytes / 16;  // chunks per row
-    const int chunks = kPleHeads * cpr;
+    const int qpr = a.row_bytes / 4;  // 4-byte quads per row
+    const int quads = kPleHeads * qpr;
     const int width = kPleHeads * a.row_bytes;  // output floats per token
     for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < a.T; t += nwarps) {
         const uint32_t my_row = lane < kPleHeads ? ple_fp8_row(a, t, lane) : 0u;
-        float* dst = a.out + t * width;
-        for (int c0 = 0; c0 < chunks; c0 += 32) {
-            const int c = c0 + lane;
-            const int h = c < chunks ? c / cpr : 0;
-            const uint32_t row = __shfl_sync(0xffffffffu, my_row, h);
-            if (c < chunks) {
-                const int sub = c - h * cpr;
-                const uint4 raw = __ldg(reinterpret_cast<const uint4*>(a.table + (uint64_t)row * a.row_bytes) + sub);
-                float4 o[4];
-                fp8x16_decode(raw, a.scale, o);
-                float4* d4 = reinterpret_cast<float4*>(dst + h * a.row_bytes + sub * 16);
+        float4* dst = reinterpret_cast<float4*>(a.out + t * width);
+        // Lane l produces output float4s q = k*32 + l: 4 fp8 bytes each, so every warp-wide load
+        // reads 128 contiguous bytes (within at most two rows) and every store writes 512 contiguous
+        // bytes. kPleQuads loads per lane are in flight before any is decoded (the reference's
+        // 160-byte rows: 640 quads per token, 20 per lane).
+        for (int q0 = 0; q0 < quads; q0 += 32 * kPleQuads) {
+            uint32_t raw[kPleQuads];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) __stcs(d4 + i, o[i]);
+            for (int k = 0; k < kPleQuads; ++k) {
+                const int q = q0 + k * 32 + lane;
+                const int h = q < quads ? q / qpr : 0;
+                const uint32_t row = __shfl_sync(0xffffffffu, my_row, h);
+                if (q < quads)
+                    raw[k] = __ldg(reinterpret_cast<const uint32_t*>(a.table + (uint64_t)row * a.row_bytes) + (q - h * qpr));
+            }
+#pragma unroll
+            for (int k = 0; k < kPleQuads; ++k) {
+                const int q = q0 + k * 32 + lane;
+                if (q < quads) __stcs(dst + q, fp8x4_decode(raw[k], a.scale));
             }
         }
     }
@@ -166,12 +168,11 @@ __global__ void __launch_bounds__(512) ple_gate_kernel(const float* __restrict__
 //   acc(t) = w0*x(t-9) + w1*x(t-6) + w2*x(t-3) + w3*x(t)          (cw [c, 4])
 //   R[t,c] += gv[t,c] + acc / (1 + exp(-acc))
 // then hist[c, i] = x(T - 9 + i). With hist_snaps, the window after token t, x(t-8..t), is written
-// to hist_snaps[t, c, 0..8]. One thread per (chunk of kConvChunk tokens, 4 channels). The past
-// inputs x(t-3), x(t-6), x(t-9) are re-read through L1 (this thread loaded them a few tokens
-// earlier) instead of being carried in a 36-register window, which keeps occupancy high. The chunk
-// holding token 0 is the only reader of hist for its channels, so it also writes the new history.
+// to hist_snaps[t, c, 0..8]. The output never feeds back, so every (token, 4 channels) is its own
+// thread: 6 independent 16-byte loads (x(t-3..t-9) are rows other threads load too, L2 hits), ~40
+// registers, full occupancy. The new history is written by a second, tiny launch once every thread
+// of the first has read the old one.
 constexpr int kConvHist = 9;
-constexpr int kConvChunk = 32;
 
 // x(s) for 4 channels starting at c
 __device__ __forceinline__ float4 conv_x(const float* __restrict__ norm, const float* __restrict__ hist, int64_t s,
@@ -188,74 +189,73 @@ __device__ __forceinline__ float conv_lane(const float4& v, int j) {
 
 template <bool SNAPS>
 __global__ void __launch_bounds__(256) ple_conv_kernel(const float* __restrict__ norm, const float* __restrict__ cw,
-                                                       float* __restrict__ hist, const float* __restrict__ gv,
+                                                       const float* __restrict__ hist, const float* __restrict__ gv,
                                                        float* __restrict__ R, int64_t T, int hcd,
                                                        float* __restrict__ snaps) {
     const int c4n = hcd / 4;
-    const int64_t nchunks = (T + kConvChunk - 1) / kConvChunk;
-    const int64_t items = nchunks * c4n;
+    const int64_t items = T * c4n;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items; it += stride) {
-        const int64_t ch = it / c4n;
-        const int c = (int)(it - ch * c4n) * 4;
-        const int64_t t0 = ch * kConvChunk;
-        const int64_t t1 = t0 + kConvChunk < T ? t0 + kConvChunk : T;
-        float4 w[4];  // taps of channel c + j
+    const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    StridePos ps(i0, stride, c4n);  // item = (token q, channel group r)
+    for (int64_t it = i0; it < items; it += stride, ps.advance()) {
+        const int64_t t = ps.q;
+        const int c = ps.r * 4;
+        const float4 x0 = __ldg(reinterpret_cast<const float4*>(norm + t * hcd + c));
+        const float4 gq = __ldcs(reinterpret_cast<const float4*>(gv + t * hcd + c));
+        float4* rp = reinterpret_cast<float4*>(R + t * hcd + c);
+        const float4 rq = *rp;
+        const float4 x3 = conv_x(norm, hist, t - 3, hcd, c);
+        const float4 x6 = conv_x(norm, hist, t - 6, hcd, c);
+        const float4 x9 = conv_x(norm, hist, t - 9, hcd, c);
+        float rr[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) w[j] = __ldg(reinterpret_cast<const float4*>(cw) + c + j);
-#pragma unroll 4
-        for (int64_t t = t0; t < t1; ++t) {
-            const float4 x9 = conv_x(norm, hist, t - 9, hcd, c);
-            const float4 x6 = conv_x(norm, hist, t - 6, hcd, c);
-            const float4 x3 = conv_x(norm, hist, t - 3, hcd, c);
-            const float4 x0 = __ldg(reinterpret_cast<const float4*>(norm + t * hcd + c));
-            const float4 gq = __ldcs(reinterpret_cast<const float4*>(gv + t * hcd + c));
-            float4* rp = reinterpret_cast<float4*>(R + t * hcd + c);
-            const float4 rq = *rp;
-            float rr[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float acc = w[j].x * conv_lane(x9, j) + w[j].y * conv_lane(x6, j) + w[j].z * conv_lane(x3, j) +
-                                  w[j].w * conv_lane(x0, j);
-                float r = conv_lane(rq, j);
-                r += conv_lane(gq, j) + acc / (1.0f + __expf(-acc));
-                rr[j] = r;
-            }
-            *rp = make_float4(rr[0], rr[1], rr[2], rr[3]);
-            if (SNAPS) {
-                // x(t-8..t) of channel c + j at snaps[t, c + j, 0..8]: 36 consecutive floats
-                float win[kConvHist][4];
-#pragma unroll
-                for (int i = 0; i < kConvHist; ++i) {
-                    const float4 v = conv_x(norm, hist, t - 8 + i, hcd, c);
-                    win[i][0] = v.x; win[i][1] = v.y; win[i][2] = v.z; win[i][3] = v.w;
-                }
-                float4* sp = reinterpret_cast<float4*>(snaps + (t * hcd + c) * kConvHist);
-#pragma unroll
-                for (int k = 0; k < kConvHist; ++k) {
-                    float q[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int f = 4 * k + e;  // flat index j * 9 + i
-                        q[e] = win[f % kConvHist][f / kConvHist];
-                    }
-                    sp[k] = make_float4(q[0], q[1], q[2], q[3]);
-                }
-            }
+        for (int j = 0; j < 4; ++j) {
+            const float4 w = __ldg(reinterpret_cast<const float4*>(cw) + c + j);  // taps of channel c + j
+            const float acc = w.x * conv_lane(x9, j) + w.y * conv_lane(x6, j) + w.z * conv_lane(x3, j) +
+                              w.w * conv_lane(x0, j);
+            float r = conv_lane(rq, j);
+            r += conv_lane(gq, j) + acc / (1.0f + __expf(-acc));
+            rr[j] = r;
         }
-        if (ch == 0) {
-            // new history x(T-9+i): from norm where T-9+i >= 0, else (T < 9) from the old history,
-            // which only this thread reads (t0 == 0) and has read already.
-            float4 nh[kConvHist];
-#pragma unroll
-            for (int i = 0; i < kConvHist; ++i) nh[i] = conv_x(norm, hist, T - kConvHist + i, hcd, c);
+        __stcs(rp, make_float4(rr[0], rr[1], rr[2], rr[3]));
+        if (SNAPS) {
+            // x(t-8..t) of channel c + j at snaps[t, c + j, 0..8]: 36 consecutive floats
+            float win[kConvHist][4];
 #pragma unroll
             for (int i = 0; i < kConvHist; ++i) {
+                const float4 v = conv_x(norm, hist, t - 8 + i, hcd, c);
+                win[i][0] = v.x; win[i][1] = v.y; win[i][2] = v.z; win[i][3] = v.w;
+            }
+            float4* sp = reinterpret_cast<float4*>(snaps + (t * hcd + c) * kConvHist);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) hist[(int64_t)(c + j) * kConvHist + i] = conv_lane(nh[i], j);
+            for (int k = 0; k < kConvHist; ++k) {
+                float q[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int f = 4 * k + e;  // flat index j * 9 + i
+                    q[e] = win[f % kConvHist][f / kConvHist];
+                }
+                sp[k] = make_float4(q[0], q[1], q[2], q[3]);
             }
         }
     }
+}
+
+// hist[c, i] = x(T - 9 + i): one thread per channel; runs after ple_conv_kernel (stream order), so no
+// reader of the old history is left. Values with T - 9 + i < 0 shift down within the old history
+// (read in full before any write by the same thread).
+__global__ void __launch_bounds__(256) ple_conv_hist_kernel(const float* __restrict__ norm, float* __restrict__ hist,
+                                                            int64_t T, int hcd) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= hcd) return;
+    float nh[kConvHist];
+#pragma unroll
+    for (int i = 0; i < kConvHist; ++i) {
+        const int64_t s = T - kConvHist + i;
+        nh[i] = s >= 0 ? norm[s * hcd + c] : hist[(int64_t)c * kConvHist + kConvHist + s];
+    }
+#pragma unroll
+    for (int i = 0; i < kConvHist; ++i) hist[(int64_t)c * kConvHist + i] = nh[i];
 }
 
 }  // namespace wzyb
@@ -363,12 +363,14 @@ int wzyb_ple_conv_f32(const float* norm, const float* cw, float* hist, const flo
     wzyb::DeviceInfo di;
     const int rc = wzyb::device_info(&di);
     if (rc != WZYB_OK) return rc;
-    const int64_t items = ((T + wzyb::kConvChunk - 1) / wzyb::kConvChunk) * (hcd / 4);
+    const int64_t items = T * (hcd / 4);
     const int grid = wzyb::persistent_grid(di, 8, (items + 255) / 256);
+    cudaStream_t st = (cudaStream_t)stream;
     if (hist_snaps)
-        wzyb::ple_conv_kernel<true><<<grid, 256, 0, (cudaStream_t)stream>>>(norm, cw, hist, gv, R, T, hcd, hist_snaps);
+        wzyb::ple_conv_kernel<true><<<grid, 256, 0, st>>>(norm, cw, hist, gv, R, T, hcd, hist_snaps);
     else
-        wzyb::ple_conv_kernel<false><<<grid, 256, 0, (cudaStream_t)stream>>>(norm, cw, hist, gv, R, T, hcd, nullptr);
+        wzyb::ple_conv_kernel<false><<<grid, 256, 0, st>>>(norm, cw, hist, gv, R, T, hcd, nullptr);
+    wzyb::ple_conv_hist_kernel<<<(hcd + 255) / 256, 256, 0, st>>>(norm, hist, T, hcd);
     return wzyb::launch_status();
 }
 

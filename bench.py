@@ -279,6 +279,7 @@ def measure_kernels_4096(wz, torch, dev, peak, reps=60):
     nq = T * EXPERT_ROWS * FFN
     g32, u32 = torch.randn(nq, generator=gen, device=dev), torch.randn(nq, generator=gen, device=dev)
     q32, s32 = torch.empty(nq, dtype=torch.int8, device=dev), torch.empty(nq // 32, device=dev)
+    q16b, s16b = torch.empty(nq, dtype=torch.int8, device=dev), torch.empty(nq // 16, device=dev)
     rows = T * HC * NE
     # k norm + RoPE fused with the INT8 KV append (fp16 k, v [T, 2 x 256]; ring + full-context mirror)
     KVD = KH * HD
@@ -319,6 +320,8 @@ def measure_kernels_4096(wz, torch, dev, peak, reps=60):
         "gr_norm_q8_hc4": (lambda s: wz.gr_norm_q8_f32(R, wn, blk, inj, xn32, xq8, xs8, T, NE, HC, stream=s),
                            rows * (8 + 4 + 1) + rows // 8 + T * NE * 4 + T * HC * 4 + HC * NE * 4),
         "swiglu_q8": (lambda s: wz.swiglu_q8_f32(g32, u32, q32, s32, stream=s), nq * (8 + 1) + nq // 8),
+        "quant_act_q32_q16": (lambda s: wz.quant_act_f32(g32, q32, s32, q16b, s16b, nq // FFN, FFN, stream=s),
+                              nq * (4 + 1 + 1) + nq // 32 * 4 + nq // 16 * 4),
     })
     s = torch.cuda.current_stream()
 

@@ -230,6 +230,16 @@ int wzyb_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, w
  * (src/wzy_kernels_v2.cuh:1247-1279, launched at src/wzy_stage_v2.cuh:713). q32 [n] int8, s32 [n/32]
  * fp32, n % 32 == 0; the activation uses the reference's expression (IEEE divide). */
 int wzyb_swiglu_q8_f32(const float* gate, const float* up, int8_t* q32, float* s32, int64_t n, wzyb_stream_t stream);
+
+/* ============================================================================================
+ * fp32 activation rows x [T, cols] to int8 GEMM inputs in one pass: per 32-element group q32 [T, cols]
+ * int8 + s32 [T, cols/32] fp32, and/or per 16-element group q16 + s16 [T, cols/16]; each group
+ * d = amax/127, q = rint(x * 127/amax) clamped to [-127, 127]. Either pair may be NULL (not both);
+ * cols % 32 == 0 with q32, % 16 == 0 otherwise. Replaces quant_act_multi (src/wzy_kernels_v2.cuh:58-111;
+ * launched at src/wzy_stage_v2.cuh:449/468/609/630/697 and src/wzy_mtp.cuh:652-700).
+ * ========================================================================================== */
+int wzyb_quant_act_f32(const float* x, int8_t* q32, float* s32, int8_t* q16, float* s16, int64_t T, int cols,
+                       wzyb_stream_t stream);
 int wzyb_swiglu_interleaved_f16(const uint16_t* gu, uint16_t* out, int64_t T, int nff, wzyb_stream_t stream);
 int wzyb_swiglu_interleaved_f32_f16(const float* gu, uint16_t* out, int64_t T, int nff, wzyb_stream_t stream);
 

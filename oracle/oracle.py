@@ -28,6 +28,7 @@ _SIGS = {
     "or_gr_norm_f32": (None, [P, P, P, P, P, P, c_int64, c_int, c_int, c_float]),
     "or_gr_norm_q8_f32": (None, [P, P, P, P, P, P, P, c_int64, c_int, c_int, c_float]),
     "or_swiglu_q8_f32": (None, [P, P, P, P, c_int64]),
+    "or_quant_act_f32": (None, [P, P, P, P, P, c_int64]),
     "or_gr_write_f32": (None, [P, P, P, c_int64, c_int, c_int]),
     "or_hc_mix_f16": (None, [P, P, P, P, c_int64, c_int, c_int]),
     "or_hc_mix_f32": (None, [P, P, P, c_int64, c_int, c_int]),
@@ -131,6 +132,16 @@ def swiglu_q8_f32(g, u):
     s = np.empty(g.size // 32, dtype=np.float32)
     lib().or_swiglu_q8_f32(_p(g), _p(u), _p(q), _p(s), g.size)
     return q, s
+
+
+def quant_act_f32(x, q32=True, q16=True):
+    """(q32, s32, q16, s16) of the flat fp32 array x (None where not asked for)."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    a = (np.empty(x.size, np.int8), np.empty(x.size // 32, np.float32)) if q32 else (None, None)
+    b = (np.empty(x.size, np.int8), np.empty(x.size // 16, np.float32)) if q16 else (None, None)
+    lib().or_quant_act_f32(_p(x), _p(a[0]) if q32 else None, _p(a[1]) if q32 else None, _p(b[0]) if q16 else None,
+                           _p(b[1]) if q16 else None, x.size)
+    return a[0], a[1], b[0], b[1]
 
 
 def gr_write_f32(R, blk, inj, T, n, hc):
@@ -351,6 +362,7 @@ def ref_lib() -> ctypes.CDLL:
             "ref_pf_gr_norm_fp16": [P, P, P, P, P, I, I, I, F, P],
             "ref_gr_write_multi": [P, P, P, I, I, I, P],
             "ref_pf_gr_up_mean_fp16": [P, P, P, P, I, I, P],
+            "ref_quant_act_multi": [P, P, P, P, P, I, I, P],
             "ref_kv_append_int8_multi": [P, P, P, P, P, P, P, P, P, P, P, I, I, I, P],
             "ref_ple_gate_gv_multi": [P, P, P, P, I, I, I, P],
             "ref_ple_conv_multi": [P, P, P, P, P, I, I, P, P],

@@ -57,6 +57,13 @@ int ref_kv_append_int8_multi(const float* k, const float* v, signed char* vkq, u
     return (int)cudaGetLastError();
 }
 
+// quant_act_multi (src/wzy_kernels_v2.cuh:58-111), launched as at src/wzy_stage_v2.cuh:697.
+int ref_quant_act_multi(const float* x, signed char* q32, float* s32, signed char* q16, float* s16, int cols, int T,
+                        cudaStream_t s) {
+    quant_act_multi<<<((cols * T / 16) + 127) / 128, 128, 0, s>>>(x, q32, s32, q16, s16, cols, T);
+    return (int)cudaGetLastError();
+}
+
 // pf_gr_up_mean_fp16 (src/wzy_qsa_wmma.cuh:234-253), launched as at src/wzy_prefill_tc.cuh:712.
 int ref_pf_gr_up_mean_fp16(const __half* xn, const __half* gg, float* mixed, __half* mixed16, int T, int n_embd,
                            cudaStream_t s) {

@@ -135,16 +135,27 @@ void or_gr_norm_f32(float* R, const float* w, const float* bo, const float* inj,
 
 /* Q8_0 of one 32-element group: the xq8 path of fused_gr_norm_multi (src/wzy_kernels_v2.cuh:440-454)  */
 /* and silu_mul_quant32_multi (:1247-1279): d = amax/127; q = rint(v * 127/amax) in [-127, 127].     */
-static void q8_group(const float* v, int8_t* q, float* s) {
+static void q8_group_n(const float* v, int n, int8_t* q, float* s) {
     float am = 0.f;
-    for (int i = 0; i < 32; ++i) am = fmaxf(am, fabsf(v[i]));
+    for (int i = 0; i < n; ++i) am = fmaxf(am, fabsf(v[i]));
     const float d = am / 127.0f;
     const float inv = d > 0.f ? 127.0f / am : 0.f;
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < n; ++i) {
         int qi = (int)rintf(v[i] * inv);
         q[i] = (int8_t)(qi < -127 ? -127 : (qi > 127 ? 127 : qi));
     }
     *s = d;
+}
+
+static void q8_group(const float* v, int8_t* q, float* s) { q8_group_n(v, 32, q, s); }
+
+/* quant_act_multi (src/wzy_kernels_v2.cuh:58-111): the same rule per 32 (q32) and per 16 (q16) */
+void or_quant_act_f32(const float* x, int8_t* q32, float* s32, int8_t* q16, float* s16, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t g = 0; g < n / 16; ++g) {
+        if (q16) q8_group_n(x + g * 16, 16, q16 + g * 16, s16 + g);
+        if (q32 && (g & 1) == 0) q8_group_n(x + g * 16, 32, q32 + g * 16, s32 + g / 2);
+    }
 }
 
 void or_gr_norm_q8_f32(float* R, const float* w, const float* bo, const float* inj, float* xn, int8_t* q8,

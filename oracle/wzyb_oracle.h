@@ -35,6 +35,8 @@ void or_gr_norm_f32(float* R, const float* w, const float* bo, const float* inj,
 /* ... plus the Q8_0 side output of xn (per 32 elements: int8 codes, fp32 scale) */
 void or_gr_norm_q8_f32(float* R, const float* w, const float* bo, const float* inj, float* xn, int8_t* q8,
                        float* s8, int64_t T, int n, int hc, float eps);
+/* int8 activation quantisation per 32 and/or per 16 elements over n (multiple of 32 with q32) */
+void or_quant_act_f32(const float* x, int8_t* q32, float* s32, int8_t* q16, float* s16, int64_t n);
 /* SwiGLU fused with Q8_0 quantisation (no activation output) */
 void or_swiglu_q8_f32(const float* g, const float* u, int8_t* q, float* s, int64_t n);
 /* multi-stream residual: gated write, stream mixing, scaled SiLU to fp16 */

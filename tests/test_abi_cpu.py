@@ -73,6 +73,11 @@ def test_argument_validation_before_any_cuda_call(wz):
     assert L.wzyb_swiglu_q8_f32(A16, A16, A16, A16, 48, NULL) == wz.ERR_SHAPE
     assert L.wzyb_swiglu_q8_f32(A16, A16, A16, A8, 64, NULL) == wz.ERR_ALIGN
     assert L.wzyb_swiglu_q8_f32(A16, A16, A16, A16, 0, NULL) == wz.OK
+    # int8 activation quantisation
+    assert L.wzyb_quant_act_f32(A16, NULL, NULL, NULL, NULL, 4, 2560, NULL) == wz.ERR_NULL
+    assert L.wzyb_quant_act_f32(A16, A16, NULL, NULL, NULL, 4, 2560, NULL) == wz.ERR_NULL
+    assert L.wzyb_quant_act_f32(A16, A16, A16, NULL, NULL, 4, 2576, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_quant_act_f32(A16, A8, A16, NULL, NULL, 4, 2560, NULL) == wz.ERR_ALIGN
     # multi-stream residual
     assert L.wzyb_gr_write_f32(NULL, A16, NULL, 4, 2560, 4, NULL) == wz.ERR_NULL
     assert L.wzyb_gr_write_f32(A16, A16, NULL, 4, 2564, 4, NULL) == wz.ERR_SHAPE

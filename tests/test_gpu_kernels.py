@@ -605,3 +605,23 @@ def test_ple_conv_f32(wz, orc, T, hcd, snaps):
     assert np.array_equal(host(dh), h_ref)
     if snaps:
         assert np.array_equal(host(ds), s_ref)
+
+
+@pytest.mark.parametrize("T,cols,q32,q16", [(8, 2560, True, True), (4096, 2560, True, True), (1, 320, True, False),
+                                             (3, 48, False, True), (77, 2560, False, True)])
+def test_quant_act_f32(wz, orc, T, cols, q32, q16):
+    r = rng(T + cols)
+    x = (3 * r.standard_normal((T, cols))).astype(np.float32)
+    x[0, :32] = 0.0  # an all-zero group
+    w32, ws32, w16, ws16 = orc.quant_act_f32(x, q32, q16)
+    n = T * cols
+    d32 = torch.empty(n, dtype=torch.int8, device=DEV) if q32 else None
+    s32 = torch.empty(n // 32, dtype=torch.float32, device=DEV) if q32 else None
+    d16 = torch.empty(n, dtype=torch.int8, device=DEV) if q16 else None
+    s16 = torch.empty(n // 16, dtype=torch.float32, device=DEV) if q16 else None
+    wz.quant_act_f32(dev(x), d32, s32, d16, s16, T, cols)
+    # the same expression on the same fp32 values: identical codes and scales
+    if q32:
+        assert np.array_equal(host(d32), w32) and np.array_equal(host(s32).view(np.uint32), ws32.view(np.uint32))
+    if q16:
+        assert np.array_equal(host(d16), w16) and np.array_equal(host(s16).view(np.uint32), ws16.view(np.uint32))

@@ -394,3 +394,24 @@ def test_pin_ple_gate_and_conv(ref, orc, wz):
     oR, oh, osn = orc.ple_conv_f32(norm, cw, hist, gv, R, T, hcd, snaps=True)
     np.testing.assert_allclose(oR, host(rR), rtol=2e-6, atol=2e-6)
     assert np.array_equal(oh, host(rh)) and np.array_equal(osn, host(rs))
+
+
+def test_pin_quant_act(ref, orc, wz):
+    """quant_act_multi with both outputs (the src/wzy_stage_v2.cuh:697 launch) at n_embd 2560."""
+    r = np.random.default_rng(213)
+    T, cols = 16, 2560
+    x = (3 * r.standard_normal((T, cols))).astype(np.float32)
+    dx = dev(x)
+    n = T * cols
+    rq32, rq16 = torch.empty(n, dtype=torch.int8, device=DEV), torch.empty(n, dtype=torch.int8, device=DEV)
+    rs32, rs16 = torch.empty(n // 32, device=DEV), torch.empty(n // 16, device=DEV)
+    assert ref.ref_quant_act_multi(dx.data_ptr(), rq32.data_ptr(), rs32.data_ptr(), rq16.data_ptr(), rs16.data_ptr(),
+                                   cols, T, sp()) == 0
+    mq32, mq16 = torch.empty_like(rq32), torch.empty_like(rq16)
+    ms32, ms16 = torch.empty_like(rs32), torch.empty_like(rs16)
+    wz.quant_act_f32(dx, mq32, ms32, mq16, ms16, T, cols)
+    o32, os32, o16, os16 = orc.quant_act_f32(x)
+    for got, want, oracle in ((mq32, rq32, o32), (mq16, rq16, o16), (ms32, rs32, os32), (ms16, rs16, os16)):
+        g, w = host(got), host(want)
+        assert np.array_equal(g.view(np.uint8), w.view(np.uint8))
+        assert np.array_equal(oracle.view(np.uint8), w.view(np.uint8))

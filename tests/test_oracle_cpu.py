@@ -354,3 +354,18 @@ def test_ple_gate_and_conv_against_numpy(orc):
         for t in range(T):
             assert np.array_equal(sn[t], x[t + 1:t + 10].T.astype(np.float32))
         hist = h2
+
+
+def test_quant_act_against_numpy(orc):
+    r = np.random.default_rng(53)
+    x = (3 * r.standard_normal(32 * 40)).astype(np.float32)
+    x[64:96] = 0.0
+    q32, s32, q16, s16 = orc.quant_act_f32(x)
+    w32, d32 = _np_q8(x)
+    assert np.array_equal(q32, w32) and np.array_equal(s32, d32)
+    g = x.reshape(-1, 16)
+    am = np.abs(g).max(axis=1)
+    d = (am / np.float32(127.0)).astype(np.float32)
+    inv = np.where(d > 0, np.float32(127.0) / np.where(am > 0, am, 1), 0).astype(np.float32)
+    w16 = np.clip(np.rint(g * inv[:, None]), -127, 127).astype(np.int8).reshape(-1)
+    assert np.array_equal(q16, w16) and np.array_equal(s16, d)

@@ -369,19 +369,22 @@ __device__ __forceinline__ float2 sigmoid2(float2 z) {
     return make_float2(rcp_approx(den.x), rcp_approx(den.y));
 }
 
-// Q8_0 quantisation of one 32-element group held by 4 consecutive lanes (8 elements each), as the
-// reference's xq8 path (src/wzy_kernels_v2.cuh:440-454) and silu_mul_quant32_multi
-// (src/wzy_kernels_v2.cuh:1247-1279): amax over the group, d = amax / 127, q = rint(v * (127 / amax))
-// clamped to [-127, 127] (q = 0 when amax = 0), d stored by the group's first lane. Every lane of the
-// warp must call it (the group max is two xor shuffles); `active` lanes store.
+// Q8_0-style int8 quantisation of one group of 8*kLanes elements held by kLanes consecutive lanes (8
+// elements each): 32-element groups (kLanes 4) as the reference's xq8 path
+// (src/wzy_kernels_v2.cuh:440-454), silu_mul_quant32_multi (:1247-1279) and quant_act_multi's q32;
+// 16-element groups (kLanes 2) as quant_act_multi's q16 (:58-111). amax over the group,
+// d = amax / 127, q = rint(v * (127 / amax)) clamped to [-127, 127] (q = 0 when amax = 0), d stored
+// by the group's first lane. Every lane of the warp must call it (the group max is xor shuffles);
+// `active` lanes store.
+template <int kLanes = 4>
 __device__ __forceinline__ void q8_group_store(const float (&v)[8], bool active, signed char* q, float* s, int lane) {
     float am = 0.f;
     if (active) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
     }
-    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+#pragma unroll
+    for (int o = 1; o < kLanes; o <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
     if (!active) return;
     const float d = am / 127.0f;
     const float inv = d > 0.f ? 127.0f / am : 0.f;
@@ -392,7 +395,7 @@ __device__ __forceinline__ void q8_group_store(const float (&v)[8], bool active,
         w[i >> 2] |= ((uint32_t)(qi & 0xFF)) << ((i & 3) * 8);
     }
     *reinterpret_cast<uint2*>(q) = make_uint2(w[0], w[1]);
-    if ((lane & 3) == 0) *s = d;
+    if ((lane & (kLanes - 1)) == 0) *s = d;
 }
 
 // Sum over aligned groups of `kLanes` lanes (kLanes a power of two <= 32) with xor shuffles.

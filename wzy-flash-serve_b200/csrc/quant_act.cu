@@ -1,0 +1,51 @@
+// quant_act.cu -- fp32 activation rows to the int8 GEMM inputs, in one HBM pass.
+//
+// Math follows quant_act_multi (src/wzy_kernels_v2.cuh:58-111): per group of 32 (q32/s32) and, from
+// the same read, per group of 16 (q16/s16): d = amax / 127, q = rint(x * (127 / amax)) clamped to
+// [-127, 127]. The reference gives each thread one 16-element group (scalar 4-byte re-reads of the
+// second half for the 32-wide scale). Here a lane holds 8 elements from one 32-byte load; a 16-group
+// is 2 lanes and a 32-group 4 lanes, whose maxima are one and two xor shuffles.
+#include "launch.hpp"
+#include "common.cuh"
+
+namespace wzyb {
+
+__global__ void __launch_bounds__(256) quant_act_kernel(const float* __restrict__ x, signed char* __restrict__ q32,
+                                                        float* __restrict__ s32, signed char* __restrict__ q16,
+                                                        float* __restrict__ s16, int64_t nvec) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; base < nvec;
+         base += nwarps * 32) {
+        const int64_t v = base + lane;
+        const bool act = v < nvec;
+        float o[8] = {};
+        if (act) Vec8<float>::load_stream(x + v * 8, o);
+        if (q16 != nullptr) q8_group_store<2>(o, act, q16 + v * 8, s16 + (v >> 1), lane);
+        if (q32 != nullptr) q8_group_store<4>(o, act, q32 + v * 8, s32 + (v >> 2), lane);
+    }
+}
+
+}  // namespace wzyb
+
+extern "C" {
+
+int wzyb_quant_act_f32(const float* x, int8_t* q32, float* s32, int8_t* q16, float* s16, int64_t T, int cols,
+                       wzyb_stream_t stream) {
+    if (!x || (!q32 && !q16) || (q32 && !s32) || (q16 && !s16)) return WZYB_ERR_NULL;
+    if (T < 0 || T > (int64_t(1) << 40) || cols < 16 || (cols % (q32 ? 32 : 16)) != 0) return WZYB_ERR_SHAPE;
+    if (!wzyb::aligned16(x) || (q32 && !wzyb::aligned16(q32)) || (q16 && !wzyb::aligned16(q16)) ||
+        (s32 && ((uintptr_t)s32 & 3)) || (s16 && ((uintptr_t)s16 & 3)))
+        return WZYB_ERR_ALIGN;
+    if (T == 0) return WZYB_OK;
+    wzyb::DeviceInfo di;
+    const int rc = wzyb::device_info(&di);
+    if (rc != WZYB_OK) return rc;
+    const int64_t nvec = T * cols / 8;
+    const int grid = wzyb::persistent_grid(di, 8, (nvec + 255) / 256);
+    wzyb::quant_act_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, (signed char*)q32, s32, (signed char*)q16, s16,
+                                                                    nvec);
+    return wzyb::launch_status();
+}
+
+}  // extern "C"

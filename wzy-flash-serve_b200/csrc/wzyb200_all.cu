@@ -9,3 +9,4 @@
 #include "hc_stream.cu"
 #include "kv_append.cu"
 #include "ple_block.cu"
+#include "quant_act.cu"

@@ -112,6 +112,7 @@ _SIGS = {
     "wzyb_gr_norm_f32_f16": (c_int, [P, P, P, P, P, c_int64, c_int, c_int, c_float, S]),
     "wzyb_gr_norm_q8_f32": (c_int, [P, P, P, P, P, P, P, c_int64, c_int, c_int, c_float, S]),
     "wzyb_swiglu_q8_f32": (c_int, [P, P, P, P, c_int64, S]),
+    "wzyb_quant_act_f32": (c_int, [P, P, P, P, P, c_int64, c_int, S]),
     "wzyb_gr_write_f32": (c_int, [P, P, P, c_int64, c_int, c_int, S]),
     "wzyb_hc_mix_f16": (c_int, [P, P, P, P, c_int64, c_int, c_int, S]),
     "wzyb_hc_mix_f32": (c_int, [P, P, P, c_int64, c_int, c_int, S]),
@@ -235,6 +236,11 @@ def gr_norm_q8_f32(R, w_norm, bo_prev, inj_prev, xn, xq8, xs8, T, n_embd, hc, ep
 
 def swiglu_q8_f32(gate, up, q32, s32, stream=None):
     call("wzyb_swiglu_q8_f32", _ptr(gate), _ptr(up), _ptr(q32), _ptr(s32), gate.numel(), _stream(stream))
+
+
+def quant_act_f32(x, q32, s32, q16, s16, T, cols, stream=None):
+    """int8 per-32 (q32/s32) and/or per-16 (q16/s16) quantisation of fp32 rows x [T, cols]."""
+    call("wzyb_quant_act_f32", _ptr(x), _ptr(q32), _ptr(s32), _ptr(q16), _ptr(s16), T, cols, _stream(stream))
 
 
 def gr_write_f32(R, blk, inj, T, n_embd, hc, stream=None):

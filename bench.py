@@ -322,6 +322,10 @@ def measure_kernels_4096(wz, torch, dev, peak, reps=60):
         "swiglu_q8": (lambda s: wz.swiglu_q8_f32(g32, u32, q32, s32, stream=s), nq * (8 + 1) + nq // 8),
         "quant_act_q32_q16": (lambda s: wz.quant_act_f32(g32, q32, s32, q16b, s16b, nq // FFN, FFN, stream=s),
                               nq * (4 + 1 + 1) + nq // 32 * 4 + nq // 16 * 4),
+        "quant_act_mxfp8": (lambda s: wz.quant_act_block(g32, q16b, s16b, nq // FFN, FFN, fmt="mxfp8", stream=s),
+                            nq * (4 + 1) + nq // 32),
+        "swiglu_nvfp4": (lambda s: wz.swiglu_block(g32, u32, q16b, s16b, fmt="nvfp4", global_scale=1.0, stream=s),
+                         nq * 8 + nq // 2 + nq // 16),
     })
     s = torch.cuda.current_stream()
 

@@ -240,6 +240,34 @@ int wzyb_swiglu_q8_f32(const float* gate, const float* up, int8_t* q32, float* s
  * ========================================================================================== */
 int wzyb_quant_act_f32(const float* x, int8_t* q32, float* s32, int8_t* q16, float* s16, int64_t T, int cols,
                        wzyb_stream_t stream);
+
+/* ============================================================================================
+ * Block-scaled GEMM inputs for sm_100's tensor cores, in the same passes: the B200 form of the
+ * quantisation epilogue that the reference writes as int8 (quant_act_multi, the xq8 path of
+ * fused_gr_norm_multi, silu_mul_quant32_multi). Codes and scales are row-major over the flat
+ * element order; scale bytes need no alignment, codes 16-byte aligned.
+ *  MXFP8 (E4M3 elements, E8M0 scale, block 32): q [n] e4m3 bytes, s [n/32] E8M0 bytes. Per block:
+ *    X = 2^ceil(log2(amax / 448)) -- the smallest power of two keeping the block within +-448, so
+ *    nothing clips (OCP's floor(log2 amax) - 8 clips the block maximum by up to 12.5 %) -- s = log2(X)
+ *    + 127 (0 for an all-zero block), q = e4m3(x / X) round-to-nearest-even; inf/NaN: s = 0xFF.
+ *  NVFP4 (block 16, per-tensor scale gs): q [n/2] bytes (element 2i in the low nibble), s [n/16] e4m3
+ *    bytes. Per block: s = e4m3((amax * gs) / 6); q = e2m1(x * (gs / float(s))) round-to-nearest-even,
+ *    saturating at +-6 (0 when float(s) == 0). x ~= e2m1 * float(s) / gs.
+ * ========================================================================================== */
+int wzyb_quant_act_mxfp8_f32(const float* x, uint8_t* q, uint8_t* s, int64_t T, int cols, wzyb_stream_t stream);
+int wzyb_quant_act_nvfp4_f32(const float* x, uint8_t* q, uint8_t* s, float global_scale, int64_t T, int cols,
+                             wzyb_stream_t stream);
+/* SwiGLU (the reference's expression) straight to the block formats; n % 32 == 0. */
+int wzyb_swiglu_mxfp8_f32(const float* gate, const float* up, uint8_t* q, uint8_t* s, int64_t n,
+                          wzyb_stream_t stream);
+int wzyb_swiglu_nvfp4_f32(const float* gate, const float* up, uint8_t* q, uint8_t* s, float global_scale, int64_t n,
+                          wzyb_stream_t stream);
+/* wzyb_gr_norm_f32 with xn also written in a block format (as wzyb_gr_norm_q8_f32 writes Q8_0). */
+int wzyb_gr_norm_mxfp8_f32(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, float* xn,
+                           uint8_t* xq, uint8_t* xs, int64_t T, int n_embd, int hc, float eps, wzyb_stream_t stream);
+int wzyb_gr_norm_nvfp4_f32(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, float* xn,
+                           uint8_t* xq, uint8_t* xs, float global_scale, int64_t T, int n_embd, int hc, float eps,
+                           wzyb_stream_t stream);
 int wzyb_swiglu_interleaved_f16(const uint16_t* gu, uint16_t* out, int64_t T, int nff, wzyb_stream_t stream);
 int wzyb_swiglu_interleaved_f32_f16(const float* gu, uint16_t* out, int64_t T, int nff, wzyb_stream_t stream);
 

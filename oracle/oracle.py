@@ -29,6 +29,11 @@ _SIGS = {
     "or_gr_norm_q8_f32": (None, [P, P, P, P, P, P, P, c_int64, c_int, c_int, c_float]),
     "or_swiglu_q8_f32": (None, [P, P, P, P, c_int64]),
     "or_quant_act_f32": (None, [P, P, P, P, P, c_int64]),
+    "or_f2e4m3": (ctypes.c_uint8, [c_float]),
+    "or_e4m32f": (c_float, [ctypes.c_uint8]),
+    "or_f2e2m1": (ctypes.c_uint8, [c_float]),
+    "or_quant_mxfp8": (None, [P, P, P, c_int64]),
+    "or_quant_nvfp4": (None, [P, P, P, c_float, c_int64]),
     "or_gr_write_f32": (None, [P, P, P, c_int64, c_int, c_int]),
     "or_hc_mix_f16": (None, [P, P, P, P, c_int64, c_int, c_int]),
     "or_hc_mix_f32": (None, [P, P, P, c_int64, c_int, c_int]),
@@ -142,6 +147,22 @@ def quant_act_f32(x, q32=True, q16=True):
     lib().or_quant_act_f32(_p(x), _p(a[0]) if q32 else None, _p(a[1]) if q32 else None, _p(b[0]) if q16 else None,
                            _p(b[1]) if q16 else None, x.size)
     return a[0], a[1], b[0], b[1]
+
+
+def quant_mxfp8(x):
+    """MXFP8 of the flat fp32 array x: (e4m3 code bytes [n], E8M0 scale bytes [n/32])."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    q, sc = np.empty(x.size, np.uint8), np.empty(x.size // 32, np.uint8)
+    lib().or_quant_mxfp8(_p(x), _p(q), _p(sc), x.size)
+    return q, sc
+
+
+def quant_nvfp4(x, gs=1.0):
+    """NVFP4 of the flat fp32 array x: (e2m1 pairs [n/2], e4m3 scale bytes [n/16])."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    q, sc = np.empty(x.size // 2, np.uint8), np.empty(x.size // 16, np.uint8)
+    lib().or_quant_nvfp4(_p(x), _p(q), _p(sc), gs, x.size)
+    return q, sc
 
 
 def gr_write_f32(R, blk, inj, T, n, hc):

@@ -619,3 +619,86 @@ void or_ple_conv_f32(const float* norm, const float* cw, float* hist, const floa
         for (int i = 0; i < 9; ++i) hist[(int64_t)9 * c + i] = h[i];
     }
 }
+
+/* ------------------------------------------------------------------------------------------- */
+/* Block-scaled GEMM-input formats (no reference counterpart: the B200 form of the int8 epilogue) */
+/* e4m3 = OCP FP8 E4M3 (bias 7, max 448, NaN 0x7F), e2m1 = FP4 E2M1 {0, .5, 1, 1.5, 2, 3, 4, 6};   */
+/* both round-to-nearest-even and saturate finite overflow to the largest magnitude.             */
+/* ------------------------------------------------------------------------------------------- */
+uint8_t or_f2e4m3(float f) {
+    const uint8_t sign = signbit(f) ? 0x80 : 0x00;
+    if (isnan(f)) return 0x7F;
+    const float a = fabsf(f);
+    if (a >= 448.0f) return (uint8_t)(sign | 0x7E);
+    if (a < 0.015625f) /* below 2^-6: subnormal steps of 2^-9 (q == 8 is the first normal) */
+        return (uint8_t)(sign | (uint8_t)rintf(a * 512.0f));
+    int e;
+    frexpf(a, &e); /* a in [2^(e-1), 2^e) */
+    const int E = e - 1;
+    const float q = rintf(ldexpf(a, 3 - E)); /* 8..16 steps of 2^(E-3); 16 carries into the next binade */
+    return (uint8_t)(sign | (uint8_t)(((E + 7) << 3) + (int)q - 8));
+}
+
+float or_e4m32f(uint8_t b) {
+    const int sg = (b >> 7) & 1, e = (b >> 3) & 0xF, m = b & 7;
+    float f;
+    if (e == 15 && m == 7) return NAN;
+    if (e == 0) f = ldexpf((float)m, -9);
+    else f = ldexpf(1.f + (float)m / 8.f, e - 7);
+    return sg ? -f : f;
+}
+
+uint8_t or_f2e2m1(float f) {
+    const uint8_t sign = signbit(f) ? 0x8 : 0x0;
+    const float a = fabsf(f);
+    if (isnan(f)) return 0x7; /* the hardware's choice: positive largest */
+    if (a >= 6.0f) return (uint8_t)(sign | 0x7);
+    if (a < 2.0f) return (uint8_t)(sign | (uint8_t)rintf(a * 2.0f));     /* 0, .5, 1, 1.5, (2) */
+    if (a < 4.0f) return (uint8_t)(sign | (uint8_t)(rintf(a) + 2.0f));  /* 2, 3, (4) */
+    return (uint8_t)(sign | (uint8_t)(rintf(a * 0.5f) + 4.0f));        /* 4, 6 */
+}
+
+/* MXFP8: per 32, scale X = 2^ceil(log2(amax / 448)) (the smallest power of two keeping the block   */
+/* within +-448) as the E8M0 byte log2(X) + 127; codes e4m3(x / X). amax == 0 -> byte 0; inf/NaN -> 0xFF */
+static uint32_t mxfp8_scale_byte(float amax) {
+    const float t = amax / 448.0f;
+    uint32_t tb;
+    memcpy(&tb, &t, 4);
+    const uint32_t et = tb >> 23;
+    if (et == 0xFFu) return 0xFFu;
+    if (et == 0u) return tb <= 0x00400000u ? 0u : 1u;
+    return et + ((tb & 0x7FFFFFu) != 0u ? 1u : 0u);
+}
+
+void or_quant_mxfp8(const float* x, uint8_t* q, uint8_t* s, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t g = 0; g < n / 32; ++g) {
+        float am = 0.f;
+        for (int i = 0; i < 32; ++i) am = fmaxf(am, fabsf(x[g * 32 + i]));
+        const uint32_t e8 = mxfp8_scale_byte(am);
+        float inv = 0.f;
+        if (e8 != 0xFFu) {
+            const uint32_t ib = (254u - e8) << 23;
+            memcpy(&inv, &ib, 4);
+        }
+        for (int i = 0; i < 32; ++i) q[g * 32 + i] = or_f2e4m3(x[g * 32 + i] * inv);
+        s[g] = (uint8_t)e8;
+    }
+}
+
+/* NVFP4: per 16, scale byte e4m3((amax * gs) / 6), codes e2m1(x * (gs / float(scale))) */
+void or_quant_nvfp4(const float* x, uint8_t* q, uint8_t* s, float gs, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t g = 0; g < n / 16; ++g) {
+        float am = 0.f;
+        for (int i = 0; i < 16; ++i) am = fmaxf(am, fabsf(x[g * 16 + i]));
+        const uint8_t sc = or_f2e4m3((am * gs) / 6.0f);
+        const float sf = or_e4m32f(sc);
+        const float r = sf > 0.f ? gs / sf : 0.f;
+        for (int i = 0; i < 8; ++i) {
+            const uint8_t lo = or_f2e2m1(x[g * 16 + 2 * i] * r), hi = or_f2e2m1(x[g * 16 + 2 * i + 1] * r);
+            q[g * 8 + i] = (uint8_t)(lo | (hi << 4));
+        }
+        s[g] = sc;
+    }
+}

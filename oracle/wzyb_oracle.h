@@ -37,6 +37,12 @@ void or_gr_norm_q8_f32(float* R, const float* w, const float* bo, const float* i
                        float* s8, int64_t T, int n, int hc, float eps);
 /* int8 activation quantisation per 32 and/or per 16 elements over n (multiple of 32 with q32) */
 void or_quant_act_f32(const float* x, int8_t* q32, float* s32, int8_t* q16, float* s16, int64_t n);
+/* block-scaled formats: element codecs and the MXFP8 / NVFP4 quantisers over n (a multiple of 32 / 16) */
+uint8_t or_f2e4m3(float f);
+float or_e4m32f(uint8_t b);
+uint8_t or_f2e2m1(float f);
+void or_quant_mxfp8(const float* x, uint8_t* q, uint8_t* s, int64_t n);
+void or_quant_nvfp4(const float* x, uint8_t* q, uint8_t* s, float gs, int64_t n);
 /* SwiGLU fused with Q8_0 quantisation (no activation output) */
 void or_swiglu_q8_f32(const float* g, const float* u, int8_t* q, float* s, int64_t n);
 /* multi-stream residual: gated write, stream mixing, scaled SiLU to fp16 */

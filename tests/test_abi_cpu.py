@@ -78,6 +78,16 @@ def test_argument_validation_before_any_cuda_call(wz):
     assert L.wzyb_quant_act_f32(A16, A16, NULL, NULL, NULL, 4, 2560, NULL) == wz.ERR_NULL
     assert L.wzyb_quant_act_f32(A16, A16, A16, NULL, NULL, 4, 2576, NULL) == wz.ERR_SHAPE
     assert L.wzyb_quant_act_f32(A16, A8, A16, NULL, NULL, 4, 2560, NULL) == wz.ERR_ALIGN
+    # block-scaled formats: group sizes 32 (MXFP8) / 16 (NVFP4)
+    assert L.wzyb_quant_act_mxfp8_f32(A16, NULL, A16, 4, 2560, NULL) == wz.ERR_NULL
+    assert L.wzyb_quant_act_mxfp8_f32(A16, A16, A16, 4, 2576, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_quant_act_nvfp4_f32(A16, A16, A16, 1.0, 4, 2568, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_quant_act_nvfp4_f32(A8, A16, A16, 1.0, 4, 2560, NULL) == wz.ERR_ALIGN
+    assert L.wzyb_swiglu_mxfp8_f32(A16, A16, A16, A16, 48, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_swiglu_nvfp4_f32(A16, A16, NULL, A16, 1.0, 64, NULL) == wz.ERR_NULL
+    assert L.wzyb_gr_norm_mxfp8_f32(A16, A16, A16, A16, A16, A16, A16, 4, 2568, 4, 1e-6, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_gr_norm_nvfp4_f32(A16, A16, A16, A16, A16, A8, A16, 1.0, 4, 2560, 4, 1e-6, NULL) == wz.ERR_ALIGN
+    assert L.wzyb_gr_norm_nvfp4_f32(A16, A16, A16, A16, A16, A16, A16, 1.0, 0, 2560, 4, 1e-6, NULL) == wz.OK
     # multi-stream residual
     assert L.wzyb_gr_write_f32(NULL, A16, NULL, 4, 2560, 4, NULL) == wz.ERR_NULL
     assert L.wzyb_gr_write_f32(A16, A16, NULL, 4, 2564, 4, NULL) == wz.ERR_SHAPE

@@ -625,3 +625,68 @@ def test_quant_act_f32(wz, orc, T, cols, q32, q16):
         assert np.array_equal(host(d32), w32) and np.array_equal(host(s32).view(np.uint32), ws32.view(np.uint32))
     if q16:
         assert np.array_equal(host(d16), w16) and np.array_equal(host(s16).view(np.uint32), ws16.view(np.uint32))
+
+
+# ---------------------------------------------------------------------------------------------
+# block-scaled GEMM inputs: MXFP8 and NVFP4
+# ---------------------------------------------------------------------------------------------
+def _block_inputs(r, T, cols):
+    # rows of very different magnitudes (and an all-zero group) exercise the per-block scales
+    x = (r.standard_normal((T, cols)) * 10.0 ** r.uniform(-3, 3, (T, 1))).astype(np.float32)
+    x[0, :32] = 0.0
+    return x
+
+
+def _dev_block_out(n, fmt):
+    q = torch.empty(n if fmt == "mxfp8" else n // 2, dtype=torch.uint8, device=DEV)
+    s = torch.empty(n // (32 if fmt == "mxfp8" else 16), dtype=torch.uint8, device=DEV)
+    return q, s
+
+
+def _oracle_block(orc, x, fmt, gs):
+    return orc.quant_mxfp8(x) if fmt == "mxfp8" else orc.quant_nvfp4(x, gs)
+
+
+@pytest.mark.parametrize("fmt,gs", [("mxfp8", 1.0), ("nvfp4", 1.0), ("nvfp4", 448.0 * 6.0 / 37.0)])
+@pytest.mark.parametrize("T,cols", [(8, 2560), (4096, 2560), (3, 32)])
+def test_quant_act_block_formats(wz, orc, fmt, gs, T, cols):
+    x = _block_inputs(rng(T + cols), T, cols)
+    want_q, want_s = _oracle_block(orc, x, fmt, gs)
+    q, s = _dev_block_out(T * cols, fmt)
+    wz.quant_act_block(dev(x), q, s, T, cols, fmt=fmt, global_scale=gs)
+    assert np.array_equal(host(q), want_q) and np.array_equal(host(s), want_s)
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8", "nvfp4"])
+def test_gr_norm_block_formats(wz, orc, fmt):
+    """The norm's fp32 output and, from exactly those values, its block-format codes."""
+    r = rng(61)
+    T, n, hc = 9, 2560, 4
+    R = r.standard_normal((T * hc, n)).astype(np.float32)
+    bo = r.standard_normal((T, n)).astype(np.float32)
+    inj = r.standard_normal(T * hc).astype(np.float32)
+    w = (1 + 0.02 * r.standard_normal((hc, n))).astype(np.float32)
+    xn_ref, _, R_ref = orc.gr_norm_f32(R, w, bo, inj, T, n, hc)
+    dR, dxn = dev(R), torch.empty((T * hc, n), dtype=torch.float32, device=DEV)
+    q, s = _dev_block_out(T * hc * n, fmt)
+    wz.gr_norm_block(dR, dev(w), dev(bo), dev(inj), dxn, q, s, T, n, hc, fmt=fmt, global_scale=3.0)
+    xn = host(dxn)
+    np.testing.assert_allclose(xn, xn_ref, rtol=2e-6, atol=2e-6)
+    np.testing.assert_allclose(host(dR), R_ref, rtol=1e-6, atol=1e-6)
+    want_q, want_s = _oracle_block(orc, xn, fmt, 3.0)
+    assert np.array_equal(host(q), want_q) and np.array_equal(host(s), want_s)
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8", "nvfp4"])
+def test_swiglu_block_formats(wz, orc, fmt):
+    r = rng(62)
+    n = 640 * 512
+    g = (2 * r.standard_normal(n)).astype(np.float32)
+    u = r.standard_normal(n).astype(np.float32)
+    act = orc.swiglu(g, u)  # libm expf: the kernel's __expf can move a value across a rounding boundary
+    want_q, want_s = _oracle_block(orc, act, fmt, 1.0)
+    q, s = _dev_block_out(n, fmt)
+    wz.swiglu_block(dev(g), dev(u), q, s, fmt=fmt)
+    gq, gs_ = host(q), host(s)
+    assert (gs_ != want_s).mean() < 1e-3
+    assert (gq != want_q).mean() < 1e-3

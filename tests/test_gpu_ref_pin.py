@@ -422,3 +422,22 @@ def test_pin_quant_act(ref, orc, wz):
         g, w = host(got), host(want)
         assert np.array_equal(g.view(np.uint8), w.view(np.uint8))
         assert np.array_equal(oracle.view(np.uint8), w.view(np.uint8))
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8", "nvfp4"])
+def test_pin_swiglu_block_formats(ref, orc, wz, fmt):
+    """SwiGLU straight to MXFP8 / NVFP4 equals the oracle's quantiser applied to the reference's own
+    silu_mul_multi output (the same fp32 expression)."""
+    r = np.random.default_rng(214)
+    n = 640 * 64
+    g = (2 * r.standard_normal(n)).astype(np.float32)
+    u = r.standard_normal(n).astype(np.float32)
+    dg, du = dev(g), dev(u)
+    act = torch.empty(n, dtype=torch.float32, device=DEV)
+    assert ref.ref_silu_mul_multi(dg.data_ptr(), du.data_ptr(), act.data_ptr(), n, sp()) == 0
+    a = host(act)
+    want_q, want_s = orc.quant_mxfp8(a) if fmt == "mxfp8" else orc.quant_nvfp4(a, 2.5)
+    q = torch.empty(n if fmt == "mxfp8" else n // 2, dtype=torch.uint8, device=DEV)
+    s = torch.empty(n // (32 if fmt == "mxfp8" else 16), dtype=torch.uint8, device=DEV)
+    wz.swiglu_block(dg, du, q, s, fmt=fmt, global_scale=2.5)
+    assert np.array_equal(host(q), want_q) and np.array_equal(host(s), want_s)

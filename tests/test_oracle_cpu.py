@@ -369,3 +369,72 @@ def test_quant_act_against_numpy(orc):
     inv = np.where(d > 0, np.float32(127.0) / np.where(am > 0, am, 1), 0).astype(np.float32)
     w16 = np.clip(np.rint(g * inv[:, None]), -127, 127).astype(np.int8).reshape(-1)
     assert np.array_equal(q16, w16) and np.array_equal(s16, d)
+
+
+def _e2m1_exact(v):
+    """Round-to-nearest-even onto {0, .5, 1, 1.5, 2, 3, 4, 6} (saturating), as a code with sign bit 8."""
+    from fractions import Fraction
+
+    grid = [Fraction(0), Fraction(1, 2), Fraction(1), Fraction(3, 2), Fraction(2), Fraction(3), Fraction(4),
+            Fraction(6)]
+    a = abs(Fraction(float(v)))
+    if a >= 6:
+        code = 7
+    else:
+        best = min(range(8), key=lambda c: (abs(grid[c] - a), c & 1))  # tie -> even code (mantissa 0)
+        code = best
+    return code | (8 if np.signbit(v) else 0)
+
+
+def test_block_format_codecs(orc):
+    import torch
+
+    L = orc.lib()
+    r = np.random.default_rng(54)
+    # e4m3 encode == torch's float8_e4m3fn below the saturation point, including exact ties and subnormals
+    steps = np.concatenate([np.arange(0, 16) * 2.0 ** -9, *(np.arange(8, 16) * 2.0 ** (e - 3) for e in range(-6, 9))])
+    ties = (steps[:-1] + steps[1:]) / 2
+    x = np.concatenate([steps, ties, r.standard_normal(4000) * 10.0 ** r.integers(-4, 3, 4000)]).astype(np.float32)
+    x = x[np.abs(x) < 448]
+    x = np.concatenate([x, -x])
+    got = np.array([L.or_f2e4m3(float(v)) for v in x], dtype=np.uint8)
+    want = torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(got, want)
+    assert L.or_f2e4m3(448.0) == 0x7E and L.or_f2e4m3(1e9) == 0x7E and L.or_f2e4m3(-500.0) == 0xFE
+    # e4m3 decode of every non-NaN code == torch
+    codes = np.array([c for c in range(256) if (c & 0x7F) != 0x7F], dtype=np.uint8)
+    dec = np.array([L.or_e4m32f(int(c)) for c in codes], dtype=np.float32)
+    assert np.array_equal(dec, torch.from_numpy(codes).view(torch.float8_e4m3fn).float().numpy())
+    # e2m1 encode == the exact rational rounding, on a dense grid with every tie
+    y = np.concatenate([np.arange(-8, 8, 1 / 64), r.uniform(-7, 7, 2000)]).astype(np.float32)
+    assert [L.or_f2e2m1(float(v)) for v in y] == [_e2m1_exact(v) for v in y]
+
+
+def test_block_quantisers_against_numpy(orc):
+    L = orc.lib()
+    r = np.random.default_rng(55)
+    x = (r.standard_normal(32 * 24) * np.repeat(10.0 ** r.uniform(-3, 3, 24), 32)).astype(np.float32)
+    x[:32] = 0.0
+    q, s = orc.quant_mxfp8(x)
+    g = x.reshape(-1, 32)
+    am = np.abs(g).max(axis=1)
+    # the smallest power-of-two scale X with amax / X <= 448, as an E8M0 byte
+    e8 = np.array([0 if a == 0 else 127 + int(np.ceil(np.log2(np.float64(np.float32(a / np.float32(448.0))))))
+                   for a in am], dtype=np.uint32)
+    inv = ((254 - e8) << 23).astype(np.uint32).view(np.float32)
+    want_q = np.array([L.or_f2e4m3(float(v)) for v in (g * inv[:, None]).reshape(-1)], dtype=np.uint8)
+    assert np.array_equal(s, e8.astype(np.uint8)) and np.array_equal(q, want_q)
+    # nothing saturates: every element decodes within half an e4m3 step (2^-4 relative for normals,
+    # 2^-10 of the scale in the subnormal range)
+    dec = np.array([L.or_e4m32f(int(c)) for c in q], dtype=np.float64).reshape(-1, 32) / inv[:, None]
+    assert np.all(np.abs(dec - g) <= np.maximum(np.abs(g) * 2.0 ** -4, 2.0 ** -10 / inv[:, None]))
+    # NVFP4 with a per-tensor scale
+    gs = np.float32(37.0)
+    q4, s4 = orc.quant_nvfp4(x, gs)
+    g16 = x.reshape(-1, 16)
+    sc = np.array([L.or_f2e4m3(float(np.float32(np.float32(a * gs) / np.float32(6.0)))) for a in np.abs(g16).max(1)],
+                  dtype=np.uint8)
+    sf = np.array([L.or_e4m32f(int(c)) for c in sc], dtype=np.float32)
+    rr = np.where(sf > 0, gs / np.where(sf > 0, sf, 1), 0).astype(np.float32)
+    codes = np.array([L.or_f2e2m1(float(v)) for v in (g16 * rr[:, None]).astype(np.float32).reshape(-1)], np.uint8)
+    assert np.array_equal(s4, sc) and np.array_equal(q4, codes[0::2] | (codes[1::2] << 4))

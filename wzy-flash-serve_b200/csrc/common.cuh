@@ -6,8 +6,11 @@
 // up after a time limit instead of spinning forever.
 #pragma once
 #include <cuda_fp16.h>
+#include <cuda_fp4.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <cstring>
 
 #include "../../include/wzyb200.h"
 
@@ -396,6 +399,96 @@ __device__ __forceinline__ void q8_group_store(const float (&v)[8], bool active,
     }
     *reinterpret_cast<uint2*>(q) = make_uint2(w[0], w[1]);
     if ((lane & (kLanes - 1)) == 0) *s = d;
+}
+
+// Shared scale of an MXFP8 block as its E8M0 byte: X = 2^ceil(log2(amax / 448)), the smallest power
+// of two that keeps every element of the block within E4M3's +-448 (OCP's floor(log2 amax) - 8 would
+// clip the block maximum by up to 12.5 %). Integer work on the bits of t = amax / 448; t == 0 gives
+// the smallest scale 2^-127 (byte 0), inf/NaN gives the E8M0 NaN byte 0xFF. Host-callable so the
+// oracle-facing code paths agree bit for bit.
+__host__ __device__ __forceinline__ uint32_t mxfp8_scale_byte(float amax) {
+    const float t = amax / 448.0f;
+    uint32_t tb;
+    memcpy(&tb, &t, 4);
+    const uint32_t et = tb >> 23;  // t >= 0
+    if (et == 0xFFu) return 0xFFu;
+    if (et == 0u) return tb <= 0x00400000u ? 0u : 1u;  // zero or subnormal t: 2^-127 or 2^-126
+    return et + ((tb & 0x7FFFFFu) != 0u ? 1u : 0u);
+}
+
+// MXFP8 (E4M3 elements, E8M0 scale, block 32; the block-scaled MMA's MX format), one 32-element
+// group over 4 consecutive lanes: scale byte e8 = mxfp8_scale_byte(amax), codes e4m3(x * 2^(127 - e8)),
+// round-to-nearest-even, saturating at +-448. Every lane must call it; `active` lanes store 8 bytes.
+__device__ __forceinline__ void mxfp8_group_store(const float (&v)[8], bool active, uint8_t* q, uint8_t* s,
+                                                  int lane) {
+    float am = 0.f;
+    if (active) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
+    }
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+    if (!active) return;
+    const uint32_t e8 = mxfp8_scale_byte(am);
+    const float inv = e8 == 0xFFu ? 0.f : __uint_as_float((254u - e8) << 23);  // 1 / X
+    uint32_t w[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(v[4 * k] * inv, v[4 * k + 1] * inv), __NV_SATFINITE,
+                                                     __NV_E4M3);
+        const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(v[4 * k + 2] * inv, v[4 * k + 3] * inv),
+                                                     __NV_SATFINITE, __NV_E4M3);
+        w[k] = lo | (hi << 16);
+    }
+    *reinterpret_cast<uint2*>(q) = make_uint2(w[0], w[1]);
+    if ((lane & 3) == 0) *s = (uint8_t)e8;
+}
+
+// NVFP4 (E2M1 elements, E4M3 block scale, block 16, plus a per-tensor scale gs), one 16-element group
+// over 2 consecutive lanes. Scale byte sc = e4m3((amax * gs) / 6) (6 = the largest E2M1 value);
+// codes e2m1(x * (gs / float(sc))), 0 when sc decodes to 0; round-to-nearest-even, saturating at +-6.
+// A lane's 8 codes are 4 bytes, element 2i in the low nibble of byte i. Dequantisation:
+// x ~= e2m1 * float(sc) / gs. Every lane must call it.
+__device__ __forceinline__ void nvfp4_group_store(const float (&v)[8], bool active, float gs, uint8_t* q,
+                                                  uint8_t* s, int lane) {
+    float am = 0.f;
+    if (active) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
+    }
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+    if (!active) return;
+    const __nv_fp8_storage_t sc = __nv_cvt_float_to_fp8((am * gs) / 6.0f, __NV_SATFINITE, __NV_E4M3);
+    const __half_raw hr = __nv_cvt_fp8_to_halfraw(sc, __NV_E4M3);
+    const float sf = __half2float(__half(hr));
+    const float r = sf > 0.f ? gs / sf : 0.f;
+    uint32_t w = 0u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t b = __nv_cvt_float2_to_fp4x2(make_float2(v[2 * i] * r, v[2 * i + 1] * r), __NV_E2M1,
+                                                    cudaRoundNearest);
+        w |= (b & 0xFFu) << (8 * i);
+    }
+    *reinterpret_cast<uint32_t*>(q) = w;
+    if ((lane & 1) == 0) *s = (uint8_t)sc;
+}
+
+// GEMM-input quantisation formats of the fused and standalone quantisers.
+enum QuantFormat : int { kQfNone = 0, kQfQ8 = 1, kQfMxfp8 = 2, kQfNvfp4 = 3 };
+
+// Store this lane's 8 values (flat 8-element vector index vi of the tensor) in format QF: codes at q,
+// scales at s (Q8: int8 + fp32 per 32; MXFP8: e4m3 + E8M0 byte per 32; NVFP4: e2m1 pairs + E4M3 byte
+// per 16, per-tensor scale gs). Every lane of the warp must call it.
+template <int QF>
+__device__ __forceinline__ void quant_group_store(const float (&v)[8], bool active, void* q, void* s, float gs,
+                                                  int64_t vi, int lane) {
+    if (QF == kQfQ8) {
+        q8_group_store<4>(v, active, static_cast<signed char*>(q) + vi * 8, static_cast<float*>(s) + (vi >> 2), lane);
+    } else if (QF == kQfMxfp8) {
+        mxfp8_group_store(v, active, static_cast<uint8_t*>(q) + vi * 8, static_cast<uint8_t*>(s) + (vi >> 2), lane);
+    } else if (QF == kQfNvfp4) {
+        nvfp4_group_store(v, active, gs, static_cast<uint8_t*>(q) + vi * 4, static_cast<uint8_t*>(s) + (vi >> 1), lane);
+    }
 }
 
 // Sum over aligned groups of `kLanes` lanes (kLanes a power of two <= 32) with xor shuffles.

@@ -27,8 +27,9 @@ struct NormRowsArgs {
     int stages;
     uint32_t row_bytes;
     uint32_t stage_bytes;
-    signed char* q8;  // optional Q8_0 codes of xn [T*hc, n] (wide design only)
-    float* s8;        // its per-32-element scales [T*hc, n/32]
+    void* qout;  // optional quantised xn (wide design only): codes in the QuantFormat of the launch
+    void* sout;  // and its group scales
+    float gs;    // NVFP4 per-tensor scale
 };
 
 template <typename TI, typename TO, int VPT>
@@ -311,12 +312,13 @@ __global__ void __launch_bounds__(128) norm_rows_async_kernel(const NormRowsArgs
 // reference model's 2560-wide fp32 streams among them): a CTA of NW = blockDim/32 warps (4, 8 or 16)
 // owns one row at a time. Thread i of the CTA holds the 8-element vectors k*blockDim + i (k < VPL),
 // so each warp-wide load still covers 512 contiguous bytes and every 32-element group sits in 4
-// consecutive lanes of one warp (the Q8_0 side output quantises it with two shuffles). The warps'
+// consecutive lanes of one warp (the quantised side output -- Q8_0, MXFP8 or NVFP4 -- takes its
+// group max with one or two shuffles). The warps'
 // partial sums of squares meet in shared memory behind ONE barrier per row: the partials are
 // double-buffered by row parity, and a warp can only come back to a slot after passing the next
 // row's barrier, which the slowest warp reaches only once it has read the slot. Rows are spread
 // over a persistent grid; several CTAs per SM keep rows in flight across the barriers.
-template <typename TI, typename TO, int VPL, bool Q8>
+template <typename TI, typename TO, int VPL, int QF>
 __global__ void __launch_bounds__(512) norm_rows_wide_kernel(const NormRowsArgs a) {
     __shared__ float part[2][16];
     const int lane = threadIdx.x & 31;
@@ -385,9 +387,9 @@ __global__ void __launch_bounds__(512) norm_rows_wide_kernel(const NormRowsArgs 
                 Vec8<TO>::store2(y + u * n + e, o);
                 if (has_x) Vec8<TI>::store2(res + u * n + e, v);
             }
-            if (Q8) {  // every lane: the group max is a shuffle
+            if (QF != kQfNone) {  // every lane: the group max is a shuffle
                 const float yo[8] = {o[0].x, o[0].y, o[1].x, o[1].y, o[2].x, o[2].y, o[3].x, o[3].y};
-                q8_group_store(yo, e < n, a.q8 + u * n + e, a.s8 + ((u * n + e) >> 5), lane);
+                quant_group_store<QF>(yo, e < n, a.qout, a.sout, a.gs, (u * n + e) >> 3, lane);
             }
         }
     }
@@ -405,21 +407,21 @@ static void wide_shape(int vecs, int& nw, int& vpl) {
     vpl = need <= 1 ? 1 : need <= 2 ? 2 : need <= 3 ? 3 : need <= 4 ? 4 : need <= 6 ? 6 : 8;
 }
 
-template <typename TI, typename TO, bool Q8>
+template <typename TI, typename TO, int QF>
 static int launch_norm_rows_wide(const NormRowsArgs& a, const DeviceInfo& di, cudaStream_t stream) {
     int nw = 0, vpl = 0;
     wide_shape<TI>(a.n / 8, nw, vpl);
     const int threads = nw * 32;
     const void* kern = nullptr;
 #define WZYB_NRW(V) \
-    if (vpl == V) kern = (const void*)norm_rows_wide_kernel<TI, TO, V, Q8>;
+    if (vpl == V) kern = (const void*)norm_rows_wide_kernel<TI, TO, V, QF>;
     WZYB_NRW(1) WZYB_NRW(2) WZYB_NRW(3) WZYB_NRW(4)
     if constexpr (sizeof(TI) == 2) { WZYB_NRW(6) WZYB_NRW(8) }
 #undef WZYB_NRW
     if (kern == nullptr) return WZYB_ERR_SHAPE;
     const int grid = persistent_grid(di, resident_ctas(kern, threads, 0), a.units);
 #define WZYB_NRW(V) \
-    if (vpl == V) norm_rows_wide_kernel<TI, TO, V, Q8><<<grid, threads, 0, stream>>>(a);
+    if (vpl == V) norm_rows_wide_kernel<TI, TO, V, QF><<<grid, threads, 0, stream>>>(a);
     WZYB_NRW(1) WZYB_NRW(2) WZYB_NRW(3) WZYB_NRW(4)
     if constexpr (sizeof(TI) == 2) { WZYB_NRW(6) WZYB_NRW(8) }
 #undef WZYB_NRW
@@ -454,8 +456,8 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
     a.w_offset = w_offset;
     a.row_bytes = (uint32_t)(n * sizeof(TI));
     a.stage_bytes = a.row_bytes * (x ? 2u : 1u);
-    a.q8 = nullptr;
-    a.s8 = nullptr;
+    a.qout = a.sout = nullptr;
+    a.gs = 1.0f;
 
     // Direct design while a row fits one warp's register budget (<= 12 fp16 or 6 fp32 vectors per
     // lane), the wide design (CTA-owned rows) past it; the TMA ring only on request.
@@ -463,7 +465,7 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
     const int vpl_max = sizeof(TI) == 2 ? 12 : 6;
     const int var = variant(kFamNorm);
     if (var == WZYB_VARIANT_WIDE || (var != WZYB_VARIANT_RING && vpl_need > vpl_max))
-        return launch_norm_rows_wide<TI, TO, false>(a, di, stream);
+        return launch_norm_rows_wide<TI, TO, kQfNone>(a, di, stream);
     if (var == WZYB_VARIANT_ASYNC && vpl_need <= (sizeof(TI) == 2 ? 8 : 4)) {
         const int vpl = vpl_need <= 1 ? 1 : vpl_need <= 2 ? 2 : vpl_need <= 4 ? 4 : 8;
         // one row in flight per warp when every row of the call fits in one round, else two
@@ -545,15 +547,16 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
     return launch_status();
 }
 
-// Residual fold + norm with the Q8_0 side output: the wide design at every width (n <= 16384).
-template <typename TI, typename TO>
-static int launch_norm_rows_q8(const void* x, void* res, const void* w, const float* inj, void* y, signed char* q8,
-                               float* s8, int64_t T, int n, int hc, float eps, cudaStream_t stream) {
-    if (res == nullptr || w == nullptr || y == nullptr || q8 == nullptr || s8 == nullptr) return WZYB_ERR_NULL;
+// Residual fold + norm with a quantised side output of xn (format QF: Q8_0, MXFP8 or NVFP4): the
+// wide design at every width (n <= 16384; n % 32 == 0, the largest group).
+template <typename TI, typename TO, int QF>
+static int launch_norm_rows_quant(const void* x, void* res, const void* w, const float* inj, void* y, void* qout,
+                                  void* sout, float gs, int64_t T, int n, int hc, float eps, cudaStream_t stream) {
+    if (res == nullptr || w == nullptr || y == nullptr || qout == nullptr || sout == nullptr) return WZYB_ERR_NULL;
     if (T < 0 || T > (int64_t(1) << 40) || n < 32 || n > 16384 || (n % 32) != 0 || hc < 1 || hc > 64)
         return WZYB_ERR_SHAPE;
-    if (!aligned16(res) || !aligned16(w) || !aligned16(y) || (x && !aligned16(x)) || !aligned16(q8) ||
-        !aligned16(s8))
+    if (!aligned16(res) || !aligned16(w) || !aligned16(y) || (x && !aligned16(x)) || !aligned16(qout) ||
+        (QF == kQfQ8 ? !aligned16(sout) : false))
         return WZYB_ERR_ALIGN;
     if (T == 0) return WZYB_OK;
     DeviceInfo di;
@@ -572,9 +575,10 @@ static int launch_norm_rows_q8(const void* x, void* res, const void* w, const fl
     a.w_offset = 0.0f;
     a.stages = 0;
     a.row_bytes = a.stage_bytes = 0;
-    a.q8 = q8;
-    a.s8 = s8;
-    return launch_norm_rows_wide<TI, TO, true>(a, di, stream);
+    a.qout = qout;
+    a.sout = sout;
+    a.gs = gs;
+    return launch_norm_rows_wide<TI, TO, QF>(a, di, stream);
 }
 
 }  // namespace wzyb
@@ -583,8 +587,22 @@ extern "C" {
 
 int wzyb_gr_norm_q8_f32(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, float* xn,
                         int8_t* xq8, float* xs8, int64_t T, int n_embd, int hc, float eps, wzyb_stream_t stream) {
-    return wzyb::launch_norm_rows_q8<float, float>(bo_prev, R, w_norm, inj_prev, xn, (signed char*)xq8, xs8, T,
-                                                   n_embd, hc, eps, (cudaStream_t)stream);
+    return wzyb::launch_norm_rows_quant<float, float, wzyb::kQfQ8>(bo_prev, R, w_norm, inj_prev, xn, xq8, xs8, 1.0f, T,
+                                                                 n_embd, hc, eps, (cudaStream_t)stream);
+}
+
+int wzyb_gr_norm_mxfp8_f32(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, float* xn,
+                           uint8_t* xq, uint8_t* xs, int64_t T, int n_embd, int hc, float eps, wzyb_stream_t stream) {
+    return wzyb::launch_norm_rows_quant<float, float, wzyb::kQfMxfp8>(bo_prev, R, w_norm, inj_prev, xn, xq, xs, 1.0f,
+                                                                    T, n_embd, hc, eps, (cudaStream_t)stream);
+}
+
+int wzyb_gr_norm_nvfp4_f32(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, float* xn,
+                           uint8_t* xq, uint8_t* xs, float global_scale, int64_t T, int n_embd, int hc, float eps,
+                           wzyb_stream_t stream) {
+    return wzyb::launch_norm_rows_quant<float, float, wzyb::kQfNvfp4>(bo_prev, R, w_norm, inj_prev, xn, xq, xs,
+                                                                    global_scale, T, n_embd, hc, eps,
+                                                                    (cudaStream_t)stream);
 }
 
 int wzyb_add_rmsnorm_f16(const uint16_t* x, uint16_t* residual, const uint16_t* weight, uint16_t* y, int64_t T,

@@ -5,6 +5,10 @@
 // [-127, 127]. The reference gives each thread one 16-element group (scalar 4-byte re-reads of the
 // second half for the 32-wide scale). Here a lane holds 8 elements from one 32-byte load; a 16-group
 // is 2 lanes and a 32-group 4 lanes, whose maxima are one and two xor shuffles.
+//
+// The same pass also writes the block-scaled formats that sm_100's tensor cores take as GEMM
+// inputs (tcgen05.mma block scaling): MXFP8 (e4m3 codes, E8M0 scale per 32) and NVFP4 (e2m1 codes
+// two per byte, e4m3 scale per 16, a per-tensor scale). Their rules are in common.cuh.
 #include "launch.hpp"
 #include "common.cuh"
 
@@ -24,6 +28,38 @@ __global__ void __launch_bounds__(256) quant_act_kernel(const float* __restrict_
         if (q16 != nullptr) q8_group_store<2>(o, act, q16 + v * 8, s16 + (v >> 1), lane);
         if (q32 != nullptr) q8_group_store<4>(o, act, q32 + v * 8, s32 + (v >> 2), lane);
     }
+}
+
+template <int QF>
+__global__ void __launch_bounds__(256) quant_act_block_kernel(const float* __restrict__ x, void* __restrict__ q,
+                                                              void* __restrict__ s, float gs, int64_t nvec) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; base < nvec;
+         base += nwarps * 32) {
+        const int64_t v = base + lane;
+        const bool act = v < nvec;
+        float o[8] = {};
+        if (act) Vec8<float>::load_stream(x + v * 8, o);
+        quant_group_store<QF>(o, act, q, s, gs, v, lane);
+    }
+}
+
+template <int QF>
+static int launch_quant_act_block(const float* x, void* q, void* s, float gs, int64_t T, int cols,
+                                  wzyb_stream_t stream) {
+    if (!x || !q || !s) return WZYB_ERR_NULL;
+    const int group = QF == kQfNvfp4 ? 16 : 32;
+    if (T < 0 || T > (int64_t(1) << 40) || cols < group || (cols % group) != 0) return WZYB_ERR_SHAPE;
+    if (!aligned16(x) || !aligned16(q)) return WZYB_ERR_ALIGN;
+    if (T == 0) return WZYB_OK;
+    DeviceInfo di;
+    const int rc = device_info(&di);
+    if (rc != WZYB_OK) return rc;
+    const int64_t nvec = T * cols / 8;
+    const int grid = persistent_grid(di, 8, (nvec + 255) / 256);
+    quant_act_block_kernel<QF><<<grid, 256, 0, (cudaStream_t)stream>>>(x, q, s, gs, nvec);
+    return launch_status();
 }
 
 }  // namespace wzyb
@@ -46,6 +82,15 @@ int wzyb_quant_act_f32(const float* x, int8_t* q32, float* s32, int8_t* q16, flo
     wzyb::quant_act_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, (signed char*)q32, s32, (signed char*)q16, s16,
                                                                     nvec);
     return wzyb::launch_status();
+}
+
+int wzyb_quant_act_mxfp8_f32(const float* x, uint8_t* q, uint8_t* s, int64_t T, int cols, wzyb_stream_t stream) {
+    return wzyb::launch_quant_act_block<wzyb::kQfMxfp8>(x, q, s, 1.0f, T, cols, stream);
+}
+
+int wzyb_quant_act_nvfp4_f32(const float* x, uint8_t* q, uint8_t* s, float global_scale, int64_t T, int cols,
+                             wzyb_stream_t stream) {
+    return wzyb::launch_quant_act_block<wzyb::kQfNvfp4>(x, q, s, global_scale, T, cols, stream);
 }
 
 }  // extern "C"

@@ -85,15 +85,16 @@ __global__ void __launch_bounds__(kSwigluThreads) swiglu_kernel(const TI* __rest
     }
 }
 
-// SwiGLU fused with Q8_0 quantisation, no activation output: silu_mul_quant32_multi
-// (src/wzy_kernels_v2.cuh:1247-1279). A warp covers 32 consecutive 8-element vectors (8 groups of
-// 32); each group's max is two shuffles over its 4 lanes. The activation uses the reference's own
-// expression, (g / (1 + __expf(-g))) * u with the IEEE divide, so on the same inputs the codes and
-// scales come out as the reference kernel's.
-template <typename TI>
-__global__ void __launch_bounds__(256) swiglu_q8_kernel(const TI* __restrict__ gate, const TI* __restrict__ up,
-                                                        signed char* __restrict__ q, float* __restrict__ s,
-                                                        int64_t nvec) {
+// SwiGLU fused with the GEMM-input quantisation, no activation output: silu_mul_quant32_multi
+// (src/wzy_kernels_v2.cuh:1247-1279) for Q8_0, and the MXFP8 / NVFP4 block formats of sm_100's
+// block-scaled tensor-core GEMMs. A warp covers 32 consecutive 8-element vectors; a group's max is one
+// (16-element) or two (32-element) shuffles. The activation uses the reference's own expression,
+// (g / (1 + __expf(-g))) * u with the IEEE divide, so on the same inputs the Q8 codes and scales come
+// out as the reference kernel's.
+template <typename TI, int QF>
+__global__ void __launch_bounds__(256) swiglu_quant_kernel(const TI* __restrict__ gate, const TI* __restrict__ up,
+                                                           void* __restrict__ q, void* __restrict__ s, float gs,
+                                                           int64_t nvec) {
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; base < nvec;
@@ -108,7 +109,7 @@ __global__ void __launch_bounds__(256) swiglu_q8_kernel(const TI* __restrict__ g
 #pragma unroll
             for (int e = 0; e < 8; ++e) o[e] = (g[e] / (1.0f + __expf(-g[e]))) * u[e];
         }
-        q8_group_store(o, act, q + v * 8, s + (v >> 2), lane);
+        quant_group_store<QF>(o, act, q, s, gs, v, lane);
     }
 }
 
@@ -133,6 +134,23 @@ static int launch_swiglu(const TI* gate, const TI* up, TO* out, int64_t nvec, in
     return launch_status();
 }
 
+// n % 32 == 0 (the largest group); Q8 scales are fp32 (4-byte aligned), the block formats' are bytes.
+template <int QF>
+static int launch_swiglu_quant(const float* gate, const float* up, void* q, void* s, float gs, int64_t n,
+                               wzyb_stream_t stream) {
+    if (!gate || !up || !q || !s) return WZYB_ERR_NULL;
+    if (n < 0 || (n % 32) != 0) return WZYB_ERR_SHAPE;
+    if (!aligned16(gate) || !aligned16(up) || !aligned16(q) || (QF == kQfQ8 && !aligned16(s))) return WZYB_ERR_ALIGN;
+    if (n == 0) return WZYB_OK;
+    DeviceInfo di;
+    const int rc = device_info(&di);
+    if (rc != WZYB_OK) return rc;
+    const int64_t nvec = n / 8;
+    const int grid = persistent_grid(di, 8, (nvec + 255) / 256);
+    swiglu_quant_kernel<float, QF><<<grid, 256, 0, (cudaStream_t)stream>>>(gate, up, q, s, gs, nvec);
+    return launch_status();
+}
+
 }  // namespace wzyb
 
 extern "C" {
@@ -153,18 +171,17 @@ int wzyb_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, w
 }
 
 int wzyb_swiglu_q8_f32(const float* gate, const float* up, int8_t* q32, float* s32, int64_t n, wzyb_stream_t stream) {
-    if (!gate || !up || !q32 || !s32) return WZYB_ERR_NULL;
-    if (n < 0 || (n % 32) != 0) return WZYB_ERR_SHAPE;
-    if (!wzyb::aligned16(gate) || !wzyb::aligned16(up) || !wzyb::aligned16(q32) || !wzyb::aligned16(s32))
-        return WZYB_ERR_ALIGN;
-    if (n == 0) return WZYB_OK;
-    wzyb::DeviceInfo di;
-    const int rc = wzyb::device_info(&di);
-    if (rc != WZYB_OK) return rc;
-    const int64_t nvec = n / 8;
-    const int grid = wzyb::persistent_grid(di, 8, (nvec + 255) / 256);
-    wzyb::swiglu_q8_kernel<float><<<grid, 256, 0, (cudaStream_t)stream>>>(gate, up, (signed char*)q32, s32, nvec);
-    return wzyb::launch_status();
+    return wzyb::launch_swiglu_quant<wzyb::kQfQ8>(gate, up, q32, s32, 1.0f, n, stream);
+}
+
+int wzyb_swiglu_mxfp8_f32(const float* gate, const float* up, uint8_t* q, uint8_t* s, int64_t n,
+                          wzyb_stream_t stream) {
+    return wzyb::launch_swiglu_quant<wzyb::kQfMxfp8>(gate, up, q, s, 1.0f, n, stream);
+}
+
+int wzyb_swiglu_nvfp4_f32(const float* gate, const float* up, uint8_t* q, uint8_t* s, float global_scale, int64_t n,
+                          wzyb_stream_t stream) {
+    return wzyb::launch_swiglu_quant<wzyb::kQfNvfp4>(gate, up, q, s, global_scale, n, stream);
 }
 
 int wzyb_swiglu_interleaved_f16(const uint16_t* gu, uint16_t* out, int64_t T, int nff, wzyb_stream_t stream) {

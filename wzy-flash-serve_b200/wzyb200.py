@@ -113,6 +113,12 @@ _SIGS = {
     "wzyb_gr_norm_q8_f32": (c_int, [P, P, P, P, P, P, P, c_int64, c_int, c_int, c_float, S]),
     "wzyb_swiglu_q8_f32": (c_int, [P, P, P, P, c_int64, S]),
     "wzyb_quant_act_f32": (c_int, [P, P, P, P, P, c_int64, c_int, S]),
+    "wzyb_quant_act_mxfp8_f32": (c_int, [P, P, P, c_int64, c_int, S]),
+    "wzyb_quant_act_nvfp4_f32": (c_int, [P, P, P, c_float, c_int64, c_int, S]),
+    "wzyb_swiglu_mxfp8_f32": (c_int, [P, P, P, P, c_int64, S]),
+    "wzyb_swiglu_nvfp4_f32": (c_int, [P, P, P, P, c_float, c_int64, S]),
+    "wzyb_gr_norm_mxfp8_f32": (c_int, [P, P, P, P, P, P, P, c_int64, c_int, c_int, c_float, S]),
+    "wzyb_gr_norm_nvfp4_f32": (c_int, [P, P, P, P, P, P, P, c_float, c_int64, c_int, c_int, c_float, S]),
     "wzyb_gr_write_f32": (c_int, [P, P, P, c_int64, c_int, c_int, S]),
     "wzyb_hc_mix_f16": (c_int, [P, P, P, P, c_int64, c_int, c_int, S]),
     "wzyb_hc_mix_f32": (c_int, [P, P, P, c_int64, c_int, c_int, S]),
@@ -241,6 +247,32 @@ def swiglu_q8_f32(gate, up, q32, s32, stream=None):
 def quant_act_f32(x, q32, s32, q16, s16, T, cols, stream=None):
     """int8 per-32 (q32/s32) and/or per-16 (q16/s16) quantisation of fp32 rows x [T, cols]."""
     call("wzyb_quant_act_f32", _ptr(x), _ptr(q32), _ptr(s32), _ptr(q16), _ptr(s16), T, cols, _stream(stream))
+
+
+def quant_act_block(x, q, s, T, cols, fmt="mxfp8", global_scale=1.0, stream=None):
+    """MXFP8 (fmt "mxfp8") or NVFP4 ("nvfp4") codes and scale bytes of fp32 rows x [T, cols]."""
+    if fmt == "mxfp8":
+        call("wzyb_quant_act_mxfp8_f32", _ptr(x), _ptr(q), _ptr(s), T, cols, _stream(stream))
+    else:
+        call("wzyb_quant_act_nvfp4_f32", _ptr(x), _ptr(q), _ptr(s), global_scale, T, cols, _stream(stream))
+
+
+def swiglu_block(gate, up, q, s, fmt="mxfp8", global_scale=1.0, stream=None):
+    if fmt == "mxfp8":
+        call("wzyb_swiglu_mxfp8_f32", _ptr(gate), _ptr(up), _ptr(q), _ptr(s), gate.numel(), _stream(stream))
+    else:
+        call("wzyb_swiglu_nvfp4_f32", _ptr(gate), _ptr(up), _ptr(q), _ptr(s), global_scale, gate.numel(),
+             _stream(stream))
+
+
+def gr_norm_block(R, w_norm, bo_prev, inj_prev, xn, xq, xs, T, n_embd, hc, fmt="mxfp8", global_scale=1.0, eps=1e-6,
+                  stream=None):
+    if fmt == "mxfp8":
+        call("wzyb_gr_norm_mxfp8_f32", _ptr(R), _ptr(w_norm), _ptr(bo_prev), _ptr(inj_prev), _ptr(xn), _ptr(xq),
+             _ptr(xs), T, n_embd, hc, eps, _stream(stream))
+    else:
+        call("wzyb_gr_norm_nvfp4_f32", _ptr(R), _ptr(w_norm), _ptr(bo_prev), _ptr(inj_prev), _ptr(xn), _ptr(xq),
+             _ptr(xs), global_scale, T, n_embd, hc, eps, _stream(stream))
 
 
 def gr_write_f32(R, blk, inj, T, n_embd, hc, stream=None):

@@ -432,7 +432,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-kernels", action="store_true")
-    ap.add_argument("--variant", default="auto", choices=["auto", "ring", "direct", "async", "wide"],
+    ap.add_argument("--variant", default="auto", choices=["auto", "ring", "direct", "async", "wide", "pair"],
                     help="kernel design of the norm families (A/B measurement)")
     ap.add_argument("--tune", action="append", default=[],
                     help="FAMILY:CTAS_PER_SM:STAGES launch tuning (wzyb_set_launch_tuning), repeatable")
@@ -485,7 +485,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
     wz.check("wzyb_prepare_device", wz.lib().wzyb_prepare_device())
     var = {"auto": wz.VARIANT_AUTO, "ring": wz.VARIANT_RING, "direct": wz.VARIANT_DIRECT,
-           "async": wz.VARIANT_ASYNC, "wide": wz.VARIANT_WIDE}[args.variant]
+           "async": wz.VARIANT_ASYNC, "wide": wz.VARIANT_WIDE,
+           "pair": wz.VARIANT_PAIR}[args.variant]
     for fam in (wz.FAM_NORM, wz.FAM_HEAD_ROPE, wz.FAM_GDN):
         wz.set_kernel_variant(fam, var)
     for spec in args.tune:

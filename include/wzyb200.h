@@ -422,14 +422,17 @@ int wzyb_set_launch_tuning(int family, int ctas_per_sm, int stages);
  *   WZYB_VARIANT_DIRECT warp-owned units, 16-byte loads prefetched into registers, no CTA barrier
  *   WZYB_VARIANT_ASYNC  warp-owned units staged in a lane-private shared-memory ring by cp.async
  *   WZYB_VARIANT_WIDE   CTA-owned rows (4-16 warps), registers, one CTA barrier per row
+ *   WZYB_VARIANT_PAIR   (head norm+RoPE) two chunks per lane holding each rotation pair, no shuffle
  * Families 0 (add+RMSNorm), 1 (head norm+RoPE) and 2 (GDN gated norm) have the RING, DIRECT and
- * ASYNC designs; family 0 also WIDE, which AUTO picks for rows past one warp's register budget
+ * ASYNC designs; family 0 also WIDE, which AUTO picks for rows past one warp's register budget;
+ * family 1 also PAIR
  * (a family without a design falls back to AUTO; DIRECT and ASYNC do so for rows too wide). */
 #define WZYB_VARIANT_AUTO 0
 #define WZYB_VARIANT_RING 1
 #define WZYB_VARIANT_DIRECT 2
 #define WZYB_VARIANT_ASYNC 3
 #define WZYB_VARIANT_WIDE 4
+#define WZYB_VARIANT_PAIR 5
 int wzyb_set_kernel_variant(int family, int variant);
 const char* wzyb_status_string(int status);
 int wzyb_version(void);

@@ -47,10 +47,10 @@ def _faults_clear(wz):
 
 # The norm families have several kernel designs (TMA ring, direct, cp.async, CTA-wide rows; a family
 # without one falls back to its default); parity must hold for each.
-@pytest.fixture(params=["ring", "direct", "async", "wide"])
+@pytest.fixture(params=["ring", "direct", "async", "wide", "pair"])
 def variant(request, wz):
     v = {"ring": wz.VARIANT_RING, "direct": wz.VARIANT_DIRECT, "async": wz.VARIANT_ASYNC,
-         "wide": wz.VARIANT_WIDE}[request.param]
+         "wide": wz.VARIANT_WIDE, "pair": wz.VARIANT_PAIR}[request.param]
     for fam in (wz.FAM_NORM, wz.FAM_HEAD_ROPE, wz.FAM_GDN):
         wz.set_kernel_variant(fam, v)
     return request.param

@@ -238,15 +238,13 @@ __device__ __forceinline__ void norm_rope_head(float2 (&p)[4], bool q_gamma, con
     }
 }
 
-// The same per-head math with the gamma slice read from shared memory (sg = this lane's 4 float2 of
-// the head's section), which keeps 16 registers per thread free for more resident warps.
+// The same per-head math with the lane's 8 gammas given as two float4 (read from a lane-major table
+// in shared memory), which keeps 16 registers per thread free for more resident warps.
 template <int L, int HD>
-__device__ __forceinline__ void norm_rope_head_sg(float2 (&p)[4], const float2* sg, float eps, int src, bool rotate,
-                                                  const float2 (&c2)[4], const float2 (&s2)[4]) {
+__device__ __forceinline__ void norm_rope_head_sg(float2 (&p)[4], const float4 ga, const float4 gb, float eps, int src,
+                                                  bool rotate, const float2 (&c2)[4], const float2 (&s2)[4]) {
     const float ss = group_sum<L>(sumsq8(p));
     const float2 sc = splat2(rsqrt_approx(ss / (float)HD + eps));
-    const float4 ga = reinterpret_cast<const float4*>(sg)[0];
-    const float4 gb = reinterpret_cast<const float4*>(sg)[1];
     p[0] = fmul2(p[0], fmul2(sc, make_float2(ga.x, ga.y)));
     p[1] = fmul2(p[1], fmul2(sc, make_float2(ga.z, ga.w)));
     p[2] = fmul2(p[2], fmul2(sc, make_float2(gb.x, gb.y)));
@@ -288,16 +286,19 @@ __global__ void __launch_bounds__(128) head_rope_direct_kernel(const HeadRopeArg
     const int ci = (first_half ? li : li - hl) * 8;
     const int64_t base_pos = (a.d_base_pos ? (int64_t)__ldg(a.d_base_pos) : 0) + a.pos_offset;
 
-    // gammas (+ weight offset) of both sections as fp32 in shared memory
-    __shared__ __align__(16) float2 sg[2][HD / 2];
-    for (int i = threadIdx.x; i < HD; i += blockDim.x) {
-        const int s = i / (HD / 2), c = (i % (HD / 2)) * 2;
-        float2 v = splat2(0.f);
+    // gammas (+ weight offset) of both sections as fp32 in shared memory, lane-major: sgl[s][k][l] holds
+    // dims 8l + 4k .. +3, so each of a head's two 16-byte gamma loads reads one contiguous span (no
+    // bank conflicts; lanes of other heads of the same section in the warp read the same words)
+    __shared__ __align__(16) float4 sgl[2][2][L];
+    for (int i = threadIdx.x; i < 4 * L; i += blockDim.x) {
+        const int s = i / (2 * L), k = (i / L) % 2, l = i % L;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (a.sec[s].heads > 0) {
-            const T* gm = static_cast<const T*>(a.sec[s].gamma);
-            v = make_float2(a.w_offset + (float)gm[c], a.w_offset + (float)gm[c + 1]);
+            const T* gm = static_cast<const T*>(a.sec[s].gamma) + l * 8 + k * 4;
+            v = make_float4(a.w_offset + (float)gm[0], a.w_offset + (float)gm[1], a.w_offset + (float)gm[2],
+                            a.w_offset + (float)gm[3]);
         }
-        sg[s][c / 2] = v;
+        sgl[s][k][l] = v;
     }
     __syncthreads();
 
@@ -340,8 +341,124 @@ __global__ void __launch_bounds__(128) head_rope_direct_kernel(const HeadRopeArg
 #pragma unroll
                 for (int i = 0; i < 4; ++i) p[i] = splat2(0.f);
             }
-            norm_rope_head_sg<L, HD>(p, &sg[h < hq ? 0 : 1][li * 4], a.eps, src, pos_ok && rot_lane, c2, s2);
+            const int sec = h < hq ? 0 : 1;
+            norm_rope_head_sg<L, HD>(p, sgl[sec][0][li], sgl[sec][1][li], a.eps, src, pos_ok && rot_lane, c2, s2);
             if (h < htot) Vec8<T>::store2(head_ptr(h), p);
+        }
+    }
+}
+
+// Pair design: the direct design's per-token head chunks with L2 = HD/16 lanes per head, each lane
+// holding two 8-element chunks. With P = rot/16 rotary chunk pairs (c, c + P), lane m < P holds exactly
+// the pair (m, m + P), so the NeoX rotation is done inside the lane with no shuffle; lanes m >= P hold
+// two adjacent chunks of the rest of the head (2P + 2(m - P), +1). The norm reduces over L2 lanes. The
+// rotation expressions are the direct design's (own*cos + partner*(+-sin), fused), so results match it
+// bit for bit.
+template <typename T, int HD, int kNH>
+__global__ void __launch_bounds__(128) head_rope_pair_kernel(const HeadRopeArgs a) {
+    constexpr int L2 = HD / 16;   // lanes per head
+    constexpr int HPW = 32 / L2;  // heads side by side in one warp
+    constexpr int CH = kNH * HPW; // heads per chunk item
+    const int lane = threadIdx.x & 31;
+    const int li = lane % L2;
+    const int hw = lane / L2;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int hq = a.sec[0].heads, htot = hq + a.sec[1].heads;
+    const int chunks = (htot + CH - 1) / CH;
+    const int64_t items = a.T * chunks;
+    const int half = a.rot / 2, P = half / 8;
+    const bool rot_lane = li < P;
+    const int c0 = rot_lane ? li : 2 * P + 2 * (li - P);  // first chunk of this lane
+    const int c1 = rot_lane ? li + P : c0 + 1;            // second chunk
+    const int64_t base_pos = (a.d_base_pos ? (int64_t)__ldg(a.d_base_pos) : 0) + a.pos_offset;
+
+    // gammas (+ weight offset) as a lane-major table: sgl[s][k][l] = dims 4(k&1).. of chunk c0 (k < 2)
+    // or c1 (k >= 2) of lane l, so each 16-byte gamma load of a head reads one contiguous span
+    __shared__ __align__(16) float4 sgl[2][4][L2];
+    for (int i = threadIdx.x; i < 8 * L2; i += blockDim.x) {
+        const int s = i / (4 * L2), k = (i / L2) % 4, l = i % L2;
+        const int lc0 = l < P ? l : 2 * P + 2 * (l - P);
+        const int c = k < 2 ? lc0 : (l < P ? l + P : lc0 + 1);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (a.sec[s].heads > 0) {
+            const T* gm = static_cast<const T*>(a.sec[s].gamma) + c * 8 + (k & 1) * 4;
+            v = make_float4(a.w_offset + (float)gm[0], a.w_offset + (float)gm[1], a.w_offset + (float)gm[2],
+                            a.w_offset + (float)gm[3]);
+        }
+        sgl[s][k][l] = v;
+    }
+    __syncthreads();
+
+    T* const qdata = static_cast<T*>(a.sec[0].data);
+    T* const kdata = static_cast<T*>(a.sec[1].heads > 0 ? a.sec[1].data : a.sec[0].data);
+    const int64_t qrs = a.sec[0].row_stride, qhs = a.sec[0].head_stride;
+    const int64_t krs = a.sec[1].row_stride, khs = a.sec[1].head_stride;
+
+    StridePos ps(gwarp, nwarps, chunks);  // item it = (token q, chunk r)
+    for (int64_t it = gwarp; it < items; it += nwarps, ps.advance()) {
+        const int64_t t = ps.q;
+        const int h0 = ps.r * CH;
+        T* const qrow = qdata + t * qrs;
+        T* const krow = kdata + t * krs;
+        auto head_ptr = [&](int h) -> T* { return h < hq ? qrow + h * qhs : krow + (h - hq) * khs; };
+        typename Vec8<T>::Raw ra[kNH], rb[kNH];
+#pragma unroll
+        for (int j = 0; j < kNH; ++j) {
+            const int h = h0 + j * HPW + hw;
+            if (h < htot) {
+                T* hp = head_ptr(h);
+                ra[j] = Vec8<T>::ldcs_raw(hp + c0 * 8);
+                rb[j] = Vec8<T>::ldcs_raw(hp + c1 * 8);
+            }
+        }
+        const int64_t pos = base_pos + t;
+        const bool pos_ok = half > 0 && pos >= 0 && pos < a.table_rows;
+        float2 c2[4], s2[4];
+        if (pos_ok && rot_lane) {
+            Vec8<float>::load_ro2(a.cos_tab + pos * half + li * 8, c2);
+            Vec8<float>::load_ro2(a.sin_tab + pos * half + li * 8, s2);
+        }
+        if (half > 0 && !pos_ok && lane == 0 && h0 == 0) raise_fault(WZYB_FAULT_POS_RANGE);
+#pragma unroll
+        for (int j = 0; j < kNH; ++j) {
+            if (h0 + j * HPW >= htot) break;  // warp-uniform: no head of this round exists
+            const int h = h0 + j * HPW + hw;
+            const bool act = h < htot;
+            float2 pa[4], pb[4];
+            if (act) {
+                Vec8<T>::cvt2(ra[j], pa);
+                Vec8<T>::cvt2(rb[j], pb);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) pa[i] = pb[i] = splat2(0.f);
+            }
+            const float ss = group_sum<L2>(sumsq8(pa) + sumsq8(pb));
+            const float2 sc = splat2(rsqrt_approx(ss / (float)HD + a.eps));
+            const int sec = h < hq ? 0 : 1;
+            const float4 ga0 = sgl[sec][0][li], ga1 = sgl[sec][1][li], gb0 = sgl[sec][2][li], gb1 = sgl[sec][3][li];
+            pa[0] = fmul2(pa[0], fmul2(sc, make_float2(ga0.x, ga0.y)));
+            pa[1] = fmul2(pa[1], fmul2(sc, make_float2(ga0.z, ga0.w)));
+            pa[2] = fmul2(pa[2], fmul2(sc, make_float2(ga1.x, ga1.y)));
+            pa[3] = fmul2(pa[3], fmul2(sc, make_float2(ga1.z, ga1.w)));
+            pb[0] = fmul2(pb[0], fmul2(sc, make_float2(gb0.x, gb0.y)));
+            pb[1] = fmul2(pb[1], fmul2(sc, make_float2(gb0.z, gb0.w)));
+            pb[2] = fmul2(pb[2], fmul2(sc, make_float2(gb1.x, gb1.y)));
+            pb[3] = fmul2(pb[3], fmul2(sc, make_float2(gb1.z, gb1.w)));
+            if (pos_ok && rot_lane) {
+                // first half a*cos - d*sin, second half d*cos + a*sin, as own*cos + partner*(+-sin)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 a_ = pa[i], d_ = pb[i];
+                    pa[i] = ffma2(d_, make_float2(-s2[i].x, -s2[i].y), fmul2(a_, c2[i]));
+                    pb[i] = ffma2(a_, s2[i], fmul2(d_, c2[i]));
+                }
+            }
+            if (act) {
+                T* hp = head_ptr(h);
+                Vec8<T>::store2(hp + c0 * 8, pa);
+                Vec8<T>::store2(hp + c1 * 8, pb);
+            }
         }
     }
 }
@@ -473,6 +590,20 @@ static int launch_head_rope_direct(const HeadRopeArgs& a, int hd, int htot, cons
     return launch_status();
 }
 
+template <typename T, int kNH>
+static int launch_head_rope_pair(const HeadRopeArgs& a, int hd, int htot, const DeviceInfo& di, cudaStream_t stream) {
+    const void* kern = hd == 64    ? (const void*)head_rope_pair_kernel<T, 64, kNH>
+                       : hd == 128 ? (const void*)head_rope_pair_kernel<T, 128, kNH>
+                                   : (const void*)head_rope_pair_kernel<T, 256, kNH>;
+    const int ch = kNH * (512 / hd);
+    const int64_t warp_items = a.T * ((htot + ch - 1) / ch);
+    const int grid = persistent_grid(di, resident_ctas(kern, 128, 0), (warp_items + 3) / 4);
+    if (hd == 64) head_rope_pair_kernel<T, 64, kNH><<<grid, 128, 0, stream>>>(a);
+    else if (hd == 128) head_rope_pair_kernel<T, 128, kNH><<<grid, 128, 0, stream>>>(a);
+    else head_rope_pair_kernel<T, 256, kNH><<<grid, 128, 0, stream>>>(a);
+    return launch_status();
+}
+
 template <typename T>
 static int launch_head_rope(const HeadSection& q, const HeadSection& k, const float* cos_tab, const float* sin_tab,
                             int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset, int64_t T_, int hd,
@@ -538,11 +669,17 @@ static int launch_head_rope(const HeadSection& q, const HeadSection& k, const fl
         return launch_status();
     }
     if (variant(kFamHeadRope) != WZYB_VARIANT_RING) {
-        // Two instantiations: 4 heads per chunk (80 registers, 24 warps/SM; default: equal at 262K
-        // tokens, 51% vs 47% of peak at 4096) or 6 heads per chunk (96 registers, 20 warps/SM), which
-        // a ctas_per_sm tuning of 2 selects.
-        if (tuning(kFamHeadRope).ctas_per_sm == 2) return launch_head_rope_direct<T, 6>(a, hd, htot, di, stream);
-        return launch_head_rope_direct<T, 4>(a, hd, htot, di, stream);
+        // Pair design by default, 3 rounds of 2 heads per item (6 heads; the 18 heads of the benchmark's
+        // q+k are 3 whole items): 83 % of peak at 262K tokens vs 76 % for the direct design, whose rotation
+        // shuffles and two gamma loads per head kept the shared-memory pipe ~70 % busy. A ctas_per_sm
+        // tuning of 2 selects the other instantiation of either design (pair 2 rounds, direct 6 heads).
+        const bool alt = tuning(kFamHeadRope).ctas_per_sm == 2;
+        if (variant(kFamHeadRope) == WZYB_VARIANT_DIRECT) {
+            if (alt) return launch_head_rope_direct<T, 6>(a, hd, htot, di, stream);
+            return launch_head_rope_direct<T, 4>(a, hd, htot, di, stream);
+        }
+        if (alt) return launch_head_rope_pair<T, 2>(a, hd, htot, di, stream);
+        return launch_head_rope_pair<T, 3>(a, hd, htot, di, stream);
     }
 
     const int slots = htot * (hd / 8);

@@ -151,7 +151,7 @@ int wzyb_set_launch_tuning(int family, int ctas_per_sm, int stages) {
 
 int wzyb_set_kernel_variant(int family, int variant) {
     if (family < 0 || family >= wzyb::kFamCount) return WZYB_ERR_VALUE;
-    if (variant < WZYB_VARIANT_AUTO || variant > WZYB_VARIANT_WIDE) return WZYB_ERR_VALUE;
+    if (variant < WZYB_VARIANT_AUTO || variant > WZYB_VARIANT_PAIR) return WZYB_ERR_VALUE;
     wzyb::g_variant[family].store(variant);
     return WZYB_OK;
 }

@@ -24,7 +24,7 @@ OOB_CLAMP, OOB_ZERO_ID = 0, 1
 PLE_HASH_C_PRECEDENCE, PLE_HASH_XOR_THEN_ADD = 0, 1
 PLE_EOS_DEFAULT = 248044
 FAM_NORM, FAM_HEAD_ROPE, FAM_GDN, FAM_SWIGLU, FAM_GATHER = 0, 1, 2, 3, 4
-VARIANT_AUTO, VARIANT_RING, VARIANT_DIRECT, VARIANT_ASYNC, VARIANT_WIDE = 0, 1, 2, 3, 4
+VARIANT_AUTO, VARIANT_RING, VARIANT_DIRECT, VARIANT_ASYNC, VARIANT_WIDE, VARIANT_PAIR = 0, 1, 2, 3, 4, 5
 
 
 class WzybError(RuntimeError):

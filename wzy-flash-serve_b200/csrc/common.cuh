@@ -391,12 +391,16 @@ __device__ __forceinline__ void q8_group_store(const float (&v)[8], bool active,
     if (!active) return;
     const float d = am / 127.0f;
     const float inv = d > 0.f ? 127.0f / am : 0.f;
-    uint32_t w[2] = {0u, 0u};
+    // |v * inv| <= 127 * (1 + 2^-24)^2 for finite v, so a saturating round-to-nearest conversion to s8
+    // gives exactly rint clamped to [-127, 127] (NaN -> 0 either way); bytes packed with prmt.
+    uint32_t b[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int qi = max(-127, min(127, __float2int_rn(v[i] * inv)));
-        w[i >> 2] |= ((uint32_t)(qi & 0xFF)) << ((i & 3) * 8);
-    }
+    for (int i = 0; i < 8; ++i) asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(b[i]) : "f"(v[i] * inv));
+    uint32_t w[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+        w[k] = __byte_perm(__byte_perm(b[4 * k], b[4 * k + 1], 0x0040), __byte_perm(b[4 * k + 2], b[4 * k + 3], 0x0040),
+                           0x5410);
     *reinterpret_cast<uint2*>(q) = make_uint2(w[0], w[1]);
     if ((lane & (kLanes - 1)) == 0) *s = d;
 }

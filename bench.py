@@ -371,6 +371,65 @@ def measure_kernels_4096(wz, torch, dev, peak, reps=60):
     return res
 
 
+def measure_decode(wz, torch, dev, reps=200):
+    """Decode-window sizes (T = 1 and 8 tokens, the reference model's widths): device time per launch
+    with the data resident in L2, as in a decode step. The launches are captured into a CUDA graph
+    (the reference records its decode windows the same way), so the host's launch cost is not timed."""
+    NE, HC, KVD, NFF = 2560, 4, 512, 640
+    g = torch.Generator(device=dev).manual_seed(11)
+    s = None  # the wrappers launch on the current stream (the capture stream inside the graph)
+    out = {}
+    for T in (1, 8):
+        R = torch.randn((T * HC, NE), generator=g, device=dev)
+        bo = torch.randn((T, NE), generator=g, device=dev)
+        inj = torch.randn((T * HC,), generator=g, device=dev)
+        wn = 1 + 0.02 * torch.randn((HC, NE), generator=g, device=dev)
+        xn = torch.empty((T * HC, NE), device=dev)
+        xq = torch.empty((T * HC, NE), dtype=torch.int8, device=dev)
+        xs = torch.empty((T * HC, NE // 32), device=dev)
+        qg = torch.randn((T, 24, 2 * HD), generator=g, device=dev)
+        gq = 1 + 0.02 * torch.randn(HD, generator=g, device=dev)
+        cos, sin = torch.empty((64, ROT // 2), device=dev), torch.empty((64, ROT // 2), device=dev)
+        wz.rope_table(cos, sin, 64, ROT, THETA)
+        kk = torch.randn((T, KVD), generator=g, device=dev)
+        vv = torch.randn((T, KVD), generator=g, device=dev)
+        planes = [torch.zeros((64, KVD), dtype=torch.int8, device=dev) if i % 2 == 0 else
+                  torch.zeros((64, KVD // 64), dtype=torch.int16, device=dev) for i in range(4)]
+        cache = wz.kv_cache(*planes, 64, 64)
+        sff = torch.randn(NFF * T, generator=g, device=dev)
+        sup = torch.randn(NFF * T, generator=g, device=dev)
+        q8 = torch.empty(NFF * T, dtype=torch.int8, device=dev)
+        s8 = torch.empty(NFF * T // 32, device=dev)
+        jobs = {
+            "gr_norm_q8": lambda: wz.gr_norm_q8_f32(R, wn, bo, inj, xn, xq, xs, T, NE, HC, stream=s),
+            "q_norm_rope_f32": lambda: wz.head_norm_rope(qg, gq, cos, sin, T, 24, HD, 2 * HD, 48 * HD, ROT, EPS, 0.0,
+                                                         pos_offset=5, stream=s),
+            "k_rope_kv_append": lambda: wz.k_rope_kv_append(kk, gq, vv, cos, sin, T, 2, HD, cache, rot_dims=ROT,
+                                                            pos_offset=5, stream=s),
+            "gr_write": lambda: wz.gr_write_f32(R, bo, inj, T, NE, HC, stream=s),
+            "swiglu_q8": lambda: wz.swiglu_q8_f32(sff, sup, q8, s8, stream=s),
+        }
+        for name, fn in jobs.items():
+            for _ in range(20):  # first calls cache occupancy and attributes outside the capture
+                fn()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(reps):
+                    fn()
+            graph.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(5):
+                graph.replay()
+            e1.record()
+            e1.synchronize()
+            out.setdefault(name, {})[f"T{T}_us"] = round(e0.elapsed_time(e1) * 1e3 / (5 * reps), 2)
+            del graph
+    return out
+
+
 class CpuBundle:
     """The oracle (a scalar C port of the reference math, OpenMP over rows) running the same
     configs[1]+[2] bundle on T tokens of host memory, in place, with every host thread."""
@@ -553,9 +612,10 @@ def main():
                "note": "public bundle API (wzyb_attn_prep_f16 + wzyb_act_f16), pinned host buffers, "
                        "16384-token chunks on 2 streams, wall clock max over ranks"}
 
-    kernels = None
+    kernels = decode = None
     if rank == 0 and not args.no_kernels:
         kernels = measure_kernels_4096(wz, torch, dev, peak)
+        decode = measure_decode(wz, torch, dev)
 
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -607,6 +667,7 @@ def main():
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic, "algorithmic_bytes": dom_bytes},
             "kernels_4096": kernels,
+            "decode_us": decode,
             "clocks": {"sm_mhz": statistics.median(sm) if sm else None,
                        "sm_max_mhz": max((c["sm_max_mhz"] or 0) for c in clk_all if c) or None,
                        "reasons": reasons, "samples": sum(c["samples"] for c in clk_all if c)},

@@ -58,6 +58,27 @@ __global__ void __launch_bounds__(kGrwThreads) gr_write_kernel(float* __restrict
     }
 }
 
+// Decode-sized calls (a few rows: T <= 8 tokens x hc streams): one 8-element vector per thread over
+// the whole call, so every load is in flight at once instead of a warp walking its row; each thread
+// computes its row's gate (same expression).
+__global__ void __launch_bounds__(kGrwThreads) gr_write_flat_kernel(float* __restrict__ R,
+                                                                   const float* __restrict__ blk,
+                                                                   const float* __restrict__ inj, int64_t nvec,
+                                                                   int vpr, int hc) {
+    const int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (v >= nvec) return;
+    const int64_t u = v / vpr;
+    const int64_t col = (v - u * vpr) * 8;
+    const int64_t n = (int64_t)vpr * 8;
+    float2 rv[4], bv[4];
+    Vec8<float>::load2(R + u * n + col, rv);
+    Vec8<float>::load_ro2(blk + (u / hc) * n + col, bv);
+    const float2 gw = splat2(inj != nullptr ? 2.0f / (1.0f + __expf(-inj[u] / (float)hc)) : 1.0f);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) rv[i] = ffma2(bv[i], gw, rv[i]);
+    Vec8<float>::store2(R + u * n + col, rv);
+}
+
 // --- hc_mix --------------------------------------------------------------------------------------
 // Grid-stride over output vectors (token, 8 columns); each reads the hc stream vectors of xn and gg
 // at that position. Streams are summed in order c = 0..hc-1, then scaled by 1/hc (0.25 for the
@@ -168,6 +189,13 @@ int wzyb_gr_write_f32(float* R, const float* blk, const float* inj, int64_t T, i
     rc = wzyb::device_info(&di);
     if (rc != WZYB_OK) return rc;
     const int64_t rows = T * hc;
+    const int64_t nvec = rows * (n_embd / 8);
+    if (rows < (int64_t)di.sms * 4) {  // fewer rows than a quarter of the warps one wave holds
+        const int64_t blocks = (nvec + wzyb::kGrwThreads - 1) / wzyb::kGrwThreads;
+        wzyb::gr_write_flat_kernel<<<(unsigned)blocks, wzyb::kGrwThreads, 0, (cudaStream_t)stream>>>(
+            R, blk, inj, nvec, n_embd / 8, hc);
+        return wzyb::launch_status();
+    }
     const int grid = wzyb::persistent_grid(di, 8, (rows + 7) / 8);
     wzyb::gr_write_kernel<<<grid, wzyb::kGrwThreads, 0, (cudaStream_t)stream>>>(R, blk, inj, rows, n_embd, hc);
     return wzyb::launch_status();

@@ -4,8 +4,8 @@
 // (src/wzy_stage_v2.cuh:640-641, src/wzy_prefill_tc.cuh:864-865), then kv_append_int8_multi
 // (src/wzy_qsa_256k.cuh:86-145, launched at src/wzy_stage_v2.cuh:655 and src/wzy_prefill_tc.cuh:878),
 // which re-reads k and v, one 64-thread block per (64-element group, token). Here one warp owns a
-// token: it loads the token's k and v heads once, normalises and rotates k (written back in place),
-// and quantises both into the cache:
+// (token, round of heads): it loads those k and v heads once, normalises and rotates k (written back
+// in place), and quantises both into the cache:
 //   per 64-element group  sh = fp16(max|x| / 127),  d = float(sh),  q = d > 0 ? rint(x / d) : 0,
 //   q clamped to [-127, 127]; codes [cell, kvd] int8, scales [cell, kvd/64] fp16.
 // A 64-element group is 8 consecutive lanes (8 elements each); its max is three xor shuffles.
@@ -90,14 +90,15 @@ __device__ __forceinline__ void kv_q8_store(const float2 (&x)[4], bool act, int 
     }
 }
 
-// One warp per token. HD/8 lanes per head, 32/(HD/8) heads side by side; the token's heads are
-// visited in rounds of that many. The k and v vectors of kR = 2 rounds (the reference's 2 heads of
-// 256) are loaded before any arithmetic, with the cos/sin slice behind them.
-template <typename T, int HD>
+// One warp per (token, group of kR rounds of heads): HD/8 lanes per head, 32/(HD/8) heads side by
+// side per round. kR = 1 (small calls, e.g. decode) spreads a token's heads over warps for the
+// shortest chain; kR = 2 (long calls) keeps the reference's 2 heads of 256 on one warp, with the k and
+// v vectors of both rounds loaded before any arithmetic and the token's cell and cos/sin work done
+// once. The cos/sin slice is loaded behind the head vectors.
+template <typename T, int HD, int kR>
 __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
     constexpr int L = HD / 8;
     constexpr int HPW = 32 / L;
-    constexpr int kR = 2;
     const int lane = threadIdx.x & 31;
     const int li = lane % L, hw = lane / L;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -111,38 +112,39 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
     const int64_t base = (a.d_base_pos ? (int64_t)__ldg(a.d_base_pos) : 0) + a.pos_offset;
     const int64_t end = base + a.T;
     const int rounds = (a.kv_heads + HPW - 1) / HPW;
+    const int groups = (rounds + kR - 1) / kR;
+    const int64_t items = a.T * groups;
     T* const kd = static_cast<T*>(a.k);
     const T* const vd = static_cast<const T*>(a.v);
 
-    float2 g[2][4];  // g[1]: k gamma (+ offset) of this lane's 8 dims; g[0] unused
+    float2 g[4];  // k gamma (+ offset) of this lane's 8 dims
 #pragma unroll
-    for (int i = 0; i < 4; ++i) g[0][i] = g[1][i] = splat2(0.f);
+    for (int i = 0; i < 4; ++i) g[i] = splat2(0.f);
     if (a.norm_rope) {
-        Vec8<T>::load_ro2(static_cast<const T*>(a.k_gamma) + li * 8, g[1]);
+        Vec8<T>::load_ro2(static_cast<const T*>(a.k_gamma) + li * 8, g);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) g[1][i] = fadd2(splat2(a.w_offset), g[1][i]);
+        for (int i = 0; i < 4; ++i) g[i] = fadd2(splat2(a.w_offset), g[i]);
     }
 
-    for (int64_t t = gwarp; t < a.T; t += nwarps) {
+    StridePos ps(gwarp, nwarps, groups);  // item = (token q, round group r)
+    for (int64_t it = gwarp; it < items; it += nwarps, ps.advance()) {
+        const int64_t t = ps.q;
+        const int r0 = ps.r * kR;
+        typename Vec8<T>::Raw kr[kR], vr[kR];
+#pragma unroll
+        for (int j = 0; j < kR; ++j) {
+            const int h = (r0 + j) * HPW + hw;
+            if (r0 + j < rounds && h < a.kv_heads) {
+                kr[j] = Vec8<T>::ldcs_raw(kd + t * kvd + h * HD + li * 8);
+                vr[j] = Vec8<T>::ldcs_raw(vd + t * kvd + h * HD + li * 8);
+            }
+        }
         const int64_t pos = base + t;
         const bool keep = pos >= 0 && pos < a.c.max_ctx;
         const bool ring = keep && kv_in_ring(pos, end, a.c.ring_cap);
         const int64_t rcell = ring ? kv_ring_cell(pos, a.c.ring_cap) : 0;
         const bool full = keep && a.c.full_k_q != nullptr;
         const bool pos_ok = half > 0 && pos >= 0 && pos < a.table_rows;
-        // Loads first: the k and v vectors of kR rounds of heads, then the token's cos/sin slice.
-        typename Vec8<T>::Raw kr[kR], vr[kR];
-        auto load_rounds = [&](int r0) {
-#pragma unroll
-            for (int j = 0; j < kR; ++j) {
-                const int h = (r0 + j) * HPW + hw;
-                if (r0 + j < rounds && h < a.kv_heads) {
-                    kr[j] = Vec8<T>::ldcs_raw(kd + t * kvd + h * HD + li * 8);
-                    vr[j] = Vec8<T>::ldcs_raw(vd + t * kvd + h * HD + li * 8);
-                }
-            }
-        };
-        load_rounds(0);
         float2 c2[4], s2[4];
         if (a.norm_rope) {
             if (pos_ok && rot_lane) {
@@ -153,15 +155,12 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
                     for (int i = 0; i < 4; ++i) s2[i] = make_float2(-s2[i].x, -s2[i].y);
                 }
             }
-            if (half > 0 && !pos_ok && lane == 0) raise_fault(WZYB_FAULT_POS_RANGE);
+            if (half > 0 && !pos_ok && lane == 0 && r0 == 0) raise_fault(WZYB_FAULT_POS_RANGE);
         }
-        for (int r0 = 0; r0 < rounds; r0 += kR) {
-          if (r0 > 0) load_rounds(r0);  // more heads than kR rounds hold
 #pragma unroll
-          for (int j = 0; j < kR; ++j) {
-            const int r = r0 + j;
-            if (r >= rounds) break;  // warp-uniform
-            const int h = r * HPW + hw;
+        for (int j = 0; j < kR; ++j) {
+            if (r0 + j >= rounds) break;  // warp-uniform
+            const int h = (r0 + j) * HPW + hw;
             const bool act = h < a.kv_heads;
             const int64_t off = t * kvd + h * HD + li * 8;
             float2 p[4], v[4];
@@ -177,7 +176,7 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
                 const float ss = group_sum<L>(sumsq8(p));
                 const float2 sc = splat2(rsqrt_approx(ss / (float)HD + a.eps));
 #pragma unroll
-                for (int i = 0; i < 4; ++i) p[i] = fmul2(p[i], fmul2(sc, g[1][i]));
+                for (int i = 0; i < 4; ++i) p[i] = fmul2(p[i], fmul2(sc, g[i]));
                 float2 q[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -200,7 +199,6 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
                             a.c.ring_v_s + rcell * spc + sc_i, full ? a.c.full_v_q + pos * kvd + col : nullptr,
                             full ? a.c.full_v_s + pos * spc + sc_i : nullptr);
             }
-          }
         }
     }
 }
@@ -227,12 +225,21 @@ static int launch_kv_append(const KvAppendArgs& a0, int head_dim, cudaStream_t s
     DeviceInfo di;
     const int rc = device_info(&di);
     if (rc != WZYB_OK) return rc;
-    const int grid = persistent_grid(di, 8, (a.T + 7) / 8);
+    const int hpw = 32 / (head_dim / 8);
+    const int64_t rounds = (a.kv_heads + hpw - 1) / hpw;
+    // one round per warp while the call is smaller than a few warps per SM, else two
+    const bool split = a.T * rounds <= (int64_t)di.sms * 32;
+    const int64_t items = split ? a.T * rounds : a.T * ((rounds + 1) / 2);
+    const int grid = persistent_grid(di, 8, (items + 7) / 8);
+#define WZYB_KV(HDV)                                                                              \
+    if (split) kv_append_kernel<T, HDV, 1><<<grid, 256, 0, stream>>>(a);                          \
+    else kv_append_kernel<T, HDV, 2><<<grid, 256, 0, stream>>>(a);
     switch (head_dim) {
-        case 64: kv_append_kernel<T, 64><<<grid, 256, 0, stream>>>(a); break;
-        case 128: kv_append_kernel<T, 128><<<grid, 256, 0, stream>>>(a); break;
-        default: kv_append_kernel<T, 256><<<grid, 256, 0, stream>>>(a); break;
+        case 64: { WZYB_KV(64) break; }
+        case 128: { WZYB_KV(128) break; }
+        default: { WZYB_KV(256) break; }
     }
+#undef WZYB_KV
     return launch_status();
 }
 

@@ -459,10 +459,10 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
     a.qout = a.sout = nullptr;
     a.gs = 1.0f;
 
-    // Direct design while a row fits one warp's register budget (<= 12 fp16 or 6 fp32 vectors per
+    // Direct design while a row fits one warp's register budget (<= 12 fp16 or 4 fp32 vectors per
     // lane), the wide design (CTA-owned rows) past it; the TMA ring only on request.
     const int vpl_need = (n + 255) / 256;
-    const int vpl_max = sizeof(TI) == 2 ? 12 : 6;
+    const int vpl_max = sizeof(TI) == 2 ? 12 : 4;
     const int var = variant(kFamNorm);
     if (var == WZYB_VARIANT_WIDE || (var != WZYB_VARIANT_RING && vpl_need > vpl_max))
         return launch_norm_rows_wide<TI, TO, kQfNone>(a, di, stream);
@@ -499,8 +499,8 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
         WZYB_NR_PICK(1)
         WZYB_NR_PICK(2)
         WZYB_NR_PICK(4)
-        WZYB_NR_PICK(6)
-        if (sizeof(TI) == 2) {
+        if constexpr (sizeof(TI) == 2) {
+            WZYB_NR_PICK(6)
             WZYB_NR_PICK(8)
             WZYB_NR_PICK(10)
             WZYB_NR_PICK(12)
@@ -511,10 +511,15 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
             case 1: norm_rows_direct_kernel<TI, TO, 1><<<grid, 256, 0, stream>>>(a); break;
             case 2: norm_rows_direct_kernel<TI, TO, 2><<<grid, 256, 0, stream>>>(a); break;
             case 4: norm_rows_direct_kernel<TI, TO, 4><<<grid, 256, 0, stream>>>(a); break;
-            case 6: norm_rows_direct_kernel<TI, TO, 6><<<grid, 256, 0, stream>>>(a); break;
-            case 8: norm_rows_direct_kernel<TI, TO, 8><<<grid, 256, 0, stream>>>(a); break;
-            case 10: norm_rows_direct_kernel<TI, TO, 10><<<grid, 256, 0, stream>>>(a); break;
-            default: norm_rows_direct_kernel<TI, TO, 12><<<grid, 256, 0, stream>>>(a); break;
+            default:
+                // 6-12 vectors per lane only for fp16 rows (fp32 rows that long take the wide design)
+                if constexpr (sizeof(TI) == 2) {
+                    if (vpl == 6) norm_rows_direct_kernel<TI, TO, 6><<<grid, 256, 0, stream>>>(a);
+                    else if (vpl == 8) norm_rows_direct_kernel<TI, TO, 8><<<grid, 256, 0, stream>>>(a);
+                    else if (vpl == 10) norm_rows_direct_kernel<TI, TO, 10><<<grid, 256, 0, stream>>>(a);
+                    else norm_rows_direct_kernel<TI, TO, 12><<<grid, 256, 0, stream>>>(a);
+                }
+                break;
         }
         return launch_status();
     }

@@ -157,12 +157,19 @@ struct Vec8<__half> {
     __device__ __forceinline__ static void load_ro2(const __half* p, float2 (&f)[4]) {
         cvt2(__ldg(reinterpret_cast<const uint4*>(p)), f);
     }
-    __device__ __forceinline__ static void store2(__half* p, const float2 (&f)[4]) {
+    // streaming (evict-first) store: the outputs of this path are not re-read by the same kernel
+    __device__ __forceinline__ static void store2(__half* p, const float2 (&f)[4]) { __stcs(reinterpret_cast<uint4*>(p), pack2(f)); }
+    // write-back store, for warps whose one store instruction covers only part of each 128-byte line
+    // (an evict-first line can leave L2 before the other part arrives, costing a partial DRAM write)
+    __device__ __forceinline__ static void store2_wb(__half* p, const float2 (&f)[4]) {
+        *reinterpret_cast<uint4*>(p) = pack2(f);
+    }
+    __device__ __forceinline__ static uint4 pack2(const float2 (&f)[4]) {
         uint4 u;
         __half2* h = reinterpret_cast<__half2*>(&u);
 #pragma unroll
         for (int i = 0; i < 4; ++i) h[i] = __float22half2_rn(f[i]);
-        *reinterpret_cast<uint4*>(p) = u;
+        return u;
     }
     // lane-private staging: a vector occupies kChunks 16-byte chunks, chunk c of lane l at slot[c*32 + l]
     static constexpr int kChunks = 1;
@@ -247,7 +254,11 @@ struct Vec8<float> {
         f[2] = make_float2(b.x, b.y);
         f[3] = make_float2(b.z, b.w);
     }
-    __device__ __forceinline__ static void store2(float* p, const float2 (&f)[4]) {
+    __device__ __forceinline__ static void store2(float* p, const float2 (&f)[4]) {  // streaming
+        __stcs(reinterpret_cast<float4*>(p), make_float4(f[0].x, f[0].y, f[1].x, f[1].y));
+        __stcs(reinterpret_cast<float4*>(p) + 1, make_float4(f[2].x, f[2].y, f[3].x, f[3].y));
+    }
+    __device__ __forceinline__ static void store2_wb(float* p, const float2 (&f)[4]) {  // write-back
         reinterpret_cast<float4*>(p)[0] = make_float4(f[0].x, f[0].y, f[1].x, f[1].y);
         reinterpret_cast<float4*>(p)[1] = make_float4(f[2].x, f[2].y, f[3].x, f[3].y);
     }
@@ -301,6 +312,11 @@ struct Vec8<float> {
 // Position q*d + r of a grid-stride walk, advanced by a fixed step without dividing: the quotient and
 // remainder of the step are computed once, each advance is two adds and a carry. (A 64-bit division
 // per work item costs dozens of instructions, which the byte-light kernels here cannot afford.)
+// Hint that the 128-byte line holding p will be read soon: the line is fetched into L2 with no
+// register held and nothing to wait for. Used to start the next work item's HBM reads while the
+// current item is still being computed.
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 struct StridePos {
     int64_t q;
     int r;

@@ -30,6 +30,7 @@ struct NormRowsArgs {
     void* qout;  // optional quantised xn (wide design only): codes in the QuantFormat of the launch
     void* sout;  // and its group scales
     float gs;    // NVFP4 per-tensor scale
+    int lookahead;  // wide design with a quantised output: prefetch the CTA's next row into L2 (0/1)
 };
 
 template <typename TI, typename TO, int VPT>
@@ -346,6 +347,18 @@ __global__ void __launch_bounds__(512) norm_rows_wide_kernel(const NormRowsArgs 
                 if (has_x) rx[k] = Vec8<TI>::ldcs_raw(xrow + e);
             }
         }
+        if (QF != kQfNone && a.lookahead && u + gridDim.x < a.units) {  // the CTA's next row, into L2
+            const int64_t un = u + gridDim.x;
+            const int64_t tn = a.hc == 1 ? un : un / a.hc;
+#pragma unroll
+            for (int k = 0; k < VPL; ++k) {
+                const int e = k * span + threadIdx.x * 8;
+                if (e < n) {
+                    prefetch_l2(res + un * n + e);
+                    if (has_x && tn != t) prefetch_l2(x + tn * n + e);
+                }
+            }
+        }
         const float2 gate = splat2((has_x && a.inj != nullptr) ? 2.0f / (1.0f + __expf(-a.inj[u] / (float)a.hc))
                                                                 : 1.0f);
         auto residual_sum = [&](int k, float2 (&v)[4]) {  // v = residual + x * gate
@@ -458,6 +471,7 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
     a.stage_bytes = a.row_bytes * (x ? 2u : 1u);
     a.qout = a.sout = nullptr;
     a.gs = 1.0f;
+    a.lookahead = 0;  // without a quantised output it did not pay (76 vs 76 % at 4096 x 4 x 2560)
 
     // Direct design while a row fits one warp's register budget (<= 12 fp16 or 4 fp32 vectors per
     // lane), the wide design (CTA-owned rows) past it; the TMA ring only on request.
@@ -583,6 +597,9 @@ static int launch_norm_rows_quant(const void* x, void* res, const void* w, const
     a.qout = qout;
     a.sout = sout;
     a.gs = gs;
+    // on by default for the quantising rows (76 -> 80 % of peak at 4096 x 4 x 2560): the group
+    // quantiser's epilogue is long enough that the next row's reads are worth starting under it
+    a.lookahead = tuning(kFamNorm).stages == 1 ? 0 : 1;
     return launch_norm_rows_wide<TI, TO, QF>(a, di, stream);
 }
 

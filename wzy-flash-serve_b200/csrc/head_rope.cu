@@ -351,12 +351,15 @@ __global__ void __launch_bounds__(128) head_rope_direct_kernel(const HeadRopeArg
 // Pair design: the direct design's per-token head chunks with L2 = HD/16 lanes per head, each lane
 // holding two 8-element chunks. With P = rot/16 rotary chunk pairs (c, c + P), lane m < P holds exactly
 // the pair (m, m + P), so the NeoX rotation is done inside the lane with no shuffle; lanes m >= P hold
-// two adjacent chunks of the rest of the head (2P + 2(m - P), +1). The norm reduces over L2 lanes. The
+// chunks m + P and m + L2 of the rest of the head, so the first load instruction of a head covers
+// chunks [0, P) and [2P, L2 + P) and the second [P, 2P) and [L2 + P, 2 L2): every 32-byte sector is
+// read whole by one instruction (16 sectors per head, not 28). The norm reduces over L2 lanes. The
 // rotation expressions are the direct design's (own*cos + partner*(+-sin), fused), so results match it
-// bit for bit. Five CTAs per SM (<= 102 registers, 96 used with no spill) instead of the four that an
-// unbounded allocation (106) leaves: 82 -> 86 % of HBM peak at 262K tokens on the same box.
+// bit for bit. With 3 rounds per item, five CTAs per SM (<= 102 registers, 96 used with no spill)
+// instead of the four that an unbounded allocation (106) leaves: 82 -> 86 % of HBM peak at 262K
+// tokens on the same box. With 9 rounds, three (156 registers).
 template <typename T, int HD, int kNH>
-__global__ void __launch_bounds__(128, 5) head_rope_pair_kernel(const HeadRopeArgs a) {
+__global__ void __launch_bounds__(128, kNH >= 9 ? 3 : 5) head_rope_pair_kernel(const HeadRopeArgs a) {
     constexpr int L2 = HD / 16;   // lanes per head
     constexpr int HPW = 32 / L2;  // heads side by side in one warp
     constexpr int CH = kNH * HPW; // heads per chunk item
@@ -370,8 +373,8 @@ __global__ void __launch_bounds__(128, 5) head_rope_pair_kernel(const HeadRopeAr
     const int64_t items = a.T * chunks;
     const int half = a.rot / 2, P = half / 8;
     const bool rot_lane = li < P;
-    const int c0 = rot_lane ? li : 2 * P + 2 * (li - P);  // first chunk of this lane
-    const int c1 = rot_lane ? li + P : c0 + 1;            // second chunk
+    const int c0 = rot_lane ? li : li + P;       // first chunk of this lane
+    const int c1 = rot_lane ? li + P : li + L2;  // second chunk
     const int64_t base_pos = (a.d_base_pos ? (int64_t)__ldg(a.d_base_pos) : 0) + a.pos_offset;
 
     // gammas (+ weight offset) as a lane-major table: sgl[s][k][l] = dims 4(k&1).. of chunk c0 (k < 2)
@@ -379,8 +382,7 @@ __global__ void __launch_bounds__(128, 5) head_rope_pair_kernel(const HeadRopeAr
     __shared__ __align__(16) float4 sgl[2][4][L2];
     for (int i = threadIdx.x; i < 8 * L2; i += blockDim.x) {
         const int s = i / (4 * L2), k = (i / L2) % 4, l = i % L2;
-        const int lc0 = l < P ? l : 2 * P + 2 * (l - P);
-        const int c = k < 2 ? lc0 : (l < P ? l + P : lc0 + 1);
+        const int c = k < 2 ? (l < P ? l : l + P) : (l < P ? l + P : l + L2);
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (a.sec[s].heads > 0) {
             const T* gm = static_cast<const T*>(a.sec[s].gamma) + c * 8 + (k & 1) * 4;
@@ -682,6 +684,13 @@ static int launch_head_rope(const HeadSection& q, const HeadSection& k, const fl
             return launch_head_rope_direct<T, 4>(a, hd, htot, di, stream);
         }
         if (alt) return launch_head_rope_pair<T, 2>(a, hd, htot, di, stream);
+        // Long calls: 9 rounds per item (the benchmark's 18 heads are one item per token; 3 CTAs per
+        // SM, 9 KB in flight per warp): 90 -> 91 % of peak at 262K tokens. Short calls keep 3 rounds,
+        // whose 3x more items fill the GPU better (56 vs 51 % at 4096 tokens).
+        const int ch9 = 9 * (512 / hd);
+        const int64_t per_tok9 = (htot + ch9 - 1) / ch9;
+        const bool fill9 = 3 * htot >= 2 * per_tok9 * ch9;
+        if (fill9 && a.T * per_tok9 >= (int64_t)di.sms * 12 * 8) return launch_head_rope_pair<T, 9>(a, hd, htot, di, stream);
         return launch_head_rope_pair<T, 3>(a, hd, htot, di, stream);
     }
 

@@ -408,6 +408,119 @@ __global__ void __launch_bounds__(512) norm_rows_wide_kernel(const NormRowsArgs 
     }
 }
 
+// Token design for 4-stream rows (hc = 4, the reference model's hyper-connection width, with bo_prev):
+// a CTA owns a token -- its 4 (token, stream) rows and the one bo_prev row they share. Thread i holds
+// vectors k * blockDim + i of bo_prev and of the 4 rows; the 4 partial sums of squares meet in shared
+// memory behind ONE barrier per token (double-buffered by token parity, as in the wide design), then
+// each row is scaled and written. Against the row-per-CTA wide design, bo_prev is read once per token
+// instead of once per row, there is one barrier per 4 rows, and each CTA has 4 rows in flight. The
+// arithmetic per element is the wide design's; only the order of the cross-warp partial sums follows
+// this CTA's warp count.
+// Register caps: unbounded, the compiler hoists all 4 streams' gamma loads and takes 118 registers,
+// which leaves one 320-thread CTA per SM. One vector per thread fits 72 with no spill (2 CTAs of 320:
+// 79 -> 82 % of HBM peak at 4096 tokens x 4 x 2560 against the wide design); with a quantised output
+// 64 and a 32-60 byte spill (3 CTAs: 82 -> 83.5 %, where the 72 cap gives 79 %).
+template <typename TI, typename TO, int VPL, int QF>
+__global__ void __maxnreg__(VPL == 1 ? (QF == kQfNone ? 72 : 64) : 128) norm_rows_token4_kernel(const NormRowsArgs a) {
+    constexpr int HC = 4;
+    __shared__ float part[2][HC][16];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int nw = blockDim.x >> 5;
+    const int span = blockDim.x * 8;
+    const TI* __restrict__ x = static_cast<const TI*>(a.x);
+    TI* __restrict__ res = static_cast<TI*>(a.res);
+    const TI* __restrict__ w = static_cast<const TI*>(a.w);
+    TO* __restrict__ y = static_cast<TO*>(a.y);
+    const int n = a.n;
+    const int64_t T = a.units / HC;
+    int par = 0;
+
+    for (int64_t t = blockIdx.x; t < T; t += gridDim.x, par ^= 1) {
+        typename Vec8<TI>::Raw rr[HC][VPL], rx[VPL];
+        const int64_t u0 = t * HC;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int e = k * span + threadIdx.x * 8;
+            if (e < n) {
+                rx[k] = Vec8<TI>::ldcs_raw(x + t * n + e);
+#pragma unroll
+                for (int c = 0; c < HC; ++c) rr[c][k] = Vec8<TI>::ldcs_raw(res + (u0 + c) * n + e);
+            }
+        }
+        float gate[HC];
+#pragma unroll
+        for (int c = 0; c < HC; ++c) gate[c] = a.inj != nullptr ? 2.0f / (1.0f + __expf(-a.inj[u0 + c] / (float)HC)) : 1.0f;
+        auto residual_sum = [&](int c, int k, float2 (&v)[4]) {  // v = residual + x * gate
+            Vec8<TI>::cvt2(rr[c][k], v);
+            float2 xv[4];
+            Vec8<TI>::cvt2(rx[k], xv);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] = ffma2(xv[i], splat2(gate[c]), v[i]);
+        };
+#pragma unroll
+        for (int c = 0; c < HC; ++c) {
+            float ss = 0.f;
+#pragma unroll
+            for (int k = 0; k < VPL; ++k) {
+                if (k * span + threadIdx.x * 8 < n) {
+                    float2 v[4];
+                    residual_sum(c, k, v);
+                    ss += sumsq8(v);
+                }
+            }
+            ss = group_sum<32>(ss);
+            if (lane == 0) part[par][c][warp] = ss;
+        }
+        __syncthreads();
+        const float2 woff = splat2(a.w_offset);
+#pragma unroll
+        for (int c = 0; c < HC; ++c) {
+            float tot = 0.f;
+            for (int i = 0; i < nw; ++i) tot += part[par][c][i];  // same order in every thread
+            const float2 sc = splat2(rsqrt_approx(tot / (float)n + a.eps));
+            const int64_t u = u0 + c;
+#pragma unroll
+            for (int k = 0; k < VPL; ++k) {
+                const int e = k * span + threadIdx.x * 8;
+                float2 o[4] = {};
+                if (e < n) {
+                    float2 v[4], g[4];
+                    residual_sum(c, k, v);
+                    Vec8<TI>::load_ro2(w + c * n + e, g);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) o[i] = fmul2(fmul2(v[i], sc), fadd2(woff, g[i]));  // (v*sc)*g
+                    Vec8<TO>::store2(y + u * n + e, o);
+                    Vec8<TI>::store2(res + u * n + e, v);
+                }
+                if (QF != kQfNone) {  // every lane: the group max is a shuffle
+                    const float yo[8] = {o[0].x, o[0].y, o[1].x, o[1].y, o[2].x, o[2].y, o[3].x, o[3].y};
+                    quant_group_store<QF>(yo, e < n, a.qout, a.sout, a.gs, (u * n + e) >> 3, lane);
+                }
+            }
+        }
+    }
+}
+
+// Shape of the token design for a row of `vecs` vectors: VPL vectors per thread (1 or 2; 0 = the
+// design does not apply) over the fewest warps that hold the row.
+static void token4_shape(int vecs, int& nw, int& vpl) {
+    vpl = vecs <= 512 ? 1 : vecs <= 1024 ? 2 : 0;
+    nw = vpl ? (vecs + 32 * vpl - 1) / (32 * vpl) : 0;
+}
+
+template <typename TI, typename TO, int QF>
+static int launch_norm_rows_token4(const NormRowsArgs& a, int nw, int vpl, const DeviceInfo& di,
+                                   cudaStream_t stream) {
+    const int threads = nw * 32;
+    const void* kern = vpl == 1 ? (const void*)norm_rows_token4_kernel<TI, TO, 1, QF>
+                                : (const void*)norm_rows_token4_kernel<TI, TO, 2, QF>;
+    const int grid = persistent_grid(di, resident_ctas(kern, threads, 0), a.units / 4);
+    if (vpl == 1) norm_rows_token4_kernel<TI, TO, 1, QF><<<grid, threads, 0, stream>>>(a);
+    else norm_rows_token4_kernel<TI, TO, 2, QF><<<grid, threads, 0, stream>>>(a);
+    return launch_status();
+}
+
 // Warps per CTA and vectors per thread of the wide design for a row of `vecs` 8-element vectors:
 // the fewest warps (4, 8, 16) that keep VPL within the register budget, VPL rounded up to an
 // instantiated count.
@@ -423,6 +536,13 @@ static void wide_shape(int vecs, int& nw, int& vpl) {
 template <typename TI, typename TO, int QF>
 static int launch_norm_rows_wide(const NormRowsArgs& a, const DeviceInfo& di, cudaStream_t stream) {
     int nw = 0, vpl = 0;
+    if constexpr (sizeof(TI) == 4) {
+        // 4 streams sharing a bo_prev row: the token design (fp32 rows, up to 8192 wide)
+        if (a.hc == 4 && a.x != nullptr && variant(kFamNorm) != WZYB_VARIANT_WIDE) {
+            token4_shape(a.n / 8, nw, vpl);
+            if (vpl) return launch_norm_rows_token4<TI, TO, QF>(a, nw, vpl, di, stream);
+        }
+    }
     wide_shape<TI>(a.n / 8, nw, vpl);
     const int threads = nw * 32;
     const void* kern = nullptr;

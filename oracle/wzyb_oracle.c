@@ -141,7 +141,9 @@ static void q8_group_n(const float* v, int n, int8_t* q, float* s) {
     const float d = am / 127.0f;
     const float inv = d > 0.f ? 127.0f / am : 0.f;
     for (int i = 0; i < n; ++i) {
-        int qi = (int)rintf(v[i] * inv);
+        const float t = v[i] * inv;
+        /* __float2int_rn maps NaN (a NaN or infinite input) to 0 */
+        int qi = isnan(t) ? 0 : (int)rintf(t);
         q[i] = (int8_t)(qi < -127 ? -127 : (qi > 127 ? 127 : qi));
     }
     *s = d;

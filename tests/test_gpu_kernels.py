@@ -617,6 +617,10 @@ def test_quant_act_f32(wz, orc, T, cols, q32, q16):
     r = rng(T + cols)
     x = (3 * r.standard_normal((T, cols))).astype(np.float32)
     x[0, :32] = 0.0  # an all-zero group
+    if cols >= 96:
+        # non-finite inputs (NaN dropped from the group max, code 0) and exact .5 ties (amax 127: t = x)
+        x[-1, 3], x[-1, 70], x[-1, 75] = np.nan, np.inf, -np.inf
+        x[-1, 32:40] = [127.0, 2.5, 3.5, -2.5, -0.5, 0.5, 126.5, -126.5]
     w32, ws32, w16, ws16 = orc.quant_act_f32(x, q32, q16)
     n = T * cols
     d32 = torch.empty(n, dtype=torch.int8, device=DEV) if q32 else None

@@ -180,13 +180,16 @@ def test_ulp_helper():
     assert list(f16_ulp_distance(a, b)) == [1, 0, 1, 0]
 
 
-def _np_q8(v):
-    """Q8_0 per 32-element group restated in numpy (round half to even, clamp to +-127)."""
-    g = v.reshape(-1, 32).astype(np.float32)
-    am = np.abs(g).max(axis=1)
-    d = (am / np.float32(127.0)).astype(np.float32)
-    inv = np.where(d > 0, np.float32(127.0) / np.where(am > 0, am, 1), 0).astype(np.float32)
-    q = np.clip(np.rint(g * inv[:, None]), -127, 127).astype(np.int8)
+def _np_q8(v, group=32):
+    """Q8_0 per group restated in numpy (round half to even, clamp to +-127); the group max drops NaNs
+    (fmaxf) and a NaN product (NaN or infinite input) gives code 0 (__float2int_rn)."""
+    g = v.reshape(-1, group).astype(np.float32)
+    with np.errstate(invalid="ignore", divide="ignore", over="ignore"):
+        am = np.nanmax(np.where(np.isnan(g), 0, np.abs(g)), axis=1).astype(np.float32)
+        d = (am / np.float32(127.0)).astype(np.float32)
+        inv = np.where(d > 0, np.float32(127.0) / np.where(am > 0, am, 1), 0).astype(np.float32)
+        t = (g * inv[:, None]).astype(np.float32)
+        q = np.clip(np.rint(np.where(np.isnan(t), 0, t)), -127, 127).astype(np.int8)
     return q.reshape(v.shape), d
 
 
@@ -360,15 +363,15 @@ def test_quant_act_against_numpy(orc):
     r = np.random.default_rng(53)
     x = (3 * r.standard_normal(32 * 40)).astype(np.float32)
     x[64:96] = 0.0
+    x[100], x[140], x[200] = np.nan, np.inf, -np.inf  # non-finite inputs: NaN dropped from the max, code 0
+    x[256:288] = 127.0 * np.sign(r.standard_normal(32))  # amax 127: t = x exactly, so .5 ties below
+    x[257:263] = [2.5, 3.5, -2.5, -0.5, 0.5, 126.5]
     q32, s32, q16, s16 = orc.quant_act_f32(x)
     w32, d32 = _np_q8(x)
-    assert np.array_equal(q32, w32) and np.array_equal(s32, d32)
-    g = x.reshape(-1, 16)
-    am = np.abs(g).max(axis=1)
-    d = (am / np.float32(127.0)).astype(np.float32)
-    inv = np.where(d > 0, np.float32(127.0) / np.where(am > 0, am, 1), 0).astype(np.float32)
-    w16 = np.clip(np.rint(g * inv[:, None]), -127, 127).astype(np.int8).reshape(-1)
-    assert np.array_equal(q16, w16) and np.array_equal(s16, d)
+    assert np.array_equal(q32, w32) and np.array_equal(s32.view(np.uint32), d32.view(np.uint32))
+    assert list(q32[257:263]) == [2, 4, -2, 0, 0, 126]  # round half to even
+    w16, d16 = _np_q8(x, 16)
+    assert np.array_equal(q16, w16) and np.array_equal(s16.view(np.uint32), d16.view(np.uint32))
 
 
 def _e2m1_exact(v):

@@ -86,11 +86,12 @@ def test_rmsnorm_without_add(wz, orc, variant):
     assert_f16_close(host(dy), y_ref, ULP_TOL, "rmsnorm only")
 
 
-@pytest.mark.parametrize("T,n", [(19, 2560), (19, 2056), (19, 6144), (1000, 2560)])
+@pytest.mark.parametrize("T,n", [(19, 2560), (19, 6144), (700, 2056), (700, 6144), (1000, 2560)])
 @pytest.mark.parametrize("hc,with_inj,out16", [(1, False, False), (4, True, False), (4, True, True), (4, False, True)])
 def test_gr_norm_f32_hyper_connection(wz, orc, T, n, hc, with_inj, out16, variant):
-    """n 2056: a partly idle last warp; 6144: two vectors per thread; 1000 tokens: several tokens (rows)
-    per CTA, so the parity-buffered partial sums are reused."""
+    """19 tokens take the row-per-CTA design, 700+ the token design with 4 streams (hc = 4); n 2056: a
+    partly idle last warp; 6144: two vectors per thread; 1000 tokens: several tokens per CTA, so the
+    parity-buffered partial sums are reused."""
     r = rng(11 + hc + n)
     R = r.standard_normal((T * hc, n)).astype(np.float32)
     bo = r.standard_normal((T, n)).astype(np.float32)
@@ -369,7 +370,7 @@ def _q8_close(q_got, s_got, q_want, s_want, what):
 
 
 @pytest.mark.parametrize("T,n,hc", [(1, 2560, 4), (8, 2560, 4), (5, 2048, 1), (3, 96, 2), (7, 2080, 4), (3, 6144, 4),
-                                    (700, 2560, 4)])
+                                    (700, 2560, 4), (650, 2080, 4), (600, 6144, 4)])
 def test_gr_norm_q8_f32(wz, orc, T, n, hc):
     r = rng(T * n + hc)
     R = r.standard_normal((T * hc, n)).astype(np.float32)
@@ -665,11 +666,13 @@ def test_quant_act_block_formats(wz, orc, fmt, gs, T, cols):
     assert np.array_equal(host(q), want_q) and np.array_equal(host(s), want_s)
 
 
+@pytest.mark.parametrize("T", [9, 700])
 @pytest.mark.parametrize("fmt", ["mxfp8", "nvfp4"])
-def test_gr_norm_block_formats(wz, orc, fmt):
-    """The norm's fp32 output and, from exactly those values, its block-format codes."""
+def test_gr_norm_block_formats(wz, orc, fmt, T):
+    """The norm's fp32 output and, from exactly those values, its block-format codes (9 tokens: a CTA
+    per row; 700: a CTA per token)."""
     r = rng(61)
-    T, n, hc = 9, 2560, 4
+    n, hc = 2560, 4
     R = r.standard_normal((T * hc, n)).astype(np.float32)
     bo = r.standard_normal((T, n)).astype(np.float32)
     inj = r.standard_normal(T * hc).astype(np.float32)

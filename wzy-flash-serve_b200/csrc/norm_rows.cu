@@ -537,8 +537,11 @@ template <typename TI, typename TO, int QF>
 static int launch_norm_rows_wide(const NormRowsArgs& a, const DeviceInfo& di, cudaStream_t stream) {
     int nw = 0, vpl = 0;
     if constexpr (sizeof(TI) == 4) {
-        // 4 streams sharing a bo_prev row: the token design (fp32 rows, up to 8192 wide)
-        if (a.hc == 4 && a.x != nullptr && variant(kFamNorm) != WZYB_VARIANT_WIDE) {
+        // 4 streams sharing a bo_prev row: the token design (fp32 rows, up to 8192 wide), for calls of
+        // at least 4 tokens per SM. Shorter calls (decode) keep a CTA per row: 4x the CTAs, and a
+        // 1-token call takes 3.2 us there against 6.4 us with its 4 rows in one CTA.
+        if (a.hc == 4 && a.x != nullptr && variant(kFamNorm) != WZYB_VARIANT_WIDE &&
+            a.units / 4 >= (int64_t)di.sms * 4) {
             token4_shape(a.n / 8, nw, vpl);
             if (vpl) return launch_norm_rows_token4<TI, TO, QF>(a, nw, vpl, di, stream);
         }

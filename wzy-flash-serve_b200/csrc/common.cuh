@@ -414,8 +414,9 @@ __device__ __forceinline__ float2 sigmoid2(float2 z) {
 // Codes: t = fl(v * inv) (|t| <= 127 * (1 + 2^-23)^2 for finite v; rounded on its own, fmul2_unfused,
 // so exact .5 ties of t stay ties), then rint(t) as the low byte of fl(t + 1.5 * 2^23), a float whose
 // unit is 1 there, so the add itself is the round-to-nearest-even;
-// packed FMUL2/FADD2 on the FMA pipe instead of a conversion instruction per element (SwiGLU + Q8 and the
-// quantiser 80 -> 85 % of HBM peak). A lane whose 8 values are not all finite (seen by a NaN-propagating
+// packed FMA2 (+0 addend) and FADD2 on the FMA pipe instead of a conversion instruction per element
+// (SwiGLU + Q8 80 -> 82 %, the quantiser 78 -> 81 % of HBM peak). A lane whose 8 values are not all
+// finite (seen by a NaN-propagating
 // max) takes the conversion instruction instead, which maps the NaN that t then is to 0 as the
 // reference's __float2int_rn does; the group's amax drops NaNs (fmaxf) as the reference's does.
 __device__ __forceinline__ float fmax_nan(float a, float b) {
@@ -424,10 +425,11 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
     return r;
 }
 
-template <int kLanes = 4>
-__device__ __forceinline__ void q8_group_store(const float (&v)[8], bool active, signed char* q, float* s, int lane) {
+// A lane's part of a Q8 group: the max |v| of its 8 values with NaNs dropped (fmaxf, as the reference)
+// and whether all 8 are finite (a NaN-propagating max; false also for inf).
+__device__ __forceinline__ float q8_lane_max(const float (&v)[8], bool active, bool& finite) {
     float am = 0.f;
-    bool finite = true;
+    finite = true;
     if (active) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) am = fmax_nan(am, fabsf(v[i]));
@@ -438,9 +440,14 @@ __device__ __forceinline__ void q8_group_store(const float (&v)[8], bool active,
             for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
         }
     }
-#pragma unroll
-    for (int o = 1; o < kLanes; o <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    if (!active) return;
+    return am;
+}
+
+// Codes and scale of a lane's 8 values given the group's max: d = am / 127 stored by the group's
+// first lane (lane % kLanes == 0), 8 code bytes at q.
+template <int kLanes>
+__device__ __forceinline__ void q8_codes_store(const float (&v)[8], float am, bool finite, signed char* q, float* s,
+                                               int lane) {
     const float d = am / 127.0f;
     const float inv = d > 0.f ? 127.0f / am : 0.f;
     uint32_t b[8];
@@ -462,6 +469,29 @@ __device__ __forceinline__ void q8_group_store(const float (&v)[8], bool active,
                            0x5410);
     *reinterpret_cast<uint2*>(q) = make_uint2(w[0], w[1]);
     if ((lane & (kLanes - 1)) == 0) *s = d;
+}
+
+template <int kLanes = 4>
+__device__ __forceinline__ void q8_group_store(const float (&v)[8], bool active, signed char* q, float* s, int lane) {
+    bool finite;
+    float am = q8_lane_max(v, active, finite);
+#pragma unroll
+    for (int o = 1; o < kLanes; o <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    if (active) q8_codes_store<kLanes>(v, am, finite, q, s, lane);
+}
+
+// Both group sizes of quant_act_multi from one lane max: the 16-group max over 2 lanes, the 32-group
+// max as the max of two 16-group maxima (max is exact in any order, so the scales are the same as
+// two separate reductions).
+__device__ __forceinline__ void q8_group_store_16_32(const float (&v)[8], bool active, signed char* q16, float* s16,
+                                                     signed char* q32, float* s32, int lane) {
+    bool finite;
+    float am16 = q8_lane_max(v, active, finite);
+    am16 = fmaxf(am16, __shfl_xor_sync(0xffffffffu, am16, 1));
+    const float am32 = fmaxf(am16, __shfl_xor_sync(0xffffffffu, am16, 2));
+    if (!active) return;
+    q8_codes_store<2>(v, am16, finite, q16, s16, lane);
+    q8_codes_store<4>(v, am32, finite, q32, s32, lane);
 }
 
 // Shared scale of an MXFP8 block as its E8M0 byte: X = 2^ceil(log2(amax / 448)), the smallest power

@@ -25,8 +25,12 @@ __global__ void __launch_bounds__(256) quant_act_kernel(const float* __restrict_
         const bool act = v < nvec;
         float o[8] = {};
         if (act) Vec8<float>::load_stream(x + v * 8, o);
-        if (q16 != nullptr) q8_group_store<2>(o, act, q16 + v * 8, s16 + (v >> 1), lane);
-        if (q32 != nullptr) q8_group_store<4>(o, act, q32 + v * 8, s32 + (v >> 2), lane);
+        if (q16 != nullptr && q32 != nullptr) {
+            q8_group_store_16_32(o, act, q16 + v * 8, s16 + (v >> 1), q32 + v * 8, s32 + (v >> 2), lane);
+        } else {
+            if (q16 != nullptr) q8_group_store<2>(o, act, q16 + v * 8, s16 + (v >> 1), lane);
+            if (q32 != nullptr) q8_group_store<4>(o, act, q32 + v * 8, s32 + (v >> 2), lane);
+        }
     }
 }
 

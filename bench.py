@@ -6,7 +6,9 @@ of configs[4] (262,144 tokens, token-sharded across the GPUs with no collective)
     q/k RMSNorm + partial RoPE           q [T, 16, 256], k [T, 2, 256], rot 64, theta 1e7
     SwiGLU                               [11*T, 512]   (10 routed + 1 shared expert rows per token)
     GDN gated RMSNorm                    o, z [T, 32, 128]
-Inputs are larger than L2 (~24 GB per step on one GPU), so no L2 flush is needed between steps.
+Inputs are larger than L2 (~24 GB per step on one GPU), so no L2 flush is needed between steps; with
+--tokens small enough that a shard's step moves under 4x L2 (e.g. 4096 tokens on 2+ GPUs), L2 is
+flushed before every step and the step is timed from its first kernel to its last.
 Per-kernel numbers at the 4096-token configs[1]/[2]/[3] shapes are measured separately with the
 L2 flushed before every launch.
 
@@ -33,6 +35,7 @@ sys.path.insert(0, os.path.join(ROOT, "wzy-flash-serve_b200"))
 
 METRIC = "layer-kernel HBM GB/s (% of 8 TB/s) and tokens/s at 1/2/4/8 B200"
 NOMINAL_HBM_GBS = 8000.0
+L2_BYTES = 126 * (1 << 20)  # B200 L2
 
 # configs[4] = configs[1] + configs[2] at 262,144 tokens
 TOKENS = 262144
@@ -561,7 +564,23 @@ def main():
         for i in range(4):
             sh.launch(i, s)
 
+    # A shard whose step moves less than 4x the 126 MB L2 (the 4096-token config on 2+ GPUs) would be
+    # timed partly out of L2: then L2 is flushed before every step (a 256 MB write, then a 256 MB read
+    # so the write-back of the flush is not charged to the step) and the step is timed from its first
+    # kernel to its last, the flush excluded.
+    shard_bytes = n * sum(BYTES_PER_TOKEN.values())
+    flush_l2 = shard_bytes < 4 * L2_BYTES
+    if flush_l2:
+        fl_w = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        fl_r = torch.ones(256 << 20, dtype=torch.uint8, device=dev)
+
+    def flush():
+        fl_w.fill_(1)
+        fl_r.sum(dtype=torch.int32)
+
     for _ in range(args.warmup):
+        if flush_l2:
+            flush()
         step()
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
@@ -574,6 +593,8 @@ def main():
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_start.record(s)
     for k in range(args.steps):
+        if flush_l2:
+            flush()
         for i in range(4):
             ev[k][i].record(s)
             sh.launch(i, s)
@@ -583,7 +604,10 @@ def main():
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
-    ms_total = t_start.elapsed_time(t_end)
+    if flush_l2:
+        ms_total = sum(ev[k][0].elapsed_time(ev[k][4]) for k in range(args.steps))
+    else:
+        ms_total = t_start.elapsed_time(t_end)
     kern_ms = [statistics.mean(ev[k][i].elapsed_time(ev[k][i + 1]) for k in range(args.steps)) for i in range(4)]
     launches = 4 * args.steps
     faults = wz.read_faults()
@@ -651,13 +675,14 @@ def main():
             "vs_baseline": None,
             "dtype": "fp16 I/O, fp32 math",
             "data": "synthetic (seeded normal activations, N(0,0.02) weights as 1+w)",
-            "config": {"workload": "configs[4]: configs[1]+[2] layer bundle at 262,144 tokens, token-sharded, "
-                                   "no collective",
+            "config": {"workload": f"configs[4]: configs[1]+[2] layer bundle at {args.tokens:,} tokens, "
+                                   "token-sharded, no collective",
                        "tokens": args.tokens, "tokens_per_gpu": n, "hidden": HIDDEN, "q_heads": QH, "kv_heads": KH,
                        "head_dim": HD, "rot_dims": ROT, "expert_rows_per_token": EXPERT_ROWS, "ffn": FFN,
                        "gdn_heads": GDN_H, "gdn_head_dim": GDN_HD, "parallelism": f"token-shard x{world}",
                        "norm_kernel_design": args.variant,
-                       "l2": "inputs larger than L2 (no flush)"},
+                       "l2": ("L2 flushed before every step (256 MB write + 256 MB read), step timed from its "
+                              "first kernel to its last" if flush_l2 else "inputs larger than L2 (no flush)")},
             "hbm": {"bundle_gbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9, 1),
                     "bundle_frac_of_8tbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9 / NOMINAL_HBM_GBS / world, 4),
                     "bundle_frac_of_peak_per_gpu": round(step_bytes / (ms_per_step * 1e-3) / 1e9 / peak / world, 4),

@@ -312,6 +312,16 @@ struct Vec8<float> {
 // Position q*d + r of a grid-stride walk, advanced by a fixed step without dividing: the quotient and
 // remainder of the step are computed once, each advance is two adds and a carry. (A 64-bit division
 // per work item costs dozens of instructions, which the byte-light kernels here cannot afford.)
+// Programmatic dependent launch (PDL). Every kernel of the library starts with pdl_begin(): wait until
+// the previous grid in the stream has completed and its writes are visible (a no-op when the launch
+// carried no programmatic dependency), then allow the next grid in the stream to be launched. No
+// kernel touches global memory before the wait, so PDL launches keep plain stream order semantics
+// while the next launch's set-up and CTA placement overlap this grid's tail.
+__device__ __forceinline__ void pdl_begin() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Hint that the 128-byte line holding p will be read soon: the line is fetched into L2 with no
 // register held and nothing to wait for. Used to start the next work item's HBM reads while the
 // current item is still being computed.

@@ -27,6 +27,7 @@ __global__ void __launch_bounds__(kGatherThreads) gather_rows_kernel(const uint4
                                                                       int64_t row_chunks, const int32_t* __restrict__ ids,
                                                                       int64_t T, uint4* __restrict__ out, int policy,
                                                                       uint32_t* oob) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
@@ -52,6 +53,7 @@ __global__ void __launch_bounds__(kGatherThreads) gather_bf16_f32_kernel(const u
                                                                           const int32_t* __restrict__ ids, int64_t T,
                                                                           uint4* __restrict__ out, int policy,
                                                                           uint32_t* oob) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
@@ -131,6 +133,7 @@ struct PleArgs {
 
 // Flattened over (token, head, chunk); each thread keeps kRowUnroll chunks in flight.
 __global__ void __launch_bounds__(kGatherThreads) ple_gather_kernel(const PleArgs a) {
+    pdl_begin();
     const int64_t per_tok = (int64_t)a.heads * a.chunks;
     const int64_t total = a.T * per_tok;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -164,6 +167,7 @@ __global__ void __launch_bounds__(kGatherThreads) ple_gather_kernel(const PleArg
 // position is stepped without division and the row index uses a mask for power-of-two tables.
 template <int CH>
 __global__ void __launch_bounds__(kGatherThreads) ple_gather_groups_kernel(const PleArgs a) {
+    pdl_begin();
     constexpr int GPW = 32 / CH;
     const int lane = threadIdx.x & 31;
     const int c = lane % CH;
@@ -215,7 +219,7 @@ int wzyb_embed_gather_rows(const void* table, int64_t vocab, int64_t row_bytes, 
     const int rc = wzyb::device_info(&di);
     if (rc != WZYB_OK) return rc;
     const int grid = wzyb::grid_for(T * 32, 8, di);
-    wzyb::gather_rows_kernel<<<grid, wzyb::kGatherThreads, 0, (cudaStream_t)stream>>>(
+    wzyb::launch_k(wzyb::gather_rows_kernel, grid, wzyb::kGatherThreads, 0, (cudaStream_t)stream, 
         (const uint4*)table, vocab, row_bytes / 16, ids, T, (uint4*)out, oob_policy, d_oob_count);
     return wzyb::launch_status();
 }
@@ -237,7 +241,7 @@ int wzyb_embed_gather_bf16_f32(const uint16_t* table, int64_t vocab, int hidden,
     const int rc = wzyb::device_info(&di);
     if (rc != WZYB_OK) return rc;
     const int grid = wzyb::grid_for(T * 32, 8, di);
-    wzyb::gather_bf16_f32_kernel<<<grid, wzyb::kGatherThreads, 0, (cudaStream_t)stream>>>(
+    wzyb::launch_k(wzyb::gather_bf16_f32_kernel, grid, wzyb::kGatherThreads, 0, (cudaStream_t)stream, 
         (const uint4*)table, vocab, hidden / 8, ids, T, (uint4*)out, oob_policy, d_oob_count);
     return wzyb::launch_status();
 }
@@ -284,14 +288,14 @@ int wzyb_ple_gather_f16(const uint16_t* const* tables, int heads, int64_t rows_p
         const int64_t threads = T * heads * (int64_t)a.chunks / wzyb::kRowUnroll;
         const int grid = wzyb::grid_for(threads, 8, di);
         cudaStream_t s = (cudaStream_t)stream;
-        if (a.chunks == 8) wzyb::ple_gather_groups_kernel<8><<<grid, wzyb::kGatherThreads, 0, s>>>(a);
-        else if (a.chunks == 16) wzyb::ple_gather_groups_kernel<16><<<grid, wzyb::kGatherThreads, 0, s>>>(a);
-        else wzyb::ple_gather_groups_kernel<32><<<grid, wzyb::kGatherThreads, 0, s>>>(a);
+        if (a.chunks == 8) wzyb::launch_k(wzyb::ple_gather_groups_kernel<8>, grid, wzyb::kGatherThreads, 0, s, a);
+        else if (a.chunks == 16) wzyb::launch_k(wzyb::ple_gather_groups_kernel<16>, grid, wzyb::kGatherThreads, 0, s, a);
+        else wzyb::launch_k(wzyb::ple_gather_groups_kernel<32>, grid, wzyb::kGatherThreads, 0, s, a);
         return wzyb::launch_status();
     }
     const int64_t total = T * heads * (int64_t)a.chunks;
     const int grid = wzyb::grid_for((total + wzyb::kRowUnroll - 1) / wzyb::kRowUnroll, 8, di);
-    wzyb::ple_gather_kernel<<<grid, wzyb::kGatherThreads, 0, (cudaStream_t)stream>>>(a);
+    wzyb::launch_k(wzyb::ple_gather_kernel, grid, wzyb::kGatherThreads, 0, (cudaStream_t)stream, a);
     return wzyb::launch_status();
 }
 

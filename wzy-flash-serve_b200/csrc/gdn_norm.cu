@@ -56,6 +56,7 @@ struct GdnArgs {
 
 template <typename TI, typename TO, int HD, int VPT>
 __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) gdn_norm_kernel(const GdnArgs a) {
+    pdl_begin();
     constexpr int L = HD / 8;
     extern __shared__ __align__(128) unsigned char smem[];
     const int S = a.stages;
@@ -153,6 +154,7 @@ __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) gdn_norm_kernel(const G
 // shared memory, no CTA barrier: warps stream independently like a copy kernel.
 template <typename TI, typename TO, int HD, int kU, bool SILU>
 __global__ void __launch_bounds__(256, sizeof(TI) == 2 ? 3 : 2) gdn_direct_kernel(const GdnArgs a) {
+    pdl_begin();
     constexpr int L = HD / 8;
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -209,6 +211,7 @@ __global__ void __launch_bounds__(256, sizeof(TI) == 2 ? 3 : 2) gdn_direct_kerne
 // no longer what bounds the bytes in flight.
 template <typename TI, typename TO, int HD, int kP, bool SILU>
 __global__ void __launch_bounds__(256) gdn_async_kernel(const GdnArgs a) {
+    pdl_begin();
     constexpr int L = HD / 8;
     constexpr int C = Vec8<TI>::kChunks;   // 16-byte chunks per 8-element vector
     constexpr int SLOT = 2 * C * 32;       // uint4 per ring slot: o and z vectors of 32 lanes
@@ -285,18 +288,18 @@ static int launch_gdn_warp(const GdnArgs& a, int hd, bool async_design, const De
         const int rc = ensure_smem(kern, smem);
         if (rc != WZYB_OK) return rc;
         const int grid = persistent_grid(di, resident_ctas(kern, 256, smem), (warp_items + 7) / 8);
-        if (hd == 64) gdn_async_kernel<TI, TO, 64, kP, SILU><<<grid, 256, smem, stream>>>(a);
-        else if (hd == 128) gdn_async_kernel<TI, TO, 128, kP, SILU><<<grid, 256, smem, stream>>>(a);
-        else gdn_async_kernel<TI, TO, 256, kP, SILU><<<grid, 256, smem, stream>>>(a);
+        if (hd == 64) launch_k(gdn_async_kernel<TI, TO, 64, kP, SILU>, grid, 256, smem, stream, a);
+        else if (hd == 128) launch_k(gdn_async_kernel<TI, TO, 128, kP, SILU>, grid, 256, smem, stream, a);
+        else launch_k(gdn_async_kernel<TI, TO, 256, kP, SILU>, grid, 256, smem, stream, a);
         return launch_status();
     }
     const void* kern = hd == 64    ? (const void*)gdn_direct_kernel<TI, TO, 64, 4, SILU>
                        : hd == 128 ? (const void*)gdn_direct_kernel<TI, TO, 128, 4, SILU>
                                    : (const void*)gdn_direct_kernel<TI, TO, 256, 4, SILU>;
     const int grid = persistent_grid(di, resident_ctas(kern, 256, 0), (warp_items + 7) / 8);
-    if (hd == 64) gdn_direct_kernel<TI, TO, 64, 4, SILU><<<grid, 256, 0, stream>>>(a);
-    else if (hd == 128) gdn_direct_kernel<TI, TO, 128, 4, SILU><<<grid, 256, 0, stream>>>(a);
-    else gdn_direct_kernel<TI, TO, 256, 4, SILU><<<grid, 256, 0, stream>>>(a);
+    if (hd == 64) launch_k(gdn_direct_kernel<TI, TO, 64, 4, SILU>, grid, 256, 0, stream, a);
+    else if (hd == 128) launch_k(gdn_direct_kernel<TI, TO, 128, 4, SILU>, grid, 256, 0, stream, a);
+    else launch_k(gdn_direct_kernel<TI, TO, 256, 4, SILU>, grid, 256, 0, stream, a);
     return launch_status();
 }
 
@@ -356,7 +359,7 @@ static int launch_gdn(const void* o, const void* z, const void* gamma, void* y, 
     if (hd == HDV && vpt == V) {                                                   \
         rc = ensure_smem((const void*)gdn_norm_kernel<TI, TO, HDV, V>, smem);      \
         if (rc != WZYB_OK) return rc;                                              \
-        gdn_norm_kernel<TI, TO, HDV, V><<<grid, threads, smem, stream>>>(a);       \
+        launch_k(gdn_norm_kernel<TI, TO, HDV, V>, grid, threads, smem, stream, a);       \
         return launch_status();                                                    \
     }
     WZYB_GDN_CASE(64, 1)

@@ -25,6 +25,7 @@ constexpr int kGrwUnroll = 4;
 __global__ void __launch_bounds__(kGrwThreads) gr_write_kernel(float* __restrict__ R, const float* __restrict__ blk,
                                                               const float* __restrict__ inj, int64_t rows, int n,
                                                               int hc) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int vpr = n >> 3;
     const int64_t nwarps = (int64_t)gridDim.x * (kGrwThreads / 32);
@@ -65,6 +66,7 @@ __global__ void __launch_bounds__(kGrwThreads) gr_write_flat_kernel(float* __res
                                                                    const float* __restrict__ blk,
                                                                    const float* __restrict__ inj, int64_t nvec,
                                                                    int vpr, int hc) {
+    pdl_begin();
     const int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (v >= nvec) return;
     const int64_t u = v / vpr;
@@ -92,6 +94,7 @@ template <typename TI, int kHC>
 __global__ void __launch_bounds__(kMixThreads) hc_mix_kernel(const TI* __restrict__ xn, const TI* __restrict__ gg,
                                                             float* __restrict__ mixed, __half* __restrict__ mixed16,
                                                             int64_t nvec, int vpr, int hc_rt, float inv_hc) {
+    pdl_begin();
     const int hc = kHC > 0 ? kHC : hc_rt;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t v0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -134,6 +137,7 @@ __global__ void __launch_bounds__(kMixThreads) hc_mix_kernel(const TI* __restric
 // --- silu_scale ----------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) silu_scale_kernel(const float* __restrict__ lo, __half* __restrict__ out,
                                                          int64_t nvec, float scale) {
+    pdl_begin();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += stride) {
         float2 x[4];
@@ -168,9 +172,9 @@ static int launch_hc_mix(const TI* xn, const TI* gg, float* mixed, __half* mixed
     const int64_t nvec = T * vpr;
     const int grid = persistent_grid(di, 8, (nvec + kMixThreads - 1) / kMixThreads);
     if (hc == 4)
-        hc_mix_kernel<TI, 4><<<grid, kMixThreads, 0, stream>>>(xn, gg, mixed, mixed16, nvec, vpr, hc, 0.25f);
+        launch_k(hc_mix_kernel<TI, 4>, grid, kMixThreads, 0, stream, xn, gg, mixed, mixed16, nvec, vpr, hc, 0.25f);
     else
-        hc_mix_kernel<TI, 0><<<grid, kMixThreads, 0, stream>>>(xn, gg, mixed, mixed16, nvec, vpr, hc, 1.0f / (float)hc);
+        launch_k(hc_mix_kernel<TI, 0>, grid, kMixThreads, 0, stream, xn, gg, mixed, mixed16, nvec, vpr, hc, 1.0f / (float)hc);
     return launch_status();
 }
 
@@ -192,12 +196,12 @@ int wzyb_gr_write_f32(float* R, const float* blk, const float* inj, int64_t T, i
     const int64_t nvec = rows * (n_embd / 8);
     if (rows < (int64_t)di.sms * 4) {  // fewer rows than a quarter of the warps one wave holds
         const int64_t blocks = (nvec + wzyb::kGrwThreads - 1) / wzyb::kGrwThreads;
-        wzyb::gr_write_flat_kernel<<<(unsigned)blocks, wzyb::kGrwThreads, 0, (cudaStream_t)stream>>>(
+        wzyb::launch_k(wzyb::gr_write_flat_kernel, (unsigned)blocks, wzyb::kGrwThreads, 0, (cudaStream_t)stream, 
             R, blk, inj, nvec, n_embd / 8, hc);
         return wzyb::launch_status();
     }
     const int grid = wzyb::persistent_grid(di, 8, (rows + 7) / 8);
-    wzyb::gr_write_kernel<<<grid, wzyb::kGrwThreads, 0, (cudaStream_t)stream>>>(R, blk, inj, rows, n_embd, hc);
+    wzyb::launch_k(wzyb::gr_write_kernel, grid, wzyb::kGrwThreads, 0, (cudaStream_t)stream, R, blk, inj, rows, n_embd, hc);
     return wzyb::launch_status();
 }
 
@@ -222,7 +226,7 @@ int wzyb_silu_scale_f16(const float* lo, uint16_t* out, int64_t n, float scale, 
     if (rc != WZYB_OK) return rc;
     const int64_t nvec = n / 8;
     const int grid = wzyb::persistent_grid(di, 8, (nvec + 255) / 256);
-    wzyb::silu_scale_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(lo, (__half*)out, nvec, scale);
+    wzyb::launch_k(wzyb::silu_scale_kernel, grid, 256, 0, (cudaStream_t)stream, lo, (__half*)out, nvec, scale);
     return wzyb::launch_status();
 }
 

@@ -43,6 +43,7 @@ struct HeadRopeArgs {
 
 template <typename T, int HD, int VPT>
 __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) head_rope_kernel(const HeadRopeArgs a) {
+    pdl_begin();
     constexpr int L = HD / 8;  // lanes per head (8, 16 or 32)
     extern __shared__ __align__(128) unsigned char smem[];
     const int S = a.stages;
@@ -269,6 +270,7 @@ __device__ __forceinline__ void norm_rope_head_sg(float2 (&p)[4], const float4 g
 // 128-thread CTAs and ~90 registers give ~20 resident warps per SM.
 template <typename T, int HD, int kNH>
 __global__ void __launch_bounds__(128) head_rope_direct_kernel(const HeadRopeArgs a) {
+    pdl_begin();
     constexpr int L = HD / 8;
     constexpr int HPW = 32 / L;         // heads side by side in one warp
     constexpr int CH = kNH * HPW;       // heads per chunk
@@ -360,6 +362,7 @@ __global__ void __launch_bounds__(128) head_rope_direct_kernel(const HeadRopeArg
 // tokens on the same box. With 9 rounds, three (156 registers).
 template <typename T, int HD, int kNH>
 __global__ void __launch_bounds__(128, kNH >= 9 ? 3 : 5) head_rope_pair_kernel(const HeadRopeArgs a) {
+    pdl_begin();
     constexpr int L2 = HD / 16;   // lanes per head
     constexpr int HPW = 32 / L2;  // heads side by side in one warp
     constexpr int CH = kNH * HPW; // heads per chunk item
@@ -474,6 +477,7 @@ __global__ void __launch_bounds__(128, kNH >= 9 ? 3 : 5) head_rope_pair_kernel(c
 // the first-half rotary lanes and read by both halves, so each slot is bracketed by __syncwarp.
 template <typename T, int HD, int kNH, int kP>
 __global__ void __launch_bounds__(128, 6) head_rope_async_kernel(const HeadRopeArgs a) {
+    pdl_begin();
     constexpr int L = HD / 8;
     constexpr int HPW = 32 / L;
     constexpr int CH = kNH * HPW;
@@ -589,9 +593,9 @@ static int launch_head_rope_direct(const HeadRopeArgs& a, int hd, int htot, cons
     const int ch = kNH * (256 / hd);
     const int64_t warp_items = a.T * ((htot + ch - 1) / ch);
     const int grid = persistent_grid(di, resident_ctas(kern, 128, 0), (warp_items + 3) / 4);
-    if (hd == 64) head_rope_direct_kernel<T, 64, kNH><<<grid, 128, 0, stream>>>(a);
-    else if (hd == 128) head_rope_direct_kernel<T, 128, kNH><<<grid, 128, 0, stream>>>(a);
-    else head_rope_direct_kernel<T, 256, kNH><<<grid, 128, 0, stream>>>(a);
+    if (hd == 64) launch_k(head_rope_direct_kernel<T, 64, kNH>, grid, 128, 0, stream, a);
+    else if (hd == 128) launch_k(head_rope_direct_kernel<T, 128, kNH>, grid, 128, 0, stream, a);
+    else launch_k(head_rope_direct_kernel<T, 256, kNH>, grid, 128, 0, stream, a);
     return launch_status();
 }
 
@@ -603,9 +607,9 @@ static int launch_head_rope_pair(const HeadRopeArgs& a, int hd, int htot, const 
     const int ch = kNH * (512 / hd);
     const int64_t warp_items = a.T * ((htot + ch - 1) / ch);
     const int grid = persistent_grid(di, resident_ctas(kern, 128, 0), (warp_items + 3) / 4);
-    if (hd == 64) head_rope_pair_kernel<T, 64, kNH><<<grid, 128, 0, stream>>>(a);
-    else if (hd == 128) head_rope_pair_kernel<T, 128, kNH><<<grid, 128, 0, stream>>>(a);
-    else head_rope_pair_kernel<T, 256, kNH><<<grid, 128, 0, stream>>>(a);
+    if (hd == 64) launch_k(head_rope_pair_kernel<T, 64, kNH>, grid, 128, 0, stream, a);
+    else if (hd == 128) launch_k(head_rope_pair_kernel<T, 128, kNH>, grid, 128, 0, stream, a);
+    else launch_k(head_rope_pair_kernel<T, 256, kNH>, grid, 128, 0, stream, a);
     return launch_status();
 }
 
@@ -668,9 +672,9 @@ static int launch_head_rope(const HeadSection& q, const HeadSection& k, const fl
         const int ch = kNH * (256 / hd);
         const int64_t warp_items = T_ * ((htot + ch - 1) / ch);
         const int grid = persistent_grid(di, resident_ctas(kern, 128, smem), (warp_items + 3) / 4);
-        if (hd == 64) head_rope_async_kernel<T, 64, kNH, kP><<<grid, 128, smem, stream>>>(a);
-        else if (hd == 128) head_rope_async_kernel<T, 128, kNH, kP><<<grid, 128, smem, stream>>>(a);
-        else head_rope_async_kernel<T, 256, kNH, kP><<<grid, 128, smem, stream>>>(a);
+        if (hd == 64) launch_k(head_rope_async_kernel<T, 64, kNH, kP>, grid, 128, smem, stream, a);
+        else if (hd == 128) launch_k(head_rope_async_kernel<T, 128, kNH, kP>, grid, 128, smem, stream, a);
+        else launch_k(head_rope_async_kernel<T, 256, kNH, kP>, grid, 128, smem, stream, a);
         return launch_status();
     }
     if (variant(kFamHeadRope) != WZYB_VARIANT_RING) {
@@ -715,7 +719,7 @@ static int launch_head_rope(const HeadSection& q, const HeadSection& k, const fl
     if (hd == HDV && vpt == V) {                                                   \
         rc = ensure_smem((const void*)head_rope_kernel<T, HDV, V>, smem);          \
         if (rc != WZYB_OK) return rc;                                              \
-        head_rope_kernel<T, HDV, V><<<grid, threads, smem, stream>>>(a);           \
+        launch_k(head_rope_kernel<T, HDV, V>, grid, threads, smem, stream, a);           \
         return launch_status();                                                    \
     }
     WZYB_HR_CASE(64, 1)
@@ -732,6 +736,7 @@ static int launch_head_rope(const HeadSection& q, const HeadSection& k, const fl
 // RoPE cos/sin table on the device: one thread per (pos, i), fp64 pow and sincos, rounded to fp32.
 // ---------------------------------------------------------------------------------------------
 __global__ void rope_table_kernel(float* cos_tab, float* sin_tab, int64_t rows, int half, double theta, int rot) {
+    pdl_begin();
     const int64_t n = rows * half;
     for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < n;
          idx += (int64_t)gridDim.x * blockDim.x) {
@@ -807,7 +812,7 @@ int wzyb_rope_table_f32(float* d_cos, float* d_sin, int64_t rows, int rot_dims, 
     const int64_t n = rows * half;
     int64_t blocks = (n + 255) / 256;
     if (blocks > (int64_t)di.sms * 16) blocks = (int64_t)di.sms * 16;
-    wzyb::rope_table_kernel<<<(int)blocks, 256, 0, (cudaStream_t)stream>>>(d_cos, d_sin, rows, half, theta, rot_dims);
+    wzyb::launch_k(wzyb::rope_table_kernel, (int)blocks, 256, 0, (cudaStream_t)stream, d_cos, d_sin, rows, half, theta, rot_dims);
     return wzyb::launch_status();
 }
 

@@ -97,6 +97,7 @@ __device__ __forceinline__ void kv_q8_store(const float2 (&x)[4], bool act, int 
 // once. The cos/sin slice is loaded behind the head vectors.
 template <typename T, int HD, int kR>
 __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
+    pdl_begin();
     constexpr int L = HD / 8;
     constexpr int HPW = 32 / L;
     const int lane = threadIdx.x & 31;
@@ -232,8 +233,8 @@ static int launch_kv_append(const KvAppendArgs& a0, int head_dim, cudaStream_t s
     const int64_t items = split ? a.T * rounds : a.T * ((rounds + 1) / 2);
     const int grid = persistent_grid(di, 8, (items + 7) / 8);
 #define WZYB_KV(HDV)                                                                              \
-    if (split) kv_append_kernel<T, HDV, 1><<<grid, 256, 0, stream>>>(a);                          \
-    else kv_append_kernel<T, HDV, 2><<<grid, 256, 0, stream>>>(a);
+    if (split) launch_k(kv_append_kernel<T, HDV, 1>, grid, 256, 0, stream, a);                          \
+    else launch_k(kv_append_kernel<T, HDV, 2>, grid, 256, 0, stream, a);
     switch (head_dim) {
         case 64: { WZYB_KV(64) break; }
         case 128: { WZYB_KV(128) break; }

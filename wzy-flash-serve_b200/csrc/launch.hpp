@@ -53,6 +53,26 @@ constexpr int kSmemPerSm = 200 * 1024;
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Kernel launch with programmatic stream serialization (PDL; see pdl_begin in common.cuh), through
+// cudaLaunchKernelEx. WZYB_PDL=0 in the environment launches without the attribute (plain stream
+// order, for A/B measurement). Errors are left for launch_status() (cudaGetLastError).
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                     Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    (void)cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 inline int launch_status() {
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? WZYB_OK : static_cast<int>(e);

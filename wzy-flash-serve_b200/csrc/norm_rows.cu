@@ -35,6 +35,7 @@ struct NormRowsArgs {
 
 template <typename TI, typename TO, int VPT>
 __global__ void __launch_bounds__(512) norm_rows_kernel(const NormRowsArgs a) {
+    pdl_begin();
     extern __shared__ __align__(128) unsigned char smem[];
     const int S = a.stages;
     const int64_t G = gridDim.x;
@@ -155,6 +156,7 @@ __global__ void __launch_bounds__(512) norm_rows_kernel(const NormRowsArgs a) {
 // fp32, which keeps a row of 2048 at ~100 registers. No shared memory, no CTA barrier.
 template <typename TI, typename TO, int VPL>
 __global__ void __launch_bounds__(256, 2) norm_rows_direct_kernel(const NormRowsArgs a) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -226,6 +228,7 @@ __global__ void __launch_bounds__(256, 2) norm_rows_direct_kernel(const NormRows
 // flight at once (kP = 1); kP = 2 double-buffers rows for long streams.
 template <typename TI, typename TO, int VPL, int kP>
 __global__ void __launch_bounds__(128) norm_rows_async_kernel(const NormRowsArgs a) {
+    pdl_begin();
     constexpr int C = Vec8<TI>::kChunks;
     constexpr int SLOT = 2 * VPL * C * 32;  // uint4: residual vectors, then x vectors
     extern __shared__ __align__(16) uint4 sm_nr[];
@@ -321,6 +324,7 @@ __global__ void __launch_bounds__(128) norm_rows_async_kernel(const NormRowsArgs
 // over a persistent grid; several CTAs per SM keep rows in flight across the barriers.
 template <typename TI, typename TO, int VPL, int QF>
 __global__ void __launch_bounds__(512) norm_rows_wide_kernel(const NormRowsArgs a) {
+    pdl_begin();
     __shared__ float part[2][16];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -422,6 +426,7 @@ __global__ void __launch_bounds__(512) norm_rows_wide_kernel(const NormRowsArgs 
 // 64 and a 32-60 byte spill (3 CTAs: 82 -> 83.5 %, where the 72 cap gives 79 %).
 template <typename TI, typename TO, int VPL, int QF>
 __global__ void __maxnreg__(VPL == 1 ? (QF == kQfNone ? 72 : 64) : 128) norm_rows_token4_kernel(const NormRowsArgs a) {
+    pdl_begin();
     constexpr int HC = 4;
     __shared__ float part[2][HC][16];
     const int lane = threadIdx.x & 31;
@@ -516,8 +521,8 @@ static int launch_norm_rows_token4(const NormRowsArgs& a, int nw, int vpl, const
     const void* kern = vpl == 1 ? (const void*)norm_rows_token4_kernel<TI, TO, 1, QF>
                                 : (const void*)norm_rows_token4_kernel<TI, TO, 2, QF>;
     const int grid = persistent_grid(di, resident_ctas(kern, threads, 0), a.units / 4);
-    if (vpl == 1) norm_rows_token4_kernel<TI, TO, 1, QF><<<grid, threads, 0, stream>>>(a);
-    else norm_rows_token4_kernel<TI, TO, 2, QF><<<grid, threads, 0, stream>>>(a);
+    if (vpl == 1) launch_k(norm_rows_token4_kernel<TI, TO, 1, QF>, grid, threads, 0, stream, a);
+    else launch_k(norm_rows_token4_kernel<TI, TO, 2, QF>, grid, threads, 0, stream, a);
     return launch_status();
 }
 
@@ -557,7 +562,7 @@ static int launch_norm_rows_wide(const NormRowsArgs& a, const DeviceInfo& di, cu
     if (kern == nullptr) return WZYB_ERR_SHAPE;
     const int grid = persistent_grid(di, resident_ctas(kern, threads, 0), a.units);
 #define WZYB_NRW(V) \
-    if (vpl == V) norm_rows_wide_kernel<TI, TO, V, QF><<<grid, threads, 0, stream>>>(a);
+    if (vpl == V) launch_k(norm_rows_wide_kernel<TI, TO, V, QF>, grid, threads, 0, stream, a);
     WZYB_NRW(1) WZYB_NRW(2) WZYB_NRW(3) WZYB_NRW(4)
     if constexpr (sizeof(TI) == 2) { WZYB_NRW(6) WZYB_NRW(8) }
 #undef WZYB_NRW
@@ -619,7 +624,7 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
         if (rc != WZYB_OK) return rc;
         const int grid = persistent_grid(di, resident_ctas(kern, 128, smem), (a.units + 3) / 4);
 #define WZYB_NRA(V, P) \
-    if (vpl == V && kp == P) norm_rows_async_kernel<TI, TO, V, P><<<grid, 128, smem, stream>>>(a);
+    if (vpl == V && kp == P) launch_k(norm_rows_async_kernel<TI, TO, V, P>, grid, 128, smem, stream, a);
         WZYB_NRA(1, 1) WZYB_NRA(1, 2) WZYB_NRA(2, 1) WZYB_NRA(2, 2)
         WZYB_NRA(4, 1) WZYB_NRA(4, 2) WZYB_NRA(8, 1) WZYB_NRA(8, 2)
 #undef WZYB_NRA
@@ -645,16 +650,16 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
 #undef WZYB_NR_PICK
         const int grid = persistent_grid(di, resident_ctas(kern, 256, 0), (a.units + 7) / 8);
         switch (vpl) {
-            case 1: norm_rows_direct_kernel<TI, TO, 1><<<grid, 256, 0, stream>>>(a); break;
-            case 2: norm_rows_direct_kernel<TI, TO, 2><<<grid, 256, 0, stream>>>(a); break;
-            case 4: norm_rows_direct_kernel<TI, TO, 4><<<grid, 256, 0, stream>>>(a); break;
+            case 1: launch_k(norm_rows_direct_kernel<TI, TO, 1>, grid, 256, 0, stream, a); break;
+            case 2: launch_k(norm_rows_direct_kernel<TI, TO, 2>, grid, 256, 0, stream, a); break;
+            case 4: launch_k(norm_rows_direct_kernel<TI, TO, 4>, grid, 256, 0, stream, a); break;
             default:
                 // 6-12 vectors per lane only for fp16 rows (fp32 rows that long take the wide design)
                 if constexpr (sizeof(TI) == 2) {
-                    if (vpl == 6) norm_rows_direct_kernel<TI, TO, 6><<<grid, 256, 0, stream>>>(a);
-                    else if (vpl == 8) norm_rows_direct_kernel<TI, TO, 8><<<grid, 256, 0, stream>>>(a);
-                    else if (vpl == 10) norm_rows_direct_kernel<TI, TO, 10><<<grid, 256, 0, stream>>>(a);
-                    else norm_rows_direct_kernel<TI, TO, 12><<<grid, 256, 0, stream>>>(a);
+                    if (vpl == 6) launch_k(norm_rows_direct_kernel<TI, TO, 6>, grid, 256, 0, stream, a);
+                    else if (vpl == 8) launch_k(norm_rows_direct_kernel<TI, TO, 8>, grid, 256, 0, stream, a);
+                    else if (vpl == 10) launch_k(norm_rows_direct_kernel<TI, TO, 10>, grid, 256, 0, stream, a);
+                    else launch_k(norm_rows_direct_kernel<TI, TO, 12>, grid, 256, 0, stream, a);
                 }
                 break;
         }
@@ -682,9 +687,9 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
     rc = ensure_smem(kern, smem);
     if (rc != WZYB_OK) return rc;
     switch (vpt) {
-        case 1: norm_rows_kernel<TI, TO, 1><<<grid, threads, smem, stream>>>(a); break;
-        case 2: norm_rows_kernel<TI, TO, 2><<<grid, threads, smem, stream>>>(a); break;
-        default: norm_rows_kernel<TI, TO, 4><<<grid, threads, smem, stream>>>(a); break;
+        case 1: launch_k(norm_rows_kernel<TI, TO, 1>, grid, threads, smem, stream, a); break;
+        case 2: launch_k(norm_rows_kernel<TI, TO, 2>, grid, threads, smem, stream, a); break;
+        default: launch_k(norm_rows_kernel<TI, TO, 4>, grid, threads, smem, stream, a); break;
     }
     return launch_status();
 }

@@ -76,6 +76,7 @@ __device__ __forceinline__ float4 fp8x4_decode(uint32_t w, float scale) {
 // One warp per token: lanes 0..15 hash one head each; the token's rows are then read in 4-byte
 // quads spread over the lanes (each quad fetches its row index from the hashing lane).
 __global__ void __launch_bounds__(256) ple_fp8_gather_kernel(const PleFp8Args a) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const int qpr = a.row_bytes / 4;  // 4-byte quads per row
@@ -115,6 +116,7 @@ template <int VPL>
 __global__ void __launch_bounds__(512) ple_gate_kernel(const float* __restrict__ key, const float* __restrict__ query,
                                                        const float* __restrict__ value, float* __restrict__ gv,
                                                        int64_t units, int n, int hc) {
+    pdl_begin();
     __shared__ float part[2][16];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int span = blockDim.x * 8;
@@ -193,6 +195,7 @@ __global__ void __launch_bounds__(256) ple_conv_kernel(const float* __restrict__
                                                        const float* __restrict__ hist, const float* __restrict__ gv,
                                                        float* __restrict__ R, int64_t T, int hcd,
                                                        float* __restrict__ snaps) {
+    pdl_begin();
     const int c4n = hcd / 4;
     const int64_t items = T * c4n;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -252,6 +255,7 @@ __global__ void __launch_bounds__(256) ple_conv_strided_kernel(const float* __re
                                                                const float* __restrict__ hist,
                                                                const float* __restrict__ gv, float* __restrict__ R,
                                                                int64_t T, int hcd) {
+    pdl_begin();
     const int c4n = hcd / 4;
     const int64_t groups = ((T + 3 * K - 1) / (3 * K)) * 3;
     const int64_t items = groups * c4n;
@@ -299,6 +303,7 @@ __global__ void __launch_bounds__(256) ple_conv_strided_kernel(const float* __re
 // (read in full before any write by the same thread).
 __global__ void __launch_bounds__(256) ple_conv_hist_kernel(const float* __restrict__ norm, float* __restrict__ hist,
                                                             int64_t T, int hcd) {
+    pdl_begin();
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= hcd) return;
     float nh[kConvHist];
@@ -367,7 +372,7 @@ int wzyb_ple_gather_fp8_f32(const uint8_t* table, int64_t table_rows, int row_by
     a.eos = eos_id;
     a.out = out;
     const int grid = wzyb::persistent_grid(di, 8, (T + 7) / 8);
-    wzyb::ple_fp8_gather_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(a);
+    wzyb::launch_k(wzyb::ple_fp8_gather_kernel, grid, 256, 0, (cudaStream_t)stream, a);
     return wzyb::launch_status();
 }
 
@@ -397,10 +402,10 @@ int wzyb_ple_gate_f32(const float* key, const float* query, const float* value, 
                                  : (const void*)wzyb::ple_gate_kernel<4>;
     const int grid = wzyb::persistent_grid(di, wzyb::resident_ctas(kern, threads, 0), units);
     switch (need) {
-        case 1: wzyb::ple_gate_kernel<1><<<grid, threads, 0, s>>>(key, query, value, gv, units, n_embd, hc); break;
-        case 2: wzyb::ple_gate_kernel<2><<<grid, threads, 0, s>>>(key, query, value, gv, units, n_embd, hc); break;
-        case 3: wzyb::ple_gate_kernel<3><<<grid, threads, 0, s>>>(key, query, value, gv, units, n_embd, hc); break;
-        default: wzyb::ple_gate_kernel<4><<<grid, threads, 0, s>>>(key, query, value, gv, units, n_embd, hc); break;
+        case 1: wzyb::launch_k(wzyb::ple_gate_kernel<1>, grid, threads, 0, s, key, query, value, gv, units, n_embd, hc); break;
+        case 2: wzyb::launch_k(wzyb::ple_gate_kernel<2>, grid, threads, 0, s, key, query, value, gv, units, n_embd, hc); break;
+        case 3: wzyb::launch_k(wzyb::ple_gate_kernel<3>, grid, threads, 0, s, key, query, value, gv, units, n_embd, hc); break;
+        default: wzyb::launch_k(wzyb::ple_gate_kernel<4>, grid, threads, 0, s, key, query, value, gv, units, n_embd, hc); break;
     }
     return wzyb::launch_status();
 }
@@ -420,7 +425,7 @@ int wzyb_ple_conv_f32(const float* norm, const float* cw, float* hist, const flo
     if (hist_snaps) {
         const int64_t items = T * (hcd / 4);
         const int grid = wzyb::persistent_grid(di, 8, (items + 255) / 256);
-        wzyb::ple_conv_kernel<true><<<grid, 256, 0, st>>>(norm, cw, hist, gv, R, T, hcd, hist_snaps);
+        wzyb::launch_k(wzyb::ple_conv_kernel<true>, grid, 256, 0, st, norm, cw, hist, gv, R, T, hcd, hist_snaps);
     } else {
         // 4 tokens per thread: 150 -> 108 us at 4096 tokens x 10240 channels (68 -> 95 % of HBM peak;
         // 2 tokens: 109 us, 3: 115 us)
@@ -428,9 +433,9 @@ int wzyb_ple_conv_f32(const float* norm, const float* cw, float* hist, const flo
         const int64_t items = ((T + 3 * kK - 1) / (3 * kK)) * 3 * (hcd / 4);
         const void* kern = (const void*)wzyb::ple_conv_strided_kernel<kK>;
         const int grid = wzyb::persistent_grid(di, wzyb::resident_ctas(kern, 256, 0), (items + 255) / 256);
-        wzyb::ple_conv_strided_kernel<kK><<<grid, 256, 0, st>>>(norm, cw, hist, gv, R, T, hcd);
+        wzyb::launch_k(wzyb::ple_conv_strided_kernel<kK>, grid, 256, 0, st, norm, cw, hist, gv, R, T, hcd);
     }
-    wzyb::ple_conv_hist_kernel<<<(hcd + 255) / 256, 256, 0, st>>>(norm, hist, T, hcd);
+    wzyb::launch_k(wzyb::ple_conv_hist_kernel, (hcd + 255) / 256, 256, 0, st, norm, hist, T, hcd);
     return wzyb::launch_status();
 }
 

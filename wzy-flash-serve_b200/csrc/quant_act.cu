@@ -17,6 +17,7 @@ namespace wzyb {
 __global__ void __launch_bounds__(256) quant_act_kernel(const float* __restrict__ x, signed char* __restrict__ q32,
                                                         float* __restrict__ s32, signed char* __restrict__ q16,
                                                         float* __restrict__ s16, int64_t nvec) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; base < nvec;
@@ -37,6 +38,7 @@ __global__ void __launch_bounds__(256) quant_act_kernel(const float* __restrict_
 template <int QF>
 __global__ void __launch_bounds__(256) quant_act_block_kernel(const float* __restrict__ x, void* __restrict__ q,
                                                               void* __restrict__ s, float gs, int64_t nvec) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; base < nvec;
@@ -62,7 +64,7 @@ static int launch_quant_act_block(const float* x, void* q, void* s, float gs, in
     if (rc != WZYB_OK) return rc;
     const int64_t nvec = T * cols / 8;
     const int grid = persistent_grid(di, 8, (nvec + 255) / 256);
-    quant_act_block_kernel<QF><<<grid, 256, 0, (cudaStream_t)stream>>>(x, q, s, gs, nvec);
+    launch_k(quant_act_block_kernel<QF>, grid, 256, 0, (cudaStream_t)stream, x, q, s, gs, nvec);
     return launch_status();
 }
 
@@ -83,7 +85,7 @@ int wzyb_quant_act_f32(const float* x, int8_t* q32, float* s32, int8_t* q16, flo
     if (rc != WZYB_OK) return rc;
     const int64_t nvec = T * cols / 8;
     const int grid = wzyb::persistent_grid(di, 8, (nvec + 255) / 256);
-    wzyb::quant_act_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, (signed char*)q32, s32, (signed char*)q16, s16,
+    wzyb::launch_k(wzyb::quant_act_kernel, grid, 256, 0, (cudaStream_t)stream, x, (signed char*)q32, s32, (signed char*)q16, s16,
                                                                     nvec);
     return wzyb::launch_status();
 }

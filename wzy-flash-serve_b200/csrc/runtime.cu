@@ -6,6 +6,8 @@
 #include <tuple>
 #include <utility>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "launch.hpp"
 
@@ -81,6 +83,14 @@ int ensure_smem(const void* kernel, int bytes) {
     (void)bytes;
     g_smem_done.insert(key);
     return WZYB_OK;
+}
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("WZYB_PDL");
+        return !(e != nullptr && e[0] == '0');
+    }();
+    return on;
 }
 
 Tuning tuning(int family) {

@@ -60,6 +60,7 @@ template <typename TI, typename TO, bool INTERLEAVED, bool PACKED>
 __global__ void __launch_bounds__(kSwigluThreads) swiglu_kernel(const TI* __restrict__ gate, const TI* __restrict__ up,
                                                                  TO* __restrict__ out, int64_t nvec, int64_t vpr,
                                                                  int64_t nff) {
+    pdl_begin();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     for (; v + (kUnroll - 1) * stride < nvec; v += kUnroll * stride) {
@@ -95,6 +96,7 @@ template <typename TI, int QF>
 __global__ void __launch_bounds__(256) swiglu_quant_kernel(const TI* __restrict__ gate, const TI* __restrict__ up,
                                                            void* __restrict__ q, void* __restrict__ s, float gs,
                                                            int64_t nvec) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; base < nvec;
@@ -128,9 +130,9 @@ static int launch_swiglu(const TI* gate, const TI* up, TO* out, int64_t nvec, in
     const int grid = persistent_grid(di, tu.ctas_per_sm, (nvec + kSwigluThreads - 1) / kSwigluThreads);
     const bool scalar = tu.stages == 1 || (tu.stages != 2 && nvec >= (int64_t(1) << 25));
     if (scalar)
-        swiglu_kernel<TI, TO, INTERLEAVED, false><<<grid, kSwigluThreads, 0, stream>>>(gate, up, out, nvec, vpr, nff);
+        launch_k(swiglu_kernel<TI, TO, INTERLEAVED, false>, grid, kSwigluThreads, 0, stream, gate, up, out, nvec, vpr, nff);
     else
-        swiglu_kernel<TI, TO, INTERLEAVED, true><<<grid, kSwigluThreads, 0, stream>>>(gate, up, out, nvec, vpr, nff);
+        launch_k(swiglu_kernel<TI, TO, INTERLEAVED, true>, grid, kSwigluThreads, 0, stream, gate, up, out, nvec, vpr, nff);
     return launch_status();
 }
 
@@ -147,7 +149,7 @@ static int launch_swiglu_quant(const float* gate, const float* up, void* q, void
     if (rc != WZYB_OK) return rc;
     const int64_t nvec = n / 8;
     const int grid = persistent_grid(di, 8, (nvec + 255) / 256);
-    swiglu_quant_kernel<float, QF><<<grid, 256, 0, (cudaStream_t)stream>>>(gate, up, q, s, gs, nvec);
+    launch_k(swiglu_quant_kernel<float, QF>, grid, 256, 0, (cudaStream_t)stream, gate, up, q, s, gs, nvec);
     return launch_status();
 }
 

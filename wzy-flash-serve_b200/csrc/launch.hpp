@@ -55,8 +55,12 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 // Kernel launch with programmatic stream serialization (PDL; see pdl_begin in common.cuh), through
 // cudaLaunchKernelEx. WZYB_PDL=0 in the environment launches without the attribute (plain stream
-// order, for A/B measurement). Errors are left for launch_status() (cudaGetLastError).
+// order, for A/B measurement). A failed launch is kept for launch_status() in this thread.
 bool pdl_enabled();
+inline cudaError_t& launch_error_slot() {
+    static thread_local cudaError_t e = cudaSuccess;
+    return e;
+}
 template <typename... KArgs, typename... Args>
 inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                      Args&&... args) {
@@ -70,11 +74,16 @@ inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
     attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    (void)cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+    if (e != cudaSuccess && launch_error_slot() == cudaSuccess) launch_error_slot() = e;
 }
 
 inline int launch_status() {
-    const cudaError_t e = cudaGetLastError();
+    cudaError_t e = cudaGetLastError();
+    if (launch_error_slot() != cudaSuccess) {
+        if (e == cudaSuccess) e = launch_error_slot();
+        launch_error_slot() = cudaSuccess;
+    }
     return e == cudaSuccess ? WZYB_OK : static_cast<int>(e);
 }
 

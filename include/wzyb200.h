@@ -257,6 +257,28 @@ int wzyb_quant_act_f32(const float* x, int8_t* q32, float* s32, int8_t* q16, flo
 int wzyb_quant_act_mxfp8_f32(const float* x, uint8_t* q, uint8_t* s, int64_t T, int cols, wzyb_stream_t stream);
 int wzyb_quant_act_nvfp4_f32(const float* x, uint8_t* q, uint8_t* s, float global_scale, int64_t T, int cols,
                              wzyb_stream_t stream);
+/* Either format with a choice of scale-factor layout, for a GEMM that takes the codes as its A (or B)
+ * operand [rows, cols] (rows = T here, T * hc for the norm):
+ *  format     WZYB_BLOCK_MXFP8 (global_scale unused) or WZYB_BLOCK_NVFP4;
+ *  sf_layout  WZYB_SF_ROW_MAJOR: s [rows, cols/G] bytes (G = 32 MXFP8, 16 NVFP4), as the entry points
+ *               above;
+ *             WZYB_SF_TILED_128X4: the scale layout of sm_100's block-scaled MMA operands (what a
+ *               tcgen05 GEMM copies to tensor memory, and cuBLASLt's block-scaled GEMMs read): the
+ *               [rows, cols/G] scale matrix in tiles of 128 rows x 4 scale columns, 512 bytes each;
+ *               the ceil(cols/G/4) tiles of one 128-row band are consecutive, and inside a tile
+ *               scale (r, c) sits at byte (r % 32) * 16 + (r / 32) * 4 + c. s must hold
+ *               ceil(rows/128) * 128 * ceil(cols/G/4) * 4 bytes; bytes of padding rows and columns are
+ *               not written.
+ * Codes are row-major [rows, cols] in both cases. */
+#define WZYB_BLOCK_MXFP8 0
+#define WZYB_BLOCK_NVFP4 1
+#define WZYB_SF_ROW_MAJOR 0
+#define WZYB_SF_TILED_128X4 1
+int wzyb_quant_act_block_f32(const float* x, uint8_t* q, uint8_t* s, int format, int sf_layout, float global_scale,
+                             int64_t T, int cols, wzyb_stream_t stream);
+int wzyb_gr_norm_block_f32(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, float* xn,
+                           uint8_t* xq, uint8_t* xs, int format, int sf_layout, float global_scale, int64_t T,
+                           int n_embd, int hc, float eps, wzyb_stream_t stream);
 /* SwiGLU (the reference's expression) straight to the block formats; n % 32 == 0. */
 int wzyb_swiglu_mxfp8_f32(const float* gate, const float* up, uint8_t* q, uint8_t* s, int64_t n,
                           wzyb_stream_t stream);

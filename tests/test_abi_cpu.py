@@ -81,6 +81,16 @@ def test_argument_validation_before_any_cuda_call(wz):
     # block-scaled formats: group sizes 32 (MXFP8) / 16 (NVFP4)
     assert L.wzyb_quant_act_mxfp8_f32(A16, NULL, A16, 4, 2560, NULL) == wz.ERR_NULL
     assert L.wzyb_quant_act_mxfp8_f32(A16, A16, A16, 4, 2576, NULL) == wz.ERR_SHAPE
+    # the general block quantisers: format and scale layout are checked before anything is enqueued
+    assert L.wzyb_quant_act_block_f32(A16, A16, A16, 7, wz.SF_ROW_MAJOR, 1.0, 4, 2560, NULL) == wz.ERR_VALUE
+    assert L.wzyb_quant_act_block_f32(A16, A16, A16, wz.BLOCK_MXFP8, 5, 1.0, 4, 2560, NULL) == wz.ERR_VALUE
+    assert L.wzyb_quant_act_block_f32(A16, NULL, A16, wz.BLOCK_NVFP4, wz.SF_TILED_128X4, 1.0, 4, 2560, NULL) == wz.ERR_NULL
+    assert L.wzyb_gr_norm_block_f32(A16, A16, A16, A16, A16, A16, A16, 3, wz.SF_ROW_MAJOR, 1.0, 4, 2560, 4, 1e-6,
+                                    NULL) == wz.ERR_VALUE
+    assert L.wzyb_gr_norm_block_f32(A16, A16, A16, A16, A16, A16, A16, wz.BLOCK_MXFP8, 9, 1.0, 4, 2560, 4, 1e-6,
+                                    NULL) == wz.ERR_VALUE
+    assert L.wzyb_gr_norm_block_f32(A16, A16, A16, A16, A16, NULL, A16, wz.BLOCK_NVFP4, wz.SF_TILED_128X4, 1.0, 4,
+                                    2560, 4, 1e-6, NULL) == wz.ERR_NULL
     assert L.wzyb_quant_act_nvfp4_f32(A16, A16, A16, 1.0, 4, 2568, NULL) == wz.ERR_SHAPE
     assert L.wzyb_quant_act_nvfp4_f32(A8, A16, A16, 1.0, 4, 2560, NULL) == wz.ERR_ALIGN
     assert L.wzyb_swiglu_mxfp8_f32(A16, A16, A16, A16, 48, NULL) == wz.ERR_SHAPE

@@ -688,6 +688,92 @@ def test_gr_norm_block_formats(wz, orc, fmt, T):
     assert np.array_equal(host(q), want_q) and np.array_equal(host(s), want_s)
 
 
+def _to_blocked(sc, pad=0xAB):
+    """Row-major [rows, scols] scale bytes -> the tiled 128x4 layout, built by reshapes: 128 x 4 tiles,
+    the tiles of a 128-row band consecutive, and within a tile the (r // 32, r % 32, c) order swapped to
+    (r % 32, r // 32, c). Padding rows / columns hold `pad`."""
+    rows, scols = sc.shape
+    rb, cb = -(-rows // 128), -(-scols // 4)
+    p = np.full((rb * 128, cb * 4), pad, dtype=np.uint8)
+    p[:rows, :scols] = sc
+    t = p.reshape(rb, 128, cb, 4).transpose(0, 2, 1, 3)  # (band, tile, r, c)
+    t = t.reshape(rb, cb, 4, 32, 4).transpose(0, 1, 3, 2, 4)  # (band, tile, r % 32, r // 32, c)
+    return np.ascontiguousarray(t).reshape(-1)
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8", "nvfp4"])
+@pytest.mark.parametrize("T,cols", [(200, 96), (129, 2560), (8, 32)])
+def test_block_scales_tiled_layout(wz, fmt, T, cols):
+    """The tiled scale layout holds exactly the row-major scales, relaid by reshapes; codes are the
+    same; padding bytes are not written."""
+    x = _block_inputs(rng(T * 7 + cols), T, cols)
+    q0, s0 = _dev_block_out(T * cols, fmt)
+    wz.quant_act_block(dev(x), q0, s0, T, cols, fmt=fmt, global_scale=2.0)
+    q1 = torch.empty_like(q0)
+    s1 = torch.full((wz.sf_tiled_bytes(T, cols, fmt),), 0xAB, dtype=torch.uint8, device=DEV)
+    wz.quant_act_block(dev(x), q1, s1, T, cols, fmt=fmt, global_scale=2.0, sf_layout=wz.SF_TILED_128X4)
+    g = 32 if fmt == "mxfp8" else 16
+    assert np.array_equal(host(q1), host(q0))
+    assert np.array_equal(host(s1), _to_blocked(host(s0).reshape(T, cols // g)))
+
+
+@pytest.mark.parametrize("T", [9, 700])
+def test_gr_norm_block_tiled_layout(wz, T):
+    r = rng(63)
+    n, hc = 2560, 4
+    R = r.standard_normal((T * hc, n)).astype(np.float32)
+    bo = r.standard_normal((T, n)).astype(np.float32)
+    inj = r.standard_normal(T * hc).astype(np.float32)
+    w = (1 + 0.02 * r.standard_normal((hc, n))).astype(np.float32)
+    for fmt in ("mxfp8", "nvfp4"):
+        outs = []
+        for layout in (None, wz.SF_TILED_128X4):
+            dxn = torch.empty((T * hc, n), dtype=torch.float32, device=DEV)
+            q, s = _dev_block_out(T * hc * n, fmt)
+            if layout is not None:
+                s = torch.full((wz.sf_tiled_bytes(T * hc, n, fmt),), 0xAB, dtype=torch.uint8, device=DEV)
+            wz.gr_norm_block(dev(R), dev(w), dev(bo), dev(inj), dxn, q, s, T, n, hc, fmt=fmt, global_scale=3.0,
+                             sf_layout=layout)
+            outs.append((host(dxn), host(q), host(s)))
+        g = 32 if fmt == "mxfp8" else 16
+        assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
+        assert np.array_equal(outs[1][2], _to_blocked(outs[0][2].reshape(T * hc, n // g)))
+
+
+def test_mxfp8_tiled_scales_feed_a_block_scaled_gemm(wz):
+    """End to end: A [M, K] and B [N, K] quantised to MXFP8 with tiled scales go straight into the block-
+    scaled tensor-core GEMM of this torch build (torch._scaled_mm, cuBLASLt); the product matches the
+    fp32 product of the dequantised operands."""
+    if not hasattr(torch, "float8_e8m0fnu"):
+        pytest.skip("torch has no float8_e8m0fnu")
+    M, N, K = 256, 384, 512
+    r = rng(64)
+    a = (r.standard_normal((M, K)) * np.exp(r.uniform(-3, 3, (M, 1)))).astype(np.float32)
+    b = r.standard_normal((N, K)).astype(np.float32)
+    qa, qb = torch.empty(M * K, dtype=torch.uint8, device=DEV), torch.empty(N * K, dtype=torch.uint8, device=DEV)
+    sa = torch.empty(wz.sf_tiled_bytes(M, K), dtype=torch.uint8, device=DEV)
+    sb = torch.empty(wz.sf_tiled_bytes(N, K), dtype=torch.uint8, device=DEV)
+    wz.quant_act_block(dev(a), qa, sa, M, K, sf_layout=wz.SF_TILED_128X4)
+    wz.quant_act_block(dev(b), qb, sb, N, K, sf_layout=wz.SF_TILED_128X4)
+    A = qa.view(torch.float8_e4m3fn).view(M, K)
+    B = qb.view(torch.float8_e4m3fn).view(N, K)
+    try:
+        out = torch._scaled_mm(A, B.t(), scale_a=sa.view(torch.float8_e8m0fnu), scale_b=sb.view(torch.float8_e8m0fnu),
+                               out_dtype=torch.bfloat16)
+    except (RuntimeError, TypeError, ValueError) as e:
+        pytest.skip(f"no MXFP8 block-scaled GEMM in this torch build: {str(e)[:120]}")
+    # dequantise from the row-major scales of the same data
+    ra, rs = torch.empty_like(qa), torch.empty(M * K // 32, dtype=torch.uint8, device=DEV)
+    rb_, rbs = torch.empty_like(qb), torch.empty(N * K // 32, dtype=torch.uint8, device=DEV)
+    wz.quant_act_block(dev(a), ra, rs, M, K)
+    wz.quant_act_block(dev(b), rb_, rbs, N, K)
+    da = A.float() * torch.exp2(rs.float() - 127).view(M, K // 32).repeat_interleave(32, dim=1)
+    db = B.float() * torch.exp2(rbs.float() - 127).view(N, K // 32).repeat_interleave(32, dim=1)
+    want = da.double() @ db.double().t()
+    err = (out.double() - want).abs().max().item() / want.abs().max().item()
+    assert err < 1e-2, f"block-scaled GEMM vs dequantised product: {err}"
+
+
 @pytest.mark.parametrize("fmt", ["mxfp8", "nvfp4"])
 def test_swiglu_block_formats(wz, orc, fmt):
     r = rng(62)

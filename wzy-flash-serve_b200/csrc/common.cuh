@@ -594,6 +594,28 @@ __device__ __forceinline__ void quant_group_store(const float (&v)[8], bool acti
     }
 }
 
+// Scale-factor layouts of the block formats. Row-major: scale (row, c) at row * scols + c, i.e. the flat
+// element order. Tiled 128x4: the layout of sm_100's block-scaled MMA operands -- the [rows, scols]
+// scale matrix cut into tiles of 128 rows x 4 scale columns, 512 bytes each, the tiles of one 128-row
+// band consecutive along the scale columns (ncb = ceil(scols / 4) tiles per band), and inside a tile
+// scale (r, c) at (r % 32) * 16 + (r / 32) * 4 + c.
+enum ScaleLayout : int { kSfRowMajor = 0, kSfTiled128x4 = 1 };
+__host__ __device__ __forceinline__ int64_t sf_tiled_offset(int64_t row, int scol, int ncb) {
+    return ((row >> 7) * ncb + (scol >> 2)) * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4 + (scol & 3);
+}
+
+// The MXFP8 / NVFP4 store of quant_group_store with the group's scale byte at an explicit address
+// (the group's first lane writes it), for the tiled layout.
+template <int QF>
+__device__ __forceinline__ void block_group_store_at(const float (&v)[8], bool active, void* q, uint8_t* s_at,
+                                                     float gs, int64_t vi, int lane) {
+    if (QF == kQfMxfp8) {
+        mxfp8_group_store(v, active, static_cast<uint8_t*>(q) + vi * 8, s_at, lane);
+    } else if (QF == kQfNvfp4) {
+        nvfp4_group_store(v, active, gs, static_cast<uint8_t*>(q) + vi * 4, s_at, lane);
+    }
+}
+
 // Sum over aligned groups of `kLanes` lanes (kLanes a power of two <= 32) with xor shuffles.
 template <int kLanes>
 __device__ __forceinline__ float group_sum(float v) {

@@ -31,7 +31,26 @@ struct NormRowsArgs {
     void* sout;  // and its group scales
     float gs;    // NVFP4 per-tensor scale
     int lookahead;  // wide design with a quantised output: prefetch the CTA's next row into L2 (0/1)
+    int sf_layout;  // block formats: kSfRowMajor or kSfTiled128x4 scale bytes
+    int sf_ncb;     // tiled layout: 4-column scale tiles per 128-row band
 };
+
+// The quantised output of row u's 8 elements at e (every lane calls it; `e < n` lanes store).
+template <int QF>
+__device__ __forceinline__ void norm_quant_store(const NormRowsArgs& a, const float (&yo)[8], int64_t u, int e,
+                                                 int lane) {
+    const int n = a.n;
+    if constexpr (QF == kQfMxfp8 || QF == kQfNvfp4) {
+        if (a.sf_layout == kSfTiled128x4) {
+            constexpr int kG = QF == kQfNvfp4 ? 16 : 32;
+            block_group_store_at<QF>(yo, e < n, a.qout,
+                                     static_cast<uint8_t*>(a.sout) + sf_tiled_offset(u, e / kG, a.sf_ncb), a.gs,
+                                     (u * n + e) >> 3, lane);
+            return;
+        }
+    }
+    quant_group_store<QF>(yo, e < n, a.qout, a.sout, a.gs, (u * n + e) >> 3, lane);
+}
 
 template <typename TI, typename TO, int VPT>
 __global__ void __launch_bounds__(512) norm_rows_kernel(const NormRowsArgs a) {
@@ -406,7 +425,7 @@ __global__ void __launch_bounds__(512) norm_rows_wide_kernel(const NormRowsArgs 
             }
             if (QF != kQfNone) {  // every lane: the group max is a shuffle
                 const float yo[8] = {o[0].x, o[0].y, o[1].x, o[1].y, o[2].x, o[2].y, o[3].x, o[3].y};
-                quant_group_store<QF>(yo, e < n, a.qout, a.sout, a.gs, (u * n + e) >> 3, lane);
+                norm_quant_store<QF>(a, yo, u, e, lane);
             }
         }
     }
@@ -500,7 +519,7 @@ __global__ void __maxnreg__(VPL == 1 ? (QF == kQfNone ? 72 : 64) : 128) norm_row
                 }
                 if (QF != kQfNone) {  // every lane: the group max is a shuffle
                     const float yo[8] = {o[0].x, o[0].y, o[1].x, o[1].y, o[2].x, o[2].y, o[3].x, o[3].y};
-                    quant_group_store<QF>(yo, e < n, a.qout, a.sout, a.gs, (u * n + e) >> 3, lane);
+                    norm_quant_store<QF>(a, yo, u, e, lane);
                 }
             }
         }
@@ -599,6 +618,8 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
     a.stage_bytes = a.row_bytes * (x ? 2u : 1u);
     a.qout = a.sout = nullptr;
     a.gs = 1.0f;
+    a.sf_layout = kSfRowMajor;
+    a.sf_ncb = 0;
     a.lookahead = 0;  // without a quantised output it did not pay (76 vs 76 % at 4096 x 4 x 2560)
 
     // Direct design while a row fits one warp's register budget (<= 12 fp16 or 4 fp32 vectors per
@@ -698,8 +719,10 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
 // wide design at every width (n <= 16384; n % 32 == 0, the largest group).
 template <typename TI, typename TO, int QF>
 static int launch_norm_rows_quant(const void* x, void* res, const void* w, const float* inj, void* y, void* qout,
-                                  void* sout, float gs, int64_t T, int n, int hc, float eps, cudaStream_t stream) {
+                                  void* sout, float gs, int64_t T, int n, int hc, float eps, cudaStream_t stream,
+                                  int sf_layout = kSfRowMajor) {
     if (res == nullptr || w == nullptr || y == nullptr || qout == nullptr || sout == nullptr) return WZYB_ERR_NULL;
+    if (sf_layout != kSfRowMajor && (QF == kQfQ8 || sf_layout != kSfTiled128x4)) return WZYB_ERR_VALUE;
     if (T < 0 || T > (int64_t(1) << 40) || n < 32 || n > 16384 || (n % 32) != 0 || hc < 1 || hc > 64)
         return WZYB_ERR_SHAPE;
     if (!aligned16(res) || !aligned16(w) || !aligned16(y) || (x && !aligned16(x)) || !aligned16(qout) ||
@@ -725,6 +748,8 @@ static int launch_norm_rows_quant(const void* x, void* res, const void* w, const
     a.qout = qout;
     a.sout = sout;
     a.gs = gs;
+    a.sf_layout = sf_layout;
+    a.sf_ncb = (n / (QF == kQfNvfp4 ? 16 : 32) + 3) / 4;
     // on by default for the quantising rows (76 -> 80 % of peak at 4096 x 4 x 2560): the group
     // quantiser's epilogue is long enough that the next row's reads are worth starting under it
     a.lookahead = tuning(kFamNorm).stages == 1 ? 0 : 1;
@@ -753,6 +778,20 @@ int wzyb_gr_norm_nvfp4_f32(float* R, const float* w_norm, const float* bo_prev, 
     return wzyb::launch_norm_rows_quant<float, float, wzyb::kQfNvfp4>(bo_prev, R, w_norm, inj_prev, xn, xq, xs,
                                                                     global_scale, T, n_embd, hc, eps,
                                                                     (cudaStream_t)stream);
+}
+
+int wzyb_gr_norm_block_f32(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, float* xn,
+                           uint8_t* xq, uint8_t* xs, int format, int sf_layout, float global_scale, int64_t T,
+                           int n_embd, int hc, float eps, wzyb_stream_t stream) {
+    if (format == WZYB_BLOCK_MXFP8)
+        return wzyb::launch_norm_rows_quant<float, float, wzyb::kQfMxfp8>(bo_prev, R, w_norm, inj_prev, xn, xq, xs, 1.0f,
+                                                                        T, n_embd, hc, eps, (cudaStream_t)stream,
+                                                                        sf_layout);
+    if (format == WZYB_BLOCK_NVFP4)
+        return wzyb::launch_norm_rows_quant<float, float, wzyb::kQfNvfp4>(bo_prev, R, w_norm, inj_prev, xn, xq, xs,
+                                                                        global_scale, T, n_embd, hc, eps,
+                                                                        (cudaStream_t)stream, sf_layout);
+    return WZYB_ERR_VALUE;
 }
 
 int wzyb_add_rmsnorm_f16(const uint16_t* x, uint16_t* residual, const uint16_t* weight, uint16_t* y, int64_t T,

@@ -35,27 +35,34 @@ __global__ void __launch_bounds__(256) quant_act_kernel(const float* __restrict_
     }
 }
 
+// Row-major scales index by the flat vector; the tiled 128x4 layout needs the (row, scale column) of
+// each lane's vector, stepped per lane with StridePos (no division in the loop).
 template <int QF>
 __global__ void __launch_bounds__(256) quant_act_block_kernel(const float* __restrict__ x, void* __restrict__ q,
-                                                              void* __restrict__ s, float gs, int64_t nvec) {
+                                                              void* __restrict__ s, float gs, int64_t nvec, int vpr,
+                                                              int sf_layout, int ncb) {
     pdl_begin();
+    constexpr int kG = QF == kQfNvfp4 ? 16 : 32;  // elements per scale
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-    for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; base < nvec;
-         base += nwarps * 32) {
+    const int64_t first = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32;
+    StridePos ps(first + lane, nwarps * 32, vpr);  // vector v = (row q, vector in row r)
+    for (int64_t base = first; base < nvec; base += nwarps * 32, ps.advance()) {
         const int64_t v = base + lane;
         const bool act = v < nvec;
         float o[8] = {};
         if (act) Vec8<float>::load_stream(x + v * 8, o);
-        quant_group_store<QF>(o, act, q, s, gs, v, lane);
+        const int64_t soff = sf_layout == kSfTiled128x4 ? sf_tiled_offset(ps.q, ps.r * 8 / kG, ncb) : v * 8 / kG;
+        block_group_store_at<QF>(o, act, q, static_cast<uint8_t*>(s) + soff, gs, v, lane);
     }
 }
 
 template <int QF>
-static int launch_quant_act_block(const float* x, void* q, void* s, float gs, int64_t T, int cols,
+static int launch_quant_act_block(const float* x, void* q, void* s, float gs, int sf_layout, int64_t T, int cols,
                                   wzyb_stream_t stream) {
     if (!x || !q || !s) return WZYB_ERR_NULL;
     const int group = QF == kQfNvfp4 ? 16 : 32;
+    if (sf_layout != kSfRowMajor && sf_layout != kSfTiled128x4) return WZYB_ERR_VALUE;
     if (T < 0 || T > (int64_t(1) << 40) || cols < group || (cols % group) != 0) return WZYB_ERR_SHAPE;
     if (!aligned16(x) || !aligned16(q)) return WZYB_ERR_ALIGN;
     if (T == 0) return WZYB_OK;
@@ -63,8 +70,10 @@ static int launch_quant_act_block(const float* x, void* q, void* s, float gs, in
     const int rc = device_info(&di);
     if (rc != WZYB_OK) return rc;
     const int64_t nvec = T * cols / 8;
+    const int ncb = (cols / group + 3) / 4;
     const int grid = persistent_grid(di, 8, (nvec + 255) / 256);
-    launch_k(quant_act_block_kernel<QF>, grid, 256, 0, (cudaStream_t)stream, x, q, s, gs, nvec);
+    launch_k(quant_act_block_kernel<QF>, grid, 256, 0, (cudaStream_t)stream, x, q, s, gs, nvec, cols / 8, sf_layout,
+             ncb);
     return launch_status();
 }
 
@@ -91,12 +100,21 @@ int wzyb_quant_act_f32(const float* x, int8_t* q32, float* s32, int8_t* q16, flo
 }
 
 int wzyb_quant_act_mxfp8_f32(const float* x, uint8_t* q, uint8_t* s, int64_t T, int cols, wzyb_stream_t stream) {
-    return wzyb::launch_quant_act_block<wzyb::kQfMxfp8>(x, q, s, 1.0f, T, cols, stream);
+    return wzyb::launch_quant_act_block<wzyb::kQfMxfp8>(x, q, s, 1.0f, wzyb::kSfRowMajor, T, cols, stream);
 }
 
 int wzyb_quant_act_nvfp4_f32(const float* x, uint8_t* q, uint8_t* s, float global_scale, int64_t T, int cols,
                              wzyb_stream_t stream) {
-    return wzyb::launch_quant_act_block<wzyb::kQfNvfp4>(x, q, s, global_scale, T, cols, stream);
+    return wzyb::launch_quant_act_block<wzyb::kQfNvfp4>(x, q, s, global_scale, wzyb::kSfRowMajor, T, cols, stream);
+}
+
+int wzyb_quant_act_block_f32(const float* x, uint8_t* q, uint8_t* s, int format, int sf_layout, float global_scale,
+                             int64_t T, int cols, wzyb_stream_t stream) {
+    if (format == WZYB_BLOCK_MXFP8)
+        return wzyb::launch_quant_act_block<wzyb::kQfMxfp8>(x, q, s, 1.0f, sf_layout, T, cols, stream);
+    if (format == WZYB_BLOCK_NVFP4)
+        return wzyb::launch_quant_act_block<wzyb::kQfNvfp4>(x, q, s, global_scale, sf_layout, T, cols, stream);
+    return WZYB_ERR_VALUE;
 }
 
 }  // extern "C"

@@ -114,6 +114,8 @@ _SIGS = {
     "wzyb_swiglu_q8_f32": (c_int, [P, P, P, P, c_int64, S]),
     "wzyb_quant_act_f32": (c_int, [P, P, P, P, P, c_int64, c_int, S]),
     "wzyb_quant_act_mxfp8_f32": (c_int, [P, P, P, c_int64, c_int, S]),
+    "wzyb_quant_act_block_f32": (c_int, [P, P, P, c_int, c_int, c_float, c_int64, c_int, S]),
+    "wzyb_gr_norm_block_f32": (c_int, [P, P, P, P, P, P, P, c_int, c_int, c_float, c_int64, c_int, c_int, c_float, S]),
     "wzyb_quant_act_nvfp4_f32": (c_int, [P, P, P, c_float, c_int64, c_int, S]),
     "wzyb_swiglu_mxfp8_f32": (c_int, [P, P, P, P, c_int64, S]),
     "wzyb_swiglu_nvfp4_f32": (c_int, [P, P, P, P, c_float, c_int64, S]),
@@ -249,9 +251,23 @@ def quant_act_f32(x, q32, s32, q16, s16, T, cols, stream=None):
     call("wzyb_quant_act_f32", _ptr(x), _ptr(q32), _ptr(s32), _ptr(q16), _ptr(s16), T, cols, _stream(stream))
 
 
-def quant_act_block(x, q, s, T, cols, fmt="mxfp8", global_scale=1.0, stream=None):
-    """MXFP8 (fmt "mxfp8") or NVFP4 ("nvfp4") codes and scale bytes of fp32 rows x [T, cols]."""
-    if fmt == "mxfp8":
+BLOCK_MXFP8, BLOCK_NVFP4 = 0, 1
+SF_ROW_MAJOR, SF_TILED_128X4 = 0, 1
+
+
+def sf_tiled_bytes(rows, cols, fmt="mxfp8"):
+    """Bytes of a tiled-128x4 scale buffer for codes [rows, cols]."""
+    scols = cols // (32 if fmt == "mxfp8" else 16)
+    return -(-rows // 128) * 128 * (-(-scols // 4)) * 4
+
+
+def quant_act_block(x, q, s, T, cols, fmt="mxfp8", global_scale=1.0, stream=None, sf_layout=None):
+    """MXFP8 (fmt "mxfp8") or NVFP4 ("nvfp4") codes and scale bytes of fp32 rows x [T, cols]; sf_layout
+    SF_TILED_128X4 writes the scales in the block-scaled MMA operand layout."""
+    if sf_layout is not None:
+        call("wzyb_quant_act_block_f32", _ptr(x), _ptr(q), _ptr(s), BLOCK_MXFP8 if fmt == "mxfp8" else BLOCK_NVFP4,
+             sf_layout, global_scale, T, cols, _stream(stream))
+    elif fmt == "mxfp8":
         call("wzyb_quant_act_mxfp8_f32", _ptr(x), _ptr(q), _ptr(s), T, cols, _stream(stream))
     else:
         call("wzyb_quant_act_nvfp4_f32", _ptr(x), _ptr(q), _ptr(s), global_scale, T, cols, _stream(stream))
@@ -266,8 +282,12 @@ def swiglu_block(gate, up, q, s, fmt="mxfp8", global_scale=1.0, stream=None):
 
 
 def gr_norm_block(R, w_norm, bo_prev, inj_prev, xn, xq, xs, T, n_embd, hc, fmt="mxfp8", global_scale=1.0, eps=1e-6,
-                  stream=None):
-    if fmt == "mxfp8":
+                  stream=None, sf_layout=None):
+    if sf_layout is not None:
+        call("wzyb_gr_norm_block_f32", _ptr(R), _ptr(w_norm), _ptr(bo_prev), _ptr(inj_prev), _ptr(xn), _ptr(xq),
+             _ptr(xs), BLOCK_MXFP8 if fmt == "mxfp8" else BLOCK_NVFP4, sf_layout, global_scale, T, n_embd, hc, eps,
+             _stream(stream))
+    elif fmt == "mxfp8":
         call("wzyb_gr_norm_mxfp8_f32", _ptr(R), _ptr(w_norm), _ptr(bo_prev), _ptr(inj_prev), _ptr(xn), _ptr(xq),
              _ptr(xs), T, n_embd, hc, eps, _stream(stream))
     else:

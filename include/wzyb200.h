@@ -279,6 +279,10 @@ int wzyb_quant_act_block_f32(const float* x, uint8_t* q, uint8_t* s, int format,
 int wzyb_gr_norm_block_f32(float* R, const float* w_norm, const float* bo_prev, const float* inj_prev, float* xn,
                            uint8_t* xq, uint8_t* xs, int format, int sf_layout, float global_scale, int64_t T,
                            int n_embd, int hc, float eps, wzyb_stream_t stream);
+/* SwiGLU straight to a block format with a choice of scale layout: gate, up and the codes [rows, cols]
+ * (cols % 32 == 0), format and sf_layout as above. */
+int wzyb_swiglu_block_f32(const float* gate, const float* up, uint8_t* q, uint8_t* s, int format, int sf_layout,
+                          float global_scale, int64_t rows, int cols, wzyb_stream_t stream);
 /* SwiGLU (the reference's expression) straight to the block formats; n % 32 == 0. */
 int wzyb_swiglu_mxfp8_f32(const float* gate, const float* up, uint8_t* q, uint8_t* s, int64_t n,
                           wzyb_stream_t stream);

@@ -85,6 +85,10 @@ def test_argument_validation_before_any_cuda_call(wz):
     assert L.wzyb_quant_act_block_f32(A16, A16, A16, 7, wz.SF_ROW_MAJOR, 1.0, 4, 2560, NULL) == wz.ERR_VALUE
     assert L.wzyb_quant_act_block_f32(A16, A16, A16, wz.BLOCK_MXFP8, 5, 1.0, 4, 2560, NULL) == wz.ERR_VALUE
     assert L.wzyb_quant_act_block_f32(A16, NULL, A16, wz.BLOCK_NVFP4, wz.SF_TILED_128X4, 1.0, 4, 2560, NULL) == wz.ERR_NULL
+    assert L.wzyb_swiglu_block_f32(A16, A16, A16, A16, 2, wz.SF_ROW_MAJOR, 1.0, 4, 512, NULL) == wz.ERR_VALUE
+    assert L.wzyb_swiglu_block_f32(A16, A16, A16, A16, wz.BLOCK_MXFP8, 4, 1.0, 4, 512, NULL) == wz.ERR_VALUE
+    assert L.wzyb_swiglu_block_f32(A16, A16, A16, A16, wz.BLOCK_MXFP8, wz.SF_TILED_128X4, 1.0, 4, 520, NULL) == \
+        wz.ERR_SHAPE
     assert L.wzyb_gr_norm_block_f32(A16, A16, A16, A16, A16, A16, A16, 3, wz.SF_ROW_MAJOR, 1.0, 4, 2560, 4, 1e-6,
                                     NULL) == wz.ERR_VALUE
     assert L.wzyb_gr_norm_block_f32(A16, A16, A16, A16, A16, A16, A16, wz.BLOCK_MXFP8, 9, 1.0, 4, 2560, 4, 1e-6,

@@ -740,6 +740,57 @@ def test_gr_norm_block_tiled_layout(wz, T):
         assert np.array_equal(outs[1][2], _to_blocked(outs[0][2].reshape(T * hc, n // g)))
 
 
+@pytest.mark.parametrize("fmt", ["mxfp8", "nvfp4"])
+def test_swiglu_block_tiled_layout(wz, fmt):
+    r = rng(65)
+    rows, cols = 77, 512
+    g = (2 * r.standard_normal((rows, cols))).astype(np.float32)
+    u = r.standard_normal((rows, cols)).astype(np.float32)
+    q0, s0 = _dev_block_out(rows * cols, fmt)
+    wz.swiglu_block(dev(g), dev(u), q0, s0, fmt=fmt, global_scale=2.0)
+    q1 = torch.empty_like(q0)
+    s1 = torch.full((wz.sf_tiled_bytes(rows, cols, fmt),), 0xAB, dtype=torch.uint8, device=DEV)
+    wz.swiglu_block(dev(g), dev(u), q1, s1, fmt=fmt, global_scale=2.0, sf_layout=wz.SF_TILED_128X4, cols=cols)
+    gsz = 32 if fmt == "mxfp8" else 16
+    assert np.array_equal(host(q1), host(q0))
+    assert np.array_equal(host(s1), _to_blocked(host(s0).reshape(rows, cols // gsz)))
+
+
+def test_nvfp4_tiled_scales_feed_a_block_scaled_gemm(wz):
+    """As the MXFP8 case, for NVFP4 (e2m1 pairs, e4m3 scale per 16; global scale 1) through torch's FP4
+    block-scaled GEMM, where this torch build has one."""
+    if not hasattr(torch, "float4_e2m1fn_x2"):
+        pytest.skip("torch has no float4_e2m1fn_x2")
+    M, N, K = 256, 256, 512
+    r = rng(66)
+    a = r.standard_normal((M, K)).astype(np.float32)
+    b = r.standard_normal((N, K)).astype(np.float32)
+    qa, qb = torch.empty(M * K // 2, dtype=torch.uint8, device=DEV), torch.empty(N * K // 2, dtype=torch.uint8, device=DEV)
+    sa = torch.empty(wz.sf_tiled_bytes(M, K, "nvfp4"), dtype=torch.uint8, device=DEV)
+    sb = torch.empty(wz.sf_tiled_bytes(N, K, "nvfp4"), dtype=torch.uint8, device=DEV)
+    wz.quant_act_block(dev(a), qa, sa, M, K, fmt="nvfp4", sf_layout=wz.SF_TILED_128X4)
+    wz.quant_act_block(dev(b), qb, sb, N, K, fmt="nvfp4", sf_layout=wz.SF_TILED_128X4)
+    A = qa.view(torch.float4_e2m1fn_x2).view(M, K // 2)
+    B = qb.view(torch.float4_e2m1fn_x2).view(N, K // 2)
+    try:
+        out = torch._scaled_mm(A, B.t(), scale_a=sa.view(torch.float8_e4m3fn), scale_b=sb.view(torch.float8_e4m3fn),
+                               out_dtype=torch.bfloat16)
+    except (RuntimeError, TypeError, ValueError, NotImplementedError) as e:
+        pytest.skip(f"no NVFP4 block-scaled GEMM in this torch build: {str(e)[:120]}")
+    lut = torch.tensor([0, .5, 1, 1.5, 2, 3, 4, 6, -0., -.5, -1, -1.5, -2, -3, -4, -6], device=DEV)
+
+    def deq(q, rows, x):
+        rs = torch.empty(rows * K // 16, dtype=torch.uint8, device=DEV)
+        qq = torch.empty_like(q)
+        wz.quant_act_block(dev(x), qq, rs, rows, K, fmt="nvfp4")
+        v = torch.stack([lut[(qq & 0xF).long()], lut[(qq >> 4).long()]], dim=-1).view(rows, K)
+        return v * rs.view(torch.float8_e4m3fn).float().view(rows, K // 16).repeat_interleave(16, dim=1)
+
+    want = deq(qa, M, a).double() @ deq(qb, N, b).double().t()
+    err = (out.double() - want).abs().max().item() / want.abs().max().item()
+    assert err < 1e-2, f"NVFP4 block-scaled GEMM vs dequantised product: {err}"
+
+
 def test_mxfp8_tiled_scales_feed_a_block_scaled_gemm(wz):
     """End to end: A [M, K] and B [N, K] quantised to MXFP8 with tiled scales go straight into the block-
     scaled tensor-core GEMM of this torch build (torch._scaled_mm, cuBLASLt); the product matches the

@@ -95,12 +95,14 @@ __global__ void __launch_bounds__(kSwigluThreads) swiglu_kernel(const TI* __rest
 template <typename TI, int QF>
 __global__ void __launch_bounds__(256) swiglu_quant_kernel(const TI* __restrict__ gate, const TI* __restrict__ up,
                                                            void* __restrict__ q, void* __restrict__ s, float gs,
-                                                           int64_t nvec) {
+                                                           int64_t nvec, int vpr, int sf_layout, int ncb) {
     pdl_begin();
+    constexpr int kG = QF == kQfNvfp4 ? 16 : 32;  // elements per scale
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-    for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; base < nvec;
-         base += nwarps * 32) {
+    const int64_t first = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32;
+    StridePos ps(first + lane, nwarps * 32, vpr);  // vector v = (row q, vector in row r): tiled scales
+    for (int64_t base = first; base < nvec; base += nwarps * 32, ps.advance()) {
         const int64_t v = base + lane;
         const bool act = v < nvec;
         float o[8] = {};
@@ -110,6 +112,13 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const TI* __restrict_
             Vec8<TI>::load_stream(up + v * 8, u);
 #pragma unroll
             for (int e = 0; e < 8; ++e) o[e] = (g[e] / (1.0f + __expf(-g[e]))) * u[e];
+        }
+        if constexpr (QF == kQfMxfp8 || QF == kQfNvfp4) {
+            if (sf_layout == kSfTiled128x4) {
+                block_group_store_at<QF>(o, act, q, static_cast<uint8_t*>(s) + sf_tiled_offset(ps.q, ps.r * 8 / kG, ncb),
+                                         gs, v, lane);
+                continue;
+            }
         }
         quant_group_store<QF>(o, act, q, s, gs, v, lane);
     }
@@ -137,19 +146,26 @@ static int launch_swiglu(const TI* gate, const TI* up, TO* out, int64_t nvec, in
 }
 
 // n % 32 == 0 (the largest group); Q8 scales are fp32 (4-byte aligned), the block formats' are bytes.
+// n elements as rows of `cols` (cols == n for the flat forms); sf_layout for the block formats.
 template <int QF>
 static int launch_swiglu_quant(const float* gate, const float* up, void* q, void* s, float gs, int64_t n,
-                               wzyb_stream_t stream) {
+                               wzyb_stream_t stream, int64_t cols = 0, int sf_layout = kSfRowMajor) {
     if (!gate || !up || !q || !s) return WZYB_ERR_NULL;
+    if (sf_layout != kSfRowMajor && (QF == kQfQ8 || sf_layout != kSfTiled128x4)) return WZYB_ERR_VALUE;
     if (n < 0 || (n % 32) != 0) return WZYB_ERR_SHAPE;
+    if (cols == 0) cols = n;  // the flat forms: one row
+    if (n > 0 && (cols < 32 || (cols % 32) != 0 || (n % cols) != 0 || cols > (int64_t(1) << 30)))
+        return WZYB_ERR_SHAPE;
     if (!aligned16(gate) || !aligned16(up) || !aligned16(q) || (QF == kQfQ8 && !aligned16(s))) return WZYB_ERR_ALIGN;
     if (n == 0) return WZYB_OK;
     DeviceInfo di;
     const int rc = device_info(&di);
     if (rc != WZYB_OK) return rc;
     const int64_t nvec = n / 8;
+    const int ncb = (int)((cols / (QF == kQfNvfp4 ? 16 : 32) + 3) / 4);
     const int grid = persistent_grid(di, 8, (nvec + 255) / 256);
-    launch_k(swiglu_quant_kernel<float, QF>, grid, 256, 0, (cudaStream_t)stream, gate, up, q, s, gs, nvec);
+    launch_k(swiglu_quant_kernel<float, QF>, grid, 256, 0, (cudaStream_t)stream, gate, up, q, s, gs, nvec,
+             (int)(cols / 8), sf_layout, ncb);
     return launch_status();
 }
 
@@ -184,6 +200,17 @@ int wzyb_swiglu_mxfp8_f32(const float* gate, const float* up, uint8_t* q, uint8_
 int wzyb_swiglu_nvfp4_f32(const float* gate, const float* up, uint8_t* q, uint8_t* s, float global_scale, int64_t n,
                           wzyb_stream_t stream) {
     return wzyb::launch_swiglu_quant<wzyb::kQfNvfp4>(gate, up, q, s, global_scale, n, stream);
+}
+
+int wzyb_swiglu_block_f32(const float* gate, const float* up, uint8_t* q, uint8_t* s, int format, int sf_layout,
+                          float global_scale, int64_t rows, int cols, wzyb_stream_t stream) {
+    if (rows < 0 || cols < 32 || rows > (int64_t(1) << 40)) return WZYB_ERR_SHAPE;
+    if (format == WZYB_BLOCK_MXFP8)
+        return wzyb::launch_swiglu_quant<wzyb::kQfMxfp8>(gate, up, q, s, 1.0f, rows * cols, stream, cols, sf_layout);
+    if (format == WZYB_BLOCK_NVFP4)
+        return wzyb::launch_swiglu_quant<wzyb::kQfNvfp4>(gate, up, q, s, global_scale, rows * cols, stream, cols,
+                                                        sf_layout);
+    return WZYB_ERR_VALUE;
 }
 
 int wzyb_swiglu_interleaved_f16(const uint16_t* gu, uint16_t* out, int64_t T, int nff, wzyb_stream_t stream) {

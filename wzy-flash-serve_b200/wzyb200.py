@@ -115,6 +115,7 @@ _SIGS = {
     "wzyb_quant_act_f32": (c_int, [P, P, P, P, P, c_int64, c_int, S]),
     "wzyb_quant_act_mxfp8_f32": (c_int, [P, P, P, c_int64, c_int, S]),
     "wzyb_quant_act_block_f32": (c_int, [P, P, P, c_int, c_int, c_float, c_int64, c_int, S]),
+    "wzyb_swiglu_block_f32": (c_int, [P, P, P, P, c_int, c_int, c_float, c_int64, c_int, S]),
     "wzyb_gr_norm_block_f32": (c_int, [P, P, P, P, P, P, P, c_int, c_int, c_float, c_int64, c_int, c_int, c_float, S]),
     "wzyb_quant_act_nvfp4_f32": (c_int, [P, P, P, c_float, c_int64, c_int, S]),
     "wzyb_swiglu_mxfp8_f32": (c_int, [P, P, P, P, c_int64, S]),
@@ -273,8 +274,12 @@ def quant_act_block(x, q, s, T, cols, fmt="mxfp8", global_scale=1.0, stream=None
         call("wzyb_quant_act_nvfp4_f32", _ptr(x), _ptr(q), _ptr(s), global_scale, T, cols, _stream(stream))
 
 
-def swiglu_block(gate, up, q, s, fmt="mxfp8", global_scale=1.0, stream=None):
-    if fmt == "mxfp8":
+def swiglu_block(gate, up, q, s, fmt="mxfp8", global_scale=1.0, stream=None, sf_layout=None, cols=None):
+    """SwiGLU to MXFP8 / NVFP4; with sf_layout (and the row width `cols`) the scales may be tiled."""
+    if sf_layout is not None:
+        call("wzyb_swiglu_block_f32", _ptr(gate), _ptr(up), _ptr(q), _ptr(s), BLOCK_MXFP8 if fmt == "mxfp8" else
+             BLOCK_NVFP4, sf_layout, global_scale, gate.numel() // cols, cols, _stream(stream))
+    elif fmt == "mxfp8":
         call("wzyb_swiglu_mxfp8_f32", _ptr(gate), _ptr(up), _ptr(q), _ptr(s), gate.numel(), _stream(stream))
     else:
         call("wzyb_swiglu_nvfp4_f32", _ptr(gate), _ptr(up), _ptr(q), _ptr(s), global_scale, gate.numel(),

@@ -37,23 +37,29 @@ __global__ void __launch_bounds__(256) quant_act_kernel(const float* __restrict_
 
 // Row-major scales index by the flat vector; the tiled 128x4 layout needs the (row, scale column) of
 // each lane's vector, stepped per lane with StridePos (no division in the loop).
-template <int QF>
+template <int QF, int SFL>
 __global__ void __launch_bounds__(256) quant_act_block_kernel(const float* __restrict__ x, void* __restrict__ q,
                                                               void* __restrict__ s, float gs, int64_t nvec, int vpr,
-                                                              int sf_layout, int ncb) {
+                                                              int ncb) {
     pdl_begin();
     constexpr int kG = QF == kQfNvfp4 ? 16 : 32;  // elements per scale
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const int64_t first = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32;
-    StridePos ps(first + lane, nwarps * 32, vpr);  // vector v = (row q, vector in row r)
-    for (int64_t base = first; base < nvec; base += nwarps * 32, ps.advance()) {
+    // tiled scales: vector v = (row q, vector in row r), stepped; row-major scales need neither
+    StridePos ps(SFL == kSfTiled128x4 ? first + lane : 0, SFL == kSfTiled128x4 ? nwarps * 32 : 0, vpr);
+    for (int64_t base = first; base < nvec; base += nwarps * 32) {
         const int64_t v = base + lane;
         const bool act = v < nvec;
         float o[8] = {};
         if (act) Vec8<float>::load_stream(x + v * 8, o);
-        const int64_t soff = sf_layout == kSfTiled128x4 ? sf_tiled_offset(ps.q, ps.r * 8 / kG, ncb) : v * 8 / kG;
-        block_group_store_at<QF>(o, act, q, static_cast<uint8_t*>(s) + soff, gs, v, lane);
+        if constexpr (SFL == kSfTiled128x4) {
+            block_group_store_at<QF>(o, act, q, static_cast<uint8_t*>(s) + sf_tiled_offset(ps.q, ps.r * 8 / kG, ncb),
+                                     gs, v, lane);
+            ps.advance();
+        } else {
+            quant_group_store<QF>(o, act, q, s, gs, v, lane);
+        }
     }
 }
 
@@ -72,8 +78,12 @@ static int launch_quant_act_block(const float* x, void* q, void* s, float gs, in
     const int64_t nvec = T * cols / 8;
     const int ncb = (cols / group + 3) / 4;
     const int grid = persistent_grid(di, 8, (nvec + 255) / 256);
-    launch_k(quant_act_block_kernel<QF>, grid, 256, 0, (cudaStream_t)stream, x, q, s, gs, nvec, cols / 8, sf_layout,
-             ncb);
+    if (sf_layout == kSfTiled128x4)
+        launch_k(quant_act_block_kernel<QF, kSfTiled128x4>, grid, 256, 0, (cudaStream_t)stream, x, q, s, gs, nvec,
+                 cols / 8, ncb);
+    else
+        launch_k(quant_act_block_kernel<QF, kSfRowMajor>, grid, 256, 0, (cudaStream_t)stream, x, q, s, gs, nvec,
+                 cols / 8, ncb);
     return launch_status();
 }
 

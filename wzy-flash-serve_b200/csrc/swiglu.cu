@@ -92,17 +92,18 @@ __global__ void __launch_bounds__(kSwigluThreads) swiglu_kernel(const TI* __rest
 // (16-element) or two (32-element) shuffles. The activation uses the reference's own expression,
 // (g / (1 + __expf(-g))) * u with the IEEE divide, so on the same inputs the Q8 codes and scales come
 // out as the reference kernel's.
-template <typename TI, int QF>
+template <typename TI, int QF, int SFL>
 __global__ void __launch_bounds__(256) swiglu_quant_kernel(const TI* __restrict__ gate, const TI* __restrict__ up,
                                                            void* __restrict__ q, void* __restrict__ s, float gs,
-                                                           int64_t nvec, int vpr, int sf_layout, int ncb) {
+                                                           int64_t nvec, int vpr, int ncb) {
     pdl_begin();
     constexpr int kG = QF == kQfNvfp4 ? 16 : 32;  // elements per scale
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const int64_t first = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32;
-    StridePos ps(first + lane, nwarps * 32, vpr);  // vector v = (row q, vector in row r): tiled scales
-    for (int64_t base = first; base < nvec; base += nwarps * 32, ps.advance()) {
+    // tiled scales: vector v = (row q, vector in row r), stepped; row-major scales need neither
+    StridePos ps(SFL == kSfTiled128x4 ? first + lane : 0, SFL == kSfTiled128x4 ? nwarps * 32 : 0, vpr);
+    for (int64_t base = first; base < nvec; base += nwarps * 32) {
         const int64_t v = base + lane;
         const bool act = v < nvec;
         float o[8] = {};
@@ -113,14 +114,13 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const TI* __restrict_
 #pragma unroll
             for (int e = 0; e < 8; ++e) o[e] = (g[e] / (1.0f + __expf(-g[e]))) * u[e];
         }
-        if constexpr (QF == kQfMxfp8 || QF == kQfNvfp4) {
-            if (sf_layout == kSfTiled128x4) {
-                block_group_store_at<QF>(o, act, q, static_cast<uint8_t*>(s) + sf_tiled_offset(ps.q, ps.r * 8 / kG, ncb),
-                                         gs, v, lane);
-                continue;
-            }
+        if constexpr (SFL == kSfTiled128x4) {
+            block_group_store_at<QF>(o, act, q, static_cast<uint8_t*>(s) + sf_tiled_offset(ps.q, ps.r * 8 / kG, ncb),
+                                     gs, v, lane);
+            ps.advance();
+        } else {
+            quant_group_store<QF>(o, act, q, s, gs, v, lane);
         }
-        quant_group_store<QF>(o, act, q, s, gs, v, lane);
     }
 }
 
@@ -164,8 +164,15 @@ static int launch_swiglu_quant(const float* gate, const float* up, void* q, void
     const int64_t nvec = n / 8;
     const int ncb = (int)((cols / (QF == kQfNvfp4 ? 16 : 32) + 3) / 4);
     const int grid = persistent_grid(di, 8, (nvec + 255) / 256);
-    launch_k(swiglu_quant_kernel<float, QF>, grid, 256, 0, (cudaStream_t)stream, gate, up, q, s, gs, nvec,
-             (int)(cols / 8), sf_layout, ncb);
+    if constexpr (QF != kQfQ8) {
+        if (sf_layout == kSfTiled128x4) {
+            launch_k(swiglu_quant_kernel<float, QF, kSfTiled128x4>, grid, 256, 0, (cudaStream_t)stream, gate, up, q, s,
+                     gs, nvec, (int)(cols / 8), ncb);
+            return launch_status();
+        }
+    }
+    launch_k(swiglu_quant_kernel<float, QF, kSfRowMajor>, grid, 256, 0, (cudaStream_t)stream, gate, up, q, s, gs, nvec,
+             (int)(cols / 8), ncb);
     return launch_status();
 }
 

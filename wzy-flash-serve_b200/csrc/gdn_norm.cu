@@ -4,9 +4,10 @@
 // fused_gdn_step_norm_multi (src/wzy_kernels_v2.cuh:966-976):
 //   y = o * rsqrt(sum(o^2)/hd + eps) * gamma[col] / (1 + exp(-z))
 // i.e. the gate is sigmoid(z) at every reference site; WZYB_GATE_SILU selects z*sigmoid(z).
-// The reference runs one 128-thread block per (head, token) with a shared-memory reduction. Here a
-// unit is one token (o row + z row, all heads) staged by TMA bulk copies (ring.cuh); each head is
-// owned by hd/8 lanes that reduce with xor shuffles, and y leaves with one 16-byte store per lane.
+// The reference runs one 128-thread block per (head, token) with a shared-memory reduction. Here each
+// head is owned by hd/8 lanes that reduce with xor shuffles, and y leaves with one 16-byte store per
+// lane. Default (direct): a warp per 256-element slab, 4 slabs' loads in flight per warp; on request,
+// the slabs staged by cp.async (async) or whole tokens by TMA bulk copies (ring, ring.cuh).
 #include "launch.hpp"
 #include "ring.cuh"
 

@@ -5,10 +5,12 @@
 //   (a, d) = (p[i], p[i+R/2]), i < R/2:  p[i] = a*cos - d*sin;  p[i+R/2] = a*sin + d*cos
 // with cos/sin from a [pos][R/2] fp32 table built in fp64 (build_rope_cos_sin_host,
 // src/wzy_qsa_256k.cuh:33-46). The reference runs one 128-thread block per (head, token) with three
-// __syncthreads and rotates on 32 of the 128 threads. Here a unit is one token (all q heads + all k
-// heads), staged by TMA bulk copies (ring.cuh); each head is owned by hd/8 lanes holding 8 elements
-// each, reduced with xor shuffles inside the lane group, and the rotation partner (i +- R/2) is the
-// lane R/16 positions away, fetched with one shuffle per element. No shared-memory reduction.
+// __syncthreads and rotates on 32 of the 128 threads. Here no design uses a shared-memory reduction:
+//   pair   (default): hd/16 lanes per head, each holding the two 8-element chunks of a rotation pair
+//          (or two plain chunks), so the rotation needs no shuffle; heads reduced with xor shuffles;
+//          6 heads per warp item, or a whole token for long calls;
+//   direct: hd/8 lanes per head, the rotation partner fetched from the lane R/16 away by shuffles;
+//   async / ring (on request): the direct design's units staged by cp.async or TMA bulk copies.
 #include <cmath>
 
 #include "launch.hpp"

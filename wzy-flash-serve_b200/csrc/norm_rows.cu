@@ -5,9 +5,14 @@
 //   v = R + bo * gw          gw = 2*sigmoid(inj/hc) (exactly 1.0 for the single-stream add)
 //   R <- v;  xn = (v * rsqrt(sum(v^2)/n + eps)) * g
 // The reference runs one 256-thread block per (stream, token) row, reads R twice (the second pass
-// re-reads it from cache) with scalar 4-byte accesses. Here each unit (= one row of R) is staged
-// into shared memory by a TMA bulk copy S units ahead (ring.cuh), read once into registers, reduced
-// with one warp-shuffle + one CTA barrier, and both outputs are written with 16-byte stores.
+// re-reads it from cache) with scalar 4-byte accesses. Here every design reads each input once with
+// 16-byte accesses and writes both outputs with 16-byte streaming stores:
+//   direct (default while a row fits a warp's registers): a warp per row, all its vectors loaded
+//          before any arithmetic, xor-shuffle reduction, no shared memory;
+//   wide   (longer rows): a CTA per row, per-warp partial sums meeting behind one barrier; with 4
+//          streams and bo_prev, a CTA per token (its 4 rows share one bo_prev read);
+//   async  (on request): warp-owned rows staged in lane-private shared memory by cp.async;
+//   ring   (on request): rows staged by TMA bulk copies S units ahead (ring.cuh), consumed by a CTA.
 #include "launch.hpp"
 #include "ring.cuh"
 

@@ -13,7 +13,8 @@
 // The reference stages the PLE rows on the host (a hash + an 84 MB direct-mapped row cache + an
 // H2D copy per window). Here the 51 GB fp8 table sits in HBM and one warp per token hashes (16
 // lanes, one head each) and streams its 16 rows. ple_conv_multi walks T sequentially per channel
-// (10,240 threads); its output does not feed back, so here every (token, 4 channels) is a thread.
+// (10,240 threads); its output does not feed back, so here a thread takes 4 channels of 4 tokens
+// spaced by the dilation (or of one token, when the per-token history snapshots are written).
 #include <cuda_fp8.h>
 
 #include "launch.hpp"

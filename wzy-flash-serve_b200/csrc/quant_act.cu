@@ -3,8 +3,9 @@
 // Math follows quant_act_multi (src/wzy_kernels_v2.cuh:58-111): per group of 32 (q32/s32) and, from
 // the same read, per group of 16 (q16/s16): d = amax / 127, q = rint(x * (127 / amax)) clamped to
 // [-127, 127]. The reference gives each thread one 16-element group (scalar 4-byte re-reads of the
-// second half for the 32-wide scale). Here a lane holds 8 elements from one 32-byte load; a 16-group
-// is 2 lanes and a 32-group 4 lanes, whose maxima are one and two xor shuffles.
+// second half for the 32-wide scale). Here a lane holds 8 elements (two 16-byte loads); a 16-group
+// is 2 lanes and a 32-group 4 lanes: one lane max, then one xor shuffle for the 16-group max and one
+// more for the 32-group max.
 //
 // The same pass also writes the block-scaled formats that sm_100's tensor cores take as GEMM
 // inputs (tcgen05.mma block scaling): MXFP8 (e4m3 codes, E8M0 scale per 32) and NVFP4 (e2m1 codes

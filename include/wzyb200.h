@@ -428,13 +428,20 @@ int wzyb_ple_halo(const int32_t* ids, int64_t row0, const int32_t* seq_prev, int
 /* ============================================================================================
  * Runtime helpers.
  * ========================================================================================== */
-/* One-time per-device set-up (device check, SM count, shared-memory opt-in). Launchers call it
+/* Launch semantics: every kernel is launched with programmatic stream serialization (programmatic
+ * dependent launch) and begins by waiting for the previous grid in the stream to complete, before
+ * any memory access, so stream order holds exactly as for plain launches (also when captured into
+ * a CUDA graph), while the launch itself overlaps the previous kernel's tail. WZYB_PDL=0 in the
+ * environment launches without the attribute.
+ * One-time per-device set-up (device check, SM count, shared-memory opt-in). Launchers call it
  * lazily; call it explicitly before capturing a stream into a CUDA graph. */
 int wzyb_prepare_device(void);
 /* Read the current device's fault bits (synchronous); clears them when clear != 0. */
 int wzyb_read_faults(uint32_t* faults, int clear);
-/* Launch-shape tuning per kernel family (process-wide): CTAs per SM (1..16) and TMA ring depth
- * (0 = as deep as the shared-memory budget allows, else 1..64 stages).
+/* Launch-shape tuning per kernel family (process-wide), for A/B measurement: CTAs per SM (1..16) and
+ * TMA ring depth (0 = as deep as the shared-memory budget allows, else 1..64 stages) of the ring
+ * design. Outside the ring: SwiGLU stages 1 / 2 force the scalar / packed math; head norm+RoPE
+ * ctas_per_sm 2 selects the other instantiation of its design.
  * Families: 0 add+RMSNorm, 1 head norm+RoPE, 2 GDN gated norm, 3 SwiGLU, 4 gathers. */
 #define WZYB_FAM_NORM 0
 #define WZYB_FAM_HEAD_ROPE 1

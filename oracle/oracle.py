@@ -402,10 +402,47 @@ def ref_lib() -> ctypes.CDLL:
             fn.argtypes = args
         L.ref_build_rope_cos_sin_host.restype = None
         L.ref_build_rope_cos_sin_host.argtypes = [I, F, P, P]
+        L.ref_ple_src_rows.restype = c_int
+        L.ref_ple_src_rows.argtypes = [ctypes.c_char_p, P, I, P, POINTER(c_float), POINTER(c_int),
+                                       POINTER(ctypes.c_uint64)]
         L.ref_dims.restype = c_int
         L.ref_dims.argtypes = [POINTER(c_int), POINTER(c_int)]
         _ref = L
     return _ref
+
+
+def write_ple_gguf(path, table, scale):
+    """A minimal GGUF file as the reference's PleSrc::open reads it (src/wzy_stage_v2.cuh:228-283):
+    magic, version, one key "strata.ple.scale" (float32), one tensor "per_layer_token_embd.weight" of
+    dims [row_bytes, rows] at offset 0, data aligned to 32 bytes."""
+    import struct
+
+    table = np.ascontiguousarray(table, np.uint8)
+    rows, rb = table.shape
+
+    def gstr(x):
+        b = x.encode()
+        return struct.pack("<Q", len(b)) + b
+
+    head = b"GGUF" + struct.pack("<I", 3) + struct.pack("<QQ", 1, 1)
+    head += gstr("strata.ple.scale") + struct.pack("<I", 6) + struct.pack("<f", scale)
+    head += gstr("per_layer_token_embd.weight") + struct.pack("<I", 2) + struct.pack("<QQ", rb, rows)
+    head += struct.pack("<I", 0) + struct.pack("<Q", 0)
+    pad = (-len(head)) % 32
+    with open(path, "wb") as f:
+        f.write(head + b"\0" * pad)
+        f.write(table.tobytes())
+
+
+def ref_ple_src_rows(path, rows_idx):
+    """The reference's PleSrc decode of the given rows: (floats [n, row_bytes], scale, row_bytes, rows)."""
+    idx = np.ascontiguousarray(rows_idx, np.uint64)
+    out = np.empty((idx.size, 160), dtype=np.float32)
+    sc, rb, nr = c_float(), c_int(), ctypes.c_uint64()
+    rc = ref_lib().ref_ple_src_rows(str(path).encode(), _p(idx), idx.size, _p(out), ctypes.byref(sc),
+                                    ctypes.byref(rb), ctypes.byref(nr))
+    assert rc == 0, "PleSrc::open rejected the file"
+    return out, sc.value, rb.value, nr.value
 
 
 def ref_rope_table(rows, theta=1e7):

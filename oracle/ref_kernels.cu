@@ -144,6 +144,26 @@ int ref_ple_conv_multi(const float* norm, const float* cw, float* hist, const fl
     return (int)cudaGetLastError();
 }
 
+// The reference's PLE row source (PleSrc, src/wzy_stage_v2.cuh:215-324) opened on a GGUF file and asked
+// for rows idx[0..n): its own header parse (scale key, tensor offset) and fp8 decode (the 256-entry
+// table with the NaN codes as 0, times the scale), through its row cache. Host code.
+int ref_ple_src_rows(const char* path, const uint64_t* idx, int n, float* out, float* scale_out,
+                     int* row_bytes_out, uint64_t* rows_out) {
+    PleSrc* src = new PleSrc();
+    if (!src->open(path)) {
+        if (src->base) munmap(src->base, src->sz);
+        delete src;
+        return 1;
+    }
+    for (int i = 0; i < n; ++i) src->row(idx[i], out + (size_t)i * PLE_HEAD);
+    *scale_out = src->scale;
+    *row_bytes_out = src->row_bytes;
+    *rows_out = src->rows;
+    munmap(src->base, src->sz);
+    delete src;
+    return 0;
+}
+
 int ref_dims(int* ne, int* nvocab) {
     *ne = NE;
     *nvocab = NVOCAB;

@@ -441,3 +441,25 @@ def test_pin_swiglu_block_formats(ref, orc, wz, fmt):
     s = torch.empty(n // (32 if fmt == "mxfp8" else 16), dtype=torch.uint8, device=DEV)
     wz.swiglu_block(dg, du, q, s, fmt=fmt, global_scale=2.5)
     assert np.array_equal(host(q), want_q) and np.array_equal(host(s), want_s)
+
+
+def test_pin_ple_fp8_gather_against_plesrc(ref, orc, wz, tmp_path):
+    """The CUDA fp8 PLE gather against the reference's own PleSrc decode of the same GGUF table (rows
+    named by the reference hash's constants over a small synthetic table): bit-exact."""
+    r = np.random.default_rng(89)
+    vocab = [2003 + 6 * i for i in range(16)]
+    hsh = orc.PleFp8Hash(vocab=vocab)
+    table = r.integers(0, 256, (hsh.rows, 160)).astype(np.uint8)
+    table[:, 5], table[:, 6] = 0x7F, 0xFF
+    path = tmp_path / "ple-fp8.gguf"
+    orc.write_ple_gguf(path, table, 1.375)
+    T = 96
+    ids = r.integers(0, 248320, T).astype(np.int32)
+    ids[11], ids[40] = 248044, -1
+    prev = (5, 6)
+    seq = list(prev) + [int(v) for v in ids]
+    rows = [orc.ple_fp8_row(seq[t + 2], seq[t + 1], seq[t], h, hsh) for t in range(T) for h in range(16)]
+    ref_rows, scale, _, _ = orc.ref_ple_src_rows(path, rows)
+    out = torch.empty((T, 16 * 160), dtype=torch.float32, device=DEV)
+    wz.ple_gather_fp8_f32(dev(table), 160, scale, wz.ple_fp8_hash(vocab=vocab), dev(ids), out, prev_ids=prev)
+    assert np.array_equal(host(out).reshape(T * 16, 160).view(np.uint32), ref_rows.view(np.uint32))

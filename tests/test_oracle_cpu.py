@@ -329,6 +329,31 @@ def test_ple_fp8_gather_decode_and_context(orc):
             assert np.array_equal(got.view(np.uint32), dec[row].view(np.uint32)), (t, h)
 
 
+def test_ple_fp8_decode_matches_reference_plesrc(orc, tmp_path):
+    """The oracle's fp8 PLE rows against the reference's own PleSrc (src/wzy_stage_v2.cuh:215-324),
+    built from its header into oracle/_ref: the table is written as a GGUF file that PleSrc::open parses
+    (scale key, tensor offset), and PleSrc::row decodes the rows the hash names. Bit-exact, including
+    the NaN codes (read as signed zero) and subnormals."""
+    if not orc.ref_available():
+        pytest.skip("oracle/_ref/libwzyref.so not built (needs the reference sources at build time)")
+    r = np.random.default_rng(88)
+    hsh = orc.PleFp8Hash(vocab=[1009 + 4 * i for i in range(16)])
+    table = r.integers(0, 256, (hsh.rows, 160)).astype(np.uint8)
+    table[:, 0], table[:, 1], table[:, 2] = 0x7F, 0xFF, 0x03  # NaN codes, a subnormal
+    path = tmp_path / "ple-fp8.gguf"
+    orc.write_ple_gguf(path, table, 0.6172)
+    T = 40
+    ids = r.integers(-1, 248320, T).astype(np.int32)
+    ids[7] = 248044
+    prev = (17, 248044)
+    seq = list(prev) + [int(v) for v in ids]
+    rows = [orc.ple_fp8_row(seq[t + 2], seq[t + 1], seq[t], h, hsh) for t in range(T) for h in range(16)]
+    ref_rows, scale, rb, nrows = orc.ref_ple_src_rows(path, rows)
+    assert rb == 160 and nrows == hsh.rows and scale == np.float32(0.6172)
+    got = orc.ple_gather_fp8_f32(table, 160, scale, hsh, ids, prev_ids=prev)
+    assert np.array_equal(got.reshape(T * 16, 160).view(np.uint32), ref_rows.view(np.uint32))
+
+
 def test_ple_gate_and_conv_against_numpy(orc):
     r = np.random.default_rng(52)
     T, n, hc = 5, 96, 4

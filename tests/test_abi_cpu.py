@@ -148,6 +148,11 @@ def test_argument_validation_before_any_cuda_call(wz):
     assert L.wzyb_swiglu_f16(A16, A16, A16, 0, NULL) == wz.OK
     assert L.wzyb_add_rmsnorm_f16(A16, A16, A16, A16, 0, 2048, 1e-6, 1.0, NULL) == wz.OK
     # tuning knobs
+    assert L.wzyb_attn_prep_f16(None, 4, NULL) == wz.ERR_NULL
+    assert L.wzyb_act_f16(None, 4, NULL) == wz.ERR_NULL
+    bad = wz.ActArgs()
+    bad.act_rows, bad.ffn = -1, 512
+    assert L.wzyb_act_f16(ctypes.byref(bad), 4, NULL) == wz.ERR_SHAPE
     assert L.wzyb_set_launch_tuning(9, 1, 0) == wz.ERR_VALUE
     assert L.wzyb_set_launch_tuning(0, 0, 0) == wz.ERR_VALUE
 

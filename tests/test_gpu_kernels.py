@@ -317,6 +317,53 @@ def test_bitwise_deterministic(wz):
     assert np.array_equal(outs[0], outs[1])
 
 
+def test_layer_bundles_match_oracle(wz, orc):
+    """The executor's bundle entry points (wzyb_attn_prep_f16: add+RMSNorm then q/k norm+RoPE;
+    wzyb_act_f16: SwiGLU over the expert rows then the GDN gated norm) -- the calls the end-to-end
+    measurement makes -- at the configs' shapes, against the oracle."""
+    import ctypes
+
+    r = rng(91)
+    T, n, hd, rot, off = 300, 2048, 256, 64, 17
+    x, res = f16n(r, (T, n)), f16n(r, (T, n))
+    w = f16n(r, (n,), 0.02)
+    q, k = f16n(r, (T, 16, hd)), f16n(r, (T, 2, hd))
+    gq, gk = f16n(r, (hd,), 0.02), f16n(r, (hd,), 0.02)
+    c, s, dc, ds = _rope_tab(orc, T + off, rot)
+    dx, dres, dw, dy = dev(x), dev(res), dev(w), torch.empty((T, n), dtype=torch.float16, device=DEV)
+    dq, dk, dgq, dgk = dev(q), dev(k), dev(gq), dev(gk)
+    a = wz.AttnPrepArgs()
+    a.x, a.residual, a.norm_weight, a.normed, a.hidden = dx.data_ptr(), dres.data_ptr(), dw.data_ptr(), dy.data_ptr(), n
+    a.q = wz.head_tensor(dq, dgq, 16, hd, 16 * hd)
+    a.k = wz.head_tensor(dk, dgk, 2, hd, 2 * hd)
+    a.head_dim, a.rot_dims = hd, rot
+    a.cos_tab, a.sin_tab, a.table_rows = dc.data_ptr(), ds.data_ptr(), T + off
+    a.d_base_pos, a.pos_offset, a.eps, a.w_offset = None, off, 1e-6, 1.0
+    wz.call("wzyb_attn_prep_f16", ctypes.byref(a), T, wz._stream())
+    y_ref, res_ref = orc.add_rmsnorm_f16(x, res, w, 1e-6, 1.0)
+    assert np.array_equal(host(dres), res_ref)
+    assert_f16_close(host(dy), y_ref, ULP_TOL, "bundle add+rmsnorm")
+    q_ref = orc.head_norm_rope(q.reshape(-1), gq, c, s, T, 16, hd, hd, 16 * hd, rot, 1e-6, 1.0, off)
+    k_ref = orc.head_norm_rope(k.reshape(-1), gk, c, s, T, 2, hd, hd, 2 * hd, rot, 1e-6, 1.0, off)
+    assert_f16_close(host(dq).reshape(-1), q_ref, ULP_TOL, "bundle q")
+    assert_f16_close(host(dk).reshape(-1), k_ref, ULP_TOL, "bundle k")
+
+    rows, ffn, H, ghd = 11 * T, 512, 32, 128
+    g, u = f16n(r, (rows, ffn), 2.0), f16n(r, (rows, ffn))
+    o, z = f16n(r, (T, H, ghd)), f16n(r, (T, H, ghd))
+    gm = f16n(r, (ghd,), 0.02, 1.0)
+    dg, du, dact = dev(g), dev(u), torch.empty((rows, ffn), dtype=torch.float16, device=DEV)
+    do, dz, dgm, dgy = dev(o), dev(z), dev(gm), torch.empty((T, H, ghd), dtype=torch.float16, device=DEV)
+    b = wz.ActArgs()
+    b.gate, b.up, b.act, b.act_rows, b.ffn = dg.data_ptr(), du.data_ptr(), dact.data_ptr(), rows, ffn
+    b.o, b.z, b.gdn_gamma, b.gdn_out = do.data_ptr(), dz.data_ptr(), dgm.data_ptr(), dgy.data_ptr()
+    b.gdn_heads, b.gdn_head_dim, b.eps, b.gdn_w_offset, b.gate_mode = H, ghd, 1e-6, 0.0, wz.GATE_SIGMOID
+    wz.call("wzyb_act_f16", ctypes.byref(b), T, wz._stream())
+    assert_f16_close(host(dact), orc.swiglu(g, u), ULP_TOL, "bundle swiglu")
+    assert_f16_close(host(dgy), orc.gdn_gated_norm(o, z, gm, T, H, ghd, 1e-6, 0.0, 0), ULP_TOL, "bundle gdn")
+    assert wz.read_faults() == 0
+
+
 @pytest.mark.parametrize("shards", [2, 8])
 def test_sharded_equals_unsharded(wz, orc, shards):
     """Each shard gets its row slice, a RoPE pos_offset = its first row, and a 2-id PLE halo."""

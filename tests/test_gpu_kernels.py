@@ -279,6 +279,24 @@ def test_embed_gather_bf16_f32(wz, orc):
     assert np.array_equal(host(out).view(np.uint32), want.view(np.uint32))
 
 
+@pytest.mark.parametrize("row_bytes", [16, 48, 160, 4112])
+@pytest.mark.parametrize("policy", [0, 1])
+def test_embed_gather_rows_any_width(wz, orc, row_bytes, policy):
+    """The generic byte-row gather at several row widths (one 16-byte chunk to 257), with out-of-range
+    ids under both policies and the device counter of out-of-range ids."""
+    r = rng(row_bytes + policy)
+    vocab = 3001
+    table = r.integers(0, 256, (vocab, row_bytes)).astype(np.uint8)
+    ids = r.integers(0, vocab, 517).astype(np.int32)
+    ids[[0, 100, 516]] = [-7, vocab, 1 << 30]
+    want, bad = orc.embed_gather_rows(table, ids, policy)
+    out = torch.empty((ids.size, row_bytes), dtype=torch.uint8, device=DEV)
+    cnt = torch.zeros(1, dtype=torch.int32, device=DEV)
+    wz.embed_gather_rows(dev(table), dev(ids), out, oob_policy=policy, oob_count=cnt)
+    assert np.array_equal(host(out), want)
+    assert int(host(cnt)[0]) == bad == 3
+
+
 @pytest.mark.parametrize("variant", [0, 1])
 def test_ple_gather_baseline_shape(wz, orc, variant):
     """configs[3] PLE: 16 fp16 tables [2^20, 128] ~N(0,0.02), 4096 uniform ids -> [4096, 2048]."""

@@ -377,6 +377,14 @@ def swiglu_interleaved(gu, out, T, nff, stream=None):
     call(fn, _ptr(gu), _ptr(out), T, nff, _stream(stream))
 
 
+def embed_gather_rows(table, ids, out, oob_policy=OOB_CLAMP, oob_count=None, stream=None):
+    """Row copy of a [vocab, row_bytes] byte view of any table (row_bytes % 16 == 0)."""
+    vocab = table.shape[0]
+    row_bytes = table[0].numel() * table.element_size()
+    call("wzyb_embed_gather_rows", _ptr(table), vocab, row_bytes, _ptr(ids), ids.numel(), _ptr(out), oob_policy,
+         _ptr(oob_count), _stream(stream))
+
+
 def embed_gather_f16(table, ids, out, oob_policy=OOB_CLAMP, oob_count=None, stream=None):
     vocab, hidden = table.shape
     call("wzyb_embed_gather_f16", _ptr(table), vocab, hidden, _ptr(ids), ids.numel(), _ptr(out), oob_policy,

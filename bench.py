@@ -409,6 +409,10 @@ def measure_decode(wz, torch, dev, reps=200):
                                                          pos_offset=5, stream=s),
             "k_rope_kv_append": lambda: wz.k_rope_kv_append(kk, gq, vv, cos, sin, T, 2, HD, cache, rot_dims=ROT,
                                                             pos_offset=5, stream=s),
+            # q and k norm + RoPE and the INT8 append as one launch (the two rows above, fused)
+            "qk_rope_kv_append": lambda: wz.k_rope_kv_append(kk, gq, vv, cos, sin, T, 2, HD, cache, rot_dims=ROT,
+                                                             pos_offset=5, stream=s,
+                                                             q=wz.head_tensor(qg, gq, 24, 2 * HD, 48 * HD)),
             "gr_write": lambda: wz.gr_write_f32(R, bo, inj, T, NE, HC, stream=s),
             "swiglu_q8": lambda: wz.swiglu_q8_f32(sff, sup, q8, s8, stream=s),
         }

@@ -195,6 +195,21 @@ int wzyb_k_rope_kv_append_f32(float* k, const float* k_gamma, const float* v, co
                               const float* sin_tab, int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset,
                               int64_t T, int kv_heads, int head_dim, int rot_dims, float eps, float w_offset,
                               const wzyb_kv_cache* cache, wzyb_stream_t stream);
+/* The same with the token's q heads normed and rotated in place in the same launch (their own gamma
+ * and strides in *q, e.g. the reference's q interleaved with its gate, head_stride = 2*head_dim): the
+ * reference's three launches -- fused_head_norm_rope_multi on q and on k, then kv_append_int8_multi
+ * (src/wzy_stage_v2.cuh:638-655, src/wzy_prefill_tc.cuh:862-878) -- as one. q->data and q->gamma
+ * have the element type of k. */
+int wzyb_qk_rope_kv_append_f32(const wzyb_head_tensor* q, float* k, const float* k_gamma, const float* v,
+                               const float* cos_tab, const float* sin_tab, int64_t table_rows,
+                               const int32_t* d_base_pos, int64_t pos_offset, int64_t T, int kv_heads, int head_dim,
+                               int rot_dims, float eps, float w_offset, const wzyb_kv_cache* cache,
+                               wzyb_stream_t stream);
+int wzyb_qk_rope_kv_append_f16(const wzyb_head_tensor* q, uint16_t* k, const uint16_t* k_gamma, const uint16_t* v,
+                               const float* cos_tab, const float* sin_tab, int64_t table_rows,
+                               const int32_t* d_base_pos, int64_t pos_offset, int64_t T, int kv_heads, int head_dim,
+                               int rot_dims, float eps, float w_offset, const wzyb_kv_cache* cache,
+                               wzyb_stream_t stream);
 int wzyb_k_rope_kv_append_f16(uint16_t* k, const uint16_t* k_gamma, const uint16_t* v, const float* cos_tab,
                               const float* sin_tab, int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset,
                               int64_t T, int kv_heads, int head_dim, int rot_dims, float eps, float w_offset,

@@ -148,6 +148,8 @@ def test_argument_validation_before_any_cuda_call(wz):
     assert L.wzyb_swiglu_f16(A16, A16, A16, 0, NULL) == wz.OK
     assert L.wzyb_add_rmsnorm_f16(A16, A16, A16, A16, 0, 2048, 1e-6, 1.0, NULL) == wz.OK
     # tuning knobs
+    assert L.wzyb_qk_rope_kv_append_f32(None, A16, A16, A16, A16, A16, 64, NULL, 0, 4, 2, 256, 64, 1e-6, 1.0,
+                                        None, NULL) == wz.ERR_NULL
     assert L.wzyb_attn_prep_f16(None, 4, NULL) == wz.ERR_NULL
     assert L.wzyb_act_f16(None, 4, NULL) == wz.ERR_NULL
     bad = wz.ActArgs()

@@ -593,6 +593,46 @@ def test_k_rope_kv_append_fused(wz, orc, dtype, T, heads, hd, base):
     assert wz.read_faults() == 0
 
 
+@pytest.mark.parametrize("dtype", [np.float16, np.float32])
+@pytest.mark.parametrize("T,base", [(1, 700), (8, 0), (4096, 3)])
+def test_qk_rope_kv_append_one_launch(wz, orc, dtype, T, base):
+    """q norm + RoPE (the reference's q layout: 24 heads interleaved with their gates, head_stride =
+    2*hd) in the same launch as the k norm + RoPE + INT8 KV append: q against the oracle, the gate halves
+    untouched, and k and the cache bit-identical to the k-only entry point's."""
+    r = rng(T * 7 + base)
+    heads, hd, qh, rot, cap, max_ctx = 2, 256, 24, 64, 32768, 8192
+    kvd = heads * hd
+    k = r.standard_normal((T, kvd)).astype(dtype)
+    v = r.standard_normal((T, kvd)).astype(dtype)
+    kg = (0.02 * r.standard_normal(hd)).astype(dtype)
+    qbuf = r.standard_normal((T, qh, 2 * hd)).astype(dtype)
+    qg = (0.02 * r.standard_normal(hd)).astype(dtype)
+    c_, s_, dc, ds = _rope_tab(orc, base + T + 8, rot)
+    # k-only launch
+    cache1, d1 = _kv_seeded(orc, rng(5), cap, max_ctx, kvd, True)
+    dk1 = dev(k)
+    wz.k_rope_kv_append(dk1, dev(kg), dev(v), dc, ds, T, heads, hd, _kv_desc(wz, d1, cap, max_ctx, True),
+                        rot_dims=rot, eps=1e-6, w_offset=1.0, pos_offset=base)
+    # q + k + append in one launch
+    cache2, d2 = _kv_seeded(orc, rng(5), cap, max_ctx, kvd, True)
+    dk2, dq, dqg = dev(k), dev(qbuf), dev(qg)
+    wz.k_rope_kv_append(dk2, dev(kg), dev(v), dc, ds, T, heads, hd, _kv_desc(wz, d2, cap, max_ctx, True),
+                        rot_dims=rot, eps=1e-6, w_offset=1.0, pos_offset=base,
+                        q=wz.head_tensor(dq, dqg, qh, 2 * hd, 2 * qh * hd))
+    assert np.array_equal(host(dk2), host(dk1))
+    for nm in ["rkq", "rks", "rvq", "rvs", "fkq", "fks", "fvq", "fvs"]:
+        assert np.array_equal(_kv_host(d2, nm), _kv_host(d1, nm)), nm
+    want = orc.head_norm_rope(qbuf.reshape(-1), qg, c_, s_, T, qh, hd, 2 * hd, 2 * qh * hd, rot, 1e-6, 1.0,
+                              base).reshape(T, qh, 2 * hd)
+    got = host(dq)
+    assert np.array_equal(got[..., hd:], qbuf[..., hd:])  # gates untouched
+    if dtype == np.float16:
+        assert_f16_close(got[..., :hd].reshape(-1), want[..., :hd].reshape(-1), ULP_TOL, "q")
+    else:
+        np.testing.assert_allclose(got[..., :hd], want[..., :hd], rtol=1e-5, atol=1e-5)
+    assert wz.read_faults() == 0
+
+
 # ---------------------------------------------------------------------------------------------
 # the reference model's PLE: fp8 rows by the n-gram hash, gate, causal conv
 # ---------------------------------------------------------------------------------------------

@@ -42,6 +42,12 @@ struct KvAppendArgs {
     float w_offset;
     int norm_rope;
     wzyb_kv_cache c;
+    // optional q heads, normed and rotated in place in the same launch (q_heads == 0: none)
+    void* q;
+    const void* q_gamma;
+    int q_heads;
+    int64_t q_head_stride;  // elements between heads of a token
+    int64_t q_row_stride;   // elements between tokens
 };
 
 __device__ __forceinline__ bool kv_in_ring(int64_t p, int64_t end, int64_t cap) {
@@ -114,7 +120,9 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
     const int64_t end = base + a.T;
     const int rounds = (a.kv_heads + HPW - 1) / HPW;
     const int groups = (rounds + kR - 1) / kR;
-    const int64_t items = a.T * groups;
+    const int q_rounds = (a.q_heads + HPW - 1) / HPW;
+    const int per_tok = groups + (q_rounds + kR - 1) / kR;  // k/v items, then q items
+    const int64_t items = a.T * per_tok;
     T* const kd = static_cast<T*>(a.k);
     const T* const vd = static_cast<const T*>(a.v);
 
@@ -126,10 +134,71 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) g[i] = fadd2(splat2(a.w_offset), g[i]);
     }
+    // cos/sin of position pos for this lane's 8 dims (the first rotary half with -sin)
+    auto load_cos_sin = [&](int64_t pos, float2 (&c2)[4], float2 (&s2)[4]) {
+        Vec8<float>::load_ro2(a.cos_tab + pos * half + ci, c2);
+        Vec8<float>::load_ro2(a.sin_tab + pos * half + ci, s2);
+        if (first_half) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) s2[i] = make_float2(-s2[i].x, -s2[i].y);
+        }
+    };
+    // p *= rsqrt(mean(p^2) + eps) * gamma, then the pair rotation (one shuffle per element)
+    auto norm_rotate = [&](float2 (&p)[4], const float2 (&gm)[4], bool rot, const float2 (&c2)[4],
+                           const float2 (&s2)[4]) {
+        const float ss = group_sum<L>(sumsq8(p));
+        const float2 sc = splat2(rsqrt_approx(ss / (float)HD + a.eps));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) p[i] = fmul2(p[i], fmul2(sc, gm[i]));
+        float2 q[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            q[i].x = __shfl_sync(0xffffffffu, p[i].x, src);
+            q[i].y = __shfl_sync(0xffffffffu, p[i].y, src);
+        }
+        if (rot) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) p[i] = ffma2(q[i], s2[i], fmul2(p[i], c2[i]));
+        }
+    };
 
-    StridePos ps(gwarp, nwarps, groups);  // item = (token q, round group r)
+    StridePos ps(gwarp, nwarps, per_tok);  // item = (token q, round group r)
     for (int64_t it = gwarp; it < items; it += nwarps, ps.advance()) {
         const int64_t t = ps.q;
+        if (ps.r >= groups) {  // q heads of this token: norm + rotation in place, nothing appended
+            const int q0 = (ps.r - groups) * kR;
+            T* const qrow = static_cast<T*>(a.q) + t * a.q_row_stride;
+            typename Vec8<T>::Raw qr[kR];
+#pragma unroll
+            for (int j = 0; j < kR; ++j) {
+                const int h = (q0 + j) * HPW + hw;
+                if (q0 + j < q_rounds && h < a.q_heads) qr[j] = Vec8<T>::ldcs_raw(qrow + h * a.q_head_stride + li * 8);
+            }
+            float2 gq[4];
+            Vec8<T>::load_ro2(static_cast<const T*>(a.q_gamma) + li * 8, gq);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) gq[i] = fadd2(splat2(a.w_offset), gq[i]);
+            const int64_t pos = base + t;
+            const bool pos_ok = half > 0 && pos >= 0 && pos < a.table_rows;
+            float2 c2[4], s2[4];
+            if (pos_ok && rot_lane) load_cos_sin(pos, c2, s2);
+#pragma unroll
+            for (int j = 0; j < kR; ++j) {
+                if (q0 + j >= q_rounds) break;  // warp-uniform
+                const int h = (q0 + j) * HPW + hw;
+                const bool act = h < a.q_heads;
+                float2 p[4];
+                if (act) {
+                    Vec8<T>::cvt2(qr[j], p);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) p[i] = splat2(0.f);
+                }
+                norm_rotate(p, gq, pos_ok && rot_lane, c2, s2);
+                if (act) Vec8<T>::store2(qrow + h * a.q_head_stride + li * 8, p);
+            }
+            continue;
+        }
         const int r0 = ps.r * kR;
         typename Vec8<T>::Raw kr[kR], vr[kR];
 #pragma unroll
@@ -148,14 +217,7 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
         const bool pos_ok = half > 0 && pos >= 0 && pos < a.table_rows;
         float2 c2[4], s2[4];
         if (a.norm_rope) {
-            if (pos_ok && rot_lane) {
-                Vec8<float>::load_ro2(a.cos_tab + pos * half + ci, c2);
-                Vec8<float>::load_ro2(a.sin_tab + pos * half + ci, s2);
-                if (first_half) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) s2[i] = make_float2(-s2[i].x, -s2[i].y);
-                }
-            }
+            if (pos_ok && rot_lane) load_cos_sin(pos, c2, s2);
             if (half > 0 && !pos_ok && lane == 0 && r0 == 0) raise_fault(WZYB_FAULT_POS_RANGE);
         }
 #pragma unroll
@@ -173,21 +235,7 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
                 for (int i = 0; i < 4; ++i) p[i] = v[i] = splat2(0.f);
             }
             if (a.norm_rope) {
-                // p *= rsqrt(mean(p^2) + eps) * gamma, then the pair rotation (one shuffle per element)
-                const float ss = group_sum<L>(sumsq8(p));
-                const float2 sc = splat2(rsqrt_approx(ss / (float)HD + a.eps));
-#pragma unroll
-                for (int i = 0; i < 4; ++i) p[i] = fmul2(p[i], fmul2(sc, g[i]));
-                float2 q[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    q[i].x = __shfl_sync(0xffffffffu, p[i].x, src);
-                    q[i].y = __shfl_sync(0xffffffffu, p[i].y, src);
-                }
-                if (pos_ok && rot_lane) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) p[i] = ffma2(q[i], s2[i], fmul2(p[i], c2[i]));
-                }
+                norm_rotate(p, g, pos_ok && rot_lane, c2, s2);
                 if (act) Vec8<T>::store2(kd + off, p);
             }
             if (keep) {  // warp-uniform
@@ -222,15 +270,27 @@ static int launch_kv_append(const KvAppendArgs& a0, int head_dim, cudaStream_t s
         return WZYB_ERR_ALIGN;
     if (((uintptr_t)c.ring_k_s | (uintptr_t)c.ring_v_s | (uintptr_t)c.full_k_s | (uintptr_t)c.full_v_s) & 1)
         return WZYB_ERR_ALIGN;
+    if (a.q_heads > 0) {  // the fused q heads (norm_rope only)
+        if (!a.norm_rope || !a.q || !a.q_gamma) return WZYB_ERR_NULL;
+        if (a.q_heads > 256 || (a.q_heads > 1 && a.q_head_stride < head_dim) || a.q_head_stride < 0 ||
+            a.q_row_stride < 0)
+            return WZYB_ERR_SHAPE;
+        if (!aligned16(a.q) || !aligned16(a.q_gamma) || ((a.q_head_stride * (int64_t)sizeof(T)) % 16) != 0 ||
+            ((a.q_row_stride * (int64_t)sizeof(T)) % 16) != 0)
+            return WZYB_ERR_ALIGN;
+    } else if (a.q_heads < 0) {
+        return WZYB_ERR_SHAPE;
+    }
     if (a.T == 0) return WZYB_OK;
     DeviceInfo di;
     const int rc = device_info(&di);
     if (rc != WZYB_OK) return rc;
     const int hpw = 32 / (head_dim / 8);
     const int64_t rounds = (a.kv_heads + hpw - 1) / hpw;
+    const int64_t q_rounds = (a.q_heads + hpw - 1) / hpw;
     // one round per warp while the call is smaller than a few warps per SM, else two
-    const bool split = a.T * rounds <= (int64_t)di.sms * 32;
-    const int64_t items = split ? a.T * rounds : a.T * ((rounds + 1) / 2);
+    const bool split = a.T * (rounds + q_rounds) <= (int64_t)di.sms * 32;
+    const int64_t items = split ? a.T * (rounds + q_rounds) : a.T * ((rounds + 1) / 2 + (q_rounds + 1) / 2);
     const int grid = persistent_grid(di, 8, (items + 7) / 8);
 #define WZYB_KV(HDV)                                                                              \
     if (split) launch_k(kv_append_kernel<T, HDV, 1>, grid, 256, 0, stream, a);                          \
@@ -248,9 +308,14 @@ template <typename T>
 static int kv_append_entry(T* k, const T* k_gamma, const T* v, const float* cos_tab, const float* sin_tab,
                            int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset, int64_t T_, int kv_heads,
                            int head_dim, int rot_dims, float eps, float w_offset, int norm_rope,
-                           const wzyb_kv_cache* cache, cudaStream_t stream) {
+                           const wzyb_kv_cache* cache, cudaStream_t stream, const wzyb_head_tensor* q = nullptr) {
     if (cache == nullptr) return WZYB_ERR_NULL;
     KvAppendArgs a;
+    a.q = q ? q->data : nullptr;
+    a.q_gamma = q ? q->gamma : nullptr;
+    a.q_heads = q ? q->heads : 0;
+    a.q_head_stride = q ? q->head_stride : 0;
+    a.q_row_stride = q ? q->row_stride : 0;
     a.k = k;
     a.k_gamma = k_gamma;
     a.v = v;
@@ -286,6 +351,27 @@ int wzyb_k_rope_kv_append_f32(float* k, const float* k_gamma, const float* v, co
                               const wzyb_kv_cache* cache, wzyb_stream_t stream) {
     return wzyb::kv_append_entry<float>(k, k_gamma, v, cos_tab, sin_tab, table_rows, d_base_pos, pos_offset, T,
                                         kv_heads, head_dim, rot_dims, eps, w_offset, 1, cache, (cudaStream_t)stream);
+}
+
+int wzyb_qk_rope_kv_append_f32(const wzyb_head_tensor* q, float* k, const float* k_gamma, const float* v,
+                               const float* cos_tab, const float* sin_tab, int64_t table_rows,
+                               const int32_t* d_base_pos, int64_t pos_offset, int64_t T, int kv_heads, int head_dim,
+                               int rot_dims, float eps, float w_offset, const wzyb_kv_cache* cache,
+                               wzyb_stream_t stream) {
+    if (q == nullptr) return WZYB_ERR_NULL;
+    return wzyb::kv_append_entry<float>(k, k_gamma, v, cos_tab, sin_tab, table_rows, d_base_pos, pos_offset, T,
+                                        kv_heads, head_dim, rot_dims, eps, w_offset, 1, cache, (cudaStream_t)stream, q);
+}
+
+int wzyb_qk_rope_kv_append_f16(const wzyb_head_tensor* q, uint16_t* k, const uint16_t* k_gamma, const uint16_t* v,
+                               const float* cos_tab, const float* sin_tab, int64_t table_rows,
+                               const int32_t* d_base_pos, int64_t pos_offset, int64_t T, int kv_heads, int head_dim,
+                               int rot_dims, float eps, float w_offset, const wzyb_kv_cache* cache,
+                               wzyb_stream_t stream) {
+    if (q == nullptr) return WZYB_ERR_NULL;
+    return wzyb::kv_append_entry<__half>((__half*)k, (const __half*)k_gamma, (const __half*)v, cos_tab, sin_tab,
+                                         table_rows, d_base_pos, pos_offset, T, kv_heads, head_dim, rot_dims, eps,
+                                         w_offset, 1, cache, (cudaStream_t)stream, q);
 }
 
 int wzyb_k_rope_kv_append_f16(uint16_t* k, const uint16_t* k_gamma, const uint16_t* v, const float* cos_tab,

@@ -140,6 +140,16 @@ _SIGS = {
         c_int,
         [P, P, P, P, P, c_int64, P, c_int64, c_int64, c_int, c_int, c_int, c_float, c_float, POINTER(KvCache), S],
     ),
+    "wzyb_qk_rope_kv_append_f32": (
+        c_int,
+        [POINTER(HeadTensor), P, P, P, P, P, c_int64, P, c_int64, c_int64, c_int, c_int, c_int, c_float, c_float,
+         POINTER(KvCache), S],
+    ),
+    "wzyb_qk_rope_kv_append_f16": (
+        c_int,
+        [POINTER(HeadTensor), P, P, P, P, P, c_int64, P, c_int64, c_int64, c_int, c_int, c_int, c_float, c_float,
+         POINTER(KvCache), S],
+    ),
     "wzyb_head_norm_rope_f16": (
         c_int,
         [P, P, P, P, c_int64, P, c_int64, c_int64, c_int, c_int, c_int64, c_int64, c_int, c_float, c_float, S],
@@ -350,11 +360,17 @@ def kv_append_int8_f32(k, v, T, kv_heads, head_dim, cache: KvCache, d_base_pos=N
 
 
 def k_rope_kv_append(k, k_gamma, v, cos_tab, sin_tab, T, kv_heads, head_dim, cache: KvCache, rot_dims=64, eps=1e-6,
-                     w_offset=0.0, d_base_pos=None, pos_offset=0, stream=None):
-    fn = "wzyb_k_rope_kv_append_f16" if k.element_size() == 2 else "wzyb_k_rope_kv_append_f32"
+                     w_offset=0.0, d_base_pos=None, pos_offset=0, stream=None, q: HeadTensor | None = None):
+    """k norm + RoPE + INT8 KV append; with q (a HeadTensor of the same element type) the q heads are
+    normed and rotated in the same launch."""
+    f16 = k.element_size() == 2
     rows = cos_tab.numel() // max(1, rot_dims // 2) if cos_tab is not None else 0
-    call(fn, _ptr(k), _ptr(k_gamma), _ptr(v), _ptr(cos_tab), _ptr(sin_tab), rows, _ptr(d_base_pos), pos_offset, T,
-         kv_heads, head_dim, rot_dims, eps, w_offset, ctypes.byref(cache), _stream(stream))
+    args = (_ptr(k), _ptr(k_gamma), _ptr(v), _ptr(cos_tab), _ptr(sin_tab), rows, _ptr(d_base_pos), pos_offset, T,
+            kv_heads, head_dim, rot_dims, eps, w_offset, ctypes.byref(cache), _stream(stream))
+    if q is not None:
+        call("wzyb_qk_rope_kv_append_f16" if f16 else "wzyb_qk_rope_kv_append_f32", ctypes.byref(q), *args)
+    else:
+        call("wzyb_k_rope_kv_append_f16" if f16 else "wzyb_k_rope_kv_append_f32", *args)
 
 
 def rope_table(cos_tab, sin_tab, rows, rot_dims=64, theta=1e7, stream=None):

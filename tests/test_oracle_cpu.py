@@ -466,3 +466,22 @@ def test_block_quantisers_against_numpy(orc):
     rr = np.where(sf > 0, gs / np.where(sf > 0, sf, 1), 0).astype(np.float32)
     codes = np.array([L.or_f2e2m1(float(v)) for v in (g16 * rr[:, None]).astype(np.float32).reshape(-1)], np.uint8)
     assert np.array_equal(s4, sc) and np.array_equal(q4, codes[0::2] | (codes[1::2] << 4))
+
+
+@pytest.mark.parametrize("rows,scols", [(1, 1), (200, 3), (129, 80), (256, 160), (77, 33)])
+def test_tiled_scale_layout_helper(rows, scols):
+    """The GPU tests' relayout of row-major scales into the 128x4-tiled MMA operand layout (built from
+    reshapes) equals the layout's byte formula: tile (row // 128, col // 4) at ((row // 128) *
+    ceil(scols / 4) + col // 4) * 512, and (r % 32) * 16 + (r % 128 // 32) * 4 + col % 4 inside it."""
+    from test_gpu_kernels import _to_blocked
+
+    sc = (np.arange(rows * scols) % 251).astype(np.uint8).reshape(rows, scols)
+    blk = _to_blocked(sc)
+    ncb = -(-scols // 4)
+    assert blk.size == -(-rows // 128) * 128 * ncb * 4
+    r, c = np.meshgrid(np.arange(rows), np.arange(scols), indexing="ij")
+    off = ((r // 128) * ncb + c // 4) * 512 + (r % 32) * 16 + (r % 128 // 32) * 4 + c % 4
+    assert np.array_equal(blk[off], sc)
+    pad = np.ones(blk.size, bool)
+    pad[off.reshape(-1)] = False
+    assert (blk[pad] == 0xAB).all()

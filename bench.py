@@ -1,19 +1,22 @@
 """Benchmark of the B200 per-layer fused elementwise path (libwzyb200.so).
 
-One "step" = one pass of the layer bundle of BASELINE configs[1]+[2] over this rank's token shard
-of configs[4] (262,144 tokens, token-sharded across the GPUs with no collective):
-    residual add + zero-centred RMSNorm  [T, 2048]
-    q/k RMSNorm + partial RoPE           q [T, 16, 256], k [T, 2, 256], rot 64, theta 1e7
-    SwiGLU                               [11*T, 512]   (10 routed + 1 shared expert rows per token)
-    GDN gated RMSNorm                    o, z [T, 32, 128]
+One "step" = one pass of the layer bundles of BASELINE configs[1]+[2] over this rank's token shard of
+configs[4] (262,144 tokens, token-sharded across the GPUs with no collective), through the public
+bundle entry points, one kernel launch each:
+    wzyb_attn_prep_f16: residual add + zero-centred RMSNorm [T, 2048], and q/k RMSNorm + partial RoPE
+                        q [T, 16, 256], k [T, 2, 256], rot 64, theta 1e7 (host-built table)
+    wzyb_act_f16:       SwiGLU [11*T, 512] (10 routed + 1 shared expert rows per token), and the GDN
+                        gated RMSNorm o, z [T, 32, 128]
 Inputs are larger than L2 (~24 GB per step on one GPU), so no L2 flush is needed between steps; with
 --tokens small enough that a shard's step moves under 4x L2 (e.g. 4096 tokens on 2+ GPUs), L2 is
 flushed before every step and the step is timed from its first kernel to its last.
-Per-kernel numbers at the 4096-token configs[1]/[2]/[3] shapes are measured separately with the
-L2 flushed before every launch.
+Rank 0 also measures, with L2 flushed before every launch: the 4096-token bundles of configs[1], [2]
+and [3] (k4096) and their ops as separate launches, the reference-model kernels (f8), the decode-sized
+launches (dec) and configs[0] on the GPU (c0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl wzyb|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl wzyb|reference] [--tokens T]
     torchrun --nproc-per-node N bench.py --gpus N ...
+    python bench.py --profile-case NAME [--tokens T] [--steps R]   (one small case for an ncu capture)
 
 Rank 0 prints ONE JSON line.
 """
@@ -46,23 +49,32 @@ EXPERT_ROWS = 11  # 10 routed + 1 shared expert rows per token
 FFN = 512
 GDN_H, GDN_HD = 32, 128
 EPS = 1e-6
+VOCAB, PLE_HEADS, PLE_ROWS, PLE_HD = 151936, 16, 1 << 20, 128
 
 # Algorithmic bytes per token (each tensor read once, each output written once; weights separate).
 BYTES_PER_TOKEN = {
-    "add_rmsnorm": 4 * HIDDEN * 2,                       # x, res read; res, y written
-    "qk_norm_rope": 2 * (QH + KH) * HD * 2,              # q, k read + written in place
-    "swiglu": 3 * EXPERT_ROWS * FFN * 2,                 # gate, up read; act written
-    "gdn_gated_norm": 3 * GDN_H * GDN_HD * 2,            # o, z read; y written
+    "norm": 4 * HIDDEN * 2,                      # x, res read; res, y written
+    "qk": 2 * (QH + KH) * HD * 2,                # q, k read + written in place
+    "swi": 3 * EXPERT_ROWS * FFN * 2,            # gate, up read; act written
+    "gdn": 3 * GDN_H * GDN_HD * 2,               # o, z read; y written
+    "emb": 2 * HIDDEN * 2 + 4,                   # row read + written, id
+    "ple": 2 * PLE_HEADS * PLE_HD * 2 + 4,       # 16 rows read + written, id
 }
-WEIGHT_BYTES = {"add_rmsnorm": HIDDEN * 2, "qk_norm_rope": 2 * HD * 2, "swiglu": 0, "gdn_gated_norm": GDN_HD * 2}
+WEIGHT_BYTES = {"norm": HIDDEN * 2, "qk": 2 * HD * 2, "swi": 0, "gdn": GDN_HD * 2, "emb": 0, "ple": 0}
+BUNDLES = {"attn_b": ("norm", "qk"), "act_b": ("swi", "gdn"), "gath_b": ("emb", "ple")}
+STEP_BUNDLES = ["attn_b", "act_b"]
 ROPE_TABLE_BYTES_PER_TOKEN = ROT // 2 * 4 * 2  # cos + sin row per position (reported separately)
-KERNELS = ["add_rmsnorm", "qk_norm_rope", "swiglu", "gdn_gated_norm"]
 
-# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per token of the dominant kernel, from
-# one ncu capture of a 32,768-token launch (profiles/layer_kernels_32768_ncu_full.md), scaled by the
-# tokens of a launch: reads scale exactly; writes are slightly under-counted at that size because the
-# tail of the output is still in L2 when the kernel ends.
-NCU_TRAFFIC_PER_TOKEN = {"swiglu": 32101}
+
+def bundle_bytes(name, T):
+    return sum(T * BYTES_PER_TOKEN[o] + WEIGHT_BYTES[o] for o in BUNDLES[name])
+
+
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per token of the dominant kernel (the act
+# bundle), from one ncu capture of a 32,768-token launch, scaled by the tokens of a launch: reads scale
+# exactly; writes are slightly under-counted at that size because the tail of the output is still in L2
+# when the kernel ends. None until a capture of the current kernel exists.
+NCU_TRAFFIC_PER_TOKEN = {"act_b": None}
 
 
 def peaks():
@@ -125,10 +137,39 @@ class ClockSampler:
 # ------------------------------------------------------------------------------------------------
 # GPU arm
 # ------------------------------------------------------------------------------------------------
-class Shard:
-    """Device buffers of one rank's token shard and the four launches of one step."""
+def rope_tables(wz, torch, rows, dev):
+    """RoPE cos/sin [rows, 32] built on the host by the reference's own procedure
+    (build_rope_cos_sin_host), uploaded once."""
+    c, s = wz.rope_table_host(rows, ROT, THETA)
+    return torch.from_numpy(c).to(dev), torch.from_numpy(s).to(dev)
 
-    def __init__(self, wz, torch, n, row0, seed, dev):
+
+def attn_args(wz, x, res, w, y, q, k, gq, gk, cos, sin, pos_offset):
+    a = wz.AttnPrepArgs()
+    a.x, a.residual, a.norm_weight, a.normed = x.data_ptr(), res.data_ptr(), w.data_ptr(), y.data_ptr()
+    a.hidden = HIDDEN
+    a.q = wz.head_tensor(q, gq, QH, HD, QH * HD)
+    a.k = wz.head_tensor(k, gk, KH, HD, KH * HD)
+    a.head_dim, a.rot_dims = HD, ROT
+    a.cos_tab, a.sin_tab, a.table_rows = cos.data_ptr(), sin.data_ptr(), cos.shape[0]
+    a.d_base_pos, a.pos_offset = None, pos_offset
+    a.eps, a.w_offset = EPS, 1.0
+    return a
+
+
+def act_args(wz, gate, up, act, rows, o, z, gg, gy):
+    b = wz.ActArgs()
+    b.gate, b.up, b.act, b.act_rows, b.ffn = gate.data_ptr(), up.data_ptr(), act.data_ptr(), rows, FFN
+    b.o, b.z, b.gdn_gamma, b.gdn_out = o.data_ptr(), z.data_ptr(), gg.data_ptr(), gy.data_ptr()
+    b.gdn_heads, b.gdn_head_dim = GDN_H, GDN_HD
+    b.eps, b.gdn_w_offset, b.gate_mode = EPS, 0.0, wz.GATE_SIGMOID
+    return b
+
+
+class Shard:
+    """Device buffers of one rank's token shard and the two bundle launches of one step."""
+
+    def __init__(self, wz, torch, n, row0, seed, dev, cos, sin):
         self.wz, self.torch, self.n, self.row0 = wz, torch, n, row0
         g = torch.Generator(device=dev).manual_seed(seed)
         f16 = torch.float16
@@ -146,27 +187,26 @@ class Shard:
         self.o, self.z = randn((n, GDN_H, GDN_HD)), randn((n, GDN_H, GDN_HD))
         self.gg = randn((GDN_HD,), 0.02, 1.0)
         self.gy = torch.empty((n, GDN_H, GDN_HD), dtype=f16, device=dev)
-        # RoPE table for every position of the sequence (built once on the device in fp64)
-        self.cos = torch.empty((TOKENS, ROT // 2), dtype=torch.float32, device=dev)
-        self.sin = torch.empty_like(self.cos)
-        wz.rope_table(self.cos, self.sin, TOKENS, ROT, THETA)
-        self.qt = wz.head_tensor(self.q, self.gq, QH, HD, QH * HD)
-        self.kt = wz.head_tensor(self.k, self.gk, KH, HD, KH * HD)
+        self.cos, self.sin = cos, sin
+        self.a = attn_args(wz, self.x, self.res, self.w, self.y, self.q, self.k, self.gq, self.gk, cos, sin, row0)
+        self.b = act_args(wz, self.gate, self.up, self.act, n * EXPERT_ROWS, self.o, self.z, self.gg, self.gy)
+        self.ops = {  # the ops of each bundle as separate launches (k4096 breakdown)
+            "norm": lambda s: wz.add_rmsnorm_f16(self.x, self.res, self.w, self.y, EPS, 1.0, stream=s),
+            "qk": lambda s: wz.qk_norm_rope_f16(self.a.q, self.a.k, cos, sin, n, HD, ROT, EPS, 1.0,
+                                                pos_offset=row0, stream=s),
+            "swi": lambda s: wz.swiglu(self.gate, self.up, self.act, stream=s),
+            "gdn": lambda s: wz.gdn_gated_norm(self.o, self.z, self.gg, self.gy, n, GDN_H, GDN_HD, EPS, 0.0,
+                                               wz.GATE_SIGMOID, stream=s),
+        }
 
     def launch(self, i, s):
-        wz, n = self.wz, self.n
         if i == 0:
-            wz.add_rmsnorm_f16(self.x, self.res, self.w, self.y, EPS, 1.0, stream=s)
-        elif i == 1:
-            wz.qk_norm_rope_f16(self.qt, self.kt, self.cos, self.sin, n, HD, ROT, EPS, 1.0, pos_offset=self.row0,
-                                stream=s)
-        elif i == 2:
-            wz.swiglu(self.gate, self.up, self.act, stream=s)
+            self.wz.call("wzyb_attn_prep_f16", ctypes.byref(self.a), self.n, ctypes.c_void_p(s.cuda_stream))
         else:
-            wz.gdn_gated_norm(self.o, self.z, self.gg, self.gy, n, GDN_H, GDN_HD, EPS, 0.0, wz.GATE_SIGMOID, stream=s)
+            self.wz.call("wzyb_act_f16", ctypes.byref(self.b), self.n, ctypes.c_void_p(s.cuda_stream))
 
 
-def run_e2e(wz, torch, n, row0, dev, steps, chunk=16384):
+def run_e2e(wz, torch, n, row0, dev, steps, cos, sin, chunk=16384):
     """Same workload through the public bundle entry points (wzyb_attn_prep_f16, wzyb_act_f16) with
     HOST buffers: every step copies each chunk's inputs H2D from pinned host memory and its outputs
     D2H to pinned host memory, on two streams so copies of one chunk overlap compute of the other.
@@ -197,9 +237,6 @@ def run_e2e(wz, torch, n, row0, dev, steps, chunk=16384):
     gq = (torch.randn(HD, device=dev) * 0.02).to(f16)
     gk = (torch.randn(HD, device=dev) * 0.02).to(f16)
     gg = (torch.randn(GDN_HD, device=dev) * 0.02 + 1).to(f16)
-    cos = torch.empty((TOKENS, ROT // 2), dtype=torch.float32, device=dev)
-    sin = torch.empty_like(cos)
-    wz.rope_table(cos, sin, TOKENS, ROT, THETA)
     torch.cuda.synchronize()
 
     def one_step():
@@ -212,24 +249,9 @@ def run_e2e(wz, torch, n, row0, dev, steps, chunk=16384):
                 for k, _ in specs_in:
                     b[k][:m].copy_(hin[k][p0:p0 + m], non_blocking=True)
                     in_bytes += hin[k][p0:p0 + m].nbytes
-                a = wz.AttnPrepArgs()
-                a.x, a.residual, a.norm_weight, a.normed = (b["x"].data_ptr(), b["res"].data_ptr(), w.data_ptr(),
-                                                            b["y"].data_ptr())
-                a.hidden = HIDDEN
-                a.q = wz.head_tensor(b["q"], gq, QH, HD, QH * HD)
-                a.k = wz.head_tensor(b["k"], gk, KH, HD, KH * HD)
-                a.head_dim, a.rot_dims = HD, ROT
-                a.cos_tab, a.sin_tab, a.table_rows = cos.data_ptr(), sin.data_ptr(), TOKENS
-                a.d_base_pos, a.pos_offset = None, row0 + c0
-                a.eps, a.w_offset = EPS, 1.0
+                a = attn_args(wz, b["x"], b["res"], w, b["y"], b["q"], b["k"], gq, gk, cos, sin, row0 + c0)
                 wz.call("wzyb_attn_prep_f16", ctypes.byref(a), m, ctypes.c_void_p(s.cuda_stream))
-                act = wz.ActArgs()
-                act.gate, act.up, act.act = b["gate"].data_ptr(), b["up"].data_ptr(), b["act"].data_ptr()
-                act.act_rows, act.ffn = m * EXPERT_ROWS, FFN
-                act.o, act.z, act.gdn_gamma, act.gdn_out = (b["o"].data_ptr(), b["z"].data_ptr(), gg.data_ptr(),
-                                                            b["gy"].data_ptr())
-                act.gdn_heads, act.gdn_head_dim = GDN_H, GDN_HD
-                act.eps, act.gdn_w_offset, act.gate_mode = EPS, 0.0, wz.GATE_SIGMOID
+                act = act_args(wz, b["gate"], b["up"], b["act"], m * EXPERT_ROWS, b["o"], b["z"], gg, b["gy"])
                 wz.call("wzyb_act_f16", ctypes.byref(act), m, ctypes.c_void_p(s.cuda_stream))
                 for k, _ in specs_out:
                     hout[k][p0:p0 + m].copy_(b[k][:m], non_blocking=True)
@@ -250,25 +272,71 @@ def run_e2e(wz, torch, n, row0, dev, steps, chunk=16384):
     return statistics.median(times), ib, ob
 
 
-def measure_kernels_4096(wz, torch, dev, peak, reps=60):
-    """configs[1]/[2]/[3] shapes at 4096 tokens, L2 flushed (256 MB write) before every launch."""
-    T = 4096
-    sh = Shard(wz, torch, T, 0, 99, dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    flush_r = torch.ones(256 << 20, dtype=torch.uint8, device=dev)
-    gen = torch.Generator(device=dev).manual_seed(5)
-    table = (torch.randn((151936, HIDDEN), generator=gen, device=dev) * 0.02).half()
-    ids = torch.randint(0, 151936, (T,), generator=gen, device=dev, dtype=torch.int32)
-    emb = torch.empty((T, HIDDEN), dtype=torch.float16, device=dev)
-    ple_tabs = [(torch.randn((1 << 20, 128), generator=gen, device=dev) * 0.02).half() for _ in range(16)]
-    ple = torch.empty((T, 16 * 128), dtype=torch.float16, device=dev)
-    extra = {
-        "embed_gather": (lambda s: wz.embed_gather_f16(table, ids, emb, stream=s), T * HIDDEN * 2 * 2 + T * 4),
-        "ple_gather": (lambda s: wz.ple_gather_f16(ple_tabs, ids, ple, stream=s), T * 16 * 256 + T * 2048 * 2 + T * 4),
-    }
-    # the reference model's 4-stream residual (n_embd 2560): gated write, stream mixing, and the
-    # Q8_0-quantising norm and SwiGLU, at the same 4096 tokens
+class Flushed:
+    """Event timing of single launches with L2 flushed before each: a 256 MB write, then a 256 MB read
+    so the write-back of the flush's dirty lines is not charged to the timed launch."""
+
+    def __init__(self, torch, dev, reps=60):
+        self.torch, self.reps = torch, reps
+        self.flush_w = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        self.flush_r = torch.ones(256 << 20, dtype=torch.uint8, device=dev)
+        self.s = torch.cuda.current_stream()
+
+    def time(self, fn):
+        # CUDA event timestamps advance in ~2 us steps on this platform; a trimmed mean over many
+        # flushed launches (start phases vary) resolves durations below that step
+        torch, s, ts = self.torch, self.s, []
+        for r in range(self.reps + 3):
+            self.flush_w.fill_(r & 0xFF)
+            self.flush_r.sum(dtype=torch.int32)
+            # keep the stream busy while the host enqueues e0 + the launch, so no host gap is timed
+            torch.cuda._sleep(200000)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            fn(s)
+            e1.record(s)
+            e1.synchronize()
+            if r >= 3:
+                ts.append(e0.elapsed_time(e1) * 1e3)
+        ts.sort()
+        cut = len(ts) // 10
+        return statistics.mean(ts[cut:len(ts) - cut])
+
+    def copy_us(self, nbytes, dev):
+        """Size-matched yardstick: a plain device copy moving the same bytes (half read, half written)."""
+        src = self.torch.empty(nbytes // 4, dtype=self.torch.float16, device=dev)
+        dst = self.torch.empty_like(src)
+        us = self.time(lambda s: dst.copy_(src))
+        del src, dst
+        return us
+
+
+class Gathers:
+    """the token table and the 16 PLE tables with 4096 uniform ids."""
+
+    def __init__(self, wz, torch, dev, T=4096):
+        gen = torch.Generator(device=dev).manual_seed(5)
+        self.table = (torch.randn((VOCAB, HIDDEN), generator=gen, device=dev) * 0.02).half()
+        self.ids = torch.randint(0, VOCAB, (T,), generator=gen, device=dev, dtype=torch.int32)
+        self.emb = torch.empty((T, HIDDEN), dtype=torch.float16, device=dev)
+        self.tabs = [(torch.randn((PLE_ROWS, PLE_HD), generator=gen, device=dev) * 0.02).half()
+                     for _ in range(PLE_HEADS)]
+        self.ple = torch.empty((T, PLE_HEADS * PLE_HD), dtype=torch.float16, device=dev)
+        self.args = wz.embed_ple_args(self.table, self.tabs, self.ids, self.emb, self.ple)
+        self.T = T
+        self.ops = {
+            "emb": lambda s: wz.embed_gather_f16(self.table, self.ids, self.emb, stream=s),
+            "ple": lambda s: wz.ple_gather_f16(self.tabs, self.ids, self.ple, stream=s),
+        }
+        self.bundle = lambda s: wz.embed_ple_f16(self.args, T, stream=s)
+
+
+def f8_jobs(wz, torch, dev, T=4096):
+    """The reference model's own kernels (SURVEY next rows: quantisation epilogue, 4-stream residual,
+    INT8 KV append, fp8 PLE and its block) at 4096 tokens: name -> (launch, algorithmic bytes)."""
+    gen = torch.Generator(device=dev).manual_seed(6)
     NE, HC = 2560, 4
+    rows = T * HC * NE
     R = torch.randn((T * HC, NE), generator=gen, device=dev)
     blk = torch.randn((T, NE), generator=gen, device=dev)
     inj = torch.randn((T * HC,), generator=gen, device=dev)
@@ -283,8 +351,6 @@ def measure_kernels_4096(wz, torch, dev, peak, reps=60):
     g32, u32 = torch.randn(nq, generator=gen, device=dev), torch.randn(nq, generator=gen, device=dev)
     q32, s32 = torch.empty(nq, dtype=torch.int8, device=dev), torch.empty(nq // 32, device=dev)
     q16b, s16b = torch.empty(nq, dtype=torch.int8, device=dev), torch.empty(nq // 16, device=dev)
-    rows = T * HC * NE
-    # k norm + RoPE fused with the INT8 KV append (fp16 k, v [T, 2 x 256]; ring + full-context mirror)
     KVD = KH * HD
     kk16 = torch.randn((T, KVD), generator=gen, device=dev).half()
     vv16 = torch.randn((T, KVD), generator=gen, device=dev).half()
@@ -292,15 +358,10 @@ def measure_kernels_4096(wz, torch, dev, peak, reps=60):
     kv_planes = [torch.zeros((T, KVD), dtype=torch.int8, device=dev) if i % 2 == 0 else
                  torch.zeros((T, KVD // 64), dtype=torch.int16, device=dev) for i in range(8)]
     kvc = wz.kv_cache(*kv_planes[:4], T, T, *kv_planes[4:])  # ring of T cells: every token lands in it
-    kv_tab = (torch.empty((T, ROT // 2), device=dev), torch.empty((T, ROT // 2), device=dev))
-    wz.rope_table(kv_tab[0], kv_tab[1], T, ROT, THETA)
-    extra["k_rope_kv_append"] = (
-        lambda s: wz.k_rope_kv_append(kk16, kg16, vv16, kv_tab[0], kv_tab[1], T, KH, HD, kvc, rot_dims=ROT, eps=EPS,
-                                      w_offset=1.0, stream=s),
-        T * KVD * 2 * 3 + T * KVD * 4 + T * (KVD // 64) * 2 * 4 + HD * 2)
-    # the reference model's PLE: full fp8 table (320,001,446 rows x 160 B = 51.2 GB) by its n-gram hash,
-    # then the gate and the causal conv at the block's widths (n_embd 2560 x 4 streams, HCD 10240)
+    kv_tab = rope_tables(wz, torch, T, dev)
+    ids = torch.randint(0, VOCAB, (T,), generator=gen, device=dev, dtype=torch.int32)
     ple8_hash = wz.ple_fp8_hash()
+    # the reference's full fp8 table: 320,001,446 rows x 160 B = 51.2 GB
     ple8 = torch.randint(0, 256, (320001446, 160), generator=gen, device=dev, dtype=torch.uint8)
     ple8_out = torch.empty((T, 2560), device=dev)
     pk = torch.randn((T * HC, NE), generator=gen, device=dev)
@@ -308,79 +369,101 @@ def measure_kernels_4096(wz, torch, dev, peak, reps=60):
     pgv = torch.empty((T * HC, NE), device=dev)
     pcw = 0.5 * torch.randn((HC * NE, 4), generator=gen, device=dev)
     phist = torch.randn((HC * NE, 9), generator=gen, device=dev)
-    extra["ple_gather_fp8"] = (
-        lambda s: wz.ple_gather_fp8_f32(ple8, 160, 0.5, ple8_hash, ids, ple8_out, stream=s),
-        T * 16 * 160 + T * 2560 * 4 + T * 4)
-    extra["ple_gate_hc4"] = (lambda s: wz.ple_gate_f32(pk, pq, blk, pgv, T, NE, HC, stream=s),
-                             rows * 12 + T * NE * 4)
-    extra["ple_conv"] = (lambda s: wz.ple_conv_f32(xn32, pcw, phist, pgv, R, T, HC * NE, stream=s),
-                         rows * 16 + HC * NE * (4 + 9 + 9) * 4)
-    extra.update({
-        "gr_write_hc4": (lambda s: wz.gr_write_f32(R, blk, inj, T, NE, HC, stream=s), rows * 8 + T * NE * 4 + T * HC * 4),
-        "hc_mix_hc4": (lambda s: wz.hc_mix(xn16, gg16, mx, mx16, T, NE, HC, stream=s), rows * 4 + T * NE * 6),
-        "gr_norm_hc4": (lambda s: wz.gr_norm_f32(R, wn, blk, inj, xn32, T, NE, HC, stream=s),
-                        rows * (8 + 4) + T * NE * 4 + T * HC * 4 + HC * NE * 4),
-        "gr_norm_q8_hc4": (lambda s: wz.gr_norm_q8_f32(R, wn, blk, inj, xn32, xq8, xs8, T, NE, HC, stream=s),
-                           rows * (8 + 4 + 1) + rows // 8 + T * NE * 4 + T * HC * 4 + HC * NE * 4),
-        "swiglu_q8": (lambda s: wz.swiglu_q8_f32(g32, u32, q32, s32, stream=s), nq * (8 + 1) + nq // 8),
-        "quant_act_q32_q16": (lambda s: wz.quant_act_f32(g32, q32, s32, q16b, s16b, nq // FFN, FFN, stream=s),
-                              nq * (4 + 1 + 1) + nq // 32 * 4 + nq // 16 * 4),
-        "quant_act_mxfp8": (lambda s: wz.quant_act_block(g32, q16b, s16b, nq // FFN, FFN, fmt="mxfp8", stream=s),
-                            nq * (4 + 1) + nq // 32),
-        "swiglu_nvfp4": (lambda s: wz.swiglu_block(g32, u32, q16b, s16b, fmt="nvfp4", global_scale=1.0, stream=s),
-                         nq * 8 + nq // 2 + nq // 16),
-    })
-    s = torch.cuda.current_stream()
-
-    def timed(fn):
-        # CUDA event timestamps advance in ~2 us steps on this platform; a trimmed mean over many
-        # flushed launches (start phases vary) resolves durations below that step
-        ts = []
-        for r in range(reps + 3):
-            # flush L2: write a buffer larger than L2, then read another one so that the dirty lines
-            # of the write are written back here and not inside the timed kernel
-            flush.fill_(r & 0xFF)
-            flush_r.sum(dtype=torch.int32)
-            # keep the stream busy while the host enqueues e0 + the launch, so no host gap is timed
-            torch.cuda._sleep(200000)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(s)
-            fn(s)
-            e1.record(s)
-            e1.synchronize()
-            if r >= 3:
-                ts.append(e0.elapsed_time(e1) * 1e3)
-        ts.sort()
-        cut = len(ts) // 10
-        return statistics.mean(ts[cut:len(ts) - cut])
-
-    res = {}
-    jobs = [(k, (lambda s, i=i: sh.launch(i, s)), T * BYTES_PER_TOKEN[k] + WEIGHT_BYTES[k])
-            for i, k in enumerate(KERNELS)]
-    jobs += [(k, f, b) for k, (f, b) in extra.items()]
-    for name, fn, nbytes in jobs:
-        us = timed(fn)
-        # size-matched yardstick: a plain device copy moving the same bytes (half read, half written),
-        # timed the same way; at tens of MB it is itself far below the large-copy peak
-        src = torch.empty(nbytes // 4, dtype=torch.float16, device=dev)
-        dst = torch.empty_like(src)
-        copy_us = timed(lambda s: dst.copy_(src))
-        del src, dst
-        gbs = nbytes / (us * 1e-6) / 1e9
-        res[name] = {"us": round(us, 2), "bytes": int(nbytes), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
-                     "frac_of_8tbs": round(gbs / NOMINAL_HBM_GBS, 4), "copy_us": round(copy_us, 2),
-                     "frac_of_copy": round(copy_us / us, 4)}
-    del table, ple_tabs, flush, flush_r, R, blk, xn16, gg16, xn32, g32, u32, ple8, pk, pq, pgv
-    return res
+    keep = [R, blk, inj, wn, xn16, gg16, mx, mx16, xn32, xq8, xs8, g32, u32, q32, s32, q16b, s16b, kk16, vv16, kg16,
+            kv_planes, kv_tab, ids, ple8, ple8_out, pk, pq, pgv, pcw, phist]
+    jobs = {
+        "kv": (lambda s: wz.k_rope_kv_append(kk16, kg16, vv16, kv_tab[0], kv_tab[1], T, KH, HD, kvc, rot_dims=ROT,
+                                             eps=EPS, w_offset=1.0, stream=s),
+               T * KVD * 2 * 3 + T * KVD * 4 + T * (KVD // 64) * 2 * 4 + HD * 2),
+        "ple8": (lambda s: wz.ple_gather_fp8_f32(ple8, 160, 0.5, ple8_hash, ids, ple8_out, stream=s),
+                 T * 16 * 160 + T * 2560 * 4 + T * 4),
+        "gate": (lambda s: wz.ple_gate_f32(pk, pq, blk, pgv, T, NE, HC, stream=s), rows * 12 + T * NE * 4),
+        "conv": (lambda s: wz.ple_conv_f32(xn32, pcw, phist, pgv, R, T, HC * NE, stream=s),
+                 rows * 16 + HC * NE * (4 + 9 + 9) * 4),
+        "grw": (lambda s: wz.gr_write_f32(R, blk, inj, T, NE, HC, stream=s), rows * 8 + T * NE * 4 + T * HC * 4),
+        "mix": (lambda s: wz.hc_mix(xn16, gg16, mx, mx16, T, NE, HC, stream=s), rows * 4 + T * NE * 6),
+        "grn": (lambda s: wz.gr_norm_f32(R, wn, blk, inj, xn32, T, NE, HC, stream=s),
+                rows * (8 + 4) + T * NE * 4 + T * HC * 4 + HC * NE * 4),
+        "grq8": (lambda s: wz.gr_norm_q8_f32(R, wn, blk, inj, xn32, xq8, xs8, T, NE, HC, stream=s),
+                 rows * (8 + 4 + 1) + rows // 8 + T * NE * 4 + T * HC * 4 + HC * NE * 4),
+        "swq8": (lambda s: wz.swiglu_q8_f32(g32, u32, q32, s32, stream=s), nq * (8 + 1) + nq // 8),
+        "q8": (lambda s: wz.quant_act_f32(g32, q32, s32, q16b, s16b, nq // FFN, FFN, stream=s),
+               nq * (4 + 1 + 1) + nq // 32 * 4 + nq // 16 * 4),
+        "mx8": (lambda s: wz.quant_act_block(g32, q16b, s16b, nq // FFN, FFN, fmt="mxfp8", stream=s),
+                nq * (4 + 1) + nq // 32),
+        "nv4": (lambda s: wz.swiglu_block(g32, u32, q16b, s16b, fmt="nvfp4", global_scale=1.0, stream=s),
+                nq * 8 + nq // 2 + nq // 16),
+    }
+    return jobs, keep
 
 
-def measure_decode(wz, torch, dev, reps=200):
-    """Decode-window sizes (T = 1 and 8 tokens, the reference model's widths): device time per launch
-    with the data resident in L2, as in a decode step. The launches are captured into a CUDA graph
-    (the reference records its decode windows the same way), so the host's launch cost is not timed."""
+def measure_4096(wz, torch, dev, peak, cos, sin):
+    """configs[1]/[2]/[3] at 4096 tokens, L2 flushed before every launch: each bundle in one launch
+    [us, frac of peak, frac of a size-matched copy] and its ops as separate launches [us, frac]; then
+    the reference-model kernels (f8)."""
+    T = 4096
+    fl = Flushed(torch, dev)
+    sh = Shard(wz, torch, T, 0, 99, dev, cos, sin)
+    ga = Gathers(wz, torch, dev, T)
+    k4096 = {}
+    for name, fn in (("attn_b", lambda s: sh.launch(0, s)), ("act_b", lambda s: sh.launch(1, s)),
+                     ("gath_b", ga.bundle)):
+        nb = bundle_bytes(name, T)
+        us = fl.time(fn)
+        gbs = nb / (us * 1e-6) / 1e9
+        k4096[name] = [round(us, 2), round(gbs / peak, 3), round(fl.copy_us(nb, dev) / us, 3)]
+    ops = dict(sh.ops)
+    ops.update(ga.ops)
+    for name in ("norm", "qk", "swi", "gdn", "emb", "ple"):
+        nb = T * BYTES_PER_TOKEN[name] + WEIGHT_BYTES[name]
+        us = fl.time(ops[name])
+        k4096[name] = [round(us, 2), round(nb / (us * 1e-6) / 1e9 / peak, 3)]
+    del sh, ga
+    torch.cuda.empty_cache()
+    jobs, keep = f8_jobs(wz, torch, dev, T)
+    f8 = {}
+    for name, (fn, nb) in jobs.items():
+        us = fl.time(fn)
+        f8[name] = [round(us, 2), round(nb / (us * 1e-6) / 1e9 / peak, 3)]
+    del jobs, keep, fl
+    torch.cuda.empty_cache()
+    return k4096, f8
+
+
+def graph_us(torch, fn, reps=200):
+    """Device time per launch of `fn` captured `reps` times into a CUDA graph and replayed (the
+    reference records its decode windows the same way), so the host's launch cost is not timed."""
+    for _ in range(20):  # first calls cache occupancy and attributes outside the capture
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(reps):
+            fn()
+    graph.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(5):
+        graph.replay()
+    e1.record()
+    e1.synchronize()
+    del graph
+    return round(e0.elapsed_time(e1) * 1e3 / (5 * reps), 2)
+
+
+def measure_decode(wz, torch, dev):
+    """Decode-window sizes: configs[0] (1 token x 2048, add + zero-centred RMSNorm) and the reference
+    model's widths at T = 1 and 8, device time per launch with the data resident in L2."""
     NE, HC, KVD, NFF = 2560, 4, 512, 640
     g = torch.Generator(device=dev).manual_seed(11)
     s = None  # the wrappers launch on the current stream (the capture stream inside the graph)
+    x1 = torch.randn((1, HIDDEN), generator=g, device=dev).half()
+    r1 = torch.randn((1, HIDDEN), generator=g, device=dev).half()
+    w1 = (0.02 * torch.randn(HIDDEN, generator=g, device=dev)).half()
+    y1 = torch.empty((1, HIDDEN), dtype=torch.float16, device=dev)
+    c0_us = graph_us(torch, lambda: wz.add_rmsnorm_f16(x1, r1, w1, y1, EPS, 1.0, stream=s))
+    cos, sin = rope_tables(wz, torch, 64, dev)
     out = {}
     for T in (1, 8):
         R = torch.randn((T * HC, NE), generator=g, device=dev)
@@ -392,8 +475,6 @@ def measure_decode(wz, torch, dev, reps=200):
         xs = torch.empty((T * HC, NE // 32), device=dev)
         qg = torch.randn((T, 24, 2 * HD), generator=g, device=dev)
         gq = 1 + 0.02 * torch.randn(HD, generator=g, device=dev)
-        cos, sin = torch.empty((64, ROT // 2), device=dev), torch.empty((64, ROT // 2), device=dev)
-        wz.rope_table(cos, sin, 64, ROT, THETA)
         kk = torch.randn((T, KVD), generator=g, device=dev)
         vv = torch.randn((T, KVD), generator=g, device=dev)
         planes = [torch.zeros((64, KVD), dtype=torch.int8, device=dev) if i % 2 == 0 else
@@ -404,51 +485,37 @@ def measure_decode(wz, torch, dev, reps=200):
         q8 = torch.empty(NFF * T, dtype=torch.int8, device=dev)
         s8 = torch.empty(NFF * T // 32, device=dev)
         jobs = {
-            "gr_norm_q8": lambda: wz.gr_norm_q8_f32(R, wn, bo, inj, xn, xq, xs, T, NE, HC, stream=s),
-            "q_norm_rope_f32": lambda: wz.head_norm_rope(qg, gq, cos, sin, T, 24, HD, 2 * HD, 48 * HD, ROT, EPS, 0.0,
-                                                         pos_offset=5, stream=s),
-            "k_rope_kv_append": lambda: wz.k_rope_kv_append(kk, gq, vv, cos, sin, T, 2, HD, cache, rot_dims=ROT,
-                                                            pos_offset=5, stream=s),
+            "grq8": lambda: wz.gr_norm_q8_f32(R, wn, bo, inj, xn, xq, xs, T, NE, HC, stream=s),
+            "qrope": lambda: wz.head_norm_rope(qg, gq, cos, sin, T, 24, HD, 2 * HD, 48 * HD, ROT, EPS, 0.0,
+                                               pos_offset=5, stream=s),
+            "kv": lambda: wz.k_rope_kv_append(kk, gq, vv, cos, sin, T, 2, HD, cache, rot_dims=ROT, pos_offset=5,
+                                              stream=s),
             # q and k norm + RoPE and the INT8 append as one launch (the two rows above, fused)
-            "qk_rope_kv_append": lambda: wz.k_rope_kv_append(kk, gq, vv, cos, sin, T, 2, HD, cache, rot_dims=ROT,
-                                                             pos_offset=5, stream=s,
-                                                             q=wz.head_tensor(qg, gq, 24, 2 * HD, 48 * HD)),
-            "gr_write": lambda: wz.gr_write_f32(R, bo, inj, T, NE, HC, stream=s),
-            "swiglu_q8": lambda: wz.swiglu_q8_f32(sff, sup, q8, s8, stream=s),
+            "qkkv": lambda: wz.k_rope_kv_append(kk, gq, vv, cos, sin, T, 2, HD, cache, rot_dims=ROT, pos_offset=5,
+                                                stream=s, q=wz.head_tensor(qg, gq, 24, 2 * HD, 48 * HD)),
+            "grw": lambda: wz.gr_write_f32(R, bo, inj, T, NE, HC, stream=s),
+            "swq8": lambda: wz.swiglu_q8_f32(sff, sup, q8, s8, stream=s),
         }
         for name, fn in jobs.items():
-            for _ in range(20):  # first calls cache occupancy and attributes outside the capture
-                fn()
-            torch.cuda.synchronize()
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                for _ in range(reps):
-                    fn()
-            graph.replay()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            torch.cuda.synchronize()
-            e0.record()
-            for _ in range(5):
-                graph.replay()
-            e1.record()
-            e1.synchronize()
-            out.setdefault(name, {})[f"T{T}_us"] = round(e0.elapsed_time(e1) * 1e3 / (5 * reps), 2)
-            del graph
-    return out
+            out.setdefault(name, []).append(graph_us(torch, fn))
+    return c0_us, out
 
 
+# ------------------------------------------------------------------------------------------------
+# CPU baseline (rank 0, N = 1) and the reference arm: the oracle port on the host cores
+# ------------------------------------------------------------------------------------------------
 class CpuBundle:
     """The oracle (a scalar C port of the reference math, OpenMP over rows) running the same
-    configs[1]+[2] bundle on T tokens of host memory, in place, with every host thread."""
+    configs[1]+[2] bundle on T tokens of host memory, in place, with `threads` host threads."""
 
     def __init__(self, T=4096, threads=None):
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as orc
 
+        self.orc = orc
         self.L = orc.lib()
         self.T = T
         self.threads = threads or os.cpu_count() or 1
-        orc.set_threads(self.threads)
         r = np.random.default_rng(3)
         f = lambda shape, std=1.0, mean=0.0: (r.standard_normal(shape) * std + mean).astype(np.float16)  # noqa: E731
         self.x, self.res, self.y = f((T, HIDDEN)), f((T, HIDDEN)), np.empty((T, HIDDEN), np.float16)
@@ -461,6 +528,7 @@ class CpuBundle:
         self.gy = np.empty_like(self.o)
 
     def run(self):
+        self.orc.set_threads(self.threads)
         L, T, P = self.L, self.T, (lambda a: a.ctypes.data)
         L.or_add_rmsnorm_f16(P(self.x), P(self.res), P(self.w), P(self.y), T, HIDDEN, EPS, 1.0)
         L.or_head_norm_rope_f16(P(self.q), P(self.gq), P(self.cos), P(self.sin), T, 0, T, QH, HD, HD, QH * HD, ROT,
@@ -471,9 +539,9 @@ class CpuBundle:
         L.or_gdn_gated_norm_f16(P(self.o), P(self.z), P(self.gg), P(self.gy), T, GDN_H, GDN_HD, EPS, 0.0, 0)
 
 
-def cpu_baseline(T=4096, target_s=12.0):
-    """Bounded sample of the workload on the host cores: the T-token bundle repeated for ~target_s."""
-    b = CpuBundle(T)
+def cpu_rate(T, threads, target_s):
+    """tokens/s of the oracle bundle on T tokens repeated for ~target_s with `threads` threads."""
+    b = CpuBundle(T, threads)
     b.run()
     reps, t0 = 0, time.perf_counter()
     while True:
@@ -482,11 +550,221 @@ def cpu_baseline(T=4096, target_s=12.0):
         el = time.perf_counter() - t0
         if el >= target_s or reps >= 100000:
             break
-    return {"value": round(T * reps / el, 1), "unit": "tokens/s", "cores": b.threads, "kind": "port",
-            "sample": f"configs[1]+[2] bundle on {T} tokens x {reps} reps ({el:.1f} s): oracle C port of the "
-                      f"reference math, OpenMP over rows, {b.threads} threads"}
+    return round(T * reps / el, 1), reps, el, b.threads
 
 
+def cpu_decode_us(threads, reps=20000):
+    """configs[0] on the host: median wall time of one decode-step add + RMSNorm (1 x 2048), scalar C
+    code timed per call with CLOCK_MONOTONIC; `threads` > 1 runs the OpenMP row loop (one row, so only
+    its fork/join cost is added)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+
+    r = np.random.default_rng(4)
+    x = r.standard_normal((1, HIDDEN)).astype(np.float16)
+    res = r.standard_normal((1, HIDDEN)).astype(np.float16)
+    w = (0.02 * r.standard_normal(HIDDEN)).astype(np.float16)
+    if threads == 1:
+        return round(float(np.median(orc.time_add_rmsnorm_f16(x, res, w, reps))) / 1e3, 3)
+    orc.set_threads(threads)
+    y = np.empty_like(res)
+    L, P = orc.lib(), (lambda a: a.ctypes.data)
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter_ns()
+        L.or_add_rmsnorm_f16(P(x), P(res), P(w), P(y), 1, HIDDEN, EPS, 1.0)
+        ts.append(time.perf_counter_ns() - t0)
+    return round(float(np.median(ts)) / 1e3, 3)
+
+
+def cpu_baseline():
+    """Bounded sample of the workload on the host cores: the 4096-token bundle for ~12 s on every host
+    thread, a 1024-token sample on one thread, and configs[0] (>= 10^4 single-token calls)."""
+    n = os.cpu_count() or 1
+    v, reps, el, thr = cpu_rate(4096, n, 12.0)
+    v1, reps1, el1, _ = cpu_rate(1024, 1, 5.0)
+    return {"value": v, "unit": "tokens/s", "cores": thr, "kind": "port",
+            "sample": f"configs[1]+[2] bundle, 4096 tokens x {reps} reps ({el:.0f} s), oracle C port, OpenMP "
+                      f"{thr} threads; value_1t: 1024 tokens x {reps1} on 1 thread",
+            "value_1t": v1, "c0_us_1t": cpu_decode_us(1), f"c0_us_{n}t": cpu_decode_us(n)}
+
+
+def reference_gpu(peak):
+    """The reference's own kernels (compiled from its sources into oracle/_ref/libwzyref.so) on this
+    GPU at the configs[1]/[2] shapes, 4096 tokens, in the reference's own types (fp32 inputs; fp16
+    outputs where its prefill kernels write them) and launch shapes, L2 flushed before every launch:
+    name -> [us, GB/s of the reference's own bytes, frac of peak]."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    import torch
+
+    if not torch.cuda.is_available():
+        return {"unavailable": "no GPU"}
+    if not orc.ref_available():
+        return {"unavailable": "oracle/_ref/libwzyref.so not built (needs the reference sources at build time)"}
+    R = orc.ref_lib()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    T = 4096
+    g = torch.Generator(device=dev).manual_seed(21)
+    f32 = lambda *shape: torch.randn(shape, generator=g, device=dev)  # noqa: E731
+    fl = Flushed(torch, dev)
+    P = lambda t: ctypes.c_void_p(t.data_ptr() if t is not None else 0)  # noqa: E731
+    S = lambda s: ctypes.c_void_p(s.cuda_stream)  # noqa: E731
+    res, x, w = f32(T, HIDDEN), f32(T, HIDDEN), 1 + 0.02 * f32(HIDDEN)
+    y16 = torch.empty((T, HIDDEN), dtype=torch.float16, device=dev)
+    q, k, gq, gk = f32(T, QH, HD), f32(T, KH, HD), 1 + 0.02 * f32(HD), 1 + 0.02 * f32(HD)
+    c, s_ = orc.ref_rope_table(T, THETA)
+    cos, sin = torch.from_numpy(c).to(dev), torch.from_numpy(s_).to(dev)
+    base = torch.zeros(1, dtype=torch.int32, device=dev)
+    gu = f32(T * EXPERT_ROWS, 2 * FFN)
+    act16 = torch.empty((T * EXPERT_ROWS, FFN), dtype=torch.float16, device=dev)
+    o, z, gg = f32(T, GDN_H, GDN_HD), f32(T, GDN_H, GDN_HD), 1 + 0.02 * f32(GDN_HD)
+    gy16 = torch.empty((T, GDN_H, GDN_HD), dtype=torch.float16, device=dev)
+    jobs = {
+        # pf_gr_norm_fp16: R and bo fp32 read, R fp32 written, xn fp16 written
+        "norm": (lambda st: R.ref_pf_gr_norm_fp16(P(res), P(w), P(x), None, P(y16), T, HIDDEN, 1, EPS, S(st)),
+                 T * HIDDEN * (4 + 4 + 4 + 2)),
+        # fused_head_norm_rope_multi on q, then on k (fp32 in place)
+        "qk": (lambda st: (R.ref_fused_head_norm_rope_multi(P(q), P(gq), P(cos), P(sin), P(base), T, QH, HD, HD,
+                                                             QH * HD, EPS, S(st)),
+                           R.ref_fused_head_norm_rope_multi(P(k), P(gk), P(cos), P(sin), P(base), T, KH, HD, HD,
+                                                             KH * HD, EPS, S(st))),
+               T * (QH + KH) * HD * 8),
+        # pf_silu_mul_interleaved_to_fp16: rows [gate | up] fp32 -> fp16
+        "swi": (lambda st: R.ref_pf_silu_mul_interleaved_to_fp16(P(gu), P(act16), T * EXPERT_ROWS, FFN, S(st)),
+                T * EXPERT_ROWS * FFN * (8 + 2)),
+        # pf_gdn_rmsnorm_gate_parallel: o, z fp32 -> y fp16
+        "gdn": (lambda st: R.ref_pf_gdn_rmsnorm_gate_parallel(P(o), P(z), P(gg), P(gy16), T, GDN_H, EPS, S(st)),
+                T * GDN_H * GDN_HD * (4 + 4 + 2)),
+    }
+    out = {}
+    for name, (fn, nb) in jobs.items():
+        us = fl.time(fn)
+        gbs = nb / (us * 1e-6) / 1e9
+        out[name] = [round(us, 2), round(gbs, 1), round(gbs / peak, 3)]
+    out["attn_sum_us"] = round(out["norm"][0] + out["qk"][0], 2)
+    out["act_sum_us"] = round(out["swi"][0] + out["gdn"][0], 2)
+    return out
+
+
+def reference_arm(args, rank, peak):
+    """The reference's path: no standalone implementation of the norms, RoPE or SwiGLU exists in it
+    other than CUDA kernels, so rank 0 times the oracle port (its C restatement) on this host's cores;
+    other ranks exit without work. Its own GPU kernels are timed beside it (reference_gpu)."""
+    if rank != 0:
+        return
+    # each step: the bundle on a bounded token sample, sized so K steps stay within ~2 minutes
+    T = 4096 if args.steps <= 200 else max(256, (4096 * 200 // args.steps) // 64 * 64)
+    b = CpuBundle(T)
+    for _ in range(args.warmup):
+        b.run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        b.run()
+    el = time.perf_counter() - t0
+    value = round(T * args.steps / el, 1)
+    v1, _, _, _ = cpu_rate(1024, 1, 5.0)
+    cb = {"value": value, "unit": "tokens/s", "cores": b.threads, "kind": "port",
+          "sample": f"each step = configs[1]+[2] bundle on {T} of the 262,144 tokens (oracle C port of the "
+                    f"reference math, OpenMP {b.threads} threads); {args.steps} steps in {el:.1f} s",
+          "value_1t": v1}
+    try:
+        rg = reference_gpu(peak)
+    except Exception as e:  # the CPU arm stands on its own
+        rg = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "fp16 I/O, fp32 math", "data": "synthetic (seeded normal / uniform ids)",
+        "config": {"workload": "configs[4]: configs[1]+[2] bundle at 262,144 tokens (CPU: bounded sample)"},
+        "cpu_baseline": cb, "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                    "d2h_bytes_per_step": 0},
+        "reference_gpu": rg,
+    }), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------
+# single-kernel cases for ncu captures
+# ------------------------------------------------------------------------------------------------
+def profile_case(wz, torch, name, T, reps):
+    """Run one small case `reps` times (a few GB on the device at most) so ncu can capture one kernel."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    wz.check("wzyb_prepare_device", wz.lib().wzyb_prepare_device())
+    s = torch.cuda.current_stream()
+    if name in ("attn_b", "act_b", "norm", "qk", "swi", "gdn"):
+        cos, sin = rope_tables(wz, torch, T, dev)
+        sh = Shard(wz, torch, T, 0, 1, dev, cos, sin)
+        fn = {"attn_b": lambda: sh.launch(0, s), "act_b": lambda: sh.launch(1, s)}.get(name)
+        fn = fn or (lambda: sh.ops[name](s))
+    elif name in ("gath_b", "emb", "ple"):
+        ga = Gathers(wz, torch, dev, T)
+        fn = (lambda: ga.bundle(s)) if name == "gath_b" else (lambda: ga.ops[name](s))
+    else:
+        if name == "ple8":
+            # a 2 GB table of the reference's row format instead of the 51.2 GB one (capture size)
+            gen = torch.Generator(device=dev).manual_seed(1)
+            vocab = [800011 + 2 * i for i in range(16)]
+            hsh = wz.ple_fp8_hash(vocab=vocab)
+            table = torch.randint(0, 256, (sum(vocab), 160), generator=gen, device=dev, dtype=torch.uint8)
+            ids = torch.randint(0, 248320, (T,), generator=gen, device=dev, dtype=torch.int32)
+            out = torch.empty((T, 2560), device=dev)
+            fn = lambda: wz.ple_gather_fp8_f32(table, 160, 0.5, hsh, ids, out, stream=s)  # noqa: E731
+        else:
+            jobs, keep = f8_jobs_small(wz, torch, dev, T)
+            if name not in jobs:
+                raise SystemExit(f"unknown case {name}")
+            fn = lambda: jobs[name](s)  # noqa: E731
+    for _ in range(reps):
+        fn()
+    torch.cuda.synchronize()
+    print("ok", name, T, flush=True)
+
+
+def f8_jobs_small(wz, torch, dev, T):
+    """The f8 kernels without the 51.2 GB fp8 table (for captures)."""
+    gen = torch.Generator(device=dev).manual_seed(1)
+    NE, HC = 2560, 4
+    R = torch.randn((T * HC, NE), generator=gen, device=dev)
+    blk = torch.randn((T, NE), generator=gen, device=dev)
+    inj = torch.randn((T * HC,), generator=gen, device=dev)
+    wn = 1 + 0.02 * torch.randn((HC, NE), generator=gen, device=dev)
+    xn = torch.empty((T * HC, NE), device=dev)
+    xq = torch.empty((T * HC, NE), dtype=torch.int8, device=dev)
+    xs = torch.empty((T * HC, NE // 32), device=dev)
+    q16 = torch.empty((T * HC, NE), dtype=torch.int8, device=dev)
+    s16 = torch.empty((T * HC, NE // 16), device=dev)
+    x16 = torch.randn((T, HC, NE), generator=gen, device=dev).half()
+    g16 = torch.randn((T, HC, NE), generator=gen, device=dev).half()
+    m16 = torch.empty((T, NE), dtype=torch.float16, device=dev)
+    q = torch.randn((T * HC, NE), generator=gen, device=dev)
+    hcd = NE * HC
+    cw = torch.randn((hcd, 4), generator=gen, device=dev)
+    hist = torch.randn((hcd, 9), generator=gen, device=dev)
+    rc = torch.randn((T, hcd), generator=gen, device=dev)
+    k = torch.randn((T, 512), generator=gen, device=dev).half()
+    v = torch.randn((T, 512), generator=gen, device=dev).half()
+    kg = (0.02 * torch.randn(256, generator=gen, device=dev)).half()
+    pl = [torch.zeros((T, 512), dtype=torch.int8, device=dev) if i % 2 == 0 else
+          torch.zeros((T, 8), dtype=torch.int16, device=dev) for i in range(8)]
+    cache = wz.kv_cache(*pl[:4], T, T, *pl[4:])
+    c, sn = rope_tables(wz, torch, T, dev)
+    keep = [R, blk, inj, wn, xn, xq, xs, q16, s16, x16, g16, m16, q, cw, hist, rc, k, v, kg, pl, c, sn]
+    jobs = {
+        "kv": lambda st: wz.k_rope_kv_append(k, kg, v, c, sn, T, 2, 256, cache, rot_dims=64, w_offset=1.0, stream=st),
+        "conv": lambda st: wz.ple_conv_f32(R.view(T, hcd), cw, hist, xn.view(T, hcd), rc, T, hcd, stream=st),
+        "grn": lambda st: wz.gr_norm_f32(R, wn, blk, inj, xn, T, NE, HC, stream=st),
+        "grq8": lambda st: wz.gr_norm_q8_f32(R, wn, blk, inj, xn, xq, xs, T, NE, HC, stream=st),
+        "gate": lambda st: wz.ple_gate_f32(R, q, blk, xn, T, NE, HC, stream=st),
+        "mix": lambda st: wz.hc_mix(x16, g16, blk, m16, T, NE, HC, stream=st),
+        "grw": lambda st: wz.gr_write_f32(R, blk, inj, T, NE, HC, stream=st),
+        "q8": lambda st: wz.quant_act_f32(R, xq, xs, q16, s16, T * HC, NE, stream=st),
+    }
+    return jobs, keep
+
+
+# ------------------------------------------------------------------------------------------------
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -498,6 +776,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-kernels", action="store_true")
+    ap.add_argument("--split", action="store_true", help="the bundles' ops as separate launches (A/B)")
+    ap.add_argument("--profile-case", default=None,
+                    help="run one small case for an ncu capture and exit: attn_b act_b gath_b norm qk swi gdn "
+                         "emb ple ple8 kv conv grn grq8 gate mix grw q8 (--tokens, default 4096; --steps reps)")
     ap.add_argument("--variant", default="auto", choices=["auto", "ring", "direct", "async", "wide", "pair"],
                     help="kernel design of the norm families (A/B measurement)")
     ap.add_argument("--tune", action="append", default=[],
@@ -511,37 +793,18 @@ def main():
     peak, peak_kind = peaks()
 
     if args.impl == "reference":
-        # The reference's path has no standalone implementation here other than its CPU restatement:
-        # rank 0 times the oracle port on this host's cores; other ranks exit without work.
-        if rank != 0:
-            return
-        # each step: the bundle on a bounded token sample, sized so K steps stay within ~2 minutes
-        T = 4096 if args.steps <= 200 else max(256, (4096 * 200 // args.steps) // 64 * 64)
-        b = CpuBundle(T)
-        for _ in range(args.warmup):
-            b.run()
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            b.run()
-        el = time.perf_counter() - t0
-        value = round(T * args.steps / el, 1)
-        cb = {"value": value, "unit": "tokens/s", "cores": b.threads, "kind": "port",
-              "sample": f"each step = configs[1]+[2] bundle on {T} of the 262,144 tokens (oracle C port of the "
-                        f"reference math, OpenMP over rows, {b.threads} threads); {args.steps} steps in {el:.1f} s"}
-        print(json.dumps({
-            "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "fp16 I/O, fp32 math", "data": "synthetic (seeded normal / uniform ids)",
-            "config": {"workload": "configs[4]: configs[1]+[2] bundle at 262,144 tokens (CPU: bounded sample)"},
-            "cpu_baseline": cb, "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                                        "d2h_bytes_per_step": 0},
-        }), flush=True)
+        reference_arm(args, rank, peak)
         return
 
     import torch
     import torch.distributed as dist
 
     import wzyb200 as wz
+
+    if args.profile_case:
+        T = args.tokens if args.tokens != TOKENS else 4096
+        profile_case(wz, torch, args.profile_case, T, min(args.steps, 10))
+        return
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -555,24 +818,28 @@ def main():
            "pair": wz.VARIANT_PAIR}[args.variant]
     for fam in (wz.FAM_NORM, wz.FAM_HEAD_ROPE, wz.FAM_GDN):
         wz.set_kernel_variant(fam, var)
+    if args.split:
+        wz.set_kernel_variant(wz.FAM_BUNDLE, wz.VARIANT_SPLIT)
     for spec in args.tune:
         fam, ctas, stages = (int(v) for v in spec.split(":"))
         wz.set_launch_tuning(fam, ctas, stages)
 
     row0, n = wz.shard_rows(args.tokens, world, rank)
-    sh = Shard(wz, torch, n, row0, 1000 + rank, dev)
+    cos, sin = rope_tables(wz, torch, TOKENS if args.tokens <= TOKENS else args.tokens, dev)
+    sh = Shard(wz, torch, n, row0, 1000 + rank, dev, cos, sin)
     s = torch.cuda.current_stream()
     torch.cuda.synchronize()
+    nb = len(STEP_BUNDLES)
 
     def step():
-        for i in range(4):
+        for i in range(nb):
             sh.launch(i, s)
 
     # A shard whose step moves less than 4x the 126 MB L2 (the 4096-token config on 2+ GPUs) would be
     # timed partly out of L2: then L2 is flushed before every step (a 256 MB write, then a 256 MB read
     # so the write-back of the flush is not charged to the step) and the step is timed from its first
     # kernel to its last, the flush excluded.
-    shard_bytes = n * sum(BYTES_PER_TOKEN.values())
+    shard_bytes = n * sum(BYTES_PER_TOKEN[o] for b in STEP_BUNDLES for o in BUNDLES[b])
     flush_l2 = shard_bytes < 4 * L2_BYTES
     if flush_l2:
         fl_w = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -614,20 +881,20 @@ def main():
         ms_total = sum(sev[k][0].elapsed_time(sev[k][1]) for k in range(args.steps))
     else:
         ms_total = t_start.elapsed_time(t_end)
-    # Per-kernel breakdown (rank 0's hbm.per_kernel_rank0 and the roofline's achieved bytes): a separate
-    # pass of min(K, 100) steps with an event around every launch.
+    # Per-launch breakdown (rank 0's hbm and the roofline's achieved bytes): a separate pass of
+    # min(K, 100) steps with an event around every launch.
     kp = min(args.steps, 100)
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(kp)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(nb + 1)] for _ in range(kp)]
     for k in range(kp):
         if flush_l2:
             flush()
-        for i in range(4):
+        for i in range(nb):
             ev[k][i].record(s)
             sh.launch(i, s)
-        ev[k][4].record(s)
+        ev[k][nb].record(s)
     torch.cuda.synchronize()
-    kern_ms = [statistics.mean(ev[k][i].elapsed_time(ev[k][i + 1]) for k in range(kp)) for i in range(4)]
-    launches = 4 * args.steps
+    kern_ms = [statistics.mean(ev[k][i].elapsed_time(ev[k][i + 1]) for k in range(kp)) for i in range(nb)]
+    launches = nb * args.steps
     faults = wz.read_faults()
 
     t = torch.tensor([ms_total, float(faults)], dtype=torch.float64, device=dev)
@@ -642,7 +909,7 @@ def main():
 
     e2e = None
     if not args.no_e2e:
-        e2e_s, ib, ob = run_e2e(wz, torch, n, row0, dev, args.e2e_steps)
+        e2e_s, ib, ob = run_e2e(wz, torch, n, row0, dev, args.e2e_steps, cos, sin)
         tt = torch.tensor([e2e_s, float(ib), float(ob)], dtype=torch.float64, device=dev)
         if world > 1:
             mx = tt.clone()
@@ -651,13 +918,15 @@ def main():
             tt[0] = mx[0]
         e2e = {"value": round(args.tokens / float(tt[0]), 1), "unit": "tokens/s",
                "h2d_bytes_per_step": int(tt[1]), "d2h_bytes_per_step": int(tt[2]),
-               "note": "public bundle API (wzyb_attn_prep_f16 + wzyb_act_f16), pinned host buffers, "
-                       "16384-token chunks on 2 streams, wall clock max over ranks"}
+               "note": "wzyb_attn_prep_f16 + wzyb_act_f16 on pinned host buffers, 16K-token chunks, 2 streams, "
+                       "wall clock max over ranks"}
 
-    kernels = decode = None
+    k4096 = f8 = dec = c0_gpu = None
     if rank == 0 and not args.no_kernels:
-        kernels = measure_kernels_4096(wz, torch, dev, peak)
-        decode = measure_decode(wz, torch, dev)
+        del sh
+        torch.cuda.empty_cache()
+        k4096, f8 = measure_4096(wz, torch, dev, peak, cos, sin)
+        c0_gpu, dec = measure_decode(wz, torch, dev)
 
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -667,17 +936,18 @@ def main():
         dist.barrier()
     if rank == 0:
         tokens_per_s = args.tokens / (ms_per_step * 1e-3)
-        step_bytes = args.tokens * sum(BYTES_PER_TOKEN.values()) + world * sum(WEIGHT_BYTES.values())
-        dom = "swiglu"
-        dom_bytes = n * BYTES_PER_TOKEN[dom]
-        dom_ms = kern_ms[KERNELS.index(dom)]
+        step_bytes = sum(bundle_bytes(b, args.tokens) for b in STEP_BUNDLES) + (world - 1) * sum(WEIGHT_BYTES.values())
+        dom = "act_b"
+        dom_bytes = bundle_bytes(dom, n)
+        dom_ms = kern_ms[STEP_BUNDLES.index(dom)]
         achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
         traffic = NCU_TRAFFIC_PER_TOKEN[dom] * n if NCU_TRAFFIC_PER_TOKEN[dom] else None
-        per_kernel = {}
-        for i, kname in enumerate(KERNELS):
-            b = n * BYTES_PER_TOKEN[kname] + WEIGHT_BYTES[kname]
-            gbs = b / (kern_ms[i] * 1e-3) / 1e9
-            per_kernel[kname] = {"us": round(kern_ms[i] * 1e3, 1), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+        hbm = {"step_gbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9, 1),
+               "step_frac_per_gpu": round(step_bytes / (ms_per_step * 1e-3) / 1e9 / peak / world, 4),
+               "step_frac_of_8tbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9 / NOMINAL_HBM_GBS / world, 4)}
+        for i, b in enumerate(STEP_BUNDLES):
+            gbs = bundle_bytes(b, n) / (kern_ms[i] * 1e-3) / 1e9
+            hbm[b] = [round(kern_ms[i] * 1e3, 1), round(gbs / peak, 4)]
         reasons = sorted({r for c in clk_all for r in (c["reasons"] if c else [])})
         sm = [c["sm_mhz"] for c in clk_all if c and c["sm_mhz"]]
         out = {
@@ -693,34 +963,32 @@ def main():
             "vs_baseline": None,
             "dtype": "fp16 I/O, fp32 math",
             "data": "synthetic (seeded normal activations, N(0,0.02) weights as 1+w)",
-            "config": {"workload": f"configs[4]: configs[1]+[2] layer bundle at {args.tokens:,} tokens, "
-                                   "token-sharded, no collective",
-                       "tokens": args.tokens, "tokens_per_gpu": n, "hidden": HIDDEN, "q_heads": QH, "kv_heads": KH,
-                       "head_dim": HD, "rot_dims": ROT, "expert_rows_per_token": EXPERT_ROWS, "ffn": FFN,
-                       "gdn_heads": GDN_H, "gdn_head_dim": GDN_HD, "parallelism": f"token-shard x{world}",
-                       "norm_kernel_design": args.variant,
-                       "l2": ("L2 flushed before every step (256 MB write + 256 MB read), step timed from its "
-                              "first kernel to its last" if flush_l2 else "inputs larger than L2 (no flush)")},
-            "hbm": {"bundle_gbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9, 1),
-                    "bundle_frac_of_8tbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9 / NOMINAL_HBM_GBS / world, 4),
-                    "bundle_frac_of_peak_per_gpu": round(step_bytes / (ms_per_step * 1e-3) / 1e9 / peak / world, 4),
-                    "bytes_per_step": int(step_bytes), "rope_table_bytes_per_step": args.tokens *
-                    ROPE_TABLE_BYTES_PER_TOKEN, "per_kernel_rank0": per_kernel},
-            "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
-                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": traffic, "algorithmic_bytes": dom_bytes},
-            "kernels_4096": kernels,
-            "decode_us": decode,
+            "config": {"workload": f"configs[4]: configs[1]+[2] bundles at {args.tokens:,} tokens, token-sharded, "
+                                   "no collective, one launch per bundle" + (" (split)" if args.split else ""),
+                       "tokens": args.tokens, "tokens_per_gpu": n, "parallelism": f"token-shard x{world}",
+                       "rope_table": "host-built (reference procedure)",
+                       "l2": "flushed before every step" if flush_l2 else "inputs larger than L2 (no flush)",
+                       "legend": "[us, frac of measured peak(, frac of a size-matched copy)]; k4096/f8: L2 flushed "
+                                 "per launch; dec: [T=1, T=8] us, graph-replayed"},
+            "gpu_launches": launches * world,
+            "faults": any_fault,
             "clocks": {"sm_mhz": statistics.median(sm) if sm else None,
                        "sm_max_mhz": max((c["sm_max_mhz"] or 0) for c in clk_all if c) or None,
                        "reasons": reasons, "samples": sum(c["samples"] for c in clk_all if c)},
-            "gpu_launches": launches * world,
-            "faults": any_fault,
             "e2e": e2e,
             "cpu_baseline": cb,
+            "roofline": {"bound": "hbm", "kernel": "act bundle (SwiGLU + GDN, one launch)", "achieved": round(achieved, 1),
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic, "algorithmic_bytes": dom_bytes},
+            "hbm": hbm,
+            "dec": dec,
+            "f8": f8,
+            "c0": {"gpu_us": c0_gpu, "cpu_us_1t": cb.get("c0_us_1t") if cb else None},
+            "k4096": k4096,
         }
-        print(json.dumps(out), flush=True)
-    del sh
+        print(json.dumps(out, separators=(",", ":")), flush=True)
+    else:
+        del sh
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -136,7 +136,8 @@ int wzyb_head_norm_rope_f32(float* data, const float* gamma, const float* cos_ta
 /* q and k of one token in ONE launch (what the reference does with two launches,
  * src/wzy_prefill_tc.cuh:862-865). Each tensor has its own gamma, head count and strides. */
 typedef struct {
-    void* data;          /* [T, ...] fp16 (the _f16 entry point)                                 */
+    void* data;          /* [T, ...]; element type set by the entry point: fp16 for the _f16 calls,
+                            k's type for wzyb_qk_rope_kv_append_*                                 */
     const void* gamma;   /* [head_dim]                                                            */
     int heads;
     int64_t head_stride; /* elements between heads of one token                                  */
@@ -199,7 +200,9 @@ int wzyb_k_rope_kv_append_f32(float* k, const float* k_gamma, const float* v, co
  * and strides in *q, e.g. the reference's q interleaved with its gate, head_stride = 2*head_dim): the
  * reference's three launches -- fused_head_norm_rope_multi on q and on k, then kv_append_int8_multi
  * (src/wzy_stage_v2.cuh:638-655, src/wzy_prefill_tc.cuh:862-878) -- as one. q->data and q->gamma
- * have the element type of k. */
+ * have the element type of k. The q heads of different tokens must not overlap (T > 1 needs
+ * q->row_stride >= (q->heads - 1) * q->head_stride + head_dim) and q must not share bytes with k or v;
+ * either is WZYB_ERR_SHAPE. */
 int wzyb_qk_rope_kv_append_f32(const wzyb_head_tensor* q, float* k, const float* k_gamma, const float* v,
                                const float* cos_tab, const float* sin_tab, int64_t table_rows,
                                const int32_t* d_base_pos, int64_t pos_offset, int64_t T, int kv_heads, int head_dim,
@@ -386,9 +389,17 @@ uint32_t wzyb_ple_row_index(int32_t t0, int32_t t1, int32_t t2, int head, int64_
                             int32_t eos_id, int hash_variant);
 
 /* ============================================================================================
- * Layer bundles: the host-side executor issues the path's kernels in the order the reference's
- * prefill executor does (src/wzy_prefill_tc.cuh:697 norm, :862-867 q/k norm+RoPE, :942 SwiGLU,
- * :845 GDN gated norm), with the q and k tensors fused into one launch.
+ * Layer bundles: the ops that the reference's prefill executor launches one after another inside a
+ * layer (src/wzy_prefill_tc.cuh:697 residual norm and :862-867 q/k norm+RoPE; :942 SwiGLU and :845
+ * GDN gated norm) and the rows its engine stages in one host routine (stage_emb_ple_pf,
+ * src/wzy_engine_v2.cu:1210-1265), each bundle as ONE kernel launch. The ops of a bundle share no
+ * tensor: the launch splits its persistent grid between them (each CTA runs one op's code, the
+ * same code as the op's own entry point, so results are bit-identical to the separate calls).
+ * The tensors of the two ops must not overlap; if they do, or if a shape is outside the one-launch
+ * kernels' range (attn_prep: fp16 hidden <= 2560 and head_dim 64/128/256; act: head_dim 64/128/256;
+ * embed_ple: PLE head_dim 64/128/256), or a non-default design was chosen with
+ * wzyb_set_kernel_variant, the entry point issues the ops as separate launches in the order above.
+ * Arguments are validated exactly as by the per-op entry points.
  * ========================================================================================== */
 typedef struct {
     /* residual add + RMSNorm, [T, hidden] */
@@ -433,6 +444,31 @@ typedef struct {
 int wzyb_attn_prep_f16(const wzyb_attn_prep_args* a, int64_t T, wzyb_stream_t stream);
 int wzyb_act_f16(const wzyb_act_args* a, int64_t T, wzyb_stream_t stream);
 
+/* Token-embedding rows and 3-gram PLE rows of the same T ids, in one launch: what stage_emb_ple_pf
+ * (src/wzy_engine_v2.cu:1210-1265) stages on the host for a prefill chunk (one stage_one_emb row and
+ * 16 PLE rows per token). Fields as wzyb_embed_gather_f16 and wzyb_ple_gather_f16. */
+typedef struct {
+    const int32_t* ids; /* [T] device token ids, read by both gathers                           */
+    /* token embedding: emb_out[t] = table[id(t)] */
+    const uint16_t* table;
+    int64_t vocab;
+    int hidden;
+    int oob_policy;
+    uint32_t* d_oob_count; /* or NULL                                                           */
+    uint16_t* emb_out;     /* [T, hidden]                                                       */
+    /* PLE: ple_out[t, h*head_dim ...] = ple_tables[h][row_h(t)] */
+    const uint16_t* const* ple_tables; /* HOST array of ple_heads device pointers               */
+    int ple_heads;
+    int64_t ple_rows; /* rows per table                                                         */
+    int ple_head_dim;
+    const int32_t* prev_ids; /* HOST {id[-2], id[-1]} or NULL                                   */
+    int32_t eos_id;
+    int hash_variant;
+    uint16_t* ple_out; /* [T, ple_heads * ple_head_dim]                                        */
+} wzyb_embed_ple_args;
+
+int wzyb_embed_ple_f16(const wzyb_embed_ple_args* a, int64_t T, wzyb_stream_t stream);
+
 /* Token-row sharding for G independent GPUs (no collective): rank r gets rows
  * [row0, row0 + rows) of a contiguous ceil(total/G) split. */
 int wzyb_shard_rows(int64_t total, int world, int rank, int64_t* row0, int64_t* rows);
@@ -457,12 +493,13 @@ int wzyb_read_faults(uint32_t* faults, int clear);
  * TMA ring depth (0 = as deep as the shared-memory budget allows, else 1..64 stages) of the ring
  * design. Outside the ring: SwiGLU stages 1 / 2 force the scalar / packed math; head norm+RoPE
  * ctas_per_sm 2 selects the other instantiation of its design.
- * Families: 0 add+RMSNorm, 1 head norm+RoPE, 2 GDN gated norm, 3 SwiGLU, 4 gathers. */
+ * Families: 0 add+RMSNorm, 1 head norm+RoPE, 2 GDN gated norm, 3 SwiGLU, 4 gathers, 5 layer bundles. */
 #define WZYB_FAM_NORM 0
 #define WZYB_FAM_HEAD_ROPE 1
 #define WZYB_FAM_GDN 2
 #define WZYB_FAM_SWIGLU 3
 #define WZYB_FAM_GATHER 4
+#define WZYB_FAM_BUNDLE 5
 int wzyb_set_launch_tuning(int family, int ctas_per_sm, int stages);
 /* Kernel design per family (process-wide), for A/B measurement:
  *   WZYB_VARIANT_AUTO   the library's choice for the shape (default)
@@ -471,9 +508,10 @@ int wzyb_set_launch_tuning(int family, int ctas_per_sm, int stages);
  *   WZYB_VARIANT_ASYNC  warp-owned units staged in a lane-private shared-memory ring by cp.async
  *   WZYB_VARIANT_WIDE   CTA-owned rows (4-16 warps), registers, one CTA barrier per row
  *   WZYB_VARIANT_PAIR   (head norm+RoPE) two chunks per lane holding each rotation pair, no shuffle
+ *   WZYB_VARIANT_SPLIT  (layer bundles) each op of a bundle as its own launch, in the reference's order
  * Families 0 (add+RMSNorm), 1 (head norm+RoPE) and 2 (GDN gated norm) have the RING, DIRECT and
  * ASYNC designs; family 0 also WIDE, which AUTO picks for rows past one warp's register budget;
- * family 1 also PAIR
+ * family 1 also PAIR; family 5 AUTO (one launch per bundle) and SPLIT
  * (a family without a design falls back to AUTO; DIRECT and ASYNC do so for rows too wide). */
 #define WZYB_VARIANT_AUTO 0
 #define WZYB_VARIANT_RING 1
@@ -481,6 +519,7 @@ int wzyb_set_launch_tuning(int family, int ctas_per_sm, int stages);
 #define WZYB_VARIANT_ASYNC 3
 #define WZYB_VARIANT_WIDE 4
 #define WZYB_VARIANT_PAIR 5
+#define WZYB_VARIANT_SPLIT 6
 int wzyb_set_kernel_variant(int family, int variant);
 const char* wzyb_status_string(int status);
 int wzyb_version(void);

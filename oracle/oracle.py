@@ -25,6 +25,7 @@ _SIGS = {
     "or_set_threads": (None, [c_int]),
     "or_get_threads": (c_int, []),
     "or_add_rmsnorm_f16": (None, [P, P, P, P, c_int64, c_int, c_float, c_float]),
+    "or_time_add_rmsnorm_f16": (None, [P, P, P, P, c_int64, c_int, c_float, c_float, c_int, P]),
     "or_gr_norm_f32": (None, [P, P, P, P, P, P, c_int64, c_int, c_int, c_float]),
     "or_gr_norm_q8_f32": (None, [P, P, P, P, P, P, P, c_int64, c_int, c_int, c_float]),
     "or_swiglu_q8_f32": (None, [P, P, P, P, c_int64]),
@@ -103,6 +104,17 @@ def add_rmsnorm_f16(x, res, w, eps=1e-6, w_offset=1.0):
     lib().or_add_rmsnorm_f16(_p(xx), _p(res_out), _p(np.ascontiguousarray(w, dtype=np.float16)), _p(y), T, n, eps,
                              w_offset)
     return y, res_out
+
+
+def time_add_rmsnorm_f16(x, res, w, reps, eps=1e-6, w_offset=1.0):
+    """Per-call wall times (ns) of `reps` scalar add + RMSNorm calls on the calling thread (res is updated
+    in place every call, as the decode step does)."""
+    T, n = res.shape
+    samples = np.empty(reps, dtype=np.float64)
+    lib().or_time_add_rmsnorm_f16(_p(np.ascontiguousarray(x, np.float16)), _p(res),
+                                  _p(np.ascontiguousarray(w, np.float16)), _p(np.empty_like(res)), T, n, eps,
+                                  w_offset, reps, _p(samples))
+    return samples
 
 
 def gr_norm_f32(R, w, bo, inj, T, n, hc, eps=1e-6):

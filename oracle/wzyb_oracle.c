@@ -6,12 +6,14 @@
  *
  * Build: gcc -O3 -march=x86-64-v2 -ffp-contract=off -fopenmp -shared -fPIC (oracle/Makefile).
  */
+#define _POSIX_C_SOURCE 200112L /* clock_gettime under -std=c11 */
 #include "wzyb_oracle.h"
 
 #include <math.h>
 #include <omp.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
 
 /* ------------------------------------------------------------------------------------------- */
 /* IEEE binary16 <-> binary32                                                                  */
@@ -80,30 +82,50 @@ static inline float sigmoid_den(float z) { return 1.0f + expf(-z); }
 /* (src/wzy_qsa_wmma.cuh:197-232): v = R + bo*gw; R <- v; xn = (v * rsqrt(sum(v^2)/n + eps)) * g */
 /* with gw = 2*sigmoid(inj/hc) (:419), == 1.0 for the single-stream add.                        */
 /* ------------------------------------------------------------------------------------------- */
+/* one row t; v is n floats of scratch */
+static void add_rmsnorm_row_f16(const uint16_t* x, uint16_t* res, const uint16_t* w, uint16_t* y, int64_t t, int n,
+                                float eps, float w_offset, float* v) {
+    uint16_t* r = res + t * n;
+    double ss = 0.0;
+    for (int d = 0; d < n; ++d) {
+        float val = or_h2f(r[d]);
+        if (x) val = val + or_h2f(x[t * n + d]);
+        v[d] = val;
+        ss += (double)val * (double)val;
+    }
+    const float sc = 1.0f / sqrtf((float)ss / (float)n + eps);
+    for (int d = 0; d < n; ++d) {
+        const float g = w_offset + or_h2f(w[d]);
+        y[t * n + d] = or_f2h((v[d] * sc) * g);
+        if (x) r[d] = or_f2h(v[d]);
+    }
+}
+
 void or_add_rmsnorm_f16(const uint16_t* x, uint16_t* res, const uint16_t* w, uint16_t* y, int64_t T, int n,
                         float eps, float w_offset) {
 #pragma omp parallel
     {
         float* v = (float*)malloc(sizeof(float) * (size_t)n);
 #pragma omp for schedule(static)
-        for (int64_t t = 0; t < T; ++t) {
-            uint16_t* r = res + t * n;
-            double ss = 0.0;
-            for (int d = 0; d < n; ++d) {
-                float val = or_h2f(r[d]);
-                if (x) val = val + or_h2f(x[t * n + d]);
-                v[d] = val;
-                ss += (double)val * (double)val;
-            }
-            const float sc = 1.0f / sqrtf((float)ss / (float)n + eps);
-            for (int d = 0; d < n; ++d) {
-                const float g = w_offset + or_h2f(w[d]);
-                y[t * n + d] = or_f2h((v[d] * sc) * g);
-                if (x) r[d] = or_f2h(v[d]);
-            }
-        }
+        for (int64_t t = 0; t < T; ++t) add_rmsnorm_row_f16(x, res, w, y, t, n, eps, w_offset, v);
         free(v);
     }
+}
+
+/* Timing loop of the CPU baseline for the decode-step add + RMSNorm (one token): `reps` calls of the
+ * scalar row code on the same buffers, on the calling thread (the residual keeps accumulating x), each
+ * call's wall time in ns (CLOCK_MONOTONIC) written to samples_ns. */
+void or_time_add_rmsnorm_f16(const uint16_t* x, uint16_t* res, const uint16_t* w, uint16_t* y, int64_t T, int n,
+                             float eps, float w_offset, int reps, double* samples_ns) {
+    float* v = (float*)malloc(sizeof(float) * (size_t)n);
+    for (int i = 0; i < reps; ++i) {
+        struct timespec a, b;
+        clock_gettime(CLOCK_MONOTONIC, &a);
+        for (int64_t t = 0; t < T; ++t) add_rmsnorm_row_f16(x, res, w, y, t, n, eps, w_offset, v);
+        clock_gettime(CLOCK_MONOTONIC, &b);
+        samples_ns[i] = (double)(b.tv_sec - a.tv_sec) * 1e9 + (double)(b.tv_nsec - a.tv_nsec);
+    }
+    free(v);
 }
 
 void or_gr_norm_f32(float* R, const float* w, const float* bo, const float* inj, float* xn, uint16_t* xn_h16,

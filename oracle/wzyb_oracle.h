@@ -29,6 +29,9 @@ int or_get_threads(void);
 /* residual add + RMSNorm (fp16 I/O); x may be NULL (plain RMSNorm, residual untouched) */
 void or_add_rmsnorm_f16(const uint16_t* x, uint16_t* res, const uint16_t* w, uint16_t* y, int64_t T, int n,
                         float eps, float w_offset);
+/* CPU-baseline timing loop of the above on the calling thread: per-call wall time (ns) of `reps` calls */
+void or_time_add_rmsnorm_f16(const uint16_t* x, uint16_t* res, const uint16_t* w, uint16_t* y, int64_t T, int n,
+                             float eps, float w_offset, int reps, double* samples_ns);
 /* hyper-connection form, fp32 I/O (xn_h16 != NULL additionally writes an fp16 copy of xn) */
 void or_gr_norm_f32(float* R, const float* w, const float* bo, const float* inj, float* xn, uint16_t* xn_h16,
                     int64_t T, int n, int hc, float eps);

@@ -159,6 +159,89 @@ def test_argument_validation_before_any_cuda_call(wz):
     assert L.wzyb_set_launch_tuning(0, 0, 0) == wz.ERR_VALUE
 
 
+def test_qk_kv_append_q_validation(wz):
+    """Every argument error of the fused q heads of wzyb_qk_rope_kv_append_* is returned on the host before
+    any CUDA call. (No entry point can pass q heads to a call without norm + RoPE: the append-only
+    wzyb_kv_append_int8_f32 has no q argument.)"""
+    L = wz.lib()
+    kc = ctypes.byref(wz.KvCache(0x10000, 0x10000, 0x10000, 0x10000, None, None, None, None, 64, 128))
+    k, v = 0x100000, 0x200000  # k, v [4, 2 x 256] fp16: 4 KB each, far from q
+
+    def call(qt, T=4):
+        return L.wzyb_qk_rope_kv_append_f16(ctypes.byref(qt), ctypes.c_void_p(k), A16, ctypes.c_void_p(v), A16, A16,
+                                            64, NULL, 0, T, 2, 256, 64, 1e-6, 1.0, kc, NULL)
+
+    q = 0x400000
+    ok_rs = 24 * 2 * 256
+    assert call(wz.HeadTensor(q, 0x10000, 300, 512, 300 * 512)) == wz.ERR_SHAPE    # q_heads > 256
+    assert call(wz.HeadTensor(q, 0x10000, -1, 512, ok_rs)) == wz.ERR_SHAPE          # q_heads < 0
+    assert call(wz.HeadTensor(None, 0x10000, 24, 512, ok_rs)) == wz.ERR_NULL        # q->data NULL
+    assert call(wz.HeadTensor(q, None, 24, 512, ok_rs)) == wz.ERR_NULL              # q->gamma NULL
+    assert call(wz.HeadTensor(q, 0x10000, 24, 100, ok_rs)) == wz.ERR_SHAPE         # heads overlap
+    assert call(wz.HeadTensor(q, 0x10000, 24, 516, 24 * 516 + 4)) == wz.ERR_ALIGN   # head stride * 2 % 16
+    assert call(wz.HeadTensor(q, 0x10000, 24, 512, ok_rs + 4)) == wz.ERR_ALIGN      # row stride * 2 % 16
+    assert call(wz.HeadTensor(q + 8, 0x10000, 24, 512, ok_rs)) == wz.ERR_ALIGN      # q not 16-byte aligned
+    # tokens' q rows overlapping each other (row stride shorter than one token's heads), T > 1 only
+    assert call(wz.HeadTensor(q, 0x10000, 24, 512, 0)) == wz.ERR_SHAPE
+    assert call(wz.HeadTensor(q, 0x10000, 24, 512, 8 * 512)) == wz.ERR_SHAPE
+    # q sharing bytes with k or v
+    assert call(wz.HeadTensor(k, 0x10000, 2, 256, 512)) == wz.ERR_SHAPE
+    assert call(wz.HeadTensor(v + 1024, 0x10000, 1, 256, 512)) == wz.ERR_SHAPE
+    # empty call with valid arguments: a no-op that needs no device
+    assert call(wz.HeadTensor(q, 0x10000, 24, 512, ok_rs), T=0) == wz.OK
+
+
+def test_bundle_validation(wz):
+    """The one-launch bundles validate both ops' arguments before anything is enqueued, and accept the
+    SPLIT design switch of their family."""
+    L = wz.lib()
+    assert L.wzyb_embed_ple_f16(None, 4, NULL) == wz.ERR_NULL
+    e = wz.EmbedPleArgs()
+    e.ids, e.table, e.vocab, e.hidden, e.emb_out = 0x10000, 0x20000, 100, 2048, 0x30000
+    tabs = (ctypes.c_void_p * 16)(*([0x40000] * 16))
+    e.ple_tables, e.ple_heads, e.ple_rows, e.ple_head_dim, e.ple_out = (ctypes.cast(tabs, ctypes.POINTER(
+        ctypes.c_void_p)), 16, 1 << 20, 128, 0x50000)
+    e.hidden = 2044
+    assert L.wzyb_embed_ple_f16(ctypes.byref(e), 4, NULL) == wz.ERR_SHAPE
+    e.hidden, e.oob_policy = 2048, 7
+    assert L.wzyb_embed_ple_f16(ctypes.byref(e), 4, NULL) == wz.ERR_VALUE
+    e.oob_policy, e.hash_variant = 0, 9
+    assert L.wzyb_embed_ple_f16(ctypes.byref(e), 4, NULL) == wz.ERR_VALUE
+    e.hash_variant, e.ple_out = 0, 0x50008
+    assert L.wzyb_embed_ple_f16(ctypes.byref(e), 4, NULL) == wz.ERR_ALIGN
+    e.ple_out = 0x50000
+    assert L.wzyb_embed_ple_f16(ctypes.byref(e), 0, NULL) == wz.OK
+    # attn_prep: an invalid q/k argument is reported although the norm's arguments are valid
+    a = wz.AttnPrepArgs()
+    a.x, a.residual, a.norm_weight, a.normed, a.hidden = 0x10000, 0x20000, 0x30000, 0x40000, 2048
+    a.q = wz.HeadTensor(0x50000, 0x60000, 16, 256, 4096)
+    a.k = wz.HeadTensor(0x70000, 0x60000, 2, 256, 512)
+    a.head_dim, a.rot_dims, a.cos_tab, a.sin_tab, a.table_rows = 96, 64, 0x80000, 0x90000, 4096
+    assert L.wzyb_attn_prep_f16(ctypes.byref(a), 4, NULL) == wz.ERR_SHAPE
+    a.head_dim = 256
+    assert L.wzyb_attn_prep_f16(ctypes.byref(a), 0, NULL) == wz.OK
+    a.hidden = 2044
+    assert L.wzyb_attn_prep_f16(ctypes.byref(a), 4, NULL) == wz.ERR_SHAPE
+    assert L.wzyb_set_kernel_variant(wz.FAM_BUNDLE, wz.VARIANT_SPLIT) == wz.OK
+    assert L.wzyb_set_kernel_variant(wz.FAM_BUNDLE, wz.VARIANT_AUTO) == wz.OK
+    assert L.wzyb_set_kernel_variant(wz.FAM_BUNDLE, 7) == wz.ERR_VALUE
+    assert L.wzyb_set_kernel_variant(6, 0) == wz.ERR_VALUE
+
+
+def test_head_tensor_element_type_checked(wz):
+    import torch
+
+    q16 = torch.zeros((2, 4, 512), dtype=torch.float16)
+    g32 = torch.zeros(256, dtype=torch.float32)
+    with pytest.raises(ValueError):
+        wz.head_tensor(q16, g32, 4, 512, 2048)
+    t = wz.head_tensor(q16, g32.half(), 4, 512, 2048)
+    assert t.elem_size == 2
+    k32 = torch.zeros((2, 512), dtype=torch.float32)
+    with pytest.raises(ValueError):
+        wz.k_rope_kv_append(k32, g32, k32, None, None, 2, 2, 256, wz.KvCache(), q=t)
+
+
 def test_no_device_is_reported_not_crashed(wz):
     import torch
 

@@ -633,6 +633,45 @@ def test_qk_rope_kv_append_one_launch(wz, orc, dtype, T, base):
     assert wz.read_faults() == 0
 
 
+@pytest.mark.parametrize("hd,kv_heads,qh,T,rot,dpos", [(64, 2, 5, 8, 64, False), (128, 2, 7, 512, 64, True),
+                                                       (128, 1, 7, 33, 0, False), (64, 4, 5, 100, 64, True),
+                                                       (256, 2, 3, 512, 256, False), (64, 1, 9, 1, 32, True)])
+def test_qk_rope_kv_append_one_launch_shapes(wz, orc, hd, kv_heads, qh, T, rot, dpos):
+    """The one-launch q + k + append at head_dim 64 and 128 (4 or 2 heads per warp, q head counts that do
+    not fill the last warp round), rot_dims 0 and == head_dim, positions from a device base position, and
+    T = 512 (the k-only call takes one head round per warp item, the fused call two): k and the cache
+    bit-identical to the k-only entry point's, q within 2 fp16 ulp of the oracle."""
+    r = rng(hd * 31 + qh * 7 + T)
+    cap, max_ctx = 1024, 1024
+    kvd = kv_heads * hd
+    k = r.standard_normal((T, kvd)).astype(np.float16)
+    v = r.standard_normal((T, kvd)).astype(np.float16)
+    kg = (0.02 * r.standard_normal(hd)).astype(np.float16)
+    qbuf = r.standard_normal((T, qh, 2 * hd)).astype(np.float16)
+    qg = (0.02 * r.standard_normal(hd)).astype(np.float16)
+    base_dev, off = (37, 5) if dpos else (0, 11)
+    rot_t = rot if rot > 0 else 16
+    c_, s_, dc, ds = _rope_tab(orc, base_dev + off + T + 8, rot_t)
+    d_base = torch.tensor([base_dev], dtype=torch.int32, device=DEV) if dpos else None
+    kw = dict(rot_dims=rot, eps=1e-6, w_offset=1.0, pos_offset=off, d_base_pos=d_base)
+    cache1, d1 = _kv_seeded(orc, rng(5), cap, max_ctx, kvd, True)
+    dk1 = dev(k)
+    wz.k_rope_kv_append(dk1, dev(kg), dev(v), dc, ds, T, kv_heads, hd, _kv_desc(wz, d1, cap, max_ctx, True), **kw)
+    cache2, d2 = _kv_seeded(orc, rng(5), cap, max_ctx, kvd, True)
+    dk2, dq, dqg = dev(k), dev(qbuf), dev(qg)
+    wz.k_rope_kv_append(dk2, dev(kg), dev(v), dc, ds, T, kv_heads, hd, _kv_desc(wz, d2, cap, max_ctx, True),
+                        q=wz.head_tensor(dq, dqg, qh, 2 * hd, 2 * qh * hd), **kw)
+    assert np.array_equal(host(dk2), host(dk1))
+    for nm in ["rkq", "rks", "rvq", "rvs", "fkq", "fks", "fvq", "fvs"]:
+        assert np.array_equal(_kv_host(d2, nm), _kv_host(d1, nm)), nm
+    want = orc.head_norm_rope(qbuf.reshape(-1), qg, c_, s_, T, qh, hd, 2 * hd, 2 * qh * hd, rot, 1e-6, 1.0,
+                              base_dev + off).reshape(T, qh, 2 * hd)
+    got = host(dq)
+    assert np.array_equal(got[..., hd:], qbuf[..., hd:])  # gates untouched
+    assert_f16_close(got[..., :hd].reshape(-1), want[..., :hd].reshape(-1), ULP_TOL, "q")
+    assert wz.read_faults() == 0
+
+
 # ---------------------------------------------------------------------------------------------
 # the reference model's PLE: fp8 rows by the n-gram hash, gate, causal conv
 # ---------------------------------------------------------------------------------------------

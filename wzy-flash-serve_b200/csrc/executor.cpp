@@ -1,36 +1,14 @@
-// executor.cpp -- host-side layer executor for the fused elementwise path (plain C++, no CUDA
-// kernels here: it only sequences the C-ABI launchers on the caller's stream).
+// executor.cpp -- host-side planning for token-sharded runs (plain C++, no CUDA here).
 //
-// The reference's executors interleave these kernels with GEMMs inside one layer loop
-// (PrefillStageCtx::run_stage_prefill, src/wzy_prefill_tc.cuh:805-1056): the residual fold + norm
-// feeds the projections (:697), q/k norm + RoPE follows the q/k projections (:862-867), the shared
-// expert's SwiGLU follows the gate/up GEMM (:942), and the GDN gated norm follows the recurrence
-// (:845). The bundles below issue the same kernels in the same order for one layer's worth of
-// tokens, with the q and k norm+RoPE launches fused into one.
+// The path shards by token rows with no exchange step: each GPU takes a contiguous row range of the
+// sequence, its RoPE positions start at the range's first row, and its 3-gram PLE rows need the two ids
+// that precede the range (the history the reference's stage_emb_ple_pf keeps in ple_prev across
+// chunks, src/wzy_engine_v2.cu:1210-1265). The layer bundles themselves are in bundle.cu.
 #include <cstdint>
 
 #include "../../include/wzyb200.h"
 
 extern "C" {
-
-int wzyb_attn_prep_f16(const wzyb_attn_prep_args* a, int64_t T, wzyb_stream_t stream) {
-    if (a == nullptr) return WZYB_ERR_NULL;
-    int rc = wzyb_add_rmsnorm_f16(a->x, a->residual, a->norm_weight, a->normed, T, a->hidden, a->eps, a->w_offset,
-                                  stream);
-    if (rc != WZYB_OK) return rc;
-    return wzyb_qk_norm_rope_f16(&a->q, a->k.heads > 0 ? &a->k : nullptr, a->cos_tab, a->sin_tab, a->table_rows,
-                                 a->d_base_pos, a->pos_offset, T, a->head_dim, a->rot_dims, a->eps, a->w_offset,
-                                 stream);
-}
-
-int wzyb_act_f16(const wzyb_act_args* a, int64_t T, wzyb_stream_t stream) {
-    if (a == nullptr) return WZYB_ERR_NULL;
-    if (a->act_rows < 0 || a->ffn < 0) return WZYB_ERR_SHAPE;
-    int rc = wzyb_swiglu_f16(a->gate, a->up, a->act, a->act_rows * (int64_t)a->ffn, stream);
-    if (rc != WZYB_OK) return rc;
-    return wzyb_gdn_gated_norm_f16(a->o, a->z, a->gdn_gamma, a->gdn_out, T, a->gdn_heads, a->gdn_head_dim, a->eps,
-                                   a->gdn_w_offset, a->gate_mode, stream);
-}
 
 int wzyb_shard_rows(int64_t total, int world, int rank, int64_t* row0, int64_t* rows) {
     if (row0 == nullptr || rows == nullptr) return WZYB_ERR_NULL;

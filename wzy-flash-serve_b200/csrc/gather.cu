@@ -22,15 +22,30 @@ __device__ __forceinline__ int64_t resolve_id(int32_t id, int64_t vocab, int pol
     return id < 0 ? 0 : vocab - 1;
 }
 
-// One warp per output row: out[t] = table[id(t)], row_chunks 16-byte chunks per row.
-__global__ void __launch_bounds__(kGatherThreads) gather_rows_kernel(const uint4* __restrict__ table, int64_t vocab,
-                                                                      int64_t row_chunks, const int32_t* __restrict__ ids,
-                                                                      int64_t T, uint4* __restrict__ out, int policy,
-                                                                      uint32_t* oob) {
-    pdl_begin();
+struct EmbedArgs {
+    const uint4* table;
+    int64_t vocab;
+    int64_t row_chunks;  // 16-byte chunks per row
+    const int32_t* ids;
+    int64_t T;
+    uint4* out;
+    int policy;
+    uint32_t* oob;
+};
+
+// One warp per output row: out[t] = table[id(t)], row_chunks 16-byte chunks per row. The body takes
+// its CTA's index among `nctas` CTAs that share the rows (a fused bundle kernel runs it on a subset of
+// its grid).
+__device__ __forceinline__ void gather_rows_body(const EmbedArgs& a, int cta, int nctas) {
+    const uint4* __restrict__ table = a.table;
+    const int32_t* __restrict__ ids = a.ids;
+    uint4* __restrict__ out = a.out;
+    const int64_t vocab = a.vocab, row_chunks = a.row_chunks, T = a.T;
+    const int policy = a.policy;
+    uint32_t* oob = a.oob;
     const int lane = threadIdx.x & 31;
-    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-    for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
+    const int64_t warps = (int64_t)nctas * (blockDim.x >> 5);
+    for (int64_t t = (int64_t)cta * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
         const int64_t id = resolve_id(__ldg(ids + t), vocab, policy, oob, lane);
         const uint4* src = table + id * row_chunks;
         uint4* dst = out + t * row_chunks;
@@ -44,6 +59,30 @@ __global__ void __launch_bounds__(kGatherThreads) gather_rows_kernel(const uint4
                 if (c0 + 32 * k < row_chunks) __stcs(dst + c0 + 32 * k, buf[k]);
         }
     }
+}
+
+__global__ void __launch_bounds__(kGatherThreads) gather_rows_kernel(const EmbedArgs a) {
+    pdl_begin();
+    gather_rows_body(a, blockIdx.x, gridDim.x);
+}
+
+// Validates an embedding-gather call on the host and fills `a`. Returns WZYB_OK or the WZYB_ERR_* of the
+// first bad argument; nothing is enqueued.
+static int embed_prepare(const void* table, int64_t vocab, int64_t row_bytes, const int32_t* ids, int64_t T,
+                         void* out, int oob_policy, uint32_t* d_oob_count, EmbedArgs& a) {
+    if (!table || !ids || !out) return WZYB_ERR_NULL;
+    if (oob_policy != WZYB_OOB_CLAMP && oob_policy != WZYB_OOB_ZERO_ID) return WZYB_ERR_VALUE;
+    if (vocab < 1 || T < 0 || row_bytes < 16 || (row_bytes % 16) != 0) return WZYB_ERR_SHAPE;
+    if (!aligned16(table) || !aligned16(out)) return WZYB_ERR_ALIGN;
+    a.table = (const uint4*)table;
+    a.vocab = vocab;
+    a.row_chunks = row_bytes / 16;
+    a.ids = ids;
+    a.T = T;
+    a.out = (uint4*)out;
+    a.policy = oob_policy;
+    a.oob = d_oob_count;
+    return WZYB_OK;
 }
 
 // bf16 table -> fp32 rows: each lane converts 8 bf16 (16 B in) to 8 fp32 (32 B out) by shifting the
@@ -165,14 +204,15 @@ __global__ void __launch_bounds__(kGatherThreads) ple_gather_kernel(const PleArg
 // Fast path when a head row is CH = 8, 16 or 32 chunks of 16 bytes: a group of CH lanes copies one
 // (token, head) row, 32/CH groups per warp, U rows in flight per group. The (token, head) position
 // is stepped without division and the row index uses a mask for power-of-two tables.
+// The body takes its CTA's index among `nctas` CTAs that share the rows (a fused bundle kernel runs it
+// on a subset of its grid).
 template <int CH, int U>
-__global__ void __launch_bounds__(kGatherThreads) ple_gather_groups_kernel(const PleArgs a) {
-    pdl_begin();
+__device__ __forceinline__ void ple_gather_groups_body(const PleArgs& a, int cta, int nctas) {
     constexpr int GPW = 32 / CH;
     const int lane = threadIdx.x & 31;
     const int c = lane % CH;
-    const int64_t ngroups = (int64_t)gridDim.x * (blockDim.x >> 5) * GPW;
-    const int64_t ggrp = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * GPW + lane / CH;
+    const int64_t ngroups = (int64_t)nctas * (blockDim.x >> 5) * GPW;
+    const int64_t ggrp = ((int64_t)cta * (blockDim.x >> 5) + (threadIdx.x >> 5)) * GPW + lane / CH;
     const int64_t items = a.T * a.heads;
     StridePos pos(ggrp, ngroups, a.heads);  // item it = (token q, head r)
     for (int64_t base = ggrp; base < items; base += ngroups * U) {
@@ -200,6 +240,44 @@ __global__ void __launch_bounds__(kGatherThreads) ple_gather_groups_kernel(const
     }
 }
 
+template <int CH, int U>
+__global__ void __launch_bounds__(kGatherThreads) ple_gather_groups_kernel(const PleArgs a) {
+    pdl_begin();
+    ple_gather_groups_body<CH, U>(a, blockIdx.x, gridDim.x);
+}
+
+// Validates a PLE-gather call on the host and fills `a` (the table pointers are read from the host
+// array `tables`). Returns WZYB_OK or the WZYB_ERR_* of the first bad argument; nothing is enqueued.
+static int ple_prepare(const uint16_t* const* tables, int heads, int64_t rows_per_table, int head_dim,
+                       const int32_t* ids, int64_t T, const int32_t* prev_ids, int32_t eos_id, int hash_variant,
+                       uint16_t* out, PleArgs& a) {
+    if (!tables || !ids || !out) return WZYB_ERR_NULL;
+    if (hash_variant != WZYB_PLE_HASH_C_PRECEDENCE && hash_variant != WZYB_PLE_HASH_XOR_THEN_ADD)
+        return WZYB_ERR_VALUE;
+    if (heads < 1 || heads > 32 || rows_per_table < 1 || rows_per_table > (int64_t(1) << 32) || head_dim < 8 ||
+        (head_dim % 8) != 0 || T < 0)
+        return WZYB_ERR_SHAPE;
+    for (int h = 0; h < 32; ++h) a.tables[h] = nullptr;
+    for (int h = 0; h < heads; ++h) {
+        if (!tables[h]) return WZYB_ERR_NULL;
+        if (!aligned16(tables[h])) return WZYB_ERR_ALIGN;
+        a.tables[h] = (const uint4*)tables[h];
+    }
+    if (!aligned16(out)) return WZYB_ERR_ALIGN;
+    a.heads = heads;
+    a.rows = (uint64_t)rows_per_table;
+    a.chunks = head_dim / 8;
+    a.ids = ids;
+    a.T = T;
+    a.prev2 = prev_ids ? prev_ids[0] : -1;
+    a.prev1 = prev_ids ? prev_ids[1] : -1;
+    a.eos = eos_id;
+    a.variant = hash_variant;
+    a.out = (uint4*)out;
+    a.rows_mask = (rows_per_table & (rows_per_table - 1)) == 0 ? (uint32_t)(rows_per_table - 1) : 0u;
+    return WZYB_OK;
+}
+
 static int grid_for(int64_t work_threads, int ctas_per_sm, const DeviceInfo& di) {
     return persistent_grid(di, ctas_per_sm, (work_threads + kGatherThreads - 1) / kGatherThreads);
 }
@@ -210,17 +288,14 @@ extern "C" {
 
 int wzyb_embed_gather_rows(const void* table, int64_t vocab, int64_t row_bytes, const int32_t* ids, int64_t T,
                            void* out, int oob_policy, uint32_t* d_oob_count, wzyb_stream_t stream) {
-    if (!table || !ids || !out) return WZYB_ERR_NULL;
-    if (oob_policy != WZYB_OOB_CLAMP && oob_policy != WZYB_OOB_ZERO_ID) return WZYB_ERR_VALUE;
-    if (vocab < 1 || T < 0 || row_bytes < 16 || (row_bytes % 16) != 0) return WZYB_ERR_SHAPE;
-    if (!wzyb::aligned16(table) || !wzyb::aligned16(out)) return WZYB_ERR_ALIGN;
-    if (T == 0) return WZYB_OK;
+    wzyb::EmbedArgs a;
+    int rc = wzyb::embed_prepare(table, vocab, row_bytes, ids, T, out, oob_policy, d_oob_count, a);
+    if (rc != WZYB_OK || T == 0) return rc;
     wzyb::DeviceInfo di;
-    const int rc = wzyb::device_info(&di);
+    rc = wzyb::device_info(&di);
     if (rc != WZYB_OK) return rc;
     const int grid = wzyb::grid_for(T * 32, 8, di);
-    wzyb::launch_k(wzyb::gather_rows_kernel, grid, wzyb::kGatherThreads, 0, (cudaStream_t)stream, 
-        (const uint4*)table, vocab, row_bytes / 16, ids, T, (uint4*)out, oob_policy, d_oob_count);
+    wzyb::launch_k(wzyb::gather_rows_kernel, grid, wzyb::kGatherThreads, 0, (cudaStream_t)stream, a);
     return wzyb::launch_status();
 }
 
@@ -255,35 +330,12 @@ uint32_t wzyb_ple_row_index(int32_t t0, int32_t t1, int32_t t2, int head, int64_
 int wzyb_ple_gather_f16(const uint16_t* const* tables, int heads, int64_t rows_per_table, int head_dim,
                         const int32_t* ids, int64_t T, const int32_t* prev_ids, int32_t eos_id, int hash_variant,
                         uint16_t* out, wzyb_stream_t stream) {
-    if (!tables || !ids || !out) return WZYB_ERR_NULL;
-    if (hash_variant != WZYB_PLE_HASH_C_PRECEDENCE && hash_variant != WZYB_PLE_HASH_XOR_THEN_ADD)
-        return WZYB_ERR_VALUE;
-    if (heads < 1 || heads > 32 || rows_per_table < 1 || rows_per_table > (int64_t(1) << 32) || head_dim < 8 ||
-        (head_dim % 8) != 0 || T < 0)
-        return WZYB_ERR_SHAPE;
     wzyb::PleArgs a;
-    for (int h = 0; h < 32; ++h) a.tables[h] = nullptr;
-    for (int h = 0; h < heads; ++h) {
-        if (!tables[h]) return WZYB_ERR_NULL;
-        if (!wzyb::aligned16(tables[h])) return WZYB_ERR_ALIGN;
-        a.tables[h] = (const uint4*)tables[h];
-    }
-    if (!wzyb::aligned16(out)) return WZYB_ERR_ALIGN;
-    if (T == 0) return WZYB_OK;
+    int rc = wzyb::ple_prepare(tables, heads, rows_per_table, head_dim, ids, T, prev_ids, eos_id, hash_variant, out, a);
+    if (rc != WZYB_OK || T == 0) return rc;
     wzyb::DeviceInfo di;
-    const int rc = wzyb::device_info(&di);
+    rc = wzyb::device_info(&di);
     if (rc != WZYB_OK) return rc;
-    a.heads = heads;
-    a.rows = (uint64_t)rows_per_table;
-    a.chunks = head_dim / 8;
-    a.ids = ids;
-    a.T = T;
-    a.prev2 = prev_ids ? prev_ids[0] : -1;
-    a.prev1 = prev_ids ? prev_ids[1] : -1;
-    a.eos = eos_id;
-    a.variant = hash_variant;
-    a.out = (uint4*)out;
-    a.rows_mask = (rows_per_table & (rows_per_table - 1)) == 0 ? (uint32_t)(rows_per_table - 1) : 0u;
     if (a.chunks == 8 || a.chunks == 16 || a.chunks == 32) {
         // 2 rows in flight per lane group and correspondingly more groups (vs 8): 4.96 -> 6.12 TB/s at
         // 262,144 tokens x 16 heads, 4.60 -> 5.72 TB/s at 65,536, 14.1 -> 12.3 us at 4096 tokens

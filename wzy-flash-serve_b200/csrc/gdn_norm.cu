@@ -153,13 +153,14 @@ __global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) gdn_norm_kernel(const G
 // Direct design: a warp owns one 256-element slab of a token row (32/L whole heads), keeps kU slabs of
 // o and z in flight as raw 16-byte registers, then normalises each head inside its lane group. No
 // shared memory, no CTA barrier: warps stream independently like a copy kernel.
+// The body takes its CTA's index among `nctas` CTAs that share the slabs (a fused bundle kernel runs it
+// on a subset of its grid).
 template <typename TI, typename TO, int HD, int kU, bool SILU>
-__global__ void __launch_bounds__(256, sizeof(TI) == 2 ? 3 : 2) gdn_direct_kernel(const GdnArgs a) {
-    pdl_begin();
+__device__ __forceinline__ void gdn_direct_body(const GdnArgs& a, int cta, int nctas) {
     constexpr int L = HD / 8;
     const int lane = threadIdx.x & 31;
-    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-    const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t nwarps = (int64_t)nctas * (blockDim.x >> 5);
+    const int64_t gwarp = (int64_t)cta * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int row_elems = a.heads * HD;
     const int slabs = (row_elems + 255) / 256;
     const int64_t items = a.T * slabs;
@@ -204,6 +205,12 @@ __global__ void __launch_bounds__(256, sizeof(TI) == 2 ? 3 : 2) gdn_direct_kerne
             if (off[k] >= 0) Vec8<TO>::store2(y + off[k], out);
         }
     }
+}
+
+template <typename TI, typename TO, int HD, int kU, bool SILU>
+__global__ void __launch_bounds__(256, sizeof(TI) == 2 ? 3 : 2) gdn_direct_kernel(const GdnArgs a) {
+    pdl_begin();
+    gdn_direct_body<TI, TO, HD, kU, SILU>(a, blockIdx.x, gridDim.x);
 }
 
 // Async design: the direct design's warp-owned slabs, but the kP slabs in flight per warp sit in a
@@ -304,20 +311,16 @@ static int launch_gdn_warp(const GdnArgs& a, int hd, bool async_design, const De
     return launch_status();
 }
 
-template <typename TI, typename TO>
-static int launch_gdn(const void* o, const void* z, const void* gamma, void* y, int64_t T, int heads, int hd, float eps,
-                      float w_offset, int gate_mode, cudaStream_t stream) {
+// Validates a GDN gated-norm call on the host and fills `a`. Returns WZYB_OK or the WZYB_ERR_* of the
+// first bad argument; nothing is enqueued.
+template <typename TI>
+static int gdn_prepare(const void* o, const void* z, const void* gamma, void* y, int64_t T, int heads, int hd,
+                       float eps, float w_offset, int gate_mode, GdnArgs& a) {
     if (o == nullptr || z == nullptr || gamma == nullptr || y == nullptr) return WZYB_ERR_NULL;
     if (gate_mode != WZYB_GATE_SIGMOID && gate_mode != WZYB_GATE_SILU) return WZYB_ERR_VALUE;
     if (hd != 64 && hd != 128 && hd != 256) return WZYB_ERR_SHAPE;
     if (T < 0 || T > (int64_t(1) << 40) || heads < 1 || heads > 512) return WZYB_ERR_SHAPE;
     if (!aligned16(o) || !aligned16(z) || !aligned16(gamma) || !aligned16(y)) return WZYB_ERR_ALIGN;
-    if (T == 0) return WZYB_OK;
-    DeviceInfo di;
-    int rc = device_info(&di);
-    if (rc != WZYB_OK) return rc;
-
-    GdnArgs a;
     a.o = o;
     a.z = z;
     a.gamma = gamma;
@@ -329,6 +332,19 @@ static int launch_gdn(const void* o, const void* z, const void* gamma, void* y, 
     a.gate_mode = gate_mode;
     a.row_bytes = (uint32_t)((int64_t)heads * hd * sizeof(TI));
     a.stage_bytes = 2u * a.row_bytes;
+    a.stages = 0;
+    return WZYB_OK;
+}
+
+template <typename TI, typename TO>
+static int launch_gdn(const void* o, const void* z, const void* gamma, void* y, int64_t T, int heads, int hd, float eps,
+                      float w_offset, int gate_mode, cudaStream_t stream) {
+    GdnArgs a;
+    int rc = gdn_prepare<TI>(o, z, gamma, y, T, heads, hd, eps, w_offset, gate_mode, a);
+    if (rc != WZYB_OK || T == 0) return rc;
+    DeviceInfo di;
+    rc = device_info(&di);
+    if (rc != WZYB_OK) return rc;
 
     // The direct design is the default (measured on B200 at 262,144 tokens: direct 84%, cp.async 83%,
     // TMA ring 43% of HBM peak).

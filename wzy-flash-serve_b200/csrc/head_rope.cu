@@ -362,17 +362,18 @@ __global__ void __launch_bounds__(128) head_rope_direct_kernel(const HeadRopeArg
 // bit for bit. With 3 rounds per item, five CTAs per SM (<= 102 registers, 96 used with no spill)
 // instead of the four that an unbounded allocation (106) leaves: 82 -> 86 % of HBM peak at 262K
 // tokens on the same box. With 9 rounds, three (156 registers).
+// The body takes its CTA's index among `nctas` CTAs that share the items (a fused bundle kernel runs it
+// on a subset of its grid); every thread of the CTA must call it (one barrier after the gamma table).
 template <typename T, int HD, int kNH>
-__global__ void __launch_bounds__(128, kNH >= 9 ? 3 : 5) head_rope_pair_kernel(const HeadRopeArgs a) {
-    pdl_begin();
+__device__ __forceinline__ void head_rope_pair_body(const HeadRopeArgs& a, int cta, int nctas) {
     constexpr int L2 = HD / 16;   // lanes per head
     constexpr int HPW = 32 / L2;  // heads side by side in one warp
     constexpr int CH = kNH * HPW; // heads per chunk item
     const int lane = threadIdx.x & 31;
     const int li = lane % L2;
     const int hw = lane / L2;
-    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-    const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t nwarps = (int64_t)nctas * (blockDim.x >> 5);
+    const int64_t gwarp = (int64_t)cta * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int hq = a.sec[0].heads, htot = hq + a.sec[1].heads;
     const int chunks = (htot + CH - 1) / CH;
     const int64_t items = a.T * chunks;
@@ -471,6 +472,12 @@ __global__ void __launch_bounds__(128, kNH >= 9 ? 3 : 5) head_rope_pair_kernel(c
             }
         }
     }
+}
+
+template <typename T, int HD, int kNH>
+__global__ void __launch_bounds__(128, kNH >= 9 ? 3 : 5) head_rope_pair_kernel(const HeadRopeArgs a) {
+    pdl_begin();
+    head_rope_pair_body<T, HD, kNH>(a, blockIdx.x, gridDim.x);
 }
 
 // Async design: the direct design's per-token head chunks, but the kP chunks in flight per warp sit
@@ -615,10 +622,12 @@ static int launch_head_rope_pair(const HeadRopeArgs& a, int hd, int htot, const 
     return launch_status();
 }
 
+// Validates a head norm+RoPE call on the host and fills `a`. Returns WZYB_OK or the WZYB_ERR_* of the
+// first bad argument; nothing is enqueued.
 template <typename T>
-static int launch_head_rope(const HeadSection& q, const HeadSection& k, const float* cos_tab, const float* sin_tab,
-                            int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset, int64_t T_, int hd,
-                            int rot, float eps, float w_offset, cudaStream_t stream) {
+static int head_rope_prepare(const HeadSection& q, const HeadSection& k, const float* cos_tab, const float* sin_tab,
+                             int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset, int64_t T_, int hd,
+                             int rot, float eps, float w_offset, HeadRopeArgs& a) {
     if (q.data == nullptr || q.gamma == nullptr) return WZYB_ERR_NULL;
     if (k.heads > 0 && (k.data == nullptr || k.gamma == nullptr)) return WZYB_ERR_NULL;
     if (rot > 0 && (cos_tab == nullptr || sin_tab == nullptr)) return WZYB_ERR_NULL;
@@ -638,12 +647,6 @@ static int launch_head_rope(const HeadSection& q, const HeadSection& k, const fl
             return WZYB_ERR_ALIGN;
     }
     if (rot > 0 && (!aligned16(cos_tab) || !aligned16(sin_tab))) return WZYB_ERR_ALIGN;
-    if (T_ == 0) return WZYB_OK;
-    DeviceInfo di;
-    int rc = device_info(&di);
-    if (rc != WZYB_OK) return rc;
-
-    HeadRopeArgs a;
     a.sec[0] = q;
     a.sec[1] = k;
     if (k.heads == 0) a.sec[1] = HeadSection{nullptr, nullptr, 0, 0, 0};
@@ -661,6 +664,22 @@ static int launch_head_rope(const HeadSection& q, const HeadSection& k, const fl
     a.stage_bytes = a.head_bytes * (uint32_t)htot + (rot > 0 ? 2u * (uint32_t)(rot / 2) * 4u : 0u);
     a.contig[0] = (q.head_stride == hd || q.heads == 1) ? 1 : 0;
     a.contig[1] = (k.head_stride == hd || k.heads <= 1) ? 1 : 0;
+    a.stages = 0;
+    return WZYB_OK;
+}
+
+template <typename T>
+static int launch_head_rope(const HeadSection& q, const HeadSection& k, const float* cos_tab, const float* sin_tab,
+                            int64_t table_rows, const int32_t* d_base_pos, int64_t pos_offset, int64_t T_, int hd,
+                            int rot, float eps, float w_offset, cudaStream_t stream) {
+    HeadRopeArgs a;
+    int rc = head_rope_prepare<T>(q, k, cos_tab, sin_tab, table_rows, d_base_pos, pos_offset, T_, hd, rot, eps,
+                                  w_offset, a);
+    if (rc != WZYB_OK || T_ == 0) return rc;
+    DeviceInfo di;
+    rc = device_info(&di);
+    if (rc != WZYB_OK) return rc;
+    const int htot = q.heads + k.heads;
 
     if (variant(kFamHeadRope) == WZYB_VARIANT_ASYNC) {
         constexpr int kNH = 4, kP = 4;

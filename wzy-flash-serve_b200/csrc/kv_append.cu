@@ -275,9 +275,20 @@ static int launch_kv_append(const KvAppendArgs& a0, int head_dim, cudaStream_t s
         if (a.q_heads > 256 || (a.q_heads > 1 && a.q_head_stride < head_dim) || a.q_head_stride < 0 ||
             a.q_row_stride < 0)
             return WZYB_ERR_SHAPE;
+        // tokens' q heads must not overlap: each is normalised and rotated in place at its own position
+        const int64_t q_row_span = (int64_t)(a.q_heads - 1) * a.q_head_stride + head_dim;
+        if (a.T > 1 && a.q_row_stride < q_row_span) return WZYB_ERR_SHAPE;
         if (!aligned16(a.q) || !aligned16(a.q_gamma) || ((a.q_head_stride * (int64_t)sizeof(T)) % 16) != 0 ||
             ((a.q_row_stride * (int64_t)sizeof(T)) % 16) != 0)
             return WZYB_ERR_ALIGN;
+        // q is rewritten in place while k and v are read: the three must not share bytes
+        if (a.T > 0) {
+            const uintptr_t q0 = (uintptr_t)a.q;
+            const uintptr_t q1 = q0 + (uintptr_t)(((a.T - 1) * a.q_row_stride + q_row_span) * (int64_t)sizeof(T));
+            const uintptr_t kv_bytes = (uintptr_t)(a.T * (int64_t)a.kv_heads * head_dim * (int64_t)sizeof(T));
+            const uintptr_t k0 = (uintptr_t)a.k, v0 = (uintptr_t)a.v;
+            if ((q0 < k0 + kv_bytes && k0 < q1) || (q0 < v0 + kv_bytes && v0 < q1)) return WZYB_ERR_SHAPE;
+        }
     } else if (a.q_heads < 0) {
         return WZYB_ERR_SHAPE;
     }

@@ -26,7 +26,8 @@ enum KernelFamily : int {
     kFamGdn = 2,       // GDN gated norm
     kFamSwiglu = 3,    // SwiGLU
     kFamGather = 4,    // embedding / PLE gathers
-    kFamCount = 5
+    kFamBundle = 5,    // layer bundles (one launch per bundle, or the ops as separate launches)
+    kFamCount = 6
 };
 struct Tuning {
     int ctas_per_sm;

@@ -178,12 +178,13 @@ __global__ void __launch_bounds__(512) norm_rows_kernel(const NormRowsArgs a) {
 // before any arithmetic (VPL*2 loads in flight per lane); the sum of squares is reduced with five
 // xor shuffles; v is recomputed from the raw registers in the second pass instead of being kept in
 // fp32, which keeps a row of 2048 at ~100 registers. No shared memory, no CTA barrier.
+// The body takes its CTA's index among `nctas` CTAs that share the rows, so a fused bundle kernel can
+// run it on a subset of its grid.
 template <typename TI, typename TO, int VPL>
-__global__ void __launch_bounds__(256, 2) norm_rows_direct_kernel(const NormRowsArgs a) {
-    pdl_begin();
+__device__ __forceinline__ void norm_rows_direct_body(const NormRowsArgs& a, int cta, int nctas) {
     const int lane = threadIdx.x & 31;
-    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-    const int64_t gwarp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t nwarps = (int64_t)nctas * (blockDim.x >> 5);
+    const int64_t gwarp = (int64_t)cta * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const TI* __restrict__ x = static_cast<const TI*>(a.x);
     TI* __restrict__ res = static_cast<TI*>(a.res);
     const TI* __restrict__ w = static_cast<const TI*>(a.w);
@@ -243,6 +244,12 @@ __global__ void __launch_bounds__(256, 2) norm_rows_direct_kernel(const NormRows
             }
         }
     }
+}
+
+template <typename TI, typename TO, int VPL>
+__global__ void __launch_bounds__(256, 2) norm_rows_direct_kernel(const NormRowsArgs a) {
+    pdl_begin();
+    norm_rows_direct_body<TI, TO, VPL>(a, blockIdx.x, gridDim.x);
 }
 
 // Async design: one warp per row as in the direct design, but the row's residual and x vectors are
@@ -593,22 +600,15 @@ static int launch_norm_rows_wide(const NormRowsArgs& a, const DeviceInfo& di, cu
     return launch_status();
 }
 
-template <typename TI, typename TO>
-static int launch_norm_rows(const void* x, void* res, const void* w, const float* inj, void* y, int64_t T, int n,
-                            int hc, float eps, float w_offset, cudaStream_t stream) {
+// Validates a row-norm call on the host and fills `a` (every field but the launch shape's). Returns
+// WZYB_OK or the WZYB_ERR_* of the first bad argument; nothing is enqueued.
+template <typename TI>
+static int norm_rows_prepare(const void* x, void* res, const void* w, const float* inj, void* y, int64_t T, int n,
+                             int hc, float eps, float w_offset, NormRowsArgs& a) {
     if (res == nullptr || w == nullptr || y == nullptr) return WZYB_ERR_NULL;
     if (T < 0 || T > (int64_t(1) << 40) || n < 8 || n > 16384 || (n % 8) != 0 || hc < 1 || hc > 64)
         return WZYB_ERR_SHAPE;
     if (!aligned16(res) || !aligned16(w) || !aligned16(y) || (x && !aligned16(x))) return WZYB_ERR_ALIGN;
-    if (T == 0) return WZYB_OK;
-    DeviceInfo di;
-    int rc = device_info(&di);
-    if (rc != WZYB_OK) return rc;
-
-    const int vpt = n <= 4096 ? 1 : (n <= 8192 ? 2 : 4);
-    const int vecs = n / 8;
-    const int threads = ((vecs + vpt - 1) / vpt + 31) / 32 * 32;
-    NormRowsArgs a;
     a.x = x;
     a.res = res;
     a.w = w;
@@ -619,6 +619,7 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
     a.hc = hc;
     a.eps = eps;
     a.w_offset = w_offset;
+    a.stages = 0;
     a.row_bytes = (uint32_t)(n * sizeof(TI));
     a.stage_bytes = a.row_bytes * (x ? 2u : 1u);
     a.qout = a.sout = nullptr;
@@ -626,6 +627,22 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
     a.sf_layout = kSfRowMajor;
     a.sf_ncb = 0;
     a.lookahead = 0;  // without a quantised output it did not pay (76 vs 76 % at 4096 x 4 x 2560)
+    return WZYB_OK;
+}
+
+template <typename TI, typename TO>
+static int launch_norm_rows(const void* x, void* res, const void* w, const float* inj, void* y, int64_t T, int n,
+                            int hc, float eps, float w_offset, cudaStream_t stream) {
+    NormRowsArgs a;
+    int rc = norm_rows_prepare<TI>(x, res, w, inj, y, T, n, hc, eps, w_offset, a);
+    if (rc != WZYB_OK || T == 0) return rc;
+    DeviceInfo di;
+    rc = device_info(&di);
+    if (rc != WZYB_OK) return rc;
+
+    const int vpt = n <= 4096 ? 1 : (n <= 8192 ? 2 : 4);
+    const int vecs = n / 8;
+    const int threads = ((vecs + vpt - 1) / vpt + 31) / 32 * 32;
 
     // Direct design while a row fits one warp's register budget (<= 12 fp16 or 4 fp32 vectors per
     // lane), the wide design (CTA-owned rows) past it; the TMA ring only on request.

@@ -28,9 +28,9 @@ std::mutex g_dev_mu;
 std::mutex g_smem_mu;
 std::set<std::pair<const void*, int>> g_smem_done;  // (kernel, device)
 
-std::atomic<int> g_tune_ctas[kFamCount] = {{2}, {1}, {1}, {4}, {4}};
-std::atomic<int> g_tune_stages[kFamCount] = {{0}, {0}, {0}, {0}, {0}};
-std::atomic<int> g_variant[kFamCount] = {{0}, {0}, {0}, {0}, {0}};
+std::atomic<int> g_tune_ctas[kFamCount] = {{2}, {1}, {1}, {4}, {4}, {1}};
+std::atomic<int> g_tune_stages[kFamCount] = {{0}, {0}, {0}, {0}, {0}, {0}};
+std::atomic<int> g_variant[kFamCount] = {{0}, {0}, {0}, {0}, {0}, {0}};
 
 }  // namespace
 
@@ -161,7 +161,7 @@ int wzyb_set_launch_tuning(int family, int ctas_per_sm, int stages) {
 
 int wzyb_set_kernel_variant(int family, int variant) {
     if (family < 0 || family >= wzyb::kFamCount) return WZYB_ERR_VALUE;
-    if (variant < WZYB_VARIANT_AUTO || variant > WZYB_VARIANT_PAIR) return WZYB_ERR_VALUE;
+    if (variant < WZYB_VARIANT_AUTO || variant > WZYB_VARIANT_SPLIT) return WZYB_ERR_VALUE;
     wzyb::g_variant[family].store(variant);
     return WZYB_OK;
 }

@@ -56,13 +56,14 @@ __device__ __forceinline__ void swiglu_offsets(int64_t v, int64_t vpr, int64_t n
     }
 }
 
+// The body takes its CTA's index among `nctas` CTAs that share the vectors (a fused bundle kernel runs it
+// on a subset of its grid).
 template <typename TI, typename TO, bool INTERLEAVED, bool PACKED>
-__global__ void __launch_bounds__(kSwigluThreads) swiglu_kernel(const TI* __restrict__ gate, const TI* __restrict__ up,
-                                                                 TO* __restrict__ out, int64_t nvec, int64_t vpr,
-                                                                 int64_t nff) {
-    pdl_begin();
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+__device__ __forceinline__ void swiglu_body(const TI* __restrict__ gate, const TI* __restrict__ up,
+                                            TO* __restrict__ out, int64_t nvec, int64_t vpr, int64_t nff, int cta,
+                                            int nctas) {
+    const int64_t stride = (int64_t)nctas * blockDim.x;
+    int64_t v = (int64_t)cta * blockDim.x + threadIdx.x;
     for (; v + (kUnroll - 1) * stride < nvec; v += kUnroll * stride) {
         typename Vec8<TI>::Raw gr[kUnroll], ur[kUnroll];
 #pragma unroll
@@ -84,6 +85,23 @@ __global__ void __launch_bounds__(kSwigluThreads) swiglu_kernel(const TI* __rest
         swiglu_offsets<INTERLEAVED>(v, vpr, nff, gi, ui, oi);
         swiglu_vec<TI, TO, PACKED>(Vec8<TI>::ldcs_raw(gate + gi), Vec8<TI>::ldcs_raw(up + ui), out + oi);
     }
+}
+
+template <typename TI, typename TO, bool INTERLEAVED, bool PACKED>
+__global__ void __launch_bounds__(kSwigluThreads) swiglu_kernel(const TI* __restrict__ gate, const TI* __restrict__ up,
+                                                                 TO* __restrict__ out, int64_t nvec, int64_t vpr,
+                                                                 int64_t nff) {
+    pdl_begin();
+    swiglu_body<TI, TO, INTERLEAVED, PACKED>(gate, up, out, nvec, vpr, nff, blockIdx.x, gridDim.x);
+}
+
+// Math path of the SwiGLU stream for nvec 8-element vectors. Measured on B200 (same box, same inputs):
+// the packed base-2 sigmoid is faster for layer-sized calls (94% vs 86% of HBM peak at 4096 tokens x
+// 11 x 512), the scalar exp/divide form for very long streams (96% vs 93% at 262,144 tokens), so the
+// length picks, unless a SwiGLU `stages` tuning of 1 (scalar) or 2 (packed) forces one.
+static bool swiglu_scalar_math(int64_t nvec) {
+    const Tuning tu = tuning(kFamSwiglu);
+    return tu.stages == 1 || (tu.stages != 2 && nvec >= (int64_t(1) << 25));
 }
 
 // SwiGLU fused with the GEMM-input quantisation, no activation output: silu_mul_quant32_multi
@@ -131,14 +149,9 @@ static int launch_swiglu(const TI* gate, const TI* up, TO* out, int64_t nvec, in
     DeviceInfo di;
     const int rc = device_info(&di);
     if (rc != WZYB_OK) return rc;
-    // Math path. Measured on B200 (same box, same inputs): the packed base-2 sigmoid is faster for
-    // layer-sized calls (94% vs 86% of HBM peak at 4096 tokens x 11 x 512), the scalar exp/divide form
-    // for very long streams (96% vs 93% at 262,144 tokens), so the length picks, unless a SwiGLU
-    // `stages` tuning of 1 (scalar) or 2 (packed) forces one.
     const Tuning tu = tuning(kFamSwiglu);
     const int grid = persistent_grid(di, tu.ctas_per_sm, (nvec + kSwigluThreads - 1) / kSwigluThreads);
-    const bool scalar = tu.stages == 1 || (tu.stages != 2 && nvec >= (int64_t(1) << 25));
-    if (scalar)
+    if (swiglu_scalar_math(nvec))
         launch_k(swiglu_kernel<TI, TO, INTERLEAVED, false>, grid, kSwigluThreads, 0, stream, gate, up, out, nvec, vpr, nff);
     else
         launch_k(swiglu_kernel<TI, TO, INTERLEAVED, true>, grid, kSwigluThreads, 0, stream, gate, up, out, nvec, vpr, nff);

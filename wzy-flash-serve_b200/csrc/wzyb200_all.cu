@@ -10,3 +10,4 @@
 #include "kv_append.cu"
 #include "ple_block.cu"
 #include "quant_act.cu"
+#include "bundle.cu"

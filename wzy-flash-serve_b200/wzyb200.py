@@ -23,8 +23,9 @@ GATE_SIGMOID, GATE_SILU = 0, 1
 OOB_CLAMP, OOB_ZERO_ID = 0, 1
 PLE_HASH_C_PRECEDENCE, PLE_HASH_XOR_THEN_ADD = 0, 1
 PLE_EOS_DEFAULT = 248044
-FAM_NORM, FAM_HEAD_ROPE, FAM_GDN, FAM_SWIGLU, FAM_GATHER = 0, 1, 2, 3, 4
+FAM_NORM, FAM_HEAD_ROPE, FAM_GDN, FAM_SWIGLU, FAM_GATHER, FAM_BUNDLE = 0, 1, 2, 3, 4, 5
 VARIANT_AUTO, VARIANT_RING, VARIANT_DIRECT, VARIANT_ASYNC, VARIANT_WIDE, VARIANT_PAIR = 0, 1, 2, 3, 4, 5
+VARIANT_SPLIT = 6
 
 
 class WzybError(RuntimeError):
@@ -101,6 +102,26 @@ class ActArgs(ctypes.Structure):
         ("eps", c_float),
         ("gdn_w_offset", c_float),
         ("gate_mode", c_int),
+    ]
+
+
+class EmbedPleArgs(ctypes.Structure):
+    _fields_ = [
+        ("ids", c_void_p),
+        ("table", c_void_p),
+        ("vocab", c_int64),
+        ("hidden", c_int),
+        ("oob_policy", c_int),
+        ("d_oob_count", c_void_p),
+        ("emb_out", c_void_p),
+        ("ple_tables", POINTER(c_void_p)),
+        ("ple_heads", c_int),
+        ("ple_rows", c_int64),
+        ("ple_head_dim", c_int),
+        ("prev_ids", POINTER(c_int32)),
+        ("eos_id", c_int32),
+        ("hash_variant", c_int),
+        ("ple_out", c_void_p),
     ]
 
 
@@ -181,6 +202,7 @@ _SIGS = {
     "wzyb_ple_row_index": (c_uint32, [c_int32, c_int32, c_int32, c_int, c_int64, c_int32, c_int]),
     "wzyb_attn_prep_f16": (c_int, [POINTER(AttnPrepArgs), c_int64, S]),
     "wzyb_act_f16": (c_int, [POINTER(ActArgs), c_int64, S]),
+    "wzyb_embed_ple_f16": (c_int, [POINTER(EmbedPleArgs), c_int64, S]),
     "wzyb_shard_rows": (c_int, [c_int64, c_int, c_int, POINTER(c_int64), POINTER(c_int64)]),
     "wzyb_ple_halo": (c_int, [POINTER(c_int32), c_int64, POINTER(c_int32), POINTER(c_int32)]),
     "wzyb_prepare_device": (c_int, []),
@@ -336,7 +358,13 @@ def head_norm_rope(data, gamma, cos_tab, sin_tab, T, heads, head_dim, head_strid
 
 
 def head_tensor(data, gamma, heads, head_stride, row_stride) -> HeadTensor:
-    return HeadTensor(data.data_ptr(), gamma.data_ptr(), heads, head_stride, row_stride)
+    """A wzyb_head_tensor over torch tensors. The C struct holds raw pointers only; the element size of
+    data is kept on the Python object (elem_size) so wrappers can check it against the call's type."""
+    if data.element_size() != gamma.element_size():
+        raise ValueError("head_tensor: data and gamma must have the same element type")
+    t = HeadTensor(data.data_ptr(), gamma.data_ptr(), heads, head_stride, row_stride)
+    t.elem_size = data.element_size()
+    return t
 
 
 def qk_norm_rope_f16(q: HeadTensor, k: HeadTensor | None, cos_tab, sin_tab, T, head_dim, rot_dims=64, eps=1e-6,
@@ -364,6 +392,11 @@ def k_rope_kv_append(k, k_gamma, v, cos_tab, sin_tab, T, kv_heads, head_dim, cac
     """k norm + RoPE + INT8 KV append; with q (a HeadTensor of the same element type) the q heads are
     normed and rotated in the same launch."""
     f16 = k.element_size() == 2
+    if q is not None:
+        qsize = getattr(q, "elem_size", None)
+        if qsize is not None and qsize != k.element_size():
+            raise ValueError(f"k_rope_kv_append: q has {qsize}-byte elements, k has {k.element_size()}-byte; "
+                             "the fused q heads must have k's element type")
     rows = cos_tab.numel() // max(1, rot_dims // 2) if cos_tab is not None else 0
     args = (_ptr(k), _ptr(k_gamma), _ptr(v), _ptr(cos_tab), _ptr(sin_tab), rows, _ptr(d_base_pos), pos_offset, T,
             kv_heads, head_dim, rot_dims, eps, w_offset, ctypes.byref(cache), _stream(stream))
@@ -375,6 +408,17 @@ def k_rope_kv_append(k, k_gamma, v, cos_tab, sin_tab, T, kv_heads, head_dim, cac
 
 def rope_table(cos_tab, sin_tab, rows, rot_dims=64, theta=1e7, stream=None):
     call("wzyb_rope_table_f32", _ptr(cos_tab), _ptr(sin_tab), rows, rot_dims, theta, _stream(stream))
+
+
+def rope_table_host(rows, rot_dims=64, theta=1e7):
+    """The RoPE cos/sin tables [rows, rot_dims/2] fp32 built on the host by the reference's own procedure
+    (build_rope_cos_sin_host: fp64 angle, libm cos/sin, rounded to fp32), as numpy arrays."""
+    import numpy as np
+
+    c = np.empty((rows, rot_dims // 2), dtype=np.float32)
+    s = np.empty((rows, rot_dims // 2), dtype=np.float32)
+    call("wzyb_rope_table_host_f32", c.ctypes.data, s.ctypes.data, rows, rot_dims, theta)
+    return c, s
 
 
 def gdn_gated_norm(o, z, gamma, y, T, heads, head_dim=128, eps=1e-6, w_offset=0.0, gate_mode=GATE_SIGMOID,
@@ -421,6 +465,28 @@ def ple_gather_f16(tables, ids, out, prev_ids=None, eos_id=PLE_EOS_DEFAULT, hash
     prev = (c_int32 * 2)(*prev_ids) if prev_ids is not None else None
     call("wzyb_ple_gather_f16", arr, heads, rows, hd, _ptr(ids), ids.numel(), prev, eos_id, hash_variant, _ptr(out),
          _stream(stream))
+
+
+def embed_ple_args(table, ple_tables, ids, emb_out, ple_out, prev_ids=None, eos_id=PLE_EOS_DEFAULT,
+                   hash_variant=PLE_HASH_C_PRECEDENCE, oob_policy=OOB_CLAMP, oob_count=None) -> EmbedPleArgs:
+    """Arguments of wzyb_embed_ple_f16 (the token-embedding and PLE gathers of the same ids, one launch).
+    The returned struct keeps its host arrays alive."""
+    a = EmbedPleArgs()
+    a.ids, a.table = ids.data_ptr(), table.data_ptr()
+    a.vocab, a.hidden = table.shape
+    a.oob_policy, a.d_oob_count, a.emb_out = oob_policy, _ptr(oob_count), emb_out.data_ptr()
+    a._tabs = (c_void_p * len(ple_tables))(*[t.data_ptr() for t in ple_tables])
+    a.ple_tables = ctypes.cast(a._tabs, POINTER(c_void_p))
+    a.ple_heads = len(ple_tables)
+    a.ple_rows, a.ple_head_dim = ple_tables[0].shape
+    a._prev = (c_int32 * 2)(*prev_ids) if prev_ids is not None else None
+    a.prev_ids = ctypes.cast(a._prev, POINTER(c_int32)) if a._prev is not None else None
+    a.eos_id, a.hash_variant, a.ple_out = eos_id, hash_variant, ple_out.data_ptr()
+    return a
+
+
+def embed_ple_f16(args: EmbedPleArgs, T: int, stream=None):
+    call("wzyb_embed_ple_f16", ctypes.byref(args), T, _stream(stream))
 
 
 def ple_row_index(t0, t1, t2, head, rows, eos_id=PLE_EOS_DEFAULT, hash_variant=PLE_HASH_C_PRECEDENCE) -> int:

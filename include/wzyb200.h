@@ -392,10 +392,12 @@ uint32_t wzyb_ple_row_index(int32_t t0, int32_t t1, int32_t t2, int head, int64_
  * Layer bundles: the ops that the reference's prefill executor launches one after another inside a
  * layer (src/wzy_prefill_tc.cuh:697 residual norm and :862-867 q/k norm+RoPE; :942 SwiGLU and :845
  * GDN gated norm) and the rows its engine stages in one host routine (stage_emb_ple_pf,
- * src/wzy_engine_v2.cu:1210-1265), each bundle as ONE kernel launch. The ops of a bundle share no
- * tensor: the launch splits its persistent grid between them (each CTA runs one op's code, the
- * same code as the op's own entry point, so results are bit-identical to the separate calls).
- * The tensors of the two ops must not overlap; if they do, or if a shape is outside the one-launch
+ * src/wzy_engine_v2.cu:1210-1265). A bundle of up to 256 MiB of algorithmic bytes (e.g. 4096 tokens of
+ * the benchmark's layer) is ONE kernel launch: the ops share no tensor, and every CTA of the
+ * persistent grid runs both ops' code in turn (the same device code as the ops' own entry points, so
+ * results are bit-identical to the separate calls). Larger bundles are issued as the two ops' own
+ * launches, which measure as fast or faster once a launch's fixed costs are small against its
+ * traffic. The tensors of the two ops must not overlap; if they do, or if a shape is outside the one-launch
  * kernels' range (attn_prep: fp16 hidden <= 2560 and head_dim 64/128/256; act: head_dim 64/128/256;
  * embed_ple: PLE head_dim 64/128/256), or a non-default design was chosen with
  * wzyb_set_kernel_variant, the entry point issues the ops as separate launches in the order above.
@@ -492,7 +494,9 @@ int wzyb_read_faults(uint32_t* faults, int clear);
 /* Launch-shape tuning per kernel family (process-wide), for A/B measurement: CTAs per SM (1..16) and
  * TMA ring depth (0 = as deep as the shared-memory budget allows, else 1..64 stages) of the ring
  * design. Outside the ring: SwiGLU stages 1 / 2 force the scalar / packed math; head norm+RoPE
- * ctas_per_sm 2 selects the other instantiation of its design.
+ * ctas_per_sm 2 selects the other instantiation of its design. Layer bundles: stages picks the
+ * schedule (0 by size as above, 1 the persistent grid split between the ops, 2 one item per warp on a
+ * grid sized to the work, 3 both ops on every CTA, 4 the ops' own launches).
  * Families: 0 add+RMSNorm, 1 head norm+RoPE, 2 GDN gated norm, 3 SwiGLU, 4 gathers, 5 layer bundles. */
 #define WZYB_FAM_NORM 0
 #define WZYB_FAM_HEAD_ROPE 1

@@ -1,11 +1,14 @@
 """GPU parity of the one-launch layer bundles (wzyb_attn_prep_f16, wzyb_act_f16, wzyb_embed_ple_f16).
 
-Each bundle runs its two ops as roles of one persistent grid. Checked here:
+Each bundle of up to 256 MiB runs its two ops in one persistent grid (larger ones as the ops' own
+launches). Checked here:
   - against the oracle on the same seeded inputs (norms, RoPE, gate, SwiGLU within 2 fp16 ulp; the
     gathers and the residual bit-exact), at the configs' shapes (4096 tokens), a long call (20,000)
     and ragged short calls where some roles get a single CTA;
   - bit for bit against the same ops issued as separate launches (WZYB_VARIANT_SPLIT), since the one-
     launch kernels run the per-op device code;
+  - every grid schedule (split grid, one item per warp, both ops on every CTA) bit for bit against the
+    separate launches, at sizes where the ops get one item per warp, several, and uneven counts;
   - that tensors shared between the two ops make the entry point fall back to the ordered launches.
 """
 from __future__ import annotations
@@ -47,6 +50,7 @@ def _reset(wz):
     yield
     torch.cuda.synchronize()
     wz.set_kernel_variant(wz.FAM_BUNDLE, wz.VARIANT_AUTO)
+    wz.set_launch_tuning(wz.FAM_BUNDLE, 1, 0)
 
 
 def _bits(t):
@@ -203,3 +207,39 @@ def test_bundle_with_shared_tensor_keeps_launch_order(wz, orc):
     # the norm must have read the SwiGLU output that this library wrote
     want = orc.gdn_gated_norm(host(dact).reshape(T, H, ghd), z, gm, T, H, ghd, 1e-6, 0.0, 0)
     assert_f16_close(host(dgy), want, ULP_TOL, "gdn of the swiglu output")
+
+
+@pytest.mark.parametrize("sched", [1, 2, 3])
+@pytest.mark.parametrize("T", [3, 700, 4096, 9001])
+def test_bundle_schedules_bit_identical(wz, orc, sched, T):
+    """Each schedule of the one-launch grid (wzyb_set_launch_tuning(WZYB_FAM_BUNDLE, 1, sched): 1 split
+    grid, 2 one item per warp, 3 both ops on every CTA) against the ops' own launches, for all three
+    bundles, bit for bit (the schedules only move work between warps)."""
+    r = rng(1000 * sched + T)
+    wz.set_launch_tuning(wz.FAM_BUNDLE, 1, sched)
+    n, qh, kh, hd, rot, off = 2048, 16, 2, 256, 64, 5
+    inp = _attn_inputs(r, T, n, qh, kh, hd)
+    c_h, s_h = orc.rope_table(T + off, rot, 1e7)
+    c, s = dev(c_h), dev(s_h)
+    one = _run_attn(wz, inp, c, s, T, n, qh, kh, hd, rot, off, wz.VARIANT_AUTO)
+    split = _run_attn(wz, inp, c, s, T, n, qh, kh, hd, rot, off, wz.VARIANT_SPLIT)
+    for key in one:
+        assert np.array_equal(one[key], split[key]), f"attn sched {sched}: {key} differs"
+    rows, ffn, H, ghd = 11 * T, 512, 32, 128
+    ainp = dict(g=f16n(r, (rows, ffn), 2.0), u=f16n(r, (rows, ffn)), o=f16n(r, (T, H, ghd)),
+                z=f16n(r, (T, H, ghd)), gm=f16n(r, (ghd,), 0.02, 1.0))
+    one = _run_act(wz, ainp, T, rows, ffn, H, ghd, 0, wz.VARIANT_AUTO)
+    split = _run_act(wz, ainp, T, rows, ffn, H, ghd, 0, wz.VARIANT_SPLIT)
+    for key in one:
+        assert np.array_equal(one[key], split[key]), f"act sched {sched}: {key} differs"
+    vocab, hidden, heads, prow, phd = 6000, 2048, 16, 4099, 128
+    table = f16n(r, (vocab, hidden), 0.02)
+    tabs = [f16n(r, (prow, phd), 0.02) for _ in range(heads)]
+    ids = r.integers(-2, vocab + 2, T).astype(np.int32)
+    dt, dtabs, dids = dev(table), [dev(t) for t in tabs], dev(ids)
+    e1, p1, c1 = _run_embed_ple(wz, dt, dtabs, dids, T, hidden, heads, phd, (3, 4), wz.VARIANT_AUTO)
+    e2, p2, c2 = _run_embed_ple(wz, dt, dtabs, dids, T, hidden, heads, phd, (3, 4), wz.VARIANT_SPLIT)
+    assert np.array_equal(e1, e2) and np.array_equal(p1, p2) and c1 == c2, f"embed_ple sched {sched} differs"
+    want_e, bad = orc.embed_gather_rows(table, ids, 0)
+    assert np.array_equal(e1, want_e.view(np.uint16)) and c1 == bad
+    assert wz.read_faults() == 0

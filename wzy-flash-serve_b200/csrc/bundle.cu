@@ -5,15 +5,16 @@
 // norm + RoPE at :862-867; the SwiGLU at :942 and the GDN gated norm at :845) and stages the
 // token-embedding and PLE rows of a chunk in one host routine (stage_emb_ple_pf,
 // src/wzy_engine_v2.cu:1210-1265). The two ops of each bundle share no tensor, so here a bundle is ONE
-// persistent grid whose CTAs are split between the two ops: CTAs [0, g0) run op 0's body, CTAs
-// [g0, grid) op 1's. The bodies are the per-op kernels' own device code (norm_rows.cu, head_rope.cu,
-// swiglu.cu, gdn_norm.cu, gather.cu), so every output is bit-identical to the separate launches.
+// persistent grid in which every CTA runs both ops' bodies in turn (by default; the schedules below
+// also split the grid between the ops). The bodies are the per-op kernels' own device code
+// (norm_rows.cu, head_rope.cu, swiglu.cu, gdn_norm.cu, gather.cu), so every output is bit-identical
+// to the separate launches.
 //
 // Why: at layer-sized calls (4096 tokens, 67-140 MB per op) a launch is dominated by its fixed costs --
 // the launch itself, the DRAM ramp while the first loads are in flight, and the tail where the last
 // warps finish alone. One grid pays them once per bundle, and DRAM streams both ops' traffic at once.
-// The split of the grid is chosen on the host so that the most loaded warp of either op moves as few
-// bytes as possible (each op's items are dealt to its warps in turn).
+// Past a few L2's worth of bytes those costs are small, and the ops' own launches (each with its own
+// tuned occupancy) are as fast or faster, so large bundles are issued that way.
 #include "launch.hpp"
 
 namespace wzyb {
@@ -49,14 +50,43 @@ static int split_grid(int G, const RoleWork& r0, const RoleWork& r1) {
     return best;
 }
 
+// Schedules of a bundle's grid (wzyb_set_launch_tuning(WZYB_FAM_BUNDLE, ., schedule) for A/B):
+enum BundleSchedule : int {
+    kSchedAuto = 0,
+    kSchedSplit = 1,    // persistent grid split between the ops (CTAs [0, g0) op 0, the rest op 1)
+    kSchedPerItem = 2,  // one item per warp: the grid is sized to the work and the hardware's CTA
+                        // scheduler balances it (op 0's CTAs first)
+    kSchedShared = 3,   // persistent grid, every CTA runs both ops
+    kSchedLaunches = 4, // each op as its own launch
+};
+// Bundles of up to this many algorithmic bytes run as one launch with both ops on every CTA; larger
+// ones as the ops' own launches. Measured on B200 with L2 flushed before each call (us, one launch
+// with both ops per CTA / split grid / separate launches): attn_prep 142.6 MB (4096 tokens) 32.0 /
+// 32.1 / 33.8, act 239 MB 41.0 / 41.0 / 42.0, embed_ple 67 MB 16.4 / 18.5 / 17.4; at 4x the tokens the
+// separate launches are as fast or faster (embed_ple 268 MB 49.3 / 59.2 / 46.1) and at 262,144 tokens
+// faster (attn_prep 1642 / 1687 / 1506, act 2498 / 2546 / 2475): each op's own launch has its
+// own tuned occupancy, and a launch's fixed costs no longer matter.
+constexpr double kFuseMaxBytes = 256.0 * (1 << 20);
+
+static int bundle_schedule(double bundle_bytes) {
+    const int s = tuning(kFamBundle).stages;
+    if (s >= kSchedSplit && s <= kSchedLaunches) return s;
+    return bundle_bytes <= kFuseMaxBytes ? kSchedShared : kSchedLaunches;
+}
+
 // Grid and split for a bundle: every SM filled with `resident` CTAs, or, when the two ops together
-// have no more items than that many warps, one item per warp.
-static void bundle_grid(const DeviceInfo& di, int resident, const RoleWork& r0, const RoleWork& r1, int& grid,
-                        int& g0) {
+// have no more items than that many warps (or the schedule asks for it), one item per warp. g0 < 0
+// asks every CTA to run both ops.
+static void bundle_grid(const DeviceInfo& di, int resident, const RoleWork& r0, const RoleWork& r1, int sched,
+                        int& grid, int& g0) {
     const int64_t need0 = (r0.items + kBundleWarps - 1) / kBundleWarps;
     const int64_t need1 = (r1.items + kBundleWarps - 1) / kBundleWarps;
     const int64_t full = (int64_t)di.sms * resident;
-    if (need0 + need1 <= full) {
+    if (sched == kSchedShared) {
+        const int64_t need = need0 > need1 ? need0 : need1;
+        grid = (int)(need < full ? need : full);
+        g0 = -1;
+    } else if (need0 + need1 <= full || sched == kSchedPerItem) {
         g0 = (int)need0;
         grid = (int)(need0 + need1);
     } else if (need0 == 0 || need1 == 0) {
@@ -101,11 +131,17 @@ static int64_t head_span_bytes(const HeadSection& s, int64_t T, int hd, int esiz
 // ---------------------------------------------------------------------------------------------
 // configs[1] bundle: residual add + RMSNorm rows (direct design) and q/k norm + RoPE (pair design).
 // ---------------------------------------------------------------------------------------------
+// g_norm < 0: every CTA runs both ops over the whole grid (the q/k heads first, since their body
+// opens with a CTA barrier, then the norm rows with the CTA order reversed, so the warps that took
+// one more head item than others take one row fewer).
 template <int VPL, int HD>
 __global__ void __launch_bounds__(kBundleThreads, 2) attn_prep_kernel(const NormRowsArgs na, const HeadRopeArgs ha,
                                                                       int g_norm) {
     pdl_begin();
-    if ((int)blockIdx.x < g_norm) {
+    if (g_norm < 0) {
+        head_rope_pair_body<__half, HD, 3>(ha, blockIdx.x, gridDim.x);
+        norm_rows_direct_body<__half, __half, VPL>(na, (int)gridDim.x - 1 - (int)blockIdx.x, gridDim.x);
+    } else if ((int)blockIdx.x < g_norm) {
         norm_rows_direct_body<__half, __half, VPL>(na, blockIdx.x, g_norm);
     } else {
         head_rope_pair_body<__half, HD, 3>(ha, (int)blockIdx.x - g_norm, (int)gridDim.x - g_norm);
@@ -141,7 +177,9 @@ static int attn_prep_run(const wzyb_attn_prep_args* p, int64_t T, cudaStream_t s
     const int vpl_need = (n + 255) / 256;
     const int vpl = vpl_need <= 2 ? 2 : vpl_need <= 4 ? 4 : vpl_need <= 8 ? 8 : vpl_need <= 10 ? 10 : 0;
     const int vn = variant(kFamNorm), vh = variant(kFamHeadRope);
-    bool fused = variant(kFamBundle) != WZYB_VARIANT_SPLIT && vpl != 0 &&
+    const double bytes = (double)T * (8.0 * n + 4.0 * (q.heads + k.heads) * hd);
+    const int sched = bundle_schedule(bytes);
+    bool fused = variant(kFamBundle) != WZYB_VARIANT_SPLIT && sched != kSchedLaunches && vpl != 0 &&
                  (vn == WZYB_VARIANT_AUTO || vn == WZYB_VARIANT_DIRECT) &&
                  (vh == WZYB_VARIANT_AUTO || vh == WZYB_VARIANT_PAIR) && tuning(kFamHeadRope).ctas_per_sm != 2;
     if (fused) {
@@ -174,7 +212,7 @@ static int attn_prep_run(const wzyb_attn_prep_args* p, int64_t T, cudaStream_t s
     const RoleWork r_norm{T, (double)(4 * (int64_t)n * 2)};
     const RoleWork r_head{T * chunks, 2.0 * htot * hd * 2 / (double)chunks};
     int grid = 0, g0 = 0;
-    bundle_grid(di, resident_ctas(kern, kBundleThreads, 0), r_norm, r_head, grid, g0);
+    bundle_grid(di, resident_ctas(kern, kBundleThreads, 0), r_norm, r_head, sched, grid, g0);
     if (vpl == 2) attn_prep_launch<2>(hd, grid, stream, na, ha, g0);
     else if (vpl == 4) attn_prep_launch<4>(hd, grid, stream, na, ha, g0);
     else if (vpl == 8) attn_prep_launch<8>(hd, grid, stream, na, ha, g0);
@@ -190,7 +228,11 @@ __global__ void __launch_bounds__(kBundleThreads, 3) act_kernel(const __half* __
                                                                 const __half* __restrict__ up, __half* __restrict__ out,
                                                                 int64_t nvec, const GdnArgs ga, int g_swiglu) {
     pdl_begin();
-    if ((int)blockIdx.x < g_swiglu) {
+    if (g_swiglu < 0) {  // both ops on every CTA (as attn_prep_kernel)
+        gdn_direct_body<__half, __half, HD, 4, SILU>(ga, blockIdx.x, gridDim.x);
+        swiglu_body<__half, __half, false, PACKED>(gate, up, out, nvec, 0, 0, (int)gridDim.x - 1 - (int)blockIdx.x,
+                                                   gridDim.x);
+    } else if ((int)blockIdx.x < g_swiglu) {
         swiglu_body<__half, __half, false, PACKED>(gate, up, out, nvec, 0, 0, blockIdx.x, g_swiglu);
     } else {
         gdn_direct_body<__half, __half, HD, 4, SILU>(ga, (int)blockIdx.x - g_swiglu, (int)gridDim.x - g_swiglu);
@@ -225,7 +267,10 @@ static int act_run(const wzyb_act_args* p, int64_t T, cudaStream_t stream) {
 
     const int hd = p->gdn_head_dim;
     const int vg = variant(kFamGdn);
-    bool fused = variant(kFamBundle) != WZYB_VARIANT_SPLIT && (vg == WZYB_VARIANT_AUTO || vg == WZYB_VARIANT_DIRECT) &&
+    const double bytes = 6.0 * (double)n + 6.0 * (double)T * p->gdn_heads * hd;
+    const int sched = bundle_schedule(bytes);
+    bool fused = variant(kFamBundle) != WZYB_VARIANT_SPLIT && sched != kSchedLaunches &&
+                 (vg == WZYB_VARIANT_AUTO || vg == WZYB_VARIANT_DIRECT) &&
                  n > 0 && T > 0;
     if (fused) {
         const int64_t gb = T * p->gdn_heads * (int64_t)hd * 2;
@@ -256,7 +301,7 @@ static int act_run(const wzyb_act_args* p, int64_t T, cudaStream_t stream) {
     const RoleWork r_swiglu{(nvec + 127) / 128, 128.0 * 48.0};
     const RoleWork r_gdn{T * slabs, 3.0 * p->gdn_heads * hd * 2 / (double)slabs};
     int grid = 0, g0 = 0;
-    bundle_grid(di, resident_ctas(kern, kBundleThreads, 0), r_swiglu, r_gdn, grid, g0);
+    bundle_grid(di, resident_ctas(kern, kBundleThreads, 0), r_swiglu, r_gdn, sched, grid, g0);
     const __half* g = (const __half*)p->gate;
     const __half* u = (const __half*)p->up;
     __half* o = (__half*)p->act;
@@ -276,7 +321,10 @@ static int act_run(const wzyb_act_args* p, int64_t T, cudaStream_t stream) {
 template <int CH, int U>
 __global__ void __launch_bounds__(kBundleThreads) embed_ple_kernel(const EmbedArgs ea, const PleArgs pa, int g_embed) {
     pdl_begin();
-    if ((int)blockIdx.x < g_embed) {
+    if (g_embed < 0) {  // both ops on every CTA (as attn_prep_kernel)
+        gather_rows_body(ea, blockIdx.x, gridDim.x);
+        ple_gather_groups_body<CH, U>(pa, (int)gridDim.x - 1 - (int)blockIdx.x, gridDim.x);
+    } else if ((int)blockIdx.x < g_embed) {
         gather_rows_body(ea, blockIdx.x, g_embed);
     } else {
         ple_gather_groups_body<CH, U>(pa, (int)blockIdx.x - g_embed, (int)gridDim.x - g_embed);
@@ -300,7 +348,9 @@ static int embed_ple_run(const wzyb_embed_ple_args* p, int64_t T, cudaStream_t s
     if (rc != WZYB_OK || T == 0) return rc;
 
     const int ch = pa.chunks;
-    bool fused = variant(kFamBundle) != WZYB_VARIANT_SPLIT && (ch == 8 || ch == 16 || ch == 32);
+    const double bytes = (double)T * (4.0 * p->hidden + 4.0 * p->ple_heads * p->ple_head_dim);
+    const int sched = bundle_schedule(bytes);
+    bool fused = variant(kFamBundle) != WZYB_VARIANT_SPLIT && sched != kSchedLaunches && (ch == 8 || ch == 16 || ch == 32);
     if (fused) {
         const int64_t erow = (int64_t)p->hidden * 2, prow = (int64_t)p->ple_head_dim * 2;
         const Span w0[2] = {span(p->emb_out, T * erow), span(p->d_oob_count, 4)};
@@ -310,6 +360,10 @@ static int embed_ple_run(const wzyb_embed_ple_args* p, int64_t T, cudaStream_t s
         r1[0] = span(p->ids, T * 4);
         for (int h = 0; h < 32; ++h) r1[1 + h] = span(h < p->ple_heads ? p->ple_tables[h] : nullptr, p->ple_rows * prow);
         fused = !ops_conflict(w0, r0, w1, r1);
+    }
+    if (fused && variant(kFamGather) == WZYB_VARIANT_RING) {
+        rc = gather_bulk_launch(ea, pa, stream);  // both gathers as bulk copies in one launch
+        if (rc != WZYB_ERR_SHAPE) return rc;
     }
     if (!fused) {
         rc = wzyb_embed_gather_f16(p->table, p->vocab, p->hidden, p->ids, T, p->emb_out, p->oob_policy,
@@ -328,7 +382,7 @@ static int embed_ple_run(const wzyb_embed_ple_args* p, int64_t T, cudaStream_t s
     const RoleWork r_embed{T, 2.0 * (double)ea.row_chunks * 16.0};
     const RoleWork r_ple{(T * p->ple_heads + gpw - 1) / gpw, gpw * 2.0 * ch * 16.0};
     int grid = 0, g0 = 0;
-    bundle_grid(di, resident_ctas(kern, kBundleThreads, 0), r_embed, r_ple, grid, g0);
+    bundle_grid(di, resident_ctas(kern, kBundleThreads, 0), r_embed, r_ple, sched, grid, g0);
     if (ch == 8) embed_ple_launch<8>(grid, stream, ea, pa, g0);
     else if (ch == 16) embed_ple_launch<16>(grid, stream, ea, pa, g0);
     else embed_ple_launch<32>(grid, stream, ea, pa, g0);

@@ -278,6 +278,186 @@ static int ple_prepare(const uint16_t* const* tables, int heads, int64_t rows_pe
     return WZYB_OK;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Bulk design (TMA): both gathers as 1-D bulk copies through shared memory, no data in registers.
+//
+// A warp owns a ring of S shared-memory slots with one mbarrier each. For each of its units -- a
+// token's embedding row, or a token's `heads` PLE rows, which land side by side in the slot exactly
+// as they sit in the output row -- it issues bulk loads (cp.async.bulk global -> shared, completion
+// counted on the slot's mbarrier: one load per row, the PLE rows' loads from `heads` lanes at once),
+// then, once the slot is full, one bulk store of the whole output row (cp.async.bulk shared -> global,
+// a bulk async-group). A slot is refilled with the unit S ahead after the store that read it has
+// finished reading (wait_group.read), one unit behind the newest store. The ids of the warp's next
+// 32 units are loaded up front, one unit per lane, and broadcast by shuffle, so issuing a unit waits
+// on no global load. With S slots per warp, S units per warp are in flight: at 4096 tokens nearly
+// every row of the call is requested at once, which the register designs cannot hold.
+// Every wait is bounded; a warp whose wait gives up raises WZYB_FAULT_WAIT_TIMEOUT, drains the loads
+// it issued (bounded) and its stores, and stops.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// all but the newest N bulk groups of this thread have finished reading their shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// order this thread's generic-proxy view of shared memory before its later async-proxy operations
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+constexpr int kBulkWarps = 4;                 // warps per CTA, each with its own ring
+constexpr uint32_t kBulkMaxSlot = 16 * 1024;  // largest unit (output row) the bulk design stages
+
+struct BulkGatherArgs {
+    EmbedArgs e;      // token rows (e.T == 0: none)
+    PleArgs p;        // PLE rows of the same ids (p.T == 0: none)
+    int64_t units;    // e.T + p.T
+    uint32_t slot_bytes;
+    int stages;       // slots per warp
+};
+
+__global__ void __launch_bounds__(kBulkWarps * 32) gather_bulk_kernel(const BulkGatherArgs a) {
+    pdl_begin();
+    extern __shared__ __align__(128) unsigned char smem_bg[];
+    const int S = a.stages;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_bg) + warp * S;
+    unsigned char* ring = smem_bg + ((kBulkWarps * S * 8 + 127) & ~127) + (size_t)warp * S * a.slot_bytes;
+    const int64_t GW = (int64_t)gridDim.x * kBulkWarps;
+    const int64_t gw = (int64_t)blockIdx.x * kBulkWarps + warp;
+    if (gw >= a.units) return;  // warp-uniform; this warp has no unit
+    const int64_t nmine = (a.units - 1 - gw) / GW + 1;
+    const int64_t Te = a.e.T;
+    const uint32_t erow = (uint32_t)(a.e.row_chunks * 16), hbytes = (uint32_t)(a.p.chunks * 16);
+    const uint32_t prow = hbytes * (uint32_t)a.p.heads;
+
+    if (lane == 0) {
+        for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    const uint64_t pol = policy_evict_first();
+
+    // ids of units [32c, 32c + 32) of this warp, one unit per lane: (t0, h1, h2) of its token
+    int32_t my_t0 = 0, my_h1 = 0, my_h2 = 0;
+    int64_t chunk = -1;
+    auto load_ids = [&](int64_t c) {
+        const int64_t k = c * 32 + lane;
+        if (k < nmine) {
+            const int64_t u = gw + k * GW;
+            const int64_t t = u < Te ? u : u - Te;
+            my_t0 = __ldg(a.e.ids + t);
+            if (u >= Te) {
+                my_h1 = t >= 1 ? __ldg(a.e.ids + t - 1) : a.p.prev1;
+                my_h2 = t >= 2 ? __ldg(a.e.ids + t - 2) : (t == 1 ? a.p.prev1 : a.p.prev2);
+            }
+        }
+        chunk = c;
+    };
+    // issue the loads of unit k into slot k % S (warp-collective)
+    auto issue = [&](int64_t k) {
+        if (k / 32 != chunk) load_ids(k / 32);
+        const int src = (int)(k & 31);
+        const int32_t t0 = __shfl_sync(0xffffffffu, my_t0, src);
+        const int32_t h1 = __shfl_sync(0xffffffffu, my_h1, src);
+        const int32_t h2 = __shfl_sync(0xffffffffu, my_h2, src);
+        const int64_t u = gw + k * GW;
+        const int s = (int)(k % S);
+        unsigned char* slot = ring + (size_t)s * a.slot_bytes;
+        if (u < Te) {
+            if (lane == 0) {
+                const int64_t id = resolve_id(t0, a.e.vocab, a.e.policy, a.e.oob, 0);
+                mbar_arrive_expect_tx(&bars[s], erow);
+                bulk_load(slot, reinterpret_cast<const unsigned char*>(a.e.table) + id * erow, erow, &bars[s], pol);
+            }
+        } else {
+            if (lane == 0) mbar_arrive_expect_tx(&bars[s], prow);
+            __syncwarp();
+            for (int h = lane; h < a.p.heads; h += 32) {
+                const uint32_t row = ple_row_fast(t0, h1, h2, h, a.p.rows, a.p.rows_mask, a.p.eos, a.p.variant);
+                bulk_load(slot + (size_t)h * hbytes,
+                          reinterpret_cast<const unsigned char*>(a.p.tables[h]) + (size_t)row * hbytes, hbytes,
+                          &bars[s], pol);
+            }
+        }
+    };
+
+    const int64_t pre = nmine < S ? nmine : (int64_t)S;
+    for (int64_t k = 0; k < pre; ++k) issue(k);
+    int64_t issued = pre;
+    bool ok = true;
+    int64_t k = 0;
+    for (; k < nmine; ++k) {
+        const int s = (int)(k % S);
+        if (lane == 0) ok = mbar_wait(&bars[s], (uint32_t)((k / S) & 1));
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
+        const int64_t u = gw + k * GW;
+        if (lane == 0) {
+            fence_proxy_async_smem();
+            if (u < Te) bulk_store(reinterpret_cast<unsigned char*>(a.e.out) + u * erow, ring + (size_t)s * a.slot_bytes, erow);
+            else bulk_store(reinterpret_cast<unsigned char*>(a.p.out) + (u - Te) * prow, ring + (size_t)s * a.slot_bytes, prow);
+            bulk_commit();
+            bulk_wait_read<1>();  // the store of unit k - 1 has read its slot
+        }
+        __syncwarp();
+        // refill the slot of unit k - 1 with unit k - 1 + S (the first slot is refilled one unit late)
+        if (k >= 1 && issued < nmine) {
+            issue(issued);
+            ++issued;
+        }
+    }
+    if (!ok) {
+        // drain the loads that were issued but not consumed, then stop
+        if (lane == 0) {
+            const unsigned long long deadline = globaltimer_ns() + kWaitLimitNs;
+            for (int64_t i = k; i < issued; ++i)
+                if (!mbar_wait_until(&bars[i % S], (uint32_t)((i / S) & 1), deadline)) break;
+        }
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+}
+
+// Launch of the bulk design over an embedding gather (e.T > 0) and/or a PLE gather (p.T > 0) of the
+// same ids. Returns WZYB_OK, a launch status, or WZYB_ERR_SHAPE when a unit does not fit a slot.
+static int gather_bulk_launch(const EmbedArgs& e, const PleArgs& p, cudaStream_t stream) {
+    BulkGatherArgs a;
+    a.e = e;
+    a.p = p;
+    a.units = e.T + p.T;
+    if (a.units == 0) return WZYB_OK;
+    const uint32_t erow = e.T > 0 ? (uint32_t)(e.row_chunks * 16) : 0u;
+    const uint32_t prow = p.T > 0 ? (uint32_t)(p.chunks * 16 * p.heads) : 0u;
+    const uint32_t unit = erow > prow ? erow : prow;
+    if (unit == 0 || unit > kBulkMaxSlot) return WZYB_ERR_SHAPE;
+    a.slot_bytes = (unit + 127u) & ~127u;
+    DeviceInfo di;
+    int rc = device_info(&di);
+    if (rc != WZYB_OK) return rc;
+    const Tuning tu = tuning(kFamGather);
+    const int ctas_per_sm = tu.ctas_per_sm >= 1 && tu.ctas_per_sm <= 4 ? tu.ctas_per_sm : 1;
+    int stages = (int)(kSmemPerSm / ctas_per_sm / kBulkWarps / a.slot_bytes);
+    if (tu.stages > 0 && tu.stages < stages) stages = tu.stages;
+    if (stages < 2) return WZYB_ERR_SHAPE;
+    // no more slots than units per warp at one CTA per SM
+    const int64_t per_warp = (a.units + (int64_t)di.sms * kBulkWarps - 1) / ((int64_t)di.sms * kBulkWarps);
+    if (per_warp < stages) stages = per_warp < 2 ? 2 : (int)per_warp;
+    a.stages = stages;
+    const int smem = ((kBulkWarps * stages * 8 + 127) & ~127) + kBulkWarps * stages * (int)a.slot_bytes;
+    rc = ensure_smem((const void*)gather_bulk_kernel, smem);
+    if (rc != WZYB_OK) return rc;
+    const int grid = persistent_grid(di, ctas_per_sm, (a.units + kBulkWarps - 1) / kBulkWarps);
+    launch_k(gather_bulk_kernel, grid, kBulkWarps * 32, (size_t)smem, stream, a);
+    return launch_status();
+}
+
 static int grid_for(int64_t work_threads, int ctas_per_sm, const DeviceInfo& di) {
     return persistent_grid(di, ctas_per_sm, (work_threads + kGatherThreads - 1) / kGatherThreads);
 }
@@ -291,6 +471,10 @@ int wzyb_embed_gather_rows(const void* table, int64_t vocab, int64_t row_bytes, 
     wzyb::EmbedArgs a;
     int rc = wzyb::embed_prepare(table, vocab, row_bytes, ids, T, out, oob_policy, d_oob_count, a);
     if (rc != WZYB_OK || T == 0) return rc;
+    if (wzyb::variant(wzyb::kFamGather) == WZYB_VARIANT_RING && row_bytes <= wzyb::kBulkMaxSlot) {
+        wzyb::PleArgs none = {};
+        return wzyb::gather_bulk_launch(a, none, (cudaStream_t)stream);
+    }
     wzyb::DeviceInfo di;
     rc = wzyb::device_info(&di);
     if (rc != WZYB_OK) return rc;
@@ -333,6 +517,12 @@ int wzyb_ple_gather_f16(const uint16_t* const* tables, int heads, int64_t rows_p
     wzyb::PleArgs a;
     int rc = wzyb::ple_prepare(tables, heads, rows_per_table, head_dim, ids, T, prev_ids, eos_id, hash_variant, out, a);
     if (rc != WZYB_OK || T == 0) return rc;
+    if (wzyb::variant(wzyb::kFamGather) == WZYB_VARIANT_RING && (int64_t)head_dim * 2 * heads <= wzyb::kBulkMaxSlot) {
+        // the bulk design reads the ids through EmbedArgs; no token rows
+        wzyb::EmbedArgs none = {};
+        none.ids = ids;
+        return wzyb::gather_bulk_launch(none, a, (cudaStream_t)stream);
+    }
     wzyb::DeviceInfo di;
     rc = wzyb::device_info(&di);
     if (rc != WZYB_OK) return rc;

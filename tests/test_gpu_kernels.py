@@ -562,6 +562,36 @@ def test_kv_append_int8_f32(wz, orc, T, heads, hd, base, cap, max_ctx, full):
         assert np.array_equal(_kv_host(d, nm), getattr(c, nm)), nm
 
 
+def test_kv_append_codes_at_rounding_boundaries(wz, orc):
+    """The INT8 codes are rint(x / d) of the correctly rounded quotient. Values are placed on and one or
+    two fp32 ulps either side of every half-integer multiple (n + 0.5) * d of their group's scale, and
+    on the integers, where a quotient off by one ulp would change the code; bit-exact against the
+    oracle's IEEE division."""
+    r = rng(4242)
+    T, heads, hd = 2048, 2, 256
+    kvd = heads * hd
+    groups = T * kvd // 64
+    amax = (np.exp(r.uniform(-12, 6, groups)) * np.where(r.random(groups) < 0.5, -1, 1)).astype(np.float32)
+    d = (np.abs(amax) / np.float32(127)).astype(np.float32).astype(np.float16).astype(np.float32)
+    n = r.integers(-127, 127, (groups, 63)).astype(np.float64)
+    half = r.random((groups, 63)) < 0.8
+    x = ((n + np.where(half, 0.5, 0.0)) * d[:, None].astype(np.float64)).astype(np.float32)
+    step = r.integers(-2, 3, (groups, 63))
+    x = np.where(step > 0, np.nextafter(x, np.float32(np.inf)), np.where(step < 0, np.nextafter(x, np.float32(-np.inf)), x))
+    x = np.where(np.abs(step) == 2, np.where(step > 0, np.nextafter(x, np.float32(np.inf)),
+                                             np.nextafter(x, np.float32(-np.inf))), x).astype(np.float32)
+    grp = np.concatenate([amax[:, None], x], axis=1)
+    idx = np.argsort(r.random((groups, 64)), axis=1)
+    grp = np.take_along_axis(grp, idx, axis=1)
+    k = grp.reshape(T, kvd).astype(np.float32)
+    v = np.ascontiguousarray(k[::-1])
+    c, dd = _kv_seeded(orc, r, T, T, kvd, True)
+    orc.kv_append_int8_f32(k, v, T, kvd, 0, c)
+    wz.kv_append_int8_f32(dev(k), dev(v), T, heads, hd, _kv_desc(wz, dd, T, T, True))
+    for nm in _KV_PLANES:
+        assert np.array_equal(_kv_host(dd, nm), getattr(c, nm)), nm
+
+
 @pytest.mark.parametrize("dtype", [np.float16, np.float32])
 @pytest.mark.parametrize("T,heads,hd,base", [(5, 2, 256, 17), (4096, 2, 256, 0), (33, 1, 128, 3)])
 def test_k_rope_kv_append_fused(wz, orc, dtype, T, heads, hd, base):

@@ -442,7 +442,8 @@ static int gather_bulk_launch(const EmbedArgs& e, const PleArgs& p, cudaStream_t
     int rc = device_info(&di);
     if (rc != WZYB_OK) return rc;
     const Tuning tu = tuning(kFamGather);
-    const int ctas_per_sm = tu.ctas_per_sm >= 1 && tu.ctas_per_sm <= 4 ? tu.ctas_per_sm : 1;
+    int ctas_per_sm = tu.ctas_per_sm >= 1 && tu.ctas_per_sm <= 4 ? tu.ctas_per_sm : 1;
+    while (ctas_per_sm > 1 && kSmemPerSm / ctas_per_sm / kBulkWarps / (int)a.slot_bytes < 2) --ctas_per_sm;
     int stages = (int)(kSmemPerSm / ctas_per_sm / kBulkWarps / a.slot_bytes);
     if (tu.stages > 0 && tu.stages < stages) stages = tu.stages;
     if (stages < 2) return WZYB_ERR_SHAPE;

@@ -42,6 +42,8 @@ struct KvAppendArgs {
     float w_offset;
     int norm_rope;
     wzyb_kv_cache c;
+    uint64_t ring_div;    // divisor of the ring cell: ring_cap, or ring_cap - 4096 past the pinned sink
+    uint64_t ring_recip;  // floor((2^64 - 1) / ring_div), for mod_u64
     // optional q heads, normed and rotated in place in the same launch (q_heads == 0: none)
     void* q;
     const void* q_gamma;
@@ -57,10 +59,11 @@ __device__ __forceinline__ bool kv_in_ring(int64_t p, int64_t end, int64_t cap) 
     return p >= (lo > kKvSinkPin ? lo : kKvSinkPin);
 }
 
-__device__ __forceinline__ int64_t kv_ring_cell(int64_t p, int64_t cap) {
-    if (cap <= 2 * kKvSinkPin) return p % cap;
+// p >= 0; div and recip as KvAppendArgs::ring_div / ring_recip
+__device__ __forceinline__ int64_t kv_ring_cell(int64_t p, int64_t cap, uint64_t div, uint64_t recip) {
+    if (cap <= 2 * kKvSinkPin) return (int64_t)mod_u64((uint64_t)p, div, recip);
     if (p < kKvSinkPin) return p;
-    return kKvSinkPin + (p - kKvSinkPin) % (cap - kKvSinkPin);
+    return kKvSinkPin + (int64_t)mod_u64((uint64_t)(p - kKvSinkPin), div, recip);
 }
 
 // Quantise this lane's 8 elements as part of its 64-element group (lanes 8m..8m+7) and store the codes
@@ -76,11 +79,18 @@ __device__ __forceinline__ void kv_q8_store(const float2 (&x)[4], bool act, int 
     if (!act) return;
     const __half sh = __float2half_rn(am / 127.0f);
     const float d = __half2float(sh);
+    // v / d correctly rounded without a division per element (Markstein's theorem: with r = RN(1/d)
+    // and q0 = RN(v*r) within one ulp of v/d, the residual e = v - q0*d is exact under FMA and
+    // RN(q0 + e*r) is the correctly rounded quotient). d is 0 or an fp16 value >= 2^-24, so nothing
+    // underflows where the rounding can change the code (|v/d| >= 0.5).
+    const float r = d > 0.f ? __frcp_rn(d) : 0.f;
     uint32_t w[2] = {0u, 0u};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const float v = (i & 1) ? x[i >> 1].y : x[i >> 1].x;
-        const int qi = d > 0.f ? max(-127, min(127, __float2int_rn(v / d))) : 0;
+        const float q0 = __fmul_rn(v, r);
+        const float q = __fmaf_rn(__fmaf_rn(-q0, d, v), r, q0);
+        const int qi = d > 0.f ? max(-127, min(127, __float2int_rn(q))) : 0;
         w[i >> 2] |= ((uint32_t)(qi & 0xFF)) << ((i & 3) * 8);
     }
     const uint2 packed = make_uint2(w[0], w[1]);
@@ -212,7 +222,7 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
         const int64_t pos = base + t;
         const bool keep = pos >= 0 && pos < a.c.max_ctx;
         const bool ring = keep && kv_in_ring(pos, end, a.c.ring_cap);
-        const int64_t rcell = ring ? kv_ring_cell(pos, a.c.ring_cap) : 0;
+        const int64_t rcell = ring ? kv_ring_cell(pos, a.c.ring_cap, a.ring_div, a.ring_recip) : 0;
         const bool full = keep && a.c.full_k_q != nullptr;
         const bool pos_ok = half > 0 && pos >= 0 && pos < a.table_rows;
         float2 c2[4], s2[4];
@@ -253,8 +263,7 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
 }
 
 template <typename T>
-static int launch_kv_append(const KvAppendArgs& a0, int head_dim, cudaStream_t stream) {
-    const KvAppendArgs& a = a0;
+static int launch_kv_append(KvAppendArgs a, int head_dim, cudaStream_t stream) {
     const wzyb_kv_cache& c = a.c;
     if (!a.k || !a.v || !c.ring_k_q || !c.ring_k_s || !c.ring_v_q || !c.ring_v_s) return WZYB_ERR_NULL;
     const bool has_full = c.full_k_q || c.full_k_s || c.full_v_q || c.full_v_s;
@@ -296,6 +305,8 @@ static int launch_kv_append(const KvAppendArgs& a0, int head_dim, cudaStream_t s
     DeviceInfo di;
     const int rc = device_info(&di);
     if (rc != WZYB_OK) return rc;
+    a.ring_div = (uint64_t)(c.ring_cap <= 2 * kKvSinkPin ? c.ring_cap : c.ring_cap - kKvSinkPin);
+    a.ring_recip = ~0ull / a.ring_div;
     const int hpw = 32 / (head_dim / 8);
     const int64_t rounds = (a.kv_heads + hpw - 1) / hpw;
     const int64_t q_rounds = (a.q_heads + hpw - 1) / hpw;

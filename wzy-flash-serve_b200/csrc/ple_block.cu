@@ -34,6 +34,7 @@ struct PleFp8Args {
     uint64_t mult[3];
     uint64_t vocab[kPleHeads];
     uint64_t off[kPleHeads];
+    uint64_t recip[kPleHeads];  // floor((2^64 - 1) / vocab[h]), for mod_u64 (set on the host)
     const int32_t* ids;
     int64_t T;
     int32_t prev2, prev1;  // id[-2], id[-1] (negative: none)
@@ -53,46 +54,51 @@ __device__ __forceinline__ uint32_t ple_fp8_row(const PleFp8Args& a, int64_t t, 
     c2 = cut ? a.eos : p0;
     uint64_t mixed = (uint64_t)(int64_t)cur * a.mult[0] ^ (uint64_t)c1 * a.mult[1];
     if (h >= kPleHpn) mixed ^= (uint64_t)c2 * a.mult[2];
-    return (uint32_t)(mixed % a.vocab[h] + a.off[h]);
+    return (uint32_t)(mod_u64(mixed, a.vocab[h], a.recip[h]) + a.off[h]);
 }
 
 // 4 fp8 e4m3 bytes (little-endian in a u32) -> 4 fp32 values times the scale. e4m3 -> fp16 is exact
 // (hardware convert); the NaN codes (0x7F, 0xFF) read as signed zero, as in the reference's table.
+// The NaN bytes are found four at a time: (b & 0x7F) + 1 carries into bit 7 exactly when the low seven
+// bits are all ones (no carry crosses a byte), and clearing their low seven bits leaves the sign: 0x7F ->
+// 0x00 (+0), 0xFF -> 0x80 (-0). Each zero then times the scale is the same signed zero as before.
 __device__ __forceinline__ float4 fp8x4_decode(uint32_t w, float scale) {
-    float f[4];
+    const uint32_t nan = ((w & 0x7F7F7F7Fu) + 0x01010101u) & 0x80808080u;
+    w &= ~(nan - (nan >> 7));
+    float2 f[2];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
         const __nv_fp8x2_storage_t pair = (__nv_fp8x2_storage_t)((w >> (16 * j)) & 0xFFFFu);
         const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
         __half2 h2;
         *reinterpret_cast<__half2_raw*>(&h2) = hr;
-        const float2 v = __half22float2(h2);
-        const uint32_t b0 = (w >> (16 * j)) & 0xFFu, b1 = (w >> (16 * j + 8)) & 0xFFu;
-        f[2 * j] = ((b0 & 0x7Fu) == 0x7Fu ? ((b0 & 0x80u) ? -0.f : 0.f) : v.x) * scale;
-        f[2 * j + 1] = ((b1 & 0x7Fu) == 0x7Fu ? ((b1 & 0x80u) ? -0.f : 0.f) : v.y) * scale;
+        f[j] = fmul2(__half22float2(h2), splat2(scale));
     }
-    return make_float4(f[0], f[1], f[2], f[3]);
+    return make_float4(f[0].x, f[0].y, f[1].x, f[1].y);
 }
 
 // One warp per item of HPI heads of a token (HPI = 16: the whole token): lanes 0..HPI-1 hash one head
 // each; the item's rows are then read in 4-byte quads spread over the lanes (each quad fetches its row
 // index from the hashing lane).
-template <int HPI>
+// RB > 0: rows of RB bytes known at compile time (the reference's 160), so the quad -> head division
+// is a multiply; RB == 0: a.row_bytes.
+template <int HPI, int RB>
 __global__ void __launch_bounds__(256) ple_fp8_gather_kernel(const PleFp8Args a) {
     pdl_begin();
     constexpr int kParts = kPleHeads / HPI;             // items per token
     constexpr int kQ = (kPleQuads * HPI + 15) / 16;     // quads per lane in flight (20 for a whole token)
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-    const int qpr = a.row_bytes / 4;  // 4-byte quads per row
+    const int rb = RB > 0 ? RB : a.row_bytes;
+    const int qpr = rb / 4;  // 4-byte quads per row
     const int quads = HPI * qpr;
-    const int width = kPleHeads * a.row_bytes;  // output floats per token
+    const int width = kPleHeads * rb;  // output floats per token
     const int64_t items = a.T * kParts;
     for (int64_t it = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += nwarps) {
         const int64_t t = it / kParts;
         const int h0 = (int)(it - t * kParts) * HPI;
         const uint32_t my_row = lane < HPI ? ple_fp8_row(a, t, h0 + lane) : 0u;
-        float4* dst = reinterpret_cast<float4*>(a.out + t * width + (int64_t)h0 * a.row_bytes);
+        float4* dst = reinterpret_cast<float4*>(a.out + t * width + (int64_t)h0 * rb);
         // Lane l produces output float4s q = k*32 + l: 4 fp8 bytes each, so every warp-wide load
         // reads 128 contiguous bytes (within at most two rows) and every store writes 512 contiguous
         // bytes. kQ loads per lane are in flight before any is decoded.
@@ -104,7 +110,7 @@ __global__ void __launch_bounds__(256) ple_fp8_gather_kernel(const PleFp8Args a)
                 const int h = q < quads ? q / qpr : 0;
                 const uint32_t row = __shfl_sync(0xffffffffu, my_row, h);
                 if (q < quads)
-                    raw[k] = __ldg(reinterpret_cast<const uint32_t*>(a.table + (uint64_t)row * a.row_bytes) + (q - h * qpr));
+                    raw[k] = __ldg(reinterpret_cast<const uint32_t*>(a.table + (uint64_t)row * rb) + (q - h * qpr));
             }
 #pragma unroll
             for (int k = 0; k < kQ; ++k) {
@@ -381,8 +387,10 @@ int wzyb_ple_gather_fp8_f32(const uint8_t* table, int64_t table_rows, int row_by
     // 4 heads per warp item (4 items per token, 5 quads per lane in flight): 4.18 -> 4.83 TB/s at 262,144
     // tokens and 22.5 -> 20.1 us at 4096 against a warp per token; 8 heads: 3.81 TB/s, 2: 3.49, 1: 2.15
     constexpr int kHpi = 4;
+    for (int h = 0; h < 16; ++h) a.recip[h] = ~0ull / a.vocab[h];
     const int grid = wzyb::persistent_grid(di, 8, (T * (16 / kHpi) + 7) / 8);
-    wzyb::launch_k(wzyb::ple_fp8_gather_kernel<kHpi>, grid, 256, 0, (cudaStream_t)stream, a);
+    if (row_bytes == 160) wzyb::launch_k(wzyb::ple_fp8_gather_kernel<kHpi, 160>, grid, 256, 0, (cudaStream_t)stream, a);
+    else wzyb::launch_k(wzyb::ple_fp8_gather_kernel<kHpi, 0>, grid, 256, 0, (cudaStream_t)stream, a);
     return wzyb::launch_status();
 }
 

@@ -496,14 +496,17 @@ int wzyb_read_faults(uint32_t* faults, int clear);
  * design. Outside the ring: SwiGLU stages 1 / 2 force the scalar / packed math; head norm+RoPE
  * ctas_per_sm 2 selects the other instantiation of its design. Layer bundles: stages picks the
  * schedule (0 by size as above, 1 the persistent grid split between the ops, 2 one item per warp on a
- * grid sized to the work, 3 both ops on every CTA, 4 the ops' own launches).
- * Families: 0 add+RMSNorm, 1 head norm+RoPE, 2 GDN gated norm, 3 SwiGLU, 4 gathers, 5 layer bundles. */
+ * grid sized to the work, 3 both ops on every CTA, 4 the ops' own launches). KV append: stages
+ * is the rounds of heads per warp item (0 by size, 1 or 2), ctas_per_sm caps the grid (default 8).
+ * Families: 0 add+RMSNorm, 1 head norm+RoPE, 2 GDN gated norm, 3 SwiGLU, 4 gathers, 5 layer bundles,
+ * 6 KV append. */
 #define WZYB_FAM_NORM 0
 #define WZYB_FAM_HEAD_ROPE 1
 #define WZYB_FAM_GDN 2
 #define WZYB_FAM_SWIGLU 3
 #define WZYB_FAM_GATHER 4
 #define WZYB_FAM_BUNDLE 5
+#define WZYB_FAM_KV 6
 int wzyb_set_launch_tuning(int family, int ctas_per_sm, int stages);
 /* Kernel design per family (process-wide), for A/B measurement:
  *   WZYB_VARIANT_AUTO   the library's choice for the shape (default)

@@ -111,7 +111,9 @@ __device__ __forceinline__ void kv_q8_store(const float2 (&x)[4], bool act, int 
 // shortest chain; kR = 2 (long calls) keeps the reference's 2 heads of 256 on one warp, with the k and
 // v vectors of both rounds loaded before any arithmetic and the token's cell and cos/sin work done
 // once. The cos/sin slice is loaded behind the head vectors.
-template <typename T, int HD, int kR>
+// HAS_Q: the launch carries q heads (the q-item code is compiled out otherwise, which keeps the k/v-only
+// kernel's registers down).
+template <typename T, int HD, int kR, bool HAS_Q>
 __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
     pdl_begin();
     constexpr int L = HD / 8;
@@ -175,7 +177,7 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
     StridePos ps(gwarp, nwarps, per_tok);  // item = (token q, round group r)
     for (int64_t it = gwarp; it < items; it += nwarps, ps.advance()) {
         const int64_t t = ps.q;
-        if (ps.r >= groups) {  // q heads of this token: norm + rotation in place, nothing appended
+        if (HAS_Q && ps.r >= groups) {  // q heads of this token: norm + rotation in place, nothing appended
             const int q0 = (ps.r - groups) * kR;
             T* const qrow = static_cast<T*>(a.q) + t * a.q_row_stride;
             typename Vec8<T>::Raw qr[kR];
@@ -311,12 +313,18 @@ static int launch_kv_append(KvAppendArgs a, int head_dim, cudaStream_t stream) {
     const int64_t rounds = (a.kv_heads + hpw - 1) / hpw;
     const int64_t q_rounds = (a.q_heads + hpw - 1) / hpw;
     // one round per warp while the call is smaller than a few warps per SM, else two
-    const bool split = a.T * (rounds + q_rounds) <= (int64_t)di.sms * 32;
+    const Tuning tu = tuning(kFamKv);
+    const bool split = tu.stages == 1 || (tu.stages != 2 && a.T * (rounds + q_rounds) <= (int64_t)di.sms * 32);
     const int64_t items = split ? a.T * (rounds + q_rounds) : a.T * ((rounds + 1) / 2 + (q_rounds + 1) / 2);
-    const int grid = persistent_grid(di, 8, (items + 7) / 8);
+    const int grid = persistent_grid(di, tu.ctas_per_sm, (items + 7) / 8);
 #define WZYB_KV(HDV)                                                                              \
-    if (split) launch_k(kv_append_kernel<T, HDV, 1>, grid, 256, 0, stream, a);                          \
-    else launch_k(kv_append_kernel<T, HDV, 2>, grid, 256, 0, stream, a);
+    if (a.q_heads > 0) {                                                                          \
+        if (split) launch_k(kv_append_kernel<T, HDV, 1, true>, grid, 256, 0, stream, a);                \
+        else launch_k(kv_append_kernel<T, HDV, 2, true>, grid, 256, 0, stream, a);                      \
+    } else {                                                                                      \
+        if (split) launch_k(kv_append_kernel<T, HDV, 1, false>, grid, 256, 0, stream, a);               \
+        else launch_k(kv_append_kernel<T, HDV, 2, false>, grid, 256, 0, stream, a);                     \
+    }
     switch (head_dim) {
         case 64: { WZYB_KV(64) break; }
         case 128: { WZYB_KV(128) break; }

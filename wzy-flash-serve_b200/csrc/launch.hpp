@@ -27,7 +27,8 @@ enum KernelFamily : int {
     kFamSwiglu = 3,    // SwiGLU
     kFamGather = 4,    // embedding / PLE gathers
     kFamBundle = 5,    // layer bundles (one launch per bundle, or the ops as separate launches)
-    kFamCount = 6
+    kFamKv = 6,        // KV append (with k norm + RoPE and optional q heads)
+    kFamCount = 7
 };
 struct Tuning {
     int ctas_per_sm;

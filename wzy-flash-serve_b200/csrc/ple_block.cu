@@ -99,6 +99,22 @@ __global__ void __launch_bounds__(256) ple_fp8_gather_kernel(const PleFp8Args a)
         const int h0 = (int)(it - t * kParts) * HPI;
         const uint32_t my_row = lane < HPI ? ple_fp8_row(a, t, h0 + lane) : 0u;
         float4* dst = reinterpret_cast<float4*>(a.out + t * width + (int64_t)h0 * rb);
+        if constexpr (RB > 0 && (RB / 4) % (32 / HPI) == 0) {
+            // Rows of known size: 32/HPI lanes per head, each with RB/4/(32/HPI) quads of that head's
+            // row (one row index per lane, no division); each warp-wide load reads HPI 32-byte spans
+            // and each store writes HPI whole 128-byte lines.
+            constexpr int kLph = 32 / HPI, kQpl = RB / 4 / kLph;
+            const int hl = lane / kLph, ql = lane % kLph;
+            const uint32_t row = __shfl_sync(0xffffffffu, my_row, hl);
+            const uint32_t* src = reinterpret_cast<const uint32_t*>(a.table + (uint64_t)row * RB) + ql;
+            float4* d = dst + hl * (RB / 4) + ql;
+            uint32_t raw[kQpl];
+#pragma unroll
+            for (int j = 0; j < kQpl; ++j) raw[j] = __ldg(src + j * kLph);
+#pragma unroll
+            for (int j = 0; j < kQpl; ++j) __stcs(d + j * kLph, fp8x4_decode(raw[j], a.scale));
+            continue;
+        }
         // Lane l produces output float4s q = k*32 + l: 4 fp8 bytes each, so every warp-wide load
         // reads 128 contiguous bytes (within at most two rows) and every store writes 512 contiguous
         // bytes. kQ loads per lane are in flight before any is decoded.

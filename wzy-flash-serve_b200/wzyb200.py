@@ -23,7 +23,7 @@ GATE_SIGMOID, GATE_SILU = 0, 1
 OOB_CLAMP, OOB_ZERO_ID = 0, 1
 PLE_HASH_C_PRECEDENCE, PLE_HASH_XOR_THEN_ADD = 0, 1
 PLE_EOS_DEFAULT = 248044
-FAM_NORM, FAM_HEAD_ROPE, FAM_GDN, FAM_SWIGLU, FAM_GATHER, FAM_BUNDLE = 0, 1, 2, 3, 4, 5
+FAM_NORM, FAM_HEAD_ROPE, FAM_GDN, FAM_SWIGLU, FAM_GATHER, FAM_BUNDLE, FAM_KV = 0, 1, 2, 3, 4, 5, 6
 VARIANT_AUTO, VARIANT_RING, VARIANT_DIRECT, VARIANT_ASYNC, VARIANT_WIDE, VARIANT_PAIR = 0, 1, 2, 3, 4, 5
 VARIANT_SPLIT = 6
 

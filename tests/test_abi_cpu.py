@@ -225,7 +225,7 @@ def test_bundle_validation(wz):
     assert L.wzyb_set_kernel_variant(wz.FAM_BUNDLE, wz.VARIANT_SPLIT) == wz.OK
     assert L.wzyb_set_kernel_variant(wz.FAM_BUNDLE, wz.VARIANT_AUTO) == wz.OK
     assert L.wzyb_set_kernel_variant(wz.FAM_BUNDLE, 7) == wz.ERR_VALUE
-    assert L.wzyb_set_kernel_variant(6, 0) == wz.ERR_VALUE
+    assert L.wzyb_set_kernel_variant(7, 0) == wz.ERR_VALUE
 
 
 def test_head_tensor_element_type_checked(wz):

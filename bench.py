@@ -70,11 +70,21 @@ def bundle_bytes(name, T):
     return sum(T * BYTES_PER_TOKEN[o] + WEIGHT_BYTES[o] for o in BUNDLES[name])
 
 
+def bundle_fused(name, T):
+    """Whether the library runs bundle `name` of T tokens as one launch (its rule: algorithmic bytes of
+    activations, weights aside, up to 256 MiB)."""
+    return sum(T * BYTES_PER_TOKEN[o] for o in BUNDLES[name]) <= 256 * (1 << 20)
+
+
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per token of the dominant kernel (the act
 # bundle), from one ncu capture of a 32,768-token launch, scaled by the tokens of a launch: reads scale
 # exactly; writes are slightly under-counted at that size because the tail of the output is still in L2
 # when the kernel ends. None until a capture of the current kernel exists.
-NCU_TRAFFIC_PER_TOKEN = {"act_b": None}
+# DRAM bytes per token of the dominant kernel from one ncu capture (dram__bytes_read.sum +
+# dram__bytes_write.sum) of the SwiGLU launch at 32,768 tokens (738,216,448 + 331,152,128 bytes), scaled
+# by the tokens of a launch: the reads equal the algorithmic reads; the writes fall short of them by the
+# lines still in L2 when the launch ends.
+NCU_TRAFFIC_PER_TOKEN = {"swi": (738216448 + 331152128) / 32768, "act_b": None}
 
 
 def peaks():
@@ -612,6 +622,9 @@ def reference_gpu(peak):
     P = lambda t: ctypes.c_void_p(t.data_ptr() if t is not None else 0)  # noqa: E731
     S = lambda s: ctypes.c_void_p(s.cuda_stream)  # noqa: E731
     res, x, w = f32(T, HIDDEN), f32(T, HIDDEN), 1 + 0.02 * f32(HIDDEN)
+    # pf_gr_norm_fp16 reads prev_inj[t] whenever prev_bo is given (src/wzy_qsa_wmma.cuh:206): zero
+    # inject logits make its gate 2*sigmoid(0) = 1, the plain residual add of the config
+    inj0 = torch.zeros(T, dtype=torch.float32, device=dev)
     y16 = torch.empty((T, HIDDEN), dtype=torch.float16, device=dev)
     q, k, gq, gk = f32(T, QH, HD), f32(T, KH, HD), 1 + 0.02 * f32(HD), 1 + 0.02 * f32(HD)
     c, s_ = orc.ref_rope_table(T, THETA)
@@ -623,7 +636,7 @@ def reference_gpu(peak):
     gy16 = torch.empty((T, GDN_H, GDN_HD), dtype=torch.float16, device=dev)
     jobs = {
         # pf_gr_norm_fp16: R and bo fp32 read, R fp32 written, xn fp16 written
-        "norm": (lambda st: R.ref_pf_gr_norm_fp16(P(res), P(w), P(x), None, P(y16), T, HIDDEN, 1, EPS, S(st)),
+        "norm": (lambda st: R.ref_pf_gr_norm_fp16(P(res), P(w), P(x), P(inj0), P(y16), T, HIDDEN, 1, EPS, S(st)),
                  T * HIDDEN * (4 + 4 + 4 + 2)),
         # fused_head_norm_rope_multi on q, then on k (fp32 in place)
         "qk": (lambda st: (R.ref_fused_head_norm_rope_multi(P(q), P(gq), P(cos), P(sin), P(base), T, QH, HD, HD,
@@ -780,7 +793,7 @@ def main():
     ap.add_argument("--profile-case", default=None,
                     help="run one small case for an ncu capture and exit: attn_b act_b gath_b norm qk swi gdn "
                          "emb ple ple8 kv conv grn grq8 gate mix grw q8 (--tokens, default 4096; --steps reps)")
-    ap.add_argument("--variant", default="auto", choices=["auto", "ring", "direct", "async", "wide", "pair"],
+    ap.add_argument("--variant", default="auto", choices=["auto", "ring", "direct", "async", "wide", "pair"],  # ring: gathers
                     help="kernel design of the norm families (A/B measurement)")
     ap.add_argument("--tune", action="append", default=[],
                     help="FAMILY:CTAS_PER_SM:STAGES launch tuning (wzyb_set_launch_tuning), repeatable")
@@ -816,8 +829,11 @@ def main():
     var = {"auto": wz.VARIANT_AUTO, "ring": wz.VARIANT_RING, "direct": wz.VARIANT_DIRECT,
            "async": wz.VARIANT_ASYNC, "wide": wz.VARIANT_WIDE,
            "pair": wz.VARIANT_PAIR}[args.variant]
-    for fam in (wz.FAM_NORM, wz.FAM_HEAD_ROPE, wz.FAM_GDN):
-        wz.set_kernel_variant(fam, var)
+    if var == wz.VARIANT_RING:  # the TMA bulk-copy design exists for the gathers
+        wz.set_kernel_variant(wz.FAM_GATHER, var)
+    else:
+        for fam in (wz.FAM_NORM, wz.FAM_HEAD_ROPE, wz.FAM_GDN):
+            wz.set_kernel_variant(fam, var)
     if args.split:
         wz.set_kernel_variant(wz.FAM_BUNDLE, wz.VARIANT_SPLIT)
     for spec in args.tune:
@@ -883,18 +899,27 @@ def main():
         ms_total = t_start.elapsed_time(t_end)
     # Per-launch breakdown (rank 0's hbm and the roofline's achieved bytes): a separate pass of
     # min(K, 100) steps with an event around every launch.
+    # A bundle above the library's one-launch size is issued as its ops' own launches: then every op
+    # launch is timed on its own (the dominant kernel of the roofline is then the SwiGLU launch).
     kp = min(args.steps, 100)
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(nb + 1)] for _ in range(kp)]
+    per_op = not args.split and not all(bundle_fused(b, n) for b in STEP_BUNDLES)
+    units = [o for b in STEP_BUNDLES for o in BUNDLES[b]] if per_op else list(STEP_BUNDLES)
+    unit_fn = [(lambda st, o=o: sh.ops[o](st)) for o in units] if per_op else \
+              [(lambda st, i=i: sh.launch(i, st)) for i in range(nb)]
+    nu = len(units)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(nu + 1)] for _ in range(kp)]
     for k in range(kp):
         if flush_l2:
             flush()
-        for i in range(nb):
+        for i in range(nu):
             ev[k][i].record(s)
-            sh.launch(i, s)
-        ev[k][nb].record(s)
+            unit_fn[i](s)
+        ev[k][nu].record(s)
     torch.cuda.synchronize()
-    kern_ms = [statistics.mean(ev[k][i].elapsed_time(ev[k][i + 1]) for k in range(kp)) for i in range(nb)]
-    launches = nb * args.steps
+    unit_ms = {units[i]: statistics.mean(ev[k][i].elapsed_time(ev[k][i + 1]) for k in range(kp)) for i in range(nu)}
+    kern_ms = [sum(unit_ms[o] for o in BUNDLES[b]) if per_op else unit_ms[b] for b in STEP_BUNDLES]
+    launches = args.steps * sum(1 if (bundle_fused(b, n) and not args.split) else len(BUNDLES[b])
+                                for b in STEP_BUNDLES)
     faults = wz.read_faults()
 
     t = torch.tensor([ms_total, float(faults)], dtype=torch.float64, device=dev)
@@ -937,17 +962,21 @@ def main():
     if rank == 0:
         tokens_per_s = args.tokens / (ms_per_step * 1e-3)
         step_bytes = sum(bundle_bytes(b, args.tokens) for b in STEP_BUNDLES) + (world - 1) * sum(WEIGHT_BYTES.values())
-        dom = "act_b"
-        dom_bytes = bundle_bytes(dom, n)
-        dom_ms = kern_ms[STEP_BUNDLES.index(dom)]
+        dom = "swi" if per_op else "act_b"
+        dom_bytes = n * BYTES_PER_TOKEN[dom] + WEIGHT_BYTES[dom] if per_op else bundle_bytes(dom, n)
+        dom_ms = unit_ms[dom]
         achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
-        traffic = NCU_TRAFFIC_PER_TOKEN[dom] * n if NCU_TRAFFIC_PER_TOKEN[dom] else None
+        traffic = round(NCU_TRAFFIC_PER_TOKEN[dom] * n) if NCU_TRAFFIC_PER_TOKEN.get(dom) else None
         hbm = {"step_gbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9, 1),
                "step_frac_per_gpu": round(step_bytes / (ms_per_step * 1e-3) / 1e9 / peak / world, 4),
                "step_frac_of_8tbs": round(step_bytes / (ms_per_step * 1e-3) / 1e9 / NOMINAL_HBM_GBS / world, 4)}
         for i, b in enumerate(STEP_BUNDLES):
             gbs = bundle_bytes(b, n) / (kern_ms[i] * 1e-3) / 1e9
             hbm[b] = [round(kern_ms[i] * 1e3, 1), round(gbs / peak, 4)]
+        if per_op:
+            for o in units:
+                gbs = (n * BYTES_PER_TOKEN[o] + WEIGHT_BYTES[o]) / (unit_ms[o] * 1e-3) / 1e9
+                hbm[o] = [round(unit_ms[o] * 1e3, 1), round(gbs / peak, 4)]
         reasons = sorted({r for c in clk_all for r in (c["reasons"] if c else [])})
         sm = [c["sm_mhz"] for c in clk_all if c and c["sm_mhz"]]
         out = {
@@ -964,7 +993,8 @@ def main():
             "dtype": "fp16 I/O, fp32 math",
             "data": "synthetic (seeded normal activations, N(0,0.02) weights as 1+w)",
             "config": {"workload": f"configs[4]: configs[1]+[2] bundles at {args.tokens:,} tokens, token-sharded, "
-                                   "no collective, one launch per bundle" + (" (split)" if args.split else ""),
+                                   "no collective; a bundle is one launch up to 256 MiB, its ops' own launches above"
+                                   + (" (split)" if args.split else ""),
                        "tokens": args.tokens, "tokens_per_gpu": n, "parallelism": f"token-shard x{world}",
                        "rope_table": "host-built (reference procedure)",
                        "l2": "flushed before every step" if flush_l2 else "inputs larger than L2 (no flush)",
@@ -977,7 +1007,8 @@ def main():
                        "reasons": reasons, "samples": sum(c["samples"] for c in clk_all if c)},
             "e2e": e2e,
             "cpu_baseline": cb,
-            "roofline": {"bound": "hbm", "kernel": "act bundle (SwiGLU + GDN, one launch)", "achieved": round(achieved, 1),
+            "roofline": {"bound": "hbm", "kernel": "SwiGLU launch" if per_op else "act bundle (SwiGLU + GDN, one launch)",
+                         "achieved": round(achieved, 1),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic, "algorithmic_bytes": dom_bytes},
             "hbm": hbm,

@@ -510,16 +510,17 @@ int wzyb_read_faults(uint32_t* faults, int clear);
 int wzyb_set_launch_tuning(int family, int ctas_per_sm, int stages);
 /* Kernel design per family (process-wide), for A/B measurement:
  *   WZYB_VARIANT_AUTO   the library's choice for the shape (default)
- *   WZYB_VARIANT_RING   TMA bulk-copy ring staged through shared memory, one CTA barrier per unit
+ *   WZYB_VARIANT_RING   (gathers) TMA bulk copies global -> shared -> global, a ring of slots per warp
  *   WZYB_VARIANT_DIRECT warp-owned units, 16-byte loads prefetched into registers, no CTA barrier
  *   WZYB_VARIANT_ASYNC  warp-owned units staged in a lane-private shared-memory ring by cp.async
  *   WZYB_VARIANT_WIDE   CTA-owned rows (4-16 warps), registers, one CTA barrier per row
  *   WZYB_VARIANT_PAIR   (head norm+RoPE) two chunks per lane holding each rotation pair, no shuffle
  *   WZYB_VARIANT_SPLIT  (layer bundles) each op of a bundle as its own launch, in the reference's order
- * Families 0 (add+RMSNorm), 1 (head norm+RoPE) and 2 (GDN gated norm) have the RING, DIRECT and
- * ASYNC designs; family 0 also WIDE, which AUTO picks for rows past one warp's register budget;
- * family 1 also PAIR; family 5 AUTO (one launch per bundle) and SPLIT
- * (a family without a design falls back to AUTO; DIRECT and ASYNC do so for rows too wide). */
+ * Families 0 (add+RMSNorm), 1 (head norm+RoPE) and 2 (GDN gated norm) have the DIRECT and ASYNC
+ * designs; family 0 also WIDE, which AUTO picks for rows past one warp's register budget; family 1
+ * also PAIR; family 4 (gathers) RING, for output rows up to 16 KiB; family 5 AUTO (one launch per
+ * bundle) and SPLIT (a family without a design falls back to AUTO; DIRECT and ASYNC do so for rows
+ * too wide). */
 #define WZYB_VARIANT_AUTO 0
 #define WZYB_VARIANT_RING 1
 #define WZYB_VARIANT_DIRECT 2

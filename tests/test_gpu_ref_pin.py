@@ -196,7 +196,7 @@ def test_pin_plain_row_norm(ref, orc, wz):
     np.testing.assert_allclose(host(mine), host(ry), rtol=2e-6, atol=2e-6)
     assert np.array_equal(host(dx), x)
     # in place, as the reference calls it on ple_k (src/wzy_stage_v2.cuh:590), for every design
-    for v in (wz.VARIANT_AUTO, wz.VARIANT_DIRECT, wz.VARIANT_ASYNC, wz.VARIANT_RING, wz.VARIANT_WIDE):
+    for v in (wz.VARIANT_AUTO, wz.VARIANT_DIRECT, wz.VARIANT_ASYNC, wz.VARIANT_WIDE):
         wz.set_kernel_variant(wz.FAM_NORM, v)
         ip = dev(x)
         wz.gr_norm_f32(ip, dev(g), None, None, ip, T, n, hc)

@@ -7,9 +7,8 @@
 // The reference runs one 128-thread block per (head, token) with a shared-memory reduction. Here each
 // head is owned by hd/8 lanes that reduce with xor shuffles, and y leaves with one 16-byte store per
 // lane. Default (direct): a warp per 256-element slab, 4 slabs' loads in flight per warp; on request,
-// the slabs staged by cp.async (async) or whole tokens by TMA bulk copies (ring, ring.cuh).
+// the slabs staged in shared memory by cp.async (async).
 #include "launch.hpp"
-#include "ring.cuh"
 
 namespace wzyb {
 
@@ -50,105 +49,7 @@ struct GdnArgs {
     float eps;
     float w_offset;
     int gate_mode;
-    int stages;
-    uint32_t row_bytes;  // heads * hd * sizeof(TI)
-    uint32_t stage_bytes;
 };
-
-template <typename TI, typename TO, int HD, int VPT>
-__global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) gdn_norm_kernel(const GdnArgs a) {
-    pdl_begin();
-    constexpr int L = HD / 8;
-    extern __shared__ __align__(128) unsigned char smem[];
-    const int S = a.stages;
-    const int64_t G = gridDim.x;
-    const int64_t first = blockIdx.x;
-    if (first >= a.T) return;
-    const int64_t my_units = (a.T - 1 - first) / G + 1;
-    const RingSmem ring = ring_carve(smem, S);
-    ring_init(ring, S);
-
-    const int tid = threadIdx.x;
-    const int row_elems = a.heads * HD;
-    const TI* __restrict__ o = static_cast<const TI*>(a.o);
-    const TI* __restrict__ z = static_cast<const TI*>(a.z);
-    TO* __restrict__ y = static_cast<TO*>(a.y);
-
-    uint64_t pol = 0;
-    int64_t issued = 0;
-    auto issue = [&](int64_t i) {
-        const int s = (int)(i % S);
-        const int64_t t = first + i * G;
-        unsigned char* st = ring.data + (size_t)s * a.stage_bytes;
-        mbar_arrive_expect_tx(&ring.full[s], a.stage_bytes);
-        bulk_load(st, o + t * row_elems, a.row_bytes, &ring.full[s], pol);
-        bulk_load(st + a.row_bytes, z + t * row_elems, a.row_bytes, &ring.full[s], pol);
-    };
-    if (tid == 0) {
-        pol = policy_evict_first();
-        issued = my_units < S ? my_units : (int64_t)S;
-        for (int64_t i = 0; i < issued; ++i) issue(i);
-    }
-
-    int col[VPT];  // element offset inside the row
-    bool act[VPT];
-    float g[VPT][8];
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-        const int j = k * (int)blockDim.x + tid;
-        col[k] = j * 8;
-        act[k] = col[k] < row_elems;
-        if (act[k]) {
-            Vec8<TI>::load_ro(static_cast<const TI*>(a.gamma) + (j % L) * 8, g[k]);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) g[k][e] = a.w_offset + g[k][e];
-        }
-    }
-    const bool silu = a.gate_mode == WZYB_GATE_SILU;
-
-    for (int64_t i = 0; i < my_units; ++i) {
-        const int s = (int)(i % S);
-        const int64_t t = first + i * G;
-        const bool ok = mbar_wait(&ring.full[s], (uint32_t)((i / S) & 1));
-        if (!ok) *ring.abort_flag = 1;
-        float ov[VPT][8], zv[VPT][8];
-#pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-            if (act[k] && ok) {
-                const TI* so = reinterpret_cast<const TI*>(ring.data + (size_t)s * a.stage_bytes);
-                const TI* sz = reinterpret_cast<const TI*>(ring.data + (size_t)s * a.stage_bytes + a.row_bytes);
-                Vec8<TI>::load(so + col[k], ov[k]);
-                Vec8<TI>::load(sz + col[k], zv[k]);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) ov[k][e] = zv[k][e] = 0.f;
-            }
-        }
-        __syncthreads();  // the unit is in registers: the stage may be refilled
-        if (*ring.abort_flag) {
-            ring_drain(ring, S, i, issued);
-            return;
-        }
-        if (tid == 0 && issued < my_units) {
-            issue(issued);
-            ++issued;
-        }
-#pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-            float ss = 0.f;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) ss += ov[k][e] * ov[k][e];
-            ss = group_sum<L>(ss);
-            const float sc = rsqrt_approx(ss * (1.0f / (float)HD) + a.eps);
-            float out[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                out[e] = gdn_gate(ov[k][e] * sc * g[k][e], zv[k][e], silu);
-            }
-            if (act[k]) Vec8<TO>::store(y + t * row_elems + col[k], out);
-        }
-    }
-}
 
 // Direct design: a warp owns one 256-element slab of a token row (32/L whole heads), keeps kU slabs of
 // o and z in flight as raw 16-byte registers, then normalises each head inside its lane group. No
@@ -330,9 +231,6 @@ static int gdn_prepare(const void* o, const void* z, const void* gamma, void* y,
     a.eps = eps;
     a.w_offset = w_offset;
     a.gate_mode = gate_mode;
-    a.row_bytes = (uint32_t)((int64_t)heads * hd * sizeof(TI));
-    a.stage_bytes = 2u * a.row_bytes;
-    a.stages = 0;
     return WZYB_OK;
 }
 
@@ -347,46 +245,10 @@ static int launch_gdn(const void* o, const void* z, const void* gamma, void* y, 
     if (rc != WZYB_OK) return rc;
 
     // The direct design is the default (measured on B200 at 262,144 tokens: direct 84%, cp.async 83%,
-    // TMA ring 43% of HBM peak).
-    const int v = variant(kFamGdn);
-    if (v != WZYB_VARIANT_RING) {
-        const bool async_design = v == WZYB_VARIANT_ASYNC;
-        return gate_mode == WZYB_GATE_SILU ? launch_gdn_warp<TI, TO, true>(a, hd, async_design, di, stream)
-                                           : launch_gdn_warp<TI, TO, false>(a, hd, async_design, di, stream);
-    }
-
-    const int slots = heads * hd / 8;
-    const int vpt = slots <= 1024 ? 1 : 4;  // VPT 4 keeps the CTA at <= 512 threads (128 registers)
-    if (slots > 2048) return WZYB_ERR_SHAPE;
-    const int threads = ((slots + vpt - 1) / vpt + 31) / 32 * 32;
-
-    const Tuning tu = tuning(kFamGdn);
-    const int budget =
-        kSmemPerSm / tu.ctas_per_sm < di.max_smem_optin ? kSmemPerSm / tu.ctas_per_sm : di.max_smem_optin;
-    int S = tu.stages > 0 ? tu.stages : (int)((budget - (int)ring_header_bytes(32)) / (int)a.stage_bytes);
-    if (S > 32) S = 32;
-    while (S > 1 && (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes) > di.max_smem_optin) --S;
-    if (S < 1 || (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes) > di.max_smem_optin) return WZYB_ERR_SHAPE;
-    a.stages = S;
-    const int smem = (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes);
-    const int64_t want = (int64_t)di.sms * tu.ctas_per_sm;
-    const int grid = (int)(T < want ? T : want);
-
-#define WZYB_GDN_CASE(HDV, V)                                                      \
-    if (hd == HDV && vpt == V) {                                                   \
-        rc = ensure_smem((const void*)gdn_norm_kernel<TI, TO, HDV, V>, smem);      \
-        if (rc != WZYB_OK) return rc;                                              \
-        launch_k(gdn_norm_kernel<TI, TO, HDV, V>, grid, threads, smem, stream, a);       \
-        return launch_status();                                                    \
-    }
-    WZYB_GDN_CASE(64, 1)
-    WZYB_GDN_CASE(64, 4)
-    WZYB_GDN_CASE(128, 1)
-    WZYB_GDN_CASE(128, 4)
-    WZYB_GDN_CASE(256, 1)
-    WZYB_GDN_CASE(256, 4)
-#undef WZYB_GDN_CASE
-    return WZYB_ERR_SHAPE;
+    // and 43% for a TMA ring design of one barrier-synchronised unit per CTA, since removed).
+    const bool async_design = variant(kFamGdn) == WZYB_VARIANT_ASYNC;
+    return gate_mode == WZYB_GATE_SILU ? launch_gdn_warp<TI, TO, true>(a, hd, async_design, di, stream)
+                                       : launch_gdn_warp<TI, TO, false>(a, hd, async_design, di, stream);
 }
 
 }  // namespace wzyb

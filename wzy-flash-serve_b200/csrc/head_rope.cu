@@ -10,11 +10,10 @@
 //          (or two plain chunks), so the rotation needs no shuffle; heads reduced with xor shuffles;
 //          6 heads per warp item, or a whole token for long calls;
 //   direct: hd/8 lanes per head, the rotation partner fetched from the lane R/16 away by shuffles;
-//   async / ring (on request): the direct design's units staged by cp.async or TMA bulk copies.
+//   async (on request): the direct design's units staged in shared memory by cp.async.
 #include <cmath>
 
 #include "launch.hpp"
-#include "ring.cuh"
 
 namespace wzyb {
 
@@ -37,158 +36,7 @@ struct HeadRopeArgs {
     int rot;  // rot_dims
     float eps;
     float w_offset;
-    int stages;
-    uint32_t head_bytes;   // hd * sizeof(T)
-    uint32_t stage_bytes;  // (heads_q + heads_k) * head_bytes
-    int contig[2];         // head_stride == hd: one bulk copy per section
 };
-
-template <typename T, int HD, int VPT>
-__global__ void __launch_bounds__(VPT == 1 ? 1024 : 512) head_rope_kernel(const HeadRopeArgs a) {
-    pdl_begin();
-    constexpr int L = HD / 8;  // lanes per head (8, 16 or 32)
-    extern __shared__ __align__(128) unsigned char smem[];
-    const int S = a.stages;
-    const int64_t G = gridDim.x;
-    const int64_t first = blockIdx.x;
-    if (first >= a.T) return;
-    const int64_t my_units = (a.T - 1 - first) / G + 1;
-    const RingSmem ring = ring_carve(smem, S);
-    ring_init(ring, S);
-
-    const int tid = threadIdx.x, lane = tid & 31;
-    const int hq = a.sec[0].heads, hk = a.sec[1].heads, htot = hq + hk;
-    const int half = a.rot / 2;  // rotated pairs per head
-    const int hl = half / 8;     // lanes per rotation half
-    const int64_t base_pos = (a.d_base_pos ? (int64_t)__ldg(a.d_base_pos) : 0) + a.pos_offset;
-    // stage = [all heads][cos row (half floats)][sin row (half floats)]
-    const uint32_t heads_bytes = a.head_bytes * (uint32_t)htot;
-    const uint32_t tab_bytes = (uint32_t)half * 4u;
-
-    uint64_t pol = 0;
-    int64_t issued = 0;
-    auto issue = [&](int64_t i) {
-        const int s = (int)(i % S);
-        const int64_t t = first + i * G;
-        unsigned char* st = ring.data + (size_t)s * a.stage_bytes;
-        const int64_t pos = base_pos + t;
-        const bool tab = half > 0 && pos >= 0 && pos < a.table_rows;
-        mbar_arrive_expect_tx(&ring.full[s], heads_bytes + (tab ? 2u * tab_bytes : 0u));
-        if (tab) {
-            bulk_load(st + heads_bytes, a.cos_tab + pos * half, tab_bytes, &ring.full[s], pol);
-            bulk_load(st + heads_bytes + tab_bytes, a.sin_tab + pos * half, tab_bytes, &ring.full[s], pol);
-        }
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-            const HeadSection& sc = a.sec[q];
-            if (sc.heads == 0) continue;
-            const T* base = static_cast<const T*>(sc.data) + t * sc.row_stride;
-            if (a.contig[q]) {
-                bulk_load(st, base, a.head_bytes * sc.heads, &ring.full[s], pol);
-            } else {
-                for (int h = 0; h < sc.heads; ++h)
-                    bulk_load(st + (size_t)h * a.head_bytes, base + h * sc.head_stride, a.head_bytes, &ring.full[s],
-                              pol);
-            }
-            st += (size_t)sc.heads * a.head_bytes;
-        }
-    };
-    if (tid == 0) {
-        pol = policy_evict_first();
-        issued = my_units < S ? my_units : (int64_t)S;
-        for (int64_t i = 0; i < issued; ++i) issue(i);
-    }
-
-    // Fixed per-thread ownership: slot j = tid + k*blockDim -> head j / L, lane-in-head j % L.
-    int head[VPT], li[VPT], sec[VPT];
-    bool act[VPT];
-    float g[VPT][8];
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-        const int j = k * (int)blockDim.x + tid;
-        head[k] = j / L;
-        li[k] = j % L;
-        act[k] = head[k] < htot;
-        sec[k] = head[k] < hq ? 0 : 1;
-        if (act[k]) {
-            const T* gm = static_cast<const T*>(a.sec[sec[k]].gamma);
-            Vec8<T>::load_ro(gm + li[k] * 8, g[k]);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) g[k][e] = a.w_offset + g[k][e];
-        }
-    }
-
-    for (int64_t i = 0; i < my_units; ++i) {
-        const int s = (int)(i % S);
-        const int64_t t = first + i * G;
-        const int64_t pos = base_pos + t;
-        const bool pos_ok = pos >= 0 && pos < a.table_rows;
-        const bool ok = mbar_wait(&ring.full[s], (uint32_t)((i / S) & 1));
-        if (!ok) *ring.abort_flag = 1;
-        float p[VPT][8];
-        float cs[VPT][8], sn[VPT][8];
-        const unsigned char* st = ring.data + (size_t)s * a.stage_bytes;
-#pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-            if (act[k] && ok) {
-                Vec8<T>::load(reinterpret_cast<const T*>(st + (size_t)head[k] * a.head_bytes) + li[k] * 8, p[k]);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) p[k][e] = 0.f;
-            }
-            if (act[k] && ok && pos_ok && li[k] < 2 * hl) {
-                const int ci = (li[k] < hl ? li[k] : li[k] - hl) * 8;
-                Vec8<float>::load(reinterpret_cast<const float*>(st + heads_bytes) + ci, cs[k]);
-                Vec8<float>::load(reinterpret_cast<const float*>(st + heads_bytes + tab_bytes) + ci, sn[k]);
-            }
-        }
-        __syncthreads();  // every thread has its unit in registers: the stage may be refilled
-        if (*ring.abort_flag) {
-            ring_drain(ring, S, i, issued);
-            return;
-        }
-        if (tid == 0 && issued < my_units) {
-            issue(issued);
-            ++issued;
-        }
-        if (!pos_ok && tid == 0 && a.rot > 0) raise_fault(WZYB_FAULT_POS_RANGE);
-#pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-            // sum of squares over the head's L lanes (lanes of one head are an aligned group)
-            float ss = 0.f;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) ss += p[k][e] * p[k][e];
-            ss = group_sum<L>(ss);
-            const float sc = rsqrt_approx(ss / (float)HD + a.eps);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) p[k][e] *= sc * g[k][e];
-
-            // partial rotary on dims [0, rot): lane-in-head li < hl holds the first halves,
-            // hl <= li < 2*hl the second halves; the partner is hl lanes away.
-            const bool rot_lane = li[k] < 2 * hl;
-            const bool first_half = li[k] < hl;
-            const int src = rot_lane ? (first_half ? lane + hl : lane - hl) : lane;
-            float q2[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) q2[e] = __shfl_sync(0xffffffffu, p[k][e], src);
-            if (rot_lane && act[k] && pos_ok) {
-                if (first_half) {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) p[k][e] = p[k][e] * cs[k][e] - q2[e] * sn[k][e];  // a*cos - d*sin
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) p[k][e] = q2[e] * sn[k][e] + p[k][e] * cs[k][e];  // a*sin + d*cos
-                }
-            }
-            if (act[k]) {
-                const HeadSection& scn = a.sec[sec[k]];
-                const int hh = sec[k] == 0 ? head[k] : head[k] - hq;
-                T* dst = static_cast<T*>(scn.data) + t * scn.row_stride + hh * scn.head_stride + li[k] * 8;
-                Vec8<T>::store(dst, p[k]);
-            }
-        }
-    }
-}
 
 // ---- per-head math shared by the direct and async designs (packed fp32) ------------------------
 // gamma of this lane's 8 dims for the q (g[0]) and k (g[1]) sections, with the weight offset added
@@ -659,12 +507,6 @@ static int head_rope_prepare(const HeadSection& q, const HeadSection& k, const f
     a.rot = rot;
     a.eps = eps;
     a.w_offset = w_offset;
-    a.head_bytes = (uint32_t)(hd * sizeof(T));
-    const int htot = q.heads + k.heads;
-    a.stage_bytes = a.head_bytes * (uint32_t)htot + (rot > 0 ? 2u * (uint32_t)(rot / 2) * 4u : 0u);
-    a.contig[0] = (q.head_stride == hd || q.heads == 1) ? 1 : 0;
-    a.contig[1] = (k.head_stride == hd || k.heads <= 1) ? 1 : 0;
-    a.stages = 0;
     return WZYB_OK;
 }
 
@@ -698,7 +540,7 @@ static int launch_head_rope(const HeadSection& q, const HeadSection& k, const fl
         else launch_k(head_rope_async_kernel<T, 256, kNH, kP>, grid, 128, smem, stream, a);
         return launch_status();
     }
-    if (variant(kFamHeadRope) != WZYB_VARIANT_RING) {
+    {
         // Pair design by default, 3 rounds of 2 heads per item (6 heads; the 18 heads of the benchmark's
         // q+k are 3 whole items): 83 % of peak at 262K tokens vs 76 % for the direct design, whose rotation
         // shuffles and two gamma loads per head kept the shared-memory pipe ~70 % busy. A ctas_per_sm
@@ -718,39 +560,6 @@ static int launch_head_rope(const HeadSection& q, const HeadSection& k, const fl
         if (fill9 && a.T * per_tok9 >= (int64_t)di.sms * 12 * 8) return launch_head_rope_pair<T, 9>(a, hd, htot, di, stream);
         return launch_head_rope_pair<T, 3>(a, hd, htot, di, stream);
     }
-
-    const int slots = htot * (hd / 8);
-    const int vpt = slots <= 1024 ? 1 : 4;  // VPT 4 keeps the CTA at <= 512 threads (128 registers)
-    if (slots > 2048) return WZYB_ERR_SHAPE;
-    const int threads = ((slots + vpt - 1) / vpt + 31) / 32 * 32;
-
-    const Tuning tu = tuning(kFamHeadRope);
-    const int budget =
-        kSmemPerSm / tu.ctas_per_sm < di.max_smem_optin ? kSmemPerSm / tu.ctas_per_sm : di.max_smem_optin;
-    int S = tu.stages > 0 ? tu.stages : (int)((budget - (int)ring_header_bytes(32)) / (int)a.stage_bytes);
-    if (S > 32) S = 32;
-    while (S > 1 && (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes) > di.max_smem_optin) --S;
-    if (S < 1 || (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes) > di.max_smem_optin) return WZYB_ERR_SHAPE;
-    a.stages = S;
-    const int smem = (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes);
-    const int64_t want = (int64_t)di.sms * tu.ctas_per_sm;
-    const int grid = (int)(T_ < want ? T_ : want);
-
-#define WZYB_HR_CASE(HDV, V)                                                       \
-    if (hd == HDV && vpt == V) {                                                   \
-        rc = ensure_smem((const void*)head_rope_kernel<T, HDV, V>, smem);          \
-        if (rc != WZYB_OK) return rc;                                              \
-        launch_k(head_rope_kernel<T, HDV, V>, grid, threads, smem, stream, a);           \
-        return launch_status();                                                    \
-    }
-    WZYB_HR_CASE(64, 1)
-    WZYB_HR_CASE(64, 4)
-    WZYB_HR_CASE(128, 1)
-    WZYB_HR_CASE(128, 4)
-    WZYB_HR_CASE(256, 1)
-    WZYB_HR_CASE(256, 4)
-#undef WZYB_HR_CASE
-    return WZYB_ERR_SHAPE;
 }
 
 // ---------------------------------------------------------------------------------------------

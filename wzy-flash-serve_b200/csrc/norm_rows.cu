@@ -12,9 +12,7 @@
 //   wide   (longer rows): a CTA per row, per-warp partial sums meeting behind one barrier; with 4
 //          streams and bo_prev, a CTA per token (its 4 rows share one bo_prev read);
 //   async  (on request): warp-owned rows staged in lane-private shared memory by cp.async;
-//   ring   (on request): rows staged by TMA bulk copies S units ahead (ring.cuh), consumed by a CTA.
 #include "launch.hpp"
-#include "ring.cuh"
 
 namespace wzyb {
 
@@ -29,9 +27,6 @@ struct NormRowsArgs {
     int hc;
     float eps;
     float w_offset;
-    int stages;
-    uint32_t row_bytes;
-    uint32_t stage_bytes;
     void* qout;  // optional quantised xn (wide design only): codes in the QuantFormat of the launch
     void* sout;  // and its group scales
     float gs;    // NVFP4 per-tensor scale
@@ -55,122 +50,6 @@ __device__ __forceinline__ void norm_quant_store(const NormRowsArgs& a, const fl
         }
     }
     quant_group_store<QF>(yo, e < n, a.qout, a.sout, a.gs, (u * n + e) >> 3, lane);
-}
-
-template <typename TI, typename TO, int VPT>
-__global__ void __launch_bounds__(512) norm_rows_kernel(const NormRowsArgs a) {
-    pdl_begin();
-    extern __shared__ __align__(128) unsigned char smem[];
-    const int S = a.stages;
-    const int64_t G = gridDim.x;
-    const int64_t first = blockIdx.x;
-    if (first >= a.units) return;  // uniform across the CTA
-    const int64_t my_units = (a.units - 1 - first) / G + 1;
-    const RingSmem ring = ring_carve(smem, S);
-    ring_init(ring, S);
-
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
-    const TI* __restrict__ x = static_cast<const TI*>(a.x);
-    TI* __restrict__ res = static_cast<TI*>(a.res);
-    const TI* __restrict__ w = static_cast<const TI*>(a.w);
-    TO* __restrict__ y = static_cast<TO*>(a.y);
-    const bool has_x = x != nullptr;
-    const int n = a.n;
-
-    uint64_t pol = 0;
-    int64_t issued = 0;
-    auto issue = [&](int64_t i) {
-        const int s = (int)(i % S);
-        const int64_t u = first + i * G;
-        unsigned char* st = ring.data + (size_t)s * a.stage_bytes;
-        mbar_arrive_expect_tx(&ring.full[s], a.stage_bytes);
-        bulk_load(st, res + u * n, a.row_bytes, &ring.full[s], pol);
-        if (has_x) bulk_load(st + a.row_bytes, x + (u / a.hc) * n, a.row_bytes, &ring.full[s], pol);
-    };
-    if (tid == 0) {
-        pol = policy_evict_first();
-        issued = my_units < S ? my_units : (int64_t)S;
-        for (int64_t i = 0; i < issued; ++i) issue(i);
-    }
-
-    int col[VPT];
-    bool act[VPT];
-    float g[VPT][8];
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-        col[k] = (k * (int)blockDim.x + tid) * 8;
-        act[k] = col[k] < n;
-        if (act[k] && a.hc == 1) {
-            Vec8<TI>::load_ro(w + col[k], g[k]);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) g[k][j] = a.w_offset + g[k][j];
-        }
-    }
-
-    for (int64_t i = 0; i < my_units; ++i) {
-        const int s = (int)(i % S);
-        const int64_t u = first + i * G;
-        const bool ok = mbar_wait(&ring.full[s], (uint32_t)((i / S) & 1));
-        if (!ok) *ring.abort_flag = 1;
-        float v[VPT][8];
-        float ss = 0.f;
-        {
-            const TI* sr = reinterpret_cast<const TI*>(ring.data + (size_t)s * a.stage_bytes);
-            const TI* sx = reinterpret_cast<const TI*>(ring.data + (size_t)s * a.stage_bytes + a.row_bytes);
-            float gate = 1.0f;
-            if (has_x && a.inj != nullptr) gate = 2.0f / (1.0f + __expf(-a.inj[u] / (float)a.hc));
-#pragma unroll
-            for (int k = 0; k < VPT; ++k) {
-                if (act[k] && ok) {
-                    Vec8<TI>::load(sr + col[k], v[k]);
-                    if (has_x) {
-                        float xv[8];
-                        Vec8<TI>::load(sx + col[k], xv);
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) v[k][j] += xv[j] * gate;
-                    }
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) ss += v[k][j] * v[k][j];
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) v[k][j] = 0.f;
-                }
-            }
-        }
-        ss = group_sum<32>(ss);
-        if (lane == 0) ring.red[(i & 1) * 32 + warp] = ss;
-        __syncthreads();
-        if (*ring.abort_flag) {
-            ring_drain(ring, S, i, issued);
-            return;
-        }
-        if (tid == 0 && issued < my_units) {
-            issue(issued);
-            ++issued;
-        }
-        float tot = 0.f;
-        for (int q = 0; q < nwarps; ++q) tot += ring.red[(i & 1) * 32 + q];
-        const float sc = rsqrt_approx(tot / (float)n + a.eps);
-        const int c = (int)(u % a.hc);
-#pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-            if (!act[k]) continue;
-            float gk[8];
-            if (a.hc == 1) {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) gk[j] = g[k][j];
-            } else {
-                Vec8<TI>::load_ro(w + (size_t)c * n + col[k], gk);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) gk[j] = a.w_offset + gk[j];
-            }
-            float o[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) o[j] = (v[k][j] * sc) * gk[j];
-            Vec8<TO>::store(y + u * n + col[k], o);
-            if (has_x) Vec8<TI>::store(res + u * n + col[k], v[k]);
-        }
-    }
 }
 
 // Direct design: one warp per row. Lane l owns the 8-element vectors l, l+32, ... of the row, so each
@@ -619,9 +498,6 @@ static int norm_rows_prepare(const void* x, void* res, const void* w, const floa
     a.hc = hc;
     a.eps = eps;
     a.w_offset = w_offset;
-    a.stages = 0;
-    a.row_bytes = (uint32_t)(n * sizeof(TI));
-    a.stage_bytes = a.row_bytes * (x ? 2u : 1u);
     a.qout = a.sout = nullptr;
     a.gs = 1.0f;
     a.sf_layout = kSfRowMajor;
@@ -640,16 +516,12 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
     rc = device_info(&di);
     if (rc != WZYB_OK) return rc;
 
-    const int vpt = n <= 4096 ? 1 : (n <= 8192 ? 2 : 4);
-    const int vecs = n / 8;
-    const int threads = ((vecs + vpt - 1) / vpt + 31) / 32 * 32;
-
     // Direct design while a row fits one warp's register budget (<= 12 fp16 or 4 fp32 vectors per
-    // lane), the wide design (CTA-owned rows) past it; the TMA ring only on request.
+    // lane), the wide design (CTA-owned rows) past it.
     const int vpl_need = (n + 255) / 256;
     const int vpl_max = sizeof(TI) == 2 ? 12 : 4;
     const int var = variant(kFamNorm);
-    if (var == WZYB_VARIANT_WIDE || (var != WZYB_VARIANT_RING && vpl_need > vpl_max))
+    if (var == WZYB_VARIANT_WIDE || vpl_need > vpl_max)
         return launch_norm_rows_wide<TI, TO, kQfNone>(a, di, stream);
     if (var == WZYB_VARIANT_ASYNC && vpl_need <= (sizeof(TI) == 2 ? 8 : 4)) {
         const int vpl = vpl_need <= 1 ? 1 : vpl_need <= 2 ? 2 : vpl_need <= 4 ? 4 : 8;
@@ -673,7 +545,7 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
 #undef WZYB_NRA
         return launch_status();
     }
-    if (variant(kFamNorm) != WZYB_VARIANT_RING && vpl_need <= vpl_max) {
+    {
         const void* kern = nullptr;
         int vpl = 0;
 #define WZYB_NR_PICK(V)                                                  \
@@ -709,32 +581,7 @@ static int launch_norm_rows(const void* x, void* res, const void* w, const float
         return launch_status();
     }
 
-    const Tuning tu = tuning(kFamNorm);
-    const int budget = (kSmemPerSm / tu.ctas_per_sm < di.max_smem_optin ? kSmemPerSm / tu.ctas_per_sm
-                                                                          : di.max_smem_optin);
-    int S = tu.stages > 0 ? tu.stages : (int)((budget - (int)ring_header_bytes(32)) / (int)a.stage_bytes);
-    if (S > 32) S = 32;
-    while (S > 1 && (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes) > di.max_smem_optin) --S;
-    if (S < 1 || (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes) > di.max_smem_optin) return WZYB_ERR_SHAPE;
-    a.stages = S;
-    const int smem = (int)(ring_header_bytes(S) + (uint32_t)S * a.stage_bytes);
-    const int64_t want = (int64_t)di.sms * tu.ctas_per_sm;
-    const int grid = (int)(a.units < want ? a.units : want);
-
-    const void* kern = nullptr;
-    switch (vpt) {
-        case 1: kern = (const void*)norm_rows_kernel<TI, TO, 1>; break;
-        case 2: kern = (const void*)norm_rows_kernel<TI, TO, 2>; break;
-        default: kern = (const void*)norm_rows_kernel<TI, TO, 4>; break;
-    }
-    rc = ensure_smem(kern, smem);
-    if (rc != WZYB_OK) return rc;
-    switch (vpt) {
-        case 1: launch_k(norm_rows_kernel<TI, TO, 1>, grid, threads, smem, stream, a); break;
-        case 2: launch_k(norm_rows_kernel<TI, TO, 2>, grid, threads, smem, stream, a); break;
-        default: launch_k(norm_rows_kernel<TI, TO, 4>, grid, threads, smem, stream, a); break;
-    }
-    return launch_status();
+    return WZYB_ERR_SHAPE;  // not reached: every row width has the direct or the wide design
 }
 
 // Residual fold + norm with a quantised side output of xn (format QF: Q8_0, MXFP8 or NVFP4): the
@@ -765,8 +612,6 @@ static int launch_norm_rows_quant(const void* x, void* res, const void* w, const
     a.hc = hc;
     a.eps = eps;
     a.w_offset = 0.0f;
-    a.stages = 0;
-    a.row_bytes = a.stage_bytes = 0;
     a.qout = qout;
     a.sout = sout;
     a.gs = gs;

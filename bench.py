@@ -2,7 +2,8 @@
 
 One "step" = one pass of the layer bundles of BASELINE configs[1]+[2] over this rank's token shard of
 configs[4] (262,144 tokens, token-sharded across the GPUs with no collective), through the public
-bundle entry points, one kernel launch each:
+bundle entry points (one kernel launch per bundle up to 256 MiB, e.g. a 4096-token shard; the two
+ops' own launches above, as at 262,144 tokens on 1-8 GPUs):
     wzyb_attn_prep_f16: residual add + zero-centred RMSNorm [T, 2048], and q/k RMSNorm + partial RoPE
                         q [T, 16, 256], k [T, 2, 256], rot 64, theta 1e7 (host-built table)
     wzyb_act_f16:       SwiGLU [11*T, 512] (10 routed + 1 shared expert rows per token), and the GDN

@@ -331,7 +331,9 @@ static void kv_q8_group(const float* x, int8_t* q, uint16_t* s) {
     const uint16_t sh = or_f2h(am / 127.0f);
     const float d = or_h2f(sh);
     for (int i = 0; i < 64; ++i) {
-        long qi = d > 0.f ? lrintf(x[i] / d) : 0;
+        /* __float2int_rn (src/wzy_qsa_256k.cuh:121) maps NaN (a NaN input, or inf / inf) to 0 */
+        const float t = d > 0.f ? x[i] / d : 0.f;
+        long qi = isnan(t) ? 0 : lrintf(t);
         q[i] = (int8_t)(qi < -127 ? -127 : qi > 127 ? 127 : qi);
     }
     *s = sh;

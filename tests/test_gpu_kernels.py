@@ -592,6 +592,25 @@ def test_kv_append_codes_at_rounding_boundaries(wz, orc):
         assert np.array_equal(_kv_host(dd, nm), getattr(c, nm)), nm
 
 
+def test_kv_append_codes_non_finite(wz, orc):
+    """Groups holding NaN or an infinity take the scalar conversion: NaN codes are 0 (as
+    __float2int_rn), an infinite group max gives an infinite scale whose codes are 0, and the other
+    lanes of such groups keep their own codes; bit-exact against the oracle."""
+    r = rng(4343)
+    T, heads, hd = 64, 2, 256
+    kvd = heads * hd
+    k = r.standard_normal((T, kvd)).astype(np.float32)
+    v = (3 * r.standard_normal((T, kvd))).astype(np.float32)
+    k[1, 5], k[2, 70], k[3, 130] = np.nan, np.inf, -np.inf
+    v[4, 0], v[5, 63], v[6, 64] = np.nan, np.inf, np.nan
+    k[7, 200:210] = np.nan
+    c, dd = _kv_seeded(orc, r, T, T, kvd, True)
+    orc.kv_append_int8_f32(k, v, T, kvd, 0, c)
+    wz.kv_append_int8_f32(dev(k), dev(v), T, heads, hd, _kv_desc(wz, dd, T, T, True))
+    for nm in _KV_PLANES:
+        assert np.array_equal(_kv_host(dd, nm), getattr(c, nm)), nm
+
+
 @pytest.mark.parametrize("dtype", [np.float16, np.float32])
 @pytest.mark.parametrize("T,heads,hd,base", [(5, 2, 256, 17), (4096, 2, 256, 0), (33, 1, 128, 3)])
 def test_k_rope_kv_append_fused(wz, orc, dtype, T, heads, hd, base):

@@ -68,30 +68,56 @@ __device__ __forceinline__ int64_t kv_ring_cell(int64_t p, int64_t cap, uint64_t
 
 // Quantise this lane's 8 elements as part of its 64-element group (lanes 8m..8m+7) and store the codes
 // (and, from the group's first lane, the fp16 scale) to up to two cells. Every lane must call it.
+// Codes are rint(x / d) clamped to [-127, 127] of the correctly rounded quotient, computed without a
+// divide per element (Markstein's theorem: with r = RN(1/d) and q0 = RN(x*r) within one ulp of x/d,
+// the residual e = x - q0*d is exact under FMA and RN(q0 + e*r) is the correctly rounded quotient; d is
+// 0 or an fp16 value >= 2^-24, so nothing underflows where the rounding can change the code), in packed
+// fp32, clamped, and rounded to the nearest even integer as the low byte of fl(q + 1.5 * 2^23). A lane
+// holding a NaN or an infinity, or whose group max is infinite, takes the scalar conversion instead
+// (NaN -> 0 as __float2int_rn), so every code matches the reference's expression.
 __device__ __forceinline__ void kv_q8_store(const float2 (&x)[4], bool act, int lane, int8_t* q0, uint16_t* s0,
                                             int8_t* q1, uint16_t* s1) {
-    float am = 0.f;
+    float am = 0.f, an = 0.f;  // group max as the reference's fmaxf; an: this lane's max with NaN kept
 #pragma unroll
-    for (int i = 0; i < 4; ++i) am = fmaxf(am, fmaxf(fabsf(x[i].x), fabsf(x[i].y)));
+    for (int i = 0; i < 4; ++i) {
+        const float a = fabsf(x[i].x), b = fabsf(x[i].y);
+        am = fmaxf(am, fmaxf(a, b));
+        an = fmax_nan(an, fmax_nan(a, b));
+    }
     am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
     am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
     am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
     if (!act) return;
     const __half sh = __float2half_rn(am / 127.0f);
     const float d = __half2float(sh);
-    // v / d correctly rounded without a division per element (Markstein's theorem: with r = RN(1/d)
-    // and q0 = RN(v*r) within one ulp of v/d, the residual e = v - q0*d is exact under FMA and
-    // RN(q0 + e*r) is the correctly rounded quotient). d is 0 or an fp16 value >= 2^-24, so nothing
-    // underflows where the rounding can change the code (|v/d| >= 0.5).
     const float r = d > 0.f ? __frcp_rn(d) : 0.f;
-    uint32_t w[2] = {0u, 0u};
+    uint32_t w[2];
+    if (an <= 3.402823466e38f && am <= 3.402823466e38f) {
+        const float2 nr2 = splat2(-r), r2 = splat2(r), d2 = splat2(d);
+        uint32_t b[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float v = (i & 1) ? x[i >> 1].y : x[i >> 1].x;
-        const float q0 = __fmul_rn(v, r);
-        const float q = __fmaf_rn(__fmaf_rn(-q0, d, v), r, q0);
-        const int qi = d > 0.f ? max(-127, min(127, __float2int_rn(q))) : 0;
-        w[i >> 2] |= ((uint32_t)(qi & 0xFF)) << ((i & 3) * 8);
+        for (int i = 0; i < 4; ++i) {
+            const float2 nq0 = fmul2_unfused(x[i], nr2);                         // -RN(x*r)
+            const float2 e = ffma2(nq0, d2, x[i]);                               // x - q0*d, exact
+            float2 q = ffma2(e, r2, make_float2(-nq0.x, -nq0.y));                // RN(x / d)
+            q.x = fminf(fmaxf(q.x, -127.0f), 127.0f);
+            q.y = fminf(fmaxf(q.y, -127.0f), 127.0f);
+            const float2 t = fadd2(q, splat2(12582912.0f));                      // rint in the low byte
+            b[2 * i] = __float_as_uint(t.x);
+            b[2 * i + 1] = __float_as_uint(t.y);
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+            w[k] = __byte_perm(__byte_perm(b[4 * k], b[4 * k + 1], 0x0040),
+                               __byte_perm(b[4 * k + 2], b[4 * k + 3], 0x0040), 0x5410);
+    } else {
+        w[0] = w[1] = 0u;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float v = (i & 1) ? x[i >> 1].y : x[i >> 1].x;
+            const int qi = d > 0.f ? max(-127, min(127, __float2int_rn(v / d))) : 0;
+            w[i >> 2] |= ((uint32_t)(qi & 0xFF)) << ((i & 3) * 8);
+        }
     }
     const uint2 packed = make_uint2(w[0], w[1]);
     const uint16_t sbits = __half_as_ushort(sh);

@@ -2,8 +2,8 @@
 
 One "step" = one pass of the layer bundles of BASELINE configs[1]+[2] over this rank's token shard of
 configs[4] (262,144 tokens, token-sharded across the GPUs with no collective), through the public
-bundle entry points (one kernel launch per bundle up to 256 MiB, e.g. a 4096-token shard; the two
-ops' own launches above, as at 262,144 tokens on 1-8 GPUs):
+bundle entry points (one kernel launch per bundle up to a size measured per bundle, e.g. a 4096- to
+16,384-token shard; the two ops' own launches above, as at 262,144 tokens on 1-8 GPUs):
     wzyb_attn_prep_f16: residual add + zero-centred RMSNorm [T, 2048], and q/k RMSNorm + partial RoPE
                         q [T, 16, 256], k [T, 2, 256], rot 64, theta 1e7 (host-built table)
     wzyb_act_f16:       SwiGLU [11*T, 512] (10 routed + 1 shared expert rows per token), and the GDN
@@ -71,10 +71,13 @@ def bundle_bytes(name, T):
     return sum(T * BYTES_PER_TOKEN[o] + WEIGHT_BYTES[o] for o in BUNDLES[name])
 
 
+FUSE_MAX_BYTES = {"attn_b": 1.25 * (1 << 30), "act_b": 1.0 * (1 << 30), "gath_b": 96.0 * (1 << 20)}
+
+
 def bundle_fused(name, T):
     """Whether the library runs bundle `name` of T tokens as one launch (its rule: algorithmic bytes of
-    activations, weights aside, up to 256 MiB)."""
-    return sum(T * BYTES_PER_TOKEN[o] for o in BUNDLES[name]) <= 256 * (1 << 20)
+    activations, weights aside, up to a size measured per bundle)."""
+    return sum(T * BYTES_PER_TOKEN[o] for o in BUNDLES[name]) <= FUSE_MAX_BYTES[name]
 
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per token of the dominant kernel (the act
@@ -994,7 +997,8 @@ def main():
             "dtype": "fp16 I/O, fp32 math",
             "data": "synthetic (seeded normal activations, N(0,0.02) weights as 1+w)",
             "config": {"workload": f"configs[4]: configs[1]+[2] bundles at {args.tokens:,} tokens, token-sharded, "
-                                   "no collective; a bundle is one launch up to 256 MiB, its ops' own launches above"
+                                   "no collective; a bundle is one launch up to its measured size, its ops' own "
+                                   "launches above"
                                    + (" (split)" if args.split else ""),
                        "tokens": args.tokens, "tokens_per_gpu": n, "parallelism": f"token-shard x{world}",
                        "rope_table": "host-built (reference procedure)",

@@ -392,12 +392,13 @@ uint32_t wzyb_ple_row_index(int32_t t0, int32_t t1, int32_t t2, int head, int64_
  * Layer bundles: the ops that the reference's prefill executor launches one after another inside a
  * layer (src/wzy_prefill_tc.cuh:697 residual norm and :862-867 q/k norm+RoPE; :942 SwiGLU and :845
  * GDN gated norm) and the rows its engine stages in one host routine (stage_emb_ple_pf,
- * src/wzy_engine_v2.cu:1210-1265). A bundle of up to 256 MiB of algorithmic bytes (e.g. 4096 tokens of
- * the benchmark's layer) is ONE kernel launch: the ops share no tensor, and every CTA of the
- * persistent grid runs both ops' code in turn (the same device code as the ops' own entry points, so
- * results are bit-identical to the separate calls). Larger bundles are issued as the two ops' own
- * launches, which measure as fast or faster once a launch's fixed costs are small against its
- * traffic. The tensors of the two ops must not overlap; if they do, or if a shape is outside the one-launch
+ * src/wzy_engine_v2.cu:1210-1265). A bundle up to a measured size (algorithmic bytes: 1.25 GiB for
+ * attn_prep, about 37,000 tokens of the benchmark's layer; 1 GiB for act, about 18,000 tokens; 96 MiB
+ * for embed_ple, about 6,000 tokens) is ONE kernel launch: the ops share no tensor, and every CTA of
+ * the persistent grid runs both ops' code in turn, the larger items first (the same device code as
+ * the ops' own entry points, so results are bit-identical to the separate calls). Larger bundles are
+ * issued as the two ops' own launches, which measure as fast or faster once a launch's fixed costs
+ * are small against its traffic. The tensors of the two ops must not overlap; if they do, or if a shape is outside the one-launch
  * kernels' range (attn_prep: fp16 hidden <= 2560 and head_dim 64/128/256; act: head_dim 64/128/256;
  * embed_ple: PLE head_dim 64/128/256), or a non-default design was chosen with
  * wzyb_set_kernel_variant, the entry point issues the ops as separate launches in the order above.

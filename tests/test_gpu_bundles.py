@@ -1,6 +1,6 @@
 """GPU parity of the one-launch layer bundles (wzyb_attn_prep_f16, wzyb_act_f16, wzyb_embed_ple_f16).
 
-Each bundle of up to 256 MiB runs its two ops in one persistent grid (larger ones as the ops' own
+Each bundle up to its measured one-launch size runs its two ops in one persistent grid (larger ones as the ops' own
 launches). Checked here:
   - against the oracle on the same seeded inputs (norms, RoPE, gate, SwiGLU within 2 fp16 ulp; the
     gathers and the residual bit-exact), at the configs' shapes (4096 tokens), a long call (20,000)

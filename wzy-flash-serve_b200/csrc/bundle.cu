@@ -13,8 +13,9 @@
 // Why: at layer-sized calls (4096 tokens, 67-140 MB per op) a launch is dominated by its fixed costs --
 // the launch itself, the DRAM ramp while the first loads are in flight, and the tail where the last
 // warps finish alone. One grid pays them once per bundle, and DRAM streams both ops' traffic at once.
-// Past a few L2's worth of bytes those costs are small, and the ops' own launches (each with its own
-// tuned occupancy) are as fast or faster, so large bundles are issued that way.
+// Past a size measured per bundle (1.25 GiB for attn_prep, 1 GiB for act, 96 MiB for embed_ple) those
+// costs are small, and the ops' own launches (each with its own tuned occupancy) are as fast or
+// faster, so larger bundles are issued that way.
 #include "launch.hpp"
 
 namespace wzyb {
@@ -59,19 +60,23 @@ enum BundleSchedule : int {
     kSchedShared = 3,   // persistent grid, every CTA runs both ops
     kSchedLaunches = 4, // each op as its own launch
 };
-// Bundles of up to this many algorithmic bytes run as one launch with both ops on every CTA; larger
-// ones as the ops' own launches. Measured on B200 with L2 flushed before each call (us, one launch
-// with both ops per CTA / split grid / separate launches): attn_prep 142.6 MB (4096 tokens) 32.0 /
-// 32.1 / 33.8, act 239 MB 41.0 / 41.0 / 42.0, embed_ple 67 MB 16.4 / 18.5 / 17.4; at 4x the tokens the
-// separate launches are as fast or faster (embed_ple 268 MB 49.3 / 59.2 / 46.1) and at 262,144 tokens
-// faster (attn_prep 1642 / 1687 / 1506, act 2498 / 2546 / 2475): each op's own launch has its
-// own tuned occupancy, and a launch's fixed costs no longer matter.
-constexpr double kFuseMaxBytes = 256.0 * (1 << 20);
+// Bundles of up to `max_bytes` algorithmic bytes run as one launch with both ops on every CTA (the
+// larger items first); larger ones as the ops' own launches, each with its own tuned occupancy, once
+// a launch's fixed costs no longer matter. Measured on B200 with L2 flushed before each call (us, one
+// launch / the ops' launches), by token count of the benchmark's layer:
+//   attn_prep (34,816 B/token)  4096: 30.8 / 33.8   8192: 53.3 / 58.4   16384: 103.3 / 109.6
+//                               32768: 197.5 / 202.4   65536: 387.6 / 383.7
+//   act (58,368 B/token)        4096: 38.9 / 42.0   8192: 75.7 / 80.3   16384: 154.8 / 155.3
+//                               32768: 317.6 / 310.0
+//   embed_ple (16,384 B/token)  4096: 16.4 / 17.4   8192: 26.6 / 25.9   16384: 49.7 / 46.2
+constexpr double kFuseMaxAttn = 1.25 * (1 << 30);
+constexpr double kFuseMaxAct = 1.0 * (1 << 30);
+constexpr double kFuseMaxGather = 96.0 * (1 << 20);
 
-static int bundle_schedule(double bundle_bytes) {
+static int bundle_schedule(double bundle_bytes, double max_bytes) {
     const int s = tuning(kFamBundle).stages;
     if (s >= kSchedSplit && s <= kSchedLaunches) return s;
-    return bundle_bytes <= kFuseMaxBytes ? kSchedShared : kSchedLaunches;
+    return bundle_bytes <= max_bytes ? kSchedShared : kSchedLaunches;
 }
 
 // Grid and split for a bundle: every SM filled with `resident` CTAs, or, when the two ops together
@@ -131,16 +136,18 @@ static int64_t head_span_bytes(const HeadSection& s, int64_t T, int hd, int esiz
 // ---------------------------------------------------------------------------------------------
 // configs[1] bundle: residual add + RMSNorm rows (direct design) and q/k norm + RoPE (pair design).
 // ---------------------------------------------------------------------------------------------
-// g_norm < 0: every CTA runs both ops over the whole grid (the q/k heads first, since their body
-// opens with a CTA barrier, then the norm rows with the CTA order reversed, so the warps that took
-// one more head item than others take one row fewer).
+// g_norm < 0: every CTA runs both ops over the whole grid: the norm rows first (the head body's
+// gamma table is filled before them), then the head items with the CTA order reversed, so the warps
+// that took one more row than others take fewer head items.
 template <int VPL, int HD>
 __global__ void __launch_bounds__(kBundleThreads, 2) attn_prep_kernel(const NormRowsArgs na, const HeadRopeArgs ha,
                                                                       int g_norm) {
     pdl_begin();
     if (g_norm < 0) {
-        head_rope_pair_body<__half, HD, 3>(ha, blockIdx.x, gridDim.x);
-        norm_rows_direct_body<__half, __half, VPL>(na, (int)gridDim.x - 1 - (int)blockIdx.x, gridDim.x);
+        // the norm rows (the larger items) first, the head items after them fill the tail
+        head_rope_pair_body<__half, HD, 3>(ha, blockIdx.x, gridDim.x, 1);
+        norm_rows_direct_body<__half, __half, VPL>(na, blockIdx.x, gridDim.x);
+        head_rope_pair_body<__half, HD, 3>(ha, (int)gridDim.x - 1 - (int)blockIdx.x, gridDim.x, 2);
     } else if ((int)blockIdx.x < g_norm) {
         norm_rows_direct_body<__half, __half, VPL>(na, blockIdx.x, g_norm);
     } else {
@@ -178,7 +185,7 @@ static int attn_prep_run(const wzyb_attn_prep_args* p, int64_t T, cudaStream_t s
     const int vpl = vpl_need <= 2 ? 2 : vpl_need <= 4 ? 4 : vpl_need <= 8 ? 8 : vpl_need <= 10 ? 10 : 0;
     const int vn = variant(kFamNorm), vh = variant(kFamHeadRope);
     const double bytes = (double)T * (8.0 * n + 4.0 * (q.heads + k.heads) * hd);
-    const int sched = bundle_schedule(bytes);
+    const int sched = bundle_schedule(bytes, kFuseMaxAttn);
     bool fused = variant(kFamBundle) != WZYB_VARIANT_SPLIT && sched != kSchedLaunches && vpl != 0 &&
                  (vn == WZYB_VARIANT_AUTO || vn == WZYB_VARIANT_DIRECT) &&
                  (vh == WZYB_VARIANT_AUTO || vh == WZYB_VARIANT_PAIR) && tuning(kFamHeadRope).ctas_per_sm != 2;
@@ -228,10 +235,9 @@ __global__ void __launch_bounds__(kBundleThreads, 3) act_kernel(const __half* __
                                                                 const __half* __restrict__ up, __half* __restrict__ out,
                                                                 int64_t nvec, const GdnArgs ga, int g_swiglu) {
     pdl_begin();
-    if (g_swiglu < 0) {  // both ops on every CTA (as attn_prep_kernel)
-        gdn_direct_body<__half, __half, HD, 4, SILU>(ga, blockIdx.x, gridDim.x);
-        swiglu_body<__half, __half, false, PACKED>(gate, up, out, nvec, 0, 0, (int)gridDim.x - 1 - (int)blockIdx.x,
-                                                   gridDim.x);
+    if (g_swiglu < 0) {  // both ops on every CTA: the larger SwiGLU items first (as attn_prep_kernel)
+        swiglu_body<__half, __half, false, PACKED>(gate, up, out, nvec, 0, 0, blockIdx.x, gridDim.x);
+        gdn_direct_body<__half, __half, HD, 4, SILU>(ga, (int)gridDim.x - 1 - (int)blockIdx.x, gridDim.x);
     } else if ((int)blockIdx.x < g_swiglu) {
         swiglu_body<__half, __half, false, PACKED>(gate, up, out, nvec, 0, 0, blockIdx.x, g_swiglu);
     } else {
@@ -268,7 +274,7 @@ static int act_run(const wzyb_act_args* p, int64_t T, cudaStream_t stream) {
     const int hd = p->gdn_head_dim;
     const int vg = variant(kFamGdn);
     const double bytes = 6.0 * (double)n + 6.0 * (double)T * p->gdn_heads * hd;
-    const int sched = bundle_schedule(bytes);
+    const int sched = bundle_schedule(bytes, kFuseMaxAct);
     bool fused = variant(kFamBundle) != WZYB_VARIANT_SPLIT && sched != kSchedLaunches &&
                  (vg == WZYB_VARIANT_AUTO || vg == WZYB_VARIANT_DIRECT) &&
                  n > 0 && T > 0;
@@ -321,7 +327,7 @@ static int act_run(const wzyb_act_args* p, int64_t T, cudaStream_t stream) {
 template <int CH, int U>
 __global__ void __launch_bounds__(kBundleThreads) embed_ple_kernel(const EmbedArgs ea, const PleArgs pa, int g_embed) {
     pdl_begin();
-    if (g_embed < 0) {  // both ops on every CTA (as attn_prep_kernel)
+    if (g_embed < 0) {  // both ops on every CTA: the larger token rows first (as attn_prep_kernel)
         gather_rows_body(ea, blockIdx.x, gridDim.x);
         ple_gather_groups_body<CH, U>(pa, (int)gridDim.x - 1 - (int)blockIdx.x, gridDim.x);
     } else if ((int)blockIdx.x < g_embed) {
@@ -349,7 +355,7 @@ static int embed_ple_run(const wzyb_embed_ple_args* p, int64_t T, cudaStream_t s
 
     const int ch = pa.chunks;
     const double bytes = (double)T * (4.0 * p->hidden + 4.0 * p->ple_heads * p->ple_head_dim);
-    const int sched = bundle_schedule(bytes);
+    const int sched = bundle_schedule(bytes, kFuseMaxGather);
     bool fused = variant(kFamBundle) != WZYB_VARIANT_SPLIT && sched != kSchedLaunches && (ch == 8 || ch == 16 || ch == 32);
     if (fused) {
         const int64_t erow = (int64_t)p->hidden * 2, prow = (int64_t)p->ple_head_dim * 2;

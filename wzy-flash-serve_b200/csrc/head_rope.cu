@@ -212,8 +212,11 @@ __global__ void __launch_bounds__(128) head_rope_direct_kernel(const HeadRopeArg
 // tokens on the same box. With 9 rounds, three (156 registers).
 // The body takes its CTA's index among `nctas` CTAs that share the items (a fused bundle kernel runs it
 // on a subset of its grid); every thread of the CTA must call it (one barrier after the gamma table).
+// parts: 1 fills the CTA's gamma table (ending with a CTA barrier), 2 runs the items, 3 both. A kernel
+// that runs other work first fills the table at its start and runs the items later (the table is one
+// shared array per CTA).
 template <typename T, int HD, int kNH>
-__device__ __forceinline__ void head_rope_pair_body(const HeadRopeArgs& a, int cta, int nctas) {
+__device__ __forceinline__ void head_rope_pair_body(const HeadRopeArgs& a, int cta, int nctas, int parts = 3) {
     constexpr int L2 = HD / 16;   // lanes per head
     constexpr int HPW = 32 / L2;  // heads side by side in one warp
     constexpr int CH = kNH * HPW; // heads per chunk item
@@ -234,6 +237,7 @@ __device__ __forceinline__ void head_rope_pair_body(const HeadRopeArgs& a, int c
     // gammas (+ weight offset) as a lane-major table: sgl[s][k][l] = dims 4(k&1).. of chunk c0 (k < 2)
     // or c1 (k >= 2) of lane l, so each 16-byte gamma load of a head reads one contiguous span
     __shared__ __align__(16) float4 sgl[2][4][L2];
+    if (parts & 1) {
     for (int i = threadIdx.x; i < 8 * L2; i += blockDim.x) {
         const int s = i / (4 * L2), k = (i / L2) % 4, l = i % L2;
         const int c = k < 2 ? (l < P ? l : l + P) : (l < P ? l + P : l + L2);
@@ -246,6 +250,8 @@ __device__ __forceinline__ void head_rope_pair_body(const HeadRopeArgs& a, int c
         sgl[s][k][l] = v;
     }
     __syncthreads();
+    }
+    if (!(parts & 2)) return;
 
     T* const qdata = static_cast<T*>(a.sec[0].data);
     T* const kdata = static_cast<T*>(a.sec[1].heads > 0 ? a.sec[1].data : a.sec[0].data);

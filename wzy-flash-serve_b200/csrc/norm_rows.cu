@@ -70,6 +70,27 @@ __device__ __forceinline__ void norm_rows_direct_body(const NormRowsArgs& a, int
     TO* __restrict__ y = static_cast<TO*>(a.y);
     const bool has_x = x != nullptr;
     const int n = a.n;
+    // One weight row shared by every row (hc == 1): (w_offset + w) in fp32 once per CTA in shared
+    // memory, so a row reads it with two 16-byte shared loads per vector instead of a global load,
+    // eight conversions and four adds.
+    __shared__ __align__(16) float wsm[VPL * 256];
+    const bool wtab = a.hc == 1;
+    if (wtab) {
+        for (int e = threadIdx.x * 8; e < VPL * 256; e += blockDim.x * 8) {
+            float2 g[4];
+            if (e < n) {
+                Vec8<TI>::load_ro2(w + e, g);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) g[i] = fadd2(splat2(a.w_offset), g[i]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) g[i] = splat2(0.f);
+            }
+            *reinterpret_cast<float4*>(wsm + e) = make_float4(g[0].x, g[0].y, g[1].x, g[1].y);
+            *reinterpret_cast<float4*>(wsm + e + 4) = make_float4(g[2].x, g[2].y, g[3].x, g[3].y);
+        }
+        __syncthreads();
+    }
 
     for (int64_t u = gwarp; u < a.units; u += nwarps) {
         typename Vec8<TI>::Raw rr[VPL], rx[VPL];
@@ -115,9 +136,20 @@ __device__ __forceinline__ void norm_rows_direct_body(const NormRowsArgs& a, int
             if (e < n) {
                 float2 v[4], g[4], o[4];
                 residual_sum(k, v);
-                Vec8<TI>::load_ro2(wrow + e, g);
+                if (wtab) {
+                    const float4 g0 = *reinterpret_cast<const float4*>(wsm + e);
+                    const float4 g1 = *reinterpret_cast<const float4*>(wsm + e + 4);
+                    g[0] = make_float2(g0.x, g0.y);
+                    g[1] = make_float2(g0.z, g0.w);
+                    g[2] = make_float2(g1.x, g1.y);
+                    g[3] = make_float2(g1.z, g1.w);
+                } else {
+                    Vec8<TI>::load_ro2(wrow + e, g);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) o[i] = fmul2(fmul2(v[i], sc), fadd2(woff, g[i]));  // (v*sc)*g
+                    for (int i = 0; i < 4; ++i) g[i] = fadd2(woff, g[i]);
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[i] = fmul2(fmul2(v[i], sc), g[i]);  // (v*sc)*g
                 Vec8<TO>::store2(y + u * n + e, o);
                 if (has_x) Vec8<TI>::store2(res + u * n + e, v);
             }

@@ -903,13 +903,21 @@ def main():
         ms_total = t_start.elapsed_time(t_end)
     # Per-launch breakdown (rank 0's hbm and the roofline's achieved bytes): a separate pass of
     # min(K, 100) steps with an event around every launch.
-    # A bundle above the library's one-launch size is issued as its ops' own launches: then every op
-    # launch is timed on its own (the dominant kernel of the roofline is then the SwiGLU launch).
+    # A bundle above the library's one-launch size is issued as its ops' own launches: then each of
+    # its op launches is timed on its own (and the roofline's dominant kernel is the SwiGLU launch).
     kp = min(args.steps, 100)
-    per_op = not args.split and not all(bundle_fused(b, n) for b in STEP_BUNDLES)
-    units = [o for b in STEP_BUNDLES for o in BUNDLES[b]] if per_op else list(STEP_BUNDLES)
-    unit_fn = [(lambda st, o=o: sh.ops[o](st)) for o in units] if per_op else \
-              [(lambda st, i=i: sh.launch(i, st)) for i in range(nb)]
+    # (with --split the bundle call, which then issues its ops' launches itself, is timed as one unit)
+    as_call = {b: args.split or bundle_fused(b, n) for b in STEP_BUNDLES}
+    per_op = not as_call["act_b"]
+    units, unit_fn = [], []
+    for i, b in enumerate(STEP_BUNDLES):
+        if as_call[b]:
+            units.append(b)
+            unit_fn.append(lambda st, i=i: sh.launch(i, st))
+        else:
+            for o in BUNDLES[b]:
+                units.append(o)
+                unit_fn.append(lambda st, o=o: sh.ops[o](st))
     nu = len(units)
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(nu + 1)] for _ in range(kp)]
     for k in range(kp):
@@ -921,7 +929,7 @@ def main():
         ev[k][nu].record(s)
     torch.cuda.synchronize()
     unit_ms = {units[i]: statistics.mean(ev[k][i].elapsed_time(ev[k][i + 1]) for k in range(kp)) for i in range(nu)}
-    kern_ms = [sum(unit_ms[o] for o in BUNDLES[b]) if per_op else unit_ms[b] for b in STEP_BUNDLES]
+    kern_ms = [unit_ms[b] if as_call[b] else sum(unit_ms[o] for o in BUNDLES[b]) for b in STEP_BUNDLES]
     launches = args.steps * sum(1 if (bundle_fused(b, n) and not args.split) else len(BUNDLES[b])
                                 for b in STEP_BUNDLES)
     faults = wz.read_faults()
@@ -977,8 +985,8 @@ def main():
         for i, b in enumerate(STEP_BUNDLES):
             gbs = bundle_bytes(b, n) / (kern_ms[i] * 1e-3) / 1e9
             hbm[b] = [round(kern_ms[i] * 1e3, 1), round(gbs / peak, 4)]
-        if per_op:
-            for o in units:
+        for o in units:
+            if o in BYTES_PER_TOKEN:
                 gbs = (n * BYTES_PER_TOKEN[o] + WEIGHT_BYTES[o]) / (unit_ms[o] * 1e-3) / 1e9
                 hbm[o] = [round(unit_ms[o] * 1e3, 1), round(gbs / peak, 4)]
         reasons = sorted({r for c in clk_all for r in (c["reasons"] if c else [])})

@@ -492,10 +492,12 @@ int wzyb_ple_halo(const int32_t* ids, int64_t row0, const int32_t* seq_prev, int
 int wzyb_prepare_device(void);
 /* Read the current device's fault bits (synchronous); clears them when clear != 0. */
 int wzyb_read_faults(uint32_t* faults, int clear);
-/* Launch-shape tuning per kernel family (process-wide), for A/B measurement: CTAs per SM (1..16) and
- * TMA ring depth (0 = as deep as the shared-memory budget allows, else 1..64 stages) of the ring
- * design. Outside the ring: SwiGLU stages 1 / 2 force the scalar / packed math; head norm+RoPE
- * ctas_per_sm 2 selects the other instantiation of its design. Layer bundles: stages picks the
+/* Launch-shape tuning per kernel family (process-wide), for A/B measurement (ctas_per_sm 1..16,
+ * stages 0..64; what they mean per family): gathers' bulk design: CTAs per SM (1..4, default 2) and
+ * slots per warp (0 = as many as the shared-memory budget allows); add+RMSNorm: stages 1 turns off
+ * the L2 look-ahead of the quantising norm; SwiGLU: CTAs per SM of its grid (default 4), stages 1 / 2
+ * force the scalar / packed math; head
+ * norm+RoPE: ctas_per_sm 2 selects the other instantiation of its design; layer bundles: stages picks the
  * schedule (0 by size as above, 1 the persistent grid split between the ops, 2 one item per warp on a
  * grid sized to the work, 3 both ops on every CTA, 4 the ops' own launches). KV append: stages
  * is the rounds of heads per warp item (0 by size, 1 or 2), ctas_per_sm caps the grid (default 8).

@@ -107,8 +107,25 @@ __device__ __forceinline__ void norm_rows_direct_body(const NormRowsArgs& a, int
         }
         const float2 gate = splat2((has_x && a.inj != nullptr) ? 2.0f / (1.0f + __expf(-a.inj[u] / (float)a.hc))
                                                                 : 1.0f);
-        // v = residual + x * gate (packed FFMA2, the same rounding as the reference's scalar fma)
+        // v = residual + x * gate (packed FFMA2, the same rounding as the reference's scalar fma); with
+        // a unit gate and fp16 inputs, v = fp32(residual) + fp32(x) as one mixed-precision add per
+        // element (add.rn.f32.f16: the fp16 operand widened exactly, one rounding -- the same bits)
+        const bool unit_gate = !(has_x && a.inj != nullptr);
         auto residual_sum = [&](int k, float2 (&v)[4]) {
+            if constexpr (sizeof(TI) == 2) {
+                if (has_x && unit_gate) {
+                    float2 xv[4];
+                    Vec8<TI>::cvt2(rx[k], xv);
+                    const uint32_t* rw = reinterpret_cast<const uint32_t*>(&rr[k]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const unsigned short lo = (unsigned short)(rw[i] & 0xFFFFu), hi = (unsigned short)(rw[i] >> 16);
+                        asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(v[i].x) : "h"(lo), "f"(xv[i].x));
+                        asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(v[i].y) : "h"(hi), "f"(xv[i].y));
+                    }
+                    return;
+                }
+            }
             Vec8<TI>::cvt2(rr[k], v);
             if (has_x) {
                 float2 xv[4];

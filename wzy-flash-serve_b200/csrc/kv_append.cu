@@ -66,8 +66,31 @@ __device__ __forceinline__ int64_t kv_ring_cell(int64_t p, int64_t cap, uint64_t
     return kKvSinkPin + (int64_t)mod_u64((uint64_t)(p - kKvSinkPin), div, recip);
 }
 
-// Quantise this lane's 8 elements as part of its 64-element group (lanes 8m..8m+7) and store the codes
-// (and, from the group's first lane, the fp16 scale) to up to two cells. Every lane must call it.
+// This lane's max |x| (NaNs dropped, as the reference's fmaxf) and its max with NaNs kept.
+__device__ __forceinline__ void kv_lane_max(const float2 (&x)[4], float& am, float& an) {
+    am = 0.f;
+    an = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float a = fabsf(x[i].x), b = fabsf(x[i].y);
+        am = fmaxf(am, fmaxf(a, b));
+        an = fmax_nan(an, fmax_nan(a, b));
+    }
+}
+
+// The group maxima of k and of v (lanes 8m..8m+7), their shuffles interleaved.
+__device__ __forceinline__ void kv_group_max2(float& amk, float& amv) {
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+        const float tk = __shfl_xor_sync(0xffffffffu, amk, o);
+        const float tv = __shfl_xor_sync(0xffffffffu, amv, o);
+        amk = fmaxf(amk, tk);
+        amv = fmaxf(amv, tv);
+    }
+}
+
+// Quantise this lane's 8 elements as part of its 64-element group (lanes 8m..8m+7), given the group
+// max, and store the codes (and, from the group's first lane, the fp16 scale) to up to two cells.
 // Codes are rint(x / d) clamped to [-127, 127] of the correctly rounded quotient, computed without a
 // divide per element (Markstein's theorem: with r = RN(1/d) and q0 = RN(x*r) within one ulp of x/d,
 // the residual e = x - q0*d is exact under FMA and RN(q0 + e*r) is the correctly rounded quotient; d is
@@ -75,19 +98,8 @@ __device__ __forceinline__ int64_t kv_ring_cell(int64_t p, int64_t cap, uint64_t
 // fp32, clamped, and rounded to the nearest even integer as the low byte of fl(q + 1.5 * 2^23). A lane
 // holding a NaN or an infinity, or whose group max is infinite, takes the scalar conversion instead
 // (NaN -> 0 as __float2int_rn), so every code matches the reference's expression.
-__device__ __forceinline__ void kv_q8_store(const float2 (&x)[4], bool act, int lane, int8_t* q0, uint16_t* s0,
-                                            int8_t* q1, uint16_t* s1) {
-    float am = 0.f, an = 0.f;  // group max as the reference's fmaxf; an: this lane's max with NaN kept
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float a = fabsf(x[i].x), b = fabsf(x[i].y);
-        am = fmaxf(am, fmaxf(a, b));
-        an = fmax_nan(an, fmax_nan(a, b));
-    }
-    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
-    if (!act) return;
+__device__ __forceinline__ void kv_q8_codes(const float2 (&x)[4], float am, float an, int lane, int8_t* q0,
+                                            uint16_t* s0, int8_t* q1, uint16_t* s1) {
     const __half sh = __float2half_rn(am / 127.0f);
     const float d = __half2float(sh);
     const float r = d > 0.f ? __frcp_rn(d) : 0.f;
@@ -279,12 +291,18 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
             if (keep) {  // warp-uniform
                 const int col = h * HD + li * 8;
                 const int sc_i = col / kKvGroup;
-                kv_q8_store(p, act, lane, ring ? a.c.ring_k_q + rcell * kvd + col : nullptr,
-                            a.c.ring_k_s + rcell * spc + sc_i, full ? a.c.full_k_q + pos * kvd + col : nullptr,
-                            full ? a.c.full_k_s + pos * spc + sc_i : nullptr);
-                kv_q8_store(v, act, lane, ring ? a.c.ring_v_q + rcell * kvd + col : nullptr,
-                            a.c.ring_v_s + rcell * spc + sc_i, full ? a.c.full_v_q + pos * kvd + col : nullptr,
-                            full ? a.c.full_v_s + pos * spc + sc_i : nullptr);
+                float amk, ank, amv, anv;
+                kv_lane_max(p, amk, ank);
+                kv_lane_max(v, amv, anv);
+                kv_group_max2(amk, amv);
+                if (act) {
+                    kv_q8_codes(p, amk, ank, lane, ring ? a.c.ring_k_q + rcell * kvd + col : nullptr,
+                                a.c.ring_k_s + rcell * spc + sc_i, full ? a.c.full_k_q + pos * kvd + col : nullptr,
+                                full ? a.c.full_k_s + pos * spc + sc_i : nullptr);
+                    kv_q8_codes(v, amv, anv, lane, ring ? a.c.ring_v_q + rcell * kvd + col : nullptr,
+                                a.c.ring_v_s + rcell * spc + sc_i, full ? a.c.full_v_q + pos * kvd + col : nullptr,
+                                full ? a.c.full_v_s + pos * spc + sc_i : nullptr);
+                }
             }
         }
     }

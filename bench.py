@@ -346,7 +346,7 @@ class Gathers:
 
 
 def f8_jobs(wz, torch, dev, T=4096):
-    """The reference model's own kernels (SURVEY next rows: quantisation epilogue, 4-stream residual,
+    """The reference model's own kernels (the quantisation epilogue, 4-stream residual,
     INT8 KV append, fp8 PLE and its block) at 4096 tokens: name -> (launch, algorithmic bytes)."""
     gen = torch.Generator(device=dev).manual_seed(6)
     NE, HC = 2560, 4

@@ -500,7 +500,8 @@ int wzyb_read_faults(uint32_t* faults, int clear);
  * norm+RoPE: ctas_per_sm 2 selects the other instantiation of its design; layer bundles: stages picks the
  * schedule (0 by size as above, 1 the persistent grid split between the ops, 2 one item per warp on a
  * grid sized to the work, 3 both ops on every CTA, 4 the ops' own launches). KV append: stages
- * is the rounds of heads per warp item (0 by size, 1 or 2), ctas_per_sm caps the grid (default 8).
+ * is the rounds of heads per warp item (0 by size, 1 or 2), ctas_per_sm caps the grid of 128-thread CTAs
+ * (default 16).
  * Families: 0 add+RMSNorm, 1 head norm+RoPE, 2 GDN gated norm, 3 SwiGLU, 4 gathers, 5 layer bundles,
  * 6 KV append. */
 #define WZYB_FAM_NORM 0

@@ -152,7 +152,7 @@ __device__ __forceinline__ void kv_q8_codes(const float2 (&x)[4], float am, floa
 // HAS_Q: the launch carries q heads (the q-item code is compiled out otherwise, which keeps the k/v-only
 // kernel's registers down).
 template <typename T, int HD, int kR, bool HAS_Q>
-__global__ void __launch_bounds__(256) kv_append_kernel(const KvAppendArgs a) {
+__global__ void __launch_bounds__(128) kv_append_kernel(const KvAppendArgs a) {
     pdl_begin();
     constexpr int L = HD / 8;
     constexpr int HPW = 32 / L;
@@ -360,14 +360,17 @@ static int launch_kv_append(KvAppendArgs a, int head_dim, cudaStream_t stream) {
     const Tuning tu = tuning(kFamKv);
     const bool split = tu.stages == 1 || (tu.stages != 2 && a.T * (rounds + q_rounds) <= (int64_t)di.sms * 32);
     const int64_t items = split ? a.T * (rounds + q_rounds) : a.T * ((rounds + 1) / 2 + (q_rounds + 1) / 2);
-    const int grid = persistent_grid(di, tu.ctas_per_sm, (items + 7) / 8);
+    // 128-thread CTAs: the same warps per SM as 256-thread ones at these registers, in finer CTAs
+    // (4096 / 65,536 / 262,144 tokens: 14.3 -> 14.1, 105.8 -> 101.4, 390 -> 381 us)
+    constexpr int thr = 128;
+    const int grid = persistent_grid(di, tu.ctas_per_sm, (items + thr / 32 - 1) / (thr / 32));
 #define WZYB_KV(HDV)                                                                              \
     if (a.q_heads > 0) {                                                                          \
-        if (split) launch_k(kv_append_kernel<T, HDV, 1, true>, grid, 256, 0, stream, a);                \
-        else launch_k(kv_append_kernel<T, HDV, 2, true>, grid, 256, 0, stream, a);                      \
+        if (split) launch_k(kv_append_kernel<T, HDV, 1, true>, grid, thr, 0, stream, a);                \
+        else launch_k(kv_append_kernel<T, HDV, 2, true>, grid, thr, 0, stream, a);                      \
     } else {                                                                                      \
-        if (split) launch_k(kv_append_kernel<T, HDV, 1, false>, grid, 256, 0, stream, a);               \
-        else launch_k(kv_append_kernel<T, HDV, 2, false>, grid, 256, 0, stream, a);                     \
+        if (split) launch_k(kv_append_kernel<T, HDV, 1, false>, grid, thr, 0, stream, a);               \
+        else launch_k(kv_append_kernel<T, HDV, 2, false>, grid, thr, 0, stream, a);                     \
     }
     switch (head_dim) {
         case 64: { WZYB_KV(64) break; }

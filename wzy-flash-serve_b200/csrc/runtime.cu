@@ -28,7 +28,7 @@ std::mutex g_dev_mu;
 std::mutex g_smem_mu;
 std::set<std::pair<const void*, int>> g_smem_done;  // (kernel, device)
 
-std::atomic<int> g_tune_ctas[kFamCount] = {{2}, {1}, {1}, {4}, {2}, {1}, {8}};
+std::atomic<int> g_tune_ctas[kFamCount] = {{2}, {1}, {1}, {4}, {2}, {1}, {16}};
 std::atomic<int> g_tune_stages[kFamCount] = {{0}, {0}, {0}, {0}, {0}, {0}, {0}};
 std::atomic<int> g_variant[kFamCount] = {{0}, {0}, {0}, {0}, {0}, {0}, {0}};
 

@@ -592,6 +592,32 @@ def test_kv_append_codes_at_rounding_boundaries(wz, orc):
         assert np.array_equal(_kv_host(dd, nm), getattr(c, nm)), nm
 
 
+def test_kv_append_scales_at_fp16_ties(wz, orc):
+    """The fp16 scale is fp16(max / 127) of the correctly rounded fp32 quotient (the kernel computes it
+    without a divide). Group maxima on and one fp32 ulp either side of 127 times every tie point
+    between adjacent positive fp16 values, subnormal scales included, with the group's other values
+    spread below the max: scales and codes bit-exact against the oracle's IEEE division."""
+    r = rng(4545)
+    vals = np.arange(0, 0x7C00, dtype=np.uint16).view(np.float16).astype(np.float64)
+    ties = (vals[:-1] + vals[1:]) / 2
+    top = (127.0 * ties).astype(np.float32)
+    top = np.concatenate([np.nextafter(top, np.float32(0)), top, np.nextafter(top, np.float32(np.inf))])
+    heads, hd = 2, 256
+    kvd = heads * hd
+    T = -(-top.size * 64 // kvd)
+    groups = T * kvd // 64
+    top = np.concatenate([top, r.choice(top, groups - top.size)])
+    grp = (r.uniform(-1, 1, (groups, 64)) * top[:, None]).astype(np.float32)
+    grp[np.arange(groups), r.integers(0, 64, groups)] = np.where(r.random(groups) < 0.5, -top, top)
+    k = grp.reshape(T, kvd)
+    v = np.ascontiguousarray(k[::-1])
+    c, dd = _kv_seeded(orc, r, T, T, kvd, True)
+    orc.kv_append_int8_f32(k, v, T, kvd, 0, c)
+    wz.kv_append_int8_f32(dev(k), dev(v), T, heads, hd, _kv_desc(wz, dd, T, T, True))
+    for nm in _KV_PLANES:
+        assert np.array_equal(_kv_host(dd, nm), getattr(c, nm)), nm
+
+
 def test_kv_append_codes_non_finite(wz, orc):
     """Groups holding NaN or an infinity take the scalar conversion: NaN codes are 0 (as
     __float2int_rn), an infinite group max gives an infinite scale whose codes are 0, and the other
@@ -604,6 +630,14 @@ def test_kv_append_codes_non_finite(wz, orc):
     k[1, 5], k[2, 70], k[3, 130] = np.nan, np.inf, -np.inf
     v[4, 0], v[5, 63], v[6, 64] = np.nan, np.inf, np.nan
     k[7, 200:210] = np.nan
+    # finite groups whose scale max/127 is at fp16's largest value, at the tie that rounds it to
+    # infinity, and past it (fp32 inputs only): an infinite scale's codes are all 0
+    for (row, g0), top in zip([(8, 64), (9, 128), (10, 192), (11, 256), (12, 0)],
+                              [127.0 * 65504.0, 127.0 * 65520.0, 1e7, 3e38, 127.0 * 65519.0]):
+        grp = r.standard_normal(64).astype(np.float32)
+        grp *= np.float32(top / 4.0 / np.abs(grp).max())
+        grp[7] = np.float32(-top)
+        (v if row % 2 == 0 else k)[row, g0:g0 + 64] = grp
     c, dd = _kv_seeded(orc, r, T, T, kvd, True)
     orc.kv_append_int8_f32(k, v, T, kvd, 0, c)
     wz.kv_append_int8_f32(dev(k), dev(v), T, heads, hd, _kv_desc(wz, dd, T, T, True))

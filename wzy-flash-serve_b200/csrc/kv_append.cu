@@ -78,68 +78,103 @@ __device__ __forceinline__ void kv_lane_max(const float2 (&x)[4], float& am, flo
     }
 }
 
-// The group maxima of k and of v (lanes 8m..8m+7), their shuffles interleaved.
-__device__ __forceinline__ void kv_group_max2(float& amk, float& amv) {
+// The group maxima (lanes 8m..8m+7) of N vectors, their shuffles interleaved.
+template <int N>
+__device__ __forceinline__ void kv_group_max(float (&am)[N]) {
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) {
-        const float tk = __shfl_xor_sync(0xffffffffu, amk, o);
-        const float tv = __shfl_xor_sync(0xffffffffu, amv, o);
-        amk = fmaxf(amk, tk);
-        amv = fmaxf(amv, tv);
+        float t[N];
+#pragma unroll
+        for (int m = 0; m < N; ++m) t[m] = __shfl_xor_sync(0xffffffffu, am[m], o);
+#pragma unroll
+        for (int m = 0; m < N; ++m) am[m] = fmaxf(am[m], t[m]);
     }
 }
 
-// Quantise this lane's 8 elements as part of its 64-element group (lanes 8m..8m+7), given the group
-// max, and store the codes (and, from the group's first lane, the fp16 scale) to up to two cells.
-// Codes are rint(x / d) clamped to [-127, 127] of the correctly rounded quotient, computed without a
-// divide per element (Markstein's theorem: with r = RN(1/d) and q0 = RN(x*r) within one ulp of x/d,
-// the residual e = x - q0*d is exact under FMA and RN(q0 + e*r) is the correctly rounded quotient; d is
-// 0 or an fp16 value >= 2^-24, so nothing underflows where the rounding can change the code), in packed
-// fp32, clamped, and rounded to the nearest even integer as the low byte of fl(q + 1.5 * 2^23). A lane
-// holding a NaN or an infinity, or whose group max is infinite, takes the scalar conversion instead
-// (NaN -> 0 as __float2int_rn), so every code matches the reference's expression.
-__device__ __forceinline__ void kv_q8_codes(const float2 (&x)[4], float am, float an, int lane, int8_t* q0,
-                                            uint16_t* s0, int8_t* q1, uint16_t* s1) {
-    const __half sh = __float2half_rn(am / 127.0f);
-    const float d = __half2float(sh);
-    const float r = d > 0.f ? __frcp_rn(d) : 0.f;
-    uint32_t w[2];
-    if (an <= 3.402823466e38f && am <= 3.402823466e38f) {
-        const float2 nr2 = splat2(-r), r2 = splat2(r), d2 = splat2(d);
-        uint32_t b[8];
+// A group's fp16 scale fp16(RN(am / 127)) for am >= 0, with the quotient by Markstein's sequence
+// instead of a divide: r = RN(1/127) (0x3C010204), q0 = RN(am * r), e = am - q0 * 127 (exact under
+// FMA), RN(q0 + e * r) is the correctly rounded quotient wherever it is a normal fp32. Quotients below
+// 2^-126 give a zero fp16 scale either way, and am = inf keeps inf. Branch-free.
+__device__ __forceinline__ __half kv_group_scale(float am) {
+    const float r = __int_as_float(0x3C010204);
+    const float q0 = __fmul_rn(am, r);
+    const float q = fmaf(fmaf(-q0, 127.0f, am), r, q0);
+    return __float2half_rn(am <= 3.402823466e38f ? q : am);
+}
+
+// RN(1/d) for a scale d = 0 (gives 0) or a finite fp16 scale (a normal fp32 in [2^-24, 65504]), by one
+// Newton-Raphson step from the approximate reciprocal: y0 = rcp.approx(d) (within 1 ulp), then
+// RN(y0 + y0 * (1 - d * y0)). The residual 1 - d*y0 needs at most 12 significant bits (d has 11), so
+// the FMA computes it exactly, and the step leaves a relative error below 2^-44. 1/d = 2^-k / M for an
+// odd M < 2^11 lies at least 2^-36 (relative) from every fp32 rounding midpoint, so the final rounding
+// is the correct one. Branch-free; d = inf is not an input (those groups take the scalar path).
+__device__ __forceinline__ float kv_recip(float d) {
+    float y0;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y0) : "f"(d));
+    const float y = fmaf(y0, fmaf(-d, y0, 1.0f), y0);
+    return d > 0.f ? y : 0.f;
+}
+
+// The 8 codes of this lane's elements in a 64-element group with scale d (r = RN(1/d), 0 when d = 0),
+// packed little-endian into a uint2. Codes are rint(x / d) clamped to [-127, 127] of the correctly
+// rounded quotient, computed without a divide per element (Markstein's theorem: with r = RN(1/d) and
+// q0 = RN(x*r) within one ulp of x/d, the residual e = x - q0*d is exact under FMA and RN(q0 + e*r) is
+// the correctly rounded quotient; d is 0 or an fp16 value >= 2^-24, so nothing underflows where the
+// rounding can change the code), in packed fp32, and rounded to the nearest even integer as the low
+// byte of fl(q + 1.5 * 2^23). kClamp = false needs every |x| <= the group max am and d a normal fp16
+// (or 0): then d >= (am / 127)(1 - 2^-24)(1 - 2^-11), |x / d| < 127.07 and the clamp cannot act.
+// Every x must be finite and d <= 65504.
+template <bool kClamp>
+__device__ __forceinline__ uint2 kv_q8_pack(const float2 (&x)[4], float d, float r) {
+    const float2 nr2 = splat2(-r), r2 = splat2(r), d2 = splat2(d);
+    uint32_t b[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float2 nq0 = fmul2_unfused(x[i], nr2);                         // -RN(x*r)
-            const float2 e = ffma2(nq0, d2, x[i]);                               // x - q0*d, exact
-            float2 q = ffma2(e, r2, make_float2(-nq0.x, -nq0.y));                // RN(x / d)
+    for (int i = 0; i < 4; ++i) {
+        const float2 nq0 = fmul2_unfused(x[i], nr2);                         // -RN(x*r)
+        const float2 e = ffma2(nq0, d2, x[i]);                               // x - q0*d, exact
+        float2 q = ffma2(e, r2, make_float2(-nq0.x, -nq0.y));                // RN(x / d)
+        if (kClamp) {
             q.x = fminf(fmaxf(q.x, -127.0f), 127.0f);
             q.y = fminf(fmaxf(q.y, -127.0f), 127.0f);
-            const float2 t = fadd2(q, splat2(12582912.0f));                      // rint in the low byte
-            b[2 * i] = __float_as_uint(t.x);
-            b[2 * i + 1] = __float_as_uint(t.y);
         }
-#pragma unroll
-        for (int k = 0; k < 2; ++k)
-            w[k] = __byte_perm(__byte_perm(b[4 * k], b[4 * k + 1], 0x0040),
-                               __byte_perm(b[4 * k + 2], b[4 * k + 3], 0x0040), 0x5410);
-    } else {
-        w[0] = w[1] = 0u;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float v = (i & 1) ? x[i >> 1].y : x[i >> 1].x;
-            const int qi = d > 0.f ? max(-127, min(127, __float2int_rn(v / d))) : 0;
-            w[i >> 2] |= ((uint32_t)(qi & 0xFF)) << ((i & 3) * 8);
-        }
+        const float2 t = fadd2(q, splat2(12582912.0f));                      // rint in the low byte
+        b[2 * i] = __float_as_uint(t.x);
+        b[2 * i + 1] = __float_as_uint(t.y);
     }
-    const uint2 packed = make_uint2(w[0], w[1]);
-    const uint16_t sbits = __half_as_ushort(sh);
+    uint32_t w[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+        w[k] = __byte_perm(__byte_perm(b[4 * k], b[4 * k + 1], 0x0040),
+                           __byte_perm(b[4 * k + 2], b[4 * k + 3], 0x0040), 0x5410);
+    return make_uint2(w[0], w[1]);
+}
+
+// kv_q8_pack for any group: the packed path while this lane's values are finite (an, the lane's max
+// with NaNs kept, is finite) and the scale is finite; otherwise the scalar conversion, so NaN codes are
+// 0 (as __float2int_rn) and a finite group whose scale rounds to fp16 infinity (max >= 127 * 65520, fp32
+// inputs only) gets x / inf = 0, every code as the reference's expression.
+__device__ __forceinline__ uint2 kv_q8_pack_any(const float2 (&x)[4], float an, float d, float r) {
+    if (an <= 3.402823466e38f && d <= 65504.0f) return kv_q8_pack<true>(x, d, r);
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float v = (i & 1) ? x[i >> 1].y : x[i >> 1].x;
+        const int qi = d > 0.f ? max(-127, min(127, __float2int_rn(v / d))) : 0;
+        w[i >> 2] |= ((uint32_t)(qi & 0xFF)) << ((i & 3) * 8);
+    }
+    return make_uint2(w[0], w[1]);
+}
+
+// Store a lane's packed codes (and, from the group's first lane, the fp16 scale) to up to two cells.
+__device__ __forceinline__ void kv_q8_store(uint2 codes, uint16_t sbits, int lane, int8_t* q0, uint16_t* s0,
+                                            int8_t* q1, uint16_t* s1) {
     const bool first = (lane & 7) == 0;
     if (q0 != nullptr) {
-        *reinterpret_cast<uint2*>(q0) = packed;
+        *reinterpret_cast<uint2*>(q0) = codes;
         if (first) *s0 = sbits;
     }
     if (q1 != nullptr) {
-        *reinterpret_cast<uint2*>(q1) = packed;
+        *reinterpret_cast<uint2*>(q1) = codes;
         if (first) *s1 = sbits;
     }
 }
@@ -152,7 +187,7 @@ __device__ __forceinline__ void kv_q8_codes(const float2 (&x)[4], float am, floa
 // HAS_Q: the launch carries q heads (the q-item code is compiled out otherwise, which keeps the k/v-only
 // kernel's registers down).
 template <typename T, int HD, int kR, bool HAS_Q>
-__global__ void __launch_bounds__(128) kv_append_kernel(const KvAppendArgs a) {
+__global__ void __launch_bounds__(128, HAS_Q && sizeof(T) == 4 ? 3 : 4) kv_append_kernel(const KvAppendArgs a) {
     pdl_begin();
     constexpr int L = HD / 8;
     constexpr int HPW = 32 / L;
@@ -193,22 +228,38 @@ __global__ void __launch_bounds__(128) kv_append_kernel(const KvAppendArgs a) {
             for (int i = 0; i < 4; ++i) s2[i] = make_float2(-s2[i].x, -s2[i].y);
         }
     };
-    // p *= rsqrt(mean(p^2) + eps) * gamma, then the pair rotation (one shuffle per element)
-    auto norm_rotate = [&](float2 (&p)[4], const float2 (&gm)[4], bool rot, const float2 (&c2)[4],
-                           const float2 (&s2)[4]) {
-        const float ss = group_sum<L>(sumsq8(p));
-        const float2 sc = splat2(rsqrt_approx(ss / (float)HD + a.eps));
+    // p[j] *= rsqrt(mean(p[j]^2) + eps) * gamma, then the pair rotation (one shuffle per element), for
+    // the N heads in p (float2[N][4]) together, so their dependent chains interleave
+    auto norm_rotate = [&](auto& p, const float2 (&gm)[4], bool rot, const float2 (&c2)[4], const float2 (&s2)[4]) {
+        constexpr int N = sizeof(p) / sizeof(p[0]);
+        float ss[N];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) p[i] = fmul2(p[i], fmul2(sc, gm[i]));
-        float2 q[4];
+        for (int j = 0; j < N; ++j) ss[j] = sumsq8(p[j]);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            q[i].x = __shfl_sync(0xffffffffu, p[i].x, src);
-            q[i].y = __shfl_sync(0xffffffffu, p[i].y, src);
+        for (int o = L / 2; o > 0; o >>= 1) {
+            float tt[N];
+#pragma unroll
+            for (int j = 0; j < N; ++j) tt[j] = __shfl_xor_sync(0xffffffffu, ss[j], o);
+#pragma unroll
+            for (int j = 0; j < N; ++j) ss[j] += tt[j];
+        }
+        float2 q[N][4];
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+            const float2 sc = splat2(rsqrt_approx(ss[j] / (float)HD + a.eps));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) p[j][i] = fmul2(p[j][i], fmul2(sc, gm[i]));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                q[j][i].x = __shfl_sync(0xffffffffu, p[j][i].x, src);
+                q[j][i].y = __shfl_sync(0xffffffffu, p[j][i].y, src);
+            }
         }
         if (rot) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) p[i] = ffma2(q[i], s2[i], fmul2(p[i], c2[i]));
+            for (int j = 0; j < N; ++j)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) p[j][i] = ffma2(q[j][i], s2[i], fmul2(p[j][i], c2[i]));
         }
     };
 
@@ -232,20 +283,21 @@ __global__ void __launch_bounds__(128) kv_append_kernel(const KvAppendArgs a) {
             const bool pos_ok = half > 0 && pos >= 0 && pos < a.table_rows;
             float2 c2[4], s2[4];
             if (pos_ok && rot_lane) load_cos_sin(pos, c2, s2);
+            // one head at a time: interleaving the q heads' chains measured slower (register pressure)
 #pragma unroll
             for (int j = 0; j < kR; ++j) {
                 if (q0 + j >= q_rounds) break;  // warp-uniform
                 const int h = (q0 + j) * HPW + hw;
                 const bool act = h < a.q_heads;
-                float2 p[4];
+                float2 p[1][4];
                 if (act) {
-                    Vec8<T>::cvt2(qr[j], p);
+                    Vec8<T>::cvt2(qr[j], p[0]);
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) p[i] = splat2(0.f);
+                    for (int i = 0; i < 4; ++i) p[0][i] = splat2(0.f);
                 }
                 norm_rotate(p, gq, pos_ok && rot_lane, c2, s2);
-                if (act) Vec8<T>::store2(qrow + h * a.q_head_stride + li * 8, p);
+                if (act) Vec8<T>::store2(qrow + h * a.q_head_stride + li * 8, p[0]);
             }
             continue;
         }
@@ -270,39 +322,73 @@ __global__ void __launch_bounds__(128) kv_append_kernel(const KvAppendArgs a) {
             if (pos_ok && rot_lane) load_cos_sin(pos, c2, s2);
             if (half > 0 && !pos_ok && lane == 0 && r0 == 0) raise_fault(WZYB_FAULT_POS_RANGE);
         }
+        // the kR rounds' heads go through each step together, so their dependent chains interleave
+        // (a round past the last one runs on zeros and stores nothing)
+        bool act[kR];
+        int col[kR];
+        float2 p[kR][4], v[kR][4];
 #pragma unroll
         for (int j = 0; j < kR; ++j) {
-            if (r0 + j >= rounds) break;  // warp-uniform
             const int h = (r0 + j) * HPW + hw;
-            const bool act = h < a.kv_heads;
-            const int64_t off = t * kvd + h * HD + li * 8;
-            float2 p[4], v[4];
-            if (act) {
-                Vec8<T>::cvt2(kr[j], p);
-                Vec8<T>::cvt2(vr[j], v);
+            act[j] = r0 + j < rounds && h < a.kv_heads;
+            col[j] = h * HD + li * 8;
+            if (act[j]) {
+                Vec8<T>::cvt2(kr[j], p[j]);
+                Vec8<T>::cvt2(vr[j], v[j]);
             } else {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) p[i] = v[i] = splat2(0.f);
+                for (int i = 0; i < 4; ++i) p[j][i] = v[j][i] = splat2(0.f);
             }
-            if (a.norm_rope) {
-                norm_rotate(p, g, pos_ok && rot_lane, c2, s2);
-                if (act) Vec8<T>::store2(kd + off, p);
+        }
+        if (a.norm_rope) {  // warp-uniform
+            norm_rotate(p, g, pos_ok && rot_lane, c2, s2);
+#pragma unroll
+            for (int j = 0; j < kR; ++j)
+                if (act[j]) Vec8<T>::store2(kd + t * kvd + col[j], p[j]);
+        }
+        if (keep) {  // warp-uniform
+            constexpr int N = 2 * kR;  // vectors: k and v of each round
+            float am[N], an[N], d[N], r[N];
+            __half sh[N];
+#pragma unroll
+            for (int j = 0; j < kR; ++j) {
+                kv_lane_max(p[j], am[2 * j], an[2 * j]);
+                kv_lane_max(v[j], am[2 * j + 1], an[2 * j + 1]);
             }
-            if (keep) {  // warp-uniform
-                const int col = h * HD + li * 8;
-                const int sc_i = col / kKvGroup;
-                float amk, ank, amv, anv;
-                kv_lane_max(p, amk, ank);
-                kv_lane_max(v, amv, anv);
-                kv_group_max2(amk, amv);
-                if (act) {
-                    kv_q8_codes(p, amk, ank, lane, ring ? a.c.ring_k_q + rcell * kvd + col : nullptr,
-                                a.c.ring_k_s + rcell * spc + sc_i, full ? a.c.full_k_q + pos * kvd + col : nullptr,
-                                full ? a.c.full_k_s + pos * spc + sc_i : nullptr);
-                    kv_q8_codes(v, amv, anv, lane, ring ? a.c.ring_v_q + rcell * kvd + col : nullptr,
-                                a.c.ring_v_s + rcell * spc + sc_i, full ? a.c.full_v_q + pos * kvd + col : nullptr,
-                                full ? a.c.full_v_s + pos * spc + sc_i : nullptr);
+            kv_group_max<N>(am);
+            bool plain = true;  // every vector finite with a normal (or zero) fp16 scale
+#pragma unroll
+            for (int m = 0; m < N; ++m) {
+                sh[m] = kv_group_scale(am[m]);
+                d[m] = __half2float(sh[m]);
+                r[m] = kv_recip(d[m]);
+                plain = plain && an[m] <= 3.402823466e38f && d[m] <= 65504.0f &&
+                        (d[m] >= 6.103515625e-05f || d[m] == 0.f);
+            }
+            uint2 codes[N];
+            if (plain) {
+#pragma unroll
+                for (int j = 0; j < kR; ++j) {
+                    codes[2 * j] = kv_q8_pack<false>(p[j], d[2 * j], r[2 * j]);
+                    codes[2 * j + 1] = kv_q8_pack<false>(v[j], d[2 * j + 1], r[2 * j + 1]);
                 }
+            } else {
+#pragma unroll
+                for (int j = 0; j < kR; ++j) {
+                    codes[2 * j] = kv_q8_pack_any(p[j], an[2 * j], d[2 * j], r[2 * j]);
+                    codes[2 * j + 1] = kv_q8_pack_any(v[j], an[2 * j + 1], d[2 * j + 1], r[2 * j + 1]);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kR; ++j) {
+                if (!act[j]) continue;
+                const int c = col[j], sc_i = c / kKvGroup;
+                kv_q8_store(codes[2 * j], __half_as_ushort(sh[2 * j]), lane,
+                            ring ? a.c.ring_k_q + rcell * kvd + c : nullptr, a.c.ring_k_s + rcell * spc + sc_i,
+                            full ? a.c.full_k_q + pos * kvd + c : nullptr, full ? a.c.full_k_s + pos * spc + sc_i : nullptr);
+                kv_q8_store(codes[2 * j + 1], __half_as_ushort(sh[2 * j + 1]), lane,
+                            ring ? a.c.ring_v_q + rcell * kvd + c : nullptr, a.c.ring_v_s + rcell * spc + sc_i,
+                            full ? a.c.full_v_q + pos * kvd + c : nullptr, full ? a.c.full_v_s + pos * spc + sc_i : nullptr);
             }
         }
     }

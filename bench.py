@@ -728,6 +728,8 @@ def profile_case(wz, torch, name, T, reps):
             ids = torch.randint(0, 248320, (T,), generator=gen, device=dev, dtype=torch.int32)
             out = torch.empty((T, 2560), device=dev)
             fn = lambda: wz.ple_gather_fp8_f32(table, 160, 0.5, hsh, ids, out, stream=s)  # noqa: E731
+        elif name == "kv":
+            keep, fn = kv_case(wz, torch, dev, T, s)
         else:
             jobs, keep = f8_jobs_small(wz, torch, dev, T)
             if name not in jobs:
@@ -737,6 +739,21 @@ def profile_case(wz, torch, name, T, reps):
         fn()
     torch.cuda.synchronize()
     print("ok", name, T, flush=True)
+
+
+def kv_case(wz, torch, dev, T, s):
+    """k norm + RoPE + INT8 KV append at the reference model's widths (2 heads of 256), fp16 k and v, a
+    ring of T cells and the full-context mirror: only its own tensors, so larger T stay small."""
+    gen = torch.Generator(device=dev).manual_seed(1)
+    k = torch.randn((T, 512), generator=gen, device=dev).half()
+    v = torch.randn((T, 512), generator=gen, device=dev).half()
+    kg = (0.02 * torch.randn(256, generator=gen, device=dev)).half()
+    pl = [torch.zeros((T, 512), dtype=torch.int8, device=dev) if i % 2 == 0 else
+          torch.zeros((T, 8), dtype=torch.int16, device=dev) for i in range(8)]
+    cache = wz.kv_cache(*pl[:4], T, T, *pl[4:])
+    c, sn = rope_tables(wz, torch, T, dev)
+    fn = lambda: wz.k_rope_kv_append(k, kg, v, c, sn, T, 2, 256, cache, rot_dims=64, w_offset=1.0, stream=s)  # noqa: E731
+    return [k, v, kg, pl, c, sn], fn
 
 
 def f8_jobs_small(wz, torch, dev, T):
@@ -760,16 +777,8 @@ def f8_jobs_small(wz, torch, dev, T):
     cw = torch.randn((hcd, 4), generator=gen, device=dev)
     hist = torch.randn((hcd, 9), generator=gen, device=dev)
     rc = torch.randn((T, hcd), generator=gen, device=dev)
-    k = torch.randn((T, 512), generator=gen, device=dev).half()
-    v = torch.randn((T, 512), generator=gen, device=dev).half()
-    kg = (0.02 * torch.randn(256, generator=gen, device=dev)).half()
-    pl = [torch.zeros((T, 512), dtype=torch.int8, device=dev) if i % 2 == 0 else
-          torch.zeros((T, 8), dtype=torch.int16, device=dev) for i in range(8)]
-    cache = wz.kv_cache(*pl[:4], T, T, *pl[4:])
-    c, sn = rope_tables(wz, torch, T, dev)
-    keep = [R, blk, inj, wn, xn, xq, xs, q16, s16, x16, g16, m16, q, cw, hist, rc, k, v, kg, pl, c, sn]
+    keep = [R, blk, inj, wn, xn, xq, xs, q16, s16, x16, g16, m16, q, cw, hist, rc]
     jobs = {
-        "kv": lambda st: wz.k_rope_kv_append(k, kg, v, c, sn, T, 2, 256, cache, rot_dims=64, w_offset=1.0, stream=st),
         "conv": lambda st: wz.ple_conv_f32(R.view(T, hcd), cw, hist, xn.view(T, hcd), rc, T, hcd, stream=st),
         "grn": lambda st: wz.gr_norm_f32(R, wn, blk, inj, xn, T, NE, HC, stream=st),
         "grq8": lambda st: wz.gr_norm_q8_f32(R, wn, blk, inj, xn, xq, xs, T, NE, HC, stream=st),

@@ -164,8 +164,9 @@ static void q8_group_n(const float* v, int n, int8_t* q, float* s) {
     const float inv = d > 0.f ? 127.0f / am : 0.f;
     for (int i = 0; i < n; ++i) {
         const float t = v[i] * inv;
-        /* __float2int_rn maps NaN (a NaN or infinite input) to 0 */
-        int qi = isnan(t) ? 0 : (int)rintf(t);
+        /* __float2int_rn maps NaN (a NaN or infinite input) to 0 and saturates: t = +-inf (a tiny    */
+        /* nonzero amax, where 127/amax overflows) clamps to +-127                                    */
+        int qi = isnan(t) ? 0 : t >= 127.f ? 127 : t <= -127.f ? -127 : (int)rintf(t);
         q[i] = (int8_t)(qi < -127 ? -127 : (qi > 127 ? 127 : qi));
     }
     *s = d;

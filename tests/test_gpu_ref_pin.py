@@ -236,6 +236,9 @@ def test_pin_q8_side_outputs(ref, orc, wz):
     nff = 640
     g = (2 * r.standard_normal(nff * T)).astype(np.float32)
     u = r.standard_normal(nff * T).astype(np.float32)
+    # groups of tiny products: 127 / amax overflows (codes +-127 / 0), and amax / 127 rounds to 0
+    for i, scale in enumerate([1e-38, 2e-37, 1e-42, 1e-44]):
+        u[32 * i:32 * i + 32] *= np.float32(scale)
     q32 = torch.empty(nff * T, dtype=torch.int8, device=DEV)
     s32 = torch.empty(nff * T // 32, dtype=torch.float32, device=DEV)
     dg, du = dev(g), dev(u)
@@ -403,11 +406,33 @@ def test_pin_ple_gate_and_conv(ref, orc, wz):
     assert np.array_equal(oh, host(rh)) and np.array_equal(osn, host(rs))
 
 
+def _tiny_groups(r, x):
+    """Row 0 of x: Q8 groups whose max is so small that 127 / max overflows to infinity while max / 127
+    is still above 0 (codes then +-127 for nonzero values and 0 for zeros, as __float2int_rn(+-inf)
+    and of NaN clamp), at the finite edge of 127 / max, subnormal maxima whose max / 127 rounds to 0
+    or not, tiny groups holding a NaN or an infinity, and 16-element halves of different sizes."""
+    def grp(n, top):
+        g = (r.uniform(-1, 1, n) * top).astype(np.float32)
+        g[r.integers(0, n)] = np.float32(top)
+        return g
+    specs = [(1e-38, None), (3.0e-37, None), (4.0e-37, None), (1e-43, None), (5e-44, None),
+             (1e-38, np.nan), (1e-38, np.inf), (1e-40, None)]
+    for i, (top, special) in enumerate(specs):
+        g = grp(32, top)
+        g[5] = 0.0
+        if special is not None:
+            g[11] = special
+        x[0, 32 * i:32 * i + 32] = g
+    x[0, 256:272], x[0, 272:288] = grp(16, 1e-39), grp(16, 1.0)
+
+
 def test_pin_quant_act(ref, orc, wz):
-    """quant_act_multi with both outputs (the src/wzy_stage_v2.cuh:697 launch) at n_embd 2560."""
+    """quant_act_multi with both outputs (the src/wzy_stage_v2.cuh:697 launch) at n_embd 2560, with
+    the edge groups of _tiny_groups in row 0."""
     r = np.random.default_rng(213)
     T, cols = 16, 2560
     x = (3 * r.standard_normal((T, cols))).astype(np.float32)
+    _tiny_groups(r, x)
     dx = dev(x)
     n = T * cols
     rq32, rq16 = torch.empty(n, dtype=torch.int8, device=DEV), torch.empty(n, dtype=torch.int8, device=DEV)

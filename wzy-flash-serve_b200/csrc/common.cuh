@@ -442,9 +442,10 @@ __device__ __forceinline__ float2 sigmoid2(float2 z) {
 // unit is 1 there, so the add itself is the round-to-nearest-even;
 // packed FMA2 (+0 addend) and FADD2 on the FMA pipe instead of a conversion instruction per element
 // (SwiGLU + Q8 80 -> 82 %, the quantiser 78 -> 81 % of HBM peak). A lane whose 8 values are not all
-// finite (seen by a NaN-propagating
-// max) takes the conversion instruction instead, which maps the NaN that t then is to 0 as the
-// reference's __float2int_rn does; the group's amax drops NaNs (fmaxf) as the reference's does.
+// finite (seen by a NaN-propagating max), or whose group max is so small (below ~3.7e-37) that
+// 127 / amax overflows to infinity while amax / 127 does not underflow to 0, takes the reference's own
+// conversion instead: __float2int_rn(v * inv) clamped to [-127, 127], which maps the NaN that t then is
+// to 0 and t = +-inf to +-127; the group's amax drops NaNs (fmaxf) as the reference's does.
 __device__ __forceinline__ float fmax_nan(float a, float b) {
     float r;
     asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
@@ -477,7 +478,7 @@ __device__ __forceinline__ void q8_codes_store(const float (&v)[8], float am, bo
     const float d = am / 127.0f;
     const float inv = d > 0.f ? 127.0f / am : 0.f;
     uint32_t b[8];
-    if (finite) {
+    if (finite && inv <= 3.402823466e38f) {
 #pragma unroll
         for (int i = 0; i < 8; i += 2) {
             const float2 t = fadd2(fmul2_unfused(make_float2(v[i], v[i + 1]), splat2(inv)), splat2(12582912.0f));
@@ -486,7 +487,7 @@ __device__ __forceinline__ void q8_codes_store(const float (&v)[8], float am, bo
         }
     } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(b[i]) : "f"(v[i] * inv));
+        for (int i = 0; i < 8; ++i) b[i] = (uint32_t)max(-127, min(127, __float2int_rn(v[i] * inv)));
     }
     uint32_t w[2];
 #pragma unroll

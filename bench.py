@@ -369,6 +369,8 @@ def f8_jobs(wz, torch, dev, T=4096):
     kk16 = torch.randn((T, KVD), generator=gen, device=dev).half()
     vv16 = torch.randn((T, KVD), generator=gen, device=dev).half()
     kg16 = (0.02 * torch.randn(HD, generator=gen, device=dev)).half()
+    kk32, vv32 = kk16.float(), vv16.float()  # the reference's own k / v type
+    kg32 = kg16.float()
     kv_planes = [torch.zeros((T, KVD), dtype=torch.int8, device=dev) if i % 2 == 0 else
                  torch.zeros((T, KVD // 64), dtype=torch.int16, device=dev) for i in range(8)]
     kvc = wz.kv_cache(*kv_planes[:4], T, T, *kv_planes[4:])  # ring of T cells: every token lands in it
@@ -384,11 +386,14 @@ def f8_jobs(wz, torch, dev, T=4096):
     pcw = 0.5 * torch.randn((HC * NE, 4), generator=gen, device=dev)
     phist = torch.randn((HC * NE, 9), generator=gen, device=dev)
     keep = [R, blk, inj, wn, xn16, gg16, mx, mx16, xn32, xq8, xs8, g32, u32, q32, s32, q16b, s16b, kk16, vv16, kg16,
-            kv_planes, kv_tab, ids, ple8, ple8_out, pk, pq, pgv, pcw, phist]
+            kv_planes, kv_tab, ids, ple8, ple8_out, pk, pq, pgv, pcw, phist, kk32, vv32, kg32]
     jobs = {
         "kv": (lambda s: wz.k_rope_kv_append(kk16, kg16, vv16, kv_tab[0], kv_tab[1], T, KH, HD, kvc, rot_dims=ROT,
                                              eps=EPS, w_offset=1.0, stream=s),
                T * KVD * 2 * 3 + T * KVD * 4 + T * (KVD // 64) * 2 * 4 + HD * 2),
+        "kv32": (lambda s: wz.k_rope_kv_append(kk32, kg32, vv32, kv_tab[0], kv_tab[1], T, KH, HD, kvc, rot_dims=ROT,
+                                               eps=EPS, w_offset=1.0, stream=s),
+                 T * KVD * 4 * 3 + T * KVD * 4 + T * (KVD // 64) * 2 * 4 + HD * 4),
         "ple8": (lambda s: wz.ple_gather_fp8_f32(ple8, 160, 0.5, ple8_hash, ids, ple8_out, stream=s),
                  T * 16 * 160 + T * 2560 * 4 + T * 4),
         "gate": (lambda s: wz.ple_gate_f32(pk, pq, blk, pgv, T, NE, HC, stream=s), rows * 12 + T * NE * 4),
@@ -665,6 +670,79 @@ def reference_gpu(peak):
     return out
 
 
+def reference_gpu_f8(peak):
+    """The reference model's own kernels for the quantisation epilogue, the 4-stream residual, the INT8
+    KV append and the PLE block (compiled from its sources into oracle/_ref/libwzyref.so) at 4096
+    tokens, n_embd 2560, 4 streams, in its own launch shapes and types, L2 flushed before every launch:
+    name -> [us, fraction of peak]. The fraction counts the same algorithmic bytes as the GPU arm's
+    entry of that name (`kv32`: k norm + RoPE, then the append, two launches, fp32 k and v)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    import torch
+
+    if not torch.cuda.is_available():
+        return {"unavailable": "no GPU"}
+    if not orc.ref_available():
+        return {"unavailable": "oracle/_ref/libwzyref.so not built (needs the reference sources at build time)"}
+    R_ = orc.ref_lib()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    T, NE, HC = 4096, 2560, 4
+    rows, hcd, KVD = T * HC * NE, HC * NE, KH * HD
+    nq = T * EXPERT_ROWS * FFN
+    g = torch.Generator(device=dev).manual_seed(22)
+    f32 = lambda *shape: torch.randn(shape, generator=g, device=dev)  # noqa: E731
+    emp = lambda *shape, dt=torch.float32: torch.empty(shape, dtype=dt, device=dev)  # noqa: E731
+    fl = Flushed(torch, dev)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    S = lambda s: ctypes.c_void_p(s.cuda_stream)  # noqa: E731
+    R, blk, inj, wn = f32(T * HC, NE), f32(T, NE), f32(T * HC), 1 + 0.02 * f32(HC, NE)
+    xn, xq8, xs8 = emp(T * HC, NE), emp(T * HC, NE, dt=torch.int8), emp(T * HC, NE // 32)
+    xn16, gg16 = f32(T, HC, NE).half(), f32(T, HC, NE).half()
+    mx, mx16 = emp(T, NE), emp(T, NE, dt=torch.float16)
+    g32, u32 = f32(nq), f32(nq)
+    q32, s32, q16, s16 = emp(nq, dt=torch.int8), emp(nq // 32), emp(nq, dt=torch.int8), emp(nq // 16)
+    pk, pq, pgv = f32(T * HC, NE), f32(T * HC, NE), emp(T * HC, NE)
+    cw, hist = 0.5 * f32(hcd, 4), f32(hcd, 9)
+    k, v, gk = f32(T, KVD), f32(T, KVD), 1 + 0.02 * f32(HD)
+    c, s_ = orc.ref_rope_table(T, THETA)
+    cos, sin = torch.from_numpy(c).to(dev), torch.from_numpy(s_).to(dev)
+    dpos = torch.zeros(1, dtype=torch.int32, device=dev)
+    planes = [emp(T, KVD, dt=torch.int8) if i % 2 == 0 else emp(T, KVD // 64, dt=torch.int16) for i in range(8)]
+
+    def kv(st):
+        R_.ref_fused_head_norm_rope_multi(P(k), P(gk), P(cos), P(sin), P(dpos), T, KH, HD, HD, KVD, EPS, S(st))
+        R_.ref_kv_append_int8_multi(P(k), P(v), *(P(t) for t in planes), P(dpos), T, T, T, S(st))
+
+    jobs = {
+        "kv32": (kv, T * KVD * 4 * 3 + T * KVD * 4 + T * (KVD // 64) * 2 * 4 + HD * 4),
+        "gate": (lambda st: R_.ref_ple_gate_gv_multi(P(pk), P(pq), P(blk), P(pgv), T, HC, NE, S(st)),
+                 rows * 12 + T * NE * 4),
+        "conv": (lambda st: R_.ref_ple_conv_multi(P(xn), P(cw), P(hist), P(pgv), P(R), hcd, T, ctypes.c_void_p(0),
+                                                  S(st)),
+                 rows * 16 + hcd * (4 + 9 + 9) * 4),
+        "grw": (lambda st: R_.ref_gr_write_multi(P(R), P(blk), P(inj), T, NE, HC, S(st)),
+                rows * 8 + T * NE * 4 + T * HC * 4),
+        "mix": (lambda st: R_.ref_pf_gr_up_mean_fp16(P(xn16), P(gg16), P(mx), P(mx16), T, NE, S(st)),
+                rows * 4 + T * NE * 6),
+        "grn": (lambda st: R_.ref_fused_gr_norm_multi(P(R), P(wn), P(blk), P(inj), P(xn), T, NE, HC,
+                                                      ctypes.c_float(EPS), S(st)),
+                rows * (8 + 4) + T * NE * 4 + T * HC * 4 + HC * NE * 4),
+        "grq8": (lambda st: R_.ref_fused_gr_norm_multi_q8(P(R), P(wn), P(blk), P(inj), P(xn), P(xq8), P(xs8), T, NE,
+                                                          HC, ctypes.c_float(EPS), S(st)),
+                 rows * (8 + 4 + 1) + rows // 8 + T * NE * 4 + T * HC * 4 + HC * NE * 4),
+        "swq8": (lambda st: R_.ref_silu_mul_quant32_multi(P(g32), P(u32), P(q32), P(s32), nq // 32, S(st)),
+                 nq * (8 + 1) + nq // 8),
+        "q8": (lambda st: R_.ref_quant_act_multi(P(g32), P(q32), P(s32), P(q16), P(s16), FFN, nq // FFN, S(st)),
+               nq * (4 + 1 + 1) + nq // 32 * 4 + nq // 16 * 4),
+    }
+    out = {}
+    for name, (fn, nb) in jobs.items():
+        us = fl.time(fn)
+        out[name] = [round(us, 2), round(nb / (us * 1e-6) / 1e9 / peak, 3)]
+    return out
+
+
 def reference_arm(args, rank, peak):
     """The reference's path: no standalone implementation of the norms, RoPE or SwiGLU exists in it
     other than CUDA kernels, so rank 0 times the oracle port (its C restatement) on this host's cores;
@@ -690,6 +768,10 @@ def reference_arm(args, rank, peak):
         rg = reference_gpu(peak)
     except Exception as e:  # the CPU arm stands on its own
         rg = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+    try:
+        rg8 = reference_gpu_f8(peak)
+    except Exception as e:
+        rg8 = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
@@ -697,7 +779,7 @@ def reference_arm(args, rank, peak):
         "config": {"workload": "configs[4]: configs[1]+[2] bundle at 262,144 tokens (CPU: bounded sample)"},
         "cpu_baseline": cb, "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                                     "d2h_bytes_per_step": 0},
-        "reference_gpu": rg,
+        "reference_gpu": rg, "reference_gpu_f8": rg8,
     }), flush=True)
 
 

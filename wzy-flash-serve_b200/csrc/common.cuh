@@ -343,6 +343,10 @@ __host__ __device__ __forceinline__ uint64_t mod_u64(uint64_t x, uint64_t d, uin
     return r;
 }
 
+// Position (item / divisor, item % divisor) of a grid-stride loop over items start, start + step, ...,
+// advanced without a division per item. start and step (a warp's or thread's index and the grid's
+// count) fit 32 bits for every grid this library launches, where the two divisions are 32-bit ones
+// (a few instructions instead of a 64-bit division routine each); larger values take the 64-bit path.
 struct StridePos {
     int64_t q;
     int r;
@@ -350,10 +354,19 @@ struct StridePos {
     int dr;
     int d;
     __device__ __forceinline__ StridePos(int64_t start, int64_t step, int divisor) : d(divisor) {
-        q = start / divisor;
-        r = (int)(start - q * divisor);
-        dq = step / divisor;
-        dr = (int)(step - dq * divisor);
+        if (((uint64_t)start | (uint64_t)step) <= 0xFFFFFFFFull) {
+            const uint32_t s32 = (uint32_t)start, t32 = (uint32_t)step, d32 = (uint32_t)divisor;
+            const uint32_t q32 = s32 / d32, dq32 = t32 / d32;
+            q = q32;
+            r = (int)(s32 - q32 * d32);
+            dq = dq32;
+            dr = (int)(t32 - dq32 * d32);
+        } else {
+            q = start / divisor;
+            r = (int)(start - q * divisor);
+            dq = step / divisor;
+            dr = (int)(step - dq * divisor);
+        }
     }
     __device__ __forceinline__ void advance() {
         q += dq;
